@@ -1,0 +1,72 @@
+"""Semantic validation of a loaded Config (crates/rusteeze-config/src/
+validation.rs:7-195: dtype/device/TP/port/ranges; HF repo id vs local path)."""
+from __future__ import annotations
+
+import os
+import re
+from typing import List
+
+from rusteeze_b200.core.errors import ConfigError
+
+_DTYPES = {"auto", "float32", "float16", "bfloat16", "fp32", "fp16", "bf16"}
+_DEVICE_RE = re.compile(r"^(auto|cpu|cuda(:\d+)?)$")
+_HF_REPO_RE = re.compile(r"^[A-Za-z0-9_.-]+/[A-Za-z0-9_.-]+$")
+
+
+def is_hf_repo_id(s: str) -> bool:
+    return bool(_HF_REPO_RE.match(s)) and not os.path.exists(s)
+
+
+def collect_errors(cfg) -> List[str]:
+    e: List[str] = []
+    m, s, g = cfg.model, cfg.server, cfg.engine
+    if m.dtype not in _DTYPES:
+        e.append(f"model.dtype must be one of {sorted(_DTYPES)}, got {m.dtype!r}")
+    if not _DEVICE_RE.match(m.device):
+        e.append(f"model.device must be auto|cpu|cuda|cuda:N (metal/vulkan are not supported), got {m.device!r}")
+    for k in ("tensor_parallel_size", "expert_parallel_size", "data_parallel_size"):
+        v = getattr(m, k)
+        if v < 1 or v & (v - 1):
+            e.append(f"model.{k} must be a power of two >= 1, got {v}")
+    if m.pipeline_parallel_size != 1:
+        e.append("model.pipeline_parallel_size > 1 is not supported: one NVSwitch domain serves these "
+                 "models with tensor/expert parallelism")
+    if m.quantization is not None and m.quantization.method not in ("none", "fp8_block", "fp8", "fp8_e4m3"):
+        e.append(f"model.quantization.method {m.quantization.method!r} unsupported (none | fp8_block)")
+    if m.max_model_len is not None and m.max_model_len < 16:
+        e.append("model.max_model_len must be >= 16")
+    if not 0 < s.port < 65536:
+        e.append(f"server.port out of range: {s.port}")
+    if s.timeout_seconds <= 0:
+        e.append("server.timeout_seconds must be > 0")
+    if s.tls is not None and (not s.tls.cert_path or not s.tls.key_path):
+        e.append("server.tls needs cert_path and key_path")
+    if g.max_num_seqs < 1:
+        e.append("engine.max_num_seqs must be >= 1")
+    if g.max_num_batched_tokens < g.max_num_seqs:
+        e.append("engine.max_num_batched_tokens must be >= engine.max_num_seqs")
+    if g.block_size != 16:
+        e.append("engine.block_size must be 16 (the paged-attention kernels are built for 16-token blocks)")
+    if not 0.0 < g.gpu_memory_utilization <= 1.0:
+        e.append("engine.gpu_memory_utilization must be in (0, 1]")
+    if g.swap_space_gb < 0:
+        e.append("engine.swap_space_gb must be >= 0")
+    if g.scheduling.policy not in ("fcfs", "sjf", "priority"):
+        e.append(f"engine.scheduling.policy must be fcfs|sjf|priority, got {g.scheduling.policy!r}")
+    if g.scheduling.preemption_mode not in ("recompute", "swap"):
+        e.append("engine.scheduling.preemption_mode must be recompute|swap")
+    if g.comm_backend not in ("nccl", "fused"):
+        e.append("engine.comm_backend must be nccl|fused")
+    if g.speculative is not None and not 1 <= g.speculative.num_speculative_tokens <= 16:
+        e.append("engine.speculative.num_speculative_tokens must be in [1, 16]")
+    if cfg.logging.level.lower() not in ("trace", "debug", "info", "warn", "warning", "error"):
+        e.append(f"logging.level invalid: {cfg.logging.level!r}")
+    if cfg.logging.format not in ("pretty", "compact", "json"):
+        e.append("logging.format must be pretty|compact|json")
+    return e
+
+
+def validate_config(cfg) -> None:
+    errs = collect_errors(cfg)
+    if errs:
+        raise ConfigError("invalid configuration:\n  - " + "\n  - ".join(errs))

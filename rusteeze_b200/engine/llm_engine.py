@@ -1,0 +1,392 @@
+"""The engine: request intake, the step loop, stop handling, outputs.
+
+Counterpart of crates/rusteeze-engine/src/engine.rs.  The reference's
+`Engine::step` (engine.rs:357-435) schedules, builds a batch, and hands the
+worker a closure that writes ZERO logits (engine.rs:418-427), so it always
+samples token 0; `generate` runs a single step per request (engine.rs:292).
+Here `step()` runs the real model: schedule -> (swap/CoW block copies) ->
+batch build -> forward (CUDA graph for pure decode) -> on-device sampling ->
+append tokens -> stop checks (EOS unless ignore_eos, stop token ids, stop
+strings through the incremental detokenizer, max_tokens, max_model_len) ->
+free blocks of finished sequences -> RequestOutputs.  `LLM.generate` drives
+steps until every request finishes.
+
+Finish reasons: "stop" (EOS/stop token/stop string), "length" (max_tokens or
+context limit), "abort" -- the reference always reports Stop (engine.rs:
+497-555).
+"""
+from __future__ import annotations
+
+import logging
+import os
+import time
+from typing import Callable, Dict, Iterable, List, Optional, Union
+
+import numpy as np
+import torch
+
+from rusteeze_b200.config.config import Config
+from rusteeze_b200.core.errors import ContextLengthExceededError, InvalidRequestError
+from rusteeze_b200.core.outputs import RequestOutput
+from rusteeze_b200.core.sampling_params import SamplingParams
+from rusteeze_b200.core.types import RequestStatus, new_request_id
+from rusteeze_b200.engine.block_manager import make_block_manager
+from rusteeze_b200.engine.model_runner import ModelRunner
+from rusteeze_b200.engine.sampler import SampleRow
+from rusteeze_b200.engine.scheduler import (PreemptionMode, Scheduler, SchedulerConfig,
+                                            SchedulingPolicy)
+from rusteeze_b200.engine.sequence import Request, Sequence
+from rusteeze_b200.models.config import ModelConfig, get_preset
+from rusteeze_b200.models.loader import build_model
+from rusteeze_b200.tokenizer.tokenizer import IncrementalDetokenizer, load_tokenizer
+from rusteeze_b200.ops import BLOCK_SIZE
+
+log = logging.getLogger("rusteeze.engine")
+
+
+def _dtype(name: str, device: str) -> torch.dtype:
+    if name in ("auto", "bfloat16", "bf16"):
+        return torch.bfloat16 if device.startswith("cuda") else torch.float32
+    return {"float32": torch.float32, "fp32": torch.float32, "float16": torch.float16,
+            "fp16": torch.float16}[name]
+
+
+def resolve_device(name: str) -> str:
+    if name == "auto":
+        return "cuda:0" if torch.cuda.is_available() else "cpu"
+    if name == "cuda":
+        return "cuda:0"
+    return name
+
+
+class LLMEngine:
+    def __init__(self, config: Config, model=None, model_config: Optional[ModelConfig] = None,
+                 tokenizer=None, tp=None, executor=None):
+        self.config = config
+        mc = config.model
+        ec = config.engine
+        self.device = resolve_device(mc.device)
+        if model is not None:
+            self.model_config = model.cfg
+        elif model_config is not None:
+            self.model_config = model_config
+        elif mc.path:
+            self.model_config = ModelConfig.from_json_file(mc.path)
+        else:
+            self.model_config = get_preset(mc.preset or "tiny-llama")
+        self.max_model_len = min(mc.max_model_len or self.model_config.max_position_embeddings,
+                                 self.model_config.max_position_embeddings)
+        self.dtype = _dtype(mc.dtype, self.device)
+        if self.device.startswith("cuda"):
+            torch.cuda.set_device(torch.device(self.device))
+        if model is None:
+            model = build_model(self.model_config, dtype=self.dtype, device=self.device, tp=tp,
+                                model_dir=mc.path, seed=mc.seed)
+            if mc.quantization is not None and mc.quantization.method != "none":
+                from rusteeze_b200.models.quant import quantize_model_fp8
+                quantize_model_fp8(model)
+        self.model = model
+        self.tokenizer = tokenizer or load_tokenizer(mc.tokenizer or mc.path, self.model_config.vocab_size)
+        self.model_name = mc.served_name()
+        self.eos_ids = tuple(self.model_config.eos_token_id or ([self.tokenizer.eos_token_id]
+                                                               if self.tokenizer.eos_token_id is not None else []))
+        # KV cache sizing
+        num_gpu_blocks = ec.num_gpu_blocks or self._profile_num_blocks()
+        bytes_per_block = self.model_config.kv_bytes_per_token(torch.finfo(self.dtype).bits // 8) * BLOCK_SIZE
+        num_cpu_blocks = int(ec.swap_space_gb * (1 << 30) // bytes_per_block) if self.device.startswith("cuda") \
+            else min(int(ec.swap_space_gb * (1 << 30) // bytes_per_block), 1024)
+        if ec.scheduling.preemption_mode != "swap":
+            num_cpu_blocks = min(num_cpu_blocks, 0 if self.device.startswith("cuda") else num_cpu_blocks)
+        self.bm = make_block_manager(BLOCK_SIZE, num_gpu_blocks, num_cpu_blocks, ec.enable_prefix_caching)
+        spec = ec.speculative
+        self.sched_cfg = SchedulerConfig(
+            max_num_seqs=ec.max_num_seqs, max_num_batched_tokens=ec.max_num_batched_tokens,
+            max_model_len=self.max_model_len, enable_chunked_prefill=ec.enable_chunked_prefill,
+            preemption_mode=PreemptionMode(ec.scheduling.preemption_mode),
+            policy=SchedulingPolicy(ec.scheduling.policy),
+            num_lookahead_slots=spec.num_speculative_tokens if spec else 0)
+        self.scheduler = Scheduler(self.sched_cfg, self.bm)
+        self.runner = executor or ModelRunner(
+            model, num_gpu_blocks=num_gpu_blocks, num_cpu_blocks=num_cpu_blocks,
+            max_num_seqs=ec.max_num_seqs, max_num_batched_tokens=ec.max_num_batched_tokens,
+            max_model_len=self.max_model_len, use_cuda_graph=not ec.enforce_eager, seed=mc.seed)
+        if self.device.startswith("cuda") and not ec.enforce_eager and hasattr(self.runner, "capture_graphs"):
+            from rusteeze_b200.engine.model_runner import decode_graph_buckets
+            mx = min(ec.cuda_graph_max_batch or ec.max_num_seqs, ec.max_num_seqs)
+            self.runner.capture_graphs(decode_graph_buckets(mx))
+        self.requests: Dict[str, Request] = {}
+        self.seq_to_request: Dict[int, Request] = {}
+        self._rng = np.random.default_rng(mc.seed)
+        self.stats_counters = {"steps": 0, "prompt_tokens": 0, "generation_tokens": 0,
+                               "requests_finished": 0, "requests_aborted": 0}
+        self.observers: List[Callable] = []
+        self.spec = None
+        if spec is not None:
+            from rusteeze_b200.engine.spec_decode import SpecDecoder
+            self.spec = SpecDecoder(self, spec)
+
+    # ------------------------------------------------------------------ sizing
+    def _profile_num_blocks(self) -> int:
+        ec = self.config.engine
+        bytes_per_block = self.model_config.kv_bytes_per_token(torch.finfo(self.dtype).bits // 8) * BLOCK_SIZE
+        bytes_per_block //= max(1, getattr(self.model.tp, "size", 1)) if self.model_config.num_key_value_heads >= \
+            getattr(self.model.tp, "size", 1) else 1
+        if not self.device.startswith("cuda"):
+            return 64 if self.model_config.hidden_size <= 512 else 512
+        free, total = torch.cuda.mem_get_info()
+        used_by_others = total - free
+        budget = total * ec.gpu_memory_utilization - used_by_others
+        # activations / logits / graph pools headroom
+        budget -= 4 * (1 << 30)
+        n = int(budget // bytes_per_block)
+        if n < 16:
+            raise RuntimeError(f"not enough GPU memory for the KV cache ({budget / 2**30:.1f} GiB left)")
+        return n
+
+    # ------------------------------------------------------------------ requests
+    def add_request(self, request_id: Optional[str], prompt: Optional[str] = None,
+                    params: Optional[SamplingParams] = None, prompt_token_ids: Optional[List[int]] = None,
+                    arrival_time: Optional[float] = None, priority: int = 0) -> Request:
+        params = params or SamplingParams()
+        if prompt_token_ids is None:
+            if prompt is None:
+                raise InvalidRequestError("either prompt or prompt_token_ids is required")
+            prompt_token_ids = self.tokenizer.encode(prompt)
+        if not prompt_token_ids:
+            raise InvalidRequestError("empty prompt")
+        V = self.model_config.vocab_size
+        if min(prompt_token_ids) < 0 or max(prompt_token_ids) >= V:
+            raise InvalidRequestError(f"prompt token ids must be in [0, {V})")
+        if len(prompt_token_ids) >= self.max_model_len:
+            raise ContextLengthExceededError(
+                f"prompt has {len(prompt_token_ids)} tokens; the model context is {self.max_model_len}")
+        if params.use_beam_search:
+            raise InvalidRequestError("beam search is not supported; use best_of/n sampling")
+        rid = request_id or new_request_id("cmpl")
+        if rid in self.requests:
+            raise InvalidRequestError(f"duplicate request id {rid}")
+        req = Request(rid, prompt, list(prompt_token_ids), params,
+                      arrival_time if arrival_time is not None else time.monotonic(), priority)
+        if params.seed is None:
+            req.seed = int(self._rng.integers(0, 2 ** 62))
+        else:
+            req.seed = int(params.seed)
+        for s in req.seqs:
+            self._register_seq(req, s)
+            self.scheduler.add(s)
+        self.requests[rid] = req
+        return req
+
+    def _register_seq(self, req: Request, s: Sequence) -> None:
+        s.detok = IncrementalDetokenizer(self.tokenizer, req.prompt_token_ids, req.params.skip_special_tokens)
+        self.seq_to_request[s.seq_id] = req
+
+    def abort_request(self, request_id: str) -> bool:
+        req = self.requests.get(request_id)
+        if req is None:
+            return False
+        for s in req.seqs:
+            if not s.is_finished():
+                self.scheduler.remove(s)
+                self.bm.free(s.seq_id)
+                s.status = RequestStatus.FINISHED_ABORTED
+                s.finish_reason = "abort"
+        req.forked = True
+        self.stats_counters["requests_aborted"] += 1
+        self._retire(req)
+        return True
+
+    def has_unfinished_requests(self) -> bool:
+        return self.scheduler.has_unfinished()
+
+    def get_num_unfinished_requests(self) -> int:
+        return len(self.requests)
+
+    # ------------------------------------------------------------------ step
+    def step(self) -> List[RequestOutput]:
+        if self.spec is not None:
+            return self.spec.step()
+        so = self.scheduler.schedule()
+        outputs: List[RequestOutput] = []
+        # sequences ignored by the scheduler (too long)
+        for s in list(self.seq_to_request):
+            pass
+        if so.is_empty():
+            return self._collect_ignored()
+        rows, owners = self._sample_rows(so)
+        t0 = time.monotonic()
+        res = self.runner.execute(so, self.bm, rows)
+        now = time.monotonic()
+        self.stats_counters["steps"] += 1
+        touched = self._apply_results(so, res, owners, now)
+        for obs in self.observers:
+            obs(self, so, now - t0)
+        for req in touched:
+            outputs.append(req.to_output(delta=True))
+            if req.is_finished():
+                self._retire(req)
+        return outputs + self._collect_ignored()
+
+    def _collect_ignored(self) -> List[RequestOutput]:
+        outs = []
+        for req in list(self.requests.values()):
+            if any(s.status == RequestStatus.FINISHED_IGNORED for s in req.seqs) and req.is_finished():
+                outs.append(req.to_output(delta=True))
+                self._retire(req)
+        return outs
+
+    def _sample_rows(self, so):
+        rows: List[SampleRow] = []
+        owners = []
+        for ss in so.scheduled:
+            if not ss.sample:
+                continue
+            s = ss.seq
+            req = s.request
+            for j in range(ss.num_samples):
+                rows.append(SampleRow(req.params, s.token_ids[:s.prompt_len], s.output_token_ids,
+                                      seed=req.seed + 7919 * (s.index + j), offset=s.num_generated,
+                                      eos_ids=self.eos_ids, mirostat_mu=s.mirostat_mu))
+            owners.append((ss, ss.num_samples))
+        return rows, owners
+
+    def _apply_results(self, so, res, owners, now: float):
+        touched = []
+        seen = set()
+        # advance computed counters and publish full blocks to the prefix cache
+        for ss in so.scheduled:
+            s = ss.seq
+            s.num_computed = ss.ctx + ss.num_new
+            self.bm.commit(s.seq_id, s.tokens_np(), s.num_computed)
+            if ss.ctx == 0 or ss.ctx == s.num_cached:
+                self.stats_counters["prompt_tokens"] += 0
+            self.stats_counters["prompt_tokens"] += ss.num_new if s.num_generated == 0 else 0
+        i = 0
+        for ss, k in owners:
+            s = ss.seq
+            req = s.request
+            toks = res.tokens[i:i + k]
+            lps = res.logprobs[i:i + k]
+            tops = res.top_logprobs[i:i + k]
+            mus = res.mirostat_mu[i:i + k]
+            i += k
+            targets = [s]
+            if k > 1:   # fork best_of - 1 children sharing the prompt's blocks (copy-on-write)
+                for j in range(1, k):
+                    c = Sequence(req, req.prompt_token_ids, index=j)
+                    c.num_computed = s.num_computed
+                    c.num_cached = s.num_cached
+                    self.bm.fork(s.seq_id, c.seq_id)
+                    req.seqs.append(c)
+                    self._register_seq(req, c)
+                    self.scheduler.add_running(c)
+                    targets.append(c)
+                req.forked = True
+            for t, tok, lp, top, mu in zip(targets, toks, lps, tops, mus):
+                t.append_token(tok, lp, top)
+                if mu is not None:
+                    t.mirostat_mu = mu
+                if req.metrics.first_token_time is None:
+                    req.metrics.first_token_time = now
+                req.metrics.last_token_time = now
+                req.metrics.num_generated = max(req.metrics.num_generated, t.num_generated)
+                self.stats_counters["generation_tokens"] += 1
+                self._check_stop(t, tok)
+            if id(req) not in seen:
+                seen.add(id(req))
+                touched.append(req)
+        return touched
+
+    def _check_stop(self, s: Sequence, tok: int) -> None:
+        p = s.request.params
+        delta = s.detok.step(tok) if s.detok is not None else ""
+        s.output_text += delta
+        reason = None
+        n = s.num_generated
+        if n >= p.min_tokens:
+            if not p.ignore_eos and tok in self.eos_ids:
+                reason = "stop"
+                s.stop_reason = None
+            elif tok in p.stop_token_ids:
+                reason = "stop"
+                s.stop_reason = tok
+            elif p.stop:
+                for st in p.stop:
+                    pos = s.output_text.find(st, max(0, len(s.output_text) - len(delta) - len(st)))
+                    if pos >= 0:
+                        s.output_text = s.output_text[:pos + (len(st) if p.include_stop_str_in_output else 0)]
+                        reason = "stop"
+                        s.stop_reason = st
+                        break
+        if reason is None and ((p.max_tokens is not None and n >= p.max_tokens)
+                               or s.total_len >= self.max_model_len):
+            reason = "length"
+        if reason is not None:
+            s.finish_reason = reason
+            s.status = RequestStatus.FINISHED_STOPPED if reason == "stop" else RequestStatus.FINISHED_LENGTH
+            self.scheduler.remove(s)
+            self.bm.free(s.seq_id)
+
+    def _retire(self, req: Request) -> None:
+        import time as _t
+        if req.request_id in self.requests:
+            req.metrics.finished_time = _t.monotonic()
+            del self.requests[req.request_id]
+            for s in req.seqs:
+                self.seq_to_request.pop(s.seq_id, None)
+            self.stats_counters["requests_finished"] += 1
+
+    # ------------------------------------------------------------------ stats
+    def stats(self) -> dict:
+        d = dict(self.stats_counters)
+        d.update(num_waiting=self.scheduler.num_waiting, num_running=self.scheduler.num_running,
+                 num_swapped=self.scheduler.num_swapped, num_preemptions=self.scheduler.num_preemptions,
+                 kv_cache_usage=self.bm.gpu_usage(), num_gpu_blocks=self.bm.num_gpu_blocks)
+        d.update({f"block_{k}": v for k, v in self.bm.stats().items()})
+        return d
+
+
+class LLM:
+    """Offline batch API: `LLM(...).generate(prompts, SamplingParams(...))`."""
+
+    def __init__(self, model: Optional[str] = None, *, preset: Optional[str] = None,
+                 config: Optional[Config] = None, **engine_kw):
+        from rusteeze_b200.config.config import Config as _C
+        cfg = config or _C()
+        if model is not None:
+            if os.path.isdir(model):
+                cfg.model.path = model
+            else:
+                cfg.model.preset = model
+        if preset is not None:
+            cfg.model.preset = preset
+        for k, v in engine_kw.items():
+            for sec in (cfg.engine, cfg.model):
+                if hasattr(sec, k):
+                    setattr(sec, k, v)
+                    break
+            else:
+                raise TypeError(f"unknown option {k}")
+        self.engine = LLMEngine(cfg)
+
+    def generate(self, prompts: Union[None, str, List[str]] = None,
+                 sampling_params: Optional[Union[SamplingParams, List[SamplingParams]]] = None,
+                 prompt_token_ids: Optional[List[List[int]]] = None,
+                 use_tqdm: bool = False) -> List[RequestOutput]:
+        if isinstance(prompts, str):
+            prompts = [prompts]
+        n = len(prompts) if prompts is not None else len(prompt_token_ids)
+        if not isinstance(sampling_params, list):
+            sampling_params = [sampling_params or SamplingParams()] * n
+        ids = []
+        for i in range(n):
+            req = self.engine.add_request(
+                None, prompts[i] if prompts is not None else None, sampling_params[i],
+                prompt_token_ids[i] if prompt_token_ids is not None else None)
+            ids.append(req.request_id)
+        done: Dict[str, RequestOutput] = {}
+        while self.engine.has_unfinished_requests():
+            for out in self.engine.step():
+                if out.finished:
+                    done[out.request_id] = out
+        return [done[i] for i in ids]

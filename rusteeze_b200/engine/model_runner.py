@@ -1,0 +1,241 @@
+"""Per-GPU model runner: KV cache, batch staging, CUDA graphs, sampling.
+
+The reference's worker (crates/rusteeze-engine/src/worker.rs:56-164) keeps a
+preallocated logits buffer and calls an injected model closure.  Here the
+runner owns everything between a scheduler decision and sampled tokens:
+
+  * KV cache: one device tensor [num_blocks, L, 2, Hkv, 16, D].  A block holds
+    the K and V of 16 tokens for every layer contiguously, so a swap or a
+    copy-on-write copy is one contiguous transfer per block, while each
+    (block, layer, k|v, head) tile the attention kernels read is a
+    contiguous 4 KiB run (Hkv=1 slice: 16 x 128 bf16).
+  * Swap space: the same layout in pinned host memory (`swap_space` GiB).
+  * Batch staging: the C++ batch builder writes ids/positions/slots/
+    cu-seqlens/block tables into pinned host buffers, which are copied to
+    static device buffers with one async H2D each.
+  * CUDA graphs: pure-decode steps are replayed from graphs captured per
+    batch-size bucket (1, 2, 4, 8, 16, 24, 32, ... max_num_seqs); the decode
+    attention's split count is fixed per bucket and the split range is
+    derived from the live sequence lengths inside the kernel.
+  * Sampling happens on the device; only token ids (and logprobs if asked)
+    come back.
+"""
+from __future__ import annotations
+
+import math
+import time
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from rusteeze_b200.engine.sampler import SampleRow, Sampler, SampleResult
+from rusteeze_b200.engine.scheduler import SchedulerOutput
+from rusteeze_b200.models.decoder import AttentionMetadata, DecoderLM
+from rusteeze_b200.ops import BLOCK_SIZE
+
+NUM_SMS_B200 = 148
+
+
+def decode_graph_buckets(max_seqs: int) -> List[int]:
+    b = [1, 2, 4, 8, 16]
+    x = 24
+    while x < max_seqs:
+        b.append(x)
+        x += 8 if x < 64 else 16 if x < 128 else 32
+    b.append(max_seqs)
+    return sorted(set(v for v in b if v <= max_seqs))
+
+
+def choose_num_splits(batch: int, num_kv_heads: int, max_blocks: int, num_sms: int = NUM_SMS_B200) -> int:
+    """Split-KV factor so that decode attention puts >= ~2 CTAs on every SM."""
+    ctas = batch * num_kv_heads
+    if ctas >= 2 * num_sms:
+        return 1
+    s = math.ceil(2 * num_sms / ctas)
+    return max(1, min(s, max_blocks, 64))
+
+
+class ModelRunner:
+    def __init__(self, model: DecoderLM, *, num_gpu_blocks: int, num_cpu_blocks: int,
+                 max_num_seqs: int, max_num_batched_tokens: int, max_model_len: int,
+                 kv_dtype=None, use_cuda_graph: bool = True, seed: int = 0):
+        self.model = model
+        self.cfg = model.cfg
+        self.device = model.device
+        self.is_cuda = self.device.type == "cuda"
+        self.max_num_seqs = max_num_seqs
+        self.max_tokens = max(max_num_batched_tokens, max_num_seqs)
+        self.max_blocks = (max_model_len + BLOCK_SIZE - 1) // BLOCK_SIZE
+        self.kv_dtype = kv_dtype or model.dtype
+        L, D, hkv = self.cfg.num_hidden_layers, self.cfg.head_dim, model.hkv
+        self.num_gpu_blocks = num_gpu_blocks
+        self.kv_cache = torch.zeros(num_gpu_blocks, L, 2, hkv, BLOCK_SIZE, D, dtype=self.kv_dtype,
+                                    device=self.device)
+        self.kv_layers = [(self.kv_cache[:, l, 0], self.kv_cache[:, l, 1]) for l in range(L)]
+        self.cpu_cache = None
+        if num_cpu_blocks > 0:
+            self.cpu_cache = torch.zeros(num_cpu_blocks, L, 2, hkv, BLOCK_SIZE, D, dtype=self.kv_dtype,
+                                         pin_memory=self.is_cuda)
+        pin = self.is_cuda
+        T, S, MB = self.max_tokens, max_num_seqs, self.max_blocks
+        self.h_input_ids = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
+        self.h_positions = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
+        self.h_slots = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
+        self.h_qsl = torch.zeros(S + 1, dtype=torch.int32, pin_memory=pin)
+        self.h_seq_lens = torch.zeros(S, dtype=torch.int32, pin_memory=pin)
+        self.h_block_tables = torch.zeros(S, MB, dtype=torch.int32, pin_memory=pin)
+        self.h_logits_idx = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
+        dev = self.device
+        self.d_input_ids = torch.zeros(T, dtype=torch.int64, device=dev)
+        self.d_positions = torch.zeros(T, dtype=torch.int64, device=dev)
+        self.d_slots = torch.full((T,), -1, dtype=torch.int64, device=dev)
+        self.d_qsl = torch.zeros(S + 1, dtype=torch.int32, device=dev)
+        self.d_seq_lens = torch.zeros(S, dtype=torch.int32, device=dev)
+        self.d_block_tables = torch.zeros(S, MB, dtype=torch.int32, device=dev)
+        self.d_logits_idx = torch.zeros(T, dtype=torch.int64, device=dev)
+        max_splits = choose_num_splits(1, hkv, self.max_blocks)
+        self.decode_ws = (torch.empty(S * model.hq * max_splits * (D + 2), dtype=torch.float32, device=dev)
+                          if self.is_cuda else None)
+        self.sampler = Sampler(self.cfg.vocab_size)
+        self.use_cuda_graph = use_cuda_graph and self.is_cuda
+        self.graphs: Dict[int, Tuple[torch.cuda.CUDAGraph, torch.Tensor]] = {}
+        self.graph_pool = None
+        self.seed = seed
+        self.step_times: List[float] = []
+
+    # ------------------------------------------------------------------ cache ops
+    @torch.no_grad()
+    def copy_blocks(self, pairs: List[Tuple[int, int]]) -> None:
+        if not pairs:
+            return
+        src = torch.tensor([p[0] for p in pairs], dtype=torch.long, device=self.device)
+        dst = torch.tensor([p[1] for p in pairs], dtype=torch.long, device=self.device)
+        self.kv_cache.index_copy_(0, dst, self.kv_cache.index_select(0, src))
+
+    @torch.no_grad()
+    def swap_out(self, pairs: List[Tuple[int, int]]) -> None:
+        for g, c in pairs:   # one contiguous D2H per block
+            self.cpu_cache[c].copy_(self.kv_cache[g], non_blocking=True)
+
+    @torch.no_grad()
+    def swap_in(self, pairs: List[Tuple[int, int]]) -> None:
+        for c, g in pairs:
+            self.kv_cache[g].copy_(self.cpu_cache[c], non_blocking=True)
+
+    # ------------------------------------------------------------------ batch prep
+    def prepare(self, so: SchedulerOutput, bm) -> Tuple[AttentionMetadata, int, int, List[int]]:
+        sched = so.scheduled
+        S = len(sched)
+        seq_ids = np.fromiter((s.seq.seq_id for s in sched), dtype=np.int64, count=S)
+        ctx = np.fromiter((s.ctx for s in sched), dtype=np.int64, count=S)
+        n_new = np.fromiter((s.num_new for s in sched), dtype=np.int64, count=S)
+        toks = np.concatenate([s.seq.tokens_np()[s.ctx:s.ctx + s.num_new] for s in sched]) if S else \
+            np.zeros(0, dtype=np.int64)
+        T = bm.build_batch(seq_ids, ctx, n_new, toks, self.h_input_ids.data_ptr(),
+                           self.h_positions.data_ptr(), self.h_slots.data_ptr(), self.h_qsl.data_ptr(),
+                           self.h_seq_lens.data_ptr(), self.h_block_tables.data_ptr(),
+                           self.h_logits_idx.data_ptr(), self.max_blocks, 1)
+        # rows to sample: last token of sequences with sample=True, repeated num_samples times
+        rows: List[int] = []
+        lidx = self.h_logits_idx
+        sample_rows: List[int] = []
+        for i, s in enumerate(sched):
+            if s.sample:
+                for _ in range(s.num_samples):
+                    sample_rows.append(int(lidx[i]))
+                rows.append(i)
+        nd = len(so.decodes)
+        max_q = max((s.num_new for s in so.prefills), default=1)
+        max_s = int(self.h_seq_lens[:S].max()) if S else 0
+        nb = non_blocking = self.is_cuda
+        self.d_input_ids[:T].copy_(self.h_input_ids[:T], non_blocking=nb)
+        self.d_positions[:T].copy_(self.h_positions[:T], non_blocking=nb)
+        self.d_slots[:T].copy_(self.h_slots[:T], non_blocking=nb)
+        self.d_qsl[:S + 1].copy_(self.h_qsl[:S + 1], non_blocking=nb)
+        self.d_seq_lens[:S].copy_(self.h_seq_lens[:S], non_blocking=nb)
+        self.d_block_tables[:S].copy_(self.h_block_tables[:S], non_blocking=non_blocking)
+        meta = AttentionMetadata(
+            num_seqs=S, num_tokens=T, num_decode_seqs=nd, query_start_loc=self.d_qsl[:S + 1],
+            seq_lens=self.d_seq_lens[:S], block_tables=self.d_block_tables[:S],
+            slot_mapping=self.d_slots[:T], max_query_len=max_q, max_seq_len=max_s,
+            decode_num_splits=choose_num_splits(max(nd, 1), self.model.hkv, self.max_blocks),
+            decode_workspace=self.decode_ws)
+        if not self.is_cuda:
+            # host oracle path reads the metadata on the host
+            meta.query_start_loc = self.h_qsl[:S + 1].clone()
+            meta.seq_lens = self.h_seq_lens[:S].clone()
+            meta.block_tables = self.h_block_tables[:S].clone()
+        return meta, T, S, sample_rows
+
+    # ------------------------------------------------------------------ graphs
+    def _graph_bucket(self, n: int) -> Optional[int]:
+        for b in sorted(self.graphs):
+            if b >= n:
+                return b
+        return None
+
+    @torch.no_grad()
+    def capture_graphs(self, buckets: Optional[List[int]] = None) -> None:
+        """Captures decode-only forward + LM head for each batch bucket."""
+        if not self.use_cuda_graph:
+            return
+        buckets = buckets or decode_graph_buckets(self.max_num_seqs)
+        self.graph_pool = torch.cuda.graph_pool_handle()
+        stream = torch.cuda.Stream()
+        for B in sorted(buckets, reverse=True):
+            meta = self._graph_meta(B)
+            self.d_slots[:B].fill_(-1)
+            self.d_seq_lens[:B].fill_(0)
+            with torch.cuda.stream(stream):
+                for _ in range(2):     # warm-up outside capture
+                    self._decode_forward(B, meta)
+            torch.cuda.current_stream().wait_stream(stream)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self.graph_pool, stream=stream):
+                out = self._decode_forward(B, meta)
+            self.graphs[B] = (g, out, meta)
+        torch.cuda.synchronize()
+
+    def _graph_meta(self, B: int) -> AttentionMetadata:
+        return AttentionMetadata(
+            num_seqs=B, num_tokens=B, num_decode_seqs=B, query_start_loc=self.d_qsl[:B + 1],
+            seq_lens=self.d_seq_lens[:B], block_tables=self.d_block_tables[:B],
+            slot_mapping=self.d_slots[:B], max_query_len=1, max_seq_len=self.max_blocks * BLOCK_SIZE,
+            decode_num_splits=choose_num_splits(B, self.model.hkv, self.max_blocks),
+            decode_workspace=self.decode_ws)
+
+    def _decode_forward(self, B: int, meta: AttentionMetadata) -> torch.Tensor:
+        h = self.model(self.d_input_ids[:B], self.d_positions[:B], meta, self.kv_layers)
+        return self.model.compute_logits(h)
+
+    # ------------------------------------------------------------------ execute
+    @torch.no_grad()
+    def execute(self, so: SchedulerOutput, bm, rows: List[SampleRow]) -> SampleResult:
+        if so.blocks_to_swap_out:
+            self.swap_out(so.blocks_to_swap_out)
+        if so.blocks_to_swap_in:
+            self.swap_in(so.blocks_to_swap_in)
+        if so.blocks_to_copy:
+            self.copy_blocks(so.blocks_to_copy)
+        meta, T, S, sample_rows = self.prepare(so, bm)
+        logits = self.forward_logits(meta, T, S, sample_rows, pure_decode=not so.prefills)
+        return self.sampler.sample(logits, rows)
+
+    def forward_logits(self, meta: AttentionMetadata, T: int, S: int, sample_rows: List[int],
+                       pure_decode: bool) -> torch.Tensor:
+        B = self._graph_bucket(S) if (pure_decode and self.graphs and T == S) else None
+        if B is not None:
+            if B > S:   # padded rows: no KV write, empty context
+                self.d_slots[S:B].fill_(-1)
+                self.d_seq_lens[S:B].fill_(0)
+                self.d_input_ids[S:B].fill_(0)
+                self.d_positions[S:B].fill_(0)
+            g, out, _ = self.graphs[B]
+            g.replay()
+            idx = torch.tensor(sample_rows, dtype=torch.long)
+            return out.index_select(0, idx.to(out.device, non_blocking=True))
+        h = self.model(self.d_input_ids[:T], self.d_positions[:T], meta, self.kv_layers)
+        idx = torch.tensor(sample_rows, dtype=torch.long, pin_memory=self.is_cuda)
+        hs = h.index_select(0, idx.to(h.device, non_blocking=True))
+        return self.model.compute_logits(hs)

@@ -1,0 +1,246 @@
+"""Batched token sampling.
+
+Semantics follow the reference sampler (crates/rusteeze-engine/src/
+sampler.rs:56-244): repetition penalty over previously seen tokens, logit
+bias, then greedy (temperature 0 or top_k 1), or temperature -> softmax ->
+top-k -> top-p over the (not renormalised) top-k probabilities -> renormalise
+-> draw; Mirostat v1/v2 (sampler.rs:181-244).  Added here: frequency and
+presence penalties (simd_ops.rs:104-119 defines them, the reference never
+applies them), min-p, min_tokens (EOS masked until reached), per-request
+seeds (the reference reseeds every row with `i ^ 0xDEADBEEF` each call,
+parallel_sampler.rs:86-89), and logprobs.
+
+On the GPU the whole batch is sampled by one kernel launch (sm_100a
+`topk_topp_sample`: per-row max/normaliser, histogram threshold selection
+for top-k/top-p/min-p, Gumbel-max draw from a counter-based Philox stream
+keyed by (seed, step)), or `argmax_sample` when every row is greedy.  Rows
+that need Mirostat, typical-p, eta/epsilon cutoffs or guided decoding are
+copied to the host and sampled there.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence as Seq, Tuple
+
+import torch
+
+from rusteeze_b200 import ops
+from rusteeze_b200.core.sampling_params import SamplingParams
+from rusteeze_b200.ops import reference as ref
+
+_MASK = -1e30
+
+
+@dataclass
+class SampleRow:
+    params: SamplingParams
+    prompt_ids: Seq[int]
+    output_ids: Seq[int]
+    seed: int
+    offset: int
+    eos_ids: Tuple[int, ...] = ()
+    mirostat_mu: Optional[float] = None
+
+
+@dataclass
+class SampleResult:
+    tokens: List[int]
+    logprobs: List[Optional[float]]
+    top_logprobs: List[Optional[Dict[int, float]]]
+    mirostat_mu: List[Optional[float]]
+
+
+def _philox_like_seed(seed: int, offset: int) -> int:
+    x = (seed * 0x9E3779B97F4A7C15 + offset * 0xBF58476D1CE4E5B9) & ((1 << 63) - 1)
+    return x
+
+
+class Sampler:
+    def __init__(self, vocab_size: int):
+        self.vocab_size = vocab_size
+        self._param_cache: Dict[Tuple, Tuple[torch.Tensor, ...]] = {}
+
+    # ------------------------------------------------------------------ pre-processing
+    def _process_logits(self, logits: torch.Tensor, rows: List[SampleRow]) -> torch.Tensor:
+        """Penalties, logit bias, min_tokens masking (in place when possible)."""
+        need_pen = [i for i, r in enumerate(rows) if r.params.has_penalties()]
+        if need_pen:
+            sub = logits[need_pen]
+            sub_cpu_rows = [rows[i] for i in need_pen]
+            rep = torch.tensor([r.params.repetition_penalty for r in sub_cpu_rows])
+            freq = torch.tensor([r.params.frequency_penalty for r in sub_cpu_rows])
+            pres = torch.tensor([r.params.presence_penalty for r in sub_cpu_rows])
+            if logits.is_cuda:
+                sub = _apply_penalties_device(sub, sub_cpu_rows, rep, freq, pres)
+            else:
+                sub = ref.apply_penalties(sub, [list(r.output_ids) for r in sub_cpu_rows],
+                                          [list(r.prompt_ids) for r in sub_cpu_rows], rep, freq, pres)
+            logits[need_pen] = sub
+        for i, r in enumerate(rows):
+            p = r.params
+            if p.logit_bias:
+                idx = torch.tensor(list(p.logit_bias.keys()), dtype=torch.long, device=logits.device)
+                val = torch.tensor(list(p.logit_bias.values()), dtype=logits.dtype, device=logits.device)
+                logits[i].index_add_(0, idx, val)
+            if p.min_tokens and len(r.output_ids) < p.min_tokens:
+                stop = list(r.eos_ids) + list(p.stop_token_ids)
+                if stop:
+                    logits[i, torch.tensor(stop, device=logits.device)] = _MASK
+        return logits
+
+    # ------------------------------------------------------------------ main entry
+    def sample(self, logits: torch.Tensor, rows: List[SampleRow]) -> SampleResult:
+        """logits: fp32 [R, V] (device or host), one row per SampleRow."""
+        R = logits.shape[0]
+        assert R == len(rows)
+        logits = self._process_logits(logits, rows)
+        host_rows = [i for i, r in enumerate(rows) if r.params.needs_host_sampling()]
+        tokens: List[int] = [0] * R
+        lps: List[Optional[float]] = [None] * R
+        mus: List[Optional[float]] = [None] * R
+        dev_rows = [i for i in range(R) if i not in set(host_rows)] if host_rows else list(range(R))
+        if dev_rows:
+            sub = logits if len(dev_rows) == R else logits[dev_rows]
+            t, lp = self._sample_device(sub, [rows[i] for i in dev_rows])
+            for j, i in enumerate(dev_rows):
+                tokens[i] = t[j]
+                lps[i] = lp[j]
+        for i in host_rows:
+            tok, lp, mu = _host_sample(logits[i].float().cpu(), rows[i])
+            tokens[i], lps[i], mus[i] = tok, lp, mu
+        tops: List[Optional[Dict[int, float]]] = [None] * R
+        want = [i for i, r in enumerate(rows) if r.params.logprobs is not None]
+        if want:
+            lsm = torch.log_softmax(logits[want].float(), dim=-1)
+            for j, i in enumerate(want):
+                k = rows[i].params.logprobs
+                d: Dict[int, float] = {}
+                if k:
+                    v, ix = lsm[j].topk(min(k, lsm.shape[1]))
+                    d = dict(zip(ix.tolist(), v.tolist()))
+                d[tokens[i]] = float(lsm[j, tokens[i]])
+                tops[i] = d
+                lps[i] = d[tokens[i]]
+        return SampleResult(tokens, lps, tops, mus)
+
+    def _sample_device(self, logits: torch.Tensor, rows: List[SampleRow]):
+        R = logits.shape[0]
+        greedy = [r.params.is_greedy for r in rows]
+        if not logits.is_cuda:
+            return _cpu_sample(logits, rows)
+        dev = logits.device
+        want_lp = any(r.params.logprobs is not None for r in rows)
+        if all(greedy):
+            toks, lp = ops.sample(logits, None, None, None, None, None, None, greedy_all=True,
+                                  want_logprobs=want_lp)
+        else:
+            temp = torch.tensor([0.0 if g else r.params.temperature for g, r in zip(greedy, rows)],
+                                dtype=torch.float32)
+            top_k = torch.tensor([r.params.top_k for r in rows], dtype=torch.int32)
+            top_p = torch.tensor([r.params.top_p for r in rows], dtype=torch.float32)
+            min_p = torch.tensor([r.params.min_p for r in rows], dtype=torch.float32)
+            seeds = torch.tensor([r.seed & ((1 << 63) - 1) for r in rows], dtype=torch.int64)
+            offs = torch.tensor([r.offset for r in rows], dtype=torch.int64)
+            packed = [x.pin_memory().to(dev, non_blocking=True) for x in (temp, top_k, top_p, min_p, seeds, offs)]
+            toks, lp = ops.sample(logits, *packed, greedy_all=False, want_logprobs=want_lp)
+        both = torch.stack([toks.double(), lp.double()]).cpu()
+        return [int(x) for x in both[0].tolist()], both[1].tolist()
+
+
+def _apply_penalties_device(sub: torch.Tensor, rows: List[SampleRow], rep, freq, pres) -> torch.Tensor:
+    dev = sub.device
+    V = sub.shape[1]
+    for j, r in enumerate(rows):
+        p = r.params
+        row = sub[j]
+        if p.repetition_penalty != 1.0:
+            seen = torch.tensor(sorted(set(r.prompt_ids) | set(r.output_ids)), dtype=torch.long, device=dev)
+            if seen.numel():
+                v = row[seen]
+                row[seen] = torch.where(v > 0, v / p.repetition_penalty, v * p.repetition_penalty)
+        if r.output_ids and (p.frequency_penalty or p.presence_penalty):
+            cnt = torch.bincount(torch.tensor(list(r.output_ids), dtype=torch.long, device=dev),
+                                 minlength=V).float()
+            row -= p.frequency_penalty * cnt + p.presence_penalty * (cnt > 0).float()
+    return sub
+
+
+def _row_generator(seed: int, offset: int) -> torch.Generator:
+    g = torch.Generator()
+    g.manual_seed(_philox_like_seed(seed, offset))
+    return g
+
+
+def _cpu_sample(logits: torch.Tensor, rows: List[SampleRow]):
+    toks, lps = [], []
+    for i, r in enumerate(rows):
+        x = logits[i].float()
+        if r.params.is_greedy:
+            t = int(torch.argmax(x))
+            toks.append(t)
+            lps.append(float(torch.log_softmax(x, -1)[t]))
+            continue
+        p = r.params
+        probs = ref.topk_topp_minp_probs(x.unsqueeze(0), torch.tensor([p.temperature]),
+                                         torch.tensor([p.top_k]), torch.tensor([p.top_p]),
+                                         torch.tensor([p.min_p]))[0]
+        t = int(torch.multinomial(probs, 1, generator=_row_generator(r.seed, r.offset)))
+        toks.append(t)
+        lps.append(math.log(max(float(probs[t]), 1e-45)))
+    return toks, lps
+
+
+def _host_sample(x: torch.Tensor, r: SampleRow):
+    """Mirostat v1/v2, typical-p, eta/epsilon cutoffs, guided choice."""
+    p = r.params
+    g = _row_generator(r.seed, r.offset)
+    if p.temperature > 0:
+        x = x / p.temperature
+    probs = torch.softmax(x, -1)
+    if p.mirostat_mode:
+        mu = r.mirostat_mu if r.mirostat_mu is not None else 2.0 * p.mirostat_tau
+        sp, si = probs.sort(descending=True)
+        if p.mirostat_mode == 1:
+            k = max(1, min(int(math.exp(min(mu, 50.0))), sp.numel()))
+            cand, idx = sp[:k], si[:k]
+        else:
+            keep = -torch.log(sp.clamp_min(1e-30)) <= mu
+            if not keep.any():
+                keep[0] = True
+            cand, idx = sp[keep], si[keep]
+        cand = cand / cand.sum()
+        j = int(torch.multinomial(cand, 1, generator=g))
+        tok, pr = int(idx[j]), float(cand[j])
+        surprise = -math.log(max(pr, 1e-10))
+        mu = mu + p.mirostat_eta * (p.mirostat_tau - surprise)
+        return tok, math.log(max(pr, 1e-45)), mu
+    keep = torch.ones_like(probs, dtype=torch.bool)
+    if p.typical_p > 0:
+        ent = -(probs * torch.log(probs.clamp_min(1e-30))).sum()
+        dev = (-torch.log(probs.clamp_min(1e-30)) - ent).abs()
+        order = dev.argsort()
+        cum = probs[order].cumsum(0)
+        n = int((cum < p.typical_p).sum()) + 1
+        m = torch.zeros_like(keep)
+        m[order[:n]] = True
+        keep &= m
+    if p.epsilon_cutoff > 0:
+        keep &= probs >= p.epsilon_cutoff
+    if p.eta_cutoff > 0:
+        ent = -(probs * torch.log(probs.clamp_min(1e-30))).sum()
+        eps = min(p.eta_cutoff, math.sqrt(p.eta_cutoff) * math.exp(-float(ent)))
+        keep &= probs >= eps
+    if p.guided_decoding is not None and getattr(r, "allowed", None) is not None:
+        m = torch.zeros_like(keep)
+        m[list(r.allowed)] = True
+        keep &= m
+    if not keep.any():
+        keep[int(probs.argmax())] = True
+    pr = torch.where(keep, probs, torch.zeros_like(probs))
+    if p.temperature == 0:
+        tok = int(pr.argmax())
+    else:
+        pr = pr / pr.sum()
+        tok = int(torch.multinomial(pr, 1, generator=g))
+    return tok, math.log(max(float(probs[tok]), 1e-45)), None

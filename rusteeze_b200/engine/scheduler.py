@@ -1,0 +1,274 @@
+"""Continuous-batching iteration scheduler.
+
+What the reference's scheduler does (crates/rusteeze-engine/src/
+scheduler.rs:142-215): retire finished sequences, give every running
+sequence one decode token (highest priority first) within the token and
+sequence budgets, preempt what does not fit, then admit waiting prompts FCFS
+within the token budget.  Its gaps -- no KV-block availability check, no
+chunked prefill, preempted sequences never come back -- are closed here:
+
+  * every admission and every decode checks free KV blocks in the C++
+    block manager (including the copy-on-write block of forked sequences);
+  * prompts are split into chunks that fit the per-step token budget
+    (`enable_chunked_prefill`), and a chunked prompt keeps its place;
+  * preemption is either RECOMPUTE (free the blocks, re-prefill later; the
+    reference's default, scheduler.rs:48-83) or SWAP (KV moved to CPU
+    blocks and swapped back in before new prompts are admitted);
+  * waiting order is FCFS, shortest-job-first or priority
+    (crates/rusteeze-config/src/engine.rs scheduling policy knob);
+  * a watermark of free blocks is kept so that running sequences can grow.
+
+The output orders decodes (one new token each) before prefill chunks, which
+is the layout the attention kernels expect.
+"""
+from __future__ import annotations
+
+import enum
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Deque, List, Optional, Tuple
+
+from rusteeze_b200.core.types import RequestStatus
+from rusteeze_b200.engine.sequence import Sequence
+
+
+class PreemptionMode(str, enum.Enum):
+    RECOMPUTE = "recompute"
+    SWAP = "swap"
+
+
+class SchedulingPolicy(str, enum.Enum):
+    FCFS = "fcfs"
+    SJF = "sjf"
+    PRIORITY = "priority"
+
+
+@dataclass
+class SchedulerConfig:
+    max_num_seqs: int = 256
+    max_num_batched_tokens: int = 8192
+    max_model_len: int = 8192
+    enable_chunked_prefill: bool = True
+    preemption_mode: PreemptionMode = PreemptionMode.RECOMPUTE
+    policy: SchedulingPolicy = SchedulingPolicy.FCFS
+    watermark: float = 0.01
+    num_lookahead_slots: int = 0        # speculative decoding: k draft tokens
+    max_prefill_seqs: int = 64          # bound on prefill chunks per step
+
+
+@dataclass
+class ScheduledSeq:
+    seq: Sequence
+    ctx: int            # tokens with KV before this step
+    num_new: int        # tokens computed this step
+    sample: bool        # logits of the last new token are sampled
+    num_samples: int = 1
+
+
+@dataclass
+class SchedulerOutput:
+    decodes: List[ScheduledSeq] = field(default_factory=list)
+    prefills: List[ScheduledSeq] = field(default_factory=list)
+    blocks_to_copy: List[Tuple[int, int]] = field(default_factory=list)
+    blocks_to_swap_in: List[Tuple[int, int]] = field(default_factory=list)
+    blocks_to_swap_out: List[Tuple[int, int]] = field(default_factory=list)
+    preempted: List[Sequence] = field(default_factory=list)
+    num_batched_tokens: int = 0
+
+    @property
+    def scheduled(self) -> List[ScheduledSeq]:
+        return self.decodes + self.prefills
+
+    def is_empty(self) -> bool:
+        return not self.decodes and not self.prefills
+
+
+class Scheduler:
+    def __init__(self, cfg: SchedulerConfig, block_manager):
+        self.cfg = cfg
+        self.bm = block_manager
+        self.waiting: Deque[Sequence] = deque()
+        self.running: List[Sequence] = []
+        self.swapped: Deque[Sequence] = deque()
+        self.num_preemptions = 0
+        self._watermark_blocks = max(1, int(cfg.watermark * self.bm.num_gpu_blocks))
+
+    # ------------------------------------------------------------------ queue ops
+    def add(self, seq: Sequence) -> None:
+        seq.status = RequestStatus.WAITING
+        self.waiting.append(seq)
+
+    def add_running(self, seq: Sequence) -> None:
+        """A forked child joins the running set directly."""
+        seq.status = RequestStatus.RUNNING
+        self.running.append(seq)
+
+    def remove(self, seq: Sequence) -> None:
+        for q in (self.running,):
+            if seq in q:
+                q.remove(seq)
+        for dq in (self.waiting, self.swapped):
+            try:
+                dq.remove(seq)
+            except ValueError:
+                pass
+
+    def has_unfinished(self) -> bool:
+        return bool(self.waiting or self.running or self.swapped)
+
+    @property
+    def num_waiting(self) -> int:
+        return len(self.waiting)
+
+    @property
+    def num_running(self) -> int:
+        return len(self.running)
+
+    @property
+    def num_swapped(self) -> int:
+        return len(self.swapped)
+
+    # ------------------------------------------------------------------ helpers
+    def _key(self, s: Sequence):
+        r = s.request
+        return (-r.priority, r.arrival_time, s.seq_id)
+
+    def _sort_waiting(self) -> None:
+        pol = self.cfg.policy
+        if pol == SchedulingPolicy.FCFS:
+            return  # deque order is arrival order; preempted seqs are re-queued at the front
+        if pol == SchedulingPolicy.SJF:
+            key = lambda s: (s.total_len, s.request.arrival_time)  # noqa: E731
+        else:
+            key = lambda s: (-s.request.priority, s.request.arrival_time)  # noqa: E731
+        self.waiting = deque(sorted(self.waiting, key=key))
+
+    def _preempt(self, seq: Sequence, out: SchedulerOutput) -> None:
+        self.num_preemptions += 1
+        out.preempted.append(seq)
+        if self.cfg.preemption_mode == PreemptionMode.SWAP and self.bm.can_swap_out(seq.seq_id):
+            out.blocks_to_swap_out.extend(self.bm.swap_out(seq.seq_id))
+            seq.status = RequestStatus.SWAPPED
+            self.swapped.append(seq)
+        else:
+            self.bm.free(seq.seq_id)
+            seq.reset_for_recompute()
+            self.waiting.appendleft(seq)
+
+    def _lookahead(self, seq: Sequence) -> int:
+        return self.cfg.num_lookahead_slots if not seq.is_prefill else 0
+
+    # ------------------------------------------------------------------ main
+    def schedule(self) -> SchedulerOutput:
+        cfg, bm = self.cfg, self.bm
+        out = SchedulerOutput()
+        token_budget = cfg.max_num_batched_tokens
+        seq_budget = cfg.max_num_seqs
+
+        # 1. running sequences, highest priority / oldest first
+        self.running.sort(key=self._key)
+        kept: List[Sequence] = []
+        queue = list(self.running)
+        while queue:
+            seq = queue.pop(0)
+            if seq.is_prefill:
+                n = min(seq.remaining, token_budget)
+                if n <= 0 or seq_budget <= 0:
+                    kept.append(seq)        # keeps its blocks, continues next step
+                    continue
+            else:
+                n = 1
+                if token_budget < 1 + self._lookahead(seq) or seq_budget <= 0:
+                    self._preempt(seq, out)
+                    continue
+            target = seq.num_computed + n + self._lookahead(seq)
+            while bm.blocks_to_grow(seq.seq_id, target, seq.num_computed) > bm.num_free_gpu_blocks():
+                if queue:
+                    self._preempt(queue.pop(), out)   # lowest priority goes first
+                else:
+                    break
+            if bm.blocks_to_grow(seq.seq_id, target, seq.num_computed) > bm.num_free_gpu_blocks():
+                self._preempt(seq, out)
+                continue
+            out.blocks_to_copy.extend(bm.ensure_capacity(seq.seq_id, target, seq.num_computed))
+            done_prompt = seq.num_computed + n >= seq.total_len
+            ss = ScheduledSeq(seq, seq.num_computed, n, sample=done_prompt,
+                              num_samples=self._num_samples(seq) if done_prompt else 1)
+            (out.prefills if n > 1 or seq.is_prefill else out.decodes).append(ss)
+            token_budget -= n + (self._lookahead(seq) if n == 1 else 0)
+            seq_budget -= 1
+            kept.append(seq)
+        self.running = kept
+
+        # 2. swapped sequences come back before new prompts (unless we just preempted)
+        if not out.preempted:
+            while self.swapped and seq_budget > 0 and token_budget > 0:
+                seq = self.swapped[0]
+                need = len(bm.block_table(seq.seq_id)) + self._watermark_blocks
+                if need > bm.num_free_gpu_blocks():
+                    break
+                self.swapped.popleft()
+                out.blocks_to_swap_in.extend(bm.swap_in(seq.seq_id))
+                seq.status = RequestStatus.RUNNING
+                n = min(seq.remaining, token_budget) if seq.is_prefill else 1
+                target = seq.num_computed + n + self._lookahead(seq)
+                if bm.blocks_to_grow(seq.seq_id, target, seq.num_computed) > bm.num_free_gpu_blocks():
+                    self.running.append(seq)
+                    continue
+                out.blocks_to_copy.extend(bm.ensure_capacity(seq.seq_id, target, seq.num_computed))
+                done_prompt = seq.num_computed + n >= seq.total_len
+                ss = ScheduledSeq(seq, seq.num_computed, n, sample=done_prompt)
+                (out.prefills if n > 1 or seq.is_prefill else out.decodes).append(ss)
+                token_budget -= n
+                seq_budget -= 1
+                self.running.append(seq)
+
+        # 3. waiting prompts (or recompute-preempted sequences)
+        if not self.swapped:
+            self._sort_waiting()
+            n_prefill = len(out.prefills)
+            while self.waiting and seq_budget > 0 and token_budget > 0 and n_prefill < cfg.max_prefill_seqs:
+                seq = self.waiting[0]
+                if seq.total_len > cfg.max_model_len:
+                    self.waiting.popleft()
+                    seq.status = RequestStatus.FINISHED_IGNORED
+                    seq.finish_reason = "length"
+                    continue
+                toks = seq.tokens_np()
+                cached = bm.cached_prefix_len(toks) if not bm.has_seq(seq.seq_id) else seq.num_computed
+                remaining = seq.total_len - cached
+                if not cfg.enable_chunked_prefill and remaining > token_budget:
+                    break
+                n = min(remaining, token_budget)
+                need = bm.blocks_needed_for_prompt(toks, cached + n)
+                if need + self._watermark_blocks > bm.num_free_gpu_blocks():
+                    break
+                self.waiting.popleft()
+                if not bm.has_seq(seq.seq_id):
+                    got = bm.allocate_prompt(seq.seq_id, toks)
+                    seq.num_computed = got
+                    seq.num_cached = got
+                    if seq.request.metrics.first_scheduled_time is None:
+                        import time
+                        seq.request.metrics.first_scheduled_time = time.monotonic()
+                out.blocks_to_copy.extend(bm.ensure_capacity(seq.seq_id, seq.num_computed + n,
+                                                             seq.num_computed))
+                seq.status = RequestStatus.RUNNING
+                done_prompt = seq.num_computed + n >= seq.total_len
+                out.prefills.append(ScheduledSeq(seq, seq.num_computed, n, sample=done_prompt,
+                                                 num_samples=self._num_samples(seq) if done_prompt else 1))
+                self.running.append(seq)
+                token_budget -= n
+                seq_budget -= 1
+                n_prefill += 1
+
+        # decodes that are really single-token prompt tails stay as "prefill"
+        # only if they have more than one token; re-split for the kernel layout
+        out.num_batched_tokens = sum(s.num_new for s in out.decodes) + sum(s.num_new for s in out.prefills)
+        return out
+
+    def _num_samples(self, seq: Sequence) -> int:
+        r = seq.request
+        if r.forked or r.num_target_seqs == 1 or seq.num_generated > 0:
+            return 1
+        return r.num_target_seqs

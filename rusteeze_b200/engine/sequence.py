@@ -1,0 +1,152 @@
+"""Sequences and requests (sequence groups).
+
+Counterpart of crates/rusteeze-engine/src/sequence.rs:70-429 (Sequence,
+SequenceGroup, stop handling) and crates/rusteeze-core/src/sequence.rs:80-517
+(timing: TTFT, ITL).  A request with n > 1 (or best_of > n) owns several
+sequences that share the prompt's KV blocks copy-on-write after the prompt is
+prefilled.
+"""
+from __future__ import annotations
+
+import itertools
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+
+from rusteeze_b200.core.outputs import CompletionOutput, RequestOutput
+from rusteeze_b200.core.sampling_params import SamplingParams
+from rusteeze_b200.core.types import RequestMetrics, RequestStatus
+
+_seq_ids = itertools.count(1)
+
+
+class Sequence:
+    __slots__ = ("seq_id", "request", "prompt_len", "token_ids", "status", "num_computed",
+                 "num_cached", "logprobs", "cumulative_logprob", "output_text", "stop_reason",
+                 "detok", "_np", "_np_len", "index", "finish_reason", "rng_offset",
+                 "mirostat_mu", "spec_draft")
+
+    def __init__(self, request: "Request", prompt_token_ids: List[int], index: int = 0):
+        self.seq_id = next(_seq_ids)
+        self.request = request
+        self.index = index
+        self.prompt_len = len(prompt_token_ids)
+        self.token_ids: List[int] = list(prompt_token_ids)
+        self.status = RequestStatus.WAITING
+        self.num_computed = 0          # tokens whose KV is in the cache
+        self.num_cached = 0            # of those, reused from the prefix cache
+        self.logprobs: List[Dict[int, float]] = []
+        self.cumulative_logprob = 0.0
+        self.output_text = ""
+        self.stop_reason = None
+        self.finish_reason: Optional[str] = None
+        self.detok = None
+        self._np = None
+        self._np_len = -1
+        self.rng_offset = 0
+        self.mirostat_mu = None
+        self.spec_draft: List[int] = []
+
+    # ------------------------------------------------------------------
+    @property
+    def output_token_ids(self) -> List[int]:
+        return self.token_ids[self.prompt_len:]
+
+    @property
+    def num_generated(self) -> int:
+        return len(self.token_ids) - self.prompt_len
+
+    @property
+    def total_len(self) -> int:
+        return len(self.token_ids)
+
+    @property
+    def is_prefill(self) -> bool:
+        """More than one token still lacks KV (prompt or recompute after preemption)."""
+        return self.total_len - self.num_computed > 1
+
+    @property
+    def remaining(self) -> int:
+        return self.total_len - self.num_computed
+
+    def tokens_np(self) -> np.ndarray:
+        if self._np_len != len(self.token_ids):
+            self._np = np.asarray(self.token_ids, dtype=np.int64)
+            self._np_len = len(self.token_ids)
+        return self._np
+
+    def append_token(self, tok: int, logprob: Optional[float] = None,
+                     top: Optional[Dict[int, float]] = None) -> None:
+        self.token_ids.append(int(tok))
+        if logprob is not None:
+            self.cumulative_logprob += float(logprob)
+        if top is not None:
+            self.logprobs.append(top)
+
+    def is_finished(self) -> bool:
+        return self.status.is_finished
+
+    def reset_for_recompute(self) -> None:
+        """Preemption by recompute: drop all KV; prompt+generated get re-prefilled."""
+        self.num_computed = 0
+        self.num_cached = 0
+        self.status = RequestStatus.WAITING
+
+
+@dataclass
+class Request:
+    request_id: str
+    prompt: Optional[str]
+    prompt_token_ids: List[int]
+    params: SamplingParams
+    arrival_time: float
+    priority: int = 0
+    seqs: List[Sequence] = field(default_factory=list)
+    metrics: RequestMetrics = None
+    forked: bool = False
+    lora: Optional[str] = None
+    # streaming state
+    sent_text_len: Dict[int, int] = field(default_factory=dict)
+
+    def __post_init__(self) -> None:
+        if self.metrics is None:
+            self.metrics = RequestMetrics(arrival_time=self.arrival_time)
+        if not self.seqs:
+            self.seqs = [Sequence(self, self.prompt_token_ids, 0)]
+
+    @property
+    def num_target_seqs(self) -> int:
+        return self.params.best_of
+
+    def is_finished(self) -> bool:
+        # with best_of > 1 the children are forked when the prompt's last
+        # chunk is sampled; until then the request cannot be finished
+        return (self.forked or self.num_target_seqs == 1) and all(s.is_finished() for s in self.seqs)
+
+    def live_seqs(self) -> List[Sequence]:
+        return [s for s in self.seqs if not s.is_finished()]
+
+    def to_output(self, delta: bool = False) -> RequestOutput:
+        p = self.params
+        seqs = self.seqs
+        if self.is_finished() and len(seqs) > p.n:
+            # best_of > n: keep the n sequences with the highest cumulative logprob
+            seqs = sorted(seqs, key=lambda s: s.cumulative_logprob, reverse=True)[: p.n]
+        outs = []
+        deltas = []
+        for s in seqs:
+            text = s.output_text
+            outs.append(CompletionOutput(index=s.index, text=text, token_ids=list(s.output_token_ids),
+                                         cumulative_logprob=s.cumulative_logprob if p.logprobs is not None else None,
+                                         logprobs=s.logprobs if p.logprobs is not None else None,
+                                         finish_reason=s.finish_reason, stop_reason=s.stop_reason))
+            prev = self.sent_text_len.get(s.index, 0)
+            deltas.append(text[prev:])
+            if delta:
+                self.sent_text_len[s.index] = len(text)
+        return RequestOutput(request_id=self.request_id, prompt=self.prompt,
+                             prompt_token_ids=self.prompt_token_ids, outputs=outs,
+                             finished=self.is_finished(), metrics=self.metrics,
+                             num_cached_tokens=max((s.num_cached for s in self.seqs), default=0),
+                             delta_text=deltas)

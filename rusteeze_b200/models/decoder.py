@@ -1,0 +1,240 @@
+"""One decoder-only transformer covering the whole model zoo.
+
+Architectures (crates/rusteeze-model/src/config.rs:15-62 enumerates them; the
+reference implements only Llama (architectures/llama.rs:86-339) and Mistral
+(architectures/mistral.rs:178-586)):
+
+  llama / mistral  pre-norm RMSNorm, GQA attention with neox RoPE, SwiGLU MLP;
+                   Mistral adds a sliding window (mistral.rs:334-363), applied
+                   inside the attention kernel instead of as a host mask.
+  qwen2            llama + bias on the fused QKV projection.
+  phi3             llama layout; its checkpoints already store fused qkv_proj
+                   and gate_up_proj tensors.
+  mixtral          llama attention + top-2 softmax-routed sparse MoE of SwiGLU
+                   experts (absent from the reference).
+  gemma            (1 + w) RMSNorm, sqrt(hidden) embedding scale, GeGLU (tanh).
+  gemma2           gemma + sandwich norms around attention and MLP, attention
+                   and final-logit soft-capping, local/global alternating
+                   sliding window, query_pre_attn_scalar.
+
+The forward works on a flattened token batch (continuous batching): tokens of
+all sequences are concatenated; `AttentionMetadata` says which rows belong to
+which sequence and where their K/V live in the paged cache.
+
+Weights are stored fused and K-major for the GEMM kernel: qkv [(Hq+2Hkv)*D, H],
+gate_up [2I, H] as [gate | up], o [H, Hq*D], down [H, I].  Under tensor
+parallelism every rank holds its own slice (column split of qkv/gate_up by
+head/column, row split of o/down, vocab split of embedding and LM head).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import torch
+import torch.nn as nn
+
+from rusteeze_b200 import ops
+from rusteeze_b200.core.types import ModelArchitecture
+from rusteeze_b200.models.config import ModelConfig
+from rusteeze_b200.ops import reference as ref
+
+
+@dataclass
+class AttentionMetadata:
+    """Flattened-batch attention description for one forward.
+
+    Sequences [0, num_decode_seqs) are single-token decodes occupying token
+    rows [0, num_decode_seqs); the rest are prefill (or multi-token verify)
+    chunks.  For sequence i, its query rows are query_start_loc[i] :
+    query_start_loc[i+1] and they are the LAST rows of a seq_lens[i]-long
+    context whose KV pages are block_tables[i, :]."""
+    num_seqs: int
+    num_tokens: int
+    num_decode_seqs: int
+    query_start_loc: torch.Tensor          # int32 [S+1]
+    seq_lens: torch.Tensor                 # int32 [S]
+    block_tables: torch.Tensor             # int32 [S, max_blocks]
+    slot_mapping: torch.Tensor             # int64 [T]  (-1: do not write)
+    max_query_len: int = 1
+    max_seq_len: int = 0
+    decode_num_splits: int = 1
+    decode_workspace: Optional[torch.Tensor] = None
+    # rows of the hidden state whose logits are needed (last token of each seq,
+    # or every verify position for speculative decoding)
+    logits_indices: Optional[torch.Tensor] = None
+
+
+class TPGroup:
+    """Tensor-parallel context handed to the model.  Single-GPU default is a
+    no-op; `rusteeze_b200.parallel.tp.TPComm` implements the real one."""
+    rank = 0
+    size = 1
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        return x
+
+    def all_gather_last_dim(self, x: torch.Tensor) -> torch.Tensor:
+        return x
+
+    def row_parallel_linear(self, x, w, bias=None):
+        """GEMM whose output must be summed over ranks (o_proj / down_proj)."""
+        return self.all_reduce(ops.linear(x, w, bias))
+
+
+def _split(n: int, size: int, rank: int):
+    assert n % size == 0, f"dimension {n} not divisible by tensor-parallel size {size}"
+    per = n // size
+    return rank * per, (rank + 1) * per
+
+
+class DecoderLM(nn.Module):
+    def __init__(self, cfg: ModelConfig, dtype=torch.bfloat16, device="cpu",
+                 tp: Optional[TPGroup] = None, ep_rank: int = 0, ep_size: int = 1):
+        super().__init__()
+        self.cfg = cfg
+        self.tp = tp or TPGroup()
+        self.dtype = dtype
+        self.device = torch.device(device)
+        tps, tpr = self.tp.size, self.tp.rank
+        self.ep_rank, self.ep_size = ep_rank, ep_size
+        H, D = cfg.hidden_size, cfg.head_dim
+        assert cfg.num_attention_heads % tps == 0, "q heads must divide by TP size"
+        self.hq = cfg.num_attention_heads // tps
+        # KV heads are split when possible, replicated otherwise (e.g. 8 kv heads at TP16)
+        self.hkv = max(1, cfg.num_key_value_heads // tps)
+        self.inter = cfg.intermediate_size // tps if not cfg.is_moe else cfg.intermediate_size
+        self.vocab_lo, self.vocab_hi = _split(_pad_vocab(cfg.vocab_size, tps), tps, tpr)
+        arch = cfg.architecture
+        self.is_gemma = arch in (ModelArchitecture.GEMMA, ModelArchitecture.GEMMA2)
+        self.is_gemma2 = arch == ModelArchitecture.GEMMA2
+        self.act = "gelu_tanh" if (self.is_gemma or "gelu" in cfg.hidden_act) else "silu"
+        e = lambda *s: torch.empty(*s, dtype=dtype, device=device)  # noqa: E731
+
+        self.embed = nn.Parameter(e(self.vocab_hi - self.vocab_lo, H), requires_grad=False)
+        self.layers = nn.ModuleList()
+        for li in range(cfg.num_hidden_layers):
+            L = nn.Module()
+            L.input_norm = nn.Parameter(e(H), requires_grad=False)
+            L.post_attn_norm = nn.Parameter(e(H), requires_grad=False)
+            L.qkv = nn.Parameter(e((self.hq + 2 * self.hkv) * D, H), requires_grad=False)
+            L.qkv_bias = (nn.Parameter(e((self.hq + 2 * self.hkv) * D), requires_grad=False)
+                          if cfg.attention_bias else None)
+            L.o = nn.Parameter(e(H, self.hq * D), requires_grad=False)
+            if self.is_gemma2:
+                L.pre_ff_norm = nn.Parameter(e(H), requires_grad=False)
+                L.post_ff_norm = nn.Parameter(e(H), requires_grad=False)
+            if cfg.is_moe:
+                E = cfg.num_local_experts
+                assert E % ep_size == 0, "experts must divide by EP size"
+                self.e_lo, self.e_hi = _split(E, ep_size, ep_rank)
+                ne = self.e_hi - self.e_lo
+                L.router = nn.Parameter(e(E, H), requires_grad=False)
+                L.w13 = nn.Parameter(e(ne, 2 * cfg.intermediate_size, H), requires_grad=False)
+                L.w2 = nn.Parameter(e(ne, H, cfg.intermediate_size), requires_grad=False)
+            else:
+                L.gate_up = nn.Parameter(e(2 * self.inter, H), requires_grad=False)
+                L.down = nn.Parameter(e(H, self.inter), requires_grad=False)
+            L.sliding_window = cfg.layer_sliding_window(li)
+            self.layers.append(L)
+        self.norm = nn.Parameter(e(H), requires_grad=False)
+        self.lm_head = (None if cfg.tie_word_embeddings
+                        else nn.Parameter(e(self.vocab_hi - self.vocab_lo, H), requires_grad=False))
+        self.register_buffer("cos_sin", ref.rope_cos_sin_cache(
+            D, cfg.max_position_embeddings, cfg.rope_theta, cfg.rope_scaling, device=device),
+            persistent=False)
+        self.moe_impl = None   # set by parallel.moe for EP / fused dispatch
+
+    # ------------------------------------------------------------------ helpers
+    @property
+    def lm_head_weight(self) -> torch.Tensor:
+        return self.embed if self.lm_head is None else self.lm_head
+
+    def embed_tokens(self, ids: torch.Tensor) -> torch.Tensor:
+        if self.tp.size == 1:
+            h = self.embed[ids]
+        else:
+            local = ids - self.vocab_lo
+            ok = (local >= 0) & (local < self.embed.shape[0])
+            h = self.embed[local.clamp(0, self.embed.shape[0] - 1)] * ok.unsqueeze(1).to(self.dtype)
+            h = self.tp.all_reduce(h)
+        if self.cfg.embed_scale != 1.0:
+            h = h * torch.tensor(self.cfg.embed_scale, dtype=self.dtype)
+        return h
+
+    def _mlp(self, L, h: torch.Tensor) -> torch.Tensor:
+        gu = ops.linear(h, L.gate_up)
+        a = ops.silu_mul(gu) if self.act == "silu" else ops.gelu_tanh_mul(gu)
+        return self.tp.row_parallel_linear(a, L.down)
+
+    def _moe(self, L, h: torch.Tensor) -> torch.Tensor:
+        if self.moe_impl is not None:
+            return self.moe_impl(L, h)
+        return moe_forward_local(L, h, self.cfg, self.e_lo, self.e_hi, self.tp)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, meta: AttentionMetadata,
+                kv_caches: List[torch.Tensor]) -> torch.Tensor:
+        cfg = self.cfg
+        eps, off = cfg.rms_norm_eps, cfg.norm_offset
+        D = cfg.head_dim
+        h = self.embed_tokens(input_ids)
+        residual = None
+        for li, L in enumerate(self.layers):
+            kv = kv_caches[li]
+            if residual is None:
+                residual = h
+                x = ops.rms_norm(h, L.input_norm, eps, off)
+            else:
+                x, residual = ops.fused_add_rms_norm(h, residual, L.input_norm, eps, off)
+            qkv = ops.linear(x, L.qkv, L.qkv_bias)
+            q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
+                                   self.hq, self.hkv, D)
+            a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
+                                    cfg.attn_logit_softcapping)
+            h = self.tp.row_parallel_linear(a.view(a.shape[0], -1), L.o)
+            if self.is_gemma2:
+                h = ops.rms_norm(h, L.post_attn_norm, eps, off)
+                x, residual = ops.fused_add_rms_norm(h, residual, L.pre_ff_norm, eps, off)
+                h = self._mlp(L, x)
+                h = ops.rms_norm(h, L.post_ff_norm, eps, off)
+                continue
+            x, residual = ops.fused_add_rms_norm(h, residual, L.post_attn_norm, eps, off)
+            h = self._moe(L, x) if cfg.is_moe else self._mlp(L, x)
+        h, _ = ops.fused_add_rms_norm(h, residual, self.norm, eps, off)
+        return h
+
+    def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
+        """h [n, H] -> fp32 logits [n, vocab] (gathered over TP ranks)."""
+        logits = ops.linear(h, self.lm_head_weight)
+        if self.tp.size > 1:
+            logits = self.tp.all_gather_last_dim(logits)
+        logits = logits[:, : self.cfg.vocab_size].float()
+        cap = self.cfg.final_logit_softcapping
+        if cap:
+            logits = cap * torch.tanh(logits / cap)
+        return logits
+
+
+def _pad_vocab(v: int, tps: int) -> int:
+    return (v + tps - 1) // tps * tps
+
+
+def moe_forward_local(L, h: torch.Tensor, cfg: ModelConfig, e_lo: int, e_hi: int, tp) -> torch.Tensor:
+    """Top-k softmax routed MoE with this rank's experts [e_lo, e_hi); the
+    partial sums are reduced over the group by the caller's all-reduce.  This
+    is the dense-loop oracle; the GPU path replaces it with the grouped-GEMM
+    kernels in `rusteeze_b200.parallel.moe`."""
+    logits = ops.linear(h, L.router).float()
+    w, idx = ref.moe_topk_softmax(logits, cfg.num_experts_per_tok)
+    out = torch.zeros(h.shape[0], h.shape[1], dtype=torch.float32, device=h.device)
+    for e in range(e_lo, e_hi):
+        rows, slot = (idx == e).nonzero(as_tuple=True)
+        if rows.numel() == 0:
+            continue
+        xe = h.index_select(0, rows)
+        gu = ops.linear(xe, L.w13[e - e_lo])
+        y = ops.linear(ops.silu_mul(gu), L.w2[e - e_lo])
+        out.index_add_(0, rows, y.float() * w[rows, slot].unsqueeze(1))
+    out = out.to(h.dtype)
+    return tp.all_reduce(out) if (tp.size > 1) else out

@@ -1,0 +1,198 @@
+"""Device ops used by the models and engine.
+
+Every op has exactly two implementations:
+  * CUDA tensors  -> the hand-written sm_100a kernels in `rusteeze_b200._C`
+                     (built from csrc/kernels/*.cu).  If the extension is not
+                     built, calling an op on a CUDA tensor raises; there is no
+                     silent eager fallback on the GPU.
+  * CPU tensors   -> the fp32 PyTorch oracle in `ops.reference`, which is also
+                     what the numerics tests compare the kernels against.
+"""
+from __future__ import annotations
+
+import importlib
+from typing import Optional
+
+import torch
+
+from rusteeze_b200.ops import reference as ref
+from rusteeze_b200.ops.reference import BLOCK_SIZE  # noqa: F401
+
+_C = None
+_C_ERR: Optional[BaseException] = None
+
+
+def cuda_ext():
+    """The compiled kernel extension; raises loudly if it is missing."""
+    global _C, _C_ERR
+    if _C is None:
+        try:
+            _C = importlib.import_module("rusteeze_b200._C")
+        except BaseException as e:  # noqa: BLE001
+            _C_ERR = e
+            raise RuntimeError(
+                "rusteeze_b200._C (sm_100a kernels) is not built or failed to load; run "
+                "`python setup.py build_ext --inplace` (or __graft_entry__.build()). "
+                f"Underlying error: {e!r}") from e
+    return _C
+
+
+def ext_available() -> bool:
+    try:
+        cuda_ext()
+        return True
+    except RuntimeError:
+        return False
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+# ----------------------------------------------------------------------------- norms
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, offset: float = 0.0) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.rms_norm(x, w, eps, offset)
+    out = torch.empty_like(x)
+    cuda_ext().rms_norm(out, x, w, float(eps), float(offset))
+    return out
+
+
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                       offset: float = 0.0):
+    """residual += x (in place); returns (rms_norm(residual), residual)."""
+    if not x.is_cuda:
+        out, r = ref.fused_add_rms_norm(x, residual, w, eps, offset)
+        residual.copy_(r)
+        return out, residual
+    out = torch.empty_like(x)
+    cuda_ext().fused_add_rms_norm(out, x, residual, w, float(eps), float(offset))
+    return out, residual
+
+
+# ----------------------------------------------------------------------------- rope + kv write
+def rope_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
+                   k_cache: torch.Tensor, v_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                   num_q_heads: int, num_kv_heads: int, head_dim: int) -> torch.Tensor:
+    """Applies neox RoPE to the q and k parts of the fused qkv [T, (Hq+2Hkv)*D]
+    output (q in place), writes rotated k and v into the paged caches at
+    slot_mapping, and returns q as a [T, Hq, D] view."""
+    T = qkv.shape[0]
+    qs, kvs = num_q_heads * head_dim, num_kv_heads * head_dim
+    if not qkv.is_cuda:
+        q = qkv[:, :qs].view(T, num_q_heads, head_dim)
+        k = qkv[:, qs:qs + kvs].reshape(T, num_kv_heads, head_dim).clone()
+        v = qkv[:, qs + kvs:].reshape(T, num_kv_heads, head_dim)
+        qq = q.clone()
+        ref.rope(qq, k, positions, cos_sin)
+        q.copy_(qq)
+        ref.reshape_and_cache(k, v, k_cache, v_cache, slot_mapping)
+        return q
+    cuda_ext().rope_and_cache(qkv, positions, cos_sin, k_cache, v_cache, slot_mapping,
+                              num_q_heads, num_kv_heads, head_dim)
+    return qkv[:, :qs].view(T, num_q_heads, head_dim)
+
+
+# ----------------------------------------------------------------------------- activations
+def silu_mul(x: torch.Tensor) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.silu_mul(x)
+    out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
+    cuda_ext().act_mul(out, x, 0)
+    return out
+
+
+def gelu_tanh_mul(x: torch.Tensor) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.gelu_tanh_mul(x)
+    out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
+    cuda_ext().act_mul(out, x, 1)
+    return out
+
+
+# ----------------------------------------------------------------------------- attention
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, meta,
+                    scale: float, sliding_window: Optional[int] = None,
+                    softcap: Optional[float] = None) -> torch.Tensor:
+    """q [T, Hq, D] -> out [T, Hq, D].  `meta` is an AttentionMetadata."""
+    if not q.is_cuda:
+        return ref.paged_attention(q, k_cache, v_cache, meta.query_start_loc, meta.seq_lens,
+                                   meta.block_tables, scale, sliding_window, softcap)
+    out = torch.empty_like(q)
+    C = cuda_ext()
+    nd = meta.num_decode_seqs
+    win = int(sliding_window or 0)
+    cap = float(softcap or 0.0)
+    if nd > 0:
+        C.decode_attention(out, q, k_cache, v_cache, meta.seq_lens, meta.block_tables,
+                           meta.decode_workspace, nd, float(scale), win, cap,
+                           meta.decode_num_splits)
+    if meta.num_seqs > nd:
+        C.prefill_attention(out, q, k_cache, v_cache, meta.query_start_loc, meta.seq_lens,
+                            meta.block_tables, nd, meta.num_seqs - nd, meta.max_query_len,
+                            float(scale), win, cap)
+    return out
+
+
+# ----------------------------------------------------------------------------- gemm
+def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ w.T (+ bias) (+ residual).  x [M, K] bf16, w [N, K] bf16 (K-major).
+
+    On CUDA this is the tcgen05/TMEM GEMM (TMA-fed, no cluster multicast) with
+    bias and residual fused into the epilogue."""
+    if not x.is_cuda:
+        y = ref.linear(x, w, bias)
+        if residual is not None:
+            y = (y.float() + residual.float()).to(y.dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    M, N = x.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    if M == 0:
+        return out
+    cuda_ext().gemm_bf16(out, x, w, bias, residual)
+    return out
+
+
+def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
+               bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+               out_dtype=torch.bfloat16) -> torch.Tensor:
+    """Block-scaled fp8 GEMM: x bf16 [M,K] is quantised 1x128 on the fly,
+    wq e4m3 [N,K] with fp32 128x128 scales ws."""
+    if not x.is_cuda:
+        xq, xs = ref.quant_fp8_act(x)
+        y = ref.fp8_block_gemm(xq, xs, wq, ws)
+        if bias is not None:
+            y = y + bias.float()
+        if residual is not None:
+            y = y + residual.float()
+        return y.to(out_dtype)
+    C = cuda_ext()
+    M, K = x.shape
+    xq = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
+    xs = torch.empty(K // 128, M, dtype=torch.float32, device=x.device)   # K-block-major scales
+    C.quant_fp8_act(xq, xs, x)
+    out = torch.empty(M, wq.shape[0], dtype=out_dtype, device=x.device)
+    C.gemm_fp8_block(out, xq, xs, wq, ws, bias, residual)
+    return out
+
+
+# ----------------------------------------------------------------------------- sampling
+def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+           min_p: torch.Tensor, seeds: torch.Tensor, offsets: torch.Tensor, greedy_all: bool,
+           want_logprobs: bool = False):
+    """Returns (token ids int64 [B], logprob of the chosen token fp32 [B])."""
+    C = cuda_ext()
+    B, V = logits.shape
+    tokens = torch.empty(B, dtype=torch.int64, device=logits.device)
+    lp = torch.empty(B, dtype=torch.float32, device=logits.device)
+    if greedy_all:
+        C.argmax_sample(tokens, lp, logits, bool(want_logprobs))
+    else:
+        C.topk_topp_sample(tokens, lp, logits, temperature, top_k, top_p, min_p, seeds, offsets,
+                           bool(want_logprobs))
+    return tokens, lp

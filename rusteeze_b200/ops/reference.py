@@ -1,0 +1,251 @@
+"""Plain PyTorch fp32 restatements of every device op.
+
+These are the oracles for the sm_100a kernels (tests compare the CUDA output
+to these) and the CPU execution path of the engine (the tiny-Llama CPU
+configuration runs entirely on them).  Math follows the reference's CPU code:
+RMSNorm with fp32 accumulation (crates/rusteeze-model/src/architectures/
+common.rs:33-45), neox rotate-half RoPE (common.rs:142-170), SwiGLU MLP
+(common.rs:354-361), GQA attention with online-softmax semantics
+(crates/rusteeze-engine/src/flash_attention.rs:186-318), and the sampler
+pipeline penalties -> temperature -> top-k -> top-p (crates/rusteeze-engine/
+src/sampler.rs:56-244, simd_ops.rs:89-119).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+BLOCK_SIZE = 16
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, offset: float = 0.0) -> torch.Tensor:
+    xf = x.float()
+    var = xf.pow(2).mean(-1, keepdim=True)
+    return (xf * torch.rsqrt(var + eps) * (w.float() + offset)).to(x.dtype)
+
+
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                       offset: float = 0.0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """residual <- x + residual ; returns (rms_norm(residual), residual)."""
+    r = (x.float() + residual.float()).to(residual.dtype)
+    return rms_norm(r, w, eps, offset), r
+
+
+def layer_norm(x, w, b, eps):
+    return F.layer_norm(x.float(), (x.shape[-1],), w.float(), None if b is None else b.float(), eps).to(x.dtype)
+
+
+def rope_cos_sin_cache(head_dim: int, max_pos: int, theta: float, scaling=None,
+                       device=None) -> torch.Tensor:
+    """Returns [max_pos, head_dim] fp32: first half cos, second half sin."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    pos = torch.arange(max_pos, dtype=torch.float64)
+    if scaling is not None and scaling.type == "linear":
+        pos = pos / scaling.factor
+    elif scaling is not None and scaling.type == "llama3":
+        # Llama-3.1 frequency-dependent scaling of the inverse frequencies.
+        factor = scaling.factor
+        lo = scaling.low_freq_factor or 1.0
+        hi = scaling.high_freq_factor or 4.0
+        old = scaling.original_max_position_embeddings or 8192
+        lo_wl, hi_wl = old / lo, old / hi
+        wl = 2 * math.pi / inv
+        smooth = (old / wl - lo) / (hi - lo)
+        scaled = torch.where(wl > lo_wl, inv / factor, inv)
+        mid = (wl <= lo_wl) & (wl >= hi_wl)
+        inv = torch.where(mid, (1 - smooth) * inv / factor + smooth * inv, scaled)
+    elif scaling is not None and scaling.type == "dynamic":
+        base = theta * ((scaling.factor * max_pos / (scaling.original_max_position_embeddings or max_pos))
+                        - (scaling.factor - 1)) ** (head_dim / (head_dim - 2))
+        inv = 1.0 / (base ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    freqs = torch.outer(pos, inv)
+    return torch.cat([freqs.cos(), freqs.sin()], dim=-1).float().to(device)
+
+
+def rope(q: torch.Tensor, k: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor):
+    """Neox (rotate-half) RoPE, in place on q [T,Hq,D] and k [T,Hkv,D]."""
+    d = q.shape[-1]
+    cs = cos_sin[positions.long()]
+    cos, sin = cs[:, : d // 2].unsqueeze(1), cs[:, d // 2:].unsqueeze(1)
+
+    def apply(x):
+        xf = x.float()
+        x1, x2 = xf[..., : d // 2], xf[..., d // 2:]
+        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(x.dtype)
+
+    q.copy_(apply(q))
+    k.copy_(apply(k))
+    return q, k
+
+
+def reshape_and_cache(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      slot_mapping: torch.Tensor) -> None:
+    """k,v: [T, Hkv, D]; caches: [num_blocks, Hkv, BLOCK, D]; slot<0 is skipped."""
+    sm = slot_mapping.long()
+    keep = sm >= 0
+    sm = sm[keep]
+    blk, off = sm // BLOCK_SIZE, sm % BLOCK_SIZE
+    k_cache[blk, :, off, :] = k[keep].to(k_cache.dtype)
+    v_cache[blk, :, off, :] = v[keep].to(v_cache.dtype)
+
+
+def silu_mul(x: torch.Tensor) -> torch.Tensor:
+    """x: [T, 2I] laid out [gate | up] -> silu(gate) * up."""
+    g, u = x.float().chunk(2, dim=-1)
+    return (F.silu(g) * u).to(x.dtype)
+
+
+def gelu_tanh_mul(x: torch.Tensor) -> torch.Tensor:
+    g, u = x.float().chunk(2, dim=-1)
+    return (F.gelu(g, approximate="tanh") * u).to(x.dtype)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    y = x.float() @ w.float().t()
+    if bias is not None:
+        y = y + bias.float()
+    return y.to(x.dtype)
+
+
+def gather_kv(cache: torch.Tensor, block_table: torch.Tensor, seq_len: int) -> torch.Tensor:
+    """cache [nb, Hkv, BLOCK, D] -> [seq_len, Hkv, D] for one sequence."""
+    nblk = (seq_len + BLOCK_SIZE - 1) // BLOCK_SIZE
+    blocks = cache[block_table[:nblk].long()]                 # [nblk, Hkv, BLOCK, D]
+    return blocks.permute(0, 2, 1, 3).reshape(-1, cache.shape[1], cache.shape[3])[:seq_len]
+
+
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    query_start_loc: torch.Tensor, seq_lens: torch.Tensor, block_tables: torch.Tensor,
+                    scale: float, sliding_window: Optional[int] = None,
+                    softcap: Optional[float] = None) -> torch.Tensor:
+    """Varlen causal GQA attention over a paged KV cache.
+
+    q: [T, Hq, D]; sequence i owns query rows query_start_loc[i]:query_start_loc[i+1],
+    which are the LAST q_len positions of its seq_lens[i]-long context.
+    """
+    out = torch.empty_like(q)
+    hq, hkv = q.shape[1], k_cache.shape[1]
+    g = hq // hkv
+    qsl = query_start_loc.tolist()
+    for i, L in enumerate(seq_lens.tolist()):
+        a, b = qsl[i], qsl[i + 1]
+        ql = b - a
+        if ql == 0:
+            continue
+        K = gather_kv(k_cache, block_tables[i], L).float().repeat_interleave(g, dim=1)  # [L,Hq,D]
+        V = gather_kv(v_cache, block_tables[i], L).float().repeat_interleave(g, dim=1)
+        Q = q[a:b].float()
+        s = torch.einsum("qhd,khd->hqk", Q, K) * scale
+        if softcap:
+            s = softcap * torch.tanh(s / softcap)
+        qpos = torch.arange(L - ql, L).unsqueeze(1)
+        kpos = torch.arange(L).unsqueeze(0)
+        mask = kpos > qpos
+        if sliding_window:
+            mask |= kpos <= qpos - sliding_window
+        s = s.masked_fill(mask.unsqueeze(0), float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        out[a:b] = torch.einsum("hqk,khd->qhd", p, V).to(q.dtype)
+    return out
+
+
+# ----------------------------------------------------------------------------- sampling
+def apply_penalties(logits: torch.Tensor, output_tokens: list, prompt_tokens: list,
+                    rep: torch.Tensor, freq: torch.Tensor, pres: torch.Tensor) -> torch.Tensor:
+    """Repetition penalty over prompt+output tokens (divide positive, multiply
+    negative logits), then frequency/presence penalties over output tokens."""
+    logits = logits.clone()
+    for i in range(logits.shape[0]):
+        seen = set(prompt_tokens[i]) | set(output_tokens[i])
+        if rep[i] != 1.0 and seen:
+            idx = torch.tensor(sorted(seen), dtype=torch.long)
+            v = logits[i, idx]
+            logits[i, idx] = torch.where(v > 0, v / rep[i], v * rep[i])
+        if output_tokens[i] and (freq[i] != 0.0 or pres[i] != 0.0):
+            cnt = torch.bincount(torch.tensor(output_tokens[i], dtype=torch.long),
+                                 minlength=logits.shape[1]).float()
+            logits[i] -= freq[i] * cnt + pres[i] * (cnt > 0).float()
+    return logits
+
+
+def topk_topp_minp_probs(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
+                         top_p: torch.Tensor, min_p: torch.Tensor) -> torch.Tensor:
+    """Filtered, renormalised probabilities per row (temperature > 0 rows)."""
+    x = logits.float() / temperature.clamp_min(1e-5).unsqueeze(1)
+    probs = torch.softmax(x, dim=-1)
+    V = x.shape[1]
+    sp, si = probs.sort(dim=-1, descending=True)
+    ranks = torch.arange(V).unsqueeze(0)
+    k = torch.where(top_k > 0, top_k, torch.full_like(top_k, V)).unsqueeze(1)
+    keep = ranks < k
+    cum = sp.cumsum(-1) - sp                       # mass strictly before this token
+    keep &= cum < top_p.unsqueeze(1)
+    keep &= sp >= (min_p.unsqueeze(1) * sp[:, :1])
+    keep[:, 0] = True
+    sp = torch.where(keep, sp, torch.zeros_like(sp))
+    out = torch.zeros_like(probs).scatter(1, si, sp)
+    return out / out.sum(-1, keepdim=True)
+
+
+def spec_verify_greedy(draft_tokens: torch.Tensor, target_argmax: torch.Tensor):
+    """draft [B,k], target_argmax [B,k+1] -> (accepted count [B], emitted tokens [B,k+1])."""
+    B, k = draft_tokens.shape
+    match = (draft_tokens == target_argmax[:, :k]).int()
+    acc = match.cumprod(dim=1).sum(dim=1)
+    out = torch.full((B, k + 1), -1, dtype=torch.long)
+    for b in range(B):
+        n = int(acc[b])
+        out[b, :n] = draft_tokens[b, :n]
+        out[b, n] = target_argmax[b, n]
+    return acc, out
+
+
+# ----------------------------------------------------------------------------- fp8
+FP8_E4M3_MAX = 448.0
+
+
+def quant_fp8_act(x: torch.Tensor, group: int = 128):
+    """1 x group activation quant: x [M, K] -> (q e4m3 [M,K], scales fp32 [M, K/group])."""
+    M, K = x.shape
+    xg = x.float().view(M, K // group, group)
+    amax = xg.abs().amax(-1).clamp_min(1e-12)
+    s = amax / FP8_E4M3_MAX
+    q = (xg / s.unsqueeze(-1)).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
+    return q.view(M, K), s
+
+
+def quant_fp8_weight(w: torch.Tensor, block: int = 128):
+    """128x128 block weight quant: w [N, K] -> (q [N,K] e4m3, scales fp32 [ceil(N/b), K/b])."""
+    N, K = w.shape
+    nb = (N + block - 1) // block
+    wp = torch.zeros(nb * block, K, dtype=torch.float32)
+    wp[:N] = w.float()
+    wb = wp.view(nb, block, K // block, block)
+    amax = wb.abs().amax(dim=(1, 3)).clamp_min(1e-12)
+    s = amax / FP8_E4M3_MAX
+    q = (wb / s[:, None, :, None]).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
+    return q.view(nb * block, K)[:N].contiguous(), s
+
+
+def fp8_block_gemm(xq, xs, wq, ws, block: int = 128):
+    """Dequantise-then-matmul oracle of the block-scaled fp8 GEMM."""
+    M, K = xq.shape
+    N = wq.shape[0]
+    x = xq.float().view(M, K // block, block) * xs.unsqueeze(-1)
+    nb = ws.shape[0]
+    wp = torch.zeros(nb * block, K)
+    wp[:N] = wq.float()
+    w = (wp.view(nb, block, K // block, block) * ws[:, None, :, None]).view(nb * block, K)[:N]
+    return x.view(M, K) @ w.t()
+
+
+# ----------------------------------------------------------------------------- moe
+def moe_topk_softmax(router_logits: torch.Tensor, k: int):
+    """Mixtral routing: top-k over softmax, weights renormalised over the k."""
+    p = torch.softmax(router_logits.float(), dim=-1)
+    w, idx = p.topk(k, dim=-1)
+    w = w / w.sum(-1, keepdim=True)
+    return w, idx
