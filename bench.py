@@ -1,0 +1,316 @@
+#!/usr/bin/env python
+"""Serving benchmark: output tokens/s of continuous-batched Llama-3-8B.
+
+Workload (synthetic requests, random-init N(0, 0.02) weights of the named
+architecture; no network for checkpoints or datasets):
+  * Llama-3-8B: 32 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128,
+    intermediate 14336, vocab 128256, RoPE theta 5e5; bf16 weights, bf16 KV.
+  * Requests with prompt lengths uniform in [128, 2048], output lengths
+    uniform in [64, 512], top-p 0.9 at temperature 0.7, Poisson arrivals
+    (1024 requests per GPU), served with continuous batching, paged KV
+    (block 16), chunked prefill, max 256 running sequences.
+
+One engine replica per GPU (data parallel; each rank serves its own request
+stream, so per-GPU work is fixed as N grows: weak scaling).  Per rank:
+  1. ramp: engine steps until the running batch is full (untimed)
+  2. W warm-up engine steps (untimed)
+  3. K timed engine steps, bracketed by a barrier + cuda synchronize and
+     timed with CUDA events on the engine's stream; MAX over ranks.
+  value = output tokens produced in the K steps summed over ranks / max time.
+  e2e: a separate run through the public `LLMEngine` API (add_request /
+     step) that serves a fresh 256-request set from submission to the last
+     token; every step copies its inputs from pinned host memory and reads
+     the sampled tokens back.
+The inputs (weights + KV working set) are far larger than the 126 MB L2, so
+no L2 flush is needed between steps.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+Multi-GPU: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+BASELINE_TOK_S = 32000.0   # published output tok/s at batch 256 (A100, Llama-2-7B)
+
+
+def reference_unavailable() -> str:
+    return ("reference is a Rust/cargo workspace (no setup.py/pyproject, pip install --target fails: "
+            "'not installable'); no cargo/rustc in this image, and its engine samples from all-zero "
+            "logits without calling a model (crates/rusteeze-engine/src/engine.rs:418-427)")
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_workload(n, seed, vocab, rate):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    plen = rng.integers(128, 2049, n)
+    olen = rng.integers(64, 513, n)
+    gaps = rng.exponential(1.0 / rate, n)
+    arrivals = np.cumsum(gaps)
+    prompts = [rng.integers(0, vocab, int(p)).tolist() for p in plen]
+    return prompts, olen.tolist(), arrivals.tolist()
+
+
+def make_engine(args, device):
+    from rusteeze_b200.config.config import Config
+    from rusteeze_b200.engine.llm_engine import LLMEngine
+    cfg = Config()
+    cfg.model.preset = args.model
+    cfg.model.device = device
+    cfg.model.dtype = "bfloat16"
+    cfg.model.seed = 0
+    if args.fp8:
+        from rusteeze_b200.config.config import QuantizationConfig
+        cfg.model.quantization = QuantizationConfig(method="fp8_block")
+    cfg.engine.max_num_seqs = args.max_seqs
+    cfg.engine.max_num_batched_tokens = args.max_batched_tokens
+    cfg.engine.enable_chunked_prefill = True
+    cfg.engine.gpu_memory_utilization = 0.88
+    cfg.engine.swap_space_gb = 0
+    cfg.engine.cuda_graph_max_batch = args.max_seqs
+    return LLMEngine(cfg)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="rusteeze", choices=["rusteeze", "reference"])
+    ap.add_argument("--model", default="llama-3-8b")
+    ap.add_argument("--requests", type=int, default=1024)
+    ap.add_argument("--rate", type=float, default=200.0, help="Poisson arrival rate per GPU (req/s)")
+    ap.add_argument("--max-seqs", type=int, default=256)
+    ap.add_argument("--max-batched-tokens", type=int, default=4096)
+    ap.add_argument("--e2e-requests", type=int, default=256)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--fp8", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": reference_unavailable(),
+                              "metric": "output_tokens_per_s", "n_gpus": args.gpus}))
+        return 0
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from rusteeze_b200 import ops
+    from rusteeze_b200.core.sampling_params import SamplingParams
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    device = f"cuda:{local}"
+    eng = make_engine(args, device)
+    V = eng.model_config.vocab_size
+    prompts, olens, arrivals = build_workload(args.requests, 1000 + rank, V, args.rate)
+    eng_stream = torch.cuda.current_stream()
+
+    # ---------------------------------------------------------------- steady-state serving
+    t0 = time.monotonic()
+    nxt = 0
+    req_ids = {}
+
+    def admit(now):
+        nonlocal nxt
+        while nxt < len(prompts) and arrivals[nxt] <= now:
+            sp = SamplingParams(temperature=0.7, top_p=0.9, max_tokens=int(olens[nxt]), ignore_eos=True)
+            r = eng.add_request(None, None, sp, prompts[nxt])
+            req_ids[r.request_id] = nxt
+            nxt += 1
+
+    def step():
+        admit(time.monotonic() - t0)
+        return eng.step()
+
+    # 1. ramp until the batch is full
+    ramp_steps = 0
+    while eng.scheduler.num_running < args.max_seqs and ramp_steps < 400:
+        step()
+        ramp_steps += 1
+        if nxt >= len(prompts) and not eng.has_unfinished_requests():
+            break
+    # 2. warm-up
+    for _ in range(args.warmup):
+        step()
+    # 3. timed
+    gen0 = eng.stats_counters["generation_tokens"]
+    launches0 = ops.launch_count()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(local)
+    clk.start()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(eng_stream)
+    ttfts, tpots = [], []
+    for _ in range(args.steps):
+        for out in step():
+            if out.finished and out.metrics is not None:
+                if out.metrics.ttft is not None:
+                    ttfts.append(out.metrics.ttft)
+                if out.metrics.tpot is not None:
+                    tpots.append(out.metrics.tpot)
+    ev1.record(eng_stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clk.stop()
+    ms = ev0.elapsed_time(ev1)
+    launches = ops.launch_count() - launches0
+    gen = eng.stats_counters["generation_tokens"] - gen0
+    status = int(ops.cuda_ext().status()[0])
+
+    t = torch.tensor([ms, float(gen), float(launches)], dtype=torch.float64, device=device)
+    if world > 1:
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = t.clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        ms_max, gen_sum, launches_sum = tmax[0].item(), tsum[1].item(), tsum[2].item()
+    else:
+        ms_max, gen_sum, launches_sum = ms, float(gen), float(launches)
+    value = gen_sum / (ms_max / 1000.0)
+
+    # ---------------------------------------------------------------- end-to-end through the public API
+    e2e = None
+    if not args.no_e2e:
+        # drain the steady-state run so the e2e run starts from an empty engine
+        for rid in list(eng.requests):
+            eng.abort_request(rid)
+        e_prompts, e_olens, _ = build_workload(args.e2e_requests, 5000 + rank, V, 1.0)
+        h2d0, d2h0, steps0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes, eng.stats_counters["steps"]
+        gen_e0 = eng.stats_counters["generation_tokens"]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for p, o in zip(e_prompts, e_olens):
+            pin = torch.tensor(p, dtype=torch.int64).pin_memory()      # prompts arrive in pinned host memory
+            eng.add_request(None, None, SamplingParams(temperature=0.7, top_p=0.9, max_tokens=int(o),
+                                                       ignore_eos=True), pin.tolist())
+        while eng.has_unfinished_requests():
+            eng.step()
+        torch.cuda.synchronize()
+        w1 = time.perf_counter()
+        if world > 1:
+            dist.barrier()
+        egen = eng.stats_counters["generation_tokens"] - gen_e0
+        esteps = max(1, eng.stats_counters["steps"] - steps0)
+        et = torch.tensor([w1 - w0, float(egen)], dtype=torch.float64, device=device)
+        if world > 1:
+            emax = et.clone()
+            dist.all_reduce(emax, op=dist.ReduceOp.MAX)
+            esum = et.clone()
+            dist.all_reduce(esum, op=dist.ReduceOp.SUM)
+            e_s, e_gen = emax[0].item(), esum[1].item()
+        else:
+            e_s, e_gen = et[0].item(), et[1].item()
+        e2e = {"value": e_gen / e_s, "unit": "output_tokens/s",
+               "h2d_bytes_per_step": int((eng.runner.h2d_bytes - h2d0) / esteps),
+               "d2h_bytes_per_step": int((eng.runner.d2h_bytes - d2h0) / esteps),
+               "requests": args.e2e_requests * world, "wall_s": round(e_s, 3)}
+
+    if rank == 0:
+        line = {
+            "metric": "output_tokens_per_s",
+            "value": round(value, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": round(value / BASELINE_TOK_S, 4),
+            "dtype": "fp8_block" if args.fp8 else "bf16",
+            "data": "synthetic requests, random-init N(0,0.02) weights",
+            "config": {"model": args.model, "global_batch": args.max_seqs * world,
+                       "seq_len": "prompt U[128,2048] + output U[64,512]",
+                       "parallelism": f"dp{world}" if world > 1 else "tp1",
+                       "workload": f"{args.requests} req/GPU Poisson {args.rate}/s, top_p 0.9 T 0.7, "
+                                   "continuous batching, paged KV block 16, chunked prefill "
+                                   f"{args.max_batched_tokens} tok/step",
+                       "l2": "working set (16 GB weights + KV) far exceeds the 126 MB L2; no flush",
+                       "ramp_steps": ramp_steps},
+            "ttft_p50_s": round(statistics.median(ttfts), 4) if ttfts else None,
+            "tpot_p50_s": round(statistics.median(tpots), 5) if tpots else None,
+            "clocks": clocks,
+            "gpu_launches": int(launches_sum),
+            "kernel_status": status,
+            "e2e": e2e,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

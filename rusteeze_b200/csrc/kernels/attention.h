@@ -1,0 +1,51 @@
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rz {
+
+struct DecodeAttnParams {
+  __nv_bfloat16* out;             // [seqs, Hq, D] rows of the output (row stride out_stride)
+  int64_t out_stride;
+  const __nv_bfloat16* q;         // decode query rows (row stride q_stride)
+  int64_t q_stride;
+  const __nv_bfloat16* k_cache;   // [blocks, Hkv, 16, D] with block_stride elements between blocks
+  const __nv_bfloat16* v_cache;
+  int64_t block_stride;
+  const int32_t* seq_lens;        // [seqs]
+  const int32_t* block_tables;    // [seqs, bt_stride]
+  int64_t bt_stride;
+  float* workspace;               // [seqs, Hq, splits, D+2] when num_splits > 1
+  int num_seqs, num_q_heads, num_kv_heads, head_dim, num_splits;
+  float scale;
+  int window;                     // sliding window (0 = none)
+  float softcap;                  // 0 = none
+  int* status;
+};
+
+struct PrefillAttnParams {
+  __nv_bfloat16* out;             // [T, Hq, D] (row stride out_stride)
+  int64_t out_stride;
+  const __nv_bfloat16* q;         // [T, Hq, D] (row stride q_stride)
+  int64_t q_stride;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  int64_t block_stride;
+  const int32_t* query_start_loc; // [S+1] over ALL sequences of the batch
+  const int32_t* seq_lens;        // [S]
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int seq_offset;                 // first prefill sequence index
+  int num_seqs;                   // prefill sequences
+  int max_q_len;
+  int num_q_heads, num_kv_heads, head_dim;
+  float scale;
+  int window;
+  float softcap;
+};
+
+int decode_attention_launch(const DecodeAttnParams& p, cudaStream_t st);
+int prefill_attention_launch(const PrefillAttnParams& p, cudaStream_t st);
+
+}  // namespace rz

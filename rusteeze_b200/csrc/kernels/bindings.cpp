@@ -1,0 +1,306 @@
+// torch bindings for the sm_100a kernels.  Each op validates shapes/dtypes,
+// launches on the current CUDA stream, and raises on a launch error.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "attention.h"
+#include "elementwise.h"
+#include "gemm_bf16.h"
+#include "gemm_fp8.h"
+#include "sampling.h"
+#include "comm.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bfloat16")
+#define CHECK_LAST(x) TORCH_CHECK((x).stride(-1) == 1, #x " must be contiguous in the last dim")
+
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+inline void check_rc(int rc, const char* what) {
+  TORCH_CHECK(rc == 0, what, " failed with code ", rc, " (", (rc > 0 ? cudaGetErrorString(static_cast<cudaError_t>(rc)) : "bad argument"), ")");
+}
+
+// One status word per device for the bounded device-side waits.
+torch::Tensor& status_tensor(int dev) {
+  static torch::Tensor t[64];
+  if (!t[dev].defined())
+    t[dev] = torch::zeros({4}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, dev));
+  return t[dev];
+}
+int* status_ptr() {
+  int dev;
+  cudaGetDevice(&dev);
+  return status_tensor(dev).data_ptr<int>();
+}
+
+void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps, double offset) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w);
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous(), "rms_norm: contiguous tensors required");
+  const int H = x.size(-1);
+  const int rows = x.numel() / H;
+  check_rc(rz::rms_norm_launch(reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                               reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), nullptr,
+                               reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), rows, H, eps, offset,
+                               cur_stream()),
+           "rms_norm");
+}
+
+void fused_add_rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor residual, torch::Tensor w, double eps,
+                        double offset) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(residual); CHECK_BF16(w);
+  TORCH_CHECK(x.is_contiguous() && residual.is_contiguous() && out.is_contiguous(), "contiguous tensors required");
+  const int H = x.size(-1);
+  const int rows = x.numel() / H;
+  check_rc(rz::rms_norm_launch(reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                               reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                               reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()),
+                               reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), rows, H, eps, offset,
+                               cur_stream()),
+           "fused_add_rms_norm");
+}
+
+void rope_and_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin, torch::Tensor k_cache,
+                    torch::Tensor v_cache, torch::Tensor slots, int64_t Hq, int64_t Hkv, int64_t D) {
+  CHECK_CUDA(qkv); CHECK_BF16(qkv); CHECK_LAST(qkv);
+  TORCH_CHECK(positions.scalar_type() == at::kLong && slots.scalar_type() == at::kLong, "int64 positions/slots");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "fp32 contiguous cos_sin");
+  TORCH_CHECK(k_cache.stride(0) == v_cache.stride(0), "k/v caches must share the block stride");
+  TORCH_CHECK(k_cache.stride(1) == 16 * D && k_cache.stride(2) == D, "cache page layout [blocks, Hkv, 16, D]");
+  check_rc(rz::rope_cache_launch(reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0),
+                                 positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(),
+                                 reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
+                                 reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), k_cache.stride(0),
+                                 slots.data_ptr<int64_t>(), qkv.size(0), Hq, Hkv, D, cur_stream()),
+           "rope_and_cache");
+}
+
+void act_mul(torch::Tensor out, torch::Tensor x, int64_t kind) {
+  CHECK_CUDA(x); CHECK_BF16(x);
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous(), "contiguous tensors required");
+  check_rc(rz::act_mul_launch(reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                              reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.size(0), x.size(1) / 2, kind,
+                              cur_stream()),
+           "act_mul");
+}
+
+void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                      torch::Tensor seq_lens, torch::Tensor block_tables, c10::optional<torch::Tensor> workspace,
+                      int64_t num_seqs, double scale, int64_t window, double softcap, int64_t num_splits) {
+  CHECK_CUDA(q); CHECK_BF16(q);
+  rz::DecodeAttnParams p{};
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.out_stride = out.stride(0);
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.q_stride = q.stride(0);
+  TORCH_CHECK(q.stride(1) == q.size(2) && q.stride(2) == 1, "q rows must hold [Hq, D] contiguously");
+  p.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  p.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  p.block_stride = k_cache.stride(0);
+  p.seq_lens = seq_lens.data_ptr<int32_t>();
+  p.block_tables = block_tables.data_ptr<int32_t>();
+  p.bt_stride = block_tables.stride(0);
+  p.num_seqs = num_seqs;
+  p.num_q_heads = q.size(1);
+  p.num_kv_heads = k_cache.size(1);
+  p.head_dim = q.size(2);
+  p.num_splits = num_splits;
+  p.scale = scale;
+  p.window = window;
+  p.softcap = softcap;
+  p.status = status_ptr();
+  if (num_splits > 1) {
+    TORCH_CHECK(workspace.has_value() &&
+                    workspace->numel() >= num_seqs * p.num_q_heads * num_splits * (p.head_dim + 2),
+                "decode workspace too small");
+    p.workspace = workspace->data_ptr<float>();
+  }
+  check_rc(rz::decode_attention_launch(p, cur_stream()), "decode_attention");
+}
+
+void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                       torch::Tensor qsl, torch::Tensor seq_lens, torch::Tensor block_tables, int64_t seq_offset,
+                       int64_t num_seqs, int64_t max_q_len, double scale, int64_t window, double softcap) {
+  CHECK_CUDA(q); CHECK_BF16(q);
+  rz::PrefillAttnParams p{};
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.out_stride = out.stride(0);
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.q_stride = q.stride(0);
+  p.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  p.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  p.block_stride = k_cache.stride(0);
+  p.query_start_loc = qsl.data_ptr<int32_t>();
+  p.seq_lens = seq_lens.data_ptr<int32_t>();
+  p.block_tables = block_tables.data_ptr<int32_t>();
+  p.bt_stride = block_tables.stride(0);
+  p.seq_offset = seq_offset;
+  p.num_seqs = num_seqs;
+  p.max_q_len = max_q_len;
+  p.num_q_heads = q.size(1);
+  p.num_kv_heads = k_cache.size(1);
+  p.head_dim = q.size(2);
+  p.scale = scale;
+  p.window = window;
+  p.softcap = softcap;
+  check_rc(rz::prefill_attention_launch(p, cur_stream()), "prefill_attention");
+}
+
+// ---------------------------------------------------------------- GEMM
+std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi) {
+  auto pl = rz::plan_gemm(M, N, K, epi);
+  return {pl.bn, pl.k_splits};
+}
+
+// Returns the number of kernels launched (1, or 2 with a split-K reduction).
+int64_t gemm_bf16_ex(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                     c10::optional<torch::Tensor> residual, int64_t epi, int64_t bn, int64_t k_splits) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_LAST(x); CHECK_LAST(w);
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K, "gemm: K mismatch");
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0, "gemm: K and N must be multiples of 8");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "gemm: row strides must be 16-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+              "gemm: operands must be 16-byte aligned");
+  if (epi == rz::kEpiSiluMul) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "silu epilogue: N % 128, out N/2");
+  if (bn <= 0 || k_splits <= 0) {
+    auto pl = rz::plan_gemm(M, N, K, epi);
+    bn = pl.bn;
+    k_splits = pl.k_splits;
+  }
+  rz::GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.k_splits = k_splits;
+  p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldd = out.stride(0);
+  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  p.residual = residual.has_value() ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
+  p.ldr = residual.has_value() ? residual->stride(0) : 0;
+  p.epi = epi;
+  p.status = status_ptr();
+  torch::Tensor ws;
+  if (k_splits > 1) {
+    ws = torch::empty({k_splits, M, N}, x.options().dtype(torch::kFloat32));
+    p.partial = ws.data_ptr<float>();
+  }
+  check_rc(rz::gemm_bf16_launch(p, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), bn, cur_stream()),
+           "gemm_bf16");
+  return k_splits > 1 ? 2 : 1;
+}
+
+int64_t gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                  c10::optional<torch::Tensor> residual) {
+  return gemm_bf16_ex(out, x, w, bias, residual, 0, 0, 0);
+}
+
+// ---------------------------------------------------------------- FP8
+void quant_fp8_act(torch::Tensor xq, torch::Tensor xs, torch::Tensor x) {
+  CHECK_CUDA(x); CHECK_BF16(x);
+  TORCH_CHECK(x.size(1) % 128 == 0, "K must be a multiple of 128");
+  check_rc(rz::quant_fp8_act_launch(xq.data_ptr(), xs.data_ptr<float>(),
+                                    reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.size(0), x.size(1),
+                                    x.stride(0), xs.stride(0), cur_stream()),
+           "quant_fp8_act");
+}
+
+void gemm_fp8_block(torch::Tensor out, torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws,
+                    c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual) {
+  const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
+  TORCH_CHECK(K % 128 == 0 && N % 16 == 0, "fp8 gemm: K % 128, N % 16");
+  rz::Fp8GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldd = out.stride(0);
+  p.a_scale = xs.data_ptr<float>();
+  p.a_scale_ld = xs.stride(0);
+  p.b_scale = ws.data_ptr<float>();
+  p.b_scale_ld = ws.stride(0);
+  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  p.residual = residual.has_value() ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
+  p.ldr = residual.has_value() ? residual->stride(0) : 0;
+  p.status = status_ptr();
+  check_rc(rz::gemm_fp8_launch(p, xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), cur_stream()),
+           "gemm_fp8_block");
+}
+
+// ---------------------------------------------------------------- sampling
+void argmax_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, bool want_lp) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "fp32 logits");
+  check_rc(rz::argmax_sample_launch(logits.data_ptr<float>(), logits.size(0), logits.size(1), logits.stride(0),
+                                    tok.data_ptr<int64_t>(), lp.data_ptr<float>(), want_lp, cur_stream()),
+           "argmax_sample");
+}
+
+void topk_topp_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, torch::Tensor temp,
+                      torch::Tensor topk, torch::Tensor topp, torch::Tensor minp, torch::Tensor seeds,
+                      torch::Tensor offsets, bool want_lp) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "fp32 logits");
+  (void)want_lp;
+  check_rc(rz::topk_topp_sample_launch(logits.data_ptr<float>(), logits.size(0), logits.size(1), logits.stride(0),
+                                       temp.data_ptr<float>(), topk.data_ptr<int32_t>(), topp.data_ptr<float>(),
+                                       minp.data_ptr<float>(), seeds.data_ptr<int64_t>(),
+                                       offsets.data_ptr<int64_t>(), tok.data_ptr<int64_t>(), lp.data_ptr<float>(),
+                                       cur_stream()),
+           "topk_topp_sample");
+}
+
+void spec_verify(torch::Tensor out_tokens, torch::Tensor n_acc, torch::Tensor target_logits,
+                 c10::optional<torch::Tensor> draft_logits, torch::Tensor draft_tokens, torch::Tensor temp,
+                 torch::Tensor seeds, torch::Tensor offsets) {
+  const int B = draft_tokens.size(0), k = draft_tokens.size(1);
+  const int V = target_logits.size(1);
+  TORCH_CHECK(target_logits.size(0) == B * (k + 1), "target logits must have B*(k+1) rows");
+  const float* dl = nullptr;
+  if (draft_logits.has_value()) {
+    TORCH_CHECK(draft_logits->stride(0) == target_logits.stride(0), "draft/target logits must share a row stride");
+    dl = draft_logits->data_ptr<float>();
+  }
+  check_rc(rz::spec_verify_launch(target_logits.data_ptr<float>(), dl, draft_tokens.data_ptr<int64_t>(), B, k, V,
+                                  target_logits.stride(0), temp.data_ptr<float>(), seeds.data_ptr<int64_t>(),
+                                  offsets.data_ptr<int64_t>(), out_tokens.data_ptr<int64_t>(),
+                                  n_acc.data_ptr<int32_t>(), cur_stream()),
+           "spec_verify");
+}
+
+void copy_blocks(torch::Tensor cache, torch::Tensor pairs) {
+  TORCH_CHECK(pairs.scalar_type() == at::kInt && pairs.is_cuda(), "int32 CUDA pairs");
+  const int64_t block_bytes = cache.stride(0) * cache.element_size();
+  check_rc(rz::copy_blocks_launch(cache.data_ptr(), pairs.data_ptr<int32_t>(), pairs.size(0), block_bytes,
+                                  cur_stream()),
+           "copy_blocks");
+}
+
+torch::Tensor read_status() {
+  int dev;
+  cudaGetDevice(&dev);
+  return status_tensor(dev);
+}
+
+}  // namespace
+
+void bind_comm(pybind11::module_& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "rusteeze_b200 sm_100a kernels";
+  m.def("rms_norm", &rms_norm);
+  m.def("fused_add_rms_norm", &fused_add_rms_norm);
+  m.def("rope_and_cache", &rope_and_cache);
+  m.def("act_mul", &act_mul);
+  m.def("decode_attention", &decode_attention);
+  m.def("prefill_attention", &prefill_attention);
+  m.def("gemm_plan", &gemm_plan);
+  m.def("gemm_bf16", &gemm_bf16);
+  m.def("gemm_bf16_ex", &gemm_bf16_ex);
+  m.def("quant_fp8_act", &quant_fp8_act);
+  m.def("gemm_fp8_block", &gemm_fp8_block);
+  m.def("argmax_sample", &argmax_sample);
+  m.def("topk_topp_sample", &topk_topp_sample);
+  m.def("spec_verify", &spec_verify);
+  m.def("copy_blocks", &copy_blocks);
+  m.def("status", &read_status);
+  bind_comm(m);
+}

@@ -1,0 +1,224 @@
+// Memory-bound elementwise kernels (one pass over HBM each, 16-byte vectors):
+//   rms_norm            y = x * rsqrt(mean(x^2) + eps) * (w + offset)
+//   fused_add_rms_norm  r += x ; y = rms_norm(r)          (residual updated in place)
+//   rope_and_cache      neox RoPE on q (in place) and k of the fused qkv row,
+//                       rotated k and raw v written to the paged cache slot
+//   act_mul             silu(gate) * up  |  gelu_tanh(gate) * up
+// Reference math: RMSNorm with fp32 accumulation (crates/rusteeze-model/src/
+// architectures/common.rs:33-45), rotate-half RoPE (common.rs:142-170),
+// SwiGLU (common.rs:354-361); the reference's KV write is a no-op
+// (crates/rusteeze-tensor/src/cache.rs:484-505).
+#include "common.cuh"
+#include "elementwise.h"
+
+namespace rz {
+
+__device__ __forceinline__ void ld8(const __nv_bfloat16* p, float* v) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void st8(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+template <int NV>  // 8-element vectors per thread
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  v = (threadIdx.x < nw) ? red[threadIdx.x] : 0.f;
+  if (w == 0) v = warp_sum(v);
+  if (threadIdx.x == 0) red[32] = v;
+  __syncthreads();
+  return red[32];
+}
+
+// One CTA per row; blockDim = H / (8*NV).
+template <int NV, bool ADD>
+__global__ void rms_norm_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
+                                __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w,
+                                int H, float eps, float offset) {
+  __shared__ float red[33];
+  const size_t row = blockIdx.x;
+  const int c0 = threadIdx.x * 8 * NV;
+  float v[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = c0 + j * 8;
+    if (c < H) {
+      ld8(x + row * H + c, v[j]);
+      if (ADD) {
+        float r[8];
+        ld8(residual + row * H + c, r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] += r[i];
+        st8(residual + row * H + c, v[j]);
+        // the stored (rounded) residual is what later layers see: normalise that
+        ld8(residual + row * H + c, v[j]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[j][i] * v[j][i];
+    }
+  }
+  const float inv = rsqrtf(block_sum<NV>(ss, red) / H + eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = c0 + j * 8;
+    if (c < H) {
+      float g[8], o[8];
+      ld8(w + c, g);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[j][i] * inv * (g[i] + offset);
+      st8(out + row * H + c, o);
+    }
+  }
+}
+
+int rms_norm_launch(__nv_bfloat16* out, const __nv_bfloat16* x, __nv_bfloat16* residual,
+                    const __nv_bfloat16* w, int rows, int H, float eps, float offset, cudaStream_t st) {
+  if (rows == 0) return 0;
+  if (H % 8) return -1;
+  const int vecs = H / 8;
+  // up to 1024 threads, each thread NV vectors
+  int nv = (vecs + 1023) / 1024;
+  int nv_t = nv <= 1 ? 1 : (nv <= 2 ? 2 : 4);
+  const int threads = (vecs + nv_t - 1) / nv_t;
+  const int tb = ((threads + 31) / 32) * 32;
+#define RZ_LAUNCH_NORM(NV)                                                                              \
+  if (residual)                                                                                         \
+    rms_norm_kernel<NV, true><<<rows, tb, 0, st>>>(out, x, residual, w, H, eps, offset);                \
+  else                                                                                                  \
+    rms_norm_kernel<NV, false><<<rows, tb, 0, st>>>(out, x, nullptr, w, H, eps, offset);
+  if (nv_t == 1) {
+    RZ_LAUNCH_NORM(1)
+  } else if (nv_t == 2) {
+    RZ_LAUNCH_NORM(2)
+  } else {
+    RZ_LAUNCH_NORM(4)
+  }
+#undef RZ_LAUNCH_NORM
+  return static_cast<int>(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------- RoPE + KV write
+// One CTA per token.  Work items: (Hq + Hkv) heads x D/2 rotation pairs, plus Hkv x D/8 v vectors.
+__global__ void rope_cache_kernel(__nv_bfloat16* __restrict__ qkv, int qkv_stride, const int64_t* __restrict__ pos,
+                                  const float* __restrict__ cos_sin, __nv_bfloat16* __restrict__ kc,
+                                  __nv_bfloat16* __restrict__ vc, int64_t block_stride,
+                                  const int64_t* __restrict__ slots, int Hq, int Hkv, int D) {
+  const int t = blockIdx.x;
+  __nv_bfloat16* row = qkv + static_cast<size_t>(t) * qkv_stride;
+  const int64_t p = pos[t];
+  const float* cs = cos_sin + p * D;
+  const int half = D / 2;
+  const int64_t slot = slots[t];
+  const int64_t blk = slot >= 0 ? slot / 16 : 0;
+  const int off = slot >= 0 ? static_cast<int>(slot % 16) : 0;
+  const int nrot = (Hq + Hkv) * half;
+  for (int i = threadIdx.x; i < nrot; i += blockDim.x) {
+    const int h = i / half, j = i % half;
+    __nv_bfloat16* base = row + h * D;
+    const float x1 = bf2f(base[j]), x2 = bf2f(base[j + half]);
+    const float c = cs[j], s = cs[half + j];
+    const float y1 = x1 * c - x2 * s, y2 = x2 * c + x1 * s;
+    if (h < Hq) {
+      base[j] = f2bf(y1);
+      base[j + half] = f2bf(y2);
+    } else if (slot >= 0) {
+      const int kh = h - Hq;
+      __nv_bfloat16* dst = kc + blk * block_stride + (static_cast<int64_t>(kh) * 16 + off) * D;
+      dst[j] = f2bf(y1);
+      dst[j + half] = f2bf(y2);
+    }
+  }
+  if (slot >= 0) {
+    const int nv = Hkv * D / 8;
+    const __nv_bfloat16* vsrc = row + (Hq + Hkv) * D;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+      const int h = (i * 8) / D, d = (i * 8) % D;
+      *reinterpret_cast<uint4*>(vc + blk * block_stride + (static_cast<int64_t>(h) * 16 + off) * D + d) =
+          *reinterpret_cast<const uint4*>(vsrc + h * D + d);
+    }
+  }
+}
+
+int rope_cache_launch(__nv_bfloat16* qkv, int qkv_stride, const int64_t* pos, const float* cos_sin,
+                      __nv_bfloat16* kc, __nv_bfloat16* vc, int64_t block_stride, const int64_t* slots, int T,
+                      int Hq, int Hkv, int D, cudaStream_t st) {
+  if (T == 0) return 0;
+  const int work = (Hq + Hkv) * D / 2;
+  const int threads = work >= 512 ? 512 : ((work + 31) / 32) * 32;
+  rope_cache_kernel<<<T, threads, 0, st>>>(qkv, qkv_stride, pos, cos_sin, kc, vc, block_stride, slots, Hq, Hkv, D);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------- act * mul
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  return 0.5f * x * (1.f + tanhf(k0 * (x + 0.044715f * x * x * x)));
+}
+
+template <int KIND>
+__global__ void act_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x, int I,
+                               long total_vec) {
+  const long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x;
+  if (i >= total_vec) return;
+  const int vpr = I / 8;
+  const long r = i / vpr;
+  const int c = static_cast<int>(i % vpr) * 8;
+  float g[8], u[8], o[8];
+  ld8(x + r * 2 * I + c, g);
+  ld8(x + r * 2 * I + I + c, u);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float a = KIND == 0 ? g[k] / (1.f + __expf(-g[k])) : gelu_tanh(g[k]);
+    o[k] = a * u[k];
+  }
+  st8(out + r * I + c, o);
+}
+
+int act_mul_launch(__nv_bfloat16* out, const __nv_bfloat16* x, int rows, int I, int kind, cudaStream_t st) {
+  if (rows == 0) return 0;
+  if (I % 8) return -1;
+  const long total = static_cast<long>(rows) * (I / 8);
+  const int tb = 256;
+  const int grid = static_cast<int>((total + tb - 1) / tb);
+  if (kind == 0)
+    act_mul_kernel<0><<<grid, tb, 0, st>>>(out, x, I, total);
+  else
+    act_mul_kernel<1><<<grid, tb, 0, st>>>(out, x, I, total);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------- KV block copy
+// Copies whole KV blocks (all layers) src -> dst inside one cache tensor (copy-on-write).
+__global__ void copy_blocks_kernel(uint4* __restrict__ cache, const int32_t* __restrict__ pairs, int64_t vec_per_block) {
+  const int b = blockIdx.y;
+  const int64_t s = pairs[2 * b], d = pairs[2 * b + 1];
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < vec_per_block;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    cache[d * vec_per_block + i] = cache[s * vec_per_block + i];
+}
+
+int copy_blocks_launch(void* cache, const int32_t* pairs, int npairs, int64_t block_bytes, cudaStream_t st) {
+  if (npairs == 0) return 0;
+  if (block_bytes % 16) return -1;
+  dim3 grid(64, npairs);
+  copy_blocks_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<uint4*>(cache), pairs, block_bytes / 16);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace rz

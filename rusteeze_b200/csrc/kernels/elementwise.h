@@ -1,0 +1,14 @@
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rz {
+int rms_norm_launch(__nv_bfloat16* out, const __nv_bfloat16* x, __nv_bfloat16* residual, const __nv_bfloat16* w,
+                    int rows, int H, float eps, float offset, cudaStream_t st);
+int rope_cache_launch(__nv_bfloat16* qkv, int qkv_stride, const int64_t* pos, const float* cos_sin,
+                      __nv_bfloat16* kc, __nv_bfloat16* vc, int64_t block_stride, const int64_t* slots, int T,
+                      int Hq, int Hkv, int D, cudaStream_t st);
+int act_mul_launch(__nv_bfloat16* out, const __nv_bfloat16* x, int rows, int I, int kind, cudaStream_t st);
+int copy_blocks_launch(void* cache, const int32_t* pairs, int npairs, int64_t block_bytes, cudaStream_t st);
+}  // namespace rz

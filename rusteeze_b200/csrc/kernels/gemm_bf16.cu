@@ -1,0 +1,437 @@
+// bf16 GEMM on 5th-generation tensor cores: D[M,N] = A[M,K] * B[N,K]^T
+// (A = activations, B = nn.Linear-layout weights, both K-major).
+//
+// Structure (one persistent CTA per SM, 192 threads, warp-specialised):
+//   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage into a
+//               STAGES-deep shared-memory ring (128-byte swizzle), no cluster
+//               multicast (each CTA loads its own tiles; reuse comes from L2).
+//   warp 1      allocates TMEM (2 x BN fp32 columns: double-buffered
+//               accumulator) and issues tcgen05.mma (M=128, N=BN, K=16) from
+//               one thread; tcgen05.commit releases smem stages and signals
+//               a finished accumulator.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (each thread owns
+//               one accumulator row = one TMEM lane), add bias / residual,
+//               optional SiLU(gate)*up on interleaved gate/up weight rows,
+//               convert to bf16 and store; overlaps the next tile's MMAs.
+// Work units are (m tile, n tile, k split); m varies fastest so CTAs of one
+// wave share the same weight tile through L2.  With k_splits > 1 the
+// epilogue writes fp32 partials to a workspace and `gemm_splitk_reduce`
+// finishes them (small-M decode GEMMs need the extra parallelism to stream
+// weights from all 148 SMs).
+//
+// Every mbarrier wait is bounded (common.cuh); a timeout records a status
+// code and the CTA drains and exits.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm_bf16.h"
+
+namespace rz {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // one 128-byte swizzle atom of bf16
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float* v) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(dst) = u;
+}
+
+__device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* src, float* v) {
+  uint4 u = *reinterpret_cast<const uint4*>(src);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      GemmParams p) {
+  using C = GemmCfg<BN>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (base & 1023)) & 1023);
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + S * C::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_units = p.m_tiles * p.n_tiles * p.k_splits;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int ks = u % p.k_splits;
+        const int t = u / p.k_splits;
+        const int mb = t % p.m_tiles;
+        const int nb = t / p.m_tiles;
+        const int kb0 = ks * p.kb_per_split;
+        const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, p.status, kGemmProducerTimeout)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          tma_load_2d(smA + s * C::kABytes, &tmA, &full[s], kb * kBK, mb * kBM);
+          tma_load_2d(smB + s * C::kBBytes, &tmB, &full[s], kb * kBK, nb * BN);
+          if (++s == S) { s = 0; ph ^= 1; }
+        }
+      }
+      // drain: wait until the MMA warp consumed every stage we filled, so no
+      // TMA write lands in shared memory after the CTA exits
+      for (int i = 0; i < S && ok; ++i) {
+        if (!mbar_wait(&empty[s], ph ^ 1, p.status, kGemmProducerTimeout)) break;
+        if (++s == S) { s = 0; ph ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int ks = u % p.k_splits;
+        const int kb0 = ks * p.kb_per_split;
+        const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+        if (!mbar_wait(&tempty[acc], aph ^ 1, p.status, kGemmMmaTimeout)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t dtm = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[s], ph, p.status, kGemmMmaTimeout)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t da = smem_desc_k_sw128(smem_u32(smA + s * C::kABytes));
+          const uint64_t db = smem_desc_k_sw128(smem_u32(smB + s * C::kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // +32 bytes along K inside the 128-byte swizzle atom = +2 in the >>4 address field
+            umma_f16(dtm, da + 2 * k, db + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+          if (++s == S) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; aph ^= 1; }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      const int ks = u % p.k_splits;
+      const int t = u / p.k_splits;
+      const int mb = t % p.m_tiles;
+      const int nb = t / p.m_tiles;
+      if (!mbar_wait(&tfull[acc], aph, p.status, kGemmEpilogueTimeout)) break;
+      tc_fence_after();
+      const int row = mb * kBM + row_in_tile;
+      const bool row_ok = row < p.M;
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      if (p.k_splits > 1) {
+        float* dst = p.partial + (static_cast<size_t>(ks) * p.M + row) * p.N;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tacc + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = nb * BN + c * 32;
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              if (col0 + j < p.N) {
+                float4 f = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                       __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                *reinterpret_cast<float4*>(dst + col0 + j) = f;
+              }
+            }
+          }
+        }
+      } else if (p.epi == kEpiSiluMul) {
+        // tile columns: [gate 64 | up 64] pairs -> BN/2 outputs
+#pragma unroll 1
+        for (int pr = 0; pr < BN / 128; ++pr) {
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            uint32_t g[32], v[32];
+            tmem_ld_32x32b_x32(tacc + pr * 128 + h * 32, g);
+            tmem_ld_32x32b_x32(tacc + pr * 128 + 64 + h * 32, v);
+            tmem_ld_wait();
+            const int gcol = nb * BN + pr * 128 + h * 32;
+            const int ocol = nb * (BN / 2) + pr * 64 + h * 32;
+            if (row_ok && gcol < p.N) {
+              float o[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float a = __uint_as_float(g[j]);
+                float b = __uint_as_float(v[j]);
+                if (p.bias) {
+                  a += bf2f(p.bias[gcol + j]);
+                  b += bf2f(p.bias[gcol + 64 + j]);
+                }
+                o[j] = silu(a) * b;
+              }
+              __nv_bfloat16* dst = p.D + static_cast<size_t>(row) * p.ldd + ocol;
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, o + j);
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tacc + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = nb * BN + c * 32;
+          if (row_ok) {
+            __nv_bfloat16* dst = p.D + static_cast<size_t>(row) * p.ldd;
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              const int col = col0 + j;
+              if (col < p.N) {
+                float o[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[j + i]);
+                if (p.bias) {
+                  float b[8];
+                  load_bf16x8(p.bias + col, b);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) o[i] += b[i];
+                }
+                if (p.residual) {
+                  float b[8];
+                  load_bf16x8(p.residual + static_cast<size_t>(row) * p.ldr + col, b);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) o[i] += b[i];
+                }
+                store_bf16x8(dst + col, o);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; aph ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
+}
+
+// Sums k-split partials and applies the epilogue.  One thread per 8 output columns.
+__global__ void gemm_splitk_reduce(GemmParams p) {
+  const int ncols_out = p.epi == kEpiSiluMul ? p.N / 2 : p.N;
+  const int vec_per_row = ncols_out / 8;
+  const long idx = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x;
+  if (idx >= static_cast<long>(p.M) * vec_per_row) return;
+  const int row = static_cast<int>(idx / vec_per_row);
+  const int oc = static_cast<int>(idx % vec_per_row) * 8;
+  float o[8];
+  if (p.epi == kEpiSiluMul) {
+    // output col oc -> gate col (oc/64)*128 + oc%64, up col +64
+    const int gc = (oc / 64) * 128 + (oc % 64);
+    float g[8] = {0}, v[8] = {0};
+    for (int k = 0; k < p.k_splits; ++k) {
+      const float* src = p.partial + (static_cast<size_t>(k) * p.M + row) * p.N;
+      float4 a0 = *reinterpret_cast<const float4*>(src + gc);
+      float4 a1 = *reinterpret_cast<const float4*>(src + gc + 4);
+      float4 b0 = *reinterpret_cast<const float4*>(src + gc + 64);
+      float4 b1 = *reinterpret_cast<const float4*>(src + gc + 68);
+      g[0] += a0.x; g[1] += a0.y; g[2] += a0.z; g[3] += a0.w;
+      g[4] += a1.x; g[5] += a1.y; g[6] += a1.z; g[7] += a1.w;
+      v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+      v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+    }
+    for (int i = 0; i < 8; ++i) {
+      if (p.bias) {
+        g[i] += bf2f(p.bias[gc + i]);
+        v[i] += bf2f(p.bias[gc + 64 + i]);
+      }
+      o[i] = silu(g[i]) * v[i];
+    }
+  } else {
+    for (int i = 0; i < 8; ++i) o[i] = 0.f;
+    for (int k = 0; k < p.k_splits; ++k) {
+      const float* src = p.partial + (static_cast<size_t>(k) * p.M + row) * p.N + oc;
+      float4 a0 = *reinterpret_cast<const float4*>(src);
+      float4 a1 = *reinterpret_cast<const float4*>(src + 4);
+      o[0] += a0.x; o[1] += a0.y; o[2] += a0.z; o[3] += a0.w;
+      o[4] += a1.x; o[5] += a1.y; o[6] += a1.z; o[7] += a1.w;
+    }
+    if (p.bias) {
+      float b[8];
+      load_bf16x8(p.bias + oc, b);
+      for (int i = 0; i < 8; ++i) o[i] += b[i];
+    }
+    if (p.residual) {
+      float b[8];
+      load_bf16x8(p.residual + static_cast<size_t>(row) * p.ldr + oc, b);
+      for (int i = 0; i < 8; ++i) o[i] += b[i];
+    }
+  }
+  store_bf16x8(p.D + static_cast<size_t>(row) * p.ldd + oc, o);
+}
+
+// ---------------------------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D K-major tensor map: rows x cols(=K) elements, row stride ld elements,
+// box = box_rows x 64 (one 128-byte swizzle atom per row for bf16).
+int make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int elem_bytes, int64_t rows,
+                 int64_t cols, int64_t ld, int box_rows, int box_cols) {
+  auto fn = get_encode_fn();
+  if (!fn) return -1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN>
+static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B, int ldb, cudaStream_t st) {
+  using C = GemmCfg<BN>;
+  CUtensorMap ta, tb;
+  if (make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p0.M, p0.K, lda, kBM, kBK)) return -2;
+  if (make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p0.N, p0.K, ldb, BN, kBK)) return -3;
+  GemmParams p = p0;
+  p.m_tiles = (p.M + kBM - 1) / kBM;
+  p.n_tiles = (p.N + BN - 1) / BN;
+  const int units = p.m_tiles * p.n_tiles * p.k_splits;
+  const int grid = units < num_sms() ? units : num_sms();
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_bf16_tcgen05<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    attr_set = true;
+  }
+  gemm_bf16_tcgen05<BN><<<grid, 192, C::kSmemBytes, st>>>(ta, tb, p);
+  if (p.k_splits > 1) {
+    const int ncols_out = p.epi == kEpiSiluMul ? p.N / 2 : p.N;
+    const long threads = static_cast<long>(p.M) * (ncols_out / 8);
+    gemm_splitk_reduce<<<static_cast<int>((threads + 255) / 256), 256, 0, st>>>(p);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+GemmPlan plan_gemm(int M, int N, int K, int epi) {
+  // Pick (BN, k_splits) minimising an estimate of waves x per-unit cost.
+  const int sms = num_sms();
+  const int kblocks = (K + kBK - 1) / kBK;
+  GemmPlan best{256, 1, 1e30};
+  const int bns[3] = {256, 128, 64};
+  for (int bn : bns) {
+    if (epi == kEpiSiluMul && bn < 128) continue;
+    const int mt = (M + kBM - 1) / kBM;
+    const int nt = (N + bn - 1) / bn;
+    for (int ks = 1; ks <= 16; ks *= 2) {
+      if (ks > 1 && kblocks / ks < 4) break;
+      const int units = mt * nt * ks;
+      const int waves = (units + sms - 1) / sms;
+      const double kb = static_cast<double>((kblocks + ks - 1) / ks);
+      // per unit: MMA time ~ 128*bn*64*2 flop per k-block at ~8.2 TFLOP/s/SM; load time ~ (128+bn)*128 B per
+      // k-block at ~40 GB/s/SM (HBM share) -- whichever dominates
+      const double t_mma = kb * (128.0 * bn * 64 * 2) / 8.2e12;
+      const double t_mem = kb * ((128.0 + bn) * 128) / 43e9;
+      double cost = waves * (t_mma > t_mem ? t_mma : t_mem) + 2.5e-6;
+      if (ks > 1) cost += (static_cast<double>(ks) * M * N * 4 * 2) / 6.0e12 + 3e-6;  // partial traffic + launch
+      if (cost < best.cost * 0.97) best = GemmPlan{bn, ks, cost};
+    }
+  }
+  return best;
+}
+
+int gemm_bf16_launch(const GemmParams& p_in, const void* A, int lda, const void* B, int ldb, int bn,
+                     cudaStream_t st) {
+  GemmParams p = p_in;
+  p.k_blocks = (p.K + kBK - 1) / kBK;
+  p.kb_per_split = (p.k_blocks + p.k_splits - 1) / p.k_splits;
+  p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  switch (bn) {
+    case 256: return launch_bn<256>(p, A, lda, B, ldb, st);
+    case 128: return launch_bn<128>(p, A, lda, B, ldb, st);
+    case 64: return launch_bn<64>(p, A, lda, B, ldb, st);
+    default: return -1;
+  }
+}
+
+}  // namespace rz

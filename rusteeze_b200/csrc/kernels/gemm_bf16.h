@@ -1,0 +1,41 @@
+// Host-visible declarations of the tcgen05 GEMM launcher.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rz {
+
+enum GemmEpilogue : int { kEpiNone = 0, kEpiSiluMul = 1 };
+
+struct GemmParams {
+  int M, N, K;
+  int k_splits;        // >= 1
+  int k_blocks;        // filled by the launcher
+  int kb_per_split;    // filled by the launcher
+  int m_tiles, n_tiles;
+  __nv_bfloat16* D;    // output, leading dimension ldd
+  int ldd;
+  float* partial;      // [k_splits][M][N] fp32 workspace when k_splits > 1
+  const __nv_bfloat16* bias;      // [N] or nullptr
+  const __nv_bfloat16* residual;  // [M][ldr] or nullptr (kEpiNone only)
+  int ldr;
+  int epi;
+  int* status;
+};
+
+struct GemmPlan {
+  int bn;
+  int k_splits;
+  double cost;
+};
+
+GemmPlan plan_gemm(int M, int N, int K, int epi);
+int gemm_bf16_launch(const GemmParams& p, const void* A, int lda, const void* B, int ldb, int bn,
+                     cudaStream_t stream);
+int make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int elem_bytes, int64_t rows,
+                 int64_t cols, int64_t ld, int box_rows, int box_cols);
+int num_sms();
+
+}  // namespace rz

@@ -85,6 +85,8 @@ class LLMEngine:
             if mc.quantization is not None and mc.quantization.method != "none":
                 from rusteeze_b200.models.quant import quantize_model_fp8
                 quantize_model_fp8(model)
+        if self.device.startswith("cuda"):
+            model.prepare_for_gpu()
         self.model = model
         self.tokenizer = tokenizer or load_tokenizer(mc.tokenizer or mc.path, self.model_config.vocab_size)
         self.model_name = mc.served_name()
@@ -208,9 +210,6 @@ class LLMEngine:
             return self.spec.step()
         so = self.scheduler.schedule()
         outputs: List[RequestOutput] = []
-        # sequences ignored by the scheduler (too long)
-        for s in list(self.seq_to_request):
-            pass
         if so.is_empty():
             return self._collect_ignored()
         rows, owners = self._sample_rows(so)
@@ -258,9 +257,8 @@ class LLMEngine:
             s = ss.seq
             s.num_computed = ss.ctx + ss.num_new
             self.bm.commit(s.seq_id, s.tokens_np(), s.num_computed)
-            if ss.ctx == 0 or ss.ctx == s.num_cached:
-                self.stats_counters["prompt_tokens"] += 0
-            self.stats_counters["prompt_tokens"] += ss.num_new if s.num_generated == 0 else 0
+            if s.num_generated == 0:
+                self.stats_counters["prompt_tokens"] += ss.num_new
         i = 0
         for ss, k in owners:
             s = ss.seq

@@ -102,7 +102,9 @@ class ModelRunner:
         self.graphs: Dict[int, Tuple[torch.cuda.CUDAGraph, torch.Tensor]] = {}
         self.graph_pool = None
         self.seed = seed
-        self.step_times: List[float] = []
+        self.graph_launches: Dict[int, int] = {}
+        self.h2d_bytes = 0      # host->device bytes staged per step (cumulative)
+        self.d2h_bytes = 0      # device->host bytes read back (cumulative)
 
     # ------------------------------------------------------------------ cache ops
     @torch.no_grad()
@@ -149,6 +151,7 @@ class ModelRunner:
         max_q = max((s.num_new for s in so.prefills), default=1)
         max_s = int(self.h_seq_lens[:S].max()) if S else 0
         nb = non_blocking = self.is_cuda
+        self.h2d_bytes += 3 * 8 * T + 4 * (S + 1) + 4 * S + 4 * S * self.max_blocks
         self.d_input_ids[:T].copy_(self.h_input_ids[:T], non_blocking=nb)
         self.d_positions[:T].copy_(self.h_positions[:T], non_blocking=nb)
         self.d_slots[:T].copy_(self.h_slots[:T], non_blocking=nb)
@@ -192,8 +195,11 @@ class ModelRunner:
                     self._decode_forward(B, meta)
             torch.cuda.current_stream().wait_stream(stream)
             g = torch.cuda.CUDAGraph()
+            from rusteeze_b200 import ops as _ops
+            n0 = _ops.launch_count()
             with torch.cuda.graph(g, pool=self.graph_pool, stream=stream):
                 out = self._decode_forward(B, meta)
+            self.graph_launches[B] = _ops.launch_count() - n0
             self.graphs[B] = (g, out, meta)
         torch.cuda.synchronize()
 
@@ -220,7 +226,10 @@ class ModelRunner:
             self.copy_blocks(so.blocks_to_copy)
         meta, T, S, sample_rows = self.prepare(so, bm)
         logits = self.forward_logits(meta, T, S, sample_rows, pure_decode=not so.prefills)
-        return self.sampler.sample(logits, rows)
+        res = self.sampler.sample(logits, rows)
+        self.h2d_bytes += self.sampler.last_h2d_bytes
+        self.d2h_bytes += self.sampler.last_d2h_bytes
+        return res
 
     def forward_logits(self, meta: AttentionMetadata, T: int, S: int, sample_rows: List[int],
                        pure_decode: bool) -> torch.Tensor:
@@ -233,6 +242,8 @@ class ModelRunner:
                 self.d_positions[S:B].fill_(0)
             g, out, _ = self.graphs[B]
             g.replay()
+            from rusteeze_b200 import ops as _ops
+            _ops.add_launches(self.graph_launches.get(B, 0))
             idx = torch.tensor(sample_rows, dtype=torch.long)
             return out.index_select(0, idx.to(out.device, non_blocking=True))
         h = self.model(self.d_input_ids[:T], self.d_positions[:T], meta, self.kv_layers)

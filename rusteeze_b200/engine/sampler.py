@@ -60,6 +60,8 @@ class Sampler:
     def __init__(self, vocab_size: int):
         self.vocab_size = vocab_size
         self._param_cache: Dict[Tuple, Tuple[torch.Tensor, ...]] = {}
+        self.last_h2d_bytes = 0
+        self.last_d2h_bytes = 0
 
     # ------------------------------------------------------------------ pre-processing
     def _process_logits(self, logits: torch.Tensor, rows: List[SampleRow]) -> torch.Tensor:
@@ -94,6 +96,8 @@ class Sampler:
         """logits: fp32 [R, V] (device or host), one row per SampleRow."""
         R = logits.shape[0]
         assert R == len(rows)
+        self.last_h2d_bytes = 0
+        self.last_d2h_bytes = 0
         logits = self._process_logits(logits, rows)
         host_rows = [i for i, r in enumerate(rows) if r.params.needs_host_sampling()]
         tokens: List[int] = [0] * R
@@ -143,8 +147,10 @@ class Sampler:
             seeds = torch.tensor([r.seed & ((1 << 63) - 1) for r in rows], dtype=torch.int64)
             offs = torch.tensor([r.offset for r in rows], dtype=torch.int64)
             packed = [x.pin_memory().to(dev, non_blocking=True) for x in (temp, top_k, top_p, min_p, seeds, offs)]
+            self.last_h2d_bytes += sum(x.numel() * x.element_size() for x in packed)
             toks, lp = ops.sample(logits, *packed, greedy_all=False, want_logprobs=want_lp)
         both = torch.stack([toks.double(), lp.double()]).cpu()
+        self.last_d2h_bytes += both.numel() * 8
         return [int(x) for x in both[0].tolist()], both[1].tolist()
 
 

@@ -163,9 +163,25 @@ class DecoderLM(nn.Module):
         return h
 
     def _mlp(self, L, h: torch.Tensor) -> torch.Tensor:
-        gu = ops.linear(h, L.gate_up)
-        a = ops.silu_mul(gu) if self.act == "silu" else ops.gelu_tanh_mul(gu)
+        if getattr(L, "gate_up_il", None) is not None and h.is_cuda:
+            a = ops.linear_silu_mul(h, L.gate_up_il)      # SiLU(gate)*up fused in the GEMM epilogue
+        else:
+            gu = ops.linear(h, L.gate_up)
+            a = ops.silu_mul(gu) if self.act == "silu" else ops.gelu_tanh_mul(gu)
         return self.tp.row_parallel_linear(a, L.down)
+
+    @torch.no_grad()
+    def prepare_for_gpu(self) -> None:
+        """Re-lays weights for the GPU kernels: gate/up rows interleaved in
+        64-row blocks for the fused SiLU epilogue (the [gate | up] copy is
+        dropped to save HBM)."""
+        if not self.device.type == "cuda" or self.cfg.is_moe or self.act != "silu":
+            return
+        if self.inter % 64:
+            return
+        for L in self.layers:
+            L.gate_up_il = ops.interleave_gate_up(L.gate_up)
+            L.gate_up = nn.Parameter(torch.empty(0, dtype=self.dtype, device=self.device), requires_grad=False)
 
     def _moe(self, L, h: torch.Tensor) -> torch.Tensor:
         if self.moe_impl is not None:

@@ -315,3 +315,16 @@ def build_model(cfg: ModelConfig, *, dtype=torch.bfloat16, device="cpu", tp=None
     else:
         init_random(model, seed)
     return model.eval()
+
+
+@torch.no_grad()
+def to_cpu_fp32(model: DecoderLM) -> DecoderLM:
+    """An fp32 CPU copy of a (possibly GPU-prepared) model with identical weights."""
+    from rusteeze_b200.ops import deinterleave_gate_up
+    out = DecoderLM(model.cfg, dtype=torch.float32, device="cpu", tp=None)
+    for name, _shape, _slicer, _kind in logical_params(out):
+        src = _param(model, name)
+        if name.endswith("gate_up") and src.numel() == 0:
+            src = deinterleave_gate_up(_param(model, name[:-len("gate_up")] + "gate_up_il"))
+        _param(out, name).copy_(src.float().cpu())
+    return out.eval()

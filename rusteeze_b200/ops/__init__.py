@@ -49,12 +49,26 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+# Number of this package's kernels launched so far (graph replays add the
+# count recorded at capture time).  Benchmarks report the delta.
+_LAUNCHES = [0]
+
+
+def launch_count() -> int:
+    return _LAUNCHES[0]
+
+
+def add_launches(n: int) -> None:
+    _LAUNCHES[0] += n
+
+
 # ----------------------------------------------------------------------------- norms
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, offset: float = 0.0) -> torch.Tensor:
     if not x.is_cuda:
         return ref.rms_norm(x, w, eps, offset)
     out = torch.empty_like(x)
     cuda_ext().rms_norm(out, x, w, float(eps), float(offset))
+    _LAUNCHES[0] += 1
     return out
 
 
@@ -67,6 +81,7 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
         return out, residual
     out = torch.empty_like(x)
     cuda_ext().fused_add_rms_norm(out, x, residual, w, float(eps), float(offset))
+    _LAUNCHES[0] += 1
     return out, residual
 
 
@@ -90,6 +105,7 @@ def rope_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Te
         return q
     cuda_ext().rope_and_cache(qkv, positions, cos_sin, k_cache, v_cache, slot_mapping,
                               num_q_heads, num_kv_heads, head_dim)
+    _LAUNCHES[0] += 1
     return qkv[:, :qs].view(T, num_q_heads, head_dim)
 
 
@@ -99,6 +115,7 @@ def silu_mul(x: torch.Tensor) -> torch.Tensor:
         return ref.silu_mul(x)
     out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
     cuda_ext().act_mul(out, x, 0)
+    _LAUNCHES[0] += 1
     return out
 
 
@@ -107,6 +124,7 @@ def gelu_tanh_mul(x: torch.Tensor) -> torch.Tensor:
         return ref.gelu_tanh_mul(x)
     out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
     cuda_ext().act_mul(out, x, 1)
+    _LAUNCHES[0] += 1
     return out
 
 
@@ -127,10 +145,12 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         C.decode_attention(out, q, k_cache, v_cache, meta.seq_lens, meta.block_tables,
                            meta.decode_workspace, nd, float(scale), win, cap,
                            meta.decode_num_splits)
+        _LAUNCHES[0] += 2 if meta.decode_num_splits > 1 else 1
     if meta.num_seqs > nd:
         C.prefill_attention(out, q, k_cache, v_cache, meta.query_start_loc, meta.seq_lens,
                             meta.block_tables, nd, meta.num_seqs - nd, meta.max_query_len,
                             float(scale), win, cap)
+        _LAUNCHES[0] += 1
     return out
 
 
@@ -154,7 +174,34 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
         out = torch.empty(M, N, dtype=x.dtype, device=x.device)
     if M == 0:
         return out
-    cuda_ext().gemm_bf16(out, x, w, bias, residual)
+    _LAUNCHES[0] += cuda_ext().gemm_bf16(out, x, w, bias, residual)
+    return out
+
+
+def interleave_gate_up(w: torch.Tensor, block: int = 64) -> torch.Tensor:
+    """[gate(I) | up(I)] rows -> [g0:64 | u0:64 | g64:128 | u64:128 | ...], the
+    layout the GEMM's SiLU(gate)*up epilogue consumes tile by tile."""
+    two_i, K = w.shape
+    I = two_i // 2
+    assert I % block == 0
+    g, u = w[:I].view(I // block, block, K), w[I:].view(I // block, block, K)
+    return torch.stack([g, u], dim=1).reshape(two_i, K).contiguous()
+
+
+def deinterleave_gate_up(w_il: torch.Tensor, block: int = 64) -> torch.Tensor:
+    two_i, K = w_il.shape
+    I = two_i // 2
+    v = w_il.view(I // block, 2, block, K)
+    return torch.cat([v[:, 0].reshape(I, K), v[:, 1].reshape(I, K)], dim=0)
+
+
+def linear_silu_mul(x: torch.Tensor, w_il: torch.Tensor) -> torch.Tensor:
+    """silu(x @ Wg.T) * (x @ Wu.T) in one GEMM; w_il from interleave_gate_up."""
+    M = x.shape[0]
+    out = torch.empty(M, w_il.shape[0] // 2, dtype=x.dtype, device=x.device)
+    if M == 0:
+        return out
+    _LAUNCHES[0] += cuda_ext().gemm_bf16_ex(out, x, w_il, None, None, 1, 0, 0)
     return out
 
 
@@ -195,4 +242,5 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
     else:
         C.topk_topp_sample(tokens, lp, logits, temperature, top_k, top_p, min_p, seeds, offsets,
                            bool(want_logprobs))
+    _LAUNCHES[0] += 1
     return tokens, lp
