@@ -185,12 +185,17 @@ def main():
             nxt += 1
 
     def step():
-        admit(time.monotonic() - t0)
+        now = time.monotonic() - t0
+        admit(now)
+        if not eng.has_unfinished_requests() and nxt < len(prompts):
+            time.sleep(max(0.0, min(0.05, arrivals[nxt] - now)))   # idle until the next arrival
+            admit(time.monotonic() - t0)
         return eng.step()
 
-    # 1. ramp until the batch is full
+    # 1. ramp until the batch is full (bounded by wall time)
     ramp_steps = 0
-    while eng.scheduler.num_running < args.max_seqs and ramp_steps < 400:
+    ramp_deadline = time.monotonic() + 300.0
+    while eng.scheduler.num_running < args.max_seqs and time.monotonic() < ramp_deadline:
         step()
         ramp_steps += 1
         if nxt >= len(prompts) and not eng.has_unfinished_requests():

@@ -1,0 +1,137 @@
+"""HTTP middleware: bearer auth, sliding-window rate limit, request ids, timeouts.
+
+Counterpart of crates/rusteeze-api/src/middleware.rs: bearer-token auth
+(:20-45), a sliding-window rate limiter keyed by X-API-Key or
+X-Forwarded-For / client address that sets X-RateLimit-* headers
+(:48-161), request logging (:164-207) and X-Request-ID propagation
+(:215-224), and a request timeout (:227-260).  The reference builds the
+rate-limit, request-id and timeout layers but never installs them
+(routes.rs:202-233); here they are installed by `create_app`.
+"""
+from __future__ import annotations
+
+import asyncio
+import collections
+import hmac
+import logging
+import time
+import uuid
+from typing import Deque, Dict, Optional
+
+from starlette.middleware.base import BaseHTTPMiddleware
+from starlette.requests import Request
+from starlette.responses import JSONResponse
+
+from rusteeze_b200.core.errors import AuthenticationError, RateLimitError, RequestTimeoutError
+
+log = logging.getLogger("rusteeze.api")
+
+OPEN_PATHS = {"/health", "/health/live", "/health/ready", "/metrics", "/version"}
+
+
+def error_response(err) -> JSONResponse:
+    return JSONResponse(err.to_openai(), status_code=err.http_status)
+
+
+class AuthMiddleware(BaseHTTPMiddleware):
+    def __init__(self, app, api_key: Optional[str]):
+        super().__init__(app)
+        self.api_key = api_key
+
+    async def dispatch(self, request: Request, call_next):
+        if self.api_key and request.url.path not in OPEN_PATHS and request.method != "OPTIONS":
+            h = request.headers.get("authorization", "")
+            tok = h[7:] if h.lower().startswith("bearer ") else request.headers.get("x-api-key", "")
+            if not tok or not hmac.compare_digest(tok, self.api_key):
+                return error_response(AuthenticationError("invalid or missing API key"))
+        return await call_next(request)
+
+
+class SlidingWindowLimiter:
+    def __init__(self, per_minute: int, burst: int = 0, per_day: Optional[int] = None):
+        self.per_minute = per_minute
+        self.burst = burst
+        self.per_day = per_day
+        self.hits: Dict[str, Deque[float]] = collections.defaultdict(collections.deque)
+        self.day: Dict[str, Deque[float]] = collections.defaultdict(collections.deque)
+
+    def check(self, key: str, now: Optional[float] = None):
+        now = time.monotonic() if now is None else now
+        q = self.hits[key]
+        while q and now - q[0] >= 60.0:
+            q.popleft()
+        limit = self.per_minute + self.burst
+        if len(q) >= limit:
+            return False, limit, 0, 60.0 - (now - q[0])
+        if self.per_day is not None:
+            d = self.day[key]
+            while d and now - d[0] >= 86400.0:
+                d.popleft()
+            if len(d) >= self.per_day:
+                return False, limit, 0, 86400.0 - (now - d[0])
+            d.append(now)
+        q.append(now)
+        return True, limit, limit - len(q), 60.0 - (now - q[0])
+
+
+class RateLimitMiddleware(BaseHTTPMiddleware):
+    def __init__(self, app, limiter: SlidingWindowLimiter, by: str = "api_key"):
+        super().__init__(app)
+        self.limiter = limiter
+        self.by = by
+
+    def _key(self, request: Request) -> str:
+        if self.by == "api_key":
+            k = request.headers.get("x-api-key") or request.headers.get("authorization")
+            if k:
+                return "k:" + k
+        fwd = request.headers.get("x-forwarded-for")
+        if fwd:
+            return "ip:" + fwd.split(",")[0].strip()
+        return "ip:" + (request.client.host if request.client else "unknown")
+
+    async def dispatch(self, request: Request, call_next):
+        if request.url.path in OPEN_PATHS:
+            return await call_next(request)
+        ok, limit, remaining, reset = self.limiter.check(self._key(request))
+        if not ok:
+            resp = error_response(RateLimitError("rate limit exceeded"))
+            resp.headers["Retry-After"] = str(max(1, int(reset)))
+        else:
+            resp = await call_next(request)
+        resp.headers["X-RateLimit-Limit"] = str(limit)
+        resp.headers["X-RateLimit-Remaining"] = str(max(0, remaining))
+        resp.headers["X-RateLimit-Reset"] = str(max(0, int(reset)))
+        return resp
+
+
+class RequestIdMiddleware(BaseHTTPMiddleware):
+    def __init__(self, app, log_requests: bool = True):
+        super().__init__(app)
+        self.log_requests = log_requests
+
+    async def dispatch(self, request: Request, call_next):
+        rid = request.headers.get("x-request-id") or uuid.uuid4().hex
+        request.state.request_id = rid
+        t0 = time.perf_counter()
+        resp = await call_next(request)
+        resp.headers["X-Request-ID"] = rid
+        if self.log_requests:
+            log.info("%s %s %d %.1fms", request.method, request.url.path, resp.status_code,
+                     (time.perf_counter() - t0) * 1e3, extra={"request_id": rid})
+        return resp
+
+
+class TimeoutMiddleware(BaseHTTPMiddleware):
+    """Bounds time-to-response-headers.  Streaming bodies are bounded by the
+    engine's per-request deadline instead."""
+
+    def __init__(self, app, timeout_s: float):
+        super().__init__(app)
+        self.timeout_s = timeout_s
+
+    async def dispatch(self, request: Request, call_next):
+        try:
+            return await asyncio.wait_for(call_next(request), timeout=self.timeout_s)
+        except asyncio.TimeoutError:
+            return error_response(RequestTimeoutError(f"request exceeded {self.timeout_s:.0f}s"))

@@ -1,0 +1,327 @@
+"""OpenAI-compatible HTTP server.
+
+Routes (crates/rusteeze-api/src/routes.rs:19-43): POST /v1/chat/completions
+(streaming dispatch on `stream`), GET /v1/models, /health, /health/live,
+/health/ready, /metrics, /version -- plus POST /v1/completions, which the
+reference documents (crates/rusteeze-api/src/lib.rs:8) but never routes.
+Chat prompts are rendered with the model's chat template (the reference
+joins "role: content" lines, handlers.rs:222-229).  `stop`, `n`,
+`best_of`, logprobs and `stream_options.include_usage` are honoured (the
+reference ignores stop and n, handlers.rs:232-245).  SSE framing follows
+handlers.rs:143-182: a role chunk, content deltas, a finish chunk, then
+`data: [DONE]`.
+
+The engine runs in its own thread behind `AsyncLLMEngine`; handlers only
+await per-request output queues.
+"""
+from __future__ import annotations
+
+import json
+import os
+import signal
+import time
+import uuid
+from typing import AsyncIterator, List, Optional
+
+from fastapi import FastAPI, Request
+from fastapi.middleware.cors import CORSMiddleware
+from fastapi.middleware.gzip import GZipMiddleware
+from fastapi.responses import JSONResponse, PlainTextResponse, Response, StreamingResponse
+
+from rusteeze_b200 import __version__
+from rusteeze_b200.api import schemas as S
+from rusteeze_b200.api.middleware import (AuthMiddleware, RateLimitMiddleware, RequestIdMiddleware,
+                                          SlidingWindowLimiter, TimeoutMiddleware, error_response)
+from rusteeze_b200.core.errors import InvalidRequestError, RusteezeError
+from rusteeze_b200.core.sampling_params import SamplingParams
+from rusteeze_b200.metrics.registry import CONTENT_TYPE, EngineMetrics
+from rusteeze_b200.tokenizer.chat_template import ChatTemplate
+
+
+def _sampling_params(req, defaults, max_tokens_default: int, logprobs: Optional[int]) -> SamplingParams:
+    stop = req.stop if isinstance(req.stop, list) else ([req.stop] if req.stop else [])
+    mt = getattr(req, "max_completion_tokens", None) or req.max_tokens or max_tokens_default
+    return SamplingParams(
+        n=req.n, best_of=req.best_of or req.n, max_tokens=mt,
+        temperature=req.temperature if req.temperature is not None else defaults.temperature,
+        top_p=req.top_p if req.top_p is not None else defaults.top_p,
+        top_k=req.top_k if req.top_k is not None else defaults.top_k,
+        min_p=req.min_p or 0.0,
+        presence_penalty=req.presence_penalty or 0.0, frequency_penalty=req.frequency_penalty or 0.0,
+        repetition_penalty=req.repetition_penalty if req.repetition_penalty is not None
+        else defaults.repetition_penalty,
+        stop=stop, stop_token_ids=req.stop_token_ids or [], seed=req.seed,
+        logit_bias={int(k): v for k, v in (req.logit_bias or {}).items()},
+        logprobs=logprobs, ignore_eos=req.ignore_eos, min_tokens=req.min_tokens,
+        skip_special_tokens=req.skip_special_tokens,
+        include_stop_str_in_output=req.include_stop_str_in_output)
+
+
+def _sse(obj) -> str:
+    if isinstance(obj, str):
+        return f"data: {obj}\n\n"
+    return "data: " + obj.model_dump_json(exclude_none=True) + "\n\n"
+
+
+def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = None) -> FastAPI:
+    from rusteeze_b200.config.config import Config
+    cfg = config or Config()
+    eng = async_engine.engine
+    model_name = cfg.model.name or getattr(eng, "model_name", "model")
+    metrics = metrics or EngineMetrics(model_name=model_name)
+    if metrics.on_step not in eng.observers:
+        eng.observers.append(metrics.on_step)
+    template = ChatTemplate.for_model(model_name if not cfg.model.path else cfg.model.path, eng.tokenizer,
+                                      cfg.model.chat_template)
+    defaults = cfg.engine.sampling
+    started = time.time()
+
+    app = FastAPI(title="rusteeze_b200", version=__version__)
+    app.state.engine = async_engine
+    app.state.metrics = metrics
+    sc = cfg.server
+    app.add_middleware(TimeoutMiddleware, timeout_s=sc.timeout_seconds)
+    if sc.rate_limit is not None and sc.rate_limit.enabled:
+        app.add_middleware(RateLimitMiddleware,
+                           limiter=SlidingWindowLimiter(sc.rate_limit.requests_per_minute, sc.rate_limit.burst,
+                                                        sc.rate_limit.requests_per_day),
+                           by=sc.rate_limit.by)
+    app.add_middleware(AuthMiddleware, api_key=sc.api_key)
+    if sc.compression:
+        app.add_middleware(GZipMiddleware, minimum_size=1024)
+    if sc.cors.enabled:
+        app.add_middleware(CORSMiddleware, allow_origins=sc.cors.allowed_origins,
+                           allow_methods=sc.cors.allowed_methods, allow_headers=sc.cors.allowed_headers,
+                           max_age=sc.cors.max_age)
+    app.add_middleware(RequestIdMiddleware, log_requests=cfg.logging.request_logging)
+
+    @app.exception_handler(RusteezeError)
+    async def _err(_request: Request, exc: RusteezeError):
+        metrics.errors.labels(exc.code).inc()
+        return error_response(exc)
+
+    @app.exception_handler(ValueError)
+    async def _verr(_request: Request, exc: ValueError):
+        return error_response(InvalidRequestError(str(exc)))
+
+    def _check_model(name: str) -> None:
+        if name and name != model_name and not cfg.model.path == name:
+            from rusteeze_b200.core.errors import NotFoundError
+            raise NotFoundError(f"model {name!r} not found; this server serves {model_name!r}")
+
+    # ------------------------------------------------------------------ completions
+    @app.post("/v1/completions")
+    async def completions(req: S.CompletionRequest, request: Request):
+        _check_model(req.model)
+        prompts: List = []
+        p = req.prompt
+        if isinstance(p, str):
+            prompts = [(p, None)]
+        elif p and isinstance(p[0], int):
+            prompts = [(None, list(p))]
+        elif p and isinstance(p[0], list):
+            prompts = [(None, list(x)) for x in p]
+        else:
+            prompts = [(x, None) for x in p]
+        if not prompts:
+            raise InvalidRequestError("prompt must not be empty")
+        sp = _sampling_params(req, defaults, 16, req.logprobs)
+        metrics.on_request_params(sp)
+        rid = "cmpl-" + uuid.uuid4().hex
+        if req.stream:
+            return StreamingResponse(_stream_completion(rid, prompts, sp, req), media_type="text/event-stream")
+        choices, usage = [], S.Usage()
+        for pi, (text, ids) in enumerate(prompts):
+            final = None
+            async for out in async_engine.generate(text, sp, f"{rid}-{pi}", ids, priority=req.priority):
+                final = out
+            metrics.on_request_finished(final, "completions")
+            usage.prompt_tokens += len(final.prompt_token_ids)
+            for c in final.outputs:
+                usage.completion_tokens += len(c.token_ids)
+                t = ((final.prompt or eng.tokenizer.decode(final.prompt_token_ids)) if req.echo else "") + c.text
+                choices.append(S.CompletionChoice(index=pi * sp.n + c.index, text=t, finish_reason=c.finish_reason,
+                                                  logprobs=_cmpl_logprobs(eng.tokenizer, c) if req.logprobs is not None
+                                                  else None))
+        usage.total_tokens = usage.prompt_tokens + usage.completion_tokens
+        return S.CompletionResponse(id=rid, model=model_name, choices=choices, usage=usage)
+
+    async def _stream_completion(rid, prompts, sp, req) -> AsyncIterator[str]:
+        usage = S.Usage()
+        try:
+            for pi, (text, ids) in enumerate(prompts):
+                final = None
+                async for out in async_engine.generate(text, sp, f"{rid}-{pi}", ids, priority=req.priority):
+                    final = out
+                    for c, delta in zip(out.outputs, out.delta_text):
+                        if delta or c.finish_reason:
+                            chunk = S.CompletionResponse(
+                                id=rid, model=model_name, usage=S.Usage(),
+                                choices=[S.CompletionChoice(index=pi * sp.n + c.index, text=delta,
+                                                            finish_reason=c.finish_reason)])
+                            yield "data: " + chunk.model_dump_json(exclude={"usage"}, exclude_none=True) + "\n\n"
+                metrics.on_request_finished(final, "completions")
+                usage.prompt_tokens += len(final.prompt_token_ids)
+                usage.completion_tokens += sum(len(c.token_ids) for c in final.outputs)
+            if req.stream_options and req.stream_options.include_usage:
+                usage.total_tokens = usage.prompt_tokens + usage.completion_tokens
+                yield "data: " + json.dumps({"id": rid, "object": "text_completion", "model": model_name,
+                                             "choices": [], "usage": usage.model_dump()}) + "\n\n"
+        except RusteezeError as e:
+            yield "data: " + json.dumps(e.to_openai()) + "\n\n"
+        yield _sse("[DONE]")
+
+    # ------------------------------------------------------------------ chat
+    @app.post("/v1/chat/completions")
+    async def chat(req: S.ChatCompletionRequest, request: Request):
+        _check_model(req.model)
+        msgs = [m.model_dump() for m in req.messages]
+        tmpl = template if not req.chat_template else ChatTemplate(jinja=req.chat_template)
+        prompt = tmpl.apply(msgs, add_generation_prompt=req.add_generation_prompt)
+        ids = eng.tokenizer.encode(prompt, add_special_tokens=False) or eng.tokenizer.encode(prompt)
+        lp = (req.top_logprobs or 0) if req.logprobs else None
+        sp = _sampling_params(req, defaults, defaults.max_tokens, lp)
+        metrics.on_request_params(sp)
+        rid = "chatcmpl-" + uuid.uuid4().hex
+        if req.stream:
+            return StreamingResponse(_stream_chat(rid, ids, sp, req), media_type="text/event-stream")
+        final = None
+        async for out in async_engine.generate(None, sp, rid, ids, priority=req.priority):
+            final = out
+        metrics.on_request_finished(final, "chat")
+        choices = [S.ChatChoice(index=c.index, message=S.ChatMessage(role="assistant", content=c.text),
+                                finish_reason=c.finish_reason,
+                                logprobs=_chat_logprobs(eng.tokenizer, c) if req.logprobs else None)
+                   for c in final.outputs]
+        n_out = sum(len(c.token_ids) for c in final.outputs)
+        return S.ChatCompletionResponse(id=rid, model=model_name, choices=choices,
+                                        usage=S.Usage(prompt_tokens=len(ids), completion_tokens=n_out,
+                                                      total_tokens=len(ids) + n_out))
+
+    async def _stream_chat(rid, ids, sp, req) -> AsyncIterator[str]:
+        for i in range(sp.n):
+            yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
+                S.ChatChunkChoice(index=i, delta=S.ChatDelta(role="assistant", content=""))]))
+        final = None
+        try:
+            async for out in async_engine.generate(None, sp, rid, ids, priority=req.priority):
+                final = out
+                for c, delta in zip(out.outputs, out.delta_text):
+                    if delta:
+                        yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
+                            S.ChatChunkChoice(index=c.index, delta=S.ChatDelta(content=delta))]))
+                    if c.finish_reason:
+                        yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
+                            S.ChatChunkChoice(index=c.index, delta=S.ChatDelta(), finish_reason=c.finish_reason)]))
+            metrics.on_request_finished(final, "chat")
+            if req.stream_options and req.stream_options.include_usage and final is not None:
+                n_out = sum(len(c.token_ids) for c in final.outputs)
+                yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[], usage=S.Usage(
+                    prompt_tokens=len(ids), completion_tokens=n_out, total_tokens=len(ids) + n_out)))
+        except RusteezeError as e:
+            yield "data: " + json.dumps(e.to_openai()) + "\n\n"
+        yield _sse("[DONE]")
+
+    # ------------------------------------------------------------------ misc
+    @app.get("/v1/models")
+    async def models():
+        return S.ModelList(data=[S.ModelCard(id=model_name, max_model_len=getattr(eng, "max_model_len", None))])
+
+    @app.get("/health")
+    async def health():
+        st = async_engine.stats()
+        gpu = 0.0
+        try:
+            import torch
+            if torch.cuda.is_available():
+                free, total = torch.cuda.mem_get_info()
+                gpu = 1.0 - free / total
+        except Exception:  # noqa: BLE001
+            pass
+        body = S.HealthResponse(status="healthy" if async_engine.is_ready else "unhealthy", version=__version__,
+                                uptime_seconds=int(time.time() - started),
+                                requests_processed=st.get("requests_processed", 0),
+                                waiting_requests=st.get("num_waiting", 0), running_requests=st.get("num_running", 0),
+                                gpu_memory_usage=gpu, kv_cache_usage=st.get("kv_cache_usage", 0.0))
+        return JSONResponse(body.model_dump(), status_code=200 if async_engine.is_ready else 503)
+
+    @app.get("/health/live")
+    async def live():
+        return PlainTextResponse("OK")
+
+    @app.get("/health/ready")
+    async def ready():
+        if async_engine.is_ready:
+            return PlainTextResponse("READY")
+        return PlainTextResponse("NOT READY", status_code=503)
+
+    @app.get(cfg.metrics.path if cfg.metrics.enabled else "/metrics")
+    async def metrics_endpoint():
+        return Response(metrics.export(), media_type=CONTENT_TYPE)
+
+    @app.get("/version")
+    async def version():
+        import torch
+        return {"version": __version__, "name": "rusteeze_b200", "torch": torch.__version__,
+                "cuda": torch.version.cuda, "arch": "sm_100a"}
+
+    return app
+
+
+def _cmpl_logprobs(tok, c) -> S.CompletionLogProbs:
+    lp = S.CompletionLogProbs()
+    off = 0
+    for tid, d in zip(c.token_ids, c.logprobs or []):
+        s = tok.decode([tid])
+        lp.tokens.append(s)
+        lp.token_logprobs.append(d.get(tid))
+        lp.top_logprobs.append({tok.decode([k]): v for k, v in d.items()})
+        lp.text_offset.append(off)
+        off += len(s)
+    return lp
+
+
+def _chat_logprobs(tok, c) -> S.ChatLogProbs:
+    content = []
+    for tid, d in zip(c.token_ids, c.logprobs or []):
+        s = tok.decode([tid])
+        content.append(S.TokenLogProb(token=s, logprob=d.get(tid, 0.0), bytes=list(s.encode()),
+                                      top_logprobs=[S.TopLogProb(token=tok.decode([k]), logprob=v)
+                                                    for k, v in d.items() if k != tid]))
+    return S.ChatLogProbs(content=content)
+
+
+def serve(config, engine=None, host: Optional[str] = None, port: Optional[int] = None) -> None:
+    """Builds the engine (unless given), starts the engine thread and runs uvicorn
+    with graceful SIGINT/SIGTERM shutdown (crates/rusteeze-api/src/server.rs:304-330).
+    TLS is real when cert/key are configured (the reference falls back to
+    plaintext, server.rs:185-192)."""
+    import uvicorn
+    from rusteeze_b200.engine.async_engine import AsyncLLMEngine
+    from rusteeze_b200.engine.llm_engine import LLMEngine
+    eng = engine or LLMEngine(config)
+    ae = AsyncLLMEngine(eng, request_timeout_s=config.engine.request_timeout_seconds).start()
+    metrics = EngineMetrics(model_name=config.model.served_name())
+    app = create_app(ae, config, metrics)
+    if config.server.metrics_port:
+        from rusteeze_b200.metrics.exporter import start_exporter
+        start_exporter(metrics, config.server.metrics_port)
+    tls = config.server.tls
+    kw = {}
+    if tls is not None and tls.cert_path:
+        kw.update(ssl_certfile=tls.cert_path, ssl_keyfile=tls.key_path)
+    uv = uvicorn.Config(app, host=host or config.server.host, port=port or config.server.port,
+                        log_level=config.logging.level.lower().replace("warn", "warning"),
+                        timeout_keep_alive=int(config.server.keep_alive_seconds),
+                        limit_concurrency=config.server.max_connections, **kw)
+    server = uvicorn.Server(uv)
+    try:
+        server.run()
+    finally:
+        ae.shutdown()
+
+
+def serve_from_env() -> None:
+    """RUSTEEZE_HOST / RUSTEEZE_PORT / RUSTEEZE_API_KEY / RUSTEEZE_MODEL... (server.rs:333-370)."""
+    from rusteeze_b200.config.loader import load_config
+    serve(load_config())

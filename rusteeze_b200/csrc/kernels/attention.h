@@ -13,6 +13,7 @@ struct DecodeAttnParams {
   const __nv_bfloat16* k_cache;   // [blocks, Hkv, 16, D] with block_stride elements between blocks
   const __nv_bfloat16* v_cache;
   int64_t block_stride;
+  int num_blocks;                 // cache blocks (page ids outside [0, num_blocks) are rejected)
   const int32_t* seq_lens;        // [seqs]
   const int32_t* block_tables;    // [seqs, bt_stride]
   int64_t bt_stride;
@@ -32,6 +33,7 @@ struct PrefillAttnParams {
   const __nv_bfloat16* k_cache;
   const __nv_bfloat16* v_cache;
   int64_t block_stride;
+  int num_blocks;
   const int32_t* query_start_loc; // [S+1] over ALL sequences of the batch
   const int32_t* seq_lens;        // [S]
   const int32_t* block_tables;
@@ -43,6 +45,7 @@ struct PrefillAttnParams {
   float scale;
   int window;
   float softcap;
+  int* status;
 };
 
 int decode_attention_launch(const DecodeAttnParams& p, cudaStream_t st);

@@ -55,7 +55,11 @@ __global__ void __launch_bounds__(kDecThreads)
 
   const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int L = p.seq_lens[seq];
+  int L = p.seq_lens[seq];
+  if (L < 0 || L > p.bt_stride * 16) {  // longer than its block-table row: record, clamp
+    set_status(p.status, kBadArgument);
+    L = L < 0 ? 0 : static_cast<int>(p.bt_stride * 16);
+  }
   const int nblk = (L + 15) >> 4;
   const int per = (nblk + p.num_splits - 1) / p.num_splits;
   const int b0 = split * per;
@@ -85,7 +89,11 @@ __global__ void __launch_bounds__(kDecThreads)
     const int np = min(kPagesPerStage, b1 - blo);
     mbar_arrive_expect_tx(&bars[st % kDecStages], 2 * np * SM::kPageBytes);
     for (int j = 0; j < np; ++j) {
-      const int64_t page = bt[blo + j];
+      int64_t page = bt[blo + j];
+      if (page < 0 || page >= p.num_blocks) {  // corrupt block table: record and read page 0 instead
+        set_status(p.status, kBadArgument);
+        page = 0;
+      }
       const __nv_bfloat16* ksrc = p.k_cache + page * p.block_stride + static_cast<int64_t>(kvh) * 16 * D;
       const __nv_bfloat16* vsrc = p.v_cache + page * p.block_stride + static_cast<int64_t>(kvh) * 16 * D;
       bulk_load(slot + j * SM::kPageBytes, ksrc, SM::kPageBytes, &bars[st % kDecStages]);

@@ -75,6 +75,10 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnParams p) 
   const int q_len = p.query_start_loc[seq + 1] - q0;
   if (qt * kPBQ >= q_len) return;
   const int L = p.seq_lens[seq];
+  if (L > p.bt_stride * 16 || q_len > L) {  // inconsistent metadata: record and skip this tile
+    set_status(p.status, kBadArgument);
+    return;
+  }
   const int ctx0 = L - q_len;
   const int rows_valid = min(kPBQ, q_len - qt * kPBQ);
   const int qpos_lo = ctx0 + qt * kPBQ;
@@ -105,7 +109,12 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnParams p) 
       const int r = i / kChunks, c = i % kChunks;
       int page = tile * 4 + r / 16;
       page = page < nblk ? page : nblk - 1;   // beyond the context: any valid page (masked later)
-      const int64_t off = static_cast<int64_t>(bt[page]) * p.block_stride +
+      int64_t pid = bt[page];
+      if (pid < 0 || pid >= p.num_blocks) {   // corrupt block table: record and read page 0 instead
+        set_status(p.status, kBadArgument);
+        pid = 0;
+      }
+      const int64_t off = pid * p.block_stride +
                           (static_cast<int64_t>(kvh) * 16 + (r & 15)) * D + c * 8;
       cp_async16(aK + buf * kTile + swz<D>(r, c), p.k_cache + off);
       cp_async16(aV + buf * kTile + swz<D>(r, c), p.v_cache + off);

@@ -99,6 +99,7 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   p.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
   p.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
   p.block_stride = k_cache.stride(0);
+  p.num_blocks = k_cache.size(0);
   p.seq_lens = seq_lens.data_ptr<int32_t>();
   p.block_tables = block_tables.data_ptr<int32_t>();
   p.bt_stride = block_tables.stride(0);
@@ -132,6 +133,7 @@ void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache
   p.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
   p.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
   p.block_stride = k_cache.stride(0);
+  p.num_blocks = k_cache.size(0);
   p.query_start_loc = qsl.data_ptr<int32_t>();
   p.seq_lens = seq_lens.data_ptr<int32_t>();
   p.block_tables = block_tables.data_ptr<int32_t>();
@@ -145,6 +147,7 @@ void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache
   p.scale = scale;
   p.window = window;
   p.softcap = softcap;
+  p.status = status_ptr();
   check_rc(rz::prefill_attention_launch(p, cur_stream()), "prefill_attention");
 }
 

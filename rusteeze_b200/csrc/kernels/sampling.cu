@@ -175,7 +175,9 @@ __device__ void scan_buckets(const int* cnt, const float* mass, long k_target, f
       float mm = mi - m;
       for (int i = 0; i < per; ++i) {
         const int bi = lane * per + i;
-        if (cc + cnt[bi] >= k_target || mm + mass[bi] >= m_target) {
+        // the lane-level sum said the target is reached inside this lane's range; the
+        // per-bucket running sum may round differently, so the last bucket is the fallback
+        if (cc + cnt[bi] >= k_target || mm + mass[bi] >= m_target || i == per - 1) {
           b = bi;
           break;
         }

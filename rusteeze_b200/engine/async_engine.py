@@ -1,0 +1,176 @@
+"""Asynchronous front end over LLMEngine for the HTTP server.
+
+The reference's `Engine::generate` runs a single step per request and waits
+on a oneshot channel (crates/rusteeze-engine/src/engine.rs:239-300);
+`generate_stream` relies on an `Engine::run` loop nobody spawns
+(engine.rs:303-354, 558-572).  Here one dedicated thread owns the engine and
+runs `step()` back to back while work exists; requests and aborts arrive
+through a thread-safe inbox; every RequestOutput is pushed to the asyncio
+queue of its request with `call_soon_threadsafe`, so HTTP handlers stream
+tokens as they are produced.  Request timeouts (engine.rs:295, default
+600 s) abort the request inside the engine.  A watchdog marks the engine
+unhealthy when a step raises or stalls longer than `stall_timeout_s`
+(`/health/ready` then reports 503).
+"""
+from __future__ import annotations
+
+import asyncio
+import logging
+import queue
+import threading
+import time
+import traceback
+from dataclasses import dataclass
+from typing import AsyncIterator, Dict, List, Optional
+
+from rusteeze_b200.core.errors import RequestTimeoutError, ServiceUnavailableError
+from rusteeze_b200.core.outputs import RequestOutput
+from rusteeze_b200.core.sampling_params import SamplingParams
+
+log = logging.getLogger("rusteeze.async_engine")
+
+
+@dataclass
+class _Submit:
+    request_id: str
+    prompt: Optional[str]
+    prompt_token_ids: Optional[List[int]]
+    params: SamplingParams
+    priority: int
+    loop: asyncio.AbstractEventLoop
+    q: asyncio.Queue
+
+
+class AsyncLLMEngine:
+    def __init__(self, engine, request_timeout_s: float = 600.0, stall_timeout_s: float = 120.0):
+        self.engine = engine
+        self.request_timeout_s = request_timeout_s
+        self.stall_timeout_s = stall_timeout_s
+        self._inbox: "queue.Queue" = queue.Queue()
+        self._streams: Dict[str, _Submit] = {}
+        self._deadlines: Dict[str, float] = {}
+        self._wake = threading.Event()
+        self._stop = threading.Event()
+        self._thread: Optional[threading.Thread] = None
+        self.healthy = True
+        self.last_error: Optional[str] = None
+        self.last_step_start: Optional[float] = None
+        self.started_at = time.time()
+        self.requests_processed = 0
+
+    # ------------------------------------------------------------------ lifecycle
+    def start(self) -> "AsyncLLMEngine":
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._loop, name="rusteeze-engine", daemon=True)
+            self._thread.start()
+        return self
+
+    def shutdown(self, timeout: float = 10.0) -> None:
+        self._stop.set()
+        self._wake.set()
+        if self._thread is not None:
+            self._thread.join(timeout)
+
+    @property
+    def is_ready(self) -> bool:
+        if not self.healthy or self._thread is None or not self._thread.is_alive():
+            return False
+        t = self.last_step_start
+        return t is None or time.monotonic() - t < self.stall_timeout_s
+
+    # ------------------------------------------------------------------ client API
+    async def generate(self, prompt: Optional[str], params: SamplingParams, request_id: str,
+                       prompt_token_ids: Optional[List[int]] = None,
+                       priority: int = 0) -> AsyncIterator[RequestOutput]:
+        if not self.is_ready:
+            raise ServiceUnavailableError(self.last_error or "engine is not ready")
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        self._inbox.put(("add", _Submit(request_id, prompt, prompt_token_ids, params, priority, loop, q)))
+        self._wake.set()
+        try:
+            while True:
+                item = await q.get()
+                if isinstance(item, BaseException):
+                    raise item
+                yield item
+                if item.finished:
+                    return
+        finally:
+            # client went away or finished: make sure the engine drops it
+            self._inbox.put(("abort", request_id))
+            self._wake.set()
+
+    def abort(self, request_id: str) -> None:
+        self._inbox.put(("abort", request_id))
+        self._wake.set()
+
+    def stats(self) -> dict:
+        d = dict(self.engine.stats())
+        d["uptime_s"] = time.time() - self.started_at
+        d["requests_processed"] = self.requests_processed
+        d["healthy"] = self.healthy
+        return d
+
+    # ------------------------------------------------------------------ engine thread
+    def _drain_inbox(self) -> None:
+        while True:
+            try:
+                kind, item = self._inbox.get_nowait()
+            except queue.Empty:
+                return
+            if kind == "add":
+                try:
+                    self.engine.add_request(item.request_id, item.prompt, item.params, item.prompt_token_ids,
+                                            priority=item.priority)
+                    self._streams[item.request_id] = item
+                    self._deadlines[item.request_id] = time.monotonic() + self.request_timeout_s
+                except BaseException as e:  # noqa: BLE001 -- delivered to the caller
+                    item.loop.call_soon_threadsafe(item.q.put_nowait, e)
+            elif kind == "abort":
+                if item in self._streams:
+                    self.engine.abort_request(item)
+                    self._streams.pop(item, None)
+                    self._deadlines.pop(item, None)
+
+    def _expire(self) -> None:
+        now = time.monotonic()
+        for rid, dl in list(self._deadlines.items()):
+            if now > dl:
+                sub = self._streams.pop(rid, None)
+                self._deadlines.pop(rid, None)
+                self.engine.abort_request(rid)
+                if sub is not None:
+                    sub.loop.call_soon_threadsafe(sub.q.put_nowait,
+                                                  RequestTimeoutError(f"request {rid} timed out"))
+
+    def _loop(self) -> None:
+        while not self._stop.is_set():
+            self._drain_inbox()
+            self._expire()
+            if not self.engine.has_unfinished_requests():
+                self._wake.wait(0.05)
+                self._wake.clear()
+                continue
+            self.last_step_start = time.monotonic()
+            try:
+                outs = self.engine.step()
+            except BaseException as e:  # noqa: BLE001
+                self.healthy = False
+                self.last_error = f"engine step failed: {e!r}"
+                log.error("engine step failed:\n%s", traceback.format_exc())
+                for sub in self._streams.values():
+                    sub.loop.call_soon_threadsafe(sub.q.put_nowait, ServiceUnavailableError(self.last_error))
+                self._streams.clear()
+                return
+            finally:
+                self.last_step_start = None
+            for o in outs:
+                sub = self._streams.get(o.request_id)
+                if sub is None:
+                    continue
+                sub.loop.call_soon_threadsafe(sub.q.put_nowait, o)
+                if o.finished:
+                    self._streams.pop(o.request_id, None)
+                    self._deadlines.pop(o.request_id, None)
+                    self.requests_processed += 1

@@ -190,6 +190,11 @@ class ModelRunner:
             meta = self._graph_meta(B)
             self.d_slots[:B].fill_(-1)
             self.d_seq_lens[:B].fill_(0)
+            self.d_block_tables[:B].zero_()
+            self.d_input_ids[:B].zero_()
+            self.d_positions[:B].zero_()
+            # the side stream must see the buffer initialisation above
+            stream.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(stream):
                 for _ in range(2):     # warm-up outside capture
                     self._decode_forward(B, meta)

@@ -1,0 +1,99 @@
+"""Config precedence (defaults < file < env < CLI), validation, and CLI smoke tests."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+from rusteeze_b200.config.loader import ConfigLoader, env_overrides, load_file
+from rusteeze_b200.config.validation import collect_errors
+from rusteeze_b200.core.errors import ConfigError
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_precedence(tmp_path):
+    f = tmp_path / "c.yaml"
+    f.write_text("model:\n  preset: tiny-llama\n  dtype: float32\nserver:\n  port: 9000\nengine:\n  max_num_seqs: 32\n")
+    env = {"RUSTEEZE_PORT": "9100", "RUSTEEZE_MAX_SEQS": "64"}
+    cfg = ConfigLoader(str(f), environ=env).load({"engine": {"max_num_seqs": 128}, "server": {"host": None}})
+    assert cfg.model.preset == "tiny-llama"
+    assert cfg.server.port == 9100           # env beats file
+    assert cfg.engine.max_num_seqs == 128    # CLI beats env
+    assert cfg.server.host == "0.0.0.0"      # None CLI values do not override
+
+
+@pytest.mark.parametrize("ext,text", [
+    (".json", '{"engine": {"block_size": 16, "max_num_batched_tokens": 2048}}'),
+    (".toml", "[engine]\nblock_size = 16\nmax_num_batched_tokens = 2048\n"),
+])
+def test_formats(tmp_path, ext, text):
+    f = tmp_path / ("c" + ext)
+    f.write_text(text)
+    cfg = ConfigLoader(str(f), environ={}).load()
+    assert cfg.engine.max_num_batched_tokens == 2048
+
+
+def test_validation_errors(tmp_path):
+    f = tmp_path / "bad.yaml"
+    f.write_text("model:\n  dtype: int3\n  device: metal\n  pipeline_parallel_size: 2\nengine:\n  block_size: 32\n")
+    cfg = ConfigLoader(str(f), environ={}).load(validate=False)
+    errs = collect_errors(cfg)
+    assert any("dtype" in e for e in errs) and any("device" in e for e in errs)
+    assert any("pipeline_parallel_size" in e for e in errs) and any("block_size" in e for e in errs)
+    with pytest.raises(ConfigError):
+        ConfigLoader(str(f), environ={}).load()
+
+
+def test_unknown_key_rejected(tmp_path):
+    f = tmp_path / "u.yaml"
+    f.write_text("engine:\n  no_such_knob: 1\n")
+    with pytest.raises(ConfigError):
+        ConfigLoader(str(f), environ={}).load()
+
+
+def test_env_override_types():
+    assert env_overrides(environ={"RUSTEEZE_GPU_MEMORY_UTIL": "0.5"})["engine"]["gpu_memory_utilization"] == 0.5
+    with pytest.raises(ConfigError):
+        env_overrides(environ={"RUSTEEZE_PORT": "abc"})
+
+
+def test_example_config_is_valid():
+    cfg = ConfigLoader(os.path.join(ROOT, "config.example.yaml"), environ={}).load()
+    assert cfg.engine.block_size == 16
+
+
+def _cli(*args, stdin=None):
+    env = dict(os.environ, PYTHONPATH=ROOT)
+    return subprocess.run([sys.executable, "-m", "rusteeze_b200", *args], capture_output=True, text=True,
+                          cwd=ROOT, env=env, input=stdin, timeout=300)
+
+
+def test_cli_version_info_validate(tmp_path):
+    r = _cli("--json", "version")
+    assert r.returncode == 0 and json.loads(r.stdout)["version"]
+    r = _cli("info", "llama-3-8b")
+    d = json.loads(r.stdout)
+    assert 7.9 < d["parameters_billions"] < 8.1
+    f = tmp_path / "c.yaml"
+    f.write_text("engine:\n  block_size: 32\n")
+    r = _cli("--json", "validate", str(f))
+    assert r.returncode == 1 and not json.loads(r.stdout)["valid"]
+
+
+def test_cli_generate_and_benchmark_tiny():
+    r = _cli("--json", "generate", "-m", "tiny-llama", "--device", "cpu", "--dtype", "float32", "-p", "hello",
+             "--max-tokens", "4", "--temperature", "0")
+    assert r.returncode == 0, r.stderr
+    out = json.loads(r.stdout)
+    assert len(out[0]["outputs"][0]["token_ids"]) == 4
+    r = _cli("--json", "benchmark", "-m", "tiny-llama", "--device", "cpu", "--dtype", "float32", "-n", "4",
+             "--input-len", "16", "--output-len", "4", "--concurrency", "4", "--warmup", "1")
+    assert r.returncode == 0, r.stderr
+    assert json.loads(r.stdout)["output_tokens_per_s"] > 0
+
+
+def test_cli_rejects_pipeline_parallel():
+    r = _cli("serve", "-m", "tiny-llama", "--pipeline-parallel-size", "2")
+    assert r.returncode == 2 and "pipeline_parallel_size" in r.stderr

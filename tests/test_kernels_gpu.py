@@ -16,7 +16,7 @@ def C():
 
 
 def rel_err(a, b):
-    a, b = a.float(), b.float()
+    a, b = a.detach().float().cpu(), b.detach().float().cpu()
     return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
 
 
