@@ -7,54 +7,87 @@
 // softmax of its CPU FlashAttention (crates/rusteeze-engine/src/
 // flash_attention.rs:186-252).
 //
-// Grid (splits, Hkv, seqs); 128 threads.  A CTA owns one (sequence, kv head,
-// KV range) and all G = Hq/Hkv query heads of that kv head, so each KV byte
-// is read from HBM once.  Cache layout per layer: [blocks, Hkv, 16, D] with
-// a runtime block stride, so every (block, head) page is one contiguous
-// 16*D*2-byte run that a single 1-D bulk copy (cp.async.bulk) moves into a
-// 4-stage shared-memory ring, two pages (32 tokens) per stage.
-//   scores : 4 threads per token, each a quarter of D (rotated 16-byte
-//            chunks: bank-conflict free), reduced with 2 shuffles
-//   softmax: online max/sum per head, one warp per head
-//   PV     : thread = (token half, dim pair); halves merged at the end
-// With splits > 1 each CTA writes (acc, max, sum) partials to a workspace
-// and `decode_combine` merges them; the split count is fixed per launch and
-// each CTA derives its KV range from the live sequence length, so one
+// Work item = (sequence, kv head, KV split).  Each WARP owns one item and
+// runs independently -- no CTA-wide barrier in the loop:
+//   * the G = Hq/Hkv query heads of the kv head are packed into the M
+//     dimension of a 16-row tensor-core tile (rows >= G are zero), so
+//     S = Q K^T and O += P V are mma.sync m16n8k16 (bf16 in, fp32 acc) and
+//     every KV byte is read from HBM once for all G heads;
+//   * pages (16 tokens; K and V each one contiguous 16*D*2-byte run in the
+//     [blocks, Hkv, 16, D] per-layer cache view) stream into a per-warp
+//     shared-memory ring with cp.async, XOR-swizzled so ldmatrix is
+//     bank-conflict free; the warp keeps kStages pages in flight;
+//   * online softmax per head in registers (2 shuffles per row max/sum).
+// With splits > 1 each item writes (acc, max, sum) partials to a workspace
+// and `decode_combine` merges them.  The split count is fixed per launch;
+// each item derives its page range from the live sequence length, so one
 // CUDA graph serves any context length.
 #include "attention.h"
 #include "common.cuh"
 
 namespace rz {
 
-constexpr int kDecThreads = 128;
-constexpr int kPagesPerStage = 2;
-constexpr int kTokPerStage = 16 * kPagesPerStage;
-constexpr int kDecStages = 4;
 
-template <int D, int G>
-struct DecSmem {
-  static constexpr int kPageBytes = 16 * D * 2;
-  static constexpr int kStageBytes = 2 * kPagesPerStage * kPageBytes;  // K and V
-  static constexpr int kBytes = kDecStages * kStageBytes + G * D * 4 /*q*/ + G * kTokPerStage * 4 /*scores*/ +
-                                4 * G * 4 /*stats*/ + 64 /*bars*/ + 2 * G * D * 4 /*PV merge*/ + 128;
+__device__ __forceinline__ void dec_cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void dec_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void dec_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void dec_ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+__device__ __forceinline__ void dec_ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+__device__ __forceinline__ void dec_mma(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t dec_pack(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int D>
+struct DecCfg {
+  static constexpr int kWarps = D <= 128 ? 8 : 4;
+  static constexpr int kPage = 16 * D * 2;                      // bytes of one K (or V) page
+  static constexpr int kStages = D <= 64 ? 6 : (D <= 128 ? 3 : 2);
+  static constexpr int kWarpBytes = kStages * 2 * kPage + 16 * D * 2;  // K/V ring + Q tile
+  static constexpr int kSmem = kWarps * kWarpBytes;
 };
 
-template <int D, int G>
-__global__ void __launch_bounds__(kDecThreads)
-    decode_attn_kernel(DecodeAttnParams p) {
-  using SM = DecSmem<D, G>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* ring = smem;
-  float* q_s = reinterpret_cast<float*>(smem + kDecStages * SM::kStageBytes);
-  float* sc = q_s + G * D;                    // [G][32]
-  float* corr = sc + G * kTokPerStage;        // [G] rescale factors of this stage
-  float* lsum = corr + G;                     // [G] running sums
-  float* mrun = lsum + G;                     // [G] running maxima
-  uint64_t* bars = reinterpret_cast<uint64_t*>(mrun + G + (G & 1));
-  float* merge = reinterpret_cast<float*>(bars + kDecStages);
+// (row, 16-byte chunk) -> byte offset inside a [16][D] bf16 page/tile, XOR swizzled
+template <int D>
+__device__ __forceinline__ uint32_t dswz(int row, int chunk) {
+  return static_cast<uint32_t>(row * D * 2 + ((chunk ^ (row & 7)) << 4));
+}
 
-  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+template <int D>
+__global__ void __launch_bounds__(DecCfg<D>::kWarps * 32) decode_attn_kernel(DecodeAttnParams p) {
+  using C = DecCfg<D>;
+  constexpr int kChunks = D / 8;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* wbase = smem + warp * C::kWarpBytes;
+  const uint32_t aRing = smem_u32(wbase);
+  const uint32_t aQ = aRing + C::kStages * 2 * C::kPage;
+  uint8_t* sQ = wbase + C::kStages * 2 * C::kPage;
+
+  const int item = blockIdx.x * C::kWarps + warp;
+  const int n_items = p.num_seqs * p.num_kv_heads * p.num_splits;
+  if (item >= n_items) return;
+  const int split = item % p.num_splits;
+  const int kvh = (item / p.num_splits) % p.num_kv_heads;
+  const int seq = item / (p.num_splits * p.num_kv_heads);
+  const int G = p.num_q_heads / p.num_kv_heads;
+
   int L = p.seq_lens[seq];
   if (L < 0 || L > p.bt_stride * 16) {  // longer than its block-table row: record, clamp
     set_status(p.status, kBadArgument);
@@ -64,193 +97,155 @@ __global__ void __launch_bounds__(kDecThreads)
   const int per = (nblk + p.num_splits - 1) / p.num_splits;
   const int b0 = split * per;
   const int b1 = min(nblk, b0 + per);
-  const int nstage = b1 > b0 ? (b1 - b0 + kPagesPerStage - 1) / kPagesPerStage : 0;
+  const int npages = b1 > b0 ? b1 - b0 : 0;
   const int32_t* bt = p.block_tables + static_cast<int64_t>(seq) * p.bt_stride;
 
-  // q (pre-scaled) -> smem fp32
-  for (int i = tid; i < G * D; i += kDecThreads) {
-    const int g = i / D, d = i % D;
-    q_s[i] = bf2f(p.q[static_cast<int64_t>(seq) * p.q_stride + (kvh * G + g) * D + d]) * p.scale;
+  // Q tile: rows g < G are the query heads of this kv head, rows >= G are zero
+  for (int i = lane; i < 16 * kChunks; i += 32) {
+    const int r = i / kChunks, c = i % kChunks;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G)
+      v = *reinterpret_cast<const uint4*>(p.q + static_cast<int64_t>(seq) * p.q_stride +
+                                          static_cast<int64_t>(kvh * G + r) * D + c * 8);
+    *reinterpret_cast<uint4*>(sQ + dswz<D>(r, c)) = v;
   }
-  if (tid < G) {
-    lsum[tid] = 0.f;
-    mrun[tid] = -INFINITY;
-  }
-  if (tid == 0) {
-    for (int s = 0; s < kDecStages; ++s) mbar_init(&bars[s], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
 
-  auto issue = [&](int st) {
-    // thread 0: bulk-copy up to kPagesPerStage K and V pages of stage `st` into ring slot st % kDecStages
-    uint8_t* slot = ring + (st % kDecStages) * SM::kStageBytes;
-    const int blo = b0 + st * kPagesPerStage;
-    const int np = min(kPagesPerStage, b1 - blo);
-    mbar_arrive_expect_tx(&bars[st % kDecStages], 2 * np * SM::kPageBytes);
-    for (int j = 0; j < np; ++j) {
-      int64_t page = bt[blo + j];
-      if (page < 0 || page >= p.num_blocks) {  // corrupt block table: record and read page 0 instead
-        set_status(p.status, kBadArgument);
-        page = 0;
-      }
-      const __nv_bfloat16* ksrc = p.k_cache + page * p.block_stride + static_cast<int64_t>(kvh) * 16 * D;
-      const __nv_bfloat16* vsrc = p.v_cache + page * p.block_stride + static_cast<int64_t>(kvh) * 16 * D;
-      bulk_load(slot + j * SM::kPageBytes, ksrc, SM::kPageBytes, &bars[st % kDecStages]);
-      bulk_load(slot + (kPagesPerStage + j) * SM::kPageBytes, vsrc, SM::kPageBytes, &bars[st % kDecStages]);
+  auto load_page = [&](int j, int slot) {
+    int64_t pid = bt[b0 + j];
+    if (pid < 0 || pid >= p.num_blocks) {  // corrupt block table: record and read page 0 instead
+      set_status(p.status, kBadArgument);
+      pid = 0;
+    }
+    const int64_t off = pid * p.block_stride + static_cast<int64_t>(kvh) * 16 * D;
+    const uint32_t dk = aRing + slot * 2 * C::kPage;
+    const uint32_t dv = dk + C::kPage;
+#pragma unroll
+    for (int i = lane; i < 16 * kChunks; i += 32) {
+      const int r = i / kChunks, c = i % kChunks;
+      dec_cp_async16(dk + dswz<D>(r, c), p.k_cache + off + r * D + c * 8);
+      dec_cp_async16(dv + dswz<D>(r, c), p.v_cache + off + r * D + c * 8);
     }
   };
-  if (tid == 0)
-    for (int s = 0; s < kDecStages && s < nstage; ++s) issue(s);
+  // prologue: kStages-1 pages in flight (empty groups keep the group count uniform)
+#pragma unroll
+  for (int s = 0; s < C::kStages - 1; ++s) {
+    if (s < npages) load_page(s, s);
+    dec_commit();
+  }
+  __syncwarp();
 
-  // PV roles: thread = (token half th, dim pair dp)
-  constexpr int kPairs = D / 2;
-  constexpr int kPvThreads = 2 * kPairs;     // D=128 -> 128 threads
-  constexpr int kDimIters = (kPvThreads + kDecThreads - 1) / kDecThreads;
-  float acc[kDimIters][G][2];
+  float o[D / 8][4];
 #pragma unroll
-  for (int a = 0; a < kDimIters; ++a)
-#pragma unroll
-    for (int g = 0; g < G; ++g) acc[a][g][0] = acc[a][g][1] = 0.f;
-  bool ok = true;
-  const int kv_end = min(L, b1 * 16);         // keys this CTA owns: [b0*16, kv_end)
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  const float sl2 = p.scale * 1.4426950408889634f;
+  const int kv_end = min(L, b1 * 16);
 
-  for (int st = 0; st < nstage; ++st) {
-    if (ok && !mbar_wait(&bars[st % kDecStages], (st / kDecStages) & 1, p.status, kAttnTimeout)) ok = false;
-    const uint8_t* slot = ring + (st % kDecStages) * SM::kStageBytes;
-    const __nv_bfloat16* Ks = reinterpret_cast<const __nv_bfloat16*>(slot);
-    const __nv_bfloat16* Vs = reinterpret_cast<const __nv_bfloat16*>(slot + kPagesPerStage * SM::kPageBytes);
-    const int tok0 = (b0 + st * kPagesPerStage) * 16;
-    // ---- scores: token t = tid/4, quarter qd = tid%4
-    {
-      const int t = tid >> 2, qd = tid & 3;
-      constexpr int kChunks = D / 8;          // 16-byte chunks per row
-      constexpr int kMine = kChunks / 4;      // chunks per thread
-      float part[G];
+  for (int j = 0; j < npages; ++j) {
+    const int nxt = j + C::kStages - 1;
+    if (nxt < npages) load_page(nxt, nxt % C::kStages);
+    dec_commit();
+    dec_wait<C::kStages - 1>();
+    __syncwarp();
+    const uint32_t aK = aRing + (j % C::kStages) * 2 * C::kPage;
+    const uint32_t aV = aK + C::kPage;
+    // ---- S[16 heads x 16 tokens]
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-      for (int g = 0; g < G; ++g) part[g] = 0.f;
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a0, a1, a2, a3, b0r, b1r, b2r, b3r;
+      dec_ldsm_x4(aQ + dswz<D>(lane & 15, 2 * kk + (lane >> 4)), a0, a1, a2, a3);
+      dec_ldsm_x4(aK + dswz<D>((lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0r, b1r, b2r, b3r);
+      dec_mma(s[0], a0, a1, a2, a3, b0r, b1r);
+      dec_mma(s[1], a0, a1, a2, a3, b2r, b3r);
+    }
+    // ---- mask + online softmax (log2 domain); thread rows: lane/4 and lane/4 + 8
+    const int tok0 = (b0 + j) * 16;
+    float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-      for (int i = 0; i < kMine; ++i) {
-        const int c = qd + 4 * ((i + t) % kMine);
-        uint4 u = *reinterpret_cast<const uint4*>(Ks + t * D + c * 8);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-        float kf[8];
+    for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float2 f = __bfloat1622float2(h[e]);
-          kf[2 * e] = f.x;
-          kf[2 * e + 1] = f.y;
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float4* qv = reinterpret_cast<const float4*>(q_s + g * D + c * 8);
-          const float4 q0 = qv[0], q1 = qv[1];
-          part[g] += q0.x * kf[0] + q0.y * kf[1] + q0.z * kf[2] + q0.w * kf[3] + q1.x * kf[4] + q1.y * kf[5] +
-                     q1.z * kf[6] + q1.w * kf[7];
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        part[g] += __shfl_xor_sync(0xffffffffu, part[g], 1);
-        part[g] += __shfl_xor_sync(0xffffffffu, part[g], 2);
-      }
-      if (qd == 0) {
-        const int pos = tok0 + t;
+      for (int e = 0; e < 4; ++e) {
+        const int pos = tok0 + nt * 8 + 2 * (lane & 3) + (e & 1);
+        float v = s[nt][e];
+        if (p.softcap > 0.f) v = p.softcap * tanhf(v * p.scale / p.softcap) * 1.4426950408889634f;
+        else v *= sl2;
         const bool valid = pos < kv_end && (p.window <= 0 || pos > L - 1 - p.window);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float s = part[g];
-          if (p.softcap > 0.f) s = p.softcap * tanhf(s / p.softcap);
-          sc[g * kTokPerStage + t] = valid ? s : -INFINITY;
-        }
+        v = valid ? v : -INFINITY;
+        s[nt][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
     }
-    __syncthreads();
-    // ---- online softmax: warp w handles heads w, w+4, ...
-    for (int g = warp; g < G; g += kDecThreads / 32) {
-      const float s = sc[g * kTokPerStage + lane];
-      const float mx = warp_max(s);
-      const float m_old = mrun[g];
-      const float m_new = fmaxf(m_old, mx);
-      const float pr = m_new == -INFINITY ? 0.f : __expf(s - m_new);
-      const float sum = warp_sum(pr);
-      sc[g * kTokPerStage + lane] = pr;
-      __syncwarp();
-      if (lane == 0) {
-        const float cf = m_old == -INFINITY ? 0.f : __expf(m_old - m_new);
-        corr[g] = cf;
-        lsum[g] = lsum[g] * cf + sum;
-        mrun[g] = m_new;
+    float corr[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+      const float mn = fmaxf(m_r[h], mx[h]);
+      corr[h] = (m_r[h] == -INFINITY) ? 0.f : exp2f(m_r[h] - mn);
+      m_r[h] = mn;
+      l_r[h] *= corr[h];
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const float pv = m_r[h] == -INFINITY ? 0.f : exp2f(s[nt][e] - m_r[h]);
+        s[nt][e] = pv;
+        l_r[h] += pv;
       }
     }
-    __syncthreads();
-    // ---- PV (only over tokens of this stage that hold data: stale ring bytes may be NaN)
-    const int ntok = min(kTokPerStage, kv_end - tok0);
 #pragma unroll
-    for (int a = 0; a < kDimIters; ++a) {
-      const int idx = tid + a * kDecThreads;
-      if (idx < kPvThreads) {
-        const int th = idx / kPairs, dp = idx % kPairs;
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          acc[a][g][0] *= corr[g];
-          acc[a][g][1] *= corr[g];
-        }
-        const int t_end = min(th * 16 + 16, ntok);
-#pragma unroll 4
-        for (int t = th * 16; t < t_end; ++t) {
-          const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(Vs + t * D + 2 * dp));
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const float pr = sc[g * kTokPerStage + t];
-            acc[a][g][0] += pr * v.x;
-            acc[a][g][1] += pr * v.y;
-          }
-        }
-      }
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= corr[0];
+      o[i][1] *= corr[0];
+      o[i][2] *= corr[1];
+      o[i][3] *= corr[1];
     }
-    __syncthreads();  // ring slot and scores free
-    if (tid == 0 && ok && st + kDecStages < nstage) issue(st + kDecStages);
+    // ---- O += P V   (P: 16 heads x 16 tokens as the A operand)
+    const uint32_t pa0 = dec_pack(s[0][0], s[0][1]), pa1 = dec_pack(s[0][2], s[0][3]);
+    const uint32_t pa2 = dec_pack(s[1][0], s[1][1]), pa3 = dec_pack(s[1][2], s[1][3]);
+#pragma unroll
+    for (int dn = 0; dn < D / 16; ++dn) {
+      uint32_t b0r, b1r, b2r, b3r;
+      dec_ldsm_x4_t(aV + dswz<D>((lane & 7) + (((lane >> 3) & 1) << 3), 2 * dn + (lane >> 4)), b0r, b1r, b2r, b3r);
+      dec_mma(o[2 * dn], pa0, pa1, pa2, pa3, b0r, b1r);
+      dec_mma(o[2 * dn + 1], pa0, pa1, pa2, pa3, b2r, b3r);
+    }
+    __syncwarp();  // ring slot j % kStages is refilled next iteration
   }
+  dec_wait<0>();
 
-  // ---- merge the two token halves, then normalise / emit partials
+  // ---- finalise rows g < G
 #pragma unroll
-  for (int a = 0; a < kDimIters; ++a) {
-    const int idx = tid + a * kDecThreads;
-    if (idx < kPvThreads && idx >= kPairs) {
-      const int dp = idx - kPairs;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        merge[(g * D) + 2 * dp] = acc[a][g][0];
-        merge[(g * D) + 2 * dp + 1] = acc[a][g][1];
-      }
-    }
+  for (int h = 0; h < 2; ++h) {
+    l_r[h] += __shfl_xor_sync(0xffffffffu, l_r[h], 1);
+    l_r[h] += __shfl_xor_sync(0xffffffffu, l_r[h], 2);
   }
-  __syncthreads();
 #pragma unroll
-  for (int a = 0; a < kDimIters; ++a) {
-    const int idx = tid + a * kDecThreads;
-    if (idx < kPairs) {
-      const int dp = idx;
+  for (int h = 0; h < 2; ++h) {
+    const int g = (lane >> 2) + h * 8;
+    if (g >= G) continue;
+    const int qh = kvh * G + g;
+    if (p.num_splits == 1) {
+      const float inv = l_r[h] > 0.f ? 1.f / l_r[h] : 0.f;
+      __nv_bfloat16* dst = p.out + static_cast<int64_t>(seq) * p.out_stride + static_cast<int64_t>(qh) * D;
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float o0 = acc[a][g][0] + merge[g * D + 2 * dp];
-        const float o1 = acc[a][g][1] + merge[g * D + 2 * dp + 1];
-        const int qh = kvh * G + g;
-        if (p.num_splits == 1) {
-          const float l = lsum[g];
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          __nv_bfloat162 r = __floats2bfloat162_rn(o0 * inv, o1 * inv);
-          *reinterpret_cast<__nv_bfloat162*>(p.out + static_cast<int64_t>(seq) * p.out_stride + qh * D + 2 * dp) = r;
-        } else {
-          float* w = p.workspace + ((static_cast<int64_t>(seq) * p.num_q_heads + qh) * p.num_splits + split) * (D + 2);
-          w[2 * dp] = o0;
-          w[2 * dp + 1] = o1;
-          if (dp == 0) {
-            w[D] = mrun[g];
-            w[D + 1] = lsum[g];
-          }
-        }
+      for (int i = 0; i < D / 8; ++i)
+        *reinterpret_cast<__nv_bfloat162*>(dst + i * 8 + 2 * (lane & 3)) =
+            __floats2bfloat162_rn(o[i][2 * h] * inv, o[i][2 * h + 1] * inv);
+    } else {
+      float* w = p.workspace + ((static_cast<int64_t>(seq) * p.num_q_heads + qh) * p.num_splits + split) * (D + 2);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        w[i * 8 + 2 * (lane & 3)] = o[i][2 * h];
+        w[i * 8 + 2 * (lane & 3) + 1] = o[i][2 * h + 1];
+      }
+      if ((lane & 3) == 0) {
+        // running max is in log2 units; the combine kernel works in the same units
+        w[D] = m_r[h];
+        w[D + 1] = l_r[h];
       }
     }
   }
@@ -265,29 +260,29 @@ __global__ void decode_combine_kernel(DecodeAttnParams p) {
   float den = 0.f;
   for (int s = 0; s < p.num_splits; ++s) {
     const float m = w[s * (D + 2) + D];
-    den += m == -INFINITY ? 0.f : __expf(m - M) * w[s * (D + 2) + D + 1];
+    den += m == -INFINITY ? 0.f : exp2f(m - M) * w[s * (D + 2) + D + 1];
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float o = 0.f;
     for (int s = 0; s < p.num_splits; ++s) {
       const float m = w[s * (D + 2) + D];
-      if (m != -INFINITY) o += __expf(m - M) * w[s * (D + 2) + d];
+      if (m != -INFINITY) o += exp2f(m - M) * w[s * (D + 2) + d];
     }
     p.out[static_cast<int64_t>(seq) * p.out_stride + qh * D + d] = f2bf(o * inv);
   }
 }
 
-template <int D, int G>
+template <int D>
 static int launch_dec(const DecodeAttnParams& p, cudaStream_t st) {
-  using SM = DecSmem<D, G>;
+  using C = DecCfg<D>;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(decode_attn_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kBytes);
+    cudaFuncSetAttribute(decode_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     attr = true;
   }
-  dim3 grid(p.num_splits, p.num_kv_heads, p.num_seqs);
-  decode_attn_kernel<D, G><<<grid, kDecThreads, SM::kBytes, st>>>(p);
+  const int items = p.num_seqs * p.num_kv_heads * p.num_splits;
+  decode_attn_kernel<D><<<(items + C::kWarps - 1) / C::kWarps, C::kWarps * 32, C::kSmem, st>>>(p);
   if (p.num_splits > 1) decode_combine_kernel<D><<<dim3(p.num_q_heads, p.num_seqs), 128, 0, st>>>(p);
   return static_cast<int>(cudaGetLastError());
 }
@@ -295,13 +290,13 @@ static int launch_dec(const DecodeAttnParams& p, cudaStream_t st) {
 int decode_attention_launch(const DecodeAttnParams& p, cudaStream_t st) {
   if (p.num_seqs == 0) return 0;
   const int G = p.num_q_heads / p.num_kv_heads;
-#define RZ_DEC(DD, GG) \
-  if (p.head_dim == DD && G == GG) return launch_dec<DD, GG>(p, st);
-  RZ_DEC(128, 1) RZ_DEC(128, 2) RZ_DEC(128, 4) RZ_DEC(128, 8)
-  RZ_DEC(64, 1) RZ_DEC(64, 2) RZ_DEC(64, 4) RZ_DEC(64, 8)
-  RZ_DEC(256, 1) RZ_DEC(256, 2) RZ_DEC(256, 4) RZ_DEC(256, 8)
-#undef RZ_DEC
-  return -100;  // unsupported (head_dim, group) combination: caller splits heads
+  if (G < 1 || G > 16 || p.num_q_heads % p.num_kv_heads) return -100;
+  switch (p.head_dim) {
+    case 64: return launch_dec<64>(p, st);
+    case 128: return launch_dec<128>(p, st);
+    case 256: return launch_dec<256>(p, st);
+    default: return -100;
+  }
 }
 
 }  // namespace rz

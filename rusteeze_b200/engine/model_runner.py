@@ -47,13 +47,28 @@ def decode_graph_buckets(max_seqs: int) -> List[int]:
     return sorted(set(v for v in b if v <= max_seqs))
 
 
-def choose_num_splits(batch: int, num_kv_heads: int, max_blocks: int, num_sms: int = NUM_SMS_B200) -> int:
-    """Split-KV factor so that decode attention puts >= ~2 CTAs on every SM."""
-    ctas = batch * num_kv_heads
-    if ctas >= 2 * num_sms:
+def choose_num_splits(batch: int, num_kv_heads: int, max_blocks: int, num_sms: int = NUM_SMS_B200,
+                      warps_per_sm: int = 8) -> int:
+    """Split-KV factor for the decode kernel, whose work item is one warp per
+    (sequence, kv head, split): aim for about two items per resident warp so
+    the last wave is short."""
+    items = batch * num_kv_heads
+    target = 2 * num_sms * warps_per_sm
+    if items >= target:
         return 1
-    s = math.ceil(2 * num_sms / ctas)
+    s = math.ceil(target / items)
     return max(1, min(s, max_blocks, 64))
+
+
+def decode_workspace_floats(max_seqs: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                            max_blocks: int) -> int:
+    """Largest split-KV partial buffer any batch size up to max_seqs needs."""
+    need = 0
+    for b in range(1, max_seqs + 1):
+        s = choose_num_splits(b, num_kv_heads, max_blocks)
+        if s > 1:
+            need = max(need, b * num_q_heads * s * (head_dim + 2))
+    return max(need, 1)
 
 
 class ModelRunner:
@@ -94,9 +109,8 @@ class ModelRunner:
         self.d_seq_lens = torch.zeros(S, dtype=torch.int32, device=dev)
         self.d_block_tables = torch.zeros(S, MB, dtype=torch.int32, device=dev)
         self.d_logits_idx = torch.zeros(T, dtype=torch.int64, device=dev)
-        max_splits = choose_num_splits(1, hkv, self.max_blocks)
-        self.decode_ws = (torch.empty(S * model.hq * max_splits * (D + 2), dtype=torch.float32, device=dev)
-                          if self.is_cuda else None)
+        self.decode_ws = (torch.empty(decode_workspace_floats(S, model.hq, hkv, D, self.max_blocks),
+                                      dtype=torch.float32, device=dev) if self.is_cuda else None)
         self.sampler = Sampler(self.cfg.vocab_size)
         self.use_cuda_graph = use_cuda_graph and self.is_cuda
         self.graphs: Dict[int, Tuple[torch.cuda.CUDAGraph, torch.Tensor]] = {}
