@@ -271,7 +271,10 @@ __global__ void __launch_bounds__(kSampThreads)
   const float mp = minp[row];
   // min-p: keep p >= mp * p_max  <=>  u <= -ln(mp)
   const float u_minp = mp > 0.f ? -__logf(mp) : INFINITY;
-  float u_thr = INFINITY;  // keep u < u_thr (exclusive upper edge of the last kept bucket)
+  // kept set = tokens whose (coarse bucket, fine bucket) index pair is <= (kb1, kb2); the
+  // comparison uses the same integer bucket functions as the histograms, so the boundary
+  // token is classified exactly as it was counted (a float threshold can round past it)
+  int kb1 = kBuckets, kb2 = kBuckets - 1;
   const bool need = (k < V) || (pth < 1.f);
   const float u_range = (mx - mn) * invT;
   const bool clamped = u_range > kUMax;
@@ -333,13 +336,16 @@ __global__ void __launch_bounds__(kSampThreads)
         long c2;
         float m2;
         scan_buckets(cnt, mass, k - cb, m_target - mb, b2, c2, m2);
-        if (tid == 0) s_thr[3] = b2 >= kBuckets ? (b + 1) * w1 : lo + (b2 + 1) * w2;
+        if (tid == 0) s_thr[3] = static_cast<float>(b2 >= kBuckets ? kBuckets - 1 : b2);
       }
       __syncthreads();
-      u_thr = s_thr[3];
+      kb1 = b;
+      kb2 = static_cast<int>(s_thr[3]);
     }
   }
-  const float u_keep = fminf(u_thr, u_minp);
+  const float inv_w1 = 1.f / w1;
+  const float lo1 = kb1 < kBuckets ? kb1 * w1 : 0.f;
+  const float inv_w2k = 1.f / (w1 / kBuckets);   // bit-identical to pass 3's 1 / w2
 
   // pass 4: Gumbel-max over kept tokens (and their mass for the logprob)
   const uint64_t seed = static_cast<uint64_t>(seeds[row]);
@@ -349,7 +355,12 @@ __global__ void __launch_bounds__(kSampThreads)
   float kept = 0.f;
   for (int i = tid; i < V; i += blockDim.x) {
     const float u = (mx - x[i]) * invT;
-    const bool keep = (u < u_keep) || (u == 0.f);
+    bool keep = true;
+    if (kb1 < kBuckets) {
+      const int c1 = bucket_of(u, 0.f, inv_w1);
+      keep = c1 < kb1 || (c1 == kb1 && bucket_of(u, lo1, inv_w2k) <= kb2);
+    }
+    keep = (keep && u <= u_minp) || (u == 0.f);
     if (keep) {
       const float e = __expf(-u);
       kept += e;
