@@ -180,6 +180,8 @@ class DecoderLM(nn.Module):
         if self.inter % 64:
             return
         for L in self.layers:
+            if getattr(L, "gate_up_il", None) is not None:
+                continue
             L.gate_up_il = ops.interleave_gate_up(L.gate_up)
             L.gate_up = nn.Parameter(torch.empty(0, dtype=self.dtype, device=self.device), requires_grad=False)
 

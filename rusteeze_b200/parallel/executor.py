@@ -1,0 +1,173 @@
+"""Tensor-parallel execution: rank 0 schedules, every rank runs the forward.
+
+Rank 0 owns the engine (scheduler, block manager, sampler, API).  For each
+step it packs the batch plan -- the staged input arrays (token ids,
+positions, slot mapping, cu-seqlens, sequence lengths, block tables),
+sample rows, and the swap / copy-on-write block lists -- and publishes it
+on a shared-memory broadcast ring (C++ `ShmRing`, no collective and no
+device sync on the control path).  Worker ranks (one process per GPU)
+consume the plan, stage it into their own pinned buffers, and run the same
+forward on their weight shard; the model's collectives (NCCL or the fused
+peer-memory kernels) keep them in lock step.  Only rank 0 samples.
+
+Failure handling: every ring wait is bounded; a worker that sees no plan
+within `idle_timeout_s` checks the ring's closed flag and rank 0's
+liveness, and the process group's timeout turns a dead rank into an error
+on the survivors (the engine then reports unhealthy).
+"""
+from __future__ import annotations
+
+import logging
+import os
+import pickle
+import time
+from typing import List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from rusteeze_b200.engine.model_runner import ModelRunner
+from rusteeze_b200.engine.sampler import SampleResult
+
+log = logging.getLogger("rusteeze.tp")
+
+MSG_STEP, MSG_STOP = 1, 2
+
+
+def _ring_name(tag: str) -> str:
+    return f"/rz_plan_{tag}"
+
+
+class PlanChannel:
+    def __init__(self, tag: str, rank: int, world: int, slot_bytes: int = 8 << 20, create: Optional[bool] = None):
+        from rusteeze_b200.engine.block_manager import host_ext
+        H = host_ext()
+        self.rank, self.world = rank, world
+        create = (rank == 0) if create is None else create
+        self.ring = H.ShmRing(_ring_name(tag), create, 4, slot_bytes, max(0, world - 1))
+
+    def publish(self, kind: int, payload) -> None:
+        data = pickle.dumps((kind, payload), protocol=pickle.HIGHEST_PROTOCOL)
+        if not self.ring.publish(data, 60.0):
+            raise TimeoutError("tensor-parallel worker did not consume the previous plan within 60 s")
+
+    def consume(self, timeout_s: float = 1.0):
+        b = self.ring.consume(self.rank - 1, timeout_s)
+        if b is None:
+            return None
+        return pickle.loads(b)
+
+    def close(self) -> None:
+        self.ring.close()
+
+
+class TPExecutor:
+    """Drop-in for ModelRunner on rank 0 (`LLMEngine(executor=...)`)."""
+
+    def __init__(self, runner: ModelRunner, channel: PlanChannel):
+        self.runner = runner
+        self.ch = channel
+
+    def __getattr__(self, k):
+        return getattr(self.runner, k)
+
+    def capture_graphs(self, buckets=None) -> None:
+        self.ch.publish(MSG_STEP, {"capture": list(buckets) if buckets is not None else None})
+        self.runner.capture_graphs(buckets)
+
+    @torch.no_grad()
+    def execute(self, so, bm, rows) -> SampleResult:
+        r = self.runner
+        meta, T, S, sample_rows = r.prepare(so, bm)
+        MB = int(max(1, (int(r.h_seq_lens[:S].max()) + 15) // 16)) if S else 1
+        plan = {
+            "T": T, "S": S, "nd": len(so.decodes), "maxq": meta.max_query_len, "maxs": meta.max_seq_len,
+            "pure": not so.prefills, "rows": sample_rows, "mb": MB,
+            "ids": r.h_input_ids[:T].numpy().copy(), "pos": r.h_positions[:T].numpy().copy(),
+            "slots": r.h_slots[:T].numpy().copy(), "qsl": r.h_qsl[:S + 1].numpy().copy(),
+            "sl": r.h_seq_lens[:S].numpy().copy(), "bt": r.h_block_tables[:S, :MB].numpy().copy(),
+            "copy": so.blocks_to_copy, "sin": so.blocks_to_swap_in, "sout": so.blocks_to_swap_out,
+        }
+        self.ch.publish(MSG_STEP, plan)
+        if so.blocks_to_swap_out:
+            r.swap_out(so.blocks_to_swap_out)
+        if so.blocks_to_swap_in:
+            r.swap_in(so.blocks_to_swap_in)
+        if so.blocks_to_copy:
+            r.copy_blocks(so.blocks_to_copy)
+        logits = r.forward_logits(meta, T, S, sample_rows, pure_decode=not so.prefills)
+        res = r.sampler.sample(logits, rows)
+        r.h2d_bytes += r.sampler.last_h2d_bytes
+        r.d2h_bytes += r.sampler.last_d2h_bytes
+        return res
+
+    def shutdown(self) -> None:
+        try:
+            self.ch.publish(MSG_STOP, None)
+        finally:
+            self.ch.close()
+
+
+def stage_plan(runner: ModelRunner, plan) -> Tuple[object, int, int]:
+    """Worker side: copy a received plan into the runner's staging buffers."""
+    from rusteeze_b200.engine.model_runner import choose_num_splits
+    from rusteeze_b200.models.decoder import AttentionMetadata
+    r = runner
+    T, S, MB = plan["T"], plan["S"], plan["mb"]
+    r.h_input_ids[:T] = torch.from_numpy(plan["ids"])
+    r.h_positions[:T] = torch.from_numpy(plan["pos"])
+    r.h_slots[:T] = torch.from_numpy(plan["slots"])
+    r.h_qsl[:S + 1] = torch.from_numpy(plan["qsl"])
+    r.h_seq_lens[:S] = torch.from_numpy(plan["sl"])
+    r.h_block_tables[:S].zero_()
+    r.h_block_tables[:S, :MB] = torch.from_numpy(plan["bt"])
+    nb = r.is_cuda
+    r.d_input_ids[:T].copy_(r.h_input_ids[:T], non_blocking=nb)
+    r.d_positions[:T].copy_(r.h_positions[:T], non_blocking=nb)
+    r.d_slots[:T].copy_(r.h_slots[:T], non_blocking=nb)
+    r.d_qsl[:S + 1].copy_(r.h_qsl[:S + 1], non_blocking=nb)
+    r.d_seq_lens[:S].copy_(r.h_seq_lens[:S], non_blocking=nb)
+    r.d_block_tables[:S].copy_(r.h_block_tables[:S], non_blocking=nb)
+    meta = AttentionMetadata(
+        num_seqs=S, num_tokens=T, num_decode_seqs=plan["nd"], query_start_loc=r.d_qsl[:S + 1],
+        seq_lens=r.d_seq_lens[:S], block_tables=r.d_block_tables[:S], slot_mapping=r.d_slots[:T],
+        max_query_len=plan["maxq"], max_seq_len=plan["maxs"],
+        decode_num_splits=choose_num_splits(max(plan["nd"], 1), r.model.hkv, r.max_blocks),
+        decode_workspace=r.decode_ws)
+    if not r.is_cuda:
+        meta.query_start_loc = r.h_qsl[:S + 1].clone()
+        meta.seq_lens = r.h_seq_lens[:S].clone()
+        meta.block_tables = r.h_block_tables[:S].clone()
+    return meta, T, S
+
+
+@torch.no_grad()
+def worker_loop(runner: ModelRunner, channel: PlanChannel, idle_timeout_s: float = 600.0) -> int:
+    """Runs plans until rank 0 sends STOP or closes the ring.  Returns steps run."""
+    steps = 0
+    idle_since = time.monotonic()
+    while True:
+        msg = channel.consume(1.0)
+        if msg is None:
+            if channel.ring.closed:
+                return steps
+            if time.monotonic() - idle_since > idle_timeout_s:
+                log.error("worker %d: no plan from rank 0 for %.0f s, exiting", channel.rank, idle_timeout_s)
+                return steps
+            continue
+        idle_since = time.monotonic()
+        kind, plan = msg
+        if kind == MSG_STOP:
+            return steps
+        if "capture" in plan:
+            runner.capture_graphs(plan["capture"])
+            continue
+        if plan["sout"]:
+            runner.swap_out(plan["sout"])
+        if plan["sin"]:
+            runner.swap_in(plan["sin"])
+        if plan["copy"]:
+            runner.copy_blocks(plan["copy"])
+        meta, T, S = stage_plan(runner, plan)
+        runner.forward_logits(meta, T, S, plan["rows"], pure_decode=plan["pure"])
+        steps += 1

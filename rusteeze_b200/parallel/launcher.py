@@ -1,0 +1,149 @@
+"""Bring-up of a tensor-parallel engine: one process per GPU.
+
+`tp_rank_setup` is what every rank runs (under torchrun or the spawner
+below): init the process group, build this rank's weight shard, agree on
+the KV block count (MIN over ranks of what each GPU can hold), build the
+ModelRunner and the plan channel.  Rank 0 then wraps its runner in a
+`TPExecutor` and builds the `LLMEngine`; other ranks enter `worker_loop`.
+
+`TPEngineLauncher` spawns ranks 1..N-1 from the serving process (used by
+`rusteeze serve --tensor-parallel-size N`).
+"""
+from __future__ import annotations
+
+import copy
+import logging
+import os
+import socket
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from rusteeze_b200.config.config import Config
+from rusteeze_b200.engine.model_runner import ModelRunner
+from rusteeze_b200.models.config import ModelConfig, get_preset
+from rusteeze_b200.models.loader import build_model
+from rusteeze_b200.parallel.dist import DistInfo, TPComm, init_distributed
+from rusteeze_b200.parallel.executor import PlanChannel, TPExecutor, worker_loop
+
+log = logging.getLogger("rusteeze.tp")
+
+
+def free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _model_config(cfg: Config) -> ModelConfig:
+    mc = cfg.model
+    return ModelConfig.from_json_file(mc.path) if mc.path else get_preset(mc.preset or "tiny-llama")
+
+
+def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfig] = None, tag: str = "0"):
+    from rusteeze_b200.engine.llm_engine import LLMEngine, _dtype
+    mc = model_config or _model_config(cfg)
+    ec = cfg.engine
+    dev = str(info.device)
+    dtype = _dtype(cfg.model.dtype, dev)
+    max_len = min(cfg.model.max_model_len or mc.max_position_embeddings, mc.max_position_embeddings)
+    tp = TPComm(info.rank, info.world_size, group=dist.group.WORLD if info.world_size > 1 else None,
+                mode=ec.comm_backend if info.device.type == "cuda" else "nccl", device=info.device,
+                max_tokens=max(ec.max_num_batched_tokens, ec.max_num_seqs), hidden=mc.hidden_size)
+    model = build_model(mc, dtype=dtype, device=dev, tp=tp, model_dir=cfg.model.path, seed=cfg.model.seed)
+    if info.device.type == "cuda":
+        model.prepare_for_gpu()
+    # agree on the KV block count
+    if ec.num_gpu_blocks:
+        nblocks = ec.num_gpu_blocks
+    elif info.device.type == "cuda":
+        free, total = torch.cuda.mem_get_info()
+        budget = total * ec.gpu_memory_utilization - (total - free) - 4 * (1 << 30)
+        per_block = 2 * mc.num_hidden_layers * model.hkv * mc.head_dim * 16 * torch.finfo(dtype).bits // 8
+        nblocks = int(budget // per_block)
+    else:
+        nblocks = 256
+    if info.world_size > 1:
+        t = torch.tensor([nblocks], dtype=torch.int64, device=info.device if info.backend == "nccl" else "cpu")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        nblocks = int(t.item())
+    runner = ModelRunner(model, num_gpu_blocks=nblocks, num_cpu_blocks=0, max_num_seqs=ec.max_num_seqs,
+                         max_num_batched_tokens=ec.max_num_batched_tokens, max_model_len=max_len,
+                         use_cuda_graph=not ec.enforce_eager, seed=cfg.model.seed)
+    channel = None
+    if info.world_size > 1:
+        if info.rank == 0:
+            channel = PlanChannel(tag, 0, info.world_size)
+        dist.barrier()
+        if info.rank != 0:
+            channel = PlanChannel(tag, info.rank, info.world_size)
+        dist.barrier()
+    ecfg = copy.deepcopy(cfg)
+    ecfg.engine.num_gpu_blocks = nblocks
+    ecfg.engine.swap_space_gb = 0.0
+    ecfg.model.device = dev
+    if info.rank == 0:
+        executor = TPExecutor(runner, channel) if channel is not None else runner
+        engine = LLMEngine(ecfg, model=model, executor=executor)
+        return engine, runner, channel
+    return None, runner, channel
+
+
+def tp_worker_main(cfg: Config, info: DistInfo, model_config: Optional[ModelConfig] = None, tag: str = "0") -> int:
+    _, runner, channel = tp_rank_setup(cfg, info, model_config, tag)
+    steps = worker_loop(runner, channel)
+    return steps
+
+
+def _spawned_worker(rank: int, world: int, port: int, cfg_dict: dict, mc_dict: Optional[dict], tag: str,
+                    device_type: str) -> None:
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from rusteeze_b200.config.config import config_from_dict
+    cfg = config_from_dict(cfg_dict)
+    mc = ModelConfig(**mc_dict) if mc_dict else None
+    info = init_distributed(device_type=device_type)
+    try:
+        tp_worker_main(cfg, info, mc, tag)
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+class TPEngineLauncher:
+    """Spawns ranks 1..N-1 and builds rank 0's engine in this process."""
+
+    def __init__(self, cfg: Config, model_config: Optional[ModelConfig] = None, device_type: Optional[str] = None):
+        import torch.multiprocessing as mp
+        self.cfg = cfg
+        self.world = cfg.model.tensor_parallel_size
+        self.device_type = device_type or ("cuda" if torch.cuda.is_available() else "cpu")
+        port = free_port()
+        self.tag = f"{os.getpid()}_{port}"
+        ctx = mp.get_context("spawn")
+        mc_dict = model_config.to_dict() if model_config else None
+        self.procs = [ctx.Process(target=_spawned_worker, args=(r, self.world, port, cfg.to_dict(), mc_dict,
+                                                                 self.tag, self.device_type), daemon=True)
+                      for r in range(1, self.world)]
+        for p in self.procs:
+            p.start()
+        os.environ.update(RANK="0", WORLD_SIZE=str(self.world), LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(port))
+        info = init_distributed(device_type=self.device_type)
+        self._engine, self.runner, self.channel = tp_rank_setup(cfg, info, model_config, self.tag)
+
+    def engine(self):
+        return self._engine
+
+    def shutdown(self, timeout: float = 30.0) -> None:
+        if self.channel is not None:
+            self._engine.runner.shutdown()
+        for p in self.procs:
+            p.join(timeout)
+            if p.is_alive():
+                p.terminate()
+        if dist.is_initialized():
+            dist.destroy_process_group()

@@ -32,7 +32,12 @@ def peaks() -> Dict[str, float]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
-def time_ms(fn: Callable[[], None], iters: int = 20, warmup: int = 5) -> float:
+ITERS = [20, 5]     # timed iterations, warm-up launches (overridable from the command line)
+
+
+def time_ms(fn: Callable[[], None], iters: int = 0, warmup: int = -1) -> float:
+    iters = iters or ITERS[0]
+    warmup = ITERS[1] if warmup < 0 else warmup
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -167,11 +172,22 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,decode,prefill,norm,sample")
     ap.add_argument("--json", default=None)
+    ap.add_argument("--gemm", default=None, help="single GEMM case M,N,K")
+    ap.add_argument("--decode", default=None, help="single decode case B,ctx,Hq,Hkv")
+    ap.add_argument("--prefill", default=None, help="single prefill case seqs,len,Hq,Hkv")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args()
+    ITERS[0], ITERS[1] = a.iters, a.warmup
     pk = peaks()
     res = {"peaks": pk}
+    cases = {"gemm": a.gemm, "decode": a.decode, "prefill": a.prefill}
     for name in a.only.split(","):
-        res[name] = globals()[f"bench_{name}"](pk)
+        c = cases.get(name)
+        if c:
+            res[name] = globals()[f"bench_{name}"](pk, [tuple(int(x) for x in c.split(","))])
+        else:
+            res[name] = globals()[f"bench_{name}"](pk)
         for row in res[name]:
             print(json.dumps(row), flush=True)
     if a.json:

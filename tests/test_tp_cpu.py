@@ -1,0 +1,53 @@
+"""Tensor parallelism on CPU gloo ranks (world 2): the rank-0 engine with a
+worker process must produce the same greedy tokens as the single-process
+engine; plan broadcast goes over the shared-memory ring."""
+import numpy as np
+import pytest
+
+from rusteeze_b200.config.config import Config
+from rusteeze_b200.core.sampling_params import SamplingParams
+from rusteeze_b200.engine.llm_engine import LLMEngine
+from rusteeze_b200.models.config import ModelConfig
+
+
+def _cfg(tp):
+    cfg = Config()
+    cfg.model.device = "cpu"
+    cfg.model.dtype = "float32"
+    cfg.model.tensor_parallel_size = tp
+    cfg.engine.num_gpu_blocks = 96
+    cfg.engine.max_num_seqs = 4
+    cfg.engine.max_num_batched_tokens = 128
+    cfg.engine.enable_chunked_prefill = True
+    cfg.engine.comm_backend = "nccl"
+    return cfg
+
+
+MC = ModelConfig(name="tp-tiny", hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                 num_attention_heads=4, num_key_value_heads=2, vocab_size=1000, rms_norm_eps=1e-5,
+                 max_position_embeddings=512)
+
+
+def _run(eng, prompts, n=6):
+    sp = SamplingParams(temperature=0.0, max_tokens=n, ignore_eos=True)
+    ids = [eng.add_request(None, None, sp, p).request_id for p in prompts]
+    done = {}
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            if o.finished:
+                done[o.request_id] = o.outputs[0].token_ids
+    return [done[i] for i in ids]
+
+
+@pytest.mark.timeout(300)
+def test_tp2_gloo_matches_single_process():
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(0, 1000, int(n)).tolist() for n in (30, 77, 5)]
+    ref = _run(LLMEngine(_cfg(1), model_config=MC), prompts)
+    launcher = TPEngineLauncher(_cfg(2), model_config=MC, device_type="cpu")
+    try:
+        got = _run(launcher.engine(), prompts)
+    finally:
+        launcher.shutdown()
+    assert got == ref
