@@ -208,12 +208,21 @@ void quant_fp8_act(torch::Tensor xq, torch::Tensor xs, torch::Tensor x) {
            "quant_fp8_act");
 }
 
-void gemm_fp8_block(torch::Tensor out, torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws,
-                    c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual) {
+// Returns the number of kernels launched.
+int64_t gemm_fp8_block(torch::Tensor out, torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws,
+                       c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual, int64_t epi,
+                       int64_t k_splits) {
   const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
-  TORCH_CHECK(K % 128 == 0 && N % 16 == 0, "fp8 gemm: K % 128, N % 16");
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "fp8 gemm: K and N must be multiples of 128");
+  TORCH_CHECK(wq.size(1) == K, "fp8 gemm: K mismatch");
+  TORCH_CHECK(xq.element_size() == 1 && wq.element_size() == 1, "fp8 gemm: e4m3 operands");
+  TORCH_CHECK(xs.scalar_type() == at::kFloat && ws.scalar_type() == at::kFloat, "fp8 gemm: fp32 scales");
+  if (epi == rz::kEpiSiluMul) TORCH_CHECK(out.size(1) == N / 2, "silu epilogue: out has N/2 columns");
+  if (k_splits <= 0) k_splits = rz::fp8_plan_splits(M, N, K);
   rz::Fp8GemmParams p{};
   p.M = M; p.N = N; p.K = K;
+  p.k_splits = k_splits;
+  p.epi = epi;
   p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.ldd = out.stride(0);
   p.a_scale = xs.data_ptr<float>();
@@ -224,8 +233,14 @@ void gemm_fp8_block(torch::Tensor out, torch::Tensor xq, torch::Tensor xs, torch
   p.residual = residual.has_value() ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
   p.ldr = residual.has_value() ? residual->stride(0) : 0;
   p.status = status_ptr();
+  torch::Tensor wsp;
+  if (k_splits > 1) {
+    wsp = torch::empty({k_splits, M, N}, xq.options().dtype(torch::kFloat32));
+    p.partial = wsp.data_ptr<float>();
+  }
   check_rc(rz::gemm_fp8_launch(p, xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), cur_stream()),
            "gemm_fp8_block");
+  return k_splits > 1 ? 2 : 1;
 }
 
 // ---------------------------------------------------------------- sampling

@@ -32,6 +32,7 @@ struct GemmPlan {
 };
 
 GemmPlan plan_gemm(int M, int N, int K, int epi);
+__global__ void gemm_splitk_reduce(GemmParams p);
 int gemm_bf16_launch(const GemmParams& p, const void* A, int lda, const void* B, int ldb, int bn,
                      cudaStream_t stream);
 int make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int elem_bytes, int64_t rows,

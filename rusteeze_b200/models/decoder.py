@@ -162,7 +162,22 @@ class DecoderLM(nn.Module):
             h = h * torch.tensor(self.cfg.embed_scale, dtype=self.dtype)
         return h
 
+    def _lin(self, x: torch.Tensor, owner, name: str, bias=None) -> torch.Tensor:
+        q = getattr(owner, name + "_q", None)
+        if q is not None:
+            return ops.linear_fp8(x, q, getattr(owner, name + "_s"), bias)
+        return ops.linear(x, getattr(owner, name), bias)
+
+    def _row_parallel(self, x: torch.Tensor, owner, name: str) -> torch.Tensor:
+        q = getattr(owner, name + "_q", None)
+        if q is not None:
+            return self.tp.all_reduce(ops.linear_fp8(x, q, getattr(owner, name + "_s")))
+        return self.tp.row_parallel_linear(x, getattr(owner, name))
+
     def _mlp(self, L, h: torch.Tensor) -> torch.Tensor:
+        if getattr(L, "gate_up_q", None) is not None:
+            a = ops.linear_fp8(h, L.gate_up_q, L.gate_up_s, silu_mul=True)
+            return self._row_parallel(a, L, "down")
         if getattr(L, "gate_up_il", None) is not None and h.is_cuda:
             a = ops.linear_silu_mul(h, L.gate_up_il)      # SiLU(gate)*up fused in the GEMM epilogue
         else:
@@ -175,7 +190,7 @@ class DecoderLM(nn.Module):
         """Re-lays weights for the GPU kernels: gate/up rows interleaved in
         64-row blocks for the fused SiLU epilogue (the [gate | up] copy is
         dropped to save HBM)."""
-        if not self.device.type == "cuda" or self.cfg.is_moe or self.act != "silu":
+        if not self.device.type == "cuda" or self.cfg.is_moe or self.act != "silu" or getattr(self, "fp8", False):
             return
         if self.inter % 64:
             return
@@ -205,12 +220,12 @@ class DecoderLM(nn.Module):
                 x = ops.rms_norm(h, L.input_norm, eps, off)
             else:
                 x, residual = ops.fused_add_rms_norm(h, residual, L.input_norm, eps, off)
-            qkv = ops.linear(x, L.qkv, L.qkv_bias)
+            qkv = self._lin(x, L, "qkv", L.qkv_bias)
             q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
                                    self.hq, self.hkv, D)
             a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
                                     cfg.attn_logit_softcapping)
-            h = self.tp.row_parallel_linear(a.view(a.shape[0], -1), L.o)
+            h = self._row_parallel(a.view(a.shape[0], -1), L, "o")
             if self.is_gemma2:
                 h = ops.rms_norm(h, L.post_attn_norm, eps, off)
                 x, residual = ops.fused_add_rms_norm(h, residual, L.pre_ff_norm, eps, off)
@@ -224,7 +239,10 @@ class DecoderLM(nn.Module):
 
     def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
         """h [n, H] -> fp32 logits [n, vocab] (gathered over TP ranks)."""
-        logits = ops.linear(h, self.lm_head_weight)
+        if getattr(self, "lm_head_q", None) is not None:
+            logits = ops.linear_fp8(h, self.lm_head_q, self.lm_head_s)
+        else:
+            logits = ops.linear(h, self.lm_head_weight)
         if self.tp.size > 1:
             logits = self.tp.all_gather_last_dim(logits)
         logits = logits[:, : self.cfg.vocab_size].float()

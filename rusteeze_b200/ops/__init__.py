@@ -205,26 +205,45 @@ def linear_silu_mul(x: torch.Tensor, w_il: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def quant_fp8_act(x: torch.Tensor):
+    """bf16 [M, K] -> (e4m3 [M, K], fp32 scales [K/128, M]) with 1x128 groups."""
+    M, K = x.shape
+    if not x.is_cuda:
+        q, s = ref.quant_fp8_act(x)
+        return q, s.t().contiguous()
+    xq = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
+    xs = torch.empty(K // 128, M, dtype=torch.float32, device=x.device)
+    if M:
+        cuda_ext().quant_fp8_act(xq, xs, x)
+        _LAUNCHES[0] += 1
+    return xq, xs
+
+
 def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
                bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
-               out_dtype=torch.bfloat16) -> torch.Tensor:
-    """Block-scaled fp8 GEMM: x bf16 [M,K] is quantised 1x128 on the fly,
-    wq e4m3 [N,K] with fp32 128x128 scales ws."""
+               silu_mul: bool = False) -> torch.Tensor:
+    """Block-scaled fp8 GEMM: x bf16 [M,K] is quantised 1x128 on the fly (one
+    kernel), wq e4m3 [N,K] carries fp32 128x128 scales ws [N/128, K/128].
+    With silu_mul the weight rows are gate/up interleaved in 64-row blocks and
+    the output is silu(gate) * up with N/2 columns."""
+    M, N = x.shape[0], wq.shape[0]
+    n_out = N // 2 if silu_mul else N
     if not x.is_cuda:
-        xq, xs = ref.quant_fp8_act(x)
-        y = ref.fp8_block_gemm(xq, xs, wq, ws)
+        xq, xs = quant_fp8_act(x)
+        y = ref.fp8_block_gemm(xq, xs.t(), wq, ws)
         if bias is not None:
             y = y + bias.float()
+        if silu_mul:
+            v = y.view(M, N // 128, 2, 64)
+            y = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(M, n_out)
         if residual is not None:
             y = y + residual.float()
-        return y.to(out_dtype)
-    C = cuda_ext()
-    M, K = x.shape
-    xq = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
-    xs = torch.empty(K // 128, M, dtype=torch.float32, device=x.device)   # K-block-major scales
-    C.quant_fp8_act(xq, xs, x)
-    out = torch.empty(M, wq.shape[0], dtype=out_dtype, device=x.device)
-    C.gemm_fp8_block(out, xq, xs, wq, ws, bias, residual)
+        return y.to(x.dtype)
+    out = torch.empty(M, n_out, dtype=torch.bfloat16, device=x.device)
+    if M == 0:
+        return out
+    xq, xs = quant_fp8_act(x)
+    _LAUNCHES[0] += cuda_ext().gemm_fp8_block(out, xq, xs, wq, ws, bias, residual, 1 if silu_mul else 0, 0)
     return out
 
 

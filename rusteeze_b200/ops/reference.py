@@ -221,7 +221,7 @@ def quant_fp8_weight(w: torch.Tensor, block: int = 128):
     """128x128 block weight quant: w [N, K] -> (q [N,K] e4m3, scales fp32 [ceil(N/b), K/b])."""
     N, K = w.shape
     nb = (N + block - 1) // block
-    wp = torch.zeros(nb * block, K, dtype=torch.float32)
+    wp = torch.zeros(nb * block, K, dtype=torch.float32, device=w.device)
     wp[:N] = w.float()
     wb = wp.view(nb, block, K // block, block)
     amax = wb.abs().amax(dim=(1, 3)).clamp_min(1e-12)
@@ -236,7 +236,7 @@ def fp8_block_gemm(xq, xs, wq, ws, block: int = 128):
     N = wq.shape[0]
     x = xq.float().view(M, K // block, block) * xs.unsqueeze(-1)
     nb = ws.shape[0]
-    wp = torch.zeros(nb * block, K)
+    wp = torch.zeros(nb * block, K, device=wq.device)
     wp[:N] = wq.float()
     w = (wp.view(nb, block, K // block, block) * ws[:, None, :, None]).view(nb * block, K)[:N]
     return x.view(M, K) @ w.t()

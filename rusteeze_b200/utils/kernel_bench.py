@@ -85,6 +85,31 @@ def bench_gemm(pk, shapes=None) -> List[dict]:
     return out
 
 
+def bench_gemm_fp8(pk, shapes=None) -> List[dict]:
+    """Block-scaled fp8 GEMM incl. the 1x128 activation quantisation kernel."""
+    shapes = shapes or [(8, 6144, 4096), (256, 28672, 4096), (256, 4096, 14336), (1256, 28672, 4096),
+                        (1256, 4096, 14336), (4096, 4096, 4096), (8192, 8192, 8192)]
+    out = []
+    for M, N, K in shapes:
+        ncopies = max(1, min(8, int(3 * 126e6 // (N * K)) + 1))
+        qs = [ref.quant_fp8_weight(torch.randn(N, K, device="cuda") * 0.02) for _ in range(ncopies)]
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        it = [0]
+
+        def ours():
+            it[0] = (it[0] + 1) % ncopies
+            ops.linear_fp8(x, *qs[it[0]])
+
+        t = time_ms(ours)
+        flops = 2.0 * M * N * K
+        bytes_ = N * K + M * K * 2 + M * N * 2
+        out.append({"kernel": "gemm_fp8_block_tcgen05", "M": M, "N": N, "K": K, "ms": round(t, 4),
+                    "tflops": round(flops / t / 1e9, 1), "gbs": round(bytes_ / t / 1e6, 1),
+                    "frac_of_measured_hbm": round(bytes_ / t / 1e6 / pk["hbm_gbs"], 3)})
+        del qs
+    return out
+
+
 def bench_decode(pk, cases=None) -> List[dict]:
     cases = cases or [(1, 1024, 32, 8), (16, 1024, 32, 8), (64, 2048, 32, 8), (256, 1232, 32, 8),
                       (256, 4096, 32, 8)]

@@ -1,0 +1,125 @@
+"""FP8 block-scaled path: codec vs torch float8, quantised model on CPU
+(oracle math), and the sm_100a kernels (GPU) vs the dequantise-then-matmul
+fp32 oracle."""
+import dataclasses
+
+import pytest
+import torch
+
+from rusteeze_b200 import ops
+from rusteeze_b200.models.config import ModelConfig
+from rusteeze_b200.ops import reference as ref
+
+
+def test_weight_and_activation_codec_roundtrip():
+    torch.manual_seed(0)
+    w = torch.randn(300, 512) * 0.05
+    q, s = ref.quant_fp8_weight(w)
+    assert q.dtype == torch.float8_e4m3fn and s.shape == (3, 4)
+    deq = (torch.zeros(384, 512).index_copy_(0, torch.arange(300), q.float())
+           .view(3, 128, 4, 128) * s[:, None, :, None]).view(384, 512)[:300]
+    assert ((deq - w).abs().max() / w.abs().max()) < 0.07          # e4m3: 3 mantissa bits
+    x = torch.randn(7, 256)
+    xq, xs = ref.quant_fp8_act(x)
+    assert xs.shape == (7, 2)
+    back = xq.float().view(7, 2, 128) * xs.unsqueeze(-1)
+    assert torch.allclose(back.view(7, 256), x, rtol=0.07, atol=1e-3)
+
+
+def test_fp8_model_cpu_tracks_bf16_model():
+    from rusteeze_b200.models.loader import build_model
+    from rusteeze_b200.models.naive import naive_logits
+    from rusteeze_b200.models.quant import quantize_model_fp8
+    from rusteeze_b200.models.decoder import AttentionMetadata
+    mc = ModelConfig(name="fp8-tiny", hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                     num_attention_heads=4, num_key_value_heads=2, vocab_size=1024, max_position_embeddings=512)
+    m = build_model(mc, dtype=torch.float32, seed=1)
+    p = list(range(3, 40))
+    ref_logits = naive_logits(m, p)[-1]
+    quantize_model_fp8(m)
+    # paged forward of the quantised model (1 sequence, 1 block table)
+    T = len(p)
+    nb = (T + 15) // 16
+    kv = [(torch.zeros(8, m.hkv, 16, mc.head_dim), torch.zeros(8, m.hkv, 16, mc.head_dim))
+          for _ in range(mc.num_hidden_layers)]
+    meta = AttentionMetadata(num_seqs=1, num_tokens=T, num_decode_seqs=0,
+                             query_start_loc=torch.tensor([0, T], dtype=torch.int32),
+                             seq_lens=torch.tensor([T], dtype=torch.int32),
+                             block_tables=torch.arange(nb, dtype=torch.int32).view(1, nb),
+                             slot_mapping=torch.arange(T), max_query_len=T)
+    h = m(torch.tensor(p), torch.arange(T), meta, kv)
+    logits = m.compute_logits(h[-1:])[0]
+    cos = torch.nn.functional.cosine_similarity(logits, ref_logits, dim=0)
+    assert cos > 0.99, float(cos)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(1, 256, 256), (7, 4096, 4096), (256, 6144, 4096), (1300, 4096, 14336),
+                                   (64, 1024, 512), (129, 128256 // 8, 1024)])
+def test_gemm_fp8_vs_oracle(M, N, K):
+    torch.manual_seed(M + N)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda") * 0.02
+    wq, ws = ref.quant_fp8_weight(w)
+    y = ops.linear_fp8(x, wq, ws)
+    xq, xs = ops.quant_fp8_act(x)
+    r = ref.fp8_block_gemm(xq.cpu(), xs.t().cpu(), wq.cpu(), ws.cpu())
+    err = ((y.float().cpu() - r).norm() / r.norm()).item()
+    assert err < 1e-2, err
+    torch.cuda.synchronize()
+    assert int(ops.cuda_ext().status()[0]) == 0
+
+
+@pytest.mark.gpu
+def test_quant_act_kernel_matches_reference():
+    x = torch.randn(33, 1024, device="cuda", dtype=torch.bfloat16) * 3
+    q, s = ops.quant_fp8_act(x)
+    qr, sr = ref.quant_fp8_act(x.cpu())
+    assert torch.allclose(s.t().cpu(), sr, rtol=1e-6)
+    assert (q.float().cpu() - qr.float()).abs().max() <= 1.0 * qr.float().abs().max() * 0.07
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ks", [1, 4])
+def test_gemm_fp8_silu_and_splitk(ks):
+    torch.manual_seed(7)
+    M, I, K = 200, 512, 2048
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    wg = torch.randn(I, K, device="cuda") * 0.03
+    wu = torch.randn(I, K, device="cuda") * 0.03
+    wi = ops.interleave_gate_up(torch.cat([wg, wu]).to(torch.bfloat16)).float()
+    wq, ws = ref.quant_fp8_weight(wi)
+    xq, xs = ops.quant_fp8_act(x)
+    out = torch.empty(M, I, device="cuda", dtype=torch.bfloat16)
+    ops.cuda_ext().gemm_fp8_block(out, xq, xs, wq, ws, None, None, 1, ks)
+    full = ref.fp8_block_gemm(xq.cpu(), xs.t().cpu(), wq.cpu(), ws.cpu()).view(M, I // 64, 2, 64)
+    r = (torch.nn.functional.silu(full[:, :, 0]) * full[:, :, 1]).reshape(M, I)
+    err = ((out.float().cpu() - r).norm() / r.norm()).item()
+    assert err < 1.5e-2, err
+    y = torch.empty(M, 2 * I, device="cuda", dtype=torch.bfloat16)
+    res = torch.randn(M, 2 * I, device="cuda", dtype=torch.bfloat16)
+    ops.cuda_ext().gemm_fp8_block(y, xq, xs, wq, ws, None, res, 0, ks)
+    r2 = ref.fp8_block_gemm(xq.cpu(), xs.t().cpu(), wq.cpu(), ws.cpu()) + res.float().cpu()
+    assert ((y.float().cpu() - r2).norm() / r2.norm()).item() < 1e-2
+
+
+@pytest.mark.gpu
+def test_fp8_engine_llama3_shapes_runs():
+    from rusteeze_b200.config.config import Config, QuantizationConfig
+    from rusteeze_b200.core.sampling_params import SamplingParams
+    from rusteeze_b200.engine.llm_engine import LLMEngine
+    from rusteeze_b200.models.config import get_preset
+    mc = dataclasses.replace(get_preset("llama-3-8b"), num_hidden_layers=2)
+    cfg = Config()
+    cfg.model.device = "cuda:0"
+    cfg.model.quantization = QuantizationConfig(method="fp8_block")
+    cfg.engine.num_gpu_blocks = 256
+    cfg.engine.max_num_seqs = 8
+    cfg.engine.max_num_batched_tokens = 512
+    eng = LLMEngine(cfg, model_config=mc)
+    eng.add_request("a", None, SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True), list(range(5, 90)))
+    out = None
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            out = o
+    assert len(out.outputs[0].token_ids) == 6
