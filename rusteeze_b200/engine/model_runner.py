@@ -185,6 +185,41 @@ class ModelRunner:
             meta.block_tables = self.h_block_tables[:S].clone()
         return meta, T, S, sample_rows
 
+    @torch.no_grad()
+    def forward_arrays(self, bm, seq_ids, ctx, n_new, toks, logits_per_seq: int,
+                       num_decode: int = 0) -> torch.Tensor:
+        """Eager forward of an explicit token batch (speculative decoding):
+        sequence i gets n_new[i] tokens at positions ctx[i].., and the logits
+        of its last `logits_per_seq` tokens are returned in sequence order."""
+        S = len(seq_ids)
+        T = bm.build_batch(np.asarray(seq_ids, dtype=np.int64), np.asarray(ctx, dtype=np.int64),
+                           np.asarray(n_new, dtype=np.int64), np.asarray(toks, dtype=np.int64),
+                           self.h_input_ids.data_ptr(), self.h_positions.data_ptr(), self.h_slots.data_ptr(),
+                           self.h_qsl.data_ptr(), self.h_seq_lens.data_ptr(), self.h_block_tables.data_ptr(),
+                           self.h_logits_idx.data_ptr(), self.max_blocks, logits_per_seq)
+        nb = self.is_cuda
+        self.d_input_ids[:T].copy_(self.h_input_ids[:T], non_blocking=nb)
+        self.d_positions[:T].copy_(self.h_positions[:T], non_blocking=nb)
+        self.d_slots[:T].copy_(self.h_slots[:T], non_blocking=nb)
+        self.d_qsl[:S + 1].copy_(self.h_qsl[:S + 1], non_blocking=nb)
+        self.d_seq_lens[:S].copy_(self.h_seq_lens[:S], non_blocking=nb)
+        self.d_block_tables[:S].copy_(self.h_block_tables[:S], non_blocking=nb)
+        self.h2d_bytes += 3 * 8 * T + 8 * S + 4 * S * self.max_blocks
+        meta = AttentionMetadata(
+            num_seqs=S, num_tokens=T, num_decode_seqs=num_decode, query_start_loc=self.d_qsl[:S + 1],
+            seq_lens=self.d_seq_lens[:S], block_tables=self.d_block_tables[:S], slot_mapping=self.d_slots[:T],
+            max_query_len=int(max(n_new)) if S else 1, max_seq_len=int(self.h_seq_lens[:S].max()) if S else 0,
+            decode_num_splits=choose_num_splits(max(num_decode, 1), self.model.hkv, self.max_blocks),
+            decode_workspace=self.decode_ws)
+        if not self.is_cuda:
+            meta.query_start_loc = self.h_qsl[:S + 1].clone()
+            meta.seq_lens = self.h_seq_lens[:S].clone()
+            meta.block_tables = self.h_block_tables[:S].clone()
+        h = self.model(self.d_input_ids[:T], self.d_positions[:T], meta, self.kv_layers)
+        n_rows = S * logits_per_seq
+        idx = self.h_logits_idx[:n_rows].to(h.device, non_blocking=nb)
+        return self.model.compute_logits(h.index_select(0, idx))
+
     # ------------------------------------------------------------------ graphs
     def _graph_bucket(self, n: int) -> Optional[int]:
         for b in sorted(self.graphs):

@@ -1,0 +1,261 @@
+"""Draft-model speculative decoding.
+
+The reference ships an unused tree-speculation module whose acceptance rule
+(`target logit > top * threshold`, crates/rusteeze-engine/src/speculative.rs:
+291-348) does not preserve the target distribution.  Here:
+
+  * a draft model (e.g. a 1B Llama-3.2-like model next to Llama-3-70B)
+    keeps its own KV cache, indexed by the SAME block ids as the target
+    (the scheduler reserves k lookahead slots per decoding sequence);
+  * each pure-decode step runs k batched draft steps, then ONE target
+    forward over k+1 positions per sequence (the varlen paged attention
+    kernel with q_len = k+1), then the sm_100a `spec_verify` kernel:
+    greedy requests accept the longest prefix matching the target argmax;
+    sampled requests use standard rejection sampling (accept d with
+    probability min(1, p(d)/q(d)), resample from normalise(max(0, p-q)),
+    bonus token from p after k accepts) -- the emitted tokens follow the
+    target distribution exactly;
+  * rollback is implicit: a sequence's computed length advances by
+    accepted+1, so KV written for rejected positions is simply overwritten
+    later; the draft re-feeds the tokens it has not cached (1, or 2 after a
+    full accept) at the start of the next round;
+  * steps that contain prefill chunks run normally on the target and the
+    draft processes the same tokens to stay in sync.
+Sampled speculation applies temperature only (top-k/top-p requests fall
+back to plain decoding).
+"""
+from __future__ import annotations
+
+import dataclasses
+import logging
+import time
+from typing import Dict, List
+
+import numpy as np
+import torch
+
+from rusteeze_b200 import ops
+from rusteeze_b200.engine.model_runner import ModelRunner
+from rusteeze_b200.models.config import ModelConfig, get_preset
+from rusteeze_b200.models.loader import build_model
+
+log = logging.getLogger("rusteeze.spec")
+
+
+def _verify_cpu(target: torch.Tensor, draft_logits, draft: torch.Tensor, temps, seeds, offsets):
+    """Host restatement of the verify kernel (greedy exact; sampled via torch RNG)."""
+    B, k = draft.shape
+    V = target.shape[1]
+    out = torch.full((B, k + 1), -1, dtype=torch.long)
+    acc = torch.zeros(B, dtype=torch.long)
+    for b in range(B):
+        g = torch.Generator().manual_seed(int(seeds[b]) * 1000003 + int(offsets[b]))
+        for j in range(k + 1):
+            t = target[b * (k + 1) + j].float()
+            if temps[b] <= 0:
+                a = int(t.argmax())
+                if j < k and a == int(draft[b, j]):
+                    out[b, j] = a
+                    acc[b] += 1
+                    continue
+                out[b, j] = a
+                break
+            p = torch.softmax(t / temps[b], -1)
+            if j < k:
+                q = torch.softmax(draft_logits[b * k + j].float() / temps[b], -1)
+                d = int(draft[b, j])
+                if torch.rand((), generator=g) * q[d] < p[d]:
+                    out[b, j] = d
+                    acc[b] += 1
+                    continue
+                r = (p - q).clamp_min(0)
+                out[b, j] = int(torch.multinomial(r / r.sum(), 1, generator=g)) if r.sum() > 0 else d
+                break
+            out[b, j] = int(torch.multinomial(p, 1, generator=g))
+    return acc, out
+
+
+class SpecDecoder:
+    def __init__(self, engine, spec_cfg):
+        self.engine = engine
+        self.k = spec_cfg.num_speculative_tokens
+        tm = engine.model
+        if spec_cfg.draft_model:
+            dmc = ModelConfig.from_json_file(spec_cfg.draft_model)
+        else:
+            dmc = get_preset(spec_cfg.draft_preset) if spec_cfg.draft_preset else dataclasses.replace(tm.cfg)
+        if dmc.vocab_size != tm.cfg.vocab_size:
+            raise ValueError("draft and target must share the vocabulary")
+        dmc = dataclasses.replace(dmc, max_position_embeddings=max(dmc.max_position_embeddings,
+                                                                   tm.cfg.max_position_embeddings))
+        self.self_draft = not spec_cfg.draft_model and not spec_cfg.draft_preset
+        if self.self_draft:
+            self.draft = tm      # sanity mode: the target drafts for itself (acceptance must be 100% when greedy)
+        else:
+            self.draft = build_model(dmc, dtype=tm.dtype, device=str(tm.device), model_dir=spec_cfg.draft_model,
+                                     seed=engine.config.model.seed + 1)
+            if tm.device.type == "cuda":
+                self.draft.prepare_for_gpu()
+        r = engine.runner
+        self.runner: ModelRunner = r
+        self.drunner = ModelRunner(self.draft, num_gpu_blocks=r.num_gpu_blocks, num_cpu_blocks=0,
+                                   max_num_seqs=r.max_num_seqs, max_num_batched_tokens=max(
+                                       r.max_tokens, r.max_num_seqs * (self.k + 2)),
+                                   max_model_len=engine.max_model_len, use_cuda_graph=False)
+        # verify forwards need room for S*(k+1) tokens in the target's staging buffers
+        need = r.max_num_seqs * (self.k + 1)
+        if r.max_tokens < need:
+            raise ValueError(f"max_num_batched_tokens must be >= max_num_seqs*(k+1) = {need} for speculation")
+        self.draft_computed: Dict[int, int] = {}
+        self.stats = {"rounds": 0, "proposed": 0, "accepted": 0, "emitted": 0}
+
+    # ------------------------------------------------------------------ main
+    def step(self):
+        eng = self.engine
+        so = eng.scheduler.schedule()
+        if so.is_empty():
+            return eng._collect_ignored()
+        spec_ok = not so.prefills and all(
+            s.seq.request.params.top_k <= 0 and s.seq.request.params.top_p >= 1.0 and
+            s.seq.request.params.min_p == 0.0 and not s.seq.request.params.needs_host_sampling()
+            and not s.seq.request.params.has_penalties() and s.seq.request.params.logprobs is None
+            for s in so.decodes)
+        if not spec_ok:
+            return self._plain_step(so)
+        return self._spec_round(so)
+
+    def _plain_step(self, so):
+        """Normal engine step on the target; the draft processes the same tokens."""
+        eng = self.engine
+        rows, owners = eng._sample_rows(so)
+        self._draft_follow(so)
+        t0 = time.monotonic()
+        res = eng.runner.execute(so, eng.bm, rows)
+        now = time.monotonic()
+        eng.stats_counters["steps"] += 1
+        touched = eng._apply_results(so, res, owners, now)
+        for ss in so.scheduled:
+            self.draft_computed[ss.seq.seq_id] = ss.ctx + ss.num_new
+        for obs in eng.observers:
+            obs(eng, so, now - t0)
+        outs = []
+        for req in touched:
+            outs.append(req.to_output(delta=True))
+            if req.is_finished():
+                eng._retire(req)
+        return outs + eng._collect_ignored()
+
+    def _draft_follow(self, so) -> None:
+        if self.self_draft:
+            return          # the target's own KV is the draft's KV
+        sched = so.scheduled
+        if not sched:
+            return
+        ids = [s.seq.seq_id for s in sched]
+        ctx = [s.ctx for s in sched]
+        nn = [s.num_new for s in sched]
+        toks = np.concatenate([s.seq.tokens_np()[s.ctx:s.ctx + s.num_new] for s in sched])
+        self.drunner.forward_arrays(self.engine.bm, ids, ctx, nn, toks, 1, num_decode=0)
+
+    @torch.no_grad()
+    def _spec_round(self, so):
+        eng, k, bm = self.engine, self.k, self.engine.bm
+        seqs = [s.seq for s in so.decodes]
+        S = len(seqs)
+        ids = [s.seq_id for s in seqs]
+        cs = [s.num_computed for s in seqs]             # KV exists for positions < c; token at c is new
+        t0 = time.monotonic()
+        drunner = self.runner if self.self_draft else self.drunner
+        # ---- draft proposals
+        dc = [self.draft_computed.get(s.seq_id, s.num_computed) for s in seqs]
+        if self.self_draft:
+            dc = list(cs)
+        n1 = [c - d + 1 for c, d in zip(cs, dc)]
+        toks = np.concatenate([s.tokens_np()[d:c + 1] for s, d, c in zip(seqs, dc, cs)])
+        draft_tokens = torch.empty(S, k, dtype=torch.long)
+        draft_logits = []
+        temps = torch.tensor([s.request.params.temperature if not s.request.params.is_greedy else 0.0
+                              for s in seqs], dtype=torch.float32)
+        cur = None
+        for i in range(k):
+            if i == 0:
+                logits = drunner.forward_arrays(bm, ids, dc, n1, toks, 1, num_decode=0)
+            else:
+                logits = drunner.forward_arrays(bm, ids, [c + i for c in cs], [1] * S, cur, 1, num_decode=S)
+            draft_logits.append(logits)
+            nxt = self._propose(logits, temps, seqs, i)
+            draft_tokens[:, i] = nxt
+            cur = nxt.numpy()
+        # ---- one target pass over k+1 positions per sequence
+        vt = np.concatenate([np.concatenate([[s.token_ids[c]], draft_tokens[j].numpy()])
+                             for j, (s, c) in enumerate(zip(seqs, cs))]).astype(np.int64)
+        tlogits = self.runner.forward_arrays(bm, ids, cs, [k + 1] * S, vt, k + 1, num_decode=0)
+        dl = torch.stack(draft_logits, dim=1).reshape(S * k, -1)     # row b*k + j
+        seeds = torch.tensor([(s.request.seed + 7919 * s.index) & ((1 << 62) - 1) for s in seqs], dtype=torch.int64)
+        offs = torch.tensor([s.num_generated for s in seqs], dtype=torch.int64)
+        if tlogits.is_cuda:
+            dev = tlogits.device
+            out = torch.empty(S, k + 1, dtype=torch.int64, device=dev)
+            nacc = torch.empty(S, dtype=torch.int32, device=dev)
+            ops.cuda_ext().spec_verify(out, nacc, tlogits.contiguous(), dl.contiguous(), draft_tokens.to(dev),
+                                       temps.to(dev), seeds.to(dev), offs.to(dev))
+            ops.add_launches(1)
+            both = torch.cat([out.cpu(), nacc.cpu().long().view(-1, 1)], dim=1)
+            out, nacc = both[:, :k + 1], both[:, k + 1]
+        else:
+            nacc, out = _verify_cpu(tlogits, dl, draft_tokens, temps, seeds, offs)
+        now = time.monotonic()
+        # ---- apply
+        touched, seen = [], set()
+        for j, s in enumerate(seqs):
+            a = int(nacc[j])
+            emitted = [int(x) for x in out[j, :a + 1].tolist()]
+            c = cs[j]
+            self.stats["proposed"] += k
+            self.stats["accepted"] += a
+            req = s.request
+            for tok in emitted:
+                s.append_token(tok)
+                if req.metrics.first_token_time is None:
+                    req.metrics.first_token_time = now
+                req.metrics.last_token_time = now
+                req.metrics.num_generated = max(req.metrics.num_generated, s.num_generated)
+                eng.stats_counters["generation_tokens"] += 1
+                self.stats["emitted"] += 1
+                eng._check_stop(s, tok)
+                if s.is_finished():
+                    break
+            if not s.is_finished():
+                s.num_computed = c + a + 1
+                bm.commit(s.seq_id, s.tokens_np(), s.num_computed)
+                self.draft_computed[s.seq_id] = c + min(a, k - 1) + 1 if not self.self_draft else s.num_computed
+            else:
+                self.draft_computed.pop(s.seq_id, None)
+            if id(req) not in seen:
+                seen.add(id(req))
+                touched.append(req)
+        self.stats["rounds"] += 1
+        eng.stats_counters["steps"] += 1
+        for obs in eng.observers:
+            obs(eng, so, now - t0)
+        outs = []
+        for req in touched:
+            outs.append(req.to_output(delta=True))
+            if req.is_finished():
+                eng._retire(req)
+        return outs
+
+    def _propose(self, logits: torch.Tensor, temps: torch.Tensor, seqs, i: int) -> torch.Tensor:
+        """Greedy argmax, or a temperature sample (Gumbel-max) per row."""
+        lg = logits.float()
+        if bool((temps <= 0).all()):
+            return lg.argmax(-1).cpu()
+        g = torch.Generator(device=lg.device)
+        g.manual_seed(int(seqs[0].request.seed) + 104729 * (seqs[0].num_generated + i))
+        u = torch.rand(lg.shape, generator=g, device=lg.device).clamp_(1e-12, 1.0)
+        t = temps.to(lg.device).clamp_min(1e-5).unsqueeze(1)
+        keys = torch.where(temps.to(lg.device).unsqueeze(1) > 0, lg / t - torch.log(-torch.log(u)), lg)
+        return keys.argmax(-1).cpu()
+
+    def acceptance_rate(self) -> float:
+        return self.stats["accepted"] / max(1, self.stats["proposed"])
