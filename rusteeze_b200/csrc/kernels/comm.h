@@ -6,4 +6,5 @@
 
 namespace rz {
 constexpr int kMaxRanks = 8;
+constexpr int kMaxArBlocks = 128;
 }  // namespace rz

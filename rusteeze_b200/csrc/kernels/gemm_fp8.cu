@@ -33,6 +33,7 @@ constexpr int kF8Stages = 6;
 constexpr int kF8ABytes = kF8BM * kF8BK;
 constexpr int kF8BBytes = kF8BN * kF8BK;
 constexpr int kF8StageBytes = kF8ABytes + kF8BBytes;
+constexpr int kF8Parts = 4;          // TMEM partial accumulators in flight (4 x 128 columns = all of TMEM)
 constexpr int kF8Threads = 320;
 constexpr int kF8EpiThreads = 256;
 constexpr int kF8Smem = kF8Stages * kF8StageBytes + 1024 + 256;
@@ -53,8 +54,8 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + kF8Stages;
   uint64_t* pfull = bars + 2 * kF8Stages;
-  uint64_t* pempty = pfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+  uint64_t* pempty = pfull + kF8Parts;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + kF8Parts);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = p.m_tiles * p.n_tiles * p.k_splits;
@@ -64,7 +65,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kF8Parts; ++i) {
       mbar_init(&pfull[i], 1);
       mbar_init(&pempty[i], kF8EpiThreads);
     }
@@ -72,7 +73,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 2 * kF8BN);
+  if (warp == 1) tmem_alloc(tmem_slot, kF8Parts * kF8BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           umma_commit(&empty[s]);
           umma_commit(&pfull[buf]);
           if (++s == kF8Stages) { s = 0; ph ^= 1; }
-          if (++buf == 2) { buf = 0; bph ^= 1; }
+          if (++buf == kF8Parts) { buf = 0; bph ^= 1; }
         }
       }
     }
@@ -148,7 +149,17 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       float acc[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+      const float* a_col = p.a_scale + (row_ok ? row : 0);
+      const float* b_row = p.b_scale + static_cast<int64_t>(nb) * p.b_scale_ld;
+      // scales of the next k-block are loaded before waiting on the current partial
+      float sa_n = kb0 < kb1 ? a_col[static_cast<int64_t>(kb0) * p.a_scale_ld] : 0.f;
+      float sb_n = kb0 < kb1 ? b_row[kb0] : 0.f;
       for (int kb = kb0; kb < kb1; ++kb) {
+        const float sc = (row_ok ? sa_n : 0.f) * sb_n;
+        if (kb + 1 < kb1) {
+          sa_n = a_col[static_cast<int64_t>(kb + 1) * p.a_scale_ld];
+          sb_n = b_row[kb + 1];
+        }
         if (!mbar_wait(&pfull[buf], bph, p.status, kGemmEpilogueTimeout)) { ok = false; break; }
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * kF8BN;
@@ -158,14 +169,12 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(&pempty[buf]);
-        const float sa = row_ok ? p.a_scale[static_cast<int64_t>(kb) * p.a_scale_ld + row] : 0.f;
-        const float sc = sa * p.b_scale[static_cast<int64_t>(nb) * p.b_scale_ld + kb];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          acc[j] += __uint_as_float(r0[j]) * sc;
-          acc[32 + j] += __uint_as_float(r1[j]) * sc;
+          acc[j] = fmaf(__uint_as_float(r0[j]), sc, acc[j]);
+          acc[32 + j] = fmaf(__uint_as_float(r1[j]), sc, acc[32 + j]);
         }
-        if (++buf == 2) { buf = 0; bph ^= 1; }
+        if (++buf == kF8Parts) { buf = 0; bph ^= 1; }
       }
       if (!ok || !row_ok) continue;
       const int cA = nb * kF8BN + 32 * h;        // first column group
@@ -218,7 +227,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 2 * kF8BN);
+  if (warp == 1) tmem_dealloc(tmem_base, kF8Parts * kF8BN);
 }
 
 // ---------------------------------------------------------------------------- activation quant
@@ -306,8 +315,8 @@ int fp8_plan_splits(int M, int N, int K) {
   const int sms = num_sms();
   const int kblocks = K / kF8BK;
   const int tiles = ((M + kF8BM - 1) / kF8BM) * ((N + kF8BN - 1) / kF8BN);
-  int ks = 1;
-  while (ks < 8 && tiles * ks * 2 <= sms && kblocks / (ks * 2) >= 4) ks *= 2;
+  int ks = 1;   // enough units to put every SM to work on small-M (weight-streaming) GEMMs
+  while (ks < 16 && tiles * ks < sms && kblocks / (ks * 2) >= 2) ks *= 2;
   return ks;
 }
 

@@ -55,7 +55,7 @@ def test_fp8_model_cpu_tracks_bf16_model():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("M,N,K", [(1, 256, 256), (7, 4096, 4096), (256, 6144, 4096), (1300, 4096, 14336),
-                                   (64, 1024, 512), (129, 128256 // 8, 1024)])
+                                   (64, 1024, 512), (129, 128256 // 8 - 32, 1024)])
 def test_gemm_fp8_vs_oracle(M, N, K):
     torch.manual_seed(M + N)
     x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
