@@ -57,6 +57,7 @@ class AsyncLLMEngine:
         self.last_step_start: Optional[float] = None
         self.started_at = time.time()
         self.requests_processed = 0
+        self._last_status_check = 0.0
 
     # ------------------------------------------------------------------ lifecycle
     def start(self) -> "AsyncLLMEngine":
@@ -144,10 +145,32 @@ class AsyncLLMEngine:
                     sub.loop.call_soon_threadsafe(sub.q.put_nowait,
                                                   RequestTimeoutError(f"request {rid} timed out"))
 
+    def _check_device_status(self) -> None:
+        """Kernels report protocol errors (an expired bounded wait, a corrupt
+        block table) in a device status word instead of trapping; poll it about
+        once per second and mark the engine unhealthy when it is set."""
+        now = time.monotonic()
+        if now - self._last_status_check < 1.0:
+            return
+        self._last_status_check = now
+        dev = getattr(self.engine, "device", "cpu")
+        if not str(dev).startswith("cuda"):
+            return
+        try:
+            from rusteeze_b200 import ops
+            code = int(ops.cuda_ext().status()[0])
+        except Exception:  # noqa: BLE001
+            return
+        if code != 0:
+            self.healthy = False
+            self.last_error = f"device kernel status {code}"
+            log.error("device kernel reported status %d; engine marked unhealthy", code)
+
     def _loop(self) -> None:
         while not self._stop.is_set():
             self._drain_inbox()
             self._expire()
+            self._check_device_status()
             if not self.engine.has_unfinished_requests():
                 self._wake.wait(0.05)
                 self._wake.clear()

@@ -40,6 +40,7 @@ from rusteeze_b200.models.config import ModelConfig, get_preset
 from rusteeze_b200.models.loader import build_model
 from rusteeze_b200.tokenizer.tokenizer import IncrementalDetokenizer, load_tokenizer
 from rusteeze_b200.ops import BLOCK_SIZE
+from rusteeze_b200.metrics.logging_setup import nvtx_range
 
 log = logging.getLogger("rusteeze.engine")
 
@@ -208,13 +209,15 @@ class LLMEngine:
     def step(self) -> List[RequestOutput]:
         if self.spec is not None:
             return self.spec.step()
-        so = self.scheduler.schedule()
+        with nvtx_range("rz.step.schedule"):
+            so = self.scheduler.schedule()
         outputs: List[RequestOutput] = []
         if so.is_empty():
             return self._collect_ignored()
         rows, owners = self._sample_rows(so)
         t0 = time.monotonic()
-        res = self.runner.execute(so, self.bm, rows)
+        with nvtx_range("rz.step.execute"):
+            res = self.runner.execute(so, self.bm, rows)
         now = time.monotonic()
         self.stats_counters["steps"] += 1
         touched = self._apply_results(so, res, owners, now)

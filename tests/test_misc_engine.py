@@ -1,0 +1,105 @@
+"""Smaller engine components: batch-size SLO controller, memory report,
+incremental detokenizer, chat templates, sampler host paths, abort/timeout."""
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from rusteeze_b200.core.sampling_params import SamplingParams
+from rusteeze_b200.engine.batch_optimizer import BatchOptimizer, BatchOptimizerConfig
+from rusteeze_b200.tokenizer.chat_template import ChatFormat, ChatTemplate
+from rusteeze_b200.tokenizer.tokenizer import ByteTokenizer, IncrementalDetokenizer
+
+
+def test_batch_optimizer_shrinks_and_grows():
+    bo = BatchOptimizer(BatchOptimizerConfig(target_latency_s=0.05, max_batch=64, cooldown_steps=1))
+    for _ in range(20):
+        bo.observe(0.2)
+    assert bo.batch < 64
+    small = bo.batch
+    for _ in range(60):
+        bo.observe(0.005)
+    assert bo.batch > small and bo.adjustments > 1
+
+
+def test_incremental_detok_equals_full_decode():
+    tok = ByteTokenizer()
+    text = "héllo wörld — streaming ✓ text"
+    ids = tok.encode(text, add_special_tokens=False)
+    d = IncrementalDetokenizer(tok, [1])
+    out = "".join(d.step(i) for i in ids)
+    assert out == text == tok.decode(ids)
+
+
+@pytest.mark.parametrize("fmt,needle", [(ChatFormat.LLAMA3, "<|start_header_id|>assistant"),
+                                        (ChatFormat.CHATML, "<|im_start|>assistant"),
+                                        (ChatFormat.LLAMA, "[INST] <<SYS>>"), (ChatFormat.PHI3, "<|assistant|>"),
+                                        (ChatFormat.MISTRAL, "[INST] sys\n\nhi [/INST]")])
+def test_chat_templates(fmt, needle):
+    msgs = [{"role": "system", "content": "sys"}, {"role": "user", "content": "hi"}]
+    assert needle in ChatTemplate(fmt).apply(msgs)
+    assert ChatFormat.from_model_name("Meta-Llama-3-8B-Instruct") == ChatFormat.LLAMA3
+    assert ChatFormat.from_model_name("unknown") == ChatFormat.CHATML
+
+
+def test_jinja_template():
+    t = ChatTemplate(jinja="{% for m in messages %}[{{ m.role }}]{{ m.content }}{% endfor %}"
+                           "{% if add_generation_prompt %}[assistant]{% endif %}")
+    assert t.apply([{"role": "user", "content": "x"}]) == "[user]x[assistant]"
+
+
+def _tiny_engine(**kw):
+    from rusteeze_b200.config.config import Config
+    from rusteeze_b200.engine.llm_engine import LLMEngine
+    cfg = Config()
+    cfg.model.preset = "tiny-llama"
+    cfg.model.device = "cpu"
+    cfg.model.dtype = "float32"
+    cfg.engine.num_gpu_blocks = 64
+    for k, v in kw.items():
+        setattr(cfg.engine, k, v)
+    return LLMEngine(cfg)
+
+
+def test_memory_report_and_host_sampling_paths():
+    from rusteeze_b200.utils.memory import memory_report
+    eng = _tiny_engine()
+    rep = memory_report(eng)
+    assert rep["kv_blocks"] == 64 and rep["weights_gib"] > 0
+    params = [SamplingParams(temperature=1.0, mirostat_mode=2, max_tokens=4, ignore_eos=True, seed=1),
+              SamplingParams(temperature=0.9, typical_p=0.5, max_tokens=4, ignore_eos=True, seed=2),
+              SamplingParams(temperature=1.0, repetition_penalty=1.3, frequency_penalty=0.5, presence_penalty=0.2,
+                             logit_bias={7: 5.0}, max_tokens=4, ignore_eos=True, seed=3, logprobs=3),
+              SamplingParams(n=2, best_of=3, temperature=0.8, max_tokens=3, ignore_eos=True, seed=4)]
+    ids = [eng.add_request(None, "hello there", p).request_id for p in params]
+    done = {}
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            if o.finished:
+                done[o.request_id] = o
+    assert len(done[ids[2]].outputs[0].logprobs) == 4
+    assert len(done[ids[3]].outputs) == 2            # best_of 3 -> n 2
+    assert eng.bm.stats()["forks"] >= 2
+
+
+def test_stop_strings_eos_and_min_tokens():
+    eng = _tiny_engine()
+    eos = eng.eos_ids[0]
+    sp = SamplingParams(temperature=0.0, max_tokens=20, min_tokens=3, logit_bias={eos: 100.0})
+    eng.add_request("a", None, sp, [5, 6, 7])
+    out = None
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            out = o
+    # EOS is forced by the bias but masked until min_tokens is reached
+    assert len(out.outputs[0].token_ids) == 4 and out.outputs[0].finish_reason == "stop"
+
+
+def test_abort_frees_blocks():
+    eng = _tiny_engine()
+    eng.add_request("x", None, SamplingParams(max_tokens=50, ignore_eos=True), list(range(40)))
+    eng.step()
+    assert eng.bm.num_free_gpu_blocks() < 64
+    eng.abort_request("x")
+    assert eng.bm.num_free_gpu_blocks() == 64 and not eng.has_unfinished_requests()
