@@ -126,6 +126,7 @@ def make_engine(args, device):
     cfg.engine.gpu_memory_utilization = 0.88
     cfg.engine.swap_space_gb = 0
     cfg.engine.cuda_graph_max_batch = args.max_seqs
+    cfg.engine.enforce_eager = bool(getattr(args, "eager", False))
     return LLMEngine(cfg)
 
 
@@ -143,6 +144,7 @@ def main():
     ap.add_argument("--e2e-requests", type=int, default=256)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--fp8", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="disable CUDA graphs (profiling runs)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -215,6 +217,7 @@ def main():
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(eng_stream)
     ttfts, tpots = [], []
+    torch.cuda.nvtx.range_push("rz_timed")       # lets ncu --nvtx-include select steady-state launches
     for _ in range(args.steps):
         for out in step():
             if out.finished and out.metrics is not None:
@@ -222,6 +225,7 @@ def main():
                     ttfts.append(out.metrics.ttft)
                 if out.metrics.tpot is not None:
                     tpots.append(out.metrics.tpot)
+    torch.cuda.nvtx.range_pop()
     ev1.record(eng_stream)
     torch.cuda.synchronize()
     if world > 1:

@@ -231,8 +231,12 @@ class LLMEngine:
 
     def _collect_ignored(self) -> List[RequestOutput]:
         outs = []
-        for req in list(self.requests.values()):
-            if any(s.status == RequestStatus.FINISHED_IGNORED for s in req.seqs) and req.is_finished():
+        if not self.scheduler.ignored:
+            return outs
+        ign, self.scheduler.ignored = self.scheduler.ignored, []
+        for s in ign:
+            req = s.request
+            if req.request_id in self.requests and req.is_finished():
                 outs.append(req.to_output(delta=True))
                 self._retire(req)
         return outs
@@ -245,8 +249,13 @@ class LLMEngine:
                 continue
             s = ss.seq
             req = s.request
+            p = req.params
+            # token histories are only materialised for the rows that read them
+            pen = p.has_penalties()
+            prompt_ids = s.token_ids[:s.prompt_len] if pen else ()
+            output_ids = s.output_token_ids if (pen or p.min_tokens > s.num_generated) else ()
             for j in range(ss.num_samples):
-                rows.append(SampleRow(req.params, s.token_ids[:s.prompt_len], s.output_token_ids,
+                rows.append(SampleRow(p, prompt_ids, output_ids,
                                       seed=req.seed + 7919 * (s.index + j), offset=s.num_generated,
                                       eos_ids=self.eos_ids, mirostat_mu=s.mirostat_mu))
             owners.append((ss, ss.num_samples))

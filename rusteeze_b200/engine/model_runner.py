@@ -101,6 +101,8 @@ class ModelRunner:
         self.h_seq_lens = torch.zeros(S, dtype=torch.int32, pin_memory=pin)
         self.h_block_tables = torch.zeros(S, MB, dtype=torch.int32, pin_memory=pin)
         self.h_logits_idx = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
+        self.h_logits_idx_np = self.h_logits_idx.numpy()
+        self.h_seq_lens_np = self.h_seq_lens.numpy()
         dev = self.device
         self.d_input_ids = torch.zeros(T, dtype=torch.int64, device=dev)
         self.d_positions = torch.zeros(T, dtype=torch.int64, device=dev)
@@ -153,17 +155,15 @@ class ModelRunner:
                            self.h_seq_lens.data_ptr(), self.h_block_tables.data_ptr(),
                            self.h_logits_idx.data_ptr(), self.max_blocks, 1)
         # rows to sample: last token of sequences with sample=True, repeated num_samples times
-        rows: List[int] = []
-        lidx = self.h_logits_idx
+        lidx = self.h_logits_idx_np
         sample_rows: List[int] = []
         for i, s in enumerate(sched):
             if s.sample:
-                for _ in range(s.num_samples):
-                    sample_rows.append(int(lidx[i]))
-                rows.append(i)
+                li = int(lidx[i])
+                sample_rows.extend([li] * s.num_samples)
         nd = len(so.decodes)
         max_q = max((s.num_new for s in so.prefills), default=1)
-        max_s = int(self.h_seq_lens[:S].max()) if S else 0
+        max_s = int(self.h_seq_lens_np[:S].max()) if S else 0
         nb = non_blocking = self.is_cuda
         self.h2d_bytes += 3 * 8 * T + 4 * (S + 1) + 4 * S + 4 * S * self.max_blocks
         self.d_input_ids[:T].copy_(self.h_input_ids[:T], non_blocking=nb)

@@ -85,7 +85,7 @@ class Sampler:
                 idx = torch.tensor(list(p.logit_bias.keys()), dtype=torch.long, device=logits.device)
                 val = torch.tensor(list(p.logit_bias.values()), dtype=logits.dtype, device=logits.device)
                 logits[i].index_add_(0, idx, val)
-            if p.min_tokens and len(r.output_ids) < p.min_tokens:
+            if p.min_tokens and r.offset < p.min_tokens:     # offset == tokens generated so far
                 stop = list(r.eos_ids) + list(p.stop_token_ids)
                 if stop:
                     logits[i, torch.tensor(stop, device=logits.device)] = _MASK

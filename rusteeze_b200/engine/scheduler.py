@@ -91,6 +91,7 @@ class Scheduler:
         self.running: List[Sequence] = []
         self.swapped: Deque[Sequence] = deque()
         self.num_preemptions = 0
+        self.ignored: List[Sequence] = []      # too long to ever run; the engine reports and drops them
         self._watermark_blocks = max(1, int(cfg.watermark * self.bm.num_gpu_blocks))
 
     # ------------------------------------------------------------------ queue ops
@@ -233,6 +234,7 @@ class Scheduler:
                     self.waiting.popleft()
                     seq.status = RequestStatus.FINISHED_IGNORED
                     seq.finish_reason = "length"
+                    self.ignored.append(seq)
                     continue
                 toks = seq.tokens_np()
                 cached = bm.cached_prefix_len(toks) if not bm.has_seq(seq.seq_id) else seq.num_computed

@@ -24,7 +24,7 @@ _seq_ids = itertools.count(1)
 class Sequence:
     __slots__ = ("seq_id", "request", "prompt_len", "token_ids", "status", "num_computed",
                  "num_cached", "logprobs", "cumulative_logprob", "output_text", "stop_reason",
-                 "detok", "_np", "_np_len", "index", "finish_reason", "rng_offset",
+                 "detok", "_buf", "index", "finish_reason", "rng_offset",
                  "mirostat_mu", "spec_draft")
 
     def __init__(self, request: "Request", prompt_token_ids: List[int], index: int = 0):
@@ -42,8 +42,11 @@ class Sequence:
         self.stop_reason = None
         self.finish_reason: Optional[str] = None
         self.detok = None
-        self._np = None
-        self._np_len = -1
+        # int64 mirror of token_ids with room to grow: batch building slices it
+        # without converting the Python list every step
+        self._buf = np.empty(max(16, self.prompt_len + min(request.params.max_tokens or 256, 4096) + 8
+                                 if request is not None else self.prompt_len + 16), dtype=np.int64)
+        self._buf[:self.prompt_len] = prompt_token_ids
         self.rng_offset = 0
         self.mirostat_mu = None
         self.spec_draft: List[int] = []
@@ -71,14 +74,19 @@ class Sequence:
         return self.total_len - self.num_computed
 
     def tokens_np(self) -> np.ndarray:
-        if self._np_len != len(self.token_ids):
-            self._np = np.asarray(self.token_ids, dtype=np.int64)
-            self._np_len = len(self.token_ids)
-        return self._np
+        """View of all tokens (prompt + generated) as int64; valid until the next append."""
+        return self._buf[:len(self.token_ids)]
 
     def append_token(self, tok: int, logprob: Optional[float] = None,
                      top: Optional[Dict[int, float]] = None) -> None:
-        self.token_ids.append(int(tok))
+        tok = int(tok)
+        n = len(self.token_ids)
+        if n >= self._buf.shape[0]:
+            nb = np.empty(2 * self._buf.shape[0], dtype=np.int64)
+            nb[:n] = self._buf[:n]
+            self._buf = nb
+        self._buf[n] = tok
+        self.token_ids.append(tok)
         if logprob is not None:
             self.cumulative_logprob += float(logprob)
         if top is not None:
@@ -137,7 +145,7 @@ class Request:
         deltas = []
         for s in seqs:
             text = s.output_text
-            outs.append(CompletionOutput(index=s.index, text=text, token_ids=list(s.output_token_ids),
+            outs.append(CompletionOutput(index=s.index, text=text, token_ids=s.output_token_ids,
                                          cumulative_logprob=s.cumulative_logprob if p.logprobs is not None else None,
                                          logprobs=s.logprobs if p.logprobs is not None else None,
                                          finish_reason=s.finish_reason, stop_reason=s.stop_reason))

@@ -145,7 +145,10 @@ class IncrementalDetokenizer:
         self.ids.append(int(new_id))
         prefix = self.tok.decode(self.ids[self.prefix_offset:self.read_offset], self.skip)
         full = self.tok.decode(self.ids[self.prefix_offset:], self.skip)
-        if len(full) > len(prefix) and not full.endswith("�"):
+        # advance when new text appeared, or when a run of tokens that decode to
+        # nothing (special / unmapped ids) would otherwise grow the window forever
+        stalled = len(self.ids) - self.prefix_offset > 8 and full == prefix
+        if (len(full) > len(prefix) or stalled) and not full.endswith("�"):
             delta = full[len(prefix):]
             self.prefix_offset = self.read_offset
             self.read_offset = len(self.ids)
