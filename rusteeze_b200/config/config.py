@@ -27,6 +27,7 @@ class QuantizationConfig:
     method: str = "none"        # none | fp8_block (fp8 / fp8_e4m3 accepted as aliases)
     bits: int = 8
     group_size: int = 128
+    scale_format: str = "ue8m0"   # ue8m0 (power-of-two, applied in the MMA) | fp32 (applied per K block)
 
 
 @dataclass

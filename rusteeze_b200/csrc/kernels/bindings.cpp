@@ -243,6 +243,65 @@ int64_t gemm_fp8_block(torch::Tensor out, torch::Tensor xq, torch::Tensor xs, to
   return k_splits > 1 ? 2 : 1;
 }
 
+// ---------------------------------------------------------------- MXFP8 (UE8M0 block scales)
+void quant_mxf8_act(torch::Tensor xq, torch::Tensor sfa, torch::Tensor x) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_LAST(x);
+  const int M = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % 128 == 0, "K must be a multiple of 128");
+  TORCH_CHECK(xq.is_contiguous() && xq.size(0) == M && xq.size(1) == K && xq.element_size() == 1, "xq: e4m3 [M, K]");
+  TORCH_CHECK(sfa.is_contiguous() && sfa.numel() >= static_cast<int64_t>((M + 127) / 128) * (K / 128) * 512,
+              "sfa: ceil(M/128) * K/128 chunks of 512 bytes");
+  check_rc(rz::quant_mxf8_act_launch(xq.data_ptr(), reinterpret_cast<uint8_t*>(sfa.data_ptr()),
+                                     reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), M, K, x.stride(0),
+                                     cur_stream()),
+           "quant_mxf8_act");
+}
+
+// Returns the number of kernels launched (1, or 2 with a split-K reduction).
+int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch::Tensor wq, torch::Tensor sfb,
+                  c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual, int64_t epi, int64_t bn,
+                  int64_t k_splits) {
+  CHECK_CUDA(xq);
+  const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "mxf8 gemm: K and N must be multiples of 128");
+  TORCH_CHECK(wq.size(1) == K && xq.is_contiguous() && wq.is_contiguous(), "mxf8 gemm: contiguous [M,K] x [N,K]");
+  TORCH_CHECK(xq.element_size() == 1 && wq.element_size() == 1, "mxf8 gemm: e4m3 operands");
+  TORCH_CHECK(sfa.numel() >= static_cast<int64_t>((M + 127) / 128) * (K / 128) * 512 &&
+                  sfb.numel() >= static_cast<int64_t>(N / 128) * (K / 128) * 512,
+              "mxf8 gemm: scale chunk buffers too small");
+  if (epi == rz::kEpiSiluMul) TORCH_CHECK(out.size(1) == N / 2, "silu epilogue: out has N/2 columns");
+  if (bn <= 0 || k_splits <= 0) {
+    auto pl = rz::plan_gemm_mxf8(M, N, K, epi);
+    bn = pl.bn;
+    k_splits = pl.k_splits;
+  }
+  rz::GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.k_splits = k_splits;
+  p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldd = out.stride(0);
+  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  p.residual = residual.has_value() ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
+  p.ldr = residual.has_value() ? residual->stride(0) : 0;
+  p.epi = epi;
+  p.status = status_ptr();
+  p.sfa = reinterpret_cast<const uint8_t*>(sfa.data_ptr());
+  p.sfb = reinterpret_cast<const uint8_t*>(sfb.data_ptr());
+  torch::Tensor ws;
+  if (k_splits > 1) {
+    ws = torch::empty({k_splits, M, N}, xq.options().dtype(torch::kFloat32));
+    p.partial = ws.data_ptr<float>();
+  }
+  check_rc(rz::gemm_mxf8_launch(p, xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), bn, cur_stream()),
+           "gemm_mxf8");
+  return k_splits > 1 ? 2 : 1;
+}
+
+std::vector<int64_t> gemm_plan_mxf8(int64_t M, int64_t N, int64_t K, int64_t epi) {
+  auto pl = rz::plan_gemm_mxf8(M, N, K, epi);
+  return {pl.bn, pl.k_splits};
+}
+
 // ---------------------------------------------------------------- sampling
 void argmax_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, bool want_lp) {
   CHECK_CUDA(logits);
@@ -315,6 +374,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_ex", &gemm_bf16_ex);
   m.def("quant_fp8_act", &quant_fp8_act);
   m.def("gemm_fp8_block", &gemm_fp8_block);
+  m.def("quant_mxf8_act", &quant_mxf8_act);
+  m.def("gemm_mxf8", &gemm_mxf8);
+  m.def("gemm_plan_mxf8", &gemm_plan_mxf8);
   m.def("argmax_sample", &argmax_sample);
   m.def("topk_topp_sample", &topk_topp_sample);
   m.def("spec_verify", &spec_verify);

@@ -151,6 +151,35 @@ RZ_DEVICE void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t
       : "memory");
 }
 
+// kind::mxf8f6f4 with block scaling: e4m3 x e4m3 -> f32, one UE8M0 scale per
+// 32 K-elements of every A row and every B row, read from TMEM at tsfa / tsfb
+// (the top two address bits select the byte of the 32-bit scale word).
+RZ_DEVICE void umma_mxf8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t tsfa,
+                         uint32_t tsfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb)
+      : "memory");
+}
+
+// Shared -> tensor memory copy of a 32-row x 16-byte block, replicated into all
+// four 32-lane quarters of TMEM (4 columns of 32 bits per lane).
+RZ_DEVICE void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Descriptor of a plain (unswizzled) K-major block of 16-byte rows: 8-row core
+// matrices 128 bytes apart, a single core matrix along K.
+RZ_DEVICE uint64_t smem_desc_rows16(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);  // start address
+  d |= static_cast<uint64_t>(128 >> 4) << 32;           // stride byte offset: 8 rows x 16 B
+  d |= static_cast<uint64_t>(1) << 46;                  // descriptor version (sm_100)
+  return d;                                             // layout type 0: no swizzle
+}
+
 // Arrive on an mbarrier when all previously issued tcgen05.mma of this thread complete.
 RZ_DEVICE void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -187,6 +216,13 @@ RZ_DEVICE uint64_t smem_desc_k_sw128(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
+}
+// Block-scaled kind::mxf8f6f4: e4m3 x e4m3, UE8M0 scales, both K-major.  The
+// scale-factor byte ids (which K-chunk of the 32-bit scale word) sit in bits
+// 4-5 (B) and 29-30 (A); the accumulator is always f32 in this format.
+__host__ __device__ constexpr uint32_t idesc_mxf8(int M, int N, uint32_t sf_id) {
+  return (sf_id << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(N >> 3) << 17) | (1u << 23) |
+         (static_cast<uint32_t>(M >> 4) << 24) | (sf_id << 29);
 }
 // kind::f8f6f4: e4m3 x e4m3 -> f32, both K-major.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {

@@ -1,14 +1,24 @@
-// bf16 GEMM on 5th-generation tensor cores: D[M,N] = A[M,K] * B[N,K]^T
-// (A = activations, B = nn.Linear-layout weights, both K-major).
+// Tensor-core GEMM on 5th-generation tensor cores: D[M,N] = A[M,K] * B[N,K]^T
+// (A = activations, B = nn.Linear-layout weights, both K-major), in two
+// operand formats sharing one kernel template:
+//   bf16      kind::f16, 64 K-elements (128 bytes) per pipeline stage;
+//   MXFP8     kind::mxf8f6f4.block_scale: e4m3 operands, 128 K-elements per
+//             stage, one UE8M0 (power-of-two) scale per 32 K-elements of every
+//             A row and B row.  The scales travel with each stage (512-byte
+//             chunks per 128 rows, already in the tensor-memory copy layout),
+//             are moved to TMEM by tcgen05.cp and applied inside the MMA, so
+//             the accumulator needs no per-block promotion.
 //
 // Structure (one persistent CTA per SM, 192 threads, warp-specialised):
-//   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage into a
-//               STAGES-deep shared-memory ring (128-byte swizzle), no cluster
-//               multicast (each CTA loads its own tiles; reuse comes from L2).
-//   warp 1      allocates TMEM (2 x BN fp32 columns: double-buffered
-//               accumulator) and issues tcgen05.mma (M=128, N=BN, K=16) from
-//               one thread; tcgen05.commit releases smem stages and signals
-//               a finished accumulator.
+//   warp 0      TMA producer: 128-row A tile + BN-row B tile per stage into a
+//               STAGES-deep shared-memory ring (128-byte swizzle), plus the
+//               scale chunks (bulk copies) for MXFP8; no cluster multicast
+//               (each CTA loads its own tiles; reuse comes from L2).
+//   warp 1      allocates TMEM (double-buffered BN-column fp32 accumulator;
+//               MXFP8 with BN=256 keeps one accumulator so the scale columns
+//               fit) and issues the MMAs (M=128, N=BN) from one thread;
+//               tcgen05.commit releases smem stages and signals a finished
+//               accumulator.
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (each thread owns
 //               one accumulator row = one TMEM lane), add bias / residual,
 //               optional SiLU(gate)*up on interleaved gate/up weight rows,
@@ -29,16 +39,24 @@
 namespace rz {
 
 constexpr int kBM = 128;
-constexpr int kBK = 64;  // one 128-byte swizzle atom of bf16
+constexpr int kBK = 64;         // bf16 K-elements per stage: one 128-byte swizzle atom
+constexpr int kBKMx = 128;      // e4m3 K-elements per stage: the same 128 bytes
+constexpr int kSfChunk = 512;   // UE8M0 scales of 128 rows x 4 K-chunks of 32
+constexpr int kSfTmemCol = 256; // TMEM column where the MXFP8 scales live
 
-template <int BN>
+template <int BN, bool MX>
 struct GemmCfg {
   static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = BN * kBK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int kABytes = kBM * 128;
+  static constexpr int kBBytes = BN * 128;
+  static constexpr int kSfaBytes = MX ? kSfChunk : 0;
+  static constexpr int kSfbBytes = MX ? kSfChunk * (BN / 128) : 0;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // bytes landing per stage
+  static constexpr int kAccStages = (MX && BN == 256) ? 1 : 2;
+  static constexpr int kTmemCols = MX ? 512 : (2 * BN < 32 ? 32 : 2 * BN);
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(!MX || BN >= 128, "MXFP8 tiles cover whole 128-row scale chunks");
+  static_assert(!MX || kAccStages * BN <= kSfTmemCol, "accumulators overlap the scale columns");
 };
 
 __device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float* v) {
@@ -62,17 +80,20 @@ __device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* src, float* v) 
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
-template <int BN>
+template <int BN, bool MX>
 __global__ void __launch_bounds__(192, 1)
-    gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      GemmParams p) {
-  using C = GemmCfg<BN>;
+    gemm_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 GemmParams p) {
+  using C = GemmCfg<BN, MX>;
   constexpr int S = C::kStages;
+  constexpr int KS = C::kAccStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (base & 1023)) & 1023);
   uint8_t* smA = smem;
   uint8_t* smB = smem + S * C::kABytes;
+  uint8_t* smSfa = smB + S * C::kBBytes;      // 1024-aligned: A/B stage sizes are multiples of 1 KB
+  uint8_t* smSfb = smSfa + S * C::kSfaBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
@@ -119,8 +140,18 @@ __global__ void __launch_bounds__(192, 1)
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, p.status, kGemmProducerTimeout)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-          tma_load_2d(smA + s * C::kABytes, &tmA, &full[s], kb * kBK, mb * kBM);
-          tma_load_2d(smB + s * C::kBBytes, &tmB, &full[s], kb * kBK, nb * BN);
+          constexpr int kElems = MX ? kBKMx : kBK;
+          tma_load_2d(smA + s * C::kABytes, &tmA, &full[s], kb * kElems, mb * kBM);
+          tma_load_2d(smB + s * C::kBBytes, &tmB, &full[s], kb * kElems, nb * BN);
+          if constexpr (MX) {
+            bulk_load(smSfa + s * C::kSfaBytes, p.sfa + (static_cast<size_t>(mb) * p.k_blocks + kb) * kSfChunk,
+                      kSfChunk, &full[s]);
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              bulk_load(smSfb + s * C::kSfbBytes + j * kSfChunk,
+                        p.sfb + (static_cast<size_t>(nb * (BN / 128) + j) * p.k_blocks + kb) * kSfChunk,
+                        kSfChunk, &full[s]);
+          }
           if (++s == S) { s = 0; ph ^= 1; }
         }
       }
@@ -135,6 +166,8 @@ __global__ void __launch_bounds__(192, 1)
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+      const uint32_t tsfa = tmem_base + kSfTmemCol;
+      const uint32_t tsfb = tmem_base + kSfTmemCol + 4;
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;
@@ -152,17 +185,32 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           const uint64_t da = smem_desc_k_sw128(smem_u32(smA + s * C::kABytes));
           const uint64_t db = smem_desc_k_sw128(smem_u32(smB + s * C::kBBytes));
+          if constexpr (MX) {
+            // scales of this stage -> TMEM (ordered before the MMAs below in the tensor pipe)
+            tmem_cp_32x128b_warpx4(tsfa, smem_desc_rows16(smem_u32(smSfa + s * C::kSfaBytes)));
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            // +32 bytes along K inside the 128-byte swizzle atom = +2 in the >>4 address field
-            umma_f16(dtm, da + 2 * k, db + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            for (int j = 0; j < BN / 128; ++j)
+              tmem_cp_32x128b_warpx4(tsfb + 4 * j, smem_desc_rows16(smem_u32(smSfb + s * C::kSfbBytes + j * kSfChunk)));
+#pragma unroll
+            for (int k = 0; k < kBKMx / 32; ++k) {
+              // K-chunk k of 32 e4m3 = +32 bytes (+2 in the >>4 address field); its scales are byte k
+              const uint32_t sel = static_cast<uint32_t>(k) << 30;
+              umma_mxf8(dtm, da + 2 * k, db + 2 * k, idesc_mxf8(kBM, BN, k), tsfa | sel, tsfb | sel,
+                        (kb > kb0 || k > 0) ? 1u : 0u);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              // +32 bytes along K inside the 128-byte swizzle atom = +2 in the >>4 address field
+              umma_f16(dtm, da + 2 * k, db + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&empty[s]);
           if (++s == S) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
         umma_commit(&tfull[acc]);
-        if (++acc == 2) { acc = 0; aph ^= 1; }
+        if (++acc == KS) { acc = 0; aph ^= 1; }
       }
     }
   } else {
@@ -266,7 +314,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
-      if (++acc == 2) { acc = 0; aph ^= 1; }
+      if (++acc == KS) { acc = 0; aph ^= 1; }
     }
   }
 
@@ -368,12 +416,15 @@ int num_sms() {
   return n;
 }
 
-template <int BN>
+template <int BN, bool MX>
 static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B, int ldb, cudaStream_t st) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, MX>;
+  constexpr int kElems = MX ? kBKMx : kBK;
+  const CUtensorMapDataType dt = MX ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int es = MX ? 1 : 2;
   CUtensorMap ta, tb;
-  if (make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p0.M, p0.K, lda, kBM, kBK)) return -2;
-  if (make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p0.N, p0.K, ldb, BN, kBK)) return -3;
+  if (make_tmap_2d(&ta, A, dt, es, p0.M, p0.K, lda, kBM, kElems)) return -2;
+  if (make_tmap_2d(&tb, B, dt, es, p0.N, p0.K, ldb, BN, kElems)) return -3;
   GemmParams p = p0;
   p.m_tiles = (p.M + kBM - 1) / kBM;
   p.n_tiles = (p.N + BN - 1) / BN;
@@ -381,10 +432,10 @@ static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B
   const int grid = units < num_sms() ? units : num_sms();
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_bf16_tcgen05<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    cudaFuncSetAttribute(gemm_tcgen05<BN, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     attr_set = true;
   }
-  gemm_bf16_tcgen05<BN><<<grid, 192, C::kSmemBytes, st>>>(ta, tb, p);
+  gemm_tcgen05<BN, MX><<<grid, 192, C::kSmemBytes, st>>>(ta, tb, p);
   if (p.k_splits > 1) {
     const int ncols_out = p.epi == kEpiSiluMul ? p.N / 2 : p.N;
     const long threads = static_cast<long>(p.M) * (ncols_out / 8);
@@ -427,11 +478,112 @@ int gemm_bf16_launch(const GemmParams& p_in, const void* A, int lda, const void*
   p.kb_per_split = (p.k_blocks + p.k_splits - 1) / p.k_splits;
   p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
   switch (bn) {
-    case 256: return launch_bn<256>(p, A, lda, B, ldb, st);
-    case 128: return launch_bn<128>(p, A, lda, B, ldb, st);
-    case 64: return launch_bn<64>(p, A, lda, B, ldb, st);
+    case 256: return launch_bn<256, false>(p, A, lda, B, ldb, st);
+    case 128: return launch_bn<128, false>(p, A, lda, B, ldb, st);
+    case 64: return launch_bn<64, false>(p, A, lda, B, ldb, st);
     default: return -1;
   }
+}
+
+GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi) {
+  // Same waves x per-unit cost estimate as the bf16 planner, with the fp8 MMA
+  // rate (2x bf16 per SM) and 128-element K blocks.  BN=256 holds a single
+  // accumulator (the scale columns take the rest of TMEM), so its epilogue does
+  // not overlap the next tile's MMAs: charge it per unit.
+  const int sms = num_sms();
+  const int kblocks = K / kBKMx;
+  GemmPlan best{128, 1, 1e30};
+  const int bns[2] = {256, 128};
+  for (int bn : bns) {
+    if (N % bn != 0 && bn == 256) continue;
+    const int mt = (M + kBM - 1) / kBM;
+    const int nt = (N + bn - 1) / bn;
+    for (int ks = 1; ks <= 16; ks *= 2) {
+      if (ks > 1 && kblocks / ks < 4) break;
+      const int units = mt * nt * ks;
+      const int waves = (units + sms - 1) / sms;
+      const double kb = static_cast<double>((kblocks + ks - 1) / ks);
+      const double t_mma = kb * (128.0 * bn * 128 * 2) / 16.4e12;
+      const double t_mem = kb * ((128.0 + bn) * 128 + kSfChunk * (1 + bn / 128)) / 43e9;
+      double cost = waves * ((t_mma > t_mem ? t_mma : t_mem) + (bn == 256 ? 1.2e-6 : 0.0)) + 2.5e-6;
+      if (ks > 1) cost += (static_cast<double>(ks) * M * N * 4 * 2) / 6.0e12 + 3e-6;
+      if (cost < best.cost * 0.97) best = GemmPlan{bn, ks, cost};
+    }
+  }
+  return best;
+}
+
+int gemm_mxf8_launch(const GemmParams& p_in, const void* A, int lda, const void* B, int ldb, int bn,
+                     cudaStream_t st) {
+  GemmParams p = p_in;
+  if (p.K % kBKMx != 0 || p.N % 128 != 0 || !p.sfa || !p.sfb) return -4;
+  p.k_blocks = p.K / kBKMx;
+  p.kb_per_split = (p.k_blocks + p.k_splits - 1) / p.k_splits;
+  p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  switch (bn) {
+    case 256: return launch_bn<256, true>(p, A, lda, B, ldb, st);
+    case 128: return launch_bn<128, true>(p, A, lda, B, ldb, st);
+    default: return -1;
+  }
+}
+
+// ---------------------------------------------------------------------------------- MXFP8 quantisation
+// Scale byte position inside a 512-byte chunk for row r (0..127) and K-chunk kc
+// (0..3): rows r, r+32, r+64, r+96 share one 16-byte line, which is the order
+// in which tcgen05.cp.32x128b.warpx4 spreads a line over TMEM columns.
+__host__ __device__ constexpr int sf_offset(int r, int kc) { return (r & 31) * 16 + (r >> 5) * 4 + kc; }
+
+// Power-of-two scale for a block with absolute maximum amax: the smallest 2^e
+// with amax / 2^e <= 448 (the e4m3 maximum).  Returns the biased exponent
+// byte (UE8M0) and writes 2^-e to *inv.
+__device__ __forceinline__ uint32_t ue8m0_scale(float amax, float* inv) {
+  int e = -127;
+  if (amax > 0.f) {
+    const uint32_t bits = __float_as_uint(amax / 448.0f);
+    e = static_cast<int>((bits >> 23) & 0xffu) - 127 + ((bits & 0x7fffffu) != 0u ? 1 : 0);
+  }
+  e = max(-126, min(126, e));
+  *inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+  return static_cast<uint32_t>(e + 127);
+}
+
+// One warp per (row, 128-column block): 4 elements per lane.  Rows in
+// [M, M_pad) only get a neutral scale byte (their operand rows are zero-filled
+// by the tensor map).
+__global__ void quant_mxf8_act_kernel(uint8_t* __restrict__ xq, uint8_t* __restrict__ sfa,
+                                      const __nv_bfloat16* __restrict__ x, int M, int M_pad, int K, int ldx) {
+  const int kblocks = K / 128;
+  const long w = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<long>(M_pad) * kblocks) return;
+  const int row = static_cast<int>(w / kblocks);
+  const int kb = static_cast<int>(w % kblocks);
+  uint8_t* chunk = sfa + (static_cast<size_t>(row / 128) * kblocks + kb) * kSfChunk;
+  if (row >= M) {
+    if (lane == 0) *reinterpret_cast<uint32_t*>(chunk + sf_offset(row & 127, 0)) = 0x7f7f7f7fu;
+    return;
+  }
+  const __nv_bfloat16* src = x + static_cast<size_t>(row) * ldx + kb * 128 + lane * 4;
+  const uint2 u = *reinterpret_cast<const uint2*>(src);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+  const float amax = warp_max(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))));
+  float inv;
+  const uint32_t e = ue8m0_scale(amax, &inv);
+  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a.x * inv, a.y * inv), __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(b.x * inv, b.y * inv), __NV_SATFINITE, __NV_E4M3);
+  *reinterpret_cast<uint32_t*>(xq + static_cast<size_t>(row) * K + kb * 128 + lane * 4) =
+      static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  if (lane == 0) *reinterpret_cast<uint32_t*>(chunk + sf_offset(row & 127, 0)) = e * 0x01010101u;
+}
+
+int quant_mxf8_act_launch(void* xq, uint8_t* sfa, const __nv_bfloat16* x, int M, int K, int ldx, cudaStream_t st) {
+  if (K % 128 != 0) return -1;
+  const int M_pad = (M + 127) / 128 * 128;
+  const long warps = static_cast<long>(M_pad) * (K / 128);
+  quant_mxf8_act_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, st>>>(
+      static_cast<uint8_t*>(xq), sfa, x, M, M_pad, K, ldx);
+  return static_cast<int>(cudaGetLastError());
 }
 
 }  // namespace rz

@@ -23,6 +23,8 @@ struct GemmParams {
   int ldr;
   int epi;
   int* status;
+  const uint8_t* sfa;  // MXFP8 only: A scales, [ceil(M/128)][K/128] chunks of 512 bytes
+  const uint8_t* sfb;  // MXFP8 only: B scales, [N/128][K/128] chunks of 512 bytes
 };
 
 struct GemmPlan {
@@ -35,6 +37,13 @@ GemmPlan plan_gemm(int M, int N, int K, int epi);
 __global__ void gemm_splitk_reduce(GemmParams p);
 int gemm_bf16_launch(const GemmParams& p, const void* A, int lda, const void* B, int ldb, int bn,
                      cudaStream_t stream);
+// MXFP8 (e4m3 operands, UE8M0 scales per 32 K-elements): K % 128 == 0, N % 128 == 0, bn in {128, 256}.
+GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi);
+int gemm_mxf8_launch(const GemmParams& p, const void* A, int lda, const void* B, int ldb, int bn,
+                     cudaStream_t stream);
+// bf16 [M, K] (row stride ldx) -> e4m3 [M, K] + scale chunks for ceil(M/128) row blocks.
+int quant_mxf8_act_launch(void* xq, uint8_t* sfa, const __nv_bfloat16* x, int M, int K, int ldx,
+                          cudaStream_t stream);
 int make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int elem_bytes, int64_t rows,
                  int64_t cols, int64_t ld, int box_rows, int box_cols);
 int num_sms();

@@ -85,7 +85,7 @@ class LLMEngine:
                                 model_dir=mc.path, seed=mc.seed)
             if mc.quantization is not None and mc.quantization.method != "none":
                 from rusteeze_b200.models.quant import quantize_model_fp8
-                quantize_model_fp8(model)
+                quantize_model_fp8(model, getattr(mc.quantization, "scale_format", "ue8m0"))
         if self.device.startswith("cuda"):
             model.prepare_for_gpu()
         self.model = model

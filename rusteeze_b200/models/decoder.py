@@ -165,18 +165,19 @@ class DecoderLM(nn.Module):
     def _lin(self, x: torch.Tensor, owner, name: str, bias=None) -> torch.Tensor:
         q = getattr(owner, name + "_q", None)
         if q is not None:
-            return ops.linear_fp8(x, q, getattr(owner, name + "_s"), bias)
+            return ops.linear_fp8(x, q, getattr(owner, name + "_s"), bias, wsf=getattr(owner, name + "_sf", None))
         return ops.linear(x, getattr(owner, name), bias)
 
     def _row_parallel(self, x: torch.Tensor, owner, name: str) -> torch.Tensor:
         q = getattr(owner, name + "_q", None)
         if q is not None:
-            return self.tp.all_reduce(ops.linear_fp8(x, q, getattr(owner, name + "_s")))
+            return self.tp.all_reduce(ops.linear_fp8(x, q, getattr(owner, name + "_s"),
+                                                     wsf=getattr(owner, name + "_sf", None)))
         return self.tp.row_parallel_linear(x, getattr(owner, name))
 
     def _mlp(self, L, h: torch.Tensor) -> torch.Tensor:
         if getattr(L, "gate_up_q", None) is not None:
-            a = ops.linear_fp8(h, L.gate_up_q, L.gate_up_s, silu_mul=True)
+            a = ops.linear_fp8(h, L.gate_up_q, L.gate_up_s, silu_mul=True, wsf=getattr(L, "gate_up_sf", None))
             return self._row_parallel(a, L, "down")
         if getattr(L, "gate_up_il", None) is not None and h.is_cuda:
             a = ops.linear_silu_mul(h, L.gate_up_il)      # SiLU(gate)*up fused in the GEMM epilogue
@@ -240,7 +241,7 @@ class DecoderLM(nn.Module):
     def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
         """h [n, H] -> fp32 logits [n, vocab] (gathered over TP ranks)."""
         if getattr(self, "lm_head_q", None) is not None:
-            logits = ops.linear_fp8(h, self.lm_head_q, self.lm_head_s)
+            logits = ops.linear_fp8(h, self.lm_head_q, self.lm_head_s, wsf=getattr(self, "lm_head_sf", None))
         else:
             logits = ops.linear(h, self.lm_head_weight)
         if self.tp.size > 1:

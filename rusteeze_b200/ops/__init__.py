@@ -219,18 +219,37 @@ def quant_fp8_act(x: torch.Tensor):
     return xq, xs
 
 
+def quant_mxf8_act(x: torch.Tensor):
+    """bf16 [M, K] -> (e4m3 [M, K], uint8 scale chunks [ceil(M/128), K/128, 512])
+    with power-of-two 1x128 scales in the block-scaled MMA's TMEM copy layout."""
+    M, K = x.shape
+    xq = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
+    sfa = torch.empty((M + 127) // 128, K // 128, 512, dtype=torch.uint8, device=x.device)
+    if M:
+        cuda_ext().quant_mxf8_act(xq, sfa, x)
+        _LAUNCHES[0] += 1
+    return xq, sfa
+
+
 def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
                bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
-               silu_mul: bool = False) -> torch.Tensor:
+               silu_mul: bool = False, wsf: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Block-scaled fp8 GEMM: x bf16 [M,K] is quantised 1x128 on the fly (one
     kernel), wq e4m3 [N,K] carries fp32 128x128 scales ws [N/128, K/128].
+    With `wsf` (the same scales as power-of-two UE8M0 chunks) the GEMM applies
+    the scales inside the tensor-core MMA (kind::mxf8f6f4.block_scale);
+    without it, fp32 scales are applied per 128-K block in the epilogue.
     With silu_mul the weight rows are gate/up interleaved in 64-row blocks and
     the output is silu(gate) * up with N/2 columns."""
     M, N = x.shape[0], wq.shape[0]
     n_out = N // 2 if silu_mul else N
     if not x.is_cuda:
-        xq, xs = quant_fp8_act(x)
-        y = ref.fp8_block_gemm(xq, xs.t(), wq, ws)
+        if wsf is not None:
+            xq, xs_r = ref.quant_mxf8_act(x)
+            y = ref.fp8_block_gemm(xq, xs_r, wq, ws)
+        else:
+            xq, xs = quant_fp8_act(x)
+            y = ref.fp8_block_gemm(xq, xs.t(), wq, ws)
         if bias is not None:
             y = y + bias.float()
         if silu_mul:
@@ -241,6 +260,10 @@ def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
         return y.to(x.dtype)
     out = torch.empty(M, n_out, dtype=torch.bfloat16, device=x.device)
     if M == 0:
+        return out
+    if wsf is not None:
+        xq, sfa = quant_mxf8_act(x)
+        _LAUNCHES[0] += cuda_ext().gemm_mxf8(out, xq, sfa, wq, wsf, bias, residual, 1 if silu_mul else 0, 0, 0)
         return out
     xq, xs = quant_fp8_act(x)
     _LAUNCHES[0] += cuda_ext().gemm_fp8_block(out, xq, xs, wq, ws, bias, residual, 1 if silu_mul else 0, 0)

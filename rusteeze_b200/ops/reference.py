@@ -230,6 +230,73 @@ def quant_fp8_weight(w: torch.Tensor, block: int = 128):
     return q.view(nb * block, K)[:N].contiguous(), s
 
 
+def pow2_ceil(s: torch.Tensor) -> torch.Tensor:
+    """Smallest power of two >= s (s > 0): the UE8M0 scale of a block."""
+    m, e = torch.frexp(s)
+    e = torch.where(m == 0.5, e - 1, e)
+    return torch.ldexp(torch.ones_like(s), e.clamp(-126, 126))
+
+
+def quant_mxf8_act(x: torch.Tensor, group: int = 128):
+    """1 x group activation quant with power-of-two (UE8M0) scales:
+    x [M, K] -> (q e4m3 [M, K], scales fp32 [M, K/group])."""
+    M, K = x.shape
+    xg = x.float().view(M, K // group, group)
+    amax = xg.abs().amax(-1)
+    s = torch.where(amax > 0, pow2_ceil((amax / FP8_E4M3_MAX).clamp_min(1e-38)), torch.ones_like(amax))
+    q = (xg / s.unsqueeze(-1)).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
+    return q.view(M, K), s
+
+
+def quant_mxf8_weight(w: torch.Tensor, block: int = 128):
+    """128x128 block weight quant with power-of-two scales: w [N, K] ->
+    (q [N, K] e4m3, scales fp32 [ceil(N/b), K/b])."""
+    N, K = w.shape
+    nb = (N + block - 1) // block
+    wp = torch.zeros(nb * block, K, dtype=torch.float32, device=w.device)
+    wp[:N] = w.float()
+    wb = wp.view(nb, block, K // block, block)
+    amax = wb.abs().amax(dim=(1, 3))
+    s = torch.where(amax > 0, pow2_ceil((amax / FP8_E4M3_MAX).clamp_min(1e-38)), torch.ones_like(amax))
+    q = (wb / s[:, None, :, None]).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
+    return q.view(nb * block, K)[:N].contiguous(), s
+
+
+def pack_block_scales_ue8m0(s: torch.Tensor) -> torch.Tensor:
+    """fp32 power-of-two scales of 128x128 blocks [R/128, K/128] -> the GEMM's
+    scale chunks: uint8 [R/128, K/128, 512], every byte of a chunk the block's
+    biased exponent (one scale per 128 rows x 32 K-elements, all equal)."""
+    _, e = torch.frexp(s)                       # s = 0.5 * 2^e  ->  log2(s) = e - 1
+    byte = (e - 1 + 127).clamp(1, 254).to(torch.uint8)
+    return byte.unsqueeze(-1).expand(*s.shape, 512).contiguous()
+
+
+def pack_act_scales_ue8m0(s: torch.Tensor) -> torch.Tensor:
+    """fp32 power-of-two 1x128 scales [M, K/128] -> chunks [ceil(M/128), K/128, 512]:
+    row r of a 128-row block keeps its 4 K-chunk bytes at (r%32)*16 + (r/32)*4;
+    rows past M get the neutral byte 127 (scale 1)."""
+    M, kb = s.shape
+    mb = (M + 127) // 128
+    _, e = torch.frexp(s)
+    byte = (e - 1 + 127).clamp(1, 254).to(torch.uint8)
+    full = torch.full((mb * 128, kb), 127, dtype=torch.uint8, device=s.device)
+    full[:M] = byte
+    # [mb, r1(4), r0(32), kb] -> [mb, kb, r0, r1, kc(4)]
+    t = full.view(mb, 4, 32, kb).permute(0, 3, 2, 1).unsqueeze(-1).expand(mb, kb, 32, 4, 4)
+    return t.reshape(mb, kb, 512).contiguous()
+
+
+def unpack_act_scales_ue8m0(sfa: torch.Tensor, M: int, K: int) -> torch.Tensor:
+    """Inverse of the activation scale layout: chunks [ceil(M/128), K/128, 512]
+    -> fp32 scales [M, K/128] (the K-chunk-0 byte of every row)."""
+    kb = K // 128
+    ch = sfa.view(-1, kb, 512).to(torch.int32)
+    r = torch.arange(M, device=sfa.device)
+    off = (r % 128 % 32) * 16 + (r % 128 // 32) * 4
+    e = ch[r // 128].gather(2, off.view(M, 1, 1).expand(M, kb, 1)).squeeze(-1)
+    return torch.ldexp(torch.ones(M, kb, device=sfa.device), e - 127)
+
+
 def fp8_block_gemm(xq, xs, wq, ws, block: int = 128):
     """Dequantise-then-matmul oracle of the block-scaled fp8 GEMM."""
     M, K = xq.shape

@@ -110,6 +110,40 @@ def bench_gemm_fp8(pk, shapes=None) -> List[dict]:
     return out
 
 
+def bench_gemm_mxf8(pk, shapes=None, bns=(0, 128, 256)) -> List[dict]:
+    """MXFP8 GEMM (UE8M0 block scales applied in the MMA) incl. the activation
+    quantisation kernel; bn=0 is the planner's choice."""
+    shapes = shapes or [(8, 6144, 4096), (256, 28672, 4096), (256, 4096, 14336), (1256, 6144, 4096),
+                        (1256, 28672, 4096), (1256, 4096, 14336), (4096, 4096, 4096), (8192, 8192, 8192)]
+    out = []
+    C = ops.cuda_ext()
+    for M, N, K in shapes:
+        ncopies = max(1, min(8, int(3 * 126e6 // (N * K)) + 1))
+        ws = []
+        for _ in range(ncopies):
+            q, s = ref.quant_mxf8_weight(torch.randn(N, K, device="cuda") * 0.02)
+            ws.append((q, ref.pack_block_scales_ue8m0(s)))
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        for bn in bns:
+            it = [0]
+
+            def ours():
+                it[0] = (it[0] + 1) % ncopies
+                xq, sfa = ops.quant_mxf8_act(x)
+                C.gemm_mxf8(y, xq, sfa, ws[it[0]][0], ws[it[0]][1], None, None, 0, bn, 1 if bn else 0)
+
+            t = time_ms(ours)
+            flops = 2.0 * M * N * K
+            bytes_ = N * K + M * K * 2 + M * N * 2
+            plan = list(C.gemm_plan_mxf8(M, N, K, 0)) if bn == 0 else [bn, 1]
+            out.append({"kernel": "gemm_mxf8_tcgen05", "M": M, "N": N, "K": K, "bn": plan[0], "k_splits": plan[1],
+                        "ms": round(t, 4), "tflops": round(flops / t / 1e9, 1), "gbs": round(bytes_ / t / 1e6, 1),
+                        "frac_of_measured_hbm": round(bytes_ / t / 1e6 / pk["hbm_gbs"], 3)})
+        del ws
+    return out
+
+
 def bench_decode(pk, cases=None) -> List[dict]:
     cases = cases or [(1, 1024, 32, 8), (16, 1024, 32, 8), (64, 2048, 32, 8), (256, 1232, 32, 8),
                       (256, 4096, 32, 8)]
@@ -206,7 +240,7 @@ def main():
     ITERS[0], ITERS[1] = a.iters, a.warmup
     pk = peaks()
     res = {"peaks": pk}
-    cases = {"gemm": a.gemm, "decode": a.decode, "prefill": a.prefill}
+    cases = {"gemm": a.gemm, "gemm_fp8": a.gemm, "gemm_mxf8": a.gemm, "decode": a.decode, "prefill": a.prefill}
     for name in a.only.split(","):
         c = cases.get(name)
         if c:

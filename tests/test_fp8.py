@@ -123,3 +123,98 @@ def test_fp8_engine_llama3_shapes_runs():
         for o in eng.step():
             out = o
     assert len(out.outputs[0].token_ids) == 6
+
+
+# ----------------------------------------------------------------------------- MXFP8 (UE8M0 scales)
+def test_ue8m0_codec_and_scale_chunks():
+    torch.manual_seed(3)
+    w = torch.randn(256, 384) * 0.03
+    q, s = ref.quant_mxf8_weight(w)
+    assert torch.equal(s, ref.pow2_ceil(s))                      # powers of two
+    assert (q.float().abs().amax() <= 448).item()
+    deq = (q.float().view(2, 128, 3, 128) * s[:, None, :, None]).view(256, 384)
+    assert ((deq - w).abs().max() / w.abs().max()) < 0.13          # up to one extra bit lost to the pow2 scale
+    ch = ref.pack_block_scales_ue8m0(s)
+    assert ch.shape == (2, 3, 512) and (ch[0, 1] == ch[0, 1, 0]).all()
+    assert torch.equal(torch.ldexp(torch.ones(()), ch[1, 2, 0].long() - 127), s[1, 2])
+    x = torch.randn(200, 256) * 3
+    xq, xs = ref.quant_mxf8_act(x)
+    sfa = ref.pack_act_scales_ue8m0(xs)
+    assert sfa.shape == (2, 2, 512)
+    off = (71 % 32) * 16 + (71 // 32) * 4                            # x row 199 = block 1, in-block row 71
+    want = (torch.log2(xs[199]).round().long() + 127).to(torch.uint8)
+    assert torch.equal(sfa[1, :, off], want) and torch.equal(sfa[1, :, off + 3], want)
+    assert torch.equal(ref.unpack_act_scales_ue8m0(sfa, 200, 256), xs)
+    assert int(sfa[1, 0, (127 % 32) * 16 + (127 // 32) * 4]) == 127   # padded row: neutral scale
+
+
+def test_fp32_scale_format_model_cpu():
+    from rusteeze_b200.models.loader import build_model
+    from rusteeze_b200.models.quant import quantize_model_fp8
+    mc = ModelConfig(name="fp8-tiny", hidden_size=256, intermediate_size=512, num_hidden_layers=1,
+                     num_attention_heads=4, num_key_value_heads=2, vocab_size=1024, max_position_embeddings=512)
+    m = build_model(mc, dtype=torch.float32, seed=1)
+    quantize_model_fp8(m, "fp32")
+    assert getattr(m.layers[0], "qkv_sf", None) is None and m.fp8_format == "fp32"
+    m2 = build_model(mc, dtype=torch.float32, seed=1)
+    quantize_model_fp8(m2)
+    assert m2.layers[0].qkv_sf.dtype == torch.uint8 and m2.fp8_format == "ue8m0"
+
+
+@pytest.mark.gpu
+def test_quant_mxf8_act_kernel_matches_reference():
+    torch.manual_seed(5)
+    x = (torch.randn(300, 1024, device="cuda") * 2).to(torch.bfloat16)
+    x[7, :128] = 0                                                   # all-zero block
+    q, sfa = ops.quant_mxf8_act(x)
+    qr, sr = ref.quant_mxf8_act(x.cpu())
+    assert torch.equal(ref.unpack_act_scales_ue8m0(sfa.cpu(), 300, 1024)[torch.arange(300) != 7],
+                       sr[torch.arange(300) != 7])
+    assert torch.equal(q.cpu().view(torch.uint8)[torch.arange(300) != 7], qr.view(torch.uint8)[torch.arange(300) != 7])
+    assert torch.equal(sfa.cpu()[2, :, (300 % 128 + 1) % 32 * 16 + (300 % 128 + 1) // 32 * 4],
+                       torch.full((8,), 127, dtype=torch.uint8))     # padded row 301 -> neutral
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K,bn,ks", [(1, 256, 256, 128, 1), (7, 4096, 4096, 256, 1), (200, 6144, 4096, 128, 1),
+                                         (200, 6144, 4096, 256, 1), (1300, 4096, 14336, 256, 1),
+                                         (64, 1024, 512, 128, 2), (129, 16000, 1024, 128, 1),
+                                         (300, 2048, 4096, 256, 4), (1256, 28672, 4096, 0, 0)])
+def test_gemm_mxf8_vs_oracle(M, N, K, bn, ks):
+    torch.manual_seed(M + N + bn)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda") * 0.02
+    wq, ws = ref.quant_mxf8_weight(w)
+    wsf = ref.pack_block_scales_ue8m0(ws)
+    xq, sfa = ops.quant_mxf8_act(x)
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ops.cuda_ext().gemm_mxf8(y, xq, sfa, wq, wsf, None, None, 0, bn, ks)
+    xs = ref.unpack_act_scales_ue8m0(sfa.cpu(), M, K)
+    r = ref.fp8_block_gemm(xq.cpu(), xs, wq.cpu(), ws.cpu())
+    rel = ((y.float().cpu() - r).norm() / r.norm()).item()
+    assert rel < 1e-2, rel
+    assert int(ops.cuda_ext().status()[0]) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bn,ks", [(128, 1), (256, 1), (128, 4)])
+def test_gemm_mxf8_silu_bias_residual(bn, ks):
+    torch.manual_seed(11)
+    M, I, K = 150, 1024, 2048
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    wi = ops.interleave_gate_up(torch.randn(2 * I, K, device="cuda", dtype=torch.bfloat16) * 0.02)
+    wq, ws = ref.quant_mxf8_weight(wi)
+    wsf = ref.pack_block_scales_ue8m0(ws)
+    xq, sfa = ops.quant_mxf8_act(x)
+    xs = ref.unpack_act_scales_ue8m0(sfa.cpu(), M, K)
+    out = torch.empty(M, I, device="cuda", dtype=torch.bfloat16)
+    ops.cuda_ext().gemm_mxf8(out, xq, sfa, wq, wsf, None, None, 1, bn, ks)
+    full = ref.fp8_block_gemm(xq.cpu(), xs, wq.cpu(), ws.cpu()).view(M, I // 64, 2, 64)
+    r = (torch.nn.functional.silu(full[:, :, 0]) * full[:, :, 1]).reshape(M, I)
+    assert ((out.float().cpu() - r).norm() / r.norm()).item() < 1e-2
+    y = torch.empty(M, 2 * I, device="cuda", dtype=torch.bfloat16)
+    res = torch.randn(M, 2 * I, device="cuda", dtype=torch.bfloat16)
+    bias = torch.randn(2 * I, device="cuda", dtype=torch.bfloat16)
+    ops.cuda_ext().gemm_mxf8(y, xq, sfa, wq, wsf, bias, res, 0, bn, ks)
+    r2 = ref.fp8_block_gemm(xq.cpu(), xs, wq.cpu(), ws.cpu()) + res.float().cpu() + bias.float().cpu()
+    assert ((y.float().cpu() - r2).norm() / r2.norm()).item() < 1e-2

@@ -25,7 +25,7 @@ def _ar_worker(rank, world, port, q):
     from rusteeze_b200.parallel.dist import init_distributed
     info = init_distributed(timeout_s=60)
     try:
-        ar = PeerAllReduce(dist.group.WORLD, rank, world, info.device, 1 << 22)
+        ar = PeerAllReduce(dist.group.WORLD, rank, world, info.device, 1 << 23)
         errs = []
         for n in (8 * world * 4, 4096 * 8, 256 * 4096, 2048 * 4096):      # one-shot and two-shot sizes
             for it in range(3):
@@ -37,6 +37,9 @@ def _ar_worker(rank, world, port, q):
                 torch.cuda.synchronize()
                 errs.append(((y.float() - ref).abs().max() / ref.abs().max()).item())
         q.put((rank, max(errs), ar.check()))
+    except BaseException as e:  # noqa: BLE001 -- report instead of leaving the parent waiting
+        q.put((rank, repr(e), -1))
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -57,7 +60,7 @@ def test_peer_all_reduce_matches_nccl():
     for p in ps:
         p.join(60)
     for rank, err, status in res:
-        assert status == 0, f"rank {rank} status {status}"
+        assert status == 0, f"rank {rank} status {status}: {err}"
         assert err < 2e-2, f"rank {rank} rel err {err}"
 
 
