@@ -194,10 +194,17 @@ def main():
             admit(time.monotonic() - t0)
         return eng.step()
 
-    # 1. ramp until the batch is full (bounded by wall time)
+    # 1. ramp to steady state (bounded by wall time): the batch is full AND half
+    #    a batch of requests has already finished, so the timed steps mix decode
+    #    with the prefill of newly admitted requests instead of measuring the
+    #    decode-only phase right after the first admissions
     ramp_steps = 0
     ramp_deadline = time.monotonic() + 300.0
-    while eng.scheduler.num_running < args.max_seqs and time.monotonic() < ramp_deadline:
+    finished0 = eng.stats_counters["requests_finished"]
+    while time.monotonic() < ramp_deadline:
+        if (eng.scheduler.num_running >= args.max_seqs and
+                eng.stats_counters["requests_finished"] - finished0 >= args.max_seqs // 2):
+            break
         step()
         ramp_steps += 1
         if nxt >= len(prompts) and not eng.has_unfinished_requests():
@@ -207,6 +214,8 @@ def main():
         step()
     # 3. timed
     gen0 = eng.stats_counters["generation_tokens"]
+    prompt0 = eng.stats_counters["prompt_tokens"]
+    phase0 = eng.host_phase_seconds()
     launches0 = ops.launch_count()
     if world > 1:
         dist.barrier()
@@ -234,6 +243,9 @@ def main():
     ms = ev0.elapsed_time(ev1)
     launches = ops.launch_count() - launches0
     gen = eng.stats_counters["generation_tokens"] - gen0
+    prompt_toks = eng.stats_counters["prompt_tokens"] - prompt0
+    phase1 = eng.host_phase_seconds()
+    host_ms = {k: round((phase1[k] - phase0.get(k, 0.0)) * 1e3 / max(1, args.steps), 3) for k in phase1}
     status = int(ops.cuda_ext().status()[0])
 
     t = torch.tensor([ms, float(gen), float(launches)], dtype=torch.float64, device=device)
@@ -310,6 +322,8 @@ def main():
                        "ramp_steps": ramp_steps},
             "ttft_p50_s": round(statistics.median(ttfts), 4) if ttfts else None,
             "tpot_p50_s": round(statistics.median(tpots), 5) if tpots else None,
+            "prompt_tokens_per_step": round(prompt_toks / max(1, args.steps), 1),
+            "host_ms_per_step": host_ms,
             "clocks": clocks,
             "gpu_launches": int(launches_sum),
             "kernel_status": status,

@@ -494,18 +494,29 @@ GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi) {
   const int kblocks = K / kBKMx;
   GemmPlan best{128, 1, 1e30};
   const int bns[2] = {256, 128};
+  // Per unit: MMA time at the measured per-SM rate
+  // or tile-load time at ~150 GB/s/SM from L2, whichever dominates, plus a
+  // fixed pipeline fill / epilogue cost; the whole GEMM is also bounded below
+  // by streaming the weights once from HBM.  Split-K only pays when the tile
+  // grid cannot fill half of the SMs (measured: splitting a 1.1-wave grid
+  // loses to the fp32 partial traffic).
+  const double hbm_floor = (static_cast<double>(N) * K + static_cast<double>(M) * K) / 6.5e12;
   for (int bn : bns) {
     if (N % bn != 0 && bn == 256) continue;
     const int mt = (M + kBM - 1) / kBM;
     const int nt = (N + bn - 1) / bn;
     for (int ks = 1; ks <= 16; ks *= 2) {
-      if (ks > 1 && kblocks / ks < 4) break;
+      if (ks > 1 && (kblocks / ks < 4 || mt * nt * 2 > sms)) break;
       const int units = mt * nt * ks;
       const int waves = (units + sms - 1) / sms;
       const double kb = static_cast<double>((kblocks + ks - 1) / ks);
-      const double t_mma = kb * (128.0 * bn * 128 * 2) / 16.4e12;
-      const double t_mem = kb * ((128.0 + bn) * 128 + kSfChunk * (1 + bn / 128)) / 43e9;
-      double cost = waves * ((t_mma > t_mem ? t_mma : t_mem) + (bn == 256 ? 1.2e-6 : 0.0)) + 2.5e-6;
+      // 128x128 fp8 tiles are shared-memory bound (~10.5 vs ~14 TFLOP/s/SM measured)
+      const double t_mma = kb * (128.0 * bn * 128 * 2) / (bn == 256 ? 14e12 : 10.5e12);
+      const double t_mem = kb * ((128.0 + bn) * 128 + kSfChunk * (1 + bn / 128)) / 150e9;
+      const double t_unit = (t_mma > t_mem ? t_mma : t_mem) + 1.5e-6 + (bn == 256 ? 1.2e-6 : 0.0);
+      double cost = waves * t_unit;
+      if (cost < hbm_floor) cost = hbm_floor;
+      cost += 2.5e-6;
       if (ks > 1) cost += (static_cast<double>(ks) * M * N * 4 * 2) / 6.0e12 + 3e-6;
       if (cost < best.cost * 0.97) best = GemmPlan{bn, ks, cost};
     }

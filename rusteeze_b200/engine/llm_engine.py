@@ -123,6 +123,7 @@ class LLMEngine:
         self.stats_counters = {"steps": 0, "prompt_tokens": 0, "generation_tokens": 0,
                                "requests_finished": 0, "requests_aborted": 0}
         self.observers: List[Callable] = []
+        self.phase_s: Dict[str, float] = {"schedule": 0.0, "postprocess": 0.0}
         self.spec = None
         if spec is not None:
             from rusteeze_b200.engine.spec_decode import SpecDecoder
@@ -209,6 +210,7 @@ class LLMEngine:
     def step(self) -> List[RequestOutput]:
         if self.spec is not None:
             return self.spec.step()
+        h0 = time.perf_counter()
         with nvtx_range("rz.step.schedule"):
             so = self.scheduler.schedule()
         outputs: List[RequestOutput] = []
@@ -216,8 +218,10 @@ class LLMEngine:
             return self._collect_ignored()
         rows, owners = self._sample_rows(so)
         t0 = time.monotonic()
+        h1 = time.perf_counter()
         with nvtx_range("rz.step.execute"):
             res = self.runner.execute(so, self.bm, rows)
+        h2 = time.perf_counter()
         now = time.monotonic()
         self.stats_counters["steps"] += 1
         touched = self._apply_results(so, res, owners, now)
@@ -227,7 +231,18 @@ class LLMEngine:
             outputs.append(req.to_output(delta=True))
             if req.is_finished():
                 self._retire(req)
-        return outputs + self._collect_ignored()
+        outputs += self._collect_ignored()
+        ph = self.phase_s
+        ph["schedule"] += h1 - h0
+        ph["postprocess"] += time.perf_counter() - h2
+        return outputs
+
+    def host_phase_seconds(self) -> Dict[str, float]:
+        """Cumulative host seconds per step phase (schedule, prepare, enqueue,
+        sample_wait = sampling incl. the wait for the GPU, postprocess)."""
+        d = dict(self.phase_s)
+        d.update(getattr(self.runner, "phase_s", {}))
+        return d
 
     def _collect_ignored(self) -> List[RequestOutput]:
         outs = []

@@ -120,6 +120,7 @@ class ModelRunner:
         self.seed = seed
         self.graph_launches: Dict[int, int] = {}
         self.h2d_bytes = 0      # host->device bytes staged per step (cumulative)
+        self.phase_s: Dict[str, float] = {"prepare": 0.0, "enqueue": 0.0, "sample_wait": 0.0}
         self.d2h_bytes = 0      # device->host bytes read back (cumulative)
 
     # ------------------------------------------------------------------ cache ops
@@ -278,9 +279,18 @@ class ModelRunner:
             self.swap_in(so.blocks_to_swap_in)
         if so.blocks_to_copy:
             self.copy_blocks(so.blocks_to_copy)
+        t0 = time.perf_counter()
         meta, T, S, sample_rows = self.prepare(so, bm)
+        t1 = time.perf_counter()
         logits = self.forward_logits(meta, T, S, sample_rows, pure_decode=not so.prefills)
+        t2 = time.perf_counter()
         res = self.sampler.sample(logits, rows)
+        t3 = time.perf_counter()
+        # host seconds: batch build, forward enqueue, sampling (includes the wait for the GPU)
+        ph = self.phase_s
+        ph["prepare"] += t1 - t0
+        ph["enqueue"] += t2 - t1
+        ph["sample_wait"] += t3 - t2
         self.h2d_bytes += self.sampler.last_h2d_bytes
         self.d2h_bytes += self.sampler.last_d2h_bytes
         return res
