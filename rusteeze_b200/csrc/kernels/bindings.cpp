@@ -8,6 +8,7 @@
 #include "elementwise.h"
 #include "gemm_bf16.h"
 #include "gemm_fp8.h"
+#include "moe.h"
 #include "sampling.h"
 #include "comm.h"
 
@@ -302,6 +303,93 @@ std::vector<int64_t> gemm_plan_mxf8(int64_t M, int64_t N, int64_t K, int64_t epi
   return {pl.bn, pl.k_splits};
 }
 
+// ---------------------------------------------------------------- MoE
+// Grouped GEMM over 128-aligned expert segments: x [rows, K], w [G, N, K] -> out [rows, N or N/2].
+int64_t gemm_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor grp_off,
+                     torch::Tensor grp_end, int64_t epi, int64_t bn) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w);
+  TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "grouped gemm: contiguous tensors");
+  TORCH_CHECK(w.dim() == 3 && w.size(2) == x.size(1), "grouped gemm: w [G, N, K]");
+  const int G = w.size(0), N = w.size(1), K = x.size(1);
+  TORCH_CHECK(grp_off.numel() == G + 1 && grp_end.numel() == G && grp_off.scalar_type() == at::kInt,
+              "grouped gemm: int32 grp_off [G+1], grp_end [G]");
+  TORCH_CHECK(G <= rz::kMaxGemmGroups && K % 64 == 0 && N % 64 == 0, "grouped gemm: G <= 64, K/N multiples of 64");
+  if (epi == rz::kEpiSiluMul) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "silu epilogue: N % 128, out N/2");
+  if (bn <= 0) bn = (static_cast<int64_t>((x.size(0) + 127) / 128) * (N / 256) >= 2 * rz::num_sms()) ? 256 : 128;
+  rz::GemmParams p{};
+  p.N = N; p.K = K;
+  p.k_splits = 1;
+  p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldd = out.stride(0);
+  p.epi = epi;
+  p.status = status_ptr();
+  p.grp_off = grp_off.data_ptr<int>();
+  p.grp_end = grp_end.data_ptr<int>();
+  p.num_groups = G;
+  check_rc(rz::gemm_grouped_launch(p, x.data_ptr(), K, x.size(0), w.data_ptr(), K, bn, false, cur_stream()),
+           "gemm_grouped");
+  return 1;
+}
+
+// Whole MoE block for the local experts: route -> permute -> grouped gate/up (SiLU) -> grouped down
+// -> combine.  w13 holds every local expert's gate/up rows interleaved in 64-row blocks.
+// Returns the number of kernels launched.
+int64_t moe_forward(torch::Tensor out, torch::Tensor h, torch::Tensor wr, torch::Tensor w13, torch::Tensor w2,
+                    int64_t topk, int64_t e_lo, bool renormalize, c10::optional<torch::Tensor> residual) {
+  CHECK_CUDA(h); CHECK_BF16(h); CHECK_BF16(wr); CHECK_BF16(w13); CHECK_BF16(w2); CHECK_LAST(h);
+  const int M = h.size(0), H = h.size(1), E = wr.size(0), ne = w13.size(0), I = w13.size(1) / 2;
+  TORCH_CHECK(wr.size(1) == H && w13.size(2) == H && w2.size(0) == ne && w2.size(1) == H && w2.size(2) == I,
+              "moe: weight shapes");
+  TORCH_CHECK(topk >= 1 && topk <= 8 && topk <= E && E <= 32 && e_lo >= 0 && e_lo + ne <= E, "moe: expert ranges");
+  TORCH_CHECK(out.is_contiguous() && out.size(0) == M && out.size(1) == H, "moe: out [M, H]");
+  auto i32 = h.options().dtype(torch::kInt32);
+  auto cnt = torch::zeros({2 * ne}, i32);  // counts | fill
+  auto tw = torch::empty({M, topk}, h.options().dtype(torch::kFloat32));
+  auto tid = torch::empty({M, topk}, i32);
+  rz::MoeRouteParams rp{};
+  rp.h = reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()); rp.ldh = h.stride(0);
+  rp.wr = reinterpret_cast<const __nv_bfloat16*>(wr.data_ptr());
+  rp.M = M; rp.H = H; rp.E = E; rp.topk = topk; rp.e_lo = e_lo; rp.ne = ne; rp.renormalize = renormalize;
+  rp.topk_w = tw.data_ptr<float>(); rp.topk_id = tid.data_ptr<int>(); rp.counts = cnt.data_ptr<int>();
+  check_rc(rz::moe_route_launch(rp, cur_stream()), "moe_route");
+  const int64_t rows = static_cast<int64_t>(M) * topk + 128 * ne;
+  auto x_perm = torch::empty({rows, H}, h.options());
+  auto grp = torch::empty({2 * ne + 1}, i32);
+  auto pos = torch::empty({M * topk}, i32);
+  rz::MoePermuteParams pp{};
+  pp.h = rp.h; pp.ldh = rp.ldh; pp.topk_id = rp.topk_id; pp.counts = rp.counts;
+  pp.M = M; pp.H = H; pp.topk = topk; pp.e_lo = e_lo; pp.ne = ne;
+  pp.fill = rp.counts + ne; pp.grp_off = grp.data_ptr<int>(); pp.grp_end = pp.grp_off + ne + 1;
+  pp.pos_of = pos.data_ptr<int>(); pp.x_perm = reinterpret_cast<__nv_bfloat16*>(x_perm.data_ptr());
+  check_rc(rz::moe_permute_launch(pp, cur_stream()), "moe_permute");
+  auto go = grp.narrow(0, 0, ne + 1), ge = grp.narrow(0, ne + 1, ne);
+  auto act = torch::empty({rows, I}, h.options());
+  gemm_grouped(act, x_perm, w13, go, ge, rz::kEpiSiluMul, 0);
+  auto y = torch::empty({rows, H}, h.options());
+  gemm_grouped(y, act, w2, go, ge, rz::kEpiNone, 0);
+  rz::MoeCombineParams cp{};
+  cp.y = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()); cp.ldy = H;
+  cp.pos_of = pp.pos_of; cp.topk_w = rp.topk_w;
+  cp.residual = residual.has_value() ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
+  cp.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  cp.M = M; cp.H = H; cp.topk = topk;
+  check_rc(rz::moe_combine_launch(cp, cur_stream()), "moe_combine");
+  return 6;   // zero-fill, route, permute, 2 grouped GEMMs, combine
+}
+
+// Routing only (tests): fills topk weights / ids and the local expert counts.
+void moe_route(torch::Tensor tw, torch::Tensor tid, torch::Tensor counts, torch::Tensor h, torch::Tensor wr,
+               int64_t topk, int64_t e_lo, int64_t ne, bool renormalize) {
+  CHECK_CUDA(h); CHECK_BF16(h); CHECK_BF16(wr);
+  rz::MoeRouteParams rp{};
+  rp.h = reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()); rp.ldh = h.stride(0);
+  rp.wr = reinterpret_cast<const __nv_bfloat16*>(wr.data_ptr());
+  rp.M = h.size(0); rp.H = h.size(1); rp.E = wr.size(0); rp.topk = topk; rp.e_lo = e_lo; rp.ne = ne;
+  rp.renormalize = renormalize;
+  rp.topk_w = tw.data_ptr<float>(); rp.topk_id = tid.data_ptr<int>(); rp.counts = counts.data_ptr<int>();
+  check_rc(rz::moe_route_launch(rp, cur_stream()), "moe_route");
+}
+
 // ---------------------------------------------------------------- sampling
 void argmax_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, bool want_lp) {
   CHECK_CUDA(logits);
@@ -375,6 +463,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_fp8_act", &quant_fp8_act);
   m.def("gemm_fp8_block", &gemm_fp8_block);
   m.def("quant_mxf8_act", &quant_mxf8_act);
+  m.def("gemm_grouped", &gemm_grouped);
+  m.def("moe_forward", &moe_forward);
+  m.def("moe_route", &moe_route);
   m.def("gemm_mxf8", &gemm_mxf8);
   m.def("gemm_plan_mxf8", &gemm_plan_mxf8);
   m.def("argmax_sample", &argmax_sample);

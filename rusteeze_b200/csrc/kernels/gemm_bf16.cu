@@ -103,7 +103,21 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_units = p.m_tiles * p.n_tiles * p.k_splits;
+  // Grouped mode (MoE experts): A rows are expert-sorted with every expert's
+  // segment starting on a 128-row boundary (grp_off[g], g = 0..G), its valid
+  // rows ending at grp_end[g]; B holds G weight matrices of N rows each.  The
+  // segment sizes live on the device, so the tile count is read here.
+  __shared__ int s_grp[2 * kMaxGemmGroups + 1];
+  const int G = p.grp_off ? p.num_groups : 0;
+  for (int i = threadIdx.x; i < 2 * G + 1; i += blockDim.x)
+    s_grp[i] = i <= G ? p.grp_off[i] : p.grp_end[i - G - 1];
+  const int m_tiles = G ? p.grp_off[G] / kBM : p.m_tiles;
+  const int num_units = m_tiles * p.n_tiles * p.k_splits;
+  auto group_of = [&](int mb) {
+    int g = 0;
+    while (g + 1 < G && s_grp[g + 1] <= mb * kBM) ++g;
+    return g;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -133,8 +147,9 @@ __global__ void __launch_bounds__(192, 1)
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int ks = u % p.k_splits;
         const int t = u / p.k_splits;
-        const int mb = t % p.m_tiles;
-        const int nb = t / p.m_tiles;
+        const int mb = t % m_tiles;
+        const int nb = t / m_tiles;
+        const int b_row0 = (G ? group_of(mb) * p.N : 0) + nb * BN;
         const int kb0 = ks * p.kb_per_split;
         const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -142,14 +157,14 @@ __global__ void __launch_bounds__(192, 1)
           mbar_arrive_expect_tx(&full[s], C::kStageBytes);
           constexpr int kElems = MX ? kBKMx : kBK;
           tma_load_2d(smA + s * C::kABytes, &tmA, &full[s], kb * kElems, mb * kBM);
-          tma_load_2d(smB + s * C::kBBytes, &tmB, &full[s], kb * kElems, nb * BN);
+          tma_load_2d(smB + s * C::kBBytes, &tmB, &full[s], kb * kElems, b_row0);
           if constexpr (MX) {
             bulk_load(smSfa + s * C::kSfaBytes, p.sfa + (static_cast<size_t>(mb) * p.k_blocks + kb) * kSfChunk,
                       kSfChunk, &full[s]);
 #pragma unroll
             for (int j = 0; j < BN / 128; ++j)
               bulk_load(smSfb + s * C::kSfbBytes + j * kSfChunk,
-                        p.sfb + (static_cast<size_t>(nb * (BN / 128) + j) * p.k_blocks + kb) * kSfChunk,
+                        p.sfb + (static_cast<size_t>(b_row0 / 128 + j) * p.k_blocks + kb) * kSfChunk,
                         kSfChunk, &full[s]);
           }
           if (++s == S) { s = 0; ph ^= 1; }
@@ -222,12 +237,12 @@ __global__ void __launch_bounds__(192, 1)
     for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
       const int ks = u % p.k_splits;
       const int t = u / p.k_splits;
-      const int mb = t % p.m_tiles;
-      const int nb = t / p.m_tiles;
+      const int mb = t % m_tiles;
+      const int nb = t / m_tiles;
       if (!mbar_wait(&tfull[acc], aph, p.status, kGemmEpilogueTimeout)) break;
       tc_fence_after();
       const int row = mb * kBM + row_in_tile;
-      const bool row_ok = row < p.M;
+      const bool row_ok = row < (G ? s_grp[G + 1 + group_of(mb)] : p.M);
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       if (p.k_splits > 1) {
         float* dst = p.partial + (static_cast<size_t>(ks) * p.M + row) * p.N;
@@ -483,6 +498,45 @@ int gemm_bf16_launch(const GemmParams& p_in, const void* A, int lda, const void*
     case 64: return launch_bn<64, false>(p, A, lda, B, ldb, st);
     default: return -1;
   }
+}
+
+int gemm_grouped_launch(const GemmParams& p_in, const void* A, int lda, int64_t a_rows, const void* B, int ldb,
+                        int bn, bool mx, cudaStream_t st) {
+  // A: [a_rows, K] expert-sorted activations (segments 128-aligned); B: [G * N, K].
+  GemmParams p = p_in;
+  if (!p.grp_off || !p.grp_end || p.num_groups < 1 || p.num_groups > kMaxGemmGroups) return -4;
+  if (p.k_splits != 1) return -5;
+  const int kel = mx ? kBKMx : kBK;
+  p.k_blocks = (p.K + kel - 1) / kel;
+  p.kb_per_split = p.k_blocks;
+  p.M = static_cast<int>(a_rows);                 // tensor-map extent; valid rows come from grp_end
+  p.m_tiles = 0;
+  // the real tile count is known on the device only: launch one persistent CTA per SM
+  const int units_max = static_cast<int>((a_rows + kBM - 1) / kBM) * ((p.N + bn - 1) / bn);
+  const int grid = units_max < num_sms() ? (units_max > 0 ? units_max : 1) : num_sms();
+  const CUtensorMapDataType dt = mx ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int es = mx ? 1 : 2;
+  CUtensorMap ta, tb;
+  if (make_tmap_2d(&ta, A, dt, es, a_rows, p.K, lda, kBM, kel)) return -2;
+  if (make_tmap_2d(&tb, B, dt, es, static_cast<int64_t>(p.num_groups) * p.N, p.K, ldb, bn, kel)) return -3;
+  p.n_tiles = (p.N + bn - 1) / bn;
+#define RZ_GROUPED(BNV, MXV)                                                                                   \
+  {                                                                                                           \
+    using C = GemmCfg<BNV, MXV>;                                                                              \
+    static bool attr = false;                                                                                 \
+    if (!attr) {                                                                                              \
+      cudaFuncSetAttribute(gemm_tcgen05<BNV, MXV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes); \
+      attr = true;                                                                                            \
+    }                                                                                                         \
+    gemm_tcgen05<BNV, MXV><<<grid, 192, C::kSmemBytes, st>>>(ta, tb, p);                                      \
+  }
+  if (!mx && bn == 256) RZ_GROUPED(256, false)
+  else if (!mx && bn == 128) RZ_GROUPED(128, false)
+  else if (mx && bn == 256) RZ_GROUPED(256, true)
+  else if (mx && bn == 128) RZ_GROUPED(128, true)
+  else return -1;
+#undef RZ_GROUPED
+  return static_cast<int>(cudaGetLastError());
 }
 
 GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi) {

@@ -25,7 +25,14 @@ struct GemmParams {
   int* status;
   const uint8_t* sfa;  // MXFP8 only: A scales, [ceil(M/128)][K/128] chunks of 512 bytes
   const uint8_t* sfb;  // MXFP8 only: B scales, [N/128][K/128] chunks of 512 bytes
+  // grouped (MoE) mode: device arrays, 128-aligned segment starts [num_groups + 1]
+  // and valid-row ends [num_groups]; B is num_groups matrices of N rows
+  const int* grp_off;
+  const int* grp_end;
+  int num_groups;
 };
+
+constexpr int kMaxGemmGroups = 64;
 
 struct GemmPlan {
   int bn;
@@ -37,6 +44,9 @@ GemmPlan plan_gemm(int M, int N, int K, int epi);
 __global__ void gemm_splitk_reduce(GemmParams p);
 int gemm_bf16_launch(const GemmParams& p, const void* A, int lda, const void* B, int ldb, int bn,
                      cudaStream_t stream);
+// Grouped GEMM over expert-sorted rows (see GemmParams::grp_off); k_splits must be 1.
+int gemm_grouped_launch(const GemmParams& p, const void* A, int lda, int64_t a_rows, const void* B, int ldb,
+                        int bn, bool mx, cudaStream_t stream);
 // MXFP8 (e4m3 operands, UE8M0 scales per 32 K-elements): K % 128 == 0, N % 128 == 0, bn in {128, 256}.
 GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi);
 int gemm_mxf8_launch(const GemmParams& p, const void* A, int lda, const void* B, int ldb, int bn,

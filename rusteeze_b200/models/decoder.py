@@ -191,7 +191,16 @@ class DecoderLM(nn.Module):
         """Re-lays weights for the GPU kernels: gate/up rows interleaved in
         64-row blocks for the fused SiLU epilogue (the [gate | up] copy is
         dropped to save HBM)."""
-        if not self.device.type == "cuda" or self.cfg.is_moe or self.act != "silu" or getattr(self, "fp8", False):
+        if not self.device.type == "cuda" or self.act != "silu" or getattr(self, "fp8", False):
+            return
+        if self.cfg.is_moe:
+            if self.cfg.intermediate_size % 64 or self.cfg.hidden_size % 256:
+                return
+            for L in self.layers:
+                if getattr(L, "w13_il", None) is not None:
+                    continue
+                L.w13_il = ops.interleave_gate_up_experts(L.w13)
+                L.w13 = nn.Parameter(torch.empty(0, dtype=self.dtype, device=self.device), requires_grad=False)
             return
         if self.inter % 64:
             return
@@ -204,6 +213,10 @@ class DecoderLM(nn.Module):
     def _moe(self, L, h: torch.Tensor) -> torch.Tensor:
         if self.moe_impl is not None:
             return self.moe_impl(L, h)
+        if getattr(L, "w13_il", None) is not None and h.is_cuda:
+            out = ops.moe_forward(h, L.router, L.w13_il, L.w2, self.cfg.num_experts_per_tok, self.e_lo,
+                                  True)
+            return self.tp.all_reduce(out) if self.tp.size > 1 else out
         return moe_forward_local(L, h, self.cfg, self.e_lo, self.e_hi, self.tp)
 
     # ------------------------------------------------------------------ forward

@@ -326,5 +326,8 @@ def to_cpu_fp32(model: DecoderLM) -> DecoderLM:
         src = _param(model, name)
         if name.endswith("gate_up") and src.numel() == 0:
             src = deinterleave_gate_up(_param(model, name[:-len("gate_up")] + "gate_up_il"))
+        if name.endswith("w13") and src.numel() == 0:
+            il = _param(model, name + "_il")
+            src = torch.stack([deinterleave_gate_up(il[e]) for e in range(il.shape[0])])
         _param(out, name).copy_(src.float().cpu())
     return out.eval()

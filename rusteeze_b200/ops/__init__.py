@@ -270,6 +270,28 @@ def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
     return out
 
 
+# ----------------------------------------------------------------------------- MoE
+def moe_forward(h: torch.Tensor, router: torch.Tensor, w13_il: torch.Tensor, w2: torch.Tensor, topk: int,
+                e_lo: int = 0, renormalize: bool = True,
+                residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Routed MoE block over the local experts [e_lo, e_lo + w13_il.shape[0]):
+    fused router + top-k softmax, expert-sorted gather (128-aligned segments),
+    grouped tcgen05 GEMMs (gate/up with SiLU epilogue, then down) and the
+    weighted combine; no host synchronisation.  Tokens routed to experts of
+    other ranks contribute zero (the caller sums partial outputs over ranks)."""
+    out = torch.empty_like(h)
+    if h.shape[0] == 0:
+        return out
+    _LAUNCHES[0] += cuda_ext().moe_forward(out, h.contiguous(), router, w13_il, w2, topk, e_lo, renormalize,
+                                          residual)
+    return out
+
+
+def interleave_gate_up_experts(w13: torch.Tensor, block: int = 64) -> torch.Tensor:
+    """[E, 2I, K] per-expert [gate | up] rows -> the 64-row interleaved layout."""
+    return torch.stack([interleave_gate_up(w13[e], block) for e in range(w13.shape[0])]).contiguous()
+
+
 # ----------------------------------------------------------------------------- sampling
 def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
            min_p: torch.Tensor, seeds: torch.Tensor, offsets: torch.Tensor, greedy_all: bool,
