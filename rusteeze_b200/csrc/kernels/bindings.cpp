@@ -9,6 +9,7 @@
 #include "gemm_bf16.h"
 #include "gemm_fp8.h"
 #include "moe.h"
+#include "tp_fused.h"
 #include "sampling.h"
 #include "comm.h"
 
@@ -390,6 +391,97 @@ void moe_route(torch::Tensor tw, torch::Tensor tid, torch::Tensor counts, torch:
   check_rc(rz::moe_route_launch(rp, cur_stream()), "moe_route");
 }
 
+// ---------------------------------------------------------------- fused tensor-parallel boundary
+// Row-parallel GEMM whose epilogue reduce-scatters into the owners' slot buffers.  Returns n_tiles.
+int64_t gemm_peer_rs(torch::Tensor x, torch::Tensor w, std::vector<int64_t> slots, std::vector<int64_t> flags,
+                     int64_t rank, int64_t rs_rows, torch::Tensor epoch, int64_t call_idx, int64_t bn) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_LAST(x); CHECK_LAST(w);
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  const int world = static_cast<int>(slots.size());
+  TORCH_CHECK(world >= 1 && world <= rz::kMaxTpRanks && flags.size() == slots.size(), "gemm_peer_rs: 1..8 ranks");
+  TORCH_CHECK(w.size(1) == K && K % 8 == 0 && N % 8 == 0 && rs_rows % rz::kAgRowBlock == 0 &&
+                  static_cast<int64_t>(rs_rows) * world >= M,
+              "gemm_peer_rs: shapes");
+  if (bn <= 0) bn = rz::plan_gemm(M, N, K, 0).bn;
+  rz::GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.k_splits = 1;
+  p.epi = rz::kEpiPeerRS;
+  p.status = status_ptr();
+  for (int i = 0; i < world; ++i) {
+    p.rs_slot[i] = reinterpret_cast<__nv_bfloat16*>(slots[i]);
+    p.rs_flag[i] = reinterpret_cast<uint32_t*>(flags[i]);
+  }
+  p.rs_rows = rs_rows;
+  p.tp_rank = rank; p.tp_world = world;
+  p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  p.call_idx = static_cast<uint32_t>(call_idx);
+  check_rc(rz::gemm_bf16_launch(p, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), bn, cur_stream()),
+           "gemm_peer_rs");
+  return (N + bn - 1) / bn;
+}
+
+// GEMM whose A rows are all-gathered by peers: waits on the local all-gather flags per A tile.
+int64_t gemm_ag(torch::Tensor out, torch::Tensor g, torch::Tensor w, c10::optional<torch::Tensor> bias, int64_t epi,
+                torch::Tensor ag_flag, torch::Tensor epoch, int64_t call_idx) {
+  CHECK_CUDA(g); CHECK_BF16(g); CHECK_BF16(w); CHECK_LAST(g); CHECK_LAST(w);
+  const int M = g.size(0), K = g.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && K % 8 == 0 && N % 8 == 0, "gemm_ag: shapes");
+  if (epi == rz::kEpiSiluMul) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "silu epilogue: N % 128, out N/2");
+  auto pl = rz::plan_gemm(M, N, K, epi);
+  rz::GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.k_splits = pl.k_splits;
+  p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldd = out.stride(0);
+  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  p.epi = epi;
+  p.status = status_ptr();
+  p.ag_flag = reinterpret_cast<const uint32_t*>(ag_flag.data_ptr());
+  p.ag_rows = M;
+  p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  p.call_idx = static_cast<uint32_t>(call_idx);
+  torch::Tensor ws;
+  if (pl.k_splits > 1) {
+    ws = torch::empty({pl.k_splits, M, N}, g.options().dtype(torch::kFloat32));
+    p.partial = ws.data_ptr<float>();
+  }
+  check_rc(rz::gemm_bf16_launch(p, g.data_ptr(), g.stride(0), w.data_ptr(), w.stride(0), pl.bn, cur_stream()),
+           "gemm_ag");
+  return pl.k_splits > 1 ? 2 : 1;
+}
+
+void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10::optional<torch::Tensor> resid_in,
+                torch::Tensor residual, torch::Tensor w, double eps, double offset, std::vector<int64_t> gathers,
+                std::vector<int64_t> ag_flags, int64_t rank, int64_t M, int64_t rs_rows, torch::Tensor epoch,
+                int64_t call_idx) {
+  CHECK_BF16(residual); CHECK_BF16(w);
+  const int world = static_cast<int>(gathers.size());
+  TORCH_CHECK(world >= 1 && world <= rz::kMaxTpRanks && ag_flags.size() == gathers.size(), "rs_norm_ag: ranks");
+  rz::RsNormAgParams p{};
+  p.slots = reinterpret_cast<const __nv_bfloat16*>(slots.data_ptr());
+  p.rs_flag = reinterpret_cast<const uint32_t*>(rs_flag.data_ptr());
+  p.n_tiles = n_tiles;
+  p.reduce = resid_in.has_value() ? 0 : 1;
+  p.resid_in = resid_in.has_value() ? reinterpret_cast<const __nv_bfloat16*>(resid_in->data_ptr()) : nullptr;
+  p.residual = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  p.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  p.eps = eps; p.offset = offset;
+  for (int i = 0; i < world; ++i) {
+    p.gather[i] = reinterpret_cast<__nv_bfloat16*>(gathers[i]);
+    p.ag_flag[i] = reinterpret_cast<uint32_t*>(ag_flags[i]);
+  }
+  p.rank = rank; p.world = world; p.M = M; p.rs_rows = rs_rows; p.H = w.size(0);
+  p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  p.call_idx = static_cast<uint32_t>(call_idx);
+  p.status = status_ptr();
+  check_rc(rz::rs_norm_ag_launch(p, cur_stream()), "rs_norm_ag");
+}
+
+void tp_epoch_bump(torch::Tensor epoch) {
+  check_rc(rz::tp_epoch_bump_launch(reinterpret_cast<uint32_t*>(epoch.data_ptr()), cur_stream()), "tp_epoch_bump");
+}
+
 // ---------------------------------------------------------------- sampling
 void argmax_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, bool want_lp) {
   CHECK_CUDA(logits);
@@ -464,6 +556,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8_block", &gemm_fp8_block);
   m.def("quant_mxf8_act", &quant_mxf8_act);
   m.def("gemm_grouped", &gemm_grouped);
+  m.def("gemm_peer_rs", &gemm_peer_rs);
+  m.def("gemm_ag", &gemm_ag);
+  m.def("rs_norm_ag", &rs_norm_ag);
+  m.def("tp_epoch_bump", &tp_epoch_bump);
   m.def("moe_forward", &moe_forward);
   m.def("moe_route", &moe_route);
   m.def("gemm_mxf8", &gemm_mxf8);

@@ -96,6 +96,35 @@ RZ_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) 
   }
 }
 
+// ------------------------------------------------------------------ cross-GPU flags (NVLink P2P)
+RZ_DEVICE void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+RZ_DEVICE uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Spin until *flag >= target (acquire, system scope), bounded by kWaitTimeoutNs.
+RZ_DEVICE bool wait_flag_geq(const uint32_t* flag, uint32_t target, int* status, int code) {
+  if (ld_acquire_sys_u32(flag) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    if (ld_acquire_sys_u32(flag) >= target) return true;
+    if ((it & 63u) == 63u && globaltimer() - t0 > kWaitTimeoutNs) {
+      set_status(status, code);
+      return false;
+    }
+  }
+}
+// order generic-proxy writes (peer stores observed through an acquire) before
+// later async-proxy (TMA) reads of global memory
+RZ_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+// barrier among a subset of warps (id != 0; count = threads, a multiple of 32)
+RZ_DEVICE void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ------------------------------------------------------------------ TMA (no cluster multicast)
 RZ_DEVICE void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");

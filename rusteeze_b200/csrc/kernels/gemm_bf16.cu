@@ -113,6 +113,8 @@ __global__ void __launch_bounds__(192, 1)
     s_grp[i] = i <= G ? p.grp_off[i] : p.grp_end[i - G - 1];
   const int m_tiles = G ? p.grp_off[G] / kBM : p.m_tiles;
   const int num_units = m_tiles * p.n_tiles * p.k_splits;
+  const uint32_t epoch =
+      p.epoch_ptr ? *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u : 0u;
   auto group_of = [&](int mb) {
     int g = 0;
     while (g + 1 < G && s_grp[g + 1] <= mb * kBM) ++g;
@@ -150,6 +152,15 @@ __global__ void __launch_bounds__(192, 1)
         const int mb = t % m_tiles;
         const int nb = t / m_tiles;
         const int b_row0 = (G ? group_of(mb) * p.N : 0) + nb * BN;
+        if (p.ag_flag) {
+          // all-gathered A rows arrive from their owners: wait for this tile's row blocks
+          const int rb0 = mb * kBM / kAgRowBlock;
+          const int rb1 = min((p.ag_rows + kAgRowBlock - 1) / kAgRowBlock, (mb + 1) * kBM / kAgRowBlock);
+          for (int rb = rb0; rb < rb1 && ok; ++rb)
+            ok = wait_flag_geq(p.ag_flag + rb, epoch, p.status, kCommPeerTimeout);
+          fence_proxy_async_global();
+          if (!ok) break;
+        }
         const int kb0 = ks * p.kb_per_split;
         const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -292,6 +303,39 @@ __global__ void __launch_bounds__(192, 1)
               for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, o + j);
             }
           }
+        }
+      } else if (p.epi == kEpiPeerRS) {
+        // reduce-scatter: the row goes to its owner's slot for this rank, over NVLink
+        const int owner = row / p.rs_rows;
+        __nv_bfloat16* dst = row_ok ? p.rs_slot[owner] +
+                                          (static_cast<size_t>(p.tp_rank) * p.rs_rows + (row - owner * p.rs_rows)) * p.N
+                                    : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tacc + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = nb * BN + c * 32;
+          if (row_ok && col0 < p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              float o[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[j + i]);
+              store_bf16x8(dst + col0 + j, o);
+            }
+          }
+        }
+        // this warp's 32 rows are stored: publish them (per tile quarter) to each owner they touch
+        __threadfence_system();
+        __syncwarp();
+        const int r0 = mb * kBM + quarter * 32;
+        if (lane == 0 && r0 < p.M) {
+          const int r1 = min(p.M, r0 + 32) - 1;
+          for (int o = r0 / p.rs_rows; o <= r1 / p.rs_rows; ++o)
+            st_release_sys_u32(
+                p.rs_flag[o] + ((static_cast<size_t>(mb) * p.n_tiles + nb) * 4 + quarter) * p.tp_world + p.tp_rank,
+                epoch);
         }
       } else {
 #pragma unroll 1

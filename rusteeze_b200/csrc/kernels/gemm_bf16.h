@@ -7,7 +7,10 @@
 
 namespace rz {
 
-enum GemmEpilogue : int { kEpiNone = 0, kEpiSiluMul = 1 };
+enum GemmEpilogue : int { kEpiNone = 0, kEpiSiluMul = 1, kEpiPeerRS = 2 };
+
+constexpr int kMaxTpRanks = 8;
+constexpr int kAgRowBlock = 8;    // rows per all-gather flag
 
 struct GemmParams {
   int M, N, K;
@@ -30,6 +33,21 @@ struct GemmParams {
   const int* grp_off;
   const int* grp_end;
   int num_groups;
+  // tensor-parallel fusion (sequence-sharded rows: rank o owns rows [o*rs_rows, (o+1)*rs_rows))
+  //   kEpiPeerRS: every finished tile row is stored into its owner's slot buffer
+  //     rs_slot[o] + ((tp_rank * rs_rows + local row) * N) over NVLink, then each epilogue
+  //     warp releases rs_flag[o][((m_tile * n_tiles + n_tile) * 4 + quarter) * tp_world + tp_rank]
+  //     for its 32 rows;
+  //   ag_flag != null: before loading an A tile, the producer waits for the
+  //     all-gather flags of its rows (one per kAgRowBlock rows, rows < ag_rows).
+  __nv_bfloat16* rs_slot[kMaxTpRanks];
+  uint32_t* rs_flag[kMaxTpRanks];
+  int rs_rows;
+  int tp_rank, tp_world;
+  const uint32_t* ag_flag;
+  int ag_rows;
+  const uint32_t* epoch_ptr;   // device step counter; flags carry (*epoch_ptr) * 256 + call_idx + 1
+  uint32_t call_idx;
 };
 
 constexpr int kMaxGemmGroups = 64;

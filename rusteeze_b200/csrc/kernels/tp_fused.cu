@@ -1,0 +1,127 @@
+// Tensor-parallel layer boundary fused with its collectives (NVLink P2P).
+//
+// Between the row-parallel GEMMs (o_proj, down_proj) and the next column-
+// parallel GEMM (QKV, gate/up) the residual stream is sequence-sharded: rank o
+// owns rows [o*R, (o+1)*R) (R = rs_rows, a multiple of 8).  The chain is
+//
+//   GEMM + reduce-scatter   (gemm_tcgen05, kEpiPeerRS): each finished tile row
+//                            is stored into its owner's slot for this rank;
+//   rs_norm_ag (this file)   the owner sums the world slots of its rows in
+//                            fp32, adds its residual shard (kept in bf16 like
+//                            the unfused path), RMS-normalises, and stores the
+//                            normalised rows into EVERY rank's gather buffer;
+//   GEMM on gathered rows    (gemm_tcgen05 with ag_flag): the TMA producer
+//                            waits for the all-gather flags of each A tile's
+//                            rows before loading it from LOCAL memory.
+//
+// Synchronisation is by flags carrying an epoch (step counter * 256 + call
+// index + 1) stored with st.release.sys and polled with ld.acquire.sys, so no
+// flag is ever reset and CUDA-graph replays stay correct; the step counter is
+// bumped by `tp_epoch_bump` once per forward.  Buffer reuse needs no extra
+// barrier: a rank writes a slot / gather row for call c+1 only after it
+// consumed every owner's gather rows of call c, which those owners produced
+// after reading their slots of call c.  Every wait is bounded
+// (kWaitTimeoutNs); on expiry the status word records kCommPeerTimeout and the
+// kernel finishes without blocking.
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "gemm_bf16.h"
+#include "tp_fused.h"
+
+namespace rz {
+
+__device__ __forceinline__ void ld8f(const __nv_bfloat16* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8f(const float* v) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  return u;
+}
+
+// 8 warps per block, one own row per warp; block b covers rows [row0 + 8b, row0 + 8b + 8)
+__global__ void __launch_bounds__(256) rs_norm_ag_kernel(RsNormAgParams p) {
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u;
+  const int own0 = p.rank * p.rs_rows;
+  const int g0 = own0 + blockIdx.x * kAgRowBlock;          // first global row of this block
+  if (p.reduce) {
+    // tiles of quarter (g0 % 128) / 32 of m-tile g0 / 128, every n tile, every source rank
+    const int mt = g0 / 128, q = (g0 % 128) / 32;
+    const int nflags = p.n_tiles * p.world;
+    bool ok = true;
+    for (int f = threadIdx.x; f < nflags && ok; f += blockDim.x) {
+      const int nt = f / p.world, src = f % p.world;
+      ok = wait_flag_geq(p.rs_flag + ((static_cast<size_t>(mt) * p.n_tiles + nt) * 4 + q) * p.world + src, epoch,
+                         p.status, kCommPeerTimeout);
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = g0 + warp;                                 // global row
+  const int li = row - own0;                                 // row within this rank's shard
+  if (row < p.M && li < p.rs_rows) {
+    __nv_bfloat16* res = p.residual + static_cast<size_t>(li) * p.H;
+    float ss = 0.f;
+    for (int c = lane * 8; c < p.H; c += 256) {
+      float x[8], t[8];
+      if (p.reduce) {
+        ld8f(res + c, x);
+        for (int s = 0; s < p.world; ++s) {
+          ld8f(p.slots + (static_cast<size_t>(s) * p.rs_rows + li) * p.H + c, t);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] += t[i];
+        }
+      } else {
+        ld8f(p.resid_in + static_cast<size_t>(row) * p.H + c, x);
+      }
+      const uint4 r = pack8f(x);
+      *reinterpret_cast<uint4*>(res + c) = r;
+      ld8f(res + c, x);                                      // normalise the rounded residual
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / p.H + p.eps);
+    for (int c = lane * 8; c < p.H; c += 256) {
+      float x[8], w[8];
+      ld8f(res + c, x);
+      ld8f(p.w + c, w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = x[i] * inv * (w[i] + p.offset);
+      const uint4 o = pack8f(x);
+      for (int d = 0; d < p.world; ++d)
+        *reinterpret_cast<uint4*>(p.gather[d] + static_cast<size_t>(row) * p.H + c) = o;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < p.world && g0 < p.M) st_release_sys_u32(p.ag_flag[threadIdx.x] + g0 / kAgRowBlock, epoch);
+}
+
+__global__ void tp_epoch_bump_kernel(uint32_t* ep) { *ep += 1u; }
+
+int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st) {
+  if (p.rs_rows % kAgRowBlock != 0 || p.H % 256 != 0 || p.world > kMaxTpRanks) return -1;
+  const int own = min(p.M, (p.rank + 1) * p.rs_rows) - p.rank * p.rs_rows;
+  if (own <= 0) return 0;
+  rs_norm_ag_kernel<<<(own + kAgRowBlock - 1) / kAgRowBlock, 256, 0, st>>>(p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tp_epoch_bump_launch(uint32_t* ep, cudaStream_t st) {
+  tp_epoch_bump_kernel<<<1, 1, 0, st>>>(ep);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace rz

@@ -222,6 +222,8 @@ class DecoderLM(nn.Module):
     # ------------------------------------------------------------------ forward
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, meta: AttentionMetadata,
                 kv_caches: List[torch.Tensor]) -> torch.Tensor:
+        if self._fused_tp_ok(input_ids.shape[0]):
+            return self._forward_fused_tp(input_ids, positions, meta, kv_caches)
         cfg = self.cfg
         eps, off = cfg.rms_norm_eps, cfg.norm_offset
         D = cfg.head_dim
@@ -250,6 +252,49 @@ class DecoderLM(nn.Module):
             h = self._moe(L, x) if cfg.is_moe else self._mlp(L, x)
         h, _ = ops.fused_add_rms_norm(h, residual, self.norm, eps, off)
         return h
+
+    def _fused_tp_ok(self, M: int) -> bool:
+        F = getattr(self.tp, "fused_tp", None)
+        if F is None or self.tp.size == 1 or not F.fits(M) or self.device.type != "cuda":
+            return False
+        if self.cfg.is_moe or self.is_gemma2 or self.act != "silu" or getattr(self, "fp8", False):
+            return False
+        return all(getattr(L, "gate_up_il", None) is not None for L in self.layers)
+
+    def _forward_fused_tp(self, input_ids: torch.Tensor, positions: torch.Tensor, meta: AttentionMetadata,
+                          kv_caches: List[torch.Tensor]) -> torch.Tensor:
+        """Tensor-parallel forward with the collectives fused into the layer
+        boundaries: the residual stream is sequence-sharded between layers;
+        o_proj / down_proj reduce-scatter from their GEMM epilogues, the owner
+        adds its residual, RMS-normalises and all-gathers, and QKV / gate-up
+        start per tile as the gathered rows land (parallel.fused_tp).  Call
+        index c of a boundary: 0 = embedding, 2l+1 = after o_proj of layer l,
+        2l+2 = after down_proj of layer l.  Returns the final normalised hidden
+        states (replicated)."""
+        F = self.tp.fused_tp
+        cfg = self.cfg
+        eps, off = cfg.rms_norm_eps, cfg.norm_offset
+        D = cfg.head_dim
+        h = self.embed_tokens(input_ids)
+        M = h.shape[0]
+        x = F.start(h, self.layers[0].input_norm, eps, off)
+        n = len(self.layers)
+        for li, L in enumerate(self.layers):
+            kv = kv_caches[li]
+            c_attn, c_mlp = 2 * li + 1, 2 * li + 2
+            qkv = F.gemm_ag(x, L.qkv, 2 * li, L.qkv_bias)
+            q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
+                                   self.hq, self.hkv, D)
+            a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
+                                    cfg.attn_logit_softcapping)
+            F.gemm_rs(a.view(M, -1), L.o, c_attn)
+            x = F.rs_norm_ag(M, L.post_attn_norm, eps, off, c_attn)
+            act = F.gemm_ag(x, L.gate_up_il, c_attn, silu_mul=True)
+            F.gemm_rs(act, L.down, c_mlp)
+            nw = self.layers[li + 1].input_norm if li + 1 < n else self.norm
+            x = F.rs_norm_ag(M, nw, eps, off, c_mlp)
+        F.end_step()
+        return x
 
     def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
         """h [n, H] -> fp32 logits [n, vocab] (gathered over TP ranks)."""

@@ -8,9 +8,12 @@ Here `TPComm` is the real thing:
 
   * mode "nccl":  torch.distributed collectives (NCCL on GPUs, gloo on CPU
                   ranks for tests) -- the baseline.
-  * mode "fused": the peer-memory kernels of `parallel.comm` (one-shot /
-                  two-shot all-reduce over NVLink P2P, GEMM epilogues that
-                  store straight into peers' buffers).
+  * mode "fused": the peer-memory kernels: one-shot / two-shot all-reduce
+                  over NVLink P2P (`parallel.comm`) and, for dense models,
+                  layer boundaries fused with their collectives
+                  (`parallel.fused_tp`: GEMM epilogues that reduce-scatter
+                  straight into the owners' buffers, add+RMSNorm+all-gather,
+                  GEMMs that start on gathered tiles as they land).
 
 Every process group is created with a short timeout so that a dead rank
 turns into an error on the survivors instead of a hang.
@@ -68,9 +71,14 @@ class TPComm(TPGroup):
         self.mode = mode
         self.device = device
         self.fused = None
+        self.fused_tp = None
         if mode == "fused" and size > 1 and device is not None and torch.device(device).type == "cuda":
             from rusteeze_b200.parallel.comm import PeerAllReduce
+            from rusteeze_b200.parallel.fused_tp import FusedTP
             self.fused = PeerAllReduce(group, rank, size, torch.device(device), max_tokens * hidden)
+            if hidden % 256 == 0:
+                # layer boundaries: GEMM + reduce-scatter -> add + RMSNorm + all-gather -> GEMM
+                self.fused_tp = FusedTP(group, rank, size, torch.device(device), max_tokens, hidden)
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.size == 1:

@@ -1,0 +1,121 @@
+"""Tensor-parallel layer boundaries fused with their collectives.
+
+Megatron-style TP normally ends every row-parallel GEMM (o_proj, down_proj)
+with an all-reduce and then runs residual-add + RMSNorm on every rank.  Here
+the residual stream between layers is sequence-sharded (rank o owns rows
+[o*R, (o+1)*R), R = rs_rows) and the collective is folded into the kernels
+around it (csrc/kernels/tp_fused.cu, gemm_bf16.cu):
+
+  gemm_rs      row-parallel GEMM; its epilogue stores every finished tile row
+               into the owner's slot buffer over NVLink (reduce-scatter);
+  rs_norm_ag   the owner sums its slots in fp32, adds its residual shard,
+               RMS-normalises and stores the rows into every rank's gather
+               buffer (all-gather);
+  gemm_ag      the next column-parallel GEMM reads the gathered rows from
+               LOCAL memory; its TMA producer waits per A tile for the rows'
+               all-gather flags, so it starts as soon as its rows landed.
+
+One symmetric allocation per rank (torch symmetric memory) holds
+[rs flags | ag flags | slots | gather]; peers' bases come from the
+rendezvous.  The reference has no collective at all
+(crates/rusteeze-engine/src/tensor_parallel.rs:80-106).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from rusteeze_b200 import ops
+
+_ALIGN = 1024
+
+
+def _up(x: int, a: int) -> int:
+    return (x + a - 1) // a * a
+
+
+class FusedTP:
+    def __init__(self, group, rank: int, world: int, device: torch.device, max_tokens: int, hidden: int):
+        import torch.distributed._symmetric_memory as symm
+        self.group = group or dist.group.WORLD
+        self.rank, self.world, self.device, self.hidden = rank, world, device, hidden
+        self.max_tokens = max_tokens
+        self.max_rs_rows = _up(-(-max_tokens // world), 8)
+        self.max_m_tiles = -(-max_tokens // 128) + 1
+        self.max_n_tiles = -(-hidden // 64)          # n tiles of a row-parallel output at the smallest tile
+        n_rs_flags = self.max_m_tiles * self.max_n_tiles * 4 * world
+        n_ag_flags = -(-max_tokens // 8) + 16
+        self.off_rs_flag = 0
+        self.off_ag_flag = _up(self.off_rs_flag + 4 * n_rs_flags, _ALIGN)
+        self.off_slots = _up(self.off_ag_flag + 4 * n_ag_flags, _ALIGN)
+        self.off_gather = _up(self.off_slots + 2 * world * self.max_rs_rows * hidden, _ALIGN)
+        total = _up(self.off_gather + 2 * (max_tokens + 128) * hidden, _ALIGN)
+        try:
+            symm.enable_symm_mem_for_group(self.group.group_name)
+        except Exception:  # noqa: BLE001 -- newer torch enables it implicitly
+            pass
+        self.buf = symm.empty(total, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        torch.cuda.synchronize(device)
+        self.handle = symm.rendezvous(self.buf, self.group)
+        bases = [int(p) for p in self.handle.buffer_ptrs]
+        self.slot_ptrs = [b + self.off_slots for b in bases]
+        self.rs_flag_ptrs = [b + self.off_rs_flag for b in bases]
+        self.gather_ptrs = [b + self.off_gather for b in bases]
+        self.ag_flag_ptrs = [b + self.off_ag_flag for b in bases]
+        u8 = self.buf
+        self.rs_flag = u8[self.off_rs_flag:self.off_rs_flag + 4 * n_rs_flags].view(torch.int32)
+        self.ag_flag = u8[self.off_ag_flag:self.off_ag_flag + 4 * n_ag_flags].view(torch.int32)
+        self.slots = u8[self.off_slots:self.off_slots + 2 * world * self.max_rs_rows * hidden].view(torch.bfloat16)
+        self.gather = u8[self.off_gather:self.off_gather + 2 * (max_tokens + 128) * hidden].view(
+            torch.bfloat16).view(max_tokens + 128, hidden)
+        self.residual = torch.empty(self.max_rs_rows, hidden, dtype=torch.bfloat16, device=device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.n_tiles = 1
+        dist.barrier(group=self.group)
+
+    # ------------------------------------------------------------------ shapes
+    def rs_rows(self, M: int) -> int:
+        return _up(-(-M // self.world), 8)
+
+    def fits(self, M: int) -> bool:
+        return 0 < M <= self.max_tokens
+
+    # ------------------------------------------------------------------ ops
+    def start(self, h: torch.Tensor, norm_w: torch.Tensor, eps: float, offset: float) -> torch.Tensor:
+        """First boundary: x = h (replicated rows), residual shard = own rows,
+        normalised rows all-gathered.  Returns the gathered [M, H] view."""
+        M = h.shape[0]
+        C = ops.cuda_ext()
+        C.rs_norm_ag(self.slots, self.rs_flag, 1, h.contiguous(), self.residual, norm_w, eps, offset,
+                     self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch, 0)
+        ops.add_launches(1)
+        return self.gather[:M]
+
+    def gemm_rs(self, x: torch.Tensor, w: torch.Tensor, call_idx: int) -> None:
+        M = x.shape[0]
+        self.n_tiles = int(ops.cuda_ext().gemm_peer_rs(x.contiguous(), w, self.slot_ptrs, self.rs_flag_ptrs,
+                                                       self.rank, self.rs_rows(M), self.epoch, call_idx, 0))
+        ops.add_launches(1)
+
+    def rs_norm_ag(self, M: int, norm_w: torch.Tensor, eps: float, offset: float, call_idx: int) -> torch.Tensor:
+        ops.cuda_ext().rs_norm_ag(self.slots, self.rs_flag, self.n_tiles, None, self.residual, norm_w, eps, offset,
+                                  self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch,
+                                  call_idx)
+        ops.add_launches(1)
+        return self.gather[:M]
+
+    def gemm_ag(self, g: torch.Tensor, w: torch.Tensor, call_idx: int, bias: Optional[torch.Tensor] = None,
+                silu_mul: bool = False) -> torch.Tensor:
+        M = g.shape[0]
+        n_out = w.shape[0] // 2 if silu_mul else w.shape[0]
+        out = torch.empty(M, n_out, dtype=torch.bfloat16, device=g.device)
+        ops.add_launches(ops.cuda_ext().gemm_ag(out, g, w, bias, 1 if silu_mul else 0, self.ag_flag, self.epoch,
+                                                call_idx))
+        return out
+
+    def end_step(self) -> None:
+        ops.cuda_ext().tp_epoch_bump(self.epoch)
+        ops.add_launches(1)

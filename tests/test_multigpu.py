@@ -64,6 +64,64 @@ def test_peer_all_reduce_matches_nccl():
         assert err < 2e-2, f"rank {rank} rel err {err}"
 
 
+def _boundary_worker(rank, world, port, q):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from rusteeze_b200 import ops
+    from rusteeze_b200.parallel.dist import init_distributed
+    from rusteeze_b200.parallel.fused_tp import FusedTP
+    info = init_distributed(timeout_s=60)
+    try:
+        H, K = 1024, 512
+        F = FusedTP(dist.group.WORLD, rank, world, info.device, 2048, H)
+        errs = []
+        for step, M in enumerate((1, 37, 300, 1000)):
+            torch.manual_seed(step)                                  # same full tensors on every rank
+            h0 = torch.randn(M, H, device=info.device, dtype=torch.bfloat16)
+            xs = [torch.randn(M, K, device=info.device, dtype=torch.bfloat16) for _ in range(world)]
+            ws = [(torch.randn(H, K, device=info.device) * 0.05).to(torch.bfloat16) for _ in range(world)]
+            wn = (1 + 0.1 * torch.randn(H, device=info.device)).to(torch.bfloat16)
+            wq = (torch.randn(256, H, device=info.device) * 0.05).to(torch.bfloat16)
+            g = F.start(h0, wn, 1e-5, 0.0)                           # boundary 0: x = h0
+            F.gemm_rs(xs[rank], ws[rank], 1)                          # partial o_proj
+            g = F.rs_norm_ag(M, wn, 1e-5, 0.0, 1)
+            y = F.gemm_ag(g, wq, 1)                                   # consumer GEMM on gathered rows
+            F.end_step()
+            torch.cuda.synchronize()
+            part = sum(xs[r].float() @ ws[r].float().t() for r in range(world)).to(torch.bfloat16).float()
+            res = (h0.float() + part).to(torch.bfloat16).float()
+            want = res * torch.rsqrt(res.pow(2).mean(-1, keepdim=True) + 1e-5) * wn.float()
+            errs.append(((g.float() - want).norm() / want.norm()).item())
+            errs.append(((y.float() - want @ wq.float().t()).norm() / (want @ wq.float().t()).norm()).item())
+        q.put((rank, max(errs), int(ops.cuda_ext().status()[0])))
+    except BaseException as e:  # noqa: BLE001
+        q.put((rank, repr(e), -1))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_fused_tp_boundary_matches_reference():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 4)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_boundary_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(world)]
+    for p in ps:
+        p.join(60)
+    for rank, err, status in res:
+        assert status == 0, f"rank {rank} status {status}: {err}"
+        assert err < 2e-2, f"rank {rank} rel err {err}"
+
+
 @pytest.mark.timeout(600)
 @pytest.mark.parametrize("backend", ["nccl", "fused"])
 def test_tp2_engine_matches_tp1(backend):
