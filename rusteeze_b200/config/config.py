@@ -134,6 +134,7 @@ class EngineSection:
     enable_prefix_caching: bool = False
     enable_chunked_prefill: bool = False
     enforce_eager: bool = False               # disable CUDA graphs
+    async_scheduling: bool = True             # overlap host scheduling / output processing with the GPU step
     cuda_graph_max_batch: Optional[int] = None
     comm_backend: str = "fused"               # nccl | fused (peer-memory kernels)
     request_timeout_seconds: float = 600.0

@@ -32,7 +32,7 @@ from rusteeze_b200.core.sampling_params import SamplingParams
 from rusteeze_b200.core.types import RequestStatus, new_request_id
 from rusteeze_b200.engine.block_manager import make_block_manager
 from rusteeze_b200.engine.model_runner import ModelRunner
-from rusteeze_b200.engine.sampler import SampleRow
+from rusteeze_b200.engine.sampler import SampleRow, Sampler
 from rusteeze_b200.engine.scheduler import (PreemptionMode, Scheduler, SchedulerConfig,
                                             SchedulingPolicy)
 from rusteeze_b200.engine.sequence import Request, Sequence
@@ -43,6 +43,14 @@ from rusteeze_b200.ops import BLOCK_SIZE
 from rusteeze_b200.metrics.logging_setup import nvtx_range
 
 log = logging.getLogger("rusteeze.engine")
+
+
+class _InFlight:
+    """A launched step whose sampled tokens are still on the GPU."""
+    __slots__ = ("so", "handle", "owners", "rows_of", "t_launch")
+
+    def __init__(self, so, handle, owners, rows_of, t_launch):
+        self.so, self.handle, self.owners, self.rows_of, self.t_launch = so, handle, owners, rows_of, t_launch
 
 
 def _dtype(name: str, device: str) -> torch.dtype:
@@ -124,6 +132,11 @@ class LLMEngine:
                                "requests_finished": 0, "requests_aborted": 0}
         self.observers: List[Callable] = []
         self.phase_s: Dict[str, float] = {"schedule": 0.0, "postprocess": 0.0}
+        # asynchronous scheduling: single-process CUDA engine without speculation
+        self._async = (ec.async_scheduling and self.device.startswith("cuda") and spec is None
+                       and hasattr(self.runner, "launch") and executor is None)
+        self._inflight: List[_InFlight] = []
+        self._n_sync_only = 0
         self.spec = None
         if spec is not None:
             from rusteeze_b200.engine.spec_decode import SpecDecoder
@@ -178,6 +191,9 @@ class LLMEngine:
         for s in req.seqs:
             self._register_seq(req, s)
             self.scheduler.add(s)
+        req.async_ok = (Sampler.async_eligible(params) and params.n == 1 and params.best_of == 1)
+        if not req.async_ok:
+            self._n_sync_only += 1
         self.requests[rid] = req
         return req
 
@@ -201,7 +217,7 @@ class LLMEngine:
         return True
 
     def has_unfinished_requests(self) -> bool:
-        return self.scheduler.has_unfinished()
+        return self.scheduler.has_unfinished() or bool(self._inflight)
 
     def get_num_unfinished_requests(self) -> int:
         return len(self.requests)
@@ -210,6 +226,11 @@ class LLMEngine:
     def step(self) -> List[RequestOutput]:
         if self.spec is not None:
             return self.spec.step()
+        if self._async:
+            if self._n_sync_only == 0:
+                return self._step_async()
+            if self._inflight:          # a request needs host-side sampling state: drain, then go synchronous
+                return self._drain_inflight()
         h0 = time.perf_counter()
         with nvtx_range("rz.step.schedule"):
             so = self.scheduler.schedule()
@@ -244,6 +265,95 @@ class LLMEngine:
         d.update(getattr(self.runner, "phase_s", {}))
         return d
 
+    # ------------------------------------------------------------------ asynchronous scheduling
+    def _step_async(self) -> List[RequestOutput]:
+        """One pipelined step: schedule and enqueue step n+1 (decode inputs of
+        sequences whose step-n token is still on the GPU are scattered from
+        step n's sample tensor on the device), then wait for step n and apply
+        its tokens while the GPU runs n+1.  Outputs lag one step; stop
+        conditions found in step n's tokens discard the sequence's token of
+        step n+1 (its KV write lands in blocks that are only reused by later
+        steps, which the stream orders after it)."""
+        h0 = time.perf_counter()
+        with nvtx_range("rz.step.schedule"):
+            so = self.scheduler.schedule()
+        launched = False
+        if not so.is_empty():
+            prev = self._inflight[-1] if self._inflight else None
+            for ss in so.scheduled:
+                if ss.seq.pending:
+                    ss.pend_row = prev.rows_of[ss.seq.seq_id]
+            rows, owners = self._sample_rows(so)
+            h1 = time.perf_counter()
+            self.phase_s["schedule"] += h1 - h0
+            with nvtx_range("rz.step.launch"):
+                handle = self.runner.launch(so, self.bm, rows, prev.handle.tokens if prev is not None else None)
+            rows_of: Dict[int, int] = {}
+            i = 0
+            for ss, k in owners:
+                rows_of[ss.seq.seq_id] = i
+                i += k
+            for ss in so.scheduled:
+                s = ss.seq
+                if s.num_generated == 0 and s.pending == 0:
+                    self.stats_counters["prompt_tokens"] += ss.num_new
+                s.num_computed = ss.ctx + ss.num_new
+                if ss.sample:
+                    s.pending += 1
+            self._inflight.append(_InFlight(so, handle, owners, rows_of, time.monotonic()))
+            self.stats_counters["steps"] += 1
+            launched = True
+        outputs: List[RequestOutput] = []
+        if len(self._inflight) > (1 if launched else 0):
+            outputs = self._finish_oldest()
+        return outputs + self._collect_ignored()
+
+    def _finish_oldest(self) -> List[RequestOutput]:
+        done = self._inflight.pop(0)
+        res = self.runner.finish(done.handle)
+        h2 = time.perf_counter()
+        now = time.monotonic()
+        touched, seen = [], set()
+        i = 0
+        for ss, k in done.owners:
+            s = ss.seq
+            req = s.request
+            tok, lp = res.tokens[i], res.logprobs[i]
+            i += k
+            s.pending -= 1
+            if s.is_finished() or req.request_id not in self.requests:
+                continue                  # finished or aborted after this step was launched
+            s.append_token(tok, None)
+            if req.metrics.first_token_time is None:
+                req.metrics.first_token_time = now
+            req.metrics.last_token_time = now
+            req.metrics.num_generated = max(req.metrics.num_generated, s.num_generated)
+            self.stats_counters["generation_tokens"] += 1
+            self._check_stop(s, tok)
+            if id(req) not in seen:
+                seen.add(id(req))
+                touched.append(req)
+        # publish the now-known full blocks to the prefix cache
+        for ss in done.so.scheduled:
+            s = ss.seq
+            if not s.is_finished() and self.bm.has_seq(s.seq_id):
+                self.bm.commit(s.seq_id, s.tokens_np(), min(s.num_computed, len(s.token_ids)))
+        for obs in self.observers:
+            obs(self, done.so, now - done.t_launch)
+        outputs = []
+        for req in touched:
+            outputs.append(req.to_output(delta=True))
+            if req.is_finished():
+                self._retire(req)
+        self.phase_s["postprocess"] += time.perf_counter() - h2
+        return outputs
+
+    def _drain_inflight(self) -> List[RequestOutput]:
+        outs: List[RequestOutput] = []
+        while self._inflight:
+            outs += self._finish_oldest()
+        return outs + self._collect_ignored()
+
     def _collect_ignored(self) -> List[RequestOutput]:
         outs = []
         if not self.scheduler.ignored:
@@ -271,7 +381,7 @@ class LLMEngine:
             output_ids = s.output_token_ids if (pen or p.min_tokens > s.num_generated) else ()
             for j in range(ss.num_samples):
                 rows.append(SampleRow(p, prompt_ids, output_ids,
-                                      seed=req.seed + 7919 * (s.index + j), offset=s.num_generated,
+                                      seed=req.seed + 7919 * (s.index + j), offset=s.num_generated + s.pending,
                                       eos_ids=self.eos_ids, mirostat_mu=s.mirostat_mu))
             owners.append((ss, ss.num_samples))
         return rows, owners
@@ -344,7 +454,7 @@ class LLMEngine:
                         s.stop_reason = st
                         break
         if reason is None and ((p.max_tokens is not None and n >= p.max_tokens)
-                               or s.total_len >= self.max_model_len):
+                               or len(s.token_ids) >= self.max_model_len):
             reason = "length"
         if reason is not None:
             s.finish_reason = reason
@@ -355,6 +465,8 @@ class LLMEngine:
     def _retire(self, req: Request) -> None:
         import time as _t
         if req.request_id in self.requests:
+            if not getattr(req, "async_ok", True):
+                self._n_sync_only -= 1
             req.metrics.finished_time = _t.monotonic()
             del self.requests[req.request_id]
             for s in req.seqs:

@@ -34,6 +34,8 @@ from rusteeze_b200.engine.scheduler import SchedulerOutput
 from rusteeze_b200.models.decoder import AttentionMetadata, DecoderLM
 from rusteeze_b200.ops import BLOCK_SIZE
 
+_ZERO1 = np.zeros(1, dtype=np.int64)
+
 NUM_SMS_B200 = 148
 
 
@@ -94,15 +96,12 @@ class ModelRunner:
                                          pin_memory=self.is_cuda)
         pin = self.is_cuda
         T, S, MB = self.max_tokens, max_num_seqs, self.max_blocks
-        self.h_input_ids = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
-        self.h_positions = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
-        self.h_slots = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
-        self.h_qsl = torch.zeros(S + 1, dtype=torch.int32, pin_memory=pin)
-        self.h_seq_lens = torch.zeros(S, dtype=torch.int32, pin_memory=pin)
-        self.h_block_tables = torch.zeros(S, MB, dtype=torch.int32, pin_memory=pin)
-        self.h_logits_idx = torch.zeros(T, dtype=torch.int64, pin_memory=pin)
-        self.h_logits_idx_np = self.h_logits_idx.numpy()
-        self.h_seq_lens_np = self.h_seq_lens.numpy()
+        # two sets of pinned staging buffers, alternated per step: with
+        # asynchronous scheduling the next step is prepared while the previous
+        # step's host->device copies may still be queued behind the GPU
+        self._host_sets = [self._alloc_host(T, S, MB, pin) for _ in range(2)]
+        self._host_k = 0
+        self._bind_host(0)
         dev = self.device
         self.d_input_ids = torch.zeros(T, dtype=torch.int64, device=dev)
         self.d_positions = torch.zeros(T, dtype=torch.int64, device=dev)
@@ -123,13 +122,37 @@ class ModelRunner:
         self.phase_s: Dict[str, float] = {"prepare": 0.0, "enqueue": 0.0, "sample_wait": 0.0}
         self.d2h_bytes = 0      # device->host bytes read back (cumulative)
 
+    @staticmethod
+    def _alloc_host(T: int, S: int, MB: int, pin: bool) -> Dict[str, torch.Tensor]:
+        return {"h_input_ids": torch.zeros(T, dtype=torch.int64, pin_memory=pin),
+                "h_positions": torch.zeros(T, dtype=torch.int64, pin_memory=pin),
+                "h_slots": torch.zeros(T, dtype=torch.int64, pin_memory=pin),
+                "h_qsl": torch.zeros(S + 1, dtype=torch.int32, pin_memory=pin),
+                "h_seq_lens": torch.zeros(S, dtype=torch.int32, pin_memory=pin),
+                "h_block_tables": torch.zeros(S, MB, dtype=torch.int32, pin_memory=pin),
+                "h_logits_idx": torch.zeros(T, dtype=torch.int64, pin_memory=pin),
+                "h_sample_idx": torch.zeros(T, dtype=torch.int64, pin_memory=pin),
+                "h_pend": torch.zeros(2, S, dtype=torch.int64, pin_memory=pin)}
+
+    def _bind_host(self, k: int) -> None:
+        for name, t in self._host_sets[k].items():
+            setattr(self, name, t)
+        self.h_logits_idx_np = self.h_logits_idx.numpy()
+        self.h_seq_lens_np = self.h_seq_lens.numpy()
+
+    def _flip_host(self) -> None:
+        self._host_k ^= 1
+        self._bind_host(self._host_k)
+
     # ------------------------------------------------------------------ cache ops
     @torch.no_grad()
     def copy_blocks(self, pairs: List[Tuple[int, int]]) -> None:
         if not pairs:
             return
-        src = torch.tensor([p[0] for p in pairs], dtype=torch.long, device=self.device)
-        dst = torch.tensor([p[1] for p in pairs], dtype=torch.long, device=self.device)
+        src = torch.tensor([p[0] for p in pairs], dtype=torch.long, pin_memory=self.is_cuda).to(
+            self.device, non_blocking=True)
+        dst = torch.tensor([p[1] for p in pairs], dtype=torch.long, pin_memory=self.is_cuda).to(
+            self.device, non_blocking=True)
         self.kv_cache.index_copy_(0, dst, self.kv_cache.index_select(0, src))
 
     @torch.no_grad()
@@ -143,14 +166,34 @@ class ModelRunner:
             self.kv_cache[g].copy_(self.cpu_cache[c], non_blocking=True)
 
     # ------------------------------------------------------------------ batch prep
-    def prepare(self, so: SchedulerOutput, bm) -> Tuple[AttentionMetadata, int, int, List[int]]:
+    def prepare(self, so: SchedulerOutput, bm,
+                prev_tokens: Optional[torch.Tensor] = None) -> Tuple[AttentionMetadata, int, int, List[int]]:
+        """Builds the step's batch.  With asynchronous scheduling a decode
+        whose input token is still on the device (ScheduledSeq.pend_row >= 0)
+        gets a placeholder here and is filled from `prev_tokens` (the previous
+        step's sampled ids) by a device-side scatter after the copies."""
+        self._flip_host()
         sched = so.scheduled
         S = len(sched)
         seq_ids = np.fromiter((s.seq.seq_id for s in sched), dtype=np.int64, count=S)
         ctx = np.fromiter((s.ctx for s in sched), dtype=np.int64, count=S)
         n_new = np.fromiter((s.num_new for s in sched), dtype=np.int64, count=S)
-        toks = np.concatenate([s.seq.tokens_np()[s.ctx:s.ctx + s.num_new] for s in sched]) if S else \
-            np.zeros(0, dtype=np.int64)
+        pend_dst: List[int] = []
+        pend_src: List[int] = []
+        if S:
+            parts = []
+            off = 0
+            for s in sched:
+                if s.pend_row >= 0:
+                    pend_dst.append(off)
+                    pend_src.append(s.pend_row)
+                    parts.append(_ZERO1)
+                else:
+                    parts.append(s.seq.tokens_np()[s.ctx:s.ctx + s.num_new])
+                off += s.num_new
+            toks = np.concatenate(parts)
+        else:
+            toks = np.zeros(0, dtype=np.int64)
         T = bm.build_batch(seq_ids, ctx, n_new, toks, self.h_input_ids.data_ptr(),
                            self.h_positions.data_ptr(), self.h_slots.data_ptr(), self.h_qsl.data_ptr(),
                            self.h_seq_lens.data_ptr(), self.h_block_tables.data_ptr(),
@@ -173,6 +216,16 @@ class ModelRunner:
         self.d_qsl[:S + 1].copy_(self.h_qsl[:S + 1], non_blocking=nb)
         self.d_seq_lens[:S].copy_(self.h_seq_lens[:S], non_blocking=nb)
         self.d_block_tables[:S].copy_(self.h_block_tables[:S], non_blocking=non_blocking)
+        if pend_dst:
+            if prev_tokens is None:
+                raise RuntimeError("pending decode input without the previous step's samples")
+            P = len(pend_dst)
+            hp = self.h_pend
+            hp[0, :P] = torch.from_numpy(np.asarray(pend_dst, dtype=np.int64))
+            hp[1, :P] = torch.from_numpy(np.asarray(pend_src, dtype=np.int64))
+            dp = hp[:, :P].to(self.device, non_blocking=nb)
+            self.d_input_ids.index_copy_(0, dp[0], prev_tokens.index_select(0, dp[1]))
+            self.h2d_bytes += 16 * P
         meta = AttentionMetadata(
             num_seqs=S, num_tokens=T, num_decode_seqs=nd, query_start_loc=self.d_qsl[:S + 1],
             seq_lens=self.d_seq_lens[:S], block_tables=self.d_block_tables[:S],
@@ -193,6 +246,7 @@ class ModelRunner:
         sequence i gets n_new[i] tokens at positions ctx[i].., and the logits
         of its last `logits_per_seq` tokens are returned in sequence order."""
         S = len(seq_ids)
+        self._flip_host()
         T = bm.build_batch(np.asarray(seq_ids, dtype=np.int64), np.asarray(ctx, dtype=np.int64),
                            np.asarray(n_new, dtype=np.int64), np.asarray(toks, dtype=np.int64),
                            self.h_input_ids.data_ptr(), self.h_positions.data_ptr(), self.h_slots.data_ptr(),
@@ -272,6 +326,36 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ execute
     @torch.no_grad()
+    # ------------------------------------------------------------------ asynchronous steps
+    @torch.no_grad()
+    def launch(self, so: SchedulerOutput, bm, rows: List[SampleRow], prev_tokens: Optional[torch.Tensor]):
+        """Enqueues a whole step (copies, forward, sampling, result readback)
+        without waiting for the GPU; `finish` returns its SampleResult."""
+        if so.blocks_to_swap_out:
+            self.swap_out(so.blocks_to_swap_out)
+        if so.blocks_to_swap_in:
+            self.swap_in(so.blocks_to_swap_in)
+        if so.blocks_to_copy:
+            self.copy_blocks(so.blocks_to_copy)
+        t0 = time.perf_counter()
+        meta, T, S, sample_rows = self.prepare(so, bm, prev_tokens)
+        t1 = time.perf_counter()
+        logits = self.forward_logits(meta, T, S, sample_rows, pure_decode=not so.prefills)
+        t2 = time.perf_counter()
+        handle = self.sampler.launch(logits, rows)
+        ph = self.phase_s
+        ph["prepare"] += t1 - t0
+        ph["enqueue"] += time.perf_counter() - t1
+        self.h2d_bytes += self.sampler.last_h2d_bytes
+        return handle
+
+    def finish(self, handle) -> SampleResult:
+        t0 = time.perf_counter()
+        res = self.sampler.finish(handle)
+        self.phase_s["sample_wait"] += time.perf_counter() - t0
+        self.d2h_bytes += self.sampler.last_d2h_bytes
+        return res
+
     def execute(self, so: SchedulerOutput, bm, rows: List[SampleRow]) -> SampleResult:
         if so.blocks_to_swap_out:
             self.swap_out(so.blocks_to_swap_out)
@@ -308,9 +392,13 @@ class ModelRunner:
             g.replay()
             from rusteeze_b200 import ops as _ops
             _ops.add_launches(self.graph_launches.get(B, 0))
-            idx = torch.tensor(sample_rows, dtype=torch.long)
-            return out.index_select(0, idx.to(out.device, non_blocking=True))
+            return out.index_select(0, self._sample_index(sample_rows))
         h = self.model(self.d_input_ids[:T], self.d_positions[:T], meta, self.kv_layers)
-        idx = torch.tensor(sample_rows, dtype=torch.long, pin_memory=self.is_cuda)
-        hs = h.index_select(0, idx.to(h.device, non_blocking=True))
+        hs = h.index_select(0, self._sample_index(sample_rows))
         return self.model.compute_logits(hs)
+
+    def _sample_index(self, sample_rows: List[int]) -> torch.Tensor:
+        n = len(sample_rows)
+        hi = self.h_sample_idx[:n]
+        hi.copy_(torch.from_numpy(np.asarray(sample_rows, dtype=np.int64)))
+        return hi.to(self.device, non_blocking=self.is_cuda)

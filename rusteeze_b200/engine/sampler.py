@@ -23,6 +23,7 @@ import math
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence as Seq, Tuple
 
+import numpy as np
 import torch
 
 from rusteeze_b200 import ops
@@ -41,6 +42,14 @@ class SampleRow:
     offset: int
     eos_ids: Tuple[int, ...] = ()
     mirostat_mu: Optional[float] = None
+
+
+@dataclass
+class AsyncSample:
+    tokens: torch.Tensor          # device int64 [R]: next step's pending input ids
+    host: torch.Tensor            # pinned [2, >=R] float64: token ids, logprobs
+    rows: int
+    event: "torch.cuda.Event"
 
 
 @dataclass
@@ -90,6 +99,68 @@ class Sampler:
                 if stop:
                     logits[i, torch.tensor(stop, device=logits.device)] = _MASK
         return logits
+
+    # ------------------------------------------------------------------ asynchronous entry
+    @staticmethod
+    def async_eligible(params: SamplingParams) -> bool:
+        """Rows whose sampling runs entirely in the GPU kernel with nothing to
+        read back but (token, logprob): no penalties / logit bias / min_tokens
+        masks (they index with host lists), no host samplers, no top logprobs."""
+        return (not params.has_penalties() and not params.logit_bias and not params.min_tokens
+                and not params.needs_host_sampling() and params.logprobs is None)
+
+    def launch(self, logits: torch.Tensor, rows: List[SampleRow]) -> "AsyncSample":
+        """Enqueues the sampling kernel and the copy of its results into pinned
+        host memory; `finish` waits for them.  Device rows only."""
+        R = logits.shape[0]
+        self.last_h2d_bytes = 0
+        toks, lp = self._sample_device_async(logits, rows)
+        if not hasattr(self, "_pinned"):
+            self._pinned = [torch.empty(2, 1 << 14, dtype=torch.float64, pin_memory=True) for _ in range(2)]
+            self._pk = 0
+        buf = self._pinned[self._pk]
+        self._pk ^= 1
+        if R > buf.shape[1]:
+            raise ValueError("too many sample rows for the async readback buffer")
+        both = torch.stack([toks.double(), lp.double()])
+        buf[:, :R].copy_(both, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        return AsyncSample(toks, buf, R, ev)
+
+    def finish(self, a: "AsyncSample") -> SampleResult:
+        a.event.synchronize()
+        self.last_d2h_bytes = 16 * a.rows
+        vals = a.host[:, :a.rows].tolist()
+        R = a.rows
+        return SampleResult([int(x) for x in vals[0]], vals[1], [None] * R, [None] * R)
+
+    def _sample_device_async(self, logits: torch.Tensor, rows: List[SampleRow]):
+        greedy = [r.params.is_greedy for r in rows]
+        if all(greedy):
+            return ops.sample(logits, None, None, None, None, None, None, greedy_all=True, want_logprobs=False)
+        dev = logits.device
+        R = len(rows)
+        if not hasattr(self, "_param_pin"):
+            self._param_pin = [torch.empty(6, 1 << 14, dtype=torch.float64, pin_memory=True) for _ in range(2)]
+            self._ppk = 0
+        hp = self._param_pin[self._ppk]
+        self._ppk ^= 1
+        f = np.empty((4, R), dtype=np.float64)
+        f[0] = [0.0 if g else r.params.temperature for g, r in zip(greedy, rows)]
+        f[1] = [r.params.top_k for r in rows]
+        f[2] = [r.params.top_p for r in rows]
+        f[3] = [r.params.min_p for r in rows]
+        hp[:4, :R] = torch.from_numpy(f)
+        ints = torch.from_numpy(np.asarray([[r.seed & ((1 << 63) - 1) for r in rows], [r.offset for r in rows]],
+                                           dtype=np.int64))
+        d = hp[:4, :R].to(dev, non_blocking=True)
+        hi = hp[4:6, :R].view(torch.int64)
+        hi.copy_(ints)
+        di = hi.to(dev, non_blocking=True)
+        self.last_h2d_bytes += 48 * R
+        return ops.sample(logits, d[0].float(), d[1].int(), d[2].float(), d[3].float(), di[0], di[1],
+                          greedy_all=False, want_logprobs=False)
 
     # ------------------------------------------------------------------ main entry
     def sample(self, logits: torch.Tensor, rows: List[SampleRow]) -> SampleResult:

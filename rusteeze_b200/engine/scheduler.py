@@ -63,6 +63,7 @@ class ScheduledSeq:
     num_new: int        # tokens computed this step
     sample: bool        # logits of the last new token are sampled
     num_samples: int = 1
+    pend_row: int = -1  # async scheduling: row of the previous step's samples that is this step's input
 
 
 @dataclass
@@ -156,6 +157,11 @@ class Scheduler:
             seq.reset_for_recompute()
             self.waiting.appendleft(seq)
 
+    def _finishes_with_pending(self, seq: Sequence) -> bool:
+        p = seq.request.params
+        n = seq.num_generated + seq.pending
+        return (p.max_tokens is not None and n >= p.max_tokens) or seq.total_len >= self.cfg.max_model_len
+
     def _lookahead(self, seq: Sequence) -> int:
         return self.cfg.num_lookahead_slots if not seq.is_prefill else 0
 
@@ -172,6 +178,9 @@ class Scheduler:
         queue = list(self.running)
         while queue:
             seq = queue.pop(0)
+            if seq.pending and self._finishes_with_pending(seq):
+                kept.append(seq)            # its in-flight token is its last: nothing to schedule
+                continue
             if seq.is_prefill:
                 n = min(seq.remaining, token_budget)
                 if n <= 0 or seq_budget <= 0:
@@ -230,6 +239,8 @@ class Scheduler:
             n_prefill = len(out.prefills)
             while self.waiting and seq_budget > 0 and token_budget > 0 and n_prefill < cfg.max_prefill_seqs:
                 seq = self.waiting[0]
+                if seq.pending:
+                    break                   # preempted this step with a token still in flight
                 if seq.total_len > cfg.max_model_len:
                     self.waiting.popleft()
                     seq.status = RequestStatus.FINISHED_IGNORED

@@ -25,7 +25,7 @@ class Sequence:
     __slots__ = ("seq_id", "request", "prompt_len", "token_ids", "status", "num_computed",
                  "num_cached", "logprobs", "cumulative_logprob", "output_text", "stop_reason",
                  "detok", "_buf", "index", "finish_reason", "rng_offset",
-                 "mirostat_mu", "spec_draft")
+                 "mirostat_mu", "spec_draft", "pending")
 
     def __init__(self, request: "Request", prompt_token_ids: List[int], index: int = 0):
         self.seq_id = next(_seq_ids)
@@ -50,6 +50,10 @@ class Sequence:
         self.rng_offset = 0
         self.mirostat_mu = None
         self.spec_draft: List[int] = []
+        # tokens sampled by steps still running on the GPU (asynchronous
+        # scheduling): their KV position is already reserved, their value is
+        # only on the device until the step's results are applied
+        self.pending = 0
 
     # ------------------------------------------------------------------
     @property
@@ -62,7 +66,8 @@ class Sequence:
 
     @property
     def total_len(self) -> int:
-        return len(self.token_ids)
+        """Tokens of the sequence including in-flight (pending) samples."""
+        return len(self.token_ids) + self.pending
 
     @property
     def is_prefill(self) -> bool:

@@ -102,3 +102,60 @@ def test_llama3_8b_two_layers_decode():
     eng = engine(mc=mc, blocks=256, max_seqs=8)
     out = run(eng, prompts(3, seed=5, vocab=128256), n=6)
     assert all(len(o) == 6 for o in out)
+
+
+def _engine_async(flag, **kw):
+    cfg = Config()
+    cfg.model.device = "cuda:0"
+    cfg.engine.num_gpu_blocks = kw.get("blocks", 512)
+    cfg.engine.max_num_seqs = 16
+    cfg.engine.max_num_batched_tokens = 512
+    cfg.engine.enable_chunked_prefill = True
+    cfg.engine.cuda_graph_max_batch = 16
+    cfg.engine.async_scheduling = flag
+    return LLMEngine(cfg, model_config=MID)
+
+
+@pytest.mark.parametrize("temp", [0.0, 0.8])
+def test_async_scheduling_matches_sync(temp):
+    """Pipelined steps (next step enqueued before the previous one's tokens are
+    read back) produce exactly the tokens of synchronous stepping."""
+    ps = prompts(10, seed=7, lo=30, hi=700)
+    outs = []
+    for flag in (False, True):
+        eng = _engine_async(flag)
+        assert eng._async == flag
+        sps = [SamplingParams(temperature=temp, top_p=0.9, max_tokens=20 + 3 * i, ignore_eos=True, seed=100 + i)
+               for i in range(len(ps))]
+        ids = [eng.add_request(None, None, sp, p).request_id for sp, p in zip(sps, ps)]
+        done = {}
+        while eng.has_unfinished_requests():
+            for o in eng.step():
+                if o.finished:
+                    done[o.request_id] = o.outputs[0].token_ids
+        outs.append([done[i] for i in ids])
+        assert not eng._inflight
+    assert outs[0] == outs[1]
+
+
+def test_async_falls_back_for_host_sampling_and_aborts():
+    eng = _engine_async(True)
+    ps = prompts(4, seed=9)
+    a = eng.add_request(None, None, SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True), ps[0])
+    b = eng.add_request(None, None, SamplingParams(temperature=0.0, max_tokens=40, ignore_eos=True), ps[1])
+    for _ in range(3):
+        eng.step()
+    # a penalised request forces the synchronous path (after draining the pipeline)
+    c = eng.add_request(None, None, SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True,
+                                                   repetition_penalty=1.2), ps[2])
+    eng.step()
+    assert not eng._inflight
+    eng.abort_request(b.request_id)
+    done = {}
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            if o.finished:
+                done[o.request_id] = o
+    assert len(done[a.request_id].outputs[0].token_ids) == 12
+    assert len(done[c.request_id].outputs[0].token_ids) == 8
+    assert eng._n_sync_only == 0
