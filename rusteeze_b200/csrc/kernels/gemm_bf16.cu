@@ -109,8 +109,10 @@ __global__ void __launch_bounds__(192, 1)
   // segment sizes live on the device, so the tile count is read here.
   __shared__ int s_grp[2 * kMaxGemmGroups + 1];
   const int G = p.grp_off ? p.num_groups : 0;
-  for (int i = threadIdx.x; i < 2 * G + 1; i += blockDim.x)
-    s_grp[i] = i <= G ? p.grp_off[i] : p.grp_end[i - G - 1];
+  if (G > 0) {
+    for (int i = threadIdx.x; i < 2 * G + 1; i += blockDim.x)
+      s_grp[i] = i <= G ? p.grp_off[i] : p.grp_end[i - G - 1];
+  }
   const int m_tiles = G ? p.grp_off[G] / kBM : p.m_tiles;
   const int num_units = m_tiles * p.n_tiles * p.k_splits;
   const uint32_t epoch =
@@ -656,41 +658,62 @@ __device__ __forceinline__ uint32_t ue8m0_scale(float amax, float* inv) {
   return static_cast<uint32_t>(e + 127);
 }
 
-// One warp per (row, 128-column block): 4 elements per lane.  Rows in
-// [M, M_pad) only get a neutral scale byte (their operand rows are zero-filled
-// by the tensor map).
-__global__ void quant_mxf8_act_kernel(uint8_t* __restrict__ xq, uint8_t* __restrict__ sfa,
-                                      const __nv_bfloat16* __restrict__ x, int M, int M_pad, int K, int ldx) {
+// 8 threads per (row, 128-column block), 16 elements (two 16-byte loads) per
+// thread, 4 blocks per warp; the block's absolute maximum is reduced over its
+// 8 lanes.  Rows in [M, M_pad) only get a neutral scale byte (their operand
+// rows are zero-filled by the tensor map).
+__global__ void __launch_bounds__(256) quant_mxf8_act_kernel(uint8_t* __restrict__ xq, uint8_t* __restrict__ sfa,
+                                                             const __nv_bfloat16* __restrict__ x, int M, int M_pad,
+                                                             int K, int ldx) {
   const int kblocks = K / 128;
-  const long w = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= static_cast<long>(M_pad) * kblocks) return;
-  const int row = static_cast<int>(w / kblocks);
-  const int kb = static_cast<int>(w % kblocks);
+  const long g = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 3;   // (row, block) index
+  const int sub = threadIdx.x & 7;
+  if (g >= static_cast<long>(M_pad) * kblocks) return;
+  const int row = static_cast<int>(g / kblocks);
+  const int kb = static_cast<int>(g % kblocks);
   uint8_t* chunk = sfa + (static_cast<size_t>(row / 128) * kblocks + kb) * kSfChunk;
   if (row >= M) {
-    if (lane == 0) *reinterpret_cast<uint32_t*>(chunk + sf_offset(row & 127, 0)) = 0x7f7f7f7fu;
+    if (sub == 0) *reinterpret_cast<uint32_t*>(chunk + sf_offset(row & 127, 0)) = 0x7f7f7f7fu;
     return;
   }
-  const __nv_bfloat16* src = x + static_cast<size_t>(row) * ldx + kb * 128 + lane * 4;
-  const uint2 u = *reinterpret_cast<const uint2*>(src);
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-  const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
-  const float amax = warp_max(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))));
+  const __nv_bfloat16* src = x + static_cast<size_t>(row) * ldx + kb * 128 + sub * 16;
+  const uint4 u0 = *reinterpret_cast<const uint4*>(src);
+  const uint4 u1 = *reinterpret_cast<const uint4*>(src + 8);
+  float v[16];
+  const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
+  const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 a = __bfloat1622float2(h0[i]), b = __bfloat1622float2(h1[i]);
+    v[2 * i] = a.x; v[2 * i + 1] = a.y; v[8 + 2 * i] = b.x; v[8 + 2 * i + 1] = b.y;
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))));
+  }
+  // the 8 lanes of this (row, block) reduce among themselves; other groups of
+  // the warp may have returned (rows past M), so the mask names only this group
+  const unsigned gmask = 0xffu << (threadIdx.x & 24);
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, o));
   float inv;
   const uint32_t e = ue8m0_scale(amax, &inv);
-  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a.x * inv, a.y * inv), __NV_SATFINITE, __NV_E4M3);
-  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(b.x * inv, b.y * inv), __NV_SATFINITE, __NV_E4M3);
-  *reinterpret_cast<uint32_t*>(xq + static_cast<size_t>(row) * K + kb * 128 + lane * 4) =
-      static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-  if (lane == 0) *reinterpret_cast<uint32_t*>(chunk + sf_offset(row & 127, 0)) = e * 0x01010101u;
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_fp8x2_storage_t lo =
+        __nv_cvt_float2_to_fp8x2(make_float2(v[4 * i] * inv, v[4 * i + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+    const __nv_fp8x2_storage_t hi =
+        __nv_cvt_float2_to_fp8x2(make_float2(v[4 * i + 2] * inv, v[4 * i + 3] * inv), __NV_SATFINITE, __NV_E4M3);
+    w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  }
+  *reinterpret_cast<uint4*>(xq + static_cast<size_t>(row) * K + kb * 128 + sub * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+  if (sub == 0) *reinterpret_cast<uint32_t*>(chunk + sf_offset(row & 127, 0)) = e * 0x01010101u;
 }
 
 int quant_mxf8_act_launch(void* xq, uint8_t* sfa, const __nv_bfloat16* x, int M, int K, int ldx, cudaStream_t st) {
   if (K % 128 != 0) return -1;
   const int M_pad = (M + 127) / 128 * 128;
-  const long warps = static_cast<long>(M_pad) * (K / 128);
-  quant_mxf8_act_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, st>>>(
+  const long threads = static_cast<long>(M_pad) * (K / 128) * 8;
+  quant_mxf8_act_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, st>>>(
       static_cast<uint8_t*>(xq), sfa, x, M, M_pad, K, ldx);
   return static_cast<int>(cudaGetLastError());
 }

@@ -1,0 +1,185 @@
+"""Small single-kernel workloads for ncu captures.
+
+Each case builds inputs larger than L2 where the kernel streams memory (so
+DRAM counters mean something) but holds at most a few GB, runs the kernel
+once as a warm-up and once more for the capture, then synchronises and
+exits.  Usage (one GPU):
+
+    python -m rusteeze_b200.utils.profile_cases --case rms_norm
+    ncu --set full --clock-control none -k regex:rms_norm -s 1 -c 1 -o prof \\
+        python -m rusteeze_b200.utils.profile_cases --case rms_norm
+
+`--list` prints the cases with the kernel-name regex to pass to `-k`.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+
+import torch
+
+from rusteeze_b200 import ops
+from rusteeze_b200.ops import reference as ref
+
+CASES = {}
+
+
+def case(name: str, kernel: str):
+    def deco(fn):
+        CASES[name] = (fn, kernel)
+        return fn
+    return deco
+
+
+def _bf(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+@case("rms_norm", "rms_norm_kernel")
+def _rms_norm():
+    x, r, w = _bf(16384, 4096), _bf(16384, 4096), _bf(4096)
+    return lambda: ops.fused_add_rms_norm(x, r, w, 1e-5)
+
+
+@case("rope_cache", "rope_cache_kernel")
+def _rope_cache():
+    T, Hq, Hkv, D = 16384, 32, 8, 128
+    qkv = _bf(T, (Hq + 2 * Hkv) * D)
+    pos = torch.randint(0, 8192, (T,), device="cuda")
+    cs = ref.rope_cos_sin_cache(D, 8192, 500000.0, None, device="cuda")
+    nb = T // 16 + 8
+    kc, vc = _bf(nb, Hkv, 16, D), _bf(nb, Hkv, 16, D)
+    slots = torch.randperm(nb * 16, device="cuda")[:T]
+    return lambda: ops.rope_and_cache(qkv, pos, cs, kc, vc, slots, Hq, Hkv, D)
+
+
+@case("silu_mul", "act_mul_kernel")
+def _silu_mul():
+    x = _bf(8192, 2 * 14336)
+    return lambda: ops.silu_mul(x)
+
+
+@case("gemm_bf16", "gemm_tcgen05")
+def _gemm_bf16():
+    x, w = _bf(1256, 4096), _bf(28672, 4096, scale=0.02)
+    return lambda: ops.linear(x, w)
+
+
+@case("gemm_mxf8", "gemm_tcgen05")
+def _gemm_mxf8():
+    x = _bf(1256, 4096)
+    wq, ws = ref.quant_mxf8_weight(torch.randn(28672, 4096, device="cuda") * 0.02)
+    wsf = ref.pack_block_scales_ue8m0(ws)
+    xq, sfa = ops.quant_mxf8_act(x)
+    y = torch.empty(1256, 28672, device="cuda", dtype=torch.bfloat16)
+    return lambda: ops.cuda_ext().gemm_mxf8(y, xq, sfa, wq, wsf, None, None, 0, 0, 0)
+
+
+@case("quant_mxf8", "quant_mxf8_act_kernel")
+def _quant_mxf8():
+    x = _bf(8192, 14336)
+    return lambda: ops.quant_mxf8_act(x)
+
+
+@case("gemm_fp8_promote", "gemm_fp8")
+def _gemm_fp8_promote():
+    x = _bf(1256, 4096)
+    wq, ws = ref.quant_fp8_weight(torch.randn(28672, 4096, device="cuda") * 0.02)
+    return lambda: ops.linear_fp8(x, wq, ws)
+
+
+@case("decode_attention", "decode_attn_kernel")
+def _decode():
+    B, ctx, Hq, Hkv, D = 256, 1232, 32, 8, 128
+    from rusteeze_b200.engine.model_runner import choose_num_splits
+    nblk = (ctx + 15) // 16
+    nb = B * nblk + 16
+    cache = _bf(nb, 1, 2, Hkv, 16, D)
+    bt = torch.randperm(nb, device="cuda")[: B * nblk].view(B, nblk).int().contiguous()
+    sl = torch.full((B,), ctx, device="cuda", dtype=torch.int32)
+    q = _bf(B, Hq, D)
+    sp = choose_num_splits(B, Hkv, nblk)
+    ws = torch.empty(B * Hq * sp * (D + 2), device="cuda")
+    o = torch.empty_like(q)
+    return lambda: ops.cuda_ext().decode_attention(o, q, cache[:, 0, 0], cache[:, 0, 1], sl, bt, ws, B,
+                                                   D ** -0.5, 0, 0.0, sp)
+
+
+@case("prefill_attention", "prefill_attn_kernel")
+def _prefill():
+    S, L, Hq, Hkv, D = 4, 1024, 32, 8, 128
+    nblk = (L + 15) // 16
+    cache = _bf(S * nblk + 8, 1, 2, Hkv, 16, D)
+    bt = torch.arange(S * nblk, device="cuda").view(S, nblk).int().contiguous()
+    sl = torch.full((S,), L, device="cuda", dtype=torch.int32)
+    qsl = torch.arange(0, (S + 1) * L, L, device="cuda", dtype=torch.int32)
+    q = _bf(S * L, Hq, D)
+    o = torch.empty_like(q)
+    return lambda: ops.cuda_ext().prefill_attention(o, q, cache[:, 0, 0], cache[:, 0, 1], qsl, sl, bt, 0, S, L,
+                                                    D ** -0.5, 0, 0.0)
+
+
+@case("sample_topk_topp", "topk_topp_kernel")
+def _sample():
+    B, V = 256, 128256
+    logits = torch.randn(B, V, device="cuda") * 3
+    f = lambda v, dt: torch.full((B,), v, dtype=dt, device="cuda")  # noqa: E731
+    args = (f(0.7, torch.float32), f(-1, torch.int32), f(0.9, torch.float32), f(0.0, torch.float32),
+            torch.arange(B, device="cuda"), f(0, torch.int64))
+    return lambda: ops.sample(logits, *args, greedy_all=False)
+
+
+@case("spec_verify", "spec_verify_kernel")
+def _spec_verify():
+    B, k, V = 64, 4, 128256
+    tl = torch.randn(B * (k + 1), V, device="cuda") * 3
+    dl = torch.randn(B * k, V, device="cuda") * 3
+    dt = torch.randint(0, V, (B, k), device="cuda")
+    temps = torch.full((B,), 0.8, device="cuda")
+    seeds = torch.arange(B, device="cuda")
+    offs = torch.zeros(B, dtype=torch.int64, device="cuda")
+    out = torch.empty(B, k + 1, dtype=torch.int64, device="cuda")
+    nacc = torch.empty(B, dtype=torch.int32, device="cuda")
+    return lambda: ops.cuda_ext().spec_verify(out, nacc, tl, dl, dt, temps, seeds, offs)
+
+
+@case("moe_route", "moe_route_kernel")
+def _moe_route():
+    M, H, E = 16384, 4096, 8
+    h, wr = _bf(M, H), _bf(E, H, scale=0.05)
+    tw = torch.empty(M, 2, device="cuda")
+    tid = torch.empty(M, 2, device="cuda", dtype=torch.int32)
+    cnt = torch.zeros(E, device="cuda", dtype=torch.int32)
+    return lambda: ops.cuda_ext().moe_route(tw, tid, cnt, h, wr, 2, 0, E, True)
+
+
+@case("moe_grouped_gemm", "gemm_tcgen05")
+def _moe_grouped():
+    M, H, I, E = 2048, 4096, 14336, 8
+    h, router = _bf(M, H), _bf(E, H, scale=0.05)
+    w13 = ops.interleave_gate_up_experts(_bf(E, 2 * I, H, scale=0.02))
+    w2 = _bf(E, H, I, scale=0.02)
+    return lambda: ops.moe_forward(h, router, w13, w2, 2)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None)
+    ap.add_argument("--list", action="store_true")
+    a = ap.parse_args()
+    if a.list or not a.case:
+        for n, (_, k) in CASES.items():
+            print(f"{n}\t{k}")
+        return 0
+    fn = CASES[a.case][0]()
+    fn()
+    torch.cuda.synchronize()
+    fn()
+    torch.cuda.synchronize()
+    status = int(ops.cuda_ext().status()[0])
+    print(f"{a.case}: ok status={status}")
+    return 0 if status == 0 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
