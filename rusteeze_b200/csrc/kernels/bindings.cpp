@@ -259,6 +259,25 @@ void quant_mxf8_act(torch::Tensor xq, torch::Tensor sfa, torch::Tensor x) {
            "quant_mxf8_act");
 }
 
+void rms_norm_mxf8(torch::Tensor xq, torch::Tensor sfa, torch::Tensor x, c10::optional<torch::Tensor> residual,
+                   torch::Tensor w, double eps, double offset) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w);
+  TORCH_CHECK(x.is_contiguous() && xq.is_contiguous() && sfa.is_contiguous(), "rms_norm_mxf8: contiguous tensors");
+  const int M = x.size(0), H = x.size(1);
+  TORCH_CHECK(xq.size(0) == M && xq.size(1) == H && xq.element_size() == 1, "xq: e4m3 [M, H]");
+  TORCH_CHECK(sfa.numel() >= static_cast<int64_t>((M + 127) / 128) * (H / 128) * 512, "sfa too small");
+  __nv_bfloat16* res = nullptr;
+  if (residual.has_value()) {
+    TORCH_CHECK(residual->is_contiguous() && residual->sizes() == x.sizes(), "residual [M, H]");
+    res = reinterpret_cast<__nv_bfloat16*>(residual->data_ptr());
+  }
+  check_rc(rz::rms_norm_mxf8_launch(reinterpret_cast<uint8_t*>(xq.data_ptr()), reinterpret_cast<uint8_t*>(sfa.data_ptr()),
+                                    reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), res,
+                                    reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), M, H, eps, offset,
+                                    cur_stream()),
+           "rms_norm_mxf8");
+}
+
 // Returns the number of kernels launched (1, or 2 with a split-K reduction).
 int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch::Tensor wq, torch::Tensor sfb,
                   c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual, int64_t epi, int64_t bn,
@@ -555,6 +574,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_fp8_act", &quant_fp8_act);
   m.def("gemm_fp8_block", &gemm_fp8_block);
   m.def("quant_mxf8_act", &quant_mxf8_act);
+  m.def("rms_norm_mxf8", &rms_norm_mxf8);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_peer_rs", &gemm_peer_rs);
   m.def("gemm_ag", &gemm_ag);

@@ -10,6 +10,7 @@
 // (crates/rusteeze-tensor/src/cache.rs:484-505).
 #include "common.cuh"
 #include "elementwise.h"
+#include "mxfp8.cuh"
 
 namespace rz {
 
@@ -85,6 +86,69 @@ __global__ void rms_norm_kernel(__nv_bfloat16* __restrict__ out, const __nv_bflo
       st8(out + row * H + c, o);
     }
   }
+}
+
+// RMSNorm (optionally fused with the residual add) whose output goes straight
+// to the MXFP8 GEMM operand format: e4m3 values plus one UE8M0 scale per
+// 128-column block of the row (written in the GEMM's scale-chunk layout).
+// One CTA per row of [0, M_pad); one 8-element vector per thread, so a
+// 128-column block is 16 consecutive lanes.  Rows in [M, M_pad) only get the
+// neutral scale byte.
+template <bool ADD>
+__global__ void rms_norm_mxf8_kernel(uint8_t* __restrict__ xq, uint8_t* __restrict__ sfa,
+                                     const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
+                                     const __nv_bfloat16* __restrict__ w, int M, int H, float eps, float offset) {
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  const int c = threadIdx.x * 8;
+  const int kblocks = H / 128;
+  uint8_t* chunk = sfa + (static_cast<size_t>(row / 128) * kblocks + c / 128) * kSfChunkBytes + sf_offset(row & 127, 0);
+  if (row >= M) {
+    if ((threadIdx.x & 15) == 0) *reinterpret_cast<uint32_t*>(chunk) = 0x7f7f7f7fu;
+    return;
+  }
+  const size_t base = static_cast<size_t>(row) * H + c;
+  float v[8];
+  ld8(x + base, v);
+  if (ADD) {
+    float r[8];
+    ld8(residual + base, r);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] += r[i];
+    st8(residual + base, v);
+    ld8(residual + base, v);          // normalise the rounded residual, as the bf16 path does
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+  const float inv = rsqrtf(block_sum<1>(ss, red) / H + eps);
+  float g[8], o[8];
+  ld8(w + c, g);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    o[i] = v[i] * inv * (g[i] + offset);
+    amax = fmaxf(amax, fabsf(o[i]));
+  }
+  const unsigned gmask = 0xffffu << (threadIdx.x & 16);
+#pragma unroll
+  for (int s = 8; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, s));
+  float qinv;
+  const uint32_t e = ue8m0_scale(amax, &qinv);
+  *reinterpret_cast<uint2*>(xq + base) = pack_e4m3x8(o, qinv);
+  if ((threadIdx.x & 15) == 0) *reinterpret_cast<uint32_t*>(chunk) = e * 0x01010101u;
+}
+
+int rms_norm_mxf8_launch(uint8_t* xq, uint8_t* sfa, const __nv_bfloat16* x, __nv_bfloat16* residual,
+                         const __nv_bfloat16* w, int rows, int H, float eps, float offset, cudaStream_t st) {
+  if (rows == 0) return 0;
+  if (H % 128 || H > 8192) return -1;
+  const int m_pad = (rows + 127) / 128 * 128;
+  if (residual)
+    rms_norm_mxf8_kernel<true><<<m_pad, H / 8, 0, st>>>(xq, sfa, x, residual, w, rows, H, eps, offset);
+  else
+    rms_norm_mxf8_kernel<false><<<m_pad, H / 8, 0, st>>>(xq, sfa, x, nullptr, w, rows, H, eps, offset);
+  return static_cast<int>(cudaGetLastError());
 }
 
 int rms_norm_launch(__nv_bfloat16* out, const __nv_bfloat16* x, __nv_bfloat16* residual,

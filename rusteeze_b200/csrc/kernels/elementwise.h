@@ -6,6 +6,10 @@
 namespace rz {
 int rms_norm_launch(__nv_bfloat16* out, const __nv_bfloat16* x, __nv_bfloat16* residual, const __nv_bfloat16* w,
                     int rows, int H, float eps, float offset, cudaStream_t st);
+// RMSNorm (+ residual add) emitting the MXFP8 GEMM operand: xq e4m3 [rows, H] and UE8M0
+// scale chunks for ceil(rows/128) row blocks.  H % 128 == 0, H <= 8192.
+int rms_norm_mxf8_launch(uint8_t* xq, uint8_t* sfa, const __nv_bfloat16* x, __nv_bfloat16* residual,
+                         const __nv_bfloat16* w, int rows, int H, float eps, float offset, cudaStream_t st);
 int rope_cache_launch(__nv_bfloat16* qkv, int qkv_stride, const int64_t* pos, const float* cos_sin,
                       __nv_bfloat16* kc, __nv_bfloat16* vc, int64_t block_stride, const int64_t* slots, int T,
                       int Hq, int Hkv, int D, cudaStream_t st);

@@ -35,6 +35,7 @@
 
 #include "common.cuh"
 #include "gemm_bf16.h"
+#include "mxfp8.cuh"
 
 namespace rz {
 
@@ -639,25 +640,6 @@ int gemm_mxf8_launch(const GemmParams& p_in, const void* A, int lda, const void*
 }
 
 // ---------------------------------------------------------------------------------- MXFP8 quantisation
-// Scale byte position inside a 512-byte chunk for row r (0..127) and K-chunk kc
-// (0..3): rows r, r+32, r+64, r+96 share one 16-byte line, which is the order
-// in which tcgen05.cp.32x128b.warpx4 spreads a line over TMEM columns.
-__host__ __device__ constexpr int sf_offset(int r, int kc) { return (r & 31) * 16 + (r >> 5) * 4 + kc; }
-
-// Power-of-two scale for a block with absolute maximum amax: the smallest 2^e
-// with amax / 2^e <= 448 (the e4m3 maximum).  Returns the biased exponent
-// byte (UE8M0) and writes 2^-e to *inv.
-__device__ __forceinline__ uint32_t ue8m0_scale(float amax, float* inv) {
-  int e = -127;
-  if (amax > 0.f) {
-    const uint32_t bits = __float_as_uint(amax / 448.0f);
-    e = static_cast<int>((bits >> 23) & 0xffu) - 127 + ((bits & 0x7fffffu) != 0u ? 1 : 0);
-  }
-  e = max(-126, min(126, e));
-  *inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
-  return static_cast<uint32_t>(e + 127);
-}
-
 // 8 threads per (row, 128-column block), 16 elements (two 16-byte loads) per
 // thread, 4 blocks per warp; the block's absolute maximum is reduced over its
 // 8 lanes.  Rows in [M, M_pad) only get a neutral scale byte (their operand

@@ -132,7 +132,7 @@ class ModelRunner:
                 "h_block_tables": torch.zeros(S, MB, dtype=torch.int32, pin_memory=pin),
                 "h_logits_idx": torch.zeros(T, dtype=torch.int64, pin_memory=pin),
                 "h_sample_idx": torch.zeros(T, dtype=torch.int64, pin_memory=pin),
-                "h_pend": torch.zeros(2, S, dtype=torch.int64, pin_memory=pin)}
+                "h_pend": torch.zeros(2 * S, dtype=torch.int64, pin_memory=pin)}
 
     def _bind_host(self, k: int) -> None:
         for name, t in self._host_sets[k].items():
@@ -220,11 +220,10 @@ class ModelRunner:
             if prev_tokens is None:
                 raise RuntimeError("pending decode input without the previous step's samples")
             P = len(pend_dst)
-            hp = self.h_pend
-            hp[0, :P] = torch.from_numpy(np.asarray(pend_dst, dtype=np.int64))
-            hp[1, :P] = torch.from_numpy(np.asarray(pend_src, dtype=np.int64))
-            dp = hp[:, :P].to(self.device, non_blocking=nb)
-            self.d_input_ids.index_copy_(0, dp[0], prev_tokens.index_select(0, dp[1]))
+            hp = self.h_pend[:2 * P]              # [dst | src], a contiguous prefix of a pinned buffer
+            hp.copy_(torch.from_numpy(np.asarray(pend_dst + pend_src, dtype=np.int64)))
+            dp = hp.to(self.device, non_blocking=nb)
+            self.d_input_ids.index_copy_(0, dp[:P], prev_tokens.index_select(0, dp[P:]))
             self.h2d_bytes += 16 * P
         meta = AttentionMetadata(
             num_seqs=S, num_tokens=T, num_decode_seqs=nd, query_start_loc=self.d_qsl[:S + 1],

@@ -115,25 +115,27 @@ class Sampler:
         R = logits.shape[0]
         self.last_h2d_bytes = 0
         toks, lp = self._sample_device_async(logits, rows)
+        # every host staging buffer is 1-D and only used through contiguous
+        # prefixes: a strided pinned slice would make torch stage the copy
+        # through a blocking temporary
         if not hasattr(self, "_pinned"):
-            self._pinned = [torch.empty(2, 1 << 14, dtype=torch.float64, pin_memory=True) for _ in range(2)]
+            self._pinned = [torch.empty(2 << 14, dtype=torch.float64, pin_memory=True) for _ in range(2)]
             self._pk = 0
         buf = self._pinned[self._pk]
         self._pk ^= 1
-        if R > buf.shape[1]:
+        if 2 * R > buf.numel():
             raise ValueError("too many sample rows for the async readback buffer")
-        both = torch.stack([toks.double(), lp.double()])
-        buf[:, :R].copy_(both, non_blocking=True)
+        buf[:2 * R].copy_(torch.cat([toks.double(), lp.double()]), non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
         return AsyncSample(toks, buf, R, ev)
 
     def finish(self, a: "AsyncSample") -> SampleResult:
         a.event.synchronize()
-        self.last_d2h_bytes = 16 * a.rows
-        vals = a.host[:, :a.rows].tolist()
         R = a.rows
-        return SampleResult([int(x) for x in vals[0]], vals[1], [None] * R, [None] * R)
+        self.last_d2h_bytes = 16 * R
+        vals = a.host[:2 * R].tolist()
+        return SampleResult([int(x) for x in vals[:R]], vals[R:], [None] * R, [None] * R)
 
     def _sample_device_async(self, logits: torch.Tensor, rows: List[SampleRow]):
         greedy = [r.params.is_greedy for r in rows]
@@ -142,24 +144,25 @@ class Sampler:
         dev = logits.device
         R = len(rows)
         if not hasattr(self, "_param_pin"):
-            self._param_pin = [torch.empty(6, 1 << 14, dtype=torch.float64, pin_memory=True) for _ in range(2)]
+            self._param_pin = [(torch.empty(4 << 14, dtype=torch.float32, pin_memory=True),
+                                torch.empty(2 << 14, dtype=torch.int64, pin_memory=True)) for _ in range(2)]
             self._ppk = 0
-        hp = self._param_pin[self._ppk]
+        hf, hi = self._param_pin[self._ppk]
         self._ppk ^= 1
-        f = np.empty((4, R), dtype=np.float64)
-        f[0] = [0.0 if g else r.params.temperature for g, r in zip(greedy, rows)]
-        f[1] = [r.params.top_k for r in rows]
-        f[2] = [r.params.top_p for r in rows]
-        f[3] = [r.params.min_p for r in rows]
-        hp[:4, :R] = torch.from_numpy(f)
-        ints = torch.from_numpy(np.asarray([[r.seed & ((1 << 63) - 1) for r in rows], [r.offset for r in rows]],
-                                           dtype=np.int64))
-        d = hp[:4, :R].to(dev, non_blocking=True)
-        hi = hp[4:6, :R].view(torch.int64)
-        hi.copy_(ints)
-        di = hi.to(dev, non_blocking=True)
-        self.last_h2d_bytes += 48 * R
-        return ops.sample(logits, d[0].float(), d[1].int(), d[2].float(), d[3].float(), di[0], di[1],
+        if R > (1 << 14):
+            raise ValueError("too many sample rows for the async parameter buffer")
+        f = np.empty(4 * R, dtype=np.float32)
+        f[:R] = [0.0 if g else r.params.temperature for g, r in zip(greedy, rows)]
+        f[R:2 * R] = [r.params.top_k for r in rows]
+        f[2 * R:3 * R] = [r.params.top_p for r in rows]
+        f[3 * R:] = [r.params.min_p for r in rows]
+        hf[:4 * R].copy_(torch.from_numpy(f))
+        hi[:2 * R].copy_(torch.from_numpy(np.asarray([r.seed & ((1 << 63) - 1) for r in rows] +
+                                                     [r.offset for r in rows], dtype=np.int64)))
+        d = hf[:4 * R].to(dev, non_blocking=True)
+        di = hi[:2 * R].to(dev, non_blocking=True)
+        self.last_h2d_bytes += 32 * R
+        return ops.sample(logits, d[:R], d[R:2 * R].int(), d[2 * R:3 * R], d[3 * R:], di[:R], di[R:],
                           greedy_all=False, want_logprobs=False)
 
     # ------------------------------------------------------------------ main entry

@@ -229,14 +229,24 @@ class DecoderLM(nn.Module):
         D = cfg.head_dim
         h = self.embed_tokens(input_ids)
         residual = None
+        # MXFP8 weights: the norms emit the GEMM operand (e4m3 + UE8M0 scales) directly
+        mx = h.is_cuda and getattr(self, "fp8_format", None) == "ue8m0" and not self.is_gemma2
         for li, L in enumerate(self.layers):
             kv = kv_caches[li]
-            if residual is None:
-                residual = h
-                x = ops.rms_norm(h, L.input_norm, eps, off)
+            if mx:
+                if residual is None:
+                    residual = h
+                    xq = ops.rms_norm_mxf8(h, L.input_norm, eps, off)
+                else:
+                    xq = ops.rms_norm_mxf8(h, L.input_norm, eps, off, residual=residual)
+                qkv = ops.linear_mxf8_q(*xq, L.qkv_q, L.qkv_sf, L.qkv_bias)
             else:
-                x, residual = ops.fused_add_rms_norm(h, residual, L.input_norm, eps, off)
-            qkv = self._lin(x, L, "qkv", L.qkv_bias)
+                if residual is None:
+                    residual = h
+                    x = ops.rms_norm(h, L.input_norm, eps, off)
+                else:
+                    x, residual = ops.fused_add_rms_norm(h, residual, L.input_norm, eps, off)
+                qkv = self._lin(x, L, "qkv", L.qkv_bias)
             q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
                                    self.hq, self.hkv, D)
             a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
@@ -247,6 +257,11 @@ class DecoderLM(nn.Module):
                 x, residual = ops.fused_add_rms_norm(h, residual, L.pre_ff_norm, eps, off)
                 h = self._mlp(L, x)
                 h = ops.rms_norm(h, L.post_ff_norm, eps, off)
+                continue
+            if mx and not cfg.is_moe:
+                xq = ops.rms_norm_mxf8(h, L.post_attn_norm, eps, off, residual=residual)
+                a = ops.linear_mxf8_q(*xq, L.gate_up_q, L.gate_up_sf, silu_mul=True)
+                h = self._row_parallel(a, L, "down")
                 continue
             x, residual = ops.fused_add_rms_norm(h, residual, L.post_attn_norm, eps, off)
             h = self._moe(L, x) if cfg.is_moe else self._mlp(L, x)

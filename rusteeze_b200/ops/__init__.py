@@ -231,6 +231,30 @@ def quant_mxf8_act(x: torch.Tensor):
     return xq, sfa
 
 
+def rms_norm_mxf8(x: torch.Tensor, w: torch.Tensor, eps: float, offset: float = 0.0,
+                  residual: Optional[torch.Tensor] = None):
+    """RMSNorm (residual += x first when given, in place) emitting the MXFP8
+    GEMM operand directly: (e4m3 [M, H], UE8M0 scale chunks)."""
+    M, H = x.shape
+    xq = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=x.device)
+    sfa = torch.empty((M + 127) // 128, H // 128, 512, dtype=torch.uint8, device=x.device)
+    if M:
+        cuda_ext().rms_norm_mxf8(xq, sfa, x.contiguous(), residual, w, eps, offset)
+        _LAUNCHES[0] += 1
+    return xq, sfa
+
+
+def linear_mxf8_q(xq: torch.Tensor, sfa: torch.Tensor, wq: torch.Tensor, wsf: torch.Tensor,
+                  bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+                  silu_mul: bool = False) -> torch.Tensor:
+    """MXFP8 GEMM on an already quantised operand (e.g. from rms_norm_mxf8)."""
+    M, N = xq.shape[0], wq.shape[0]
+    out = torch.empty(M, N // 2 if silu_mul else N, dtype=torch.bfloat16, device=xq.device)
+    if M:
+        _LAUNCHES[0] += cuda_ext().gemm_mxf8(out, xq, sfa, wq, wsf, bias, residual, 1 if silu_mul else 0, 0, 0)
+    return out
+
+
 def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
                bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
                silu_mul: bool = False, wsf: Optional[torch.Tensor] = None) -> torch.Tensor:

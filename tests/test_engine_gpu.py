@@ -159,3 +159,28 @@ def test_async_falls_back_for_host_sampling_and_aborts():
     assert len(done[a.request_id].outputs[0].token_ids) == 12
     assert len(done[c.request_id].outputs[0].token_ids) == 8
     assert eng._n_sync_only == 0
+
+
+def test_async_launch_never_synchronises():
+    """Everything enqueued for a pipelined step (copies, forward, sampling,
+    readback) must be asynchronous w.r.t. the host: torch's sync debug mode
+    raises on any synchronising call inside `launch`."""
+    eng = _engine_async(True)
+    r = eng.runner
+    orig = r.launch
+    calls = [0]
+
+    def strict_launch(*a, **k):
+        torch.cuda.set_sync_debug_mode("error")
+        try:
+            return orig(*a, **k)
+        finally:
+            torch.cuda.set_sync_debug_mode("default")
+            calls[0] += 1
+
+    r.launch = strict_launch
+    for i, p in enumerate(prompts(6, seed=11, lo=30, hi=400)):
+        eng.add_request(None, None, SamplingParams(temperature=0.7, top_p=0.9, max_tokens=10 + i, ignore_eos=True), p)
+    while eng.has_unfinished_requests():
+        eng.step()
+    assert calls[0] > 10

@@ -218,3 +218,26 @@ def test_gemm_mxf8_silu_bias_residual(bn, ks):
     ops.cuda_ext().gemm_mxf8(y, xq, sfa, wq, wsf, bias, res, 0, bn, ks)
     r2 = ref.fp8_block_gemm(xq.cpu(), xs, wq.cpu(), ws.cpu()) + res.float().cpu() + bias.float().cpu()
     assert ((y.float().cpu() - r2).norm() / r2.norm()).item() < 1e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,H,add", [(1, 4096, False), (300, 4096, True), (129, 2048, True)])
+def test_rms_norm_mxf8_matches_norm_then_quant(M, H, add):
+    torch.manual_seed(M + H)
+    x = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).to(torch.bfloat16)
+    res = torch.randn(M, H, device="cuda", dtype=torch.bfloat16) if add else None
+    res_ref = res.clone() if add else None
+    xq, sfa = ops.rms_norm_mxf8(x, w, 1e-5, 0.0, residual=res)
+    if add:
+        y, res_ref = ops.fused_add_rms_norm(x, res_ref, w, 1e-5)
+        assert torch.equal(res, res_ref)
+    else:
+        y = ops.rms_norm(x, w, 1e-5)
+    qr, sr = ref.quant_mxf8_act(y.cpu())
+    s = ref.unpack_act_scales_ue8m0(sfa.cpu(), M, H)
+    deq = xq.float().cpu().view(M, H // 128, 128) * s.unsqueeze(-1)
+    want = qr.float().view(M, H // 128, 128) * sr.unsqueeze(-1)
+    # the fused kernel quantises the fp32 normalised values, the reference the bf16-rounded ones
+    assert ((deq - want).norm() / want.norm()).item() < 2e-2
+    assert (s == sr).float().mean().item() > 0.99
