@@ -318,6 +318,31 @@ int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch:
   return k_splits > 1 ? 2 : 1;
 }
 
+// gate/up MXFP8 GEMM whose SiLU(gate)*up epilogue writes the down projection's MXFP8 operand.
+int64_t gemm_mxf8_silu_q(torch::Tensor q_out, torch::Tensor sf_out, torch::Tensor xq, torch::Tensor sfa,
+                         torch::Tensor wq, torch::Tensor sfb, c10::optional<torch::Tensor> bias) {
+  CHECK_CUDA(xq);
+  const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
+  TORCH_CHECK(K % 128 == 0 && N % 256 == 0 && wq.size(1) == K, "mxf8 silu_q: K % 128, N % 256");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.size(0) == M && q_out.size(1) == N / 2 && q_out.element_size() == 1,
+              "q_out: e4m3 [M, N/2]");
+  TORCH_CHECK(sf_out.numel() >= static_cast<int64_t>((M + 127) / 128) * (N / 256) * 512, "sf_out too small");
+  rz::GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.k_splits = 1;
+  p.ldd = q_out.stride(0);
+  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  p.epi = rz::kEpiSiluMulMx;
+  p.status = status_ptr();
+  p.sfa = reinterpret_cast<const uint8_t*>(sfa.data_ptr());
+  p.sfb = reinterpret_cast<const uint8_t*>(sfb.data_ptr());
+  p.q_out = reinterpret_cast<uint8_t*>(q_out.data_ptr());
+  p.sf_out = reinterpret_cast<uint8_t*>(sf_out.data_ptr());
+  check_rc(rz::gemm_mxf8_launch(p, xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), 256, cur_stream()),
+           "gemm_mxf8_silu_q");
+  return 1;
+}
+
 std::vector<int64_t> gemm_plan_mxf8(int64_t M, int64_t N, int64_t K, int64_t epi) {
   auto pl = rz::plan_gemm_mxf8(M, N, K, epi);
   return {pl.bn, pl.k_splits};
@@ -584,6 +609,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &moe_route);
   m.def("gemm_mxf8", &gemm_mxf8);
   m.def("gemm_plan_mxf8", &gemm_plan_mxf8);
+  m.def("gemm_mxf8_silu_q", &gemm_mxf8_silu_q);
   m.def("argmax_sample", &argmax_sample);
   m.def("topk_topp_sample", &topk_topp_sample);
   m.def("spec_verify", &spec_verify);

@@ -307,6 +307,55 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
         }
+      } else if (p.epi == kEpiSiluMulMx) {
+        // SiLU(gate)*up emitted as the next MXFP8 GEMM's operand.  With BN = 256 the
+        // tile's 128 outputs of this row are exactly one 1x128 scale block: pass 1
+        // finds its absolute maximum, pass 2 recomputes and quantises.
+        if constexpr (BN == 256) {
+          float amax = 0.f;
+#pragma unroll 1
+          for (int pass = 0; pass < 2; ++pass) {
+            float inv = 1.f;
+            uint32_t e = 127u;
+            if (pass == 1) e = ue8m0_scale(amax, &inv);
+#pragma unroll 1
+            for (int pr = 0; pr < 2; ++pr) {
+#pragma unroll 1
+              for (int h = 0; h < 2; ++h) {
+                uint32_t g[32], v[32];
+                tmem_ld_32x32b_x32(tacc + pr * 128 + h * 32, g);
+                tmem_ld_32x32b_x32(tacc + pr * 128 + 64 + h * 32, v);
+                tmem_ld_wait();
+                const int gcol = nb * BN + pr * 128 + h * 32;
+                float o[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  float a = __uint_as_float(g[j]);
+                  float b = __uint_as_float(v[j]);
+                  if (p.bias) {
+                    a += bf2f(p.bias[gcol + j]);
+                    b += bf2f(p.bias[gcol + 64 + j]);
+                  }
+                  o[j] = silu(a) * b;
+                }
+                if (pass == 0) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(o[j]));
+                } else if (row_ok) {
+                  uint8_t* dst = p.q_out + static_cast<size_t>(row) * p.ldd + nb * 128 + pr * 64 + h * 32;
+#pragma unroll
+                  for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint2*>(dst + j) = pack_e4m3x8(o + j, inv);
+                }
+              }
+            }
+            if (pass == 1) {
+              // rows past M keep the neutral scale (their operand rows are never loaded as data)
+              const int kbo = p.N / 256;            // 128-column scale blocks of the output row
+              *reinterpret_cast<uint32_t*>(p.sf_out + (static_cast<size_t>(mb) * kbo + nb) * kSfChunkBytes +
+                                           sf_offset(row_in_tile, 0)) = (row_ok ? e : 127u) * 0x01010101u;
+            }
+          }
+        }
       } else if (p.epi == kEpiPeerRS) {
         // reduce-scatter: the row goes to its owner's slot for this rank, over NVLink
         const int owner = row / p.rs_rows;

@@ -7,7 +7,9 @@
 
 namespace rz {
 
-enum GemmEpilogue : int { kEpiNone = 0, kEpiSiluMul = 1, kEpiPeerRS = 2 };
+// kEpiSiluMulMx: SiLU(gate)*up written as e4m3 (q_out, row stride ldd) plus UE8M0 1x128
+// scales (sf_out, [ceil(M/128)][N/256] chunks); BN = 256 only.
+enum GemmEpilogue : int { kEpiNone = 0, kEpiSiluMul = 1, kEpiPeerRS = 2, kEpiSiluMulMx = 3 };
 
 constexpr int kMaxTpRanks = 8;
 constexpr int kAgRowBlock = 8;    // rows per all-gather flag
@@ -48,6 +50,8 @@ struct GemmParams {
   int ag_rows;
   const uint32_t* epoch_ptr;   // device step counter; flags carry (*epoch_ptr) * 256 + call_idx + 1
   uint32_t call_idx;
+  uint8_t* q_out;              // kEpiSiluMulMx outputs
+  uint8_t* sf_out;
 };
 
 constexpr int kMaxGemmGroups = 64;

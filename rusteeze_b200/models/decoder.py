@@ -260,8 +260,13 @@ class DecoderLM(nn.Module):
                 continue
             if mx and not cfg.is_moe:
                 xq = ops.rms_norm_mxf8(h, L.post_attn_norm, eps, off, residual=residual)
-                a = ops.linear_mxf8_q(*xq, L.gate_up_q, L.gate_up_sf, silu_mul=True)
-                h = self._row_parallel(a, L, "down")
+                if L.gate_up_q.shape[0] % 256 == 0:
+                    # the SiLU epilogue emits the down projection's fp8 operand directly
+                    aq = ops.linear_mxf8_silu_q(*xq, L.gate_up_q, L.gate_up_sf)
+                    h = self.tp.all_reduce(ops.linear_mxf8_q(*aq, L.down_q, L.down_sf))
+                else:
+                    a = ops.linear_mxf8_q(*xq, L.gate_up_q, L.gate_up_sf, silu_mul=True)
+                    h = self._row_parallel(a, L, "down")
                 continue
             x, residual = ops.fused_add_rms_norm(h, residual, L.post_attn_norm, eps, off)
             h = self._moe(L, x) if cfg.is_moe else self._mlp(L, x)

@@ -255,6 +255,18 @@ def linear_mxf8_q(xq: torch.Tensor, sfa: torch.Tensor, wq: torch.Tensor, wsf: to
     return out
 
 
+def linear_mxf8_silu_q(xq: torch.Tensor, sfa: torch.Tensor, wq: torch.Tensor, wsf: torch.Tensor,
+                       bias: Optional[torch.Tensor] = None):
+    """gate/up MXFP8 GEMM (rows interleaved in 64-row blocks) whose epilogue
+    emits SiLU(gate)*up directly as the next MXFP8 operand (e4m3 + scales)."""
+    M, N = xq.shape[0], wq.shape[0]
+    q = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=xq.device)
+    sf = torch.empty((M + 127) // 128, N // 256, 512, dtype=torch.uint8, device=xq.device)
+    if M:
+        _LAUNCHES[0] += cuda_ext().gemm_mxf8_silu_q(q, sf, xq, sfa, wq, wsf, bias)
+    return q, sf
+
+
 def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
                bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
                silu_mul: bool = False, wsf: Optional[torch.Tensor] = None) -> torch.Tensor:

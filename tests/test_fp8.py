@@ -241,3 +241,23 @@ def test_rms_norm_mxf8_matches_norm_then_quant(M, H, add):
     # the fused kernel quantises the fp32 normalised values, the reference the bf16-rounded ones
     assert ((deq - want).norm() / want.norm()).item() < 2e-2
     assert (s == sr).float().mean().item() > 0.99
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 200, 1300])
+def test_gemm_mxf8_silu_emits_mxf8_operand(M):
+    torch.manual_seed(M)
+    I, K = 1024, 2048
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    wi = ops.interleave_gate_up(torch.randn(2 * I, K, device="cuda", dtype=torch.bfloat16) * 0.02)
+    wq, ws = ref.quant_mxf8_weight(wi)
+    wsf = ref.pack_block_scales_ue8m0(ws)
+    xq, sfa = ops.quant_mxf8_act(x)
+    q, sf = ops.linear_mxf8_silu_q(xq, sfa, wq, wsf)
+    bf = ops.linear_mxf8_q(xq, sfa, wq, wsf, silu_mul=True)            # same GEMM, bf16 epilogue
+    qr, sr = ref.quant_mxf8_act(bf.cpu())
+    s = ref.unpack_act_scales_ue8m0(sf.cpu(), M, I)
+    deq = q.float().cpu().view(M, I // 128, 128) * s.unsqueeze(-1)
+    want = qr.float().view(M, I // 128, 128) * sr.unsqueeze(-1)
+    assert ((deq - want).norm() / want.norm()).item() < 2e-2
+    assert int(ops.cuda_ext().status()[0]) == 0
