@@ -4,7 +4,10 @@
 Workload (synthetic requests, random-init N(0, 0.02) weights of the named
 architecture; no network for checkpoints or datasets):
   * Llama-3-8B: 32 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128,
-    intermediate 14336, vocab 128256, RoPE theta 5e5; bf16 weights, bf16 KV.
+    intermediate 14336, vocab 128256, RoPE theta 5e5; block-scaled fp8 e4m3
+    weights (128x128 weight scales, 1x128 activation scales, both powers of
+    two so the tensor core applies them: MXFP8 / UE8M0), bf16 activations
+    and KV (`--dtype bf16` runs unquantised bf16 weights).
   * Requests with prompt lengths uniform in [128, 2048], output lengths
     uniform in [64, 512], top-p 0.9 at temperature 0.7, Poisson arrivals
     (1024 requests per GPU), served with continuous batching, paged KV
@@ -117,7 +120,7 @@ def make_engine(args, device):
     cfg.model.device = device
     cfg.model.dtype = "bfloat16"
     cfg.model.seed = 0
-    if args.fp8:
+    if args.dtype == "fp8":
         from rusteeze_b200.config.config import QuantizationConfig
         cfg.model.quantization = QuantizationConfig(method="fp8_block")
     cfg.engine.max_num_seqs = args.max_seqs
@@ -143,8 +146,16 @@ def main():
     ap.add_argument("--max-batched-tokens", type=int, default=4096)
     ap.add_argument("--e2e-requests", type=int, default=256)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--fp8", action="store_true")
+    ap.add_argument("--dtype", default="fp8", choices=["fp8", "bf16"],
+                    help="fp8: block-scaled e4m3 weights (the Llama-3-8B serving configuration); bf16: unquantised")
+    ap.add_argument("--fp8", action="store_true", help="same as --dtype fp8 (the default)")
     ap.add_argument("--eager", action="store_true", help="disable CUDA graphs (profiling runs)")
+    ap.add_argument("--workload", default="poisson", choices=["poisson", "static"],
+                    help="poisson: continuous batching (default); static: batches of --batches requests, "
+                         "--static-prompt prompt tokens, --static-output greedy tokens (README table shape)")
+    ap.add_argument("--batches", default="1,8,32,128,256")
+    ap.add_argument("--static-prompt", type=int, default=512)
+    ap.add_argument("--static-output", type=int, default=128)
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -168,6 +179,8 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     device = f"cuda:{local}"
+    if args.workload == "static":
+        return static_batches(args, device, world, rank)
     eng = make_engine(args, device)
     V = eng.model_config.vocab_size
     prompts, olens, arrivals = build_workload(args.requests, 1000 + rank, V, args.rate)
@@ -310,7 +323,8 @@ def main():
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": round(value / BASELINE_TOK_S, 4),
-            "dtype": "fp8_block" if args.fp8 else "bf16",
+            "dtype": ("fp8_e4m3 weights (128x128 UE8M0 block scales), 1x128 UE8M0 activation scales, "
+                      "bf16 activations/KV, fp32 accumulate") if args.dtype == "fp8" else "bf16",
             "data": "synthetic requests, random-init N(0,0.02) weights",
             "config": {"model": args.model, "global_batch": args.max_seqs * world,
                        "seq_len": "prompt U[128,2048] + output U[64,512]",
@@ -330,6 +344,57 @@ def main():
             "e2e": e2e,
         }
         print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def static_batches(args, device, world, rank):
+    """Static batches (all requests admitted together, greedy, EOS ignored):
+    for each batch size B, B prompts of --static-prompt random tokens decode
+    --static-output tokens; output tok/s = B * output / (device time from the
+    first step to the last token), timed with CUDA events, MAX over ranks.
+    One JSON line per batch size."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from rusteeze_b200.core.sampling_params import SamplingParams
+    eng = make_engine(args, device)
+    V = eng.model_config.vocab_size
+    rng = np.random.default_rng(rank)
+    stream = torch.cuda.current_stream()
+    for B in [int(x) for x in args.batches.split(",")]:
+        def run_once():
+            for _ in range(B):
+                eng.add_request(None, None, SamplingParams(temperature=0.0, max_tokens=args.static_output,
+                                                           ignore_eos=True),
+                                rng.integers(0, V, args.static_prompt).tolist())
+            ttft = []
+            while eng.has_unfinished_requests():
+                for o in eng.step():
+                    if o.finished and o.metrics.ttft is not None:
+                        ttft.append(o.metrics.ttft)
+            return ttft
+        run_once()                                   # warm-up (graphs, allocator)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ttft = run_once()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+        if rank == 0:
+            tok = B * args.static_output * world
+            print(json.dumps({"metric": "output_tokens_per_s", "workload": "static", "batch": B,
+                              "value": round(tok / (ms / 1000.0), 1), "unit": "tokens/s", "n_gpus": world,
+                              "ms_total": round(ms, 2), "ttft_p50_s": round(statistics.median(ttft), 4),
+                              "dtype": args.dtype, "config": {"model": args.model, "prompt": args.static_prompt,
+                                                              "output": args.static_output}}), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0

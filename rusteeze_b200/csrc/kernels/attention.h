@@ -50,5 +50,8 @@ struct PrefillAttnParams {
 
 int decode_attention_launch(const DecodeAttnParams& p, cudaStream_t st);
 int prefill_attention_launch(const PrefillAttnParams& p, cudaStream_t st);
+// tcgen05 FlashAttention prefill (head_dim 128, query heads per kv head dividing 128)
+bool prefill_tc_supported(const PrefillAttnParams& p);
+int prefill_tc_launch(const PrefillAttnParams& p, cudaStream_t st);
 
 }  // namespace rz

@@ -123,9 +123,10 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   check_rc(rz::decode_attention_launch(p, cur_stream()), "decode_attention");
 }
 
-void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
-                       torch::Tensor qsl, torch::Tensor seq_lens, torch::Tensor block_tables, int64_t seq_offset,
-                       int64_t num_seqs, int64_t max_q_len, double scale, int64_t window, double softcap) {
+void prefill_attention_impl(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                            torch::Tensor qsl, torch::Tensor seq_lens, torch::Tensor block_tables, int64_t seq_offset,
+                            int64_t num_seqs, int64_t max_q_len, double scale, int64_t window, double softcap,
+                            int64_t impl) {
   CHECK_CUDA(q); CHECK_BF16(q);
   rz::PrefillAttnParams p{};
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
@@ -150,7 +151,18 @@ void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache
   p.window = window;
   p.softcap = softcap;
   p.status = status_ptr();
-  check_rc(rz::prefill_attention_launch(p, cur_stream()), "prefill_attention");
+  // impl: 0 = tensor-core kernel when the shape allows it, 1 = mma.sync kernel, 2 = tensor-core kernel or error
+  const bool tc = impl != 1 && rz::prefill_tc_supported(p);
+  TORCH_CHECK(impl != 2 || tc, "prefill_attention: shape not supported by the tcgen05 kernel");
+  check_rc(tc ? rz::prefill_tc_launch(p, cur_stream()) : rz::prefill_attention_launch(p, cur_stream()),
+           "prefill_attention");
+}
+
+void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                       torch::Tensor qsl, torch::Tensor seq_lens, torch::Tensor block_tables, int64_t seq_offset,
+                       int64_t num_seqs, int64_t max_q_len, double scale, int64_t window, double softcap) {
+  prefill_attention_impl(out, q, k_cache, v_cache, qsl, seq_lens, block_tables, seq_offset, num_seqs, max_q_len,
+                         scale, window, softcap, 0);
 }
 
 // ---------------------------------------------------------------- GEMM
@@ -593,6 +605,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("act_mul", &act_mul);
   m.def("decode_attention", &decode_attention);
   m.def("prefill_attention", &prefill_attention);
+  m.def("prefill_attention_impl", &prefill_attention_impl);
   m.def("gemm_plan", &gemm_plan);
   m.def("gemm_bf16", &gemm_bf16);
   m.def("gemm_bf16_ex", &gemm_bf16_ex);

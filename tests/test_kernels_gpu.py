@@ -329,3 +329,27 @@ def test_spec_verify_sampled_is_distribution_preserving():
     first = out[:, 0].cpu()
     freq = torch.bincount(first, minlength=V).float() / N
     assert (freq - p).abs().max() < 0.02
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (8, 8), (16, 2)])
+@pytest.mark.parametrize("window,softcap", [(0, 0.0), (100, 0.0), (0, 30.0)])
+def test_prefill_tcgen05_matches_mma_sync_and_oracle(Hq, Hkv, window, softcap):
+    """tcgen05 FlashAttention prefill (impl 2) vs the mma.sync kernel (impl 1) and the fp32 oracle,
+    over full prompts, chunked continuations (context > 0), 1-token tails and long sequences."""
+    D = 128
+    specs = [(77, 77), (300, 100), (130, 1), (2048, 700), (16, 16), (129, 129), (1000, 1000)]
+    seq_lens = [s for s, _ in specs]
+    q_lens = [q for _, q in specs]
+    cache, bt, q, qsl, sl = _paged_setup(seq_lens, q_lens, Hq, Hkv, D, seed=21)
+    kc, vc = cache[:, 0, 0], cache[:, 0, 1]
+    r = ref.paged_attention(q, kc, vc, qsl, sl, bt, D ** -0.5, window or None, softcap or None)
+    cd = cache.to(DEV)
+    outs = []
+    for impl in (1, 2):
+        out = torch.zeros(q.shape, device=DEV, dtype=torch.bfloat16)
+        C().prefill_attention_impl(out, q.to(DEV), cd[:, 0, 0], cd[:, 0, 1], qsl.to(DEV), sl.to(DEV), bt.to(DEV),
+                                   0, len(specs), max(q_lens), D ** -0.5, window, softcap, impl)
+        outs.append(out)
+    assert rel_err(outs[1], r) < 1.5e-2
+    assert rel_err(outs[1], outs[0].float()) < 1.5e-2
+    assert int(C().status()[0]) == 0

@@ -89,6 +89,7 @@ def _boundary_worker(rank, world, port, q):
             y = F.gemm_ag(g, wq, 1)                                   # consumer GEMM on gathered rows
             F.end_step()
             torch.cuda.synchronize()
+            dist.barrier()              # the next iteration's all-gather writes into peers' buffers
             part = sum(xs[r].float() @ ws[r].float().t() for r in range(world)).to(torch.bfloat16).float()
             res = (h0.float() + part).to(torch.bfloat16).float()
             want = res * torch.rsqrt(res.pow(2).mean(-1, keepdim=True) + 1e-5) * wn.float()
