@@ -102,6 +102,11 @@ def _spawned_worker(rank: int, world: int, port: int, cfg_dict: dict, mc_dict: O
                     device_type: str) -> None:
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
                       MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    wd = float(os.environ.get("RZ_WORKER_WATCHDOG_S", "0") or 0)
+    if wd > 0:
+        # diagnostics: a worker stuck for `wd` seconds prints every thread's stack and exits
+        import faulthandler
+        faulthandler.dump_traceback_later(wd, exit=True)
     from rusteeze_b200.config.config import config_from_dict
     cfg = config_from_dict(cfg_dict)
     mc = ModelConfig(**mc_dict) if mc_dict else None

@@ -162,6 +162,9 @@ def test_tp2_engine_matches_tp1(backend):
                     done[o.request_id] = o.outputs[0]
         return [done[i] for i in ids]
 
+    import faulthandler
+    os.environ["RZ_WORKER_WATCHDOG_S"] = "240"
+    faulthandler.dump_traceback_later(270, exit=False)     # stacks of a stuck rank 0 in the log
     ref = run(LLMEngine(cfg(1), model_config=mc))
     launcher = TPEngineLauncher(cfg(2), model_config=mc)
     try:
@@ -170,6 +173,7 @@ def test_tp2_engine_matches_tp1(backend):
         launcher.shutdown()
     # bf16 reduction order differs between 1 and 2 ranks: compare the first token exactly and
     # the first-step logprob of the chosen token closely
+    faulthandler.cancel_dump_traceback_later()
     for a, b in zip(got, ref):
         assert a.token_ids[0] == b.token_ids[0]
         assert abs(a.logprobs[0][a.token_ids[0]] - b.logprobs[0][b.token_ids[0]]) < 0.1
