@@ -105,6 +105,24 @@ def _decode():
                                                    D ** -0.5, 0, 0.0, sp)
 
 
+def _prefill_setup():
+    S, L, Hq, Hkv, D = 4, 1024, 32, 8, 128
+    nblk = (L + 15) // 16
+    cache = _bf(S * nblk + 8, 1, 2, Hkv, 16, D)
+    bt = torch.arange(S * nblk, device="cuda").view(S, nblk).int().contiguous()
+    sl = torch.full((S,), L, device="cuda", dtype=torch.int32)
+    qsl = torch.arange(0, (S + 1) * L, L, device="cuda", dtype=torch.int32)
+    q = _bf(S * L, Hq, D)
+    return cache, bt, sl, qsl, q, torch.empty_like(q), S, L, D
+
+
+@case("prefill_attention_tc", "prefill_tc_kernel")
+def _prefill_tc():
+    cache, bt, sl, qsl, q, o, S, L, D = _prefill_setup()
+    return lambda: ops.cuda_ext().prefill_attention_impl(o, q, cache[:, 0, 0], cache[:, 0, 1], qsl, sl, bt, 0, S, L,
+                                                         D ** -0.5, 0, 0.0, 2)
+
+
 @case("prefill_attention", "prefill_attn_kernel")
 def _prefill():
     S, L, Hq, Hkv, D = 4, 1024, 32, 8, 128
