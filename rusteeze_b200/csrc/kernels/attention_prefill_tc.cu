@@ -32,8 +32,8 @@ namespace rz {
 namespace {
 
 constexpr int kTile = 16 * 1024;        // one 128-row x 128-byte swizzled half tile
-constexpr int kPfThreads = 192;
-constexpr int kPfSmem = 12 * kTile + 1024 + 256;   // Q(2) P(2) K(2x2) V(2x2) halves
+constexpr int kPfThreads = 320;   // producer, MMA, 8 softmax warps (2 per TMEM lane quarter)
+constexpr int kPfSmem = 12 * kTile + 1024 + 256 + 3072;   // Q(2) P(2) K(2x2) V(2x2) halves, barriers, exchange
 
 }  // namespace
 
@@ -44,6 +44,7 @@ struct PfTcArgs {
   int tiles_per_seq;
 };
 
+template <bool SOFTCAP, bool WINDOW>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       const PfTcArgs a) {
@@ -81,7 +82,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* p_full = bars + 10;
   uint64_t* p_empty = bars + 11;
   uint64_t* o_full = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* mx_bar = bars + 13;          // the two threads of a row exchange their half-row maxima
+  uint64_t* fin_bar = bars + 14;         // ... and their half-row sums at the end
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  float* xch = reinterpret_cast<float*>(bars + 16);   // maxima [2 tile parities][2 halves][128 rows]
+  float* xsum = xch + 512;                              // sums [2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -90,11 +95,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
+      mbar_init(&s_empty[i], 256);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(p_empty, 1);
     mbar_init(o_full, 1);
+    mbar_init(mx_bar, 256);
+    mbar_init(fin_bar, 256);
     fence_mbar_init();
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
@@ -194,43 +201,58 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax / epilogue
+    // warps 2..9: lane quarter = warp & 3 gives the row, (warp - 2) / 4 the 64-column half
     const int quarter = warp & 3;
+    const int hc = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const int t = r / a.G, g = r % a.G;
     const int pos = ctx + tok0 + t;
+    const int lo = WINDOW ? pos - p.window + 1 : -0x40000000;   // valid kv positions: [lo, pos]
     const float l2e = 1.4426950408889634f;
-    const float sc = p.softcap > 0.f ? 1.f : p.scale * l2e;
+    const float sc = p.scale * l2e;
     float m_use = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
       const int s = j & 1;
       if (!mbar_wait(&s_full[s], (j >> 1) & 1, p.status, kAttnTimeout)) { ok = false; break; }
       tc_fence_after();
-      float x[128];
+      float x[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t u[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_off + s * 128 + c * 32, u);
+        tmem_ld_32x32b_x32(tmem_base + lane_off + s * 128 + hc * 64 + c * 32, u);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(u[i]);
       }
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
-      const int kv0 = kv_beg + j * 128;
+      const int c0 = kv_beg + j * 128 + hc * 64;     // kv position of x[0]
       float mx = -INFINITY;
+      if (!SOFTCAP && c0 >= lo && c0 + 63 <= pos) {  // interior tile: nothing masked
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const int kp = kv0 + c;
-        const bool valid = kp <= pos && (p.window <= 0 || kp > pos - p.window);
-        float v = x[c];
-        if (p.softcap > 0.f) v = p.softcap * tanhf(v * p.scale / p.softcap) * l2e;
-        else v *= sc;
-        v = valid ? v : -INFINITY;
-        x[c] = v;
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < 64; ++c) {
+          x[c] *= sc;
+          mx = fmaxf(mx, x[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          float v = x[c];
+          if (SOFTCAP) v = p.softcap * tanhf(v * p.scale / p.softcap) * l2e;
+          else v *= sc;
+          const int kp = c0 + c;
+          v = (kp >= lo && kp <= pos) ? v : -INFINITY;
+          x[c] = v;
+          mx = fmaxf(mx, v);
+        }
       }
+      // row maximum = max of the two half rows (exchanged through shared memory)
+      xch[(s * 2 + hc) * 128 + r] = mx;
+      mbar_arrive(mx_bar);
+      if (!mbar_wait(mx_bar, j & 1, p.status, kAttnTimeout)) { ok = false; break; }
+      mx = fmaxf(mx, xch[(s * 2 + (hc ^ 1)) * 128 + r]);
       float alpha = 1.f;
       bool rescale = false;
       if (mx > m_use + 8.f) {               // also the first finite maximum (m_use = -inf)
@@ -239,14 +261,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         m_use = mx;
       }
       float rs = 0.f;
-      uint32_t pk[64];
+      uint32_t pk[32];
+      if (m_use == -INFINITY) {
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float e0 = m_use == -INFINITY ? 0.f : exp2f(x[2 * c] - m_use);
-        const float e1 = m_use == -INFINITY ? 0.f : exp2f(x[2 * c + 1] - m_use);
-        const __nv_bfloat162 b2 = __floats2bfloat162_rn(e0, e1);
-        rs += __bfloat162float(b2.x) + __bfloat162float(b2.y);   // sum what the MMA will see
-        pk[c] = *reinterpret_cast<const uint32_t*>(&b2);
+        for (int c = 0; c < 32; ++c) pk[c] = 0u;
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const __nv_bfloat162 b2 = __floats2bfloat162_rn(exp2f(x[2 * c] - m_use), exp2f(x[2 * c + 1] - m_use));
+          const float2 f = __bfloat1622float2(b2);
+          rs += f.x + f.y;                   // sum what the MMA will see
+          pk[c] = *reinterpret_cast<const uint32_t*>(&b2);
+        }
       }
       l = l * alpha + rs;
       // P / O may be touched only after the previous PV MMA finished
@@ -256,35 +282,38 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (__any_sync(0xffffffffu, rescale)) {
         if (!rescale) alpha = 1.f;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t u[32];
-          tmem_ld_32x32b_x32(tmem_base + lane_off + 256 + c * 32, u);
+          const uint32_t ta = tmem_base + lane_off + 256 + hc * 64 + c * 32;
+          tmem_ld_32x32b_x32(ta, u);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-          tmem_st_32x32b_x32(tmem_base + lane_off + 256 + c * 32, u);
+          tmem_st_32x32b_x32(ta, u);
         }
         tmem_st_wait();
       }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const int half = c >> 3, cc = c & 7;
-        *reinterpret_cast<uint4*>(sP + half * kTile + r * 128 + ((cc ^ (r & 7)) << 4)) =
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(sP + hc * kTile + r * 128 + ((c ^ (r & 7)) << 4)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(o_full, 0, p.status, kAttnTimeout)) {
+    // row sum = sum of the two half rows
+    xsum[hc * 128 + r] = l;
+    mbar_arrive(fin_bar);
+    if (ok && mbar_wait(fin_bar, 0, p.status, kAttnTimeout) && mbar_wait(o_full, 0, p.status, kAttnTimeout)) {
+      l += xsum[(hc ^ 1) * 128 + r];
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* dst = p.out + static_cast<size_t>(q0 + tok0 + min(t, ntok - 1)) * p.out_stride +
-                           (kvh * a.G + g) * D;
+                           (kvh * a.G + g) * D + hc * 64;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t u[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_off + 256 + c * 32, u);   // warp-collective: every lane
+        tmem_ld_32x32b_x32(tmem_base + lane_off + 256 + hc * 64 + c * 32, u);   // warp-collective
         tmem_ld_wait();
         if (t < ntok) {
 #pragma unroll
@@ -350,13 +379,22 @@ int prefill_tc_launch(const PrefillAttnParams& p, cudaStream_t st) {
   CUtensorMap tk, tv;
   if (make_tmap_paged(&tk, p.k_cache, p.num_blocks, p.num_kv_heads, p.block_stride)) return -2;
   if (make_tmap_paged(&tv, p.v_cache, p.num_blocks, p.num_kv_heads, p.block_stride)) return -3;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
-    attr = true;
-  }
   dim3 grid(p.num_seqs * a.tiles_per_seq, p.num_kv_heads);
-  prefill_tc_kernel<<<grid, kPfThreads, kPfSmem, st>>>(tk, tv, a);
+#define RZ_PF(SC, WIN)                                                                                    \
+  {                                                                                                       \
+    static bool attr = false;                                                                             \
+    if (!attr) {                                                                                          \
+      cudaFuncSetAttribute(prefill_tc_kernel<SC, WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem); \
+      attr = true;                                                                                        \
+    }                                                                                                     \
+    prefill_tc_kernel<SC, WIN><<<grid, kPfThreads, kPfSmem, st>>>(tk, tv, a);                             \
+  }
+  const bool sc = p.softcap > 0.f, win = p.window > 0;
+  if (sc && win) RZ_PF(true, true)
+  else if (sc) RZ_PF(true, false)
+  else if (win) RZ_PF(false, true)
+  else RZ_PF(false, false)
+#undef RZ_PF
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -178,34 +178,46 @@ int rms_norm_launch(__nv_bfloat16* out, const __nv_bfloat16* x, __nv_bfloat16* r
 }
 
 // ---------------------------------------------------------------------------- RoPE + KV write
-// One CTA per token.  Work items: (Hq + Hkv) heads x D/2 rotation pairs, plus Hkv x D/8 v vectors.
-__global__ void rope_cache_kernel(__nv_bfloat16* __restrict__ qkv, int qkv_stride, const int64_t* __restrict__ pos,
-                                  const float* __restrict__ cos_sin, __nv_bfloat16* __restrict__ kc,
-                                  __nv_bfloat16* __restrict__ vc, int64_t block_stride,
-                                  const int64_t* __restrict__ slots, int Hq, int Hkv, int D) {
+// One CTA per token.  Work items: (Hq + Hkv) heads x (D/2)/8 rotation vectors (8 elements of the
+// first half with the matching 8 of the second half, 16-byte loads), plus Hkv x D/8 v vectors.
+__global__ void __launch_bounds__(128) rope_cache_kernel(__nv_bfloat16* __restrict__ qkv, int qkv_stride,
+                                                         const int64_t* __restrict__ pos,
+                                                         const float* __restrict__ cos_sin,
+                                                         __nv_bfloat16* __restrict__ kc,
+                                                         __nv_bfloat16* __restrict__ vc, int64_t block_stride,
+                                                         const int64_t* __restrict__ slots, int Hq, int Hkv, int D) {
   const int t = blockIdx.x;
   __nv_bfloat16* row = qkv + static_cast<size_t>(t) * qkv_stride;
   const int64_t p = pos[t];
   const float* cs = cos_sin + p * D;
   const int half = D / 2;
+  const int hv = half / 8;
   const int64_t slot = slots[t];
   const int64_t blk = slot >= 0 ? slot / 16 : 0;
   const int off = slot >= 0 ? static_cast<int>(slot % 16) : 0;
-  const int nrot = (Hq + Hkv) * half;
+  const int nrot = (Hq + Hkv) * hv;
   for (int i = threadIdx.x; i < nrot; i += blockDim.x) {
-    const int h = i / half, j = i % half;
+    const int h = i / hv, j = (i % hv) * 8;
     __nv_bfloat16* base = row + h * D;
-    const float x1 = bf2f(base[j]), x2 = bf2f(base[j + half]);
-    const float c = cs[j], s = cs[half + j];
-    const float y1 = x1 * c - x2 * s, y2 = x2 * c + x1 * s;
+    float x1[8], x2[8], c[8], sn[8], y1[8], y2[8];
+    ld8(base + j, x1);
+    ld8(base + j + half, x2);
+    *reinterpret_cast<float4*>(c) = *reinterpret_cast<const float4*>(cs + j);
+    *reinterpret_cast<float4*>(c + 4) = *reinterpret_cast<const float4*>(cs + j + 4);
+    *reinterpret_cast<float4*>(sn) = *reinterpret_cast<const float4*>(cs + half + j);
+    *reinterpret_cast<float4*>(sn + 4) = *reinterpret_cast<const float4*>(cs + half + j + 4);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      y1[k] = x1[k] * c[k] - x2[k] * sn[k];
+      y2[k] = x2[k] * c[k] + x1[k] * sn[k];
+    }
     if (h < Hq) {
-      base[j] = f2bf(y1);
-      base[j + half] = f2bf(y2);
+      st8(base + j, y1);
+      st8(base + j + half, y2);
     } else if (slot >= 0) {
-      const int kh = h - Hq;
-      __nv_bfloat16* dst = kc + blk * block_stride + (static_cast<int64_t>(kh) * 16 + off) * D;
-      dst[j] = f2bf(y1);
-      dst[j + half] = f2bf(y2);
+      __nv_bfloat16* dst = kc + blk * block_stride + (static_cast<int64_t>(h - Hq) * 16 + off) * D;
+      st8(dst + j, y1);
+      st8(dst + j + half, y2);
     }
   }
   if (slot >= 0) {
@@ -223,9 +235,8 @@ int rope_cache_launch(__nv_bfloat16* qkv, int qkv_stride, const int64_t* pos, co
                       __nv_bfloat16* kc, __nv_bfloat16* vc, int64_t block_stride, const int64_t* slots, int T,
                       int Hq, int Hkv, int D, cudaStream_t st) {
   if (T == 0) return 0;
-  const int work = (Hq + Hkv) * D / 2;
-  const int threads = work >= 512 ? 512 : ((work + 31) / 32) * 32;
-  rope_cache_kernel<<<T, threads, 0, st>>>(qkv, qkv_stride, pos, cos_sin, kc, vc, block_stride, slots, Hq, Hkv, D);
+  if (D % 16 != 0 || qkv_stride % 8 != 0) return -1;
+  rope_cache_kernel<<<T, 128, 0, st>>>(qkv, qkv_stride, pos, cos_sin, kc, vc, block_stride, slots, Hq, Hkv, D);
   return static_cast<int>(cudaGetLastError());
 }
 

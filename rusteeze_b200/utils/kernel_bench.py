@@ -187,15 +187,16 @@ def bench_prefill(pk, cases=None) -> List[dict]:
         q = torch.randn(S * L, Hq, D, device="cuda", dtype=torch.bfloat16)
         o = torch.empty_like(q)
 
-        def fn():
-            ops.cuda_ext().prefill_attention(o, q, cache[:, 0, 0], cache[:, 0, 1], qsl, sl, bt, 0, S, L, D ** -0.5,
-                                             0, 0.0)
+        for impl, name in ((1, "prefill_attention_mma_sync"), (2, "prefill_attention_tcgen05")):
+            def fn():
+                ops.cuda_ext().prefill_attention_impl(o, q, cache[:, 0, 0], cache[:, 0, 1], qsl, sl, bt, 0, S, L,
+                                                      D ** -0.5, 0, 0.0, impl)
 
-        t = time_ms(fn)
-        flops = 4.0 * S * Hq * D * L * (L + 1) / 2      # causal
-        out.append({"kernel": "prefill_attention", "seqs": S, "len": L, "Hq": Hq, "Hkv": Hkv, "ms": round(t, 4),
-                    "tflops": round(flops / t / 1e9, 1),
-                    "frac_of_measured_bf16": round(flops / t / 1e9 / pk["bf16_tflops"], 3)})
+            t = time_ms(fn)
+            flops = 4.0 * S * Hq * D * L * (L + 1) / 2      # causal
+            out.append({"kernel": name, "seqs": S, "len": L, "Hq": Hq, "Hkv": Hkv, "ms": round(t, 4),
+                        "tflops": round(flops / t / 1e9, 1),
+                        "frac_of_measured_bf16": round(flops / t / 1e9 / pk["bf16_tflops"], 3)})
     return out
 
 
