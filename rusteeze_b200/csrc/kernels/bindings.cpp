@@ -151,9 +151,9 @@ void prefill_attention_impl(torch::Tensor out, torch::Tensor q, torch::Tensor k_
   p.window = window;
   p.softcap = softcap;
   p.status = status_ptr();
-  // impl: 0 = default (mma.sync kernel until the tensor-core kernel is tuned), 1 = mma.sync kernel,
-  //       2 = tensor-core kernel (error if the shape is not supported)
-  const bool tc = impl == 2 && rz::prefill_tc_supported(p);
+  // impl: 0 = tensor-core kernel when the shape allows it (head_dim 128), else mma.sync;
+  //       1 = mma.sync kernel; 2 = tensor-core kernel (error if the shape is not supported)
+  const bool tc = impl != 1 && rz::prefill_tc_supported(p);
   TORCH_CHECK(impl != 2 || tc, "prefill_attention: shape not supported by the tcgen05 kernel");
   check_rc(tc ? rz::prefill_tc_launch(p, cur_stream()) : rz::prefill_attention_launch(p, cur_stream()),
            "prefill_attention");
