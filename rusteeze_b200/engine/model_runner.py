@@ -281,6 +281,18 @@ class ModelRunner:
                 return b
         return None
 
+    def release_graphs(self) -> None:
+        """Drops the captured graphs and their memory pool.  Graphs that contain
+        NCCL collectives must be released before the process group is
+        destroyed, or the teardown waits on them forever."""
+        self.graphs = {}
+        self.graph_pool = None
+        import gc
+        gc.collect()
+        if self.is_cuda:
+            torch.cuda.synchronize(self.device)
+            torch.cuda.empty_cache()
+
     @torch.no_grad()
     def capture_graphs(self, buckets: Optional[List[int]] = None) -> None:
         """Captures decode-only forward + LM head for each batch bucket."""

@@ -94,7 +94,10 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
 
 def tp_worker_main(cfg: Config, info: DistInfo, model_config: Optional[ModelConfig] = None, tag: str = "0") -> int:
     _, runner, channel = tp_rank_setup(cfg, info, model_config, tag)
-    steps = worker_loop(runner, channel)
+    try:
+        steps = worker_loop(runner, channel)
+    finally:
+        runner.release_graphs()        # graphs holding NCCL calls block destroy_process_group
     return steps
 
 
@@ -146,6 +149,8 @@ class TPEngineLauncher:
     def shutdown(self, timeout: float = 30.0) -> None:
         if self.channel is not None:
             self._engine.runner.shutdown()
+        # graphs holding NCCL calls must go before the process group, on every rank
+        self.runner.release_graphs()
         for p in self.procs:
             p.join(timeout)
             if p.is_alive():
