@@ -234,13 +234,36 @@ __global__ void __launch_bounds__(kSampThreads)
   const float* x = logits + row * ld;
   const float T = temp[row];
   const int tid = threadIdx.x;
+  // every pass walks the row as 16-byte vectors (4 logits per load, more bytes in flight per
+  // thread) when the row allows it, plus a scalar tail
+  const bool vec = (ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
+  const int nv4 = vec ? V / 4 : 0;
+  auto for_each = [&](auto&& f) {
+#pragma unroll 2
+    for (int i4 = tid; i4 < nv4; i4 += blockDim.x) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i4);
+      f(4 * i4, v.x);
+      f(4 * i4 + 1, v.y);
+      f(4 * i4 + 2, v.z);
+      f(4 * i4 + 3, v.w);
+    }
+    for (int i = 4 * nv4 + tid; i < V; i += blockDim.x) f(i, __ldg(x + i));
+  };
 
-  // pass 1: max and min (the histogram spans the actual range of u)
-  float mx = -INFINITY, mn = INFINITY;
-  for (int i = tid; i < V; i += blockDim.x) {
-    mx = fmaxf(mx, x[i]);
-    mn = fminf(mn, x[i]);
-  }
+  // pass 1: max and min (the histogram spans the actual range of u) and, for sampled rows,
+  // the normaliser Z = sum exp((x - max) / T) kept as a running (max, sum) pair per thread
+  float mx = -INFINITY, mn = INFINITY, zs = 0.f;
+  const float invT = T > 0.f ? 1.f / T : 0.f;
+  for_each([&](int, float v) {
+    if (v > mx) {
+      zs = (mx == -INFINITY ? 0.f : zs * __expf((mx - v) * invT)) + 1.f;
+      mx = v;
+    } else if (mx != -INFINITY) {
+      zs += __expf((v - mx) * invT);
+    }
+    mn = fminf(mn, v);
+  });
+  const float tmx = mx;
   mx = block_max(mx, redv);
   mn = -block_max(-mn, redv);
   if (T <= 0.f) {  // greedy row inside a sampled batch
@@ -261,9 +284,7 @@ __global__ void __launch_bounds__(kSampThreads)
     }
     return;
   }
-  const float invT = 1.f / T;
-  float z = 0.f;
-  for (int i = tid; i < V; i += blockDim.x) z += __expf((x[i] - mx) * invT);
+  float z = tmx == -INFINITY ? 0.f : zs * __expf((tmx - mx) * invT);
   z = block_sum_f(z, redv);
 
   const int k = topk[row] > 0 ? min(topk[row], V) : V;
@@ -289,13 +310,10 @@ __global__ void __launch_bounds__(kSampThreads)
     }
     __syncthreads();
     const float inv_w = 1.f / w1;
-    for (int i0 = 0; i0 < V; i0 += blockDim.x) {
-      const int i = i0 + tid;
-      if (i < V) {
-        const float u = (mx - x[i]) * invT;
-        hist_add(cnt, mass, bucket_of(u, 0.f, inv_w), __expf(-u));
-      }
-    }
+    for_each([&](int, float v) {
+      const float u = (mx - v) * invT;
+      hist_add(cnt, mass, bucket_of(u, 0.f, inv_w), __expf(-u));
+    });
     __syncthreads();
     if (tid < 32) {
       int b;
@@ -323,13 +341,10 @@ __global__ void __launch_bounds__(kSampThreads)
       }
       __syncthreads();
       const float inv_w2 = 1.f / w2;
-      for (int i0 = 0; i0 < V; i0 += blockDim.x) {
-        const int i = i0 + tid;
-        if (i < V) {
-          const float u = (mx - x[i]) * invT;
-          if (bucket_of(u, 0.f, inv_w) == b) hist_add(cnt, mass, bucket_of(u, lo, inv_w2), __expf(-u));
-        }
-      }
+      for_each([&](int, float v) {
+        const float u = (mx - v) * invT;
+        if (bucket_of(u, 0.f, inv_w) == b) hist_add(cnt, mass, bucket_of(u, lo, inv_w2), __expf(-u));
+      });
       __syncthreads();
       if (tid < 32) {
         int b2;
@@ -353,8 +368,8 @@ __global__ void __launch_bounds__(kSampThreads)
   float best = -INFINITY;
   int bi = 0x7fffffff;
   float kept = 0.f;
-  for (int i = tid; i < V; i += blockDim.x) {
-    const float u = (mx - x[i]) * invT;
+  for_each([&](int i, float v) {
+    const float u = (mx - v) * invT;
     bool keep = true;
     if (kb1 < kBuckets) {
       const int c1 = bucket_of(u, 0.f, inv_w1);
@@ -374,7 +389,7 @@ __global__ void __launch_bounds__(kSampThreads)
         bi = i;
       }
     }
-  }
+  });
   block_argmax(best, bi, redv, redi);
   kept = block_sum_f(kept, redv);
   if (tid == 0) {

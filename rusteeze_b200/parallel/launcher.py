@@ -53,7 +53,11 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
     tp = TPComm(info.rank, info.world_size, group=dist.group.WORLD if info.world_size > 1 else None,
                 mode=ec.comm_backend if info.device.type == "cuda" else "nccl", device=info.device,
                 max_tokens=max(ec.max_num_batched_tokens, ec.max_num_seqs), hidden=mc.hidden_size)
-    model = build_model(mc, dtype=dtype, device=dev, tp=tp, model_dir=cfg.model.path, seed=cfg.model.seed)
+    # MoE: attention is tensor-parallel, the experts are split over the same ranks (expert
+    # parallelism); every rank routes all tokens and the partial outputs are summed
+    ep_rank, ep_size = (info.rank, info.world_size) if mc.is_moe else (0, 1)
+    model = build_model(mc, dtype=dtype, device=dev, tp=tp, ep_rank=ep_rank, ep_size=ep_size,
+                        model_dir=cfg.model.path, seed=cfg.model.seed)
     if info.device.type == "cuda":
         model.prepare_for_gpu()
     # agree on the KV block count

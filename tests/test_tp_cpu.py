@@ -51,3 +51,25 @@ def test_tp2_gloo_matches_single_process():
     finally:
         launcher.shutdown()
     assert got == ref
+
+
+@pytest.mark.timeout(300)
+def test_tp2_gloo_mixtral_expert_parallel_matches_single_process():
+    """Mixtral-style MoE at TP2: attention heads split, experts split over the
+    ranks (EP2), partial expert outputs summed -- tokens equal the 1-process run."""
+    from rusteeze_b200.models.config import ModelArchitecture
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    mc = ModelConfig(name="ep-tiny", architecture=ModelArchitecture.MIXTRAL, hidden_size=128,
+                     intermediate_size=192, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                     vocab_size=1000, rms_norm_eps=1e-5, max_position_embeddings=512, num_local_experts=4,
+                     num_experts_per_tok=2)
+    assert mc.is_moe
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, 1000, int(n)).tolist() for n in (40, 9)]
+    ref = _run(LLMEngine(_cfg(1), model_config=mc), prompts)
+    launcher = TPEngineLauncher(_cfg(2), model_config=mc, device_type="cpu")
+    try:
+        got = _run(launcher.engine(), prompts)
+    finally:
+        launcher.shutdown()
+    assert got == ref
