@@ -389,17 +389,20 @@ int64_t gemm_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch:
   return 1;
 }
 
-// Whole MoE block for the local experts: route -> permute -> grouped gate/up (SiLU) -> grouped down
-// -> combine.  w13 holds every local expert's gate/up rows interleaved in 64-row blocks.
-// Returns the number of kernels launched.
-int64_t moe_forward(torch::Tensor out, torch::Tensor h, torch::Tensor wr, torch::Tensor w13, torch::Tensor w2,
-                    int64_t topk, int64_t e_lo, bool renormalize, c10::optional<torch::Tensor> residual) {
+// Local experts of an MoE block: route -> permute -> grouped gate/up (SiLU) -> grouped down.
+// w13 holds every local expert's gate/up rows interleaved in 64-row blocks.  Returns (y, pos_of,
+// topk_w): expert outputs in expert-sorted rows and, per (token, slot), its row in y (-1 when the
+// slot's expert lives on another rank) and gate weight.
+struct MoeExpertOut {
+  torch::Tensor y, pos, tw;
+};
+MoeExpertOut moe_experts(torch::Tensor h, torch::Tensor wr, torch::Tensor w13, torch::Tensor w2, int64_t topk,
+                         int64_t e_lo, bool renormalize) {
   CHECK_CUDA(h); CHECK_BF16(h); CHECK_BF16(wr); CHECK_BF16(w13); CHECK_BF16(w2); CHECK_LAST(h);
   const int M = h.size(0), H = h.size(1), E = wr.size(0), ne = w13.size(0), I = w13.size(1) / 2;
   TORCH_CHECK(wr.size(1) == H && w13.size(2) == H && w2.size(0) == ne && w2.size(1) == H && w2.size(2) == I,
               "moe: weight shapes");
   TORCH_CHECK(topk >= 1 && topk <= 8 && topk <= E && E <= 32 && e_lo >= 0 && e_lo + ne <= E, "moe: expert ranges");
-  TORCH_CHECK(out.is_contiguous() && out.size(0) == M && out.size(1) == H, "moe: out [M, H]");
   auto i32 = h.options().dtype(torch::kInt32);
   auto cnt = torch::zeros({2 * ne}, i32);  // counts | fill
   auto tw = torch::empty({M, topk}, h.options().dtype(torch::kFloat32));
@@ -425,14 +428,56 @@ int64_t moe_forward(torch::Tensor out, torch::Tensor h, torch::Tensor wr, torch:
   gemm_grouped(act, x_perm, w13, go, ge, rz::kEpiSiluMul, 0);
   auto y = torch::empty({rows, H}, h.options());
   gemm_grouped(y, act, w2, go, ge, rz::kEpiNone, 0);
+  return {y, pos, tw};
+}
+
+// Whole MoE block for the local experts with the weighted combine on this rank.
+// Returns the number of kernels launched.
+int64_t moe_forward(torch::Tensor out, torch::Tensor h, torch::Tensor wr, torch::Tensor w13, torch::Tensor w2,
+                    int64_t topk, int64_t e_lo, bool renormalize, c10::optional<torch::Tensor> residual) {
+  const int M = h.size(0), H = h.size(1);
+  TORCH_CHECK(out.is_contiguous() && out.size(0) == M && out.size(1) == H, "moe: out [M, H]");
+  auto e = moe_experts(h, wr, w13, w2, topk, e_lo, renormalize);
   rz::MoeCombineParams cp{};
-  cp.y = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()); cp.ldy = H;
-  cp.pos_of = pp.pos_of; cp.topk_w = rp.topk_w;
+  cp.y = reinterpret_cast<const __nv_bfloat16*>(e.y.data_ptr()); cp.ldy = H;
+  cp.pos_of = e.pos.data_ptr<int>(); cp.topk_w = e.tw.data_ptr<float>();
   cp.residual = residual.has_value() ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
   cp.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   cp.M = M; cp.H = H; cp.topk = topk;
   check_rc(rz::moe_combine_launch(cp, cur_stream()), "moe_combine");
   return 6;   // zero-fill, route, permute, 2 grouped GEMMs, combine
+}
+
+// Expert-parallel MoE block: local experts, then every local (token, slot) output row is sent to
+// the token's owner rank (slot buffers + flags over NVLink) for rs_norm_ag in MoE mode.
+int64_t moe_forward_peer(torch::Tensor h, torch::Tensor wr, torch::Tensor w13, torch::Tensor w2, int64_t topk,
+                         int64_t e_lo, bool renormalize, std::vector<int64_t> slots, std::vector<int64_t> flags,
+                         int64_t rs_rows, torch::Tensor epoch, int64_t call_idx) {
+  const int M = h.size(0), H = h.size(1);
+  const int world = static_cast<int>(slots.size());
+  TORCH_CHECK(world >= 1 && world <= rz::kMaxTpRanks && flags.size() == slots.size() && topk <= world &&
+                  static_cast<int64_t>(rs_rows) * world >= M,
+              "moe_forward_peer: ranks / slots");
+  auto e = moe_experts(h, wr, w13, w2, topk, e_lo, renormalize);
+  rz::MoeCombinePeerParams cp{};
+  cp.y = reinterpret_cast<const __nv_bfloat16*>(e.y.data_ptr());
+  cp.pos_of = e.pos.data_ptr<int>(); cp.topk_w = e.tw.data_ptr<float>();
+  for (int i = 0; i < world; ++i) {
+    cp.slot[i] = reinterpret_cast<__nv_bfloat16*>(slots[i]);
+    cp.flag[i] = reinterpret_cast<uint32_t*>(flags[i]);
+  }
+  cp.M = M; cp.H = H; cp.topk = topk; cp.rs_rows = rs_rows;
+  cp.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  cp.call_idx = static_cast<uint32_t>(call_idx);
+  check_rc(rz::moe_combine_peer_launch(cp, cur_stream()), "moe_combine_peer");
+  return 6;
+}
+
+void ag_wait(torch::Tensor ag_flag, int64_t M, torch::Tensor epoch, int64_t call_idx) {
+  check_rc(rz::ag_wait_launch(reinterpret_cast<const uint32_t*>(ag_flag.data_ptr()), M,
+                              reinterpret_cast<const uint32_t*>(epoch.data_ptr()), static_cast<uint32_t>(call_idx),
+                              status_ptr(), cur_stream()),
+           "ag_wait");
 }
 
 // Routing only (tests): fills topk weights / ids and the local expert counts.
@@ -511,7 +556,7 @@ int64_t gemm_ag(torch::Tensor out, torch::Tensor g, torch::Tensor w, c10::option
 void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10::optional<torch::Tensor> resid_in,
                 torch::Tensor residual, torch::Tensor w, double eps, double offset, std::vector<int64_t> gathers,
                 std::vector<int64_t> ag_flags, int64_t rank, int64_t M, int64_t rs_rows, torch::Tensor epoch,
-                int64_t call_idx) {
+                int64_t call_idx, int64_t moe_topk, c10::optional<torch::Tensor> moe_flag) {
   CHECK_BF16(residual); CHECK_BF16(w);
   const int world = static_cast<int>(gathers.size());
   TORCH_CHECK(world >= 1 && world <= rz::kMaxTpRanks && ag_flags.size() == gathers.size(), "rs_norm_ag: ranks");
@@ -532,6 +577,11 @@ void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10
   p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
   p.call_idx = static_cast<uint32_t>(call_idx);
   p.status = status_ptr();
+  p.moe_topk = static_cast<int>(moe_topk);
+  if (moe_topk > 0) {
+    TORCH_CHECK(moe_flag.has_value(), "rs_norm_ag: MoE mode needs the moe flags");
+    p.moe_flag = reinterpret_cast<const uint32_t*>(moe_flag->data_ptr());
+  }
   check_rc(rz::rs_norm_ag_launch(p, cur_stream()), "rs_norm_ag");
 }
 
@@ -618,6 +668,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_peer_rs", &gemm_peer_rs);
   m.def("gemm_ag", &gemm_ag);
   m.def("rs_norm_ag", &rs_norm_ag);
+  m.def("moe_forward_peer", &moe_forward_peer);
+  m.def("ag_wait", &ag_wait);
   m.def("tp_epoch_bump", &tp_epoch_bump);
   m.def("moe_forward", &moe_forward);
   m.def("moe_route", &moe_route);

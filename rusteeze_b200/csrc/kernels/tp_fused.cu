@@ -55,7 +55,17 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(RsNormAgParams p) {
   const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u;
   const int own0 = p.rank * p.rs_rows;
   const int g0 = own0 + blockIdx.x * kAgRowBlock;          // first global row of this block
-  if (p.reduce) {
+  if (p.reduce && p.moe_topk > 0) {
+    // every (row, slot) of this block was written by the rank that owns the slot's expert
+    const int nflags = kAgRowBlock * p.moe_topk;
+    bool ok = true;
+    for (int f = threadIdx.x; f < nflags && ok; f += blockDim.x) {
+      const int rr = f / p.moe_topk, k = f % p.moe_topk;
+      const int li0 = g0 - own0 + rr;
+      if (g0 + rr < p.M && li0 < p.rs_rows)
+        ok = wait_flag_geq(p.moe_flag + static_cast<size_t>(k) * p.rs_rows + li0, epoch, p.status, kCommPeerTimeout);
+    }
+  } else if (p.reduce) {
     // tiles of quarter (g0 % 128) / 32 of m-tile g0 / 128, every n tile, every source rank
     const int mt = g0 / 128, q = (g0 % 128) / 32;
     const int nflags = p.n_tiles * p.world;
@@ -77,7 +87,8 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(RsNormAgParams p) {
       float x[8], t[8];
       if (p.reduce) {
         ld8f(res + c, x);
-        for (int s = 0; s < p.world; ++s) {
+        const int nsrc = p.moe_topk > 0 ? p.moe_topk : p.world;
+        for (int s = 0; s < nsrc; ++s) {
           ld8f(p.slots + (static_cast<size_t>(s) * p.rs_rows + li) * p.H + c, t);
 #pragma unroll
           for (int i = 0; i < 8; ++i) x[i] += t[i];
@@ -110,6 +121,57 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(RsNormAgParams p) {
 }
 
 __global__ void tp_epoch_bump_kernel(uint32_t* ep) { *ep += 1u; }
+
+// one warp per (token, slot) pair
+__global__ void __launch_bounds__(256) moe_combine_peer_kernel(MoeCombinePeerParams p) {
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u;
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int pairs = p.M * p.topk;
+  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < pairs; i += gridDim.x * warps) {
+    const int pos = p.pos_of[i];
+    if (pos < 0) continue;                                   // warp-uniform: the expert is on another rank
+    const int t = i / p.topk, k = i % p.topk;
+    const int owner = t / p.rs_rows, li = t - owner * p.rs_rows;
+    const float w = p.topk_w[i];
+    const __nv_bfloat16* src = p.y + static_cast<size_t>(pos) * p.H;
+    __nv_bfloat16* dst = p.slot[owner] + (static_cast<size_t>(k) * p.rs_rows + li) * p.H;
+    for (int c = lane * 8; c < p.H; c += 256) {
+      float v[8];
+      ld8f(src + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= w;
+      *reinterpret_cast<uint4*>(dst + c) = pack8f(v);
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) st_release_sys_u32(p.flag[owner] + static_cast<size_t>(k) * p.rs_rows + li, epoch);
+  }
+}
+
+__global__ void ag_wait_kernel(const uint32_t* ag_flag, int nrb, const uint32_t* epoch_ptr, uint32_t call_idx,
+                               int* status) {
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(epoch_ptr) * 256u + call_idx + 1u;
+  for (int rb = blockIdx.x * blockDim.x + threadIdx.x; rb < nrb; rb += gridDim.x * blockDim.x)
+    if (!wait_flag_geq(ag_flag + rb, epoch, status, kCommPeerTimeout)) return;
+}
+
+int moe_combine_peer_launch(const MoeCombinePeerParams& p, cudaStream_t st) {
+  if (p.H % 8 != 0) return -1;
+  const int pairs = p.M * p.topk;
+  if (pairs == 0) return 0;
+  int blocks = (pairs + 7) / 8;
+  blocks = blocks > 1024 ? 1024 : blocks;
+  moe_combine_peer_kernel<<<blocks, 256, 0, st>>>(p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int ag_wait_launch(const uint32_t* ag_flag, int M, const uint32_t* epoch_ptr, uint32_t call_idx, int* status,
+                   cudaStream_t st) {
+  const int nrb = (M + kAgRowBlock - 1) / kAgRowBlock;
+  if (nrb == 0) return 0;
+  ag_wait_kernel<<<(nrb + 127) / 128, 128, 0, st>>>(ag_flag, nrb, epoch_ptr, call_idx, status);
+  return static_cast<int>(cudaGetLastError());
+}
 
 int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st) {
   if (p.rs_rows % kAgRowBlock != 0 || p.H % 256 != 0 || p.world > kMaxTpRanks) return -1;

@@ -23,9 +23,30 @@ struct RsNormAgParams {
   const uint32_t* epoch_ptr;
   uint32_t call_idx;
   int* status;
+  // MoE combine mode (moe_topk > 0): slots hold [topk][rs_rows][H] expert outputs (already
+  // weighted by the gates), each row k-slot released by its own flag moe_flag[k * rs_rows + row]
+  int moe_topk;
+  const uint32_t* moe_flag;
+};
+
+// Expert-parallel combine: every local (token, slot) pair's weighted expert output row goes
+// to the token's owner, slot k, over NVLink; one release flag per written row.
+struct MoeCombinePeerParams {
+  const __nv_bfloat16* y;           // expert outputs (rows of the expert-sorted buffer)
+  const int* pos_of;                // [M * topk] row of each pair in y, -1 if the expert is not local
+  const float* topk_w;              // [M * topk]
+  __nv_bfloat16* slot[kMaxTpRanks]; // every rank's slot buffer [topk][rs_rows][H]
+  uint32_t* flag[kMaxTpRanks];      // every rank's moe flags [topk][rs_rows]
+  int M, H, topk, rs_rows;
+  const uint32_t* epoch_ptr;
+  uint32_t call_idx;
 };
 
 int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st);
+int moe_combine_peer_launch(const MoeCombinePeerParams& p, cudaStream_t st);
+// waits (bounded) until the all-gather flags of rows [0, M) carry this call's epoch
+int ag_wait_launch(const uint32_t* ag_flag, int M, const uint32_t* epoch_ptr, uint32_t call_idx, int* status,
+                   cudaStream_t st);
 int tp_epoch_bump_launch(uint32_t* ep, cudaStream_t st);
 
 }  // namespace rz

@@ -277,8 +277,12 @@ class DecoderLM(nn.Module):
         F = getattr(self.tp, "fused_tp", None)
         if F is None or self.tp.size == 1 or not F.fits(M) or self.device.type != "cuda":
             return False
-        if self.cfg.is_moe or self.is_gemma2 or self.act != "silu" or getattr(self, "fp8", False):
+        if self.is_gemma2 or self.act != "silu" or getattr(self, "fp8", False):
             return False
+        if self.cfg.is_moe:
+            # experts split over the ranks; top-k slots must fit the per-rank slot buffer
+            return (self.ep_size == self.tp.size and self.cfg.num_experts_per_tok <= self.tp.size
+                    and all(getattr(L, "w13_il", None) is not None for L in self.layers))
         return all(getattr(L, "gate_up_il", None) is not None for L in self.layers)
 
     def _forward_fused_tp(self, input_ids: torch.Tensor, positions: torch.Tensor, meta: AttentionMetadata,
@@ -309,9 +313,14 @@ class DecoderLM(nn.Module):
                                     cfg.attn_logit_softcapping)
             F.gemm_rs(a.view(M, -1), L.o, c_attn)
             x = F.rs_norm_ag(M, L.post_attn_norm, eps, off, c_attn)
+            nw = self.layers[li + 1].input_norm if li + 1 < n else self.norm
+            if cfg.is_moe:
+                k = cfg.num_experts_per_tok
+                F.moe(x, L.router, L.w13_il, L.w2, k, self.e_lo, c_attn, c_mlp)
+                x = F.rs_norm_ag(M, nw, eps, off, c_mlp, moe_topk=k)
+                continue
             act = F.gemm_ag(x, L.gate_up_il, c_attn, silu_mul=True)
             F.gemm_rs(act, L.down, c_mlp)
-            nw = self.layers[li + 1].input_norm if li + 1 < n else self.norm
             x = F.rs_norm_ag(M, nw, eps, off, c_mlp)
         F.end_step()
         return x

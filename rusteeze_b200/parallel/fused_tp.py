@@ -13,7 +13,12 @@ around it (csrc/kernels/tp_fused.cu, gemm_bf16.cu):
                buffer (all-gather);
   gemm_ag      the next column-parallel GEMM reads the gathered rows from
                LOCAL memory; its TMA producer waits per A tile for the rows'
-               all-gather flags, so it starts as soon as its rows landed.
+               all-gather flags, so it starts as soon as its rows landed;
+  moe          expert parallelism (Mixtral): the all-gather above is the
+               dispatch (every rank sees every token); each rank runs its own
+               experts and its combine kernel stores every weighted expert
+               output row straight into the owner's slot k over NVLink, so the
+               owner's rs_norm_ag sums top-k slots instead of world partials.
 
 One symmetric allocation per rank (torch symmetric memory) holds
 [rs flags | ag flags | slots | gather]; peers' bases come from the
@@ -47,9 +52,11 @@ class FusedTP:
         self.max_n_tiles = -(-hidden // 64)          # n tiles of a row-parallel output at the smallest tile
         n_rs_flags = self.max_m_tiles * self.max_n_tiles * 4 * world
         n_ag_flags = -(-max_tokens // 8) + 16
+        n_moe_flags = 8 * self.max_rs_rows                 # [topk <= 8][rs_rows]
         self.off_rs_flag = 0
         self.off_ag_flag = _up(self.off_rs_flag + 4 * n_rs_flags, _ALIGN)
-        self.off_slots = _up(self.off_ag_flag + 4 * n_ag_flags, _ALIGN)
+        self.off_moe_flag = _up(self.off_ag_flag + 4 * n_ag_flags, _ALIGN)
+        self.off_slots = _up(self.off_moe_flag + 4 * n_moe_flags, _ALIGN)
         self.off_gather = _up(self.off_slots + 2 * world * self.max_rs_rows * hidden, _ALIGN)
         total = _up(self.off_gather + 2 * (max_tokens + 128) * hidden, _ALIGN)
         try:
@@ -65,9 +72,11 @@ class FusedTP:
         self.rs_flag_ptrs = [b + self.off_rs_flag for b in bases]
         self.gather_ptrs = [b + self.off_gather for b in bases]
         self.ag_flag_ptrs = [b + self.off_ag_flag for b in bases]
+        self.moe_flag_ptrs = [b + self.off_moe_flag for b in bases]
         u8 = self.buf
         self.rs_flag = u8[self.off_rs_flag:self.off_rs_flag + 4 * n_rs_flags].view(torch.int32)
         self.ag_flag = u8[self.off_ag_flag:self.off_ag_flag + 4 * n_ag_flags].view(torch.int32)
+        self.moe_flag = u8[self.off_moe_flag:self.off_moe_flag + 4 * n_moe_flags].view(torch.int32)
         self.slots = u8[self.off_slots:self.off_slots + 2 * world * self.max_rs_rows * hidden].view(torch.bfloat16)
         self.gather = u8[self.off_gather:self.off_gather + 2 * (max_tokens + 128) * hidden].view(
             torch.bfloat16).view(max_tokens + 128, hidden)
@@ -90,9 +99,22 @@ class FusedTP:
         M = h.shape[0]
         C = ops.cuda_ext()
         C.rs_norm_ag(self.slots, self.rs_flag, 1, h.contiguous(), self.residual, norm_w, eps, offset,
-                     self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch, 0)
+                     self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch, 0, 0, None)
         ops.add_launches(1)
         return self.gather[:M]
+
+    def moe(self, g: torch.Tensor, router: torch.Tensor, w13_il: torch.Tensor, w2: torch.Tensor, topk: int,
+            e_lo: int, call_idx_in: int, call_idx: int) -> None:
+        """Expert-parallel MoE on the all-gathered rows: waits for the rows of
+        boundary `call_idx_in`, runs this rank's experts, and sends every
+        weighted expert output row to its token's owner (slot k) with a flag;
+        `rs_norm_ag(..., moe_topk=topk)` then sums the slots on the owner."""
+        M = g.shape[0]
+        C = ops.cuda_ext()
+        C.ag_wait(self.ag_flag, M, self.epoch, call_idx_in)
+        ops.add_launches(1)
+        ops.add_launches(C.moe_forward_peer(g, router, w13_il, w2, topk, e_lo, True, self.slot_ptrs,
+                                            self.moe_flag_ptrs, self.rs_rows(M), self.epoch, call_idx))
 
     def gemm_rs(self, x: torch.Tensor, w: torch.Tensor, call_idx: int) -> None:
         M = x.shape[0]
@@ -100,10 +122,11 @@ class FusedTP:
                                                        self.rank, self.rs_rows(M), self.epoch, call_idx, 0))
         ops.add_launches(1)
 
-    def rs_norm_ag(self, M: int, norm_w: torch.Tensor, eps: float, offset: float, call_idx: int) -> torch.Tensor:
+    def rs_norm_ag(self, M: int, norm_w: torch.Tensor, eps: float, offset: float, call_idx: int,
+                   moe_topk: int = 0) -> torch.Tensor:
         ops.cuda_ext().rs_norm_ag(self.slots, self.rs_flag, self.n_tiles, None, self.residual, norm_w, eps, offset,
                                   self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch,
-                                  call_idx)
+                                  call_idx, moe_topk, self.moe_flag if moe_topk else None)
         ops.add_launches(1)
         return self.gather[:M]
 

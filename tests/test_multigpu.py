@@ -124,18 +124,28 @@ def test_fused_tp_boundary_matches_reference():
 
 
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("backend", ["nccl", "fused"])
-def test_tp2_engine_matches_tp1(backend):
+@pytest.mark.parametrize("backend,arch", [("nccl", "llama"), ("fused", "llama"), ("nccl", "mixtral"),
+                                          ("fused", "mixtral")])
+def test_tp2_engine_matches_tp1(backend, arch):
+    """TP2 engine (rank 0 schedules, worker process over the plan ring) vs the
+    single-GPU engine.  Mixtral: attention TP2 + experts EP2; with the fused
+    backend the MoE dispatch is the fused all-gather and the combine stores
+    expert rows straight into the owners' slots."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import numpy as np
     from rusteeze_b200.config.config import Config
     from rusteeze_b200.core.sampling_params import SamplingParams
     from rusteeze_b200.engine.llm_engine import LLMEngine
-    from rusteeze_b200.models.config import ModelConfig
+    from rusteeze_b200.models.config import ModelArchitecture, ModelConfig
     from rusteeze_b200.parallel.launcher import TPEngineLauncher
-    mc = ModelConfig(name="tp-mid", hidden_size=1024, intermediate_size=2816, num_hidden_layers=2,
-                     num_attention_heads=8, num_key_value_heads=2, vocab_size=32000, max_position_embeddings=2048)
+    if arch == "llama":
+        mc = ModelConfig(name="tp-mid", hidden_size=1024, intermediate_size=2816, num_hidden_layers=2,
+                         num_attention_heads=8, num_key_value_heads=2, vocab_size=32000, max_position_embeddings=2048)
+    else:
+        mc = ModelConfig(name="ep-mid", architecture=ModelArchitecture.MIXTRAL, hidden_size=1024,
+                         intermediate_size=1792, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
+                         vocab_size=32000, max_position_embeddings=2048, num_local_experts=4, num_experts_per_tok=2)
 
     def cfg(tp):
         c = Config()
