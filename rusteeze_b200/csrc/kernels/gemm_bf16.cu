@@ -9,7 +9,7 @@
 //             are moved to TMEM by tcgen05.cp and applied inside the MMA, so
 //             the accumulator needs no per-block promotion.
 //
-// Structure (one persistent CTA per SM, 192 threads, warp-specialised):
+// Structure (one persistent CTA per SM, 320 threads, warp-specialised):
 //   warp 0      TMA producer: 128-row A tile + BN-row B tile per stage into a
 //               STAGES-deep shared-memory ring (128-byte swizzle), plus the
 //               scale chunks (bulk copies) for MXFP8; no cluster multicast
@@ -19,10 +19,14 @@
 //               fit) and issues the MMAs (M=128, N=BN) from one thread;
 //               tcgen05.commit releases smem stages and signals a finished
 //               accumulator.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (each thread owns
-//               one accumulator row = one TMEM lane), add bias / residual,
-//               optional SiLU(gate)*up on interleaved gate/up weight rows,
-//               convert to bf16 and store; overlaps the next tile's MMAs.
+//   warps 2..9  epilogue, two warps per TMEM lane quarter (one accumulator row
+//               per thread, half of the tile's columns per warp): the warp
+//               copies its share of the accumulator to registers with
+//               tcgen05.ld and releases the TMEM buffer at once, then adds
+//               bias / residual, applies SiLU(gate)*up on interleaved gate/up
+//               weight rows (optionally re-quantising to MXFP8), converts and
+//               stores -- overlapping the next tile's MMAs even when there is
+//               a single accumulator.
 // Work units are (m tile, n tile, k split); m varies fastest so CTAs of one
 // wave share the same weight tile through L2.  With k_splits > 1 the
 // epilogue writes fp32 partials to a workspace and `gemm_splitk_reduce`
@@ -44,6 +48,7 @@ constexpr int kBK = 64;         // bf16 K-elements per stage: one 128-byte swizz
 constexpr int kBKMx = 128;      // e4m3 K-elements per stage: the same 128 bytes
 constexpr int kSfChunk = 512;   // UE8M0 scales of 128 rows x 4 K-chunks of 32
 constexpr int kSfTmemCol = 256; // TMEM column where the MXFP8 scales live
+constexpr int kGemmThreads = 320;  // warp 0 TMA producer, warp 1 MMA issuer, warps 2..9 epilogue
 
 template <int BN, bool MX>
 struct GemmCfg {
@@ -82,7 +87,7 @@ __device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* src, float* v) 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 template <int BN, bool MX>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  GemmParams p) {
   using C = GemmCfg<BN, MX>;
@@ -101,6 +106,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull = bars + 2 * S;
   uint64_t* tempty = bars + 2 * S + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+  uint64_t* xbar = bars + 2 * S + 5;       // the two epilogue warps of a lane quarter exchange row maxima
+  __shared__ float s_amax[256];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -131,8 +138,9 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], 256);
     }
+    mbar_init(xbar, 256);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -243,11 +251,17 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    // ---------------------------------------------------------------- epilogue (warps 2..9)
+    // Two warps per TMEM lane quarter, each owning half of the tile's columns.  A warp
+    // first pulls its whole share of the accumulator into registers and releases the
+    // TMEM buffer, then does bias / residual / activation / conversion and the stores
+    // while the MMA warp already accumulates the next tile into it.
     const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;       // column half of the tile
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t aph = 0;
+    uint32_t xph = 0;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
       const int ks = u % p.k_splits;
       const int t = u / p.k_splits;
@@ -258,153 +272,138 @@ __global__ void __launch_bounds__(192, 1)
       const int row = mb * kBM + row_in_tile;
       const bool row_ok = row < (G ? s_grp[G + 1 + group_of(mb)] : p.M);
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      if (p.k_splits > 1) {
-        float* dst = p.partial + (static_cast<size_t>(ks) * p.M + row) * p.N;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tacc + c * 32, r);
-          tmem_ld_wait();
-          const int col0 = nb * BN + c * 32;
-          if (row_ok) {
+      if (p.epi == kEpiSiluMul || p.epi == kEpiSiluMulMx) {
+        // gate/up rows interleaved in 64-row blocks: tile column pair pr holds [gate 64 | up 64];
+        // this warp takes the 32-column sub-chunk `half` of every pair
+        constexpr int NI = BN / 128 > 0 ? BN / 128 : 1;
+        uint32_t g[NI][32], v[NI][32];
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              if (col0 + j < p.N) {
-                float4 f = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                       __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-                *reinterpret_cast<float4*>(dst + col0 + j) = f;
-              }
+        for (int it = 0; it < NI; ++it) {
+          tmem_ld_32x32b_x32(tacc + it * 128 + half * 32, g[it]);
+          tmem_ld_32x32b_x32(tacc + it * 128 + 64 + half * 32, v[it]);
+        }
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        float o[NI][32];
+        float amax = 0.f;
+#pragma unroll
+        for (int it = 0; it < NI; ++it) {
+          const int gcol = nb * BN + it * 128 + half * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float a = __uint_as_float(g[it][j]);
+            float b = __uint_as_float(v[it][j]);
+            if (p.bias && gcol < p.N) {
+              a += bf2f(p.bias[gcol + j]);
+              b += bf2f(p.bias[gcol + 64 + j]);
             }
+            o[it][j] = silu(a) * b;
+            amax = fmaxf(amax, fabsf(o[it][j]));
           }
         }
-      } else if (p.epi == kEpiSiluMul) {
-        // tile columns: [gate 64 | up 64] pairs -> BN/2 outputs
-#pragma unroll 1
-        for (int pr = 0; pr < BN / 128; ++pr) {
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            uint32_t g[32], v[32];
-            tmem_ld_32x32b_x32(tacc + pr * 128 + h * 32, g);
-            tmem_ld_32x32b_x32(tacc + pr * 128 + 64 + h * 32, v);
-            tmem_ld_wait();
-            const int gcol = nb * BN + pr * 128 + h * 32;
-            const int ocol = nb * (BN / 2) + pr * 64 + h * 32;
-            if (row_ok && gcol < p.N) {
-              float o[32];
+        if (p.epi == kEpiSiluMul) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                float a = __uint_as_float(g[j]);
-                float b = __uint_as_float(v[j]);
-                if (p.bias) {
-                  a += bf2f(p.bias[gcol + j]);
-                  b += bf2f(p.bias[gcol + 64 + j]);
-                }
-                o[j] = silu(a) * b;
-              }
+          for (int it = 0; it < NI; ++it) {
+            const int gcol = nb * BN + it * 128 + half * 32;
+            const int ocol = nb * (BN / 2) + it * 64 + half * 32;
+            if (row_ok && gcol < p.N) {
               __nv_bfloat16* dst = p.D + static_cast<size_t>(row) * p.ldd + ocol;
 #pragma unroll
-              for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, o + j);
+              for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, o[it] + j);
             }
           }
+        } else if constexpr (BN == 256) {
+          // SiLU(gate)*up as the next MXFP8 operand: the tile's 128 outputs of this row are one
+          // 1x128 scale block, split over the two warps of this lane quarter
+          s_amax[half * 128 + row_in_tile] = amax;
+          mbar_arrive(xbar);
+          if (!mbar_wait(xbar, xph, p.status, kGemmEpilogueTimeout)) break;
+          xph ^= 1;
+          amax = fmaxf(amax, s_amax[(half ^ 1) * 128 + row_in_tile]);
+          float inv;
+          const uint32_t e = ue8m0_scale(amax, &inv);
+          if (row_ok) {
+#pragma unroll
+            for (int it = 0; it < NI; ++it) {
+              uint8_t* dst = p.q_out + static_cast<size_t>(row) * p.ldd + nb * 128 + it * 64 + half * 32;
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint2*>(dst + j) = pack_e4m3x8(o[it] + j, inv);
+            }
+          }
+          if (half == 0) {
+            // rows past M keep the neutral scale (their operand rows are never loaded as data)
+            const int kbo = p.N / 256;      // 128-column scale blocks of the output row
+            *reinterpret_cast<uint32_t*>(p.sf_out + (static_cast<size_t>(mb) * kbo + nb) * kSfChunkBytes +
+                                         sf_offset(row_in_tile, 0)) = (row_ok ? e : 127u) * 0x01010101u;
+          }
         }
-      } else if (p.epi == kEpiSiluMulMx) {
-        // SiLU(gate)*up emitted as the next MXFP8 GEMM's operand.  With BN = 256 the
-        // tile's 128 outputs of this row are exactly one 1x128 scale block: pass 1
-        // finds its absolute maximum, pass 2 recomputes and quantises.
-        if constexpr (BN == 256) {
-          float amax = 0.f;
-#pragma unroll 1
-          for (int pass = 0; pass < 2; ++pass) {
-            float inv = 1.f;
-            uint32_t e = 127u;
-            if (pass == 1) e = ue8m0_scale(amax, &inv);
-#pragma unroll 1
-            for (int pr = 0; pr < 2; ++pr) {
-#pragma unroll 1
-              for (int h = 0; h < 2; ++h) {
-                uint32_t g[32], v[32];
-                tmem_ld_32x32b_x32(tacc + pr * 128 + h * 32, g);
-                tmem_ld_32x32b_x32(tacc + pr * 128 + 64 + h * 32, v);
-                tmem_ld_wait();
-                const int gcol = nb * BN + pr * 128 + h * 32;
-                float o[32];
+      } else {
+        constexpr int NC = BN / 64;          // 32-column chunks in this warp's half
+        uint32_t r[NC][32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  float a = __uint_as_float(g[j]);
-                  float b = __uint_as_float(v[j]);
-                  if (p.bias) {
-                    a += bf2f(p.bias[gcol + j]);
-                    b += bf2f(p.bias[gcol + 64 + j]);
-                  }
-                  o[j] = silu(a) * b;
-                }
-                if (pass == 0) {
+        for (int c = 0; c < NC; ++c) tmem_ld_32x32b_x32(tacc + half * (BN / 2) + c * 32, r[c]);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        const int colh = nb * BN + half * (BN / 2);
+        if (p.k_splits > 1) {
+          float* dst = p.partial + (static_cast<size_t>(ks) * p.M + row) * p.N;
 #pragma unroll
-                  for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(o[j]));
-                } else if (row_ok) {
-                  uint8_t* dst = p.q_out + static_cast<size_t>(row) * p.ldd + nb * 128 + pr * 64 + h * 32;
+          for (int c = 0; c < NC; ++c) {
+            const int col0 = colh + c * 32;
+            if (row_ok) {
 #pragma unroll
-                  for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint2*>(dst + j) = pack_e4m3x8(o + j, inv);
+              for (int j = 0; j < 32; j += 4) {
+                if (col0 + j < p.N) {
+                  float4 f = make_float4(__uint_as_float(r[c][j]), __uint_as_float(r[c][j + 1]),
+                                         __uint_as_float(r[c][j + 2]), __uint_as_float(r[c][j + 3]));
+                  *reinterpret_cast<float4*>(dst + col0 + j) = f;
                 }
               }
             }
-            if (pass == 1) {
-              // rows past M keep the neutral scale (their operand rows are never loaded as data)
-              const int kbo = p.N / 256;            // 128-column scale blocks of the output row
-              *reinterpret_cast<uint32_t*>(p.sf_out + (static_cast<size_t>(mb) * kbo + nb) * kSfChunkBytes +
-                                           sf_offset(row_in_tile, 0)) = (row_ok ? e : 127u) * 0x01010101u;
+          }
+        } else if (p.epi == kEpiPeerRS) {
+          // reduce-scatter: the row goes to its owner's slot for this rank, over NVLink
+          const int owner = row / p.rs_rows;
+          __nv_bfloat16* dst = row_ok ? p.rs_slot[owner] + (static_cast<size_t>(p.tp_rank) * p.rs_rows +
+                                                            (row - owner * p.rs_rows)) * p.N
+                                      : nullptr;
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            const int col0 = colh + c * 32;
+            if (row_ok && col0 < p.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                float o[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[c][j + i]);
+                store_bf16x8(dst + col0 + j, o);
+              }
             }
           }
-        }
-      } else if (p.epi == kEpiPeerRS) {
-        // reduce-scatter: the row goes to its owner's slot for this rank, over NVLink
-        const int owner = row / p.rs_rows;
-        __nv_bfloat16* dst = row_ok ? p.rs_slot[owner] +
-                                          (static_cast<size_t>(p.tp_rank) * p.rs_rows + (row - owner * p.rs_rows)) * p.N
-                                    : nullptr;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tacc + c * 32, r);
-          tmem_ld_wait();
-          const int col0 = nb * BN + c * 32;
-          if (row_ok && col0 < p.N) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              float o[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[j + i]);
-              store_bf16x8(dst + col0 + j, o);
-            }
+          // this warp's 32 rows x half the columns are stored: publish them to each owner they touch
+          __threadfence_system();
+          __syncwarp();
+          const int r0 = mb * kBM + quarter * 32;
+          if (lane == 0 && r0 < p.M) {
+            const int r1 = min(p.M, r0 + 32) - 1;
+            for (int o = r0 / p.rs_rows; o <= r1 / p.rs_rows; ++o)
+              st_release_sys_u32(p.rs_flag[o] + ((static_cast<size_t>(mb) * p.n_tiles + nb) * 8 + quarter * 2 + half) *
+                                                    p.tp_world + p.tp_rank,
+                                 epoch);
           }
-        }
-        // this warp's 32 rows are stored: publish them (per tile quarter) to each owner they touch
-        __threadfence_system();
-        __syncwarp();
-        const int r0 = mb * kBM + quarter * 32;
-        if (lane == 0 && r0 < p.M) {
-          const int r1 = min(p.M, r0 + 32) - 1;
-          for (int o = r0 / p.rs_rows; o <= r1 / p.rs_rows; ++o)
-            st_release_sys_u32(
-                p.rs_flag[o] + ((static_cast<size_t>(mb) * p.n_tiles + nb) * 4 + quarter) * p.tp_world + p.tp_rank,
-                epoch);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tacc + c * 32, r);
-          tmem_ld_wait();
-          const int col0 = nb * BN + c * 32;
-          if (row_ok) {
-            __nv_bfloat16* dst = p.D + static_cast<size_t>(row) * p.ldd;
+        } else if (row_ok) {
+          __nv_bfloat16* dst = p.D + static_cast<size_t>(row) * p.ldd;
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
-              const int col = col0 + j;
+              const int col = colh + c * 32 + j;
               if (col < p.N) {
                 float o[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[j + i]);
+                for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[c][j + i]);
                 if (p.bias) {
                   float b[8];
                   load_bf16x8(p.bias + col, b);
@@ -423,8 +422,6 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
       if (++acc == KS) { acc = 0; aph ^= 1; }
     }
   }
@@ -546,7 +543,7 @@ static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B
     cudaFuncSetAttribute(gemm_tcgen05<BN, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     attr_set = true;
   }
-  gemm_tcgen05<BN, MX><<<grid, 192, C::kSmemBytes, st>>>(ta, tb, p);
+  gemm_tcgen05<BN, MX><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);
   if (p.k_splits > 1) {
     const int ncols_out = p.epi == kEpiSiluMul ? p.N / 2 : p.N;
     const long threads = static_cast<long>(p.M) * (ncols_out / 8);
@@ -624,7 +621,7 @@ int gemm_grouped_launch(const GemmParams& p_in, const void* A, int lda, int64_t 
       cudaFuncSetAttribute(gemm_tcgen05<BNV, MXV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes); \
       attr = true;                                                                                            \
     }                                                                                                         \
-    gemm_tcgen05<BNV, MXV><<<grid, 192, C::kSmemBytes, st>>>(ta, tb, p);                                      \
+    gemm_tcgen05<BNV, MXV><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);                             \
   }
   if (!mx && bn == 256) RZ_GROUPED(256, false)
   else if (!mx && bn == 128) RZ_GROUPED(128, false)

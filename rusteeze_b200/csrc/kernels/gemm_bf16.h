@@ -38,8 +38,8 @@ struct GemmParams {
   // tensor-parallel fusion (sequence-sharded rows: rank o owns rows [o*rs_rows, (o+1)*rs_rows))
   //   kEpiPeerRS: every finished tile row is stored into its owner's slot buffer
   //     rs_slot[o] + ((tp_rank * rs_rows + local row) * N) over NVLink, then each epilogue
-  //     warp releases rs_flag[o][((m_tile * n_tiles + n_tile) * 4 + quarter) * tp_world + tp_rank]
-  //     for its 32 rows;
+  //     warp releases rs_flag[o][((m_tile * n_tiles + n_tile) * 8 + quarter * 2 + column half)
+  //     * tp_world + tp_rank] for its 32 rows x half the tile's columns;
   //   ag_flag != null: before loading an A tile, the producer waits for the
   //     all-gather flags of its rows (one per kAgRowBlock rows, rows < ag_rows).
   __nv_bfloat16* rs_slot[kMaxTpRanks];

@@ -66,14 +66,15 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(RsNormAgParams p) {
         ok = wait_flag_geq(p.moe_flag + static_cast<size_t>(k) * p.rs_rows + li0, epoch, p.status, kCommPeerTimeout);
     }
   } else if (p.reduce) {
-    // tiles of quarter (g0 % 128) / 32 of m-tile g0 / 128, every n tile, every source rank
+    // lane quarter (g0 % 128) / 32 of m-tile g0 / 128: both column halves of every n tile,
+    // from every source rank (one flag per epilogue warp of the producing GEMM)
     const int mt = g0 / 128, q = (g0 % 128) / 32;
-    const int nflags = p.n_tiles * p.world;
+    const int nflags = p.n_tiles * 2 * p.world;
     bool ok = true;
     for (int f = threadIdx.x; f < nflags && ok; f += blockDim.x) {
-      const int nt = f / p.world, src = f % p.world;
-      ok = wait_flag_geq(p.rs_flag + ((static_cast<size_t>(mt) * p.n_tiles + nt) * 4 + q) * p.world + src, epoch,
-                         p.status, kCommPeerTimeout);
+      const int nt = f / (2 * p.world), h = (f / p.world) & 1, src = f % p.world;
+      ok = wait_flag_geq(p.rs_flag + ((static_cast<size_t>(mt) * p.n_tiles + nt) * 8 + q * 2 + h) * p.world + src,
+                         epoch, p.status, kCommPeerTimeout);
     }
   }
   __syncthreads();

@@ -50,7 +50,7 @@ class FusedTP:
         self.max_rs_rows = _up(-(-max_tokens // world), 8)
         self.max_m_tiles = -(-max_tokens // 128) + 1
         self.max_n_tiles = -(-hidden // 64)          # n tiles of a row-parallel output at the smallest tile
-        n_rs_flags = self.max_m_tiles * self.max_n_tiles * 4 * world
+        n_rs_flags = self.max_m_tiles * self.max_n_tiles * 8 * world   # [m tile][n tile][quarter x half][src]
         n_ag_flags = -(-max_tokens // 8) + 16
         n_moe_flags = 8 * self.max_rs_rows                 # [topk <= 8][rs_rows]
         self.off_rs_flag = 0
