@@ -123,6 +123,67 @@ def test_fused_tp_boundary_matches_reference():
         assert err < 2e-2, f"rank {rank} rel err {err}"
 
 
+def _tp_model(arch):
+    from rusteeze_b200.models.config import ModelArchitecture, ModelConfig
+    if arch == "llama":
+        return ModelConfig(name="tp-mid", hidden_size=1024, intermediate_size=2816, num_hidden_layers=2,
+                           num_attention_heads=8, num_key_value_heads=2, vocab_size=32000,
+                           max_position_embeddings=2048)
+    return ModelConfig(name="ep-mid", architecture=ModelArchitecture.MIXTRAL, hidden_size=1024,
+                       intermediate_size=1792, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
+                       vocab_size=32000, max_position_embeddings=2048, num_local_experts=4, num_experts_per_tok=2)
+
+
+def _tp_cfg(tp, backend):
+    from rusteeze_b200.config.config import Config
+    c = Config()
+    c.model.device = "cuda:0"
+    c.model.dtype = "bfloat16"
+    c.model.tensor_parallel_size = tp
+    c.engine.num_gpu_blocks = 256
+    c.engine.max_num_seqs = 8
+    c.engine.max_num_batched_tokens = 1024
+    c.engine.enable_chunked_prefill = True
+    c.engine.comm_backend = backend
+    return c
+
+
+def _tp_prompts():
+    import numpy as np
+    rng = np.random.default_rng(0)
+    return [rng.integers(0, 32000, int(n)).tolist() for n in (50, 130, 20)]
+
+
+def _tp_run(eng, prompts):
+    from rusteeze_b200.core.sampling_params import SamplingParams
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True, logprobs=1)
+    ids = [eng.add_request(None, None, sp, p).request_id for p in prompts]
+    done = {}
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            if o.finished:
+                done[o.request_id] = o.outputs[0]
+    return [(done[i].token_ids, done[i].logprobs[0][done[i].token_ids[0]]) for i in ids]
+
+
+def _tp2_child(backend, arch, q):
+    """Rank 0 of a TP2 engine in a fresh process (torch symmetric memory keys
+    its buffers by a per-process allocation count, so every launch starts clean)."""
+    import faulthandler
+    os.environ["RZ_WORKER_WATCHDOG_S"] = "240"
+    faulthandler.dump_traceback_later(270, exit=True)
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    try:
+        launcher = TPEngineLauncher(_tp_cfg(2, backend), model_config=_tp_model(arch))
+        try:
+            q.put(("ok", _tp_run(launcher.engine(), _tp_prompts())))
+        finally:
+            launcher.shutdown()
+    except BaseException as e:  # noqa: BLE001
+        q.put(("error", repr(e)))
+        raise
+
+
 @pytest.mark.timeout(600)
 @pytest.mark.parametrize("backend,arch", [("nccl", "llama"), ("fused", "llama"), ("nccl", "mixtral"),
                                           ("fused", "mixtral")])
@@ -133,57 +194,18 @@ def test_tp2_engine_matches_tp1(backend, arch):
     expert rows straight into the owners' slots."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    import numpy as np
-    from rusteeze_b200.config.config import Config
-    from rusteeze_b200.core.sampling_params import SamplingParams
+    import torch.multiprocessing as mp
     from rusteeze_b200.engine.llm_engine import LLMEngine
-    from rusteeze_b200.models.config import ModelArchitecture, ModelConfig
-    from rusteeze_b200.parallel.launcher import TPEngineLauncher
-    if arch == "llama":
-        mc = ModelConfig(name="tp-mid", hidden_size=1024, intermediate_size=2816, num_hidden_layers=2,
-                         num_attention_heads=8, num_key_value_heads=2, vocab_size=32000, max_position_embeddings=2048)
-    else:
-        mc = ModelConfig(name="ep-mid", architecture=ModelArchitecture.MIXTRAL, hidden_size=1024,
-                         intermediate_size=1792, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
-                         vocab_size=32000, max_position_embeddings=2048, num_local_experts=4, num_experts_per_tok=2)
-
-    def cfg(tp):
-        c = Config()
-        c.model.device = "cuda:0"
-        c.model.dtype = "bfloat16"
-        c.model.tensor_parallel_size = tp
-        c.engine.num_gpu_blocks = 256
-        c.engine.max_num_seqs = 8
-        c.engine.max_num_batched_tokens = 1024
-        c.engine.enable_chunked_prefill = True
-        c.engine.comm_backend = backend
-        return c
-
-    rng = np.random.default_rng(0)
-    prompts = [rng.integers(0, 32000, int(n)).tolist() for n in (50, 130, 20)]
-    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True, logprobs=1)
-
-    def run(eng):
-        ids = [eng.add_request(None, None, sp, p).request_id for p in prompts]
-        done = {}
-        while eng.has_unfinished_requests():
-            for o in eng.step():
-                if o.finished:
-                    done[o.request_id] = o.outputs[0]
-        return [done[i] for i in ids]
-
-    import faulthandler
-    os.environ["RZ_WORKER_WATCHDOG_S"] = "240"
-    faulthandler.dump_traceback_later(270, exit=False)     # stacks of a stuck rank 0 in the log
-    ref = run(LLMEngine(cfg(1), model_config=mc))
-    launcher = TPEngineLauncher(cfg(2), model_config=mc)
-    try:
-        got = run(launcher.engine())
-    finally:
-        launcher.shutdown()
+    ref = _tp_run(LLMEngine(_tp_cfg(1, backend), model_config=_tp_model(arch)), _tp_prompts())
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_tp2_child, args=(backend, arch, q))
+    p.start()
+    status, got = q.get(timeout=420)
+    p.join(60)
+    assert status == "ok", got
     # bf16 reduction order differs between 1 and 2 ranks: compare the first token exactly and
     # the first-step logprob of the chosen token closely
-    faulthandler.cancel_dump_traceback_later()
-    for a, b in zip(got, ref):
-        assert a.token_ids[0] == b.token_ids[0]
-        assert abs(a.logprobs[0][a.token_ids[0]] - b.logprobs[0][b.token_ids[0]]) < 0.1
+    for (ta, la), (tb, lb) in zip(got, ref):
+        assert ta[0] == tb[0]
+        assert abs(la - lb) < 0.1
