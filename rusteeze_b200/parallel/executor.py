@@ -64,19 +64,32 @@ class PlanChannel:
 class TPExecutor:
     """Drop-in for ModelRunner on rank 0 (`LLMEngine(executor=...)`)."""
 
-    def __init__(self, runner: ModelRunner, channel: PlanChannel):
+    def __init__(self, runner: ModelRunner, channel: PlanChannel, liveness=None):
         self.runner = runner
         self.ch = channel
+        # callable -> list of dead worker ranks (the launcher watches its child processes);
+        # checked before every plan so a dead rank is reported instead of stalling a collective
+        self.liveness = liveness
 
     def __getattr__(self, k):
         return getattr(self.runner, k)
 
+    def _check_workers(self) -> None:
+        if self.liveness is None:
+            return
+        dead = self.liveness()
+        if dead:
+            from rusteeze_b200.core.errors import DistributedError
+            raise DistributedError(f"tensor-parallel worker rank(s) {dead} exited; the engine must be restarted")
+
     def capture_graphs(self, buckets=None) -> None:
+        self._check_workers()
         self.ch.publish(MSG_STEP, {"capture": list(buckets) if buckets is not None else None})
         self.runner.capture_graphs(buckets)
 
     @torch.no_grad()
     def execute(self, so, bm, rows) -> SampleResult:
+        self._check_workers()
         r = self.runner
         meta, T, S, sample_rows = r.prepare(so, bm)
         MB = int(max(1, (int(r.h_seq_lens[:S].max()) + 15) // 16)) if S else 1

@@ -43,7 +43,8 @@ def _model_config(cfg: Config) -> ModelConfig:
     return ModelConfig.from_json_file(mc.path) if mc.path else get_preset(mc.preset or "tiny-llama")
 
 
-def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfig] = None, tag: str = "0"):
+def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfig] = None, tag: str = "0",
+                  liveness=None):
     from rusteeze_b200.engine.llm_engine import LLMEngine, _dtype
     mc = model_config or _model_config(cfg)
     ec = cfg.engine
@@ -90,7 +91,7 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
     ecfg.engine.swap_space_gb = 0.0
     ecfg.model.device = dev
     if info.rank == 0:
-        executor = TPExecutor(runner, channel) if channel is not None else runner
+        executor = TPExecutor(runner, channel, liveness) if channel is not None else runner
         engine = LLMEngine(ecfg, model=model, executor=executor)
         return engine, runner, channel
     return None, runner, channel
@@ -117,7 +118,7 @@ def _spawned_worker(rank: int, world: int, port: int, cfg_dict: dict, mc_dict: O
     from rusteeze_b200.config.config import config_from_dict
     cfg = config_from_dict(cfg_dict)
     mc = ModelConfig(**mc_dict) if mc_dict else None
-    info = init_distributed(device_type=device_type)
+    info = init_distributed(device_type=device_type, timeout_s=float(os.environ.get("RZ_PG_TIMEOUT_S", "120")))
     try:
         tp_worker_main(cfg, info, mc, tag)
     finally:
@@ -144,15 +145,23 @@ class TPEngineLauncher:
             p.start()
         os.environ.update(RANK="0", WORLD_SIZE=str(self.world), LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
                           MASTER_PORT=str(port))
-        info = init_distributed(device_type=self.device_type)
-        self._engine, self.runner, self.channel = tp_rank_setup(cfg, info, model_config, self.tag)
+        info = init_distributed(device_type=self.device_type, timeout_s=float(os.environ.get("RZ_PG_TIMEOUT_S", "120")))
+        self._engine, self.runner, self.channel = tp_rank_setup(cfg, info, model_config, self.tag,
+                                                                liveness=self.dead_workers)
+
+    def dead_workers(self):
+        """Ranks whose worker process has exited."""
+        return [r for r, p in enumerate(self.procs, start=1) if not p.is_alive()]
 
     def engine(self):
         return self._engine
 
     def shutdown(self, timeout: float = 30.0) -> None:
         if self.channel is not None:
-            self._engine.runner.shutdown()
+            try:
+                self._engine.runner.shutdown()
+            except Exception:  # noqa: BLE001 -- a dead worker cannot consume the stop message
+                pass
         # graphs holding NCCL calls must go before the process group, on every rank
         self.runner.release_graphs()
         for p in self.procs:

@@ -353,3 +353,31 @@ def test_prefill_tcgen05_matches_mma_sync_and_oracle(Hq, Hkv, window, softcap):
     assert rel_err(outs[1], r) < 1.5e-2
     assert rel_err(outs[1], outs[0].float()) < 1.5e-2
     assert int(C().status()[0]) == 0
+
+
+def test_bounded_peer_wait_reports_timeout_and_context_survives():
+    """Failure detection on the device without a fault: the fused TP boundary
+    kernel waits for reduce-scatter flags that nothing sets (two 'ranks' whose
+    peer buffers are local tensors).  The wait gives up after ~1 s, the status
+    word reports kCommPeerTimeout (4) and the CUDA context keeps working."""
+    import time
+    H, rs_rows, M = 1024, 8, 16
+    slots = torch.zeros(2 * rs_rows * H, device=DEV, dtype=torch.bfloat16)
+    rs_flag = torch.zeros(4096, device=DEV, dtype=torch.int32)
+    gathers = [torch.zeros(M + 128, H, device=DEV, dtype=torch.bfloat16) for _ in range(2)]
+    ag = [torch.zeros(64, device=DEV, dtype=torch.int32) for _ in range(2)]
+    residual = torch.zeros(rs_rows, H, device=DEV, dtype=torch.bfloat16)
+    w = torch.ones(H, device=DEV, dtype=torch.bfloat16)
+    epoch = torch.zeros(1, device=DEV, dtype=torch.int32)
+    C().status().zero_()
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    C().rs_norm_ag(slots, rs_flag, 1, None, residual, w, 1e-5, 0.0, [g.data_ptr() for g in gathers],
+                   [a.data_ptr() for a in ag], 0, M, rs_rows, epoch, 1, 0, None)
+    torch.cuda.synchronize()
+    dt = time.monotonic() - t0
+    assert int(C().status()[0]) == 4
+    assert 0.5 < dt < 30.0
+    C().status().zero_()
+    x = torch.randn(64, 64, device=DEV)
+    assert torch.allclose((x @ x.t()).cpu(), x.cpu() @ x.cpu().t(), atol=1e-3)

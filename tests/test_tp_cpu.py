@@ -73,3 +73,37 @@ def test_tp2_gloo_mixtral_expert_parallel_matches_single_process():
     finally:
         launcher.shutdown()
     assert got == ref
+
+
+@pytest.mark.timeout(300)
+def test_dead_worker_is_reported_not_hung():
+    """Failure injection on the host: the worker process of a gloo TP2 engine is
+    killed between steps; rank 0's next step raises DistributedError at once
+    (liveness check before the plan is published) instead of blocking in a
+    collective, and shutdown completes."""
+    import os
+    import time
+    from rusteeze_b200.core.errors import DistributedError
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    os.environ["RZ_PG_TIMEOUT_S"] = "20"
+    rng = np.random.default_rng(2)
+    launcher = TPEngineLauncher(_cfg(2), model_config=MC, device_type="cpu")
+    try:
+        eng = launcher.engine()
+        sp = SamplingParams(temperature=0.0, max_tokens=50, ignore_eos=True)
+        eng.add_request(None, None, sp, rng.integers(0, 1000, 20).tolist())
+        for _ in range(3):
+            eng.step()
+        victim = launcher.procs[0]
+        victim.kill()                       # our own child process, by handle
+        victim.join(10)
+        assert launcher.dead_workers() == [1]
+        t0 = time.monotonic()
+        with pytest.raises(DistributedError):
+            eng.step()
+        assert time.monotonic() - t0 < 5.0
+    finally:
+        os.environ.pop("RZ_PG_TIMEOUT_S", None)
+        t1 = time.monotonic()
+        launcher.shutdown(timeout=5.0)
+        assert time.monotonic() - t1 < 60.0
