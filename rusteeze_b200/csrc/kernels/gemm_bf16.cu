@@ -272,7 +272,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = mb * kBM + row_in_tile;
       const bool row_ok = row < (G ? s_grp[G + 1 + group_of(mb)] : p.M);
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      if (p.epi == kEpiSiluMul || p.epi == kEpiSiluMulMx) {
+      if (p.k_splits == 1 && (p.epi == kEpiSiluMul || p.epi == kEpiSiluMulMx)) {
+        // (split-K partials always take the raw fp32 path below; the reduce kernel applies the epilogue)
         // gate/up rows interleaved in 64-row blocks: tile column pair pr holds [gate 64 | up 64];
         // this warp takes the 32-column sub-chunk `half` of every pair
         constexpr int NI = BN / 128 > 0 ? BN / 128 : 1;
