@@ -161,21 +161,32 @@ def init_random(model: DecoderLM, seed: int = 0, std: float = 0.02) -> DecoderLM
 
 # ----------------------------------------------------------------------------- HF checkpoints
 def discover_weight_files(model_dir: str):
-    idx = os.path.join(model_dir, "model.safetensors.index.json")
-    if os.path.exists(idx):
-        with open(idx) as f:
-            files = sorted(set(json.load(f)["weight_map"].values()))
-        return [os.path.join(model_dir, x) for x in files]
-    files = sorted(glob.glob(os.path.join(model_dir, "*.safetensors")))
-    if not files:
-        raise ModelLoadError(f"no *.safetensors files in {model_dir}")
-    return files
+    """safetensors (preferred; sharded via model.safetensors.index.json) or, as
+    the reference's loader also accepts, PyTorch `pytorch_model*.bin` files
+    (sharded via pytorch_model.bin.index.json)."""
+    for index_name, pattern in (("model.safetensors.index.json", "*.safetensors"),
+                                ("pytorch_model.bin.index.json", "pytorch_model*.bin")):
+        idx = os.path.join(model_dir, index_name)
+        if os.path.exists(idx):
+            with open(idx) as f:
+                files = sorted(set(json.load(f)["weight_map"].values()))
+            return [os.path.join(model_dir, x) for x in files]
+        files = sorted(glob.glob(os.path.join(model_dir, pattern)))
+        if files:
+            return files
+    raise ModelLoadError(f"no *.safetensors or pytorch_model*.bin files in {model_dir}")
 
 
 class _TensorIndex:
     def __init__(self, files):
-        from safetensors import safe_open
-        self.handles = [safe_open(f, framework="pt", device="cpu") for f in files]
+        self.handles = []
+        for f in files:
+            if f.endswith(".safetensors"):
+                from safetensors import safe_open
+                self.handles.append(safe_open(f, framework="pt", device="cpu"))
+            else:
+                # PyTorch pickles are loaded tensor-only (no code execution) and memory-mapped
+                self.handles.append(torch.load(f, map_location="cpu", weights_only=True, mmap=True))
         self.where: Dict[str, int] = {}
         for i, h in enumerate(self.handles):
             for k in h.keys():
@@ -187,7 +198,8 @@ class _TensorIndex:
     def get(self, k: str) -> torch.Tensor:
         if k not in self.where:
             raise ModelLoadError(f"missing weight {k}")
-        return self.handles[self.where[k]].get_tensor(k)
+        h = self.handles[self.where[k]]
+        return h[k] if isinstance(h, dict) else h.get_tensor(k)
 
 
 def _hf_full(ix: _TensorIndex, cfg: ModelConfig, name: str) -> torch.Tensor:

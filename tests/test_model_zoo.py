@@ -71,6 +71,29 @@ def test_hf_checkpoint_roundtrip(tmp_path, arch):
     assert torch.allclose(naive_logits(m, p), naive_logits(m2, p), atol=1e-5)
 
 
+def test_pytorch_bin_checkpoint_loads(tmp_path):
+    """The same weights saved as sharded pytorch_model-*.bin files (with index) load identically."""
+    import json
+    from safetensors.torch import load_file
+    mc = tiny_variant(A.LLAMA)
+    m = build_model(mc, dtype=torch.float32, seed=6)
+    st = tmp_path / "st"
+    save_hf_checkpoint(m, str(st), shard_bytes=200_000)
+    out = tmp_path / "bin"
+    out.mkdir()
+    (out / "config.json").write_text((st / "config.json").read_text())
+    wm = {}
+    for j, f in enumerate(sorted(st.glob("*.safetensors"))):
+        name = f"pytorch_model-{j + 1:05d}-of-00099.bin"
+        tensors = load_file(str(f))
+        torch.save(tensors, out / name)
+        wm.update({k: name for k in tensors})
+    (out / "pytorch_model.bin.index.json").write_text(json.dumps({"weight_map": wm}))
+    m2 = build_model(ModelConfig.from_json_file(str(out)), dtype=torch.float32, model_dir=str(out))
+    p = [7, 1, 8, 2, 8]
+    assert torch.allclose(naive_logits(m, p), naive_logits(m2, p), atol=1e-5)
+
+
 class _FakeTP(TPGroup):
     def __init__(self, rank, size):
         self.rank, self.size = rank, size
