@@ -18,7 +18,6 @@ from __future__ import annotations
 
 import json
 import os
-import signal
 import time
 import uuid
 from typing import AsyncIterator, List, Optional

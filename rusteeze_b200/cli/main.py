@@ -192,7 +192,6 @@ def cmd_benchmark(a) -> int:
     tokens with EOS ignored), at most --concurrency in flight; device-timed
     where the engine runs on CUDA.  Reports output tok/s, TTFT/TPOT p50/p99."""
     import numpy as np
-    import statistics
     from rusteeze_b200.core.sampling_params import SamplingParams
     cfg = _load_config(a, {"engine": {"max_num_seqs": max(a.concurrency, 1),
                                       "max_num_batched_tokens": max(8192, a.concurrency)}})

@@ -26,7 +26,7 @@ from __future__ import annotations
 import enum
 from collections import deque
 from dataclasses import dataclass, field
-from typing import Deque, List, Optional, Tuple
+from typing import Deque, List, Tuple
 
 from rusteeze_b200.core.types import RequestStatus
 from rusteeze_b200.engine.sequence import Sequence

@@ -29,7 +29,7 @@ from __future__ import annotations
 import dataclasses
 import logging
 import time
-from typing import Dict, List
+from typing import Dict
 
 import numpy as np
 import torch

@@ -28,7 +28,7 @@ head/column, row split of o/down, vocab split of embedding and LM head).
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import List, Optional
 
 import torch

@@ -21,7 +21,7 @@ import logging
 import os
 import pickle
 import time
-from typing import List, Optional, Tuple
+from typing import Optional, Tuple
 
 import numpy as np
 import torch

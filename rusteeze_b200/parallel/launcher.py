@@ -15,7 +15,7 @@ import copy
 import logging
 import os
 import socket
-from typing import Optional, Tuple
+from typing import Optional
 
 import torch
 import torch.distributed as dist

@@ -28,7 +28,7 @@ from __future__ import annotations
 import re
 import time
 from dataclasses import dataclass, field
-from typing import Any, List, Optional, Tuple
+from typing import List, Optional, Tuple
 
 from rusteeze_b200.rlm.variable_store import VariableStore
 

@@ -21,10 +21,10 @@ from __future__ import annotations
 
 import time
 from dataclasses import dataclass, field
-from typing import Callable, Dict, List, Optional, Protocol, Tuple
+from typing import Dict, List, Optional, Protocol, Tuple
 
-from rusteeze_b200.rlm.prompt_env import (EnvLimits, ExecResult, PendingSubcall, PromptEnvironment,
-                                          adaptive_chunk, parse_model_output)
+from rusteeze_b200.rlm.prompt_env import (EnvLimits, ExecResult, PromptEnvironment, adaptive_chunk,
+                                          parse_model_output)
 from rusteeze_b200.rlm.recursive_scheduler import RecursiveScheduler, SchedulerLimits
 
 SYSTEM_PROMPT = """You are operating a REPL over a long prompt stored in variable __prompt__.
