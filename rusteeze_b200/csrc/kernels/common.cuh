@@ -117,6 +117,33 @@ RZ_DEVICE bool wait_flag_geq(const uint32_t* flag, uint32_t target, int* status,
     }
   }
 }
+RZ_DEVICE uint32_t ld_relaxed_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+RZ_DEVICE void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Spin until every flag in [flags, flags + n) is >= target.  The flags are polled with
+// relaxed loads (independent, so their latencies overlap) and one system-scope fence
+// after they are all seen gives the acquire ordering.  Bounded by kWaitTimeoutNs.
+RZ_DEVICE bool wait_flags_geq(const uint32_t* flags, int n, uint32_t target, int* status, int code) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    bool all = true;
+    for (int i = 0; i < n; ++i) all &= ld_relaxed_sys_u32(flags + i) >= target;
+    if (all) {
+      fence_acq_rel_sys();
+      return true;
+    }
+    if (it == 0) t0 = globaltimer();
+    else if ((it & 15u) == 15u && globaltimer() - t0 > kWaitTimeoutNs) {
+      set_status(status, code);
+      return false;
+    }
+  }
+}
+
 // order generic-proxy writes (peer stores observed through an acquire) before
 // later async-proxy (TMA) reads of global memory
 RZ_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }

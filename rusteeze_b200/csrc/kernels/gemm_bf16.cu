@@ -60,8 +60,10 @@ struct GemmCfg {
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // bytes landing per stage
   static constexpr int kAccStages = (MX && BN == 256) ? 1 : 2;
   static constexpr int kTmemCols = MX ? 512 : (2 * BN < 32 ? 32 : 2 * BN);
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kOutStageBytes = 8 * 32 * 64;   // epilogue transpose: 8 warps x 32 rows x 32 bf16
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kOutStageBytes;
   static_assert(!MX || BN >= 128, "MXFP8 tiles cover whole 128-row scale chunks");
+  static_assert(kSmemBytes <= 227 * 1024 - 2048, "dynamic + static shared memory must fit one CTA");
   static_assert(!MX || kAccStages * BN <= kSfTmemCol, "accumulators overlap the scale columns");
 };
 
@@ -107,6 +109,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = bars + 2 * S + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
   uint64_t* xbar = bars + 2 * S + 5;       // the two epilogue warps of a lane quarter exchange row maxima
+  uint4* sm_out = reinterpret_cast<uint4*>(smem + S * C::kStageBytes + 256);
   __shared__ float s_amax[256];
 
   const int warp = threadIdx.x >> 5;
@@ -157,20 +160,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
+      uint64_t ag_ready = 0;                 // m tiles whose all-gathered rows were already seen
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int ks = u % p.k_splits;
         const int t = u / p.k_splits;
         const int mb = t % m_tiles;
         const int nb = t / m_tiles;
         const int b_row0 = (G ? group_of(mb) * p.N : 0) + nb * BN;
-        if (p.ag_flag) {
-          // all-gathered A rows arrive from their owners: wait for this tile's row blocks
+        if (p.ag_flag && !(mb < 64 && ((ag_ready >> mb) & 1ull))) {
+          // all-gathered A rows arrive from their owners: wait (once per m tile) for this
+          // tile's row blocks, polling all of its flags together
           const int rb0 = mb * kBM / kAgRowBlock;
           const int rb1 = min((p.ag_rows + kAgRowBlock - 1) / kAgRowBlock, (mb + 1) * kBM / kAgRowBlock);
-          for (int rb = rb0; rb < rb1 && ok; ++rb)
-            ok = wait_flag_geq(p.ag_flag + rb, epoch, p.status, kCommPeerTimeout);
+          ok = wait_flags_geq(p.ag_flag + rb0, rb1 - rb0, epoch, p.status, kCommPeerTimeout);
           fence_proxy_async_global();
           if (!ok) break;
+          if (mb < 64) ag_ready |= 1ull << mb;
         }
         const int kb0 = ks * p.kb_per_split;
         const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
@@ -365,28 +370,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         } else if (p.epi == kEpiPeerRS) {
-          // reduce-scatter: the row goes to its owner's slot for this rank, over NVLink
-          const int owner = row / p.rs_rows;
-          __nv_bfloat16* dst = row_ok ? p.rs_slot[owner] + (static_cast<size_t>(p.tp_rank) * p.rs_rows +
-                                                            (row - owner * p.rs_rows)) * p.N
-                                      : nullptr;
+          // reduce-scatter: each row goes to its owner's slot for this rank, over NVLink.
+          // Every 32-column chunk is transposed through shared memory (16-byte units
+          // XOR-swizzled by row pair, conflict-free both ways) so that 4 lanes store 64
+          // contiguous bytes of one row: 64-byte peer writes instead of 16-byte ones.
+          uint4* stg = sm_out + (warp - 2) * 128;
+          const int r0 = mb * kBM + quarter * 32;
 #pragma unroll
           for (int c = 0; c < NC; ++c) {
             const int col0 = colh + c * 32;
-            if (row_ok && col0 < p.N) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                float o[8];
+            for (int j = 0; j < 4; ++j) {
+              float o[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[c][j + i]);
-                store_bf16x8(dst + col0 + j, o);
+              for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(r[c][j * 8 + i]);
+              uint4 u;
+              __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) h2[i] = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+              stg[lane * 4 + (j ^ ((lane >> 1) & 3))] = u;
+            }
+            __syncwarp();
+#pragma unroll
+            for (int ps = 0; ps < 4; ++ps) {
+              const int rr = ps * 8 + (lane >> 2), j = lane & 3;
+              const int grow = r0 + rr, gcol = col0 + j * 8;
+              const uint4 v = stg[rr * 4 + (j ^ ((rr >> 1) & 3))];
+              if (grow < p.M && gcol < p.N) {
+                const int owner = grow / p.rs_rows;
+                *reinterpret_cast<uint4*>(p.rs_slot[owner] +
+                                          (static_cast<size_t>(p.tp_rank) * p.rs_rows + (grow - owner * p.rs_rows)) *
+                                              p.N + gcol) = v;
               }
             }
+            __syncwarp();
           }
           // this warp's 32 rows x half the columns are stored: publish them to each owner they touch
           __threadfence_system();
           __syncwarp();
-          const int r0 = mb * kBM + quarter * 32;
           if (lane == 0 && r0 < p.M) {
             const int r1 = min(p.M, r0 + 32) - 1;
             for (int o = r0 / p.rs_rows; o <= r1 / p.rs_rows; ++o)

@@ -50,20 +50,27 @@ __device__ __forceinline__ uint4 pack8f(const float* v) {
   return u;
 }
 
-// 8 warps per block, one own row per warp; block b covers rows [row0 + 8b, row0 + 8b + 8)
-__global__ void __launch_bounds__(256) rs_norm_ag_kernel(RsNormAgParams p) {
+// 16 warps per block, 2 warps (64 threads) per own row; block b covers rows
+// [row0 + 8b, row0 + 8b + 8).  Thread t of a row owns the 8-column chunks
+// t, t + 64, ...: CH chunks (H <= CH * 512), kept in registers between the
+// sum, the norm and the all-gather so the residual is read once.
+constexpr int kRsThreads = 512;
+constexpr int kRsRowThreads = 64;
+
+template <int CH>
+__global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p) {
   const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u;
   const int own0 = p.rank * p.rs_rows;
   const int g0 = own0 + blockIdx.x * kAgRowBlock;          // first global row of this block
   if (p.reduce && p.moe_topk > 0) {
     // every (row, slot) of this block was written by the rank that owns the slot's expert
     const int nflags = kAgRowBlock * p.moe_topk;
-    bool ok = true;
-    for (int f = threadIdx.x; f < nflags && ok; f += blockDim.x) {
+    const int f = threadIdx.x;
+    if (f < nflags) {
       const int rr = f / p.moe_topk, k = f % p.moe_topk;
       const int li0 = g0 - own0 + rr;
       if (g0 + rr < p.M && li0 < p.rs_rows)
-        ok = wait_flag_geq(p.moe_flag + static_cast<size_t>(k) * p.rs_rows + li0, epoch, p.status, kCommPeerTimeout);
+        wait_flag_geq(p.moe_flag + static_cast<size_t>(k) * p.rs_rows + li0, epoch, p.status, kCommPeerTimeout);
     }
   } else if (p.reduce) {
     // lane quarter (g0 % 128) / 32 of m-tile g0 / 128: both column halves of every n tile,
@@ -78,42 +85,69 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(RsNormAgParams p) {
     }
   }
   __syncthreads();
+  static_assert(kRsThreads / kRsRowThreads == kAgRowBlock, "one row per 128 threads, one flag block per CTA");
+  __shared__ float s_ss[kAgRowBlock][kRsRowThreads / 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = g0 + warp;                                 // global row
+  const int rr = warp >> 1, sub = warp & 1;                  // row of the block, warp within the row
+  const int tr = sub * 32 + lane;                            // thread within the row
+  const int row = g0 + rr;                                   // global row
   const int li = row - own0;                                 // row within this rank's shard
-  if (row < p.M && li < p.rs_rows) {
+  const bool live = row < p.M && li < p.rs_rows;
+  uint4 xr[CH];                                              // the rounded residual, bf16
+  float ss = 0.f;
+  if (live) {
     __nv_bfloat16* res = p.residual + static_cast<size_t>(li) * p.H;
-    float ss = 0.f;
-    for (int c = lane * 8; c < p.H; c += 256) {
-      float x[8], t[8];
-      if (p.reduce) {
-        ld8f(res + c, x);
-        const int nsrc = p.moe_topk > 0 ? p.moe_topk : p.world;
-        for (int s = 0; s < nsrc; ++s) {
-          ld8f(p.slots + (static_cast<size_t>(s) * p.rs_rows + li) * p.H + c, t);
+    const int nsrc = p.reduce ? (p.moe_topk > 0 ? p.moe_topk : p.world) : 0;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) x[i] += t[i];
+    for (int j = 0; j < CH; ++j) {
+      const int c = (tr + j * kRsRowThreads) * 8;
+      if (c < p.H) {
+        float x[8], t[8];
+        if (p.reduce) {
+          ld8f(res + c, x);
+          for (int s = 0; s < nsrc; ++s) {
+            ld8f(p.slots + (static_cast<size_t>(s) * p.rs_rows + li) * p.H + c, t);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[i] += t[i];
+          }
+        } else {
+          ld8f(p.resid_in + static_cast<size_t>(row) * p.H + c, x);
         }
-      } else {
-        ld8f(p.resid_in + static_cast<size_t>(row) * p.H + c, x);
+        xr[j] = pack8f(x);
+        *reinterpret_cast<uint4*>(res + c) = xr[j];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xr[j]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {                        // normalise the rounded residual
+          const float2 f = __bfloat1622float2(h[i]);
+          ss += f.x * f.x + f.y * f.y;
+        }
       }
-      const uint4 r = pack8f(x);
-      *reinterpret_cast<uint4*>(res + c) = r;
-      ld8f(res + c, x);                                      // normalise the rounded residual
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
     }
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / p.H + p.eps);
-    for (int c = lane * 8; c < p.H; c += 256) {
-      float x[8], w[8];
-      ld8f(res + c, x);
-      ld8f(p.w + c, w);
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) s_ss[rr][sub] = ss;
+  __syncthreads();
+  if (live) {
+    const float inv = rsqrtf((s_ss[rr][0] + s_ss[rr][1]) / p.H + p.eps);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = x[i] * inv * (w[i] + p.offset);
-      const uint4 o = pack8f(x);
-      for (int d = 0; d < p.world; ++d)
-        *reinterpret_cast<uint4*>(p.gather[d] + static_cast<size_t>(row) * p.H + c) = o;
+    for (int j = 0; j < CH; ++j) {
+      const int c = (tr + j * kRsRowThreads) * 8;
+      if (c < p.H) {
+        float x[8], w[8];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xr[j]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h[i]);
+          x[2 * i] = f.x;
+          x[2 * i + 1] = f.y;
+        }
+        ld8f(p.w + c, w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = x[i] * inv * (w[i] + p.offset);
+        const uint4 o = pack8f(x);
+        for (int d = 0; d < p.world; ++d)
+          *reinterpret_cast<uint4*>(p.gather[d] + static_cast<size_t>(row) * p.H + c) = o;
+      }
     }
   }
   __threadfence_system();
@@ -175,10 +209,17 @@ int ag_wait_launch(const uint32_t* ag_flag, int M, const uint32_t* epoch_ptr, ui
 }
 
 int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st) {
-  if (p.rs_rows % kAgRowBlock != 0 || p.H % 256 != 0 || p.world > kMaxTpRanks) return -1;
+  if (p.rs_rows % kAgRowBlock != 0 || p.H % 8 != 0 || p.H > kRsNormAgMaxH || p.world > kMaxTpRanks ||
+      kAgRowBlock * p.moe_topk > kRsThreads)
+    return -1;
   const int own = min(p.M, (p.rank + 1) * p.rs_rows) - p.rank * p.rs_rows;
   if (own <= 0) return 0;
-  rs_norm_ag_kernel<<<(own + kAgRowBlock - 1) / kAgRowBlock, 256, 0, st>>>(p);
+  const dim3 grid((own + kAgRowBlock - 1) / kAgRowBlock);
+  const int ch = (p.H / 8 + kRsRowThreads - 1) / kRsRowThreads;
+  if (ch <= 4) rs_norm_ag_kernel<4><<<grid, kRsThreads, 0, st>>>(p);
+  else if (ch <= 8) rs_norm_ag_kernel<8><<<grid, kRsThreads, 0, st>>>(p);
+  else if (ch <= 12) rs_norm_ag_kernel<12><<<grid, kRsThreads, 0, st>>>(p);
+  else rs_norm_ag_kernel<16><<<grid, kRsThreads, 0, st>>>(p);
   return static_cast<int>(cudaGetLastError());
 }
 

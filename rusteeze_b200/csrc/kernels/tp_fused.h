@@ -8,6 +8,8 @@
 
 namespace rz {
 
+constexpr int kRsNormAgMaxH = 8192;   // hidden sizes the add+RMSNorm+all-gather kernel holds in registers
+
 struct RsNormAgParams {
   const __nv_bfloat16* slots;          // local slot buffer [world][rs_rows][H]
   const uint32_t* rs_flag;             // local reduce-scatter flags [m tiles][n_tiles][4][world]

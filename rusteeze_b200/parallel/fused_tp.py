@@ -90,7 +90,8 @@ class FusedTP:
         return _up(-(-M // self.world), 8)
 
     def fits(self, M: int) -> bool:
-        return 0 < M <= self.max_tokens
+        # the add+RMSNorm+all-gather kernel keeps a row in registers: hidden <= 8192, 8-column chunks
+        return 0 < M <= self.max_tokens and self.hidden <= 8192 and self.hidden % 8 == 0
 
     # ------------------------------------------------------------------ ops
     def start(self, h: torch.Tensor, norm_w: torch.Tensor, eps: float, offset: float) -> torch.Tensor:

@@ -75,8 +75,37 @@ def main() -> int:
             F.start(h0, w_n, 1e-5, 0.0)
             F.end_step()
 
+        def local_o():
+            ops.linear(x, w_o)
+
+        def local_qkv():
+            ops.linear(h0, w_qkv)
+
         out = {"M": M, "world": W}
-        for name, fn in (("fused", fused), ("baseline", baseline), ("start", start_only)):
+        # per-kernel split of the fused chain: events between its launches on the stream
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        split = [0.0, 0.0, 0.0]
+        for it in range(a.warmup + a.iters):
+            F.start(h0, w_n, 1e-5, 0.0)
+            ev[0].record()
+            F.gemm_rs(x, w_o, 1)
+            ev[1].record()
+            gg = F.rs_norm_ag(M, w_n, 1e-5, 0.0, 1)
+            ev[2].record()
+            F.gemm_ag(gg, w_qkv, 1)
+            ev[3].record()
+            F.end_step()
+            torch.cuda.synchronize()
+            dist.barrier()
+            if it >= a.warmup:
+                for i in range(3):
+                    split[i] += ev[i].elapsed_time(ev[i + 1]) / a.iters
+        st = torch.tensor(split, device=dev)
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        out.update(gemm_rs_ms=round(st[0].item(), 4), rs_norm_ag_ms=round(st[1].item(), 4),
+                   gemm_ag_ms=round(st[2].item(), 4))
+        for name, fn in (("fused", fused), ("baseline", baseline), ("start", start_only),
+                         ("local_o_gemm", local_o), ("local_qkv_gemm", local_qkv)):
             for _ in range(a.warmup):
                 fn()
             dist.barrier()
