@@ -504,7 +504,7 @@ int64_t gemm_peer_rs(torch::Tensor x, torch::Tensor w, std::vector<int64_t> slot
   TORCH_CHECK(w.size(1) == K && K % 8 == 0 && N % 8 == 0 && rs_rows % rz::kAgRowBlock == 0 &&
                   static_cast<int64_t>(rs_rows) * world >= M,
               "gemm_peer_rs: shapes");
-  if (bn <= 0) bn = rz::plan_gemm(M, N, K, 0).bn;
+  if (bn <= 0) bn = rz::plan_gemm(M, N, K, 0, /*max_splits=*/1).bn;   // the epilogue stores final rows
   rz::GemmParams p{};
   p.M = M; p.N = N; p.K = K;
   p.k_splits = 1;

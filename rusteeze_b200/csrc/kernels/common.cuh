@@ -127,6 +127,13 @@ RZ_DEVICE void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memo
 // Spin until every flag in [flags, flags + n) is >= target.  The flags are polled with
 // relaxed loads (independent, so their latencies overlap) and one system-scope fence
 // after they are all seen gives the acquire ordering.  Bounded by kWaitTimeoutNs.
+// Programmatic dependent launch.  A kernel that calls pdl_trigger() lets the next kernel
+// on its stream (launched with the programmatic-serialization attribute) start once
+// every CTA of this grid has started; such a dependent synchronises on flags, and calls
+// pdl_wait() before it exits so that its completion still implies this grid's.
+RZ_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+RZ_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 RZ_DEVICE bool wait_flags_geq(const uint32_t* flags, int n, uint32_t target, int* status, int code) {
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {

@@ -128,6 +128,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_units = m_tiles * p.n_tiles * p.k_splits;
   const uint32_t epoch =
       p.epoch_ptr ? *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u : 0u;
+  // GEMMs that feed or consume a collective finish whole m tiles first: the reduce-scatter
+  // consumer and the all-gather producer both work in row blocks
+  const bool row_major = p.epi == kEpiPeerRS || p.ag_flag != nullptr;
+  pdl_trigger();
   auto group_of = [&](int mb) {
     int g = 0;
     while (g + 1 < G && s_grp[g + 1] <= mb * kBM) ++g;
@@ -164,8 +168,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int ks = u % p.k_splits;
         const int t = u / p.k_splits;
-        const int mb = t % m_tiles;
-        const int nb = t / m_tiles;
+        const int mb = row_major ? t / p.n_tiles : t % m_tiles;
+        const int nb = row_major ? t % p.n_tiles : t / m_tiles;
         const int b_row0 = (G ? group_of(mb) * p.N : 0) + nb * BN;
         if (p.ag_flag && !(mb < 64 && ((ag_ready >> mb) & 1ull))) {
           // all-gathered A rows arrive from their owners: wait (once per m tile) for this
@@ -261,6 +265,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // first pulls its whole share of the accumulator into registers and releases the
     // TMEM buffer, then does bias / residual / activation / conversion and the stores
     // while the MMA warp already accumulates the next tile into it.
+    // Launched as a programmatic dependent (the all-gather consumer), the TMA and MMA
+    // warps start on gathered rows while the previous kernels still run, but nothing is
+    // stored before they completed: the output and split-K buffers come from the caching
+    // allocator, which may hand out memory those kernels still read.
+    pdl_wait();
     const int quarter = warp & 3;           // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;       // column half of the tile
     const int row_in_tile = quarter * 32 + lane;
@@ -270,8 +279,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
       const int ks = u % p.k_splits;
       const int t = u / p.k_splits;
-      const int mb = t % m_tiles;
-      const int nb = t / m_tiles;
+      const int mb = row_major ? t / p.n_tiles : t % m_tiles;
+      const int nb = row_major ? t % p.n_tiles : t / m_tiles;
       if (!mbar_wait(&tfull[acc], aph, p.status, kGemmEpilogueTimeout)) break;
       tc_fence_after();
       const int row = mb * kBM + row_in_tile;
@@ -405,10 +414,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             __syncwarp();
           }
-          // this warp's 32 rows x half the columns are stored: publish them to each owner they touch
-          __threadfence_system();
+          // this warp's 32 rows x half the columns are stored: publish them to each owner they
+          // touch (the warp barrier orders all lanes' stores before lane 0's fence + release)
           __syncwarp();
           if (lane == 0 && r0 < p.M) {
+            __threadfence_system();
             const int r1 = min(p.M, r0 + 32) - 1;
             for (int o = r0 / p.rs_rows; o <= r1 / p.rs_rows; ++o)
               st_release_sys_u32(p.rs_flag[o] + ((static_cast<size_t>(mb) * p.n_tiles + nb) * 8 + quarter * 2 + half) *
@@ -452,6 +462,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
+  pdl_wait();   // a programmatic dependent completes only after its primary grid
 }
 
 // Sums k-split partials and applies the epilogue.  One thread per 8 output columns.
@@ -565,7 +576,24 @@ static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B
     cudaFuncSetAttribute(gemm_tcgen05<BN, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     attr_set = true;
   }
-  gemm_tcgen05<BN, MX><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);
+  if (p.ag_flag) {
+    // the A rows are guarded by all-gather flags: start while the previous kernel (the
+    // add+RMSNorm+all-gather) is still running, as soon as all of its CTAs are resident
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05<BN, MX>, ta, tb, p);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  } else {
+    gemm_tcgen05<BN, MX><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);
+  }
   if (p.k_splits > 1) {
     const int ncols_out = p.epi == kEpiSiluMul ? p.N / 2 : p.N;
     const long threads = static_cast<long>(p.M) * (ncols_out / 8);
@@ -574,8 +602,8 @@ static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B
   return static_cast<int>(cudaGetLastError());
 }
 
-GemmPlan plan_gemm(int M, int N, int K, int epi) {
-  // Pick (BN, k_splits) minimising an estimate of waves x per-unit cost.
+GemmPlan plan_gemm(int M, int N, int K, int epi, int max_splits) {
+  // Pick (BN, k_splits <= max_splits) minimising an estimate of waves x per-unit cost.
   const int sms = num_sms();
   const int kblocks = (K + kBK - 1) / kBK;
   GemmPlan best{256, 1, 1e30};
@@ -584,7 +612,7 @@ GemmPlan plan_gemm(int M, int N, int K, int epi) {
     if (epi == kEpiSiluMul && bn < 128) continue;
     const int mt = (M + kBM - 1) / kBM;
     const int nt = (N + bn - 1) / bn;
-    for (int ks = 1; ks <= 16; ks *= 2) {
+    for (int ks = 1; ks <= max_splits; ks *= 2) {
       if (ks > 1 && kblocks / ks < 4) break;
       const int units = mt * nt * ks;
       const int waves = (units + sms - 1) / sms;

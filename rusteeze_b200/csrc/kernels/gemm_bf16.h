@@ -62,7 +62,7 @@ struct GemmPlan {
   double cost;
 };
 
-GemmPlan plan_gemm(int M, int N, int K, int epi);
+GemmPlan plan_gemm(int M, int N, int K, int epi, int max_splits = 16);
 __global__ void gemm_splitk_reduce(GemmParams p);
 int gemm_bf16_launch(const GemmParams& p, const void* A, int lda, const void* B, int ldb, int bn,
                      cudaStream_t stream);

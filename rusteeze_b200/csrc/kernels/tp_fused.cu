@@ -59,6 +59,10 @@ constexpr int kRsRowThreads = 64;
 
 template <int CH>
 __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p) {
+  // With reduce, this kernel is a programmatic dependent of the reduce-scatter GEMM: its
+  // blocks take the SMs that GEMM CTAs leave and finish rows as their m tiles land (every
+  // input is flag-guarded; every output is a persistent buffer no earlier kernel reads).
+  pdl_trigger();
   const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u;
   const int own0 = p.rank * p.rs_rows;
   const int g0 = own0 + blockIdx.x * kAgRowBlock;          // first global row of this block
@@ -150,9 +154,14 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
       }
     }
   }
-  __threadfence_system();
+  // publish: the block barrier orders every thread's stores before the flag thread's
+  // system-scope fence + release (cumulative), so one fence per destination suffices
   __syncthreads();
-  if (threadIdx.x < p.world && g0 < p.M) st_release_sys_u32(p.ag_flag[threadIdx.x] + g0 / kAgRowBlock, epoch);
+  if (threadIdx.x < p.world && g0 < p.M) {
+    __threadfence_system();
+    st_release_sys_u32(p.ag_flag[threadIdx.x] + g0 / kAgRowBlock, epoch);
+  }
+  pdl_wait();   // complete only after the primary grid
 }
 
 __global__ void tp_epoch_bump_kernel(uint32_t* ep) { *ep += 1u; }
@@ -177,9 +186,11 @@ __global__ void __launch_bounds__(256) moe_combine_peer_kernel(MoeCombinePeerPar
       for (int j = 0; j < 8; ++j) v[j] *= w;
       *reinterpret_cast<uint4*>(dst + c) = pack8f(v);
     }
-    __threadfence_system();
     __syncwarp();
-    if (lane == 0) st_release_sys_u32(p.flag[owner] + static_cast<size_t>(k) * p.rs_rows + li, epoch);
+    if (lane == 0) {
+      __threadfence_system();
+      st_release_sys_u32(p.flag[owner] + static_cast<size_t>(k) * p.rs_rows + li, epoch);
+    }
   }
 }
 
@@ -214,12 +225,21 @@ int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st) {
     return -1;
   const int own = min(p.M, (p.rank + 1) * p.rs_rows) - p.rank * p.rs_rows;
   if (own <= 0) return 0;
-  const dim3 grid((own + kAgRowBlock - 1) / kAgRowBlock);
   const int ch = (p.H / 8 + kRsRowThreads - 1) / kRsRowThreads;
-  if (ch <= 4) rs_norm_ag_kernel<4><<<grid, kRsThreads, 0, st>>>(p);
-  else if (ch <= 8) rs_norm_ag_kernel<8><<<grid, kRsThreads, 0, st>>>(p);
-  else if (ch <= 12) rs_norm_ag_kernel<12><<<grid, kRsThreads, 0, st>>>(p);
-  else rs_norm_ag_kernel<16><<<grid, kRsThreads, 0, st>>>(p);
+  void (*k)(RsNormAgParams) = ch <= 4 ? rs_norm_ag_kernel<4>
+                              : ch <= 8 ? rs_norm_ag_kernel<8>
+                              : ch <= 12 ? rs_norm_ag_kernel<12> : rs_norm_ag_kernel<16>;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((own + kAgRowBlock - 1) / kAgRowBlock);
+  cfg.blockDim = dim3(kRsThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.reduce ? 1 : 0;     // the replicated input of reduce == 0 is not flag-guarded
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k, p);
+  if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }
 

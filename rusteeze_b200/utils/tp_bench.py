@@ -6,8 +6,12 @@ Chain timed (Llama-3-8B shapes, TP = world size):
             A tile as its gathered rows land           (parallel.fused_tp)
   baseline  o_proj GEMM -> NCCL all-reduce -> fused add + RMSNorm -> QKV GEMM
 
-Each variant runs `--iters` times after warm-up; CUDA events on the launching
-stream, MAX over ranks.  Roofline of the fused chain = the slower of
+Each variant runs `--iters` times after warm-up, eagerly and as one CUDA graph
+of `--iters` chains replayed `--replays` times (the speedup and roofline
+fraction use the graph numbers: the engine replays decode steps from graphs);
+CUDA events on the launching stream, MAX over ranks.  The per-kernel split
+(gemm_rs / rs_norm_ag / gemm_ag) is eager, with a barrier per iteration, so it
+also carries the ranks' launch skew.  Roofline of the fused chain = the slower of
   compute: FLOPs of both GEMMs / measured bf16 GEMM peak, and
   NVLink:  bytes each rank must send (reduce-scatter + all-gather of M x H bf16,
            (W-1)/W of it leaves the GPU each way) / 770 GB/s per direction.
@@ -34,6 +38,7 @@ def main() -> int:
     ap.add_argument("--tokens", default="256,1024,4096")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--replays", type=int, default=5)
     a = ap.parse_args()
     from rusteeze_b200.parallel.dist import init_distributed
     from rusteeze_b200.parallel.fused_tp import FusedTP
@@ -119,8 +124,38 @@ def main() -> int:
             t = torch.tensor([e0.elapsed_time(e1) / a.iters], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             out[name + "_ms"] = round(t.item(), 4)
+        # the same chains replayed from CUDA graphs (as the engine runs them): no host launch gaps
+        for name, fn in (("fused", fused), ("baseline", baseline), ("start", start_only)):
+            s2 = torch.cuda.Stream()
+            s2.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s2):
+                for _ in range(2):
+                    fn()
+            torch.cuda.current_stream().wait_stream(s2)
+            dist.barrier()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                for _ in range(a.iters):
+                    fn()
+            for _ in range(2):
+                gr.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.replays):
+                gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / (a.iters * a.replays)], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            out[name + "_graph_ms"] = round(t.item(), 4)
+            del gr                       # graphs holding NCCL calls go before the process group
+            torch.cuda.synchronize()
         # the fused chain includes one `start` boundary (it seeds the residual shard): report without it
-        chain = out["fused_ms"] - out["start_ms"]
+        chain = out["fused_graph_ms"] - out["start_graph_ms"]
         flops = 2.0 * M * o_k * H + 2.0 * M * H * qkv_n
         t_compute = flops / (peaks["bf16_tflops"] * 1e12) * 1e3
         bytes_out = 2 * M * H * 2 * (W - 1) / W          # RS + AG bytes leaving each GPU
@@ -128,7 +163,7 @@ def main() -> int:
         roof = max(t_compute, t_link)
         out.update(fused_chain_ms=round(chain, 4), roofline_ms=round(roof, 4),
                    roofline_frac=round(roof / chain, 3) if chain > 0 else None,
-                   speedup_vs_nccl=round(out["baseline_ms"] / chain, 3) if chain > 0 else None,
+                   speedup_vs_nccl=round(out["baseline_graph_ms"] / chain, 3) if chain > 0 else None,
                    status=int(ops.cuda_ext().status()[0]))
         rows.append(out)
         if rank == 0:
