@@ -60,7 +60,8 @@ struct GemmCfg {
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // bytes landing per stage
   static constexpr int kAccStages = (MX && BN == 256) ? 1 : 2;
   static constexpr int kTmemCols = MX ? 512 : (2 * BN < 32 ? 32 : 2 * BN);
-  static constexpr int kOutStageBytes = 8 * 32 * 64;   // epilogue transpose: 8 warps x 32 rows x 32 bf16
+  // epilogue transpose for the peer reduce-scatter (bf16 only): 8 warps x 32 rows x 32 bf16
+  static constexpr int kOutStageBytes = MX ? 0 : 8 * 32 * 64;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kOutStageBytes;
   static_assert(!MX || BN >= 128, "MXFP8 tiles cover whole 128-row scale chunks");
   static_assert(kSmemBytes <= 227 * 1024 - 2048, "dynamic + static shared memory must fit one CTA");
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // warps start on gathered rows while the previous kernels still run, but nothing is
     // stored before they completed: the output and split-K buffers come from the caching
     // allocator, which may hand out memory those kernels still read.
-    pdl_wait();
+    if (p.ag_flag) pdl_wait();
     const int quarter = warp & 3;           // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;       // column half of the tile
     const int row_in_tile = quarter * 32 + lane;
@@ -378,7 +379,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
             }
           }
-        } else if (p.epi == kEpiPeerRS) {
+        } else if (!MX && p.epi == kEpiPeerRS) {   // the MXFP8 launcher rejects this epilogue
           // reduce-scatter: each row goes to its owner's slot for this rank, over NVLink.
           // Every 32-column chunk is transposed through shared memory (16-byte units
           // XOR-swizzled by row pair, conflict-free both ways) so that 4 lanes store 64
@@ -724,7 +725,7 @@ GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi) {
 int gemm_mxf8_launch(const GemmParams& p_in, const void* A, int lda, const void* B, int ldb, int bn,
                      cudaStream_t st) {
   GemmParams p = p_in;
-  if (p.K % kBKMx != 0 || p.N % 128 != 0 || !p.sfa || !p.sfb) return -4;
+  if (p.K % kBKMx != 0 || p.N % 128 != 0 || !p.sfa || !p.sfb || p.epi == kEpiPeerRS) return -4;
   p.k_blocks = p.K / kBKMx;
   p.kb_per_split = (p.k_blocks + p.k_splits - 1) / p.k_splits;
   p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
