@@ -13,8 +13,10 @@ architecture; no network for checkpoints or datasets):
     (1024 requests per GPU), served with continuous batching, paged KV
     (block 16), chunked prefill, max 256 running sequences.
 
-One engine replica per GPU (data parallel; each rank serves its own request
-stream, so per-GPU work is fixed as N grows: weak scaling).  Per rank:
+One engine replica per GPU (data parallel: every rank serves the same seeded
+synthetic request stream as the 1-GPU run, so per-GPU work is identical at
+every N: weak scaling, and the MAX over ranks is not a max over different
+prefill/decode mixes).  Per rank:
   1. ramp: engine steps until the running batch is full (untimed)
   2. W warm-up engine steps (untimed)
   3. K timed engine steps, bracketed by a barrier + cuda synchronize and
@@ -183,7 +185,7 @@ def main():
         return static_batches(args, device, world, rank)
     eng = make_engine(args, device)
     V = eng.model_config.vocab_size
-    prompts, olens, arrivals = build_workload(args.requests, 1000 + rank, V, args.rate)
+    prompts, olens, arrivals = build_workload(args.requests, 1000, V, args.rate)
     eng_stream = torch.cuda.current_stream()
 
     # ---------------------------------------------------------------- steady-state serving
@@ -278,7 +280,7 @@ def main():
         # drain the steady-state run so the e2e run starts from an empty engine
         for rid in list(eng.requests):
             eng.abort_request(rid)
-        e_prompts, e_olens, _ = build_workload(args.e2e_requests, 5000 + rank, V, 1.0)
+        e_prompts, e_olens, _ = build_workload(args.e2e_requests, 5000, V, 1.0)
         h2d0, d2h0, steps0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes, eng.stats_counters["steps"]
         gen_e0 = eng.stats_counters["generation_tokens"]
         if world > 1:
