@@ -115,8 +115,12 @@ def build_workload(n, seed, vocab, rate):
 
 
 def make_engine(args, device):
-    from rusteeze_b200.config.config import Config
     from rusteeze_b200.engine.llm_engine import LLMEngine
+    return LLMEngine(make_config(args, device))
+
+
+def make_config(args, device):
+    from rusteeze_b200.config.config import Config
     cfg = Config()
     cfg.model.preset = args.model
     cfg.model.device = device
@@ -132,7 +136,7 @@ def make_engine(args, device):
     cfg.engine.swap_space_gb = 0
     cfg.engine.cuda_graph_max_batch = args.max_seqs
     cfg.engine.enforce_eager = bool(getattr(args, "eager", False))
-    return LLMEngine(cfg)
+    return cfg
 
 
 def main():
@@ -152,6 +156,10 @@ def main():
                     help="fp8: block-scaled e4m3 weights (the Llama-3-8B serving configuration); bf16: unquantised")
     ap.add_argument("--fp8", action="store_true", help="same as --dtype fp8 (the default)")
     ap.add_argument("--eager", action="store_true", help="disable CUDA graphs (profiling runs)")
+    ap.add_argument("--parallel", default="dp", choices=["dp", "tp"],
+                    help="dp: one engine replica per GPU (default); tp: one tensor-parallel engine over all GPUs")
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                    help="tensor-parallel collectives: fused peer-memory kernels or the NCCL baseline")
     ap.add_argument("--workload", default="poisson", choices=["poisson", "static"],
                     help="poisson: continuous batching (default); static: batches of --batches requests, "
                          "--static-prompt prompt tokens, --static-output greedy tokens (README table shape)")
@@ -170,13 +178,12 @@ def main():
                               "metric": "output_tokens_per_s", "n_gpus": args.gpus}))
         return 0
 
-    import numpy as np
     import torch
     import torch.distributed as dist
-    from rusteeze_b200 import ops
-    from rusteeze_b200.core.sampling_params import SamplingParams
 
     torch.cuda.set_device(local)
+    if world > 1 and args.parallel == "tp":
+        return serve_tp(args, world, rank)
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
@@ -184,6 +191,61 @@ def main():
     if args.workload == "static":
         return static_batches(args, device, world, rank)
     eng = make_engine(args, device)
+    line = serve(args, eng, device, rank, local, world)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def serve_tp(args, world, rank):
+    """Tensor-parallel serving of the same workload: ONE engine over all N GPUs.
+    Rank 0 schedules and samples; ranks 1..N-1 run the forward on their weight
+    shard from the plan ring; the collectives are the fused peer-memory kernels
+    (`--comm fused`: GEMM + reduce-scatter, add + RMSNorm + all-gather) or NCCL.
+    Timed windows come from `TPExecutor.timer` (CUDA events on every rank, MAX)."""
+    import torch
+    import torch.distributed as dist
+    from rusteeze_b200.parallel.dist import init_distributed
+    from rusteeze_b200.parallel.executor import worker_loop
+    from rusteeze_b200.parallel.launcher import tp_rank_setup
+    info = init_distributed(timeout_s=600)
+    cfg = make_config(args, str(info.device))
+    cfg.model.tensor_parallel_size = world
+    cfg.engine.comm_backend = args.comm
+    eng, runner, channel = tp_rank_setup(cfg, info, tag=f"bench{os.environ.get('MASTER_PORT', '0')}")
+    try:
+        if rank != 0:
+            worker_loop(runner, channel)
+            return 0
+        try:
+            line = serve(args, eng, str(info.device), 0, int(os.environ.get("LOCAL_RANK", "0")), 1,
+                         tp_timer=eng.runner.timer)
+        finally:
+            eng.runner.shutdown()
+        line.update(n_gpus=world, scaling="strong", gpu_launches_scope="rank 0")
+        line["config"]["parallelism"] = f"tp{world} ({args.comm} collectives)"
+        line["config"]["global_batch"] = args.max_seqs
+        line["config"]["workload"] = line["config"]["workload"].replace("req/GPU", "req")
+        print(json.dumps(line), flush=True)
+        return 0
+    finally:
+        runner.release_graphs()            # graphs holding NCCL calls go before the process group
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+def serve(args, eng, device, rank, local, world, tp_timer=None):
+    """The serving measurement on one engine: ramp to steady state, W warm-up
+    steps, K device-timed steps, then the end-to-end run through the public API.
+    `world` > 1 means data-parallel replicas (every rank runs this; MAX / SUM over
+    ranks); with `tp_timer` (tensor parallel) only rank 0 runs it and the timer
+    takes the MAX over the TP ranks.  Returns the JSON line (rank 0)."""
+    import torch
+    import torch.distributed as dist
+    from rusteeze_b200 import ops
+    from rusteeze_b200.core.sampling_params import SamplingParams
     V = eng.model_config.vocab_size
     prompts, olens, arrivals = build_workload(args.requests, 1000, V, args.rate)
     eng_stream = torch.cuda.current_stream()
@@ -239,6 +301,8 @@ def main():
     clk.start()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    if tp_timer is not None:
+        tp_timer("start")
     ev0.record(eng_stream)
     ttfts, tpots = [], []
     torch.cuda.nvtx.range_push("rz_timed")       # lets ncu --nvtx-include select steady-state launches
@@ -251,11 +315,12 @@ def main():
                     tpots.append(out.metrics.tpot)
     torch.cuda.nvtx.range_pop()
     ev1.record(eng_stream)
+    tp_ms = tp_timer("stop") if tp_timer is not None else None
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = clk.stop()
-    ms = ev0.elapsed_time(ev1)
+    ms = ev0.elapsed_time(ev1) if tp_ms is None else tp_ms
     launches = ops.launch_count() - launches0
     gen = eng.stats_counters["generation_tokens"] - gen0
     prompt_toks = eng.stats_counters["prompt_tokens"] - prompt0
@@ -313,42 +378,38 @@ def main():
                "d2h_bytes_per_step": int((eng.runner.d2h_bytes - d2h0) / esteps),
                "requests": args.e2e_requests * world, "wall_s": round(e_s, 3)}
 
-    if rank == 0:
-        line = {
-            "metric": "output_tokens_per_s",
-            "value": round(value, 1),
-            "unit": "tokens/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(ms_max / args.steps, 3),
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": round(value / BASELINE_TOK_S, 4),
-            "dtype": ("fp8_e4m3 weights (128x128 UE8M0 block scales), 1x128 UE8M0 activation scales, "
-                      "bf16 activations/KV, fp32 accumulate") if args.dtype == "fp8" else "bf16",
-            "data": "synthetic requests, random-init N(0,0.02) weights",
-            "config": {"model": args.model, "global_batch": args.max_seqs * world,
-                       "seq_len": "prompt U[128,2048] + output U[64,512]",
-                       "parallelism": f"dp{world}" if world > 1 else "tp1",
-                       "workload": f"{args.requests} req/GPU Poisson {args.rate}/s, top_p 0.9 T 0.7, "
-                                   "continuous batching, paged KV block 16, chunked prefill "
-                                   f"{args.max_batched_tokens} tok/step",
-                       "l2": "working set (16 GB weights + KV) far exceeds the 126 MB L2; no flush",
-                       "ramp_steps": ramp_steps},
-            "ttft_p50_s": round(statistics.median(ttfts), 4) if ttfts else None,
-            "tpot_p50_s": round(statistics.median(tpots), 5) if tpots else None,
-            "prompt_tokens_per_step": round(prompt_toks / max(1, args.steps), 1),
-            "host_ms_per_step": host_ms,
-            "clocks": clocks,
-            "gpu_launches": int(launches_sum),
-            "kernel_status": status,
-            "e2e": e2e,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
-    return 0
+    line = {
+        "metric": "output_tokens_per_s",
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": round(value / BASELINE_TOK_S, 4),
+        "dtype": ("fp8_e4m3 weights (128x128 UE8M0 block scales), 1x128 UE8M0 activation scales, "
+                  "bf16 activations/KV, fp32 accumulate") if args.dtype == "fp8" else "bf16",
+        "data": "synthetic requests, random-init N(0,0.02) weights",
+        "config": {"model": args.model, "global_batch": args.max_seqs * world,
+                   "seq_len": "prompt U[128,2048] + output U[64,512]",
+                   "parallelism": f"dp{world}" if world > 1 else "tp1",
+                   "workload": f"{args.requests} req/GPU Poisson {args.rate}/s, top_p 0.9 T 0.7, "
+                               "continuous batching, paged KV block 16, chunked prefill "
+                               f"{args.max_batched_tokens} tok/step",
+                   "l2": "working set (16 GB weights + KV) far exceeds the 126 MB L2; no flush",
+                   "ramp_steps": ramp_steps},
+        "ttft_p50_s": round(statistics.median(ttfts), 4) if ttfts else None,
+        "tpot_p50_s": round(statistics.median(tpots), 5) if tpots else None,
+        "prompt_tokens_per_step": round(prompt_toks / max(1, args.steps), 1),
+        "host_ms_per_step": host_ms,
+        "clocks": clocks,
+        "gpu_launches": int(launches_sum),
+        "kernel_status": status,
+        "e2e": e2e,
+    }
+    return line
 
 
 def static_batches(args, device, world, rank):

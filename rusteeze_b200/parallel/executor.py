@@ -70,6 +70,7 @@ class TPExecutor:
         # callable -> list of dead worker ranks (the launcher watches its child processes);
         # checked before every plan so a dead rank is reported instead of stalling a collective
         self.liveness = liveness
+        self._tstate: dict = {}
 
     def __getattr__(self, k):
         return getattr(self.runner, k)
@@ -114,11 +115,44 @@ class TPExecutor:
         r.d2h_bytes += r.sampler.last_d2h_bytes
         return res
 
+    def timer(self, kind: str) -> Optional[float]:
+        """Device-timed window over every rank: "start" marks it on each rank's stream,
+        "stop" returns its length in ms, the MAX over ranks (one all-reduce that the
+        workers join when they consume the stop message, after their last step)."""
+        self._check_workers()
+        self.ch.publish(MSG_STEP, {"timer": kind})
+        return _timer_mark(self.runner, kind, self._tstate)
+
     def shutdown(self) -> None:
         try:
             self.ch.publish(MSG_STOP, None)
         finally:
             self.ch.close()
+
+
+def _timer_mark(runner: ModelRunner, kind: str, state: dict) -> Optional[float]:
+    """One rank's side of `TPExecutor.timer`: CUDA events on the runner's stream (host
+    clock on CPU ranks); "stop" all-reduces the elapsed ms with MAX over ranks."""
+    import torch.distributed as dist
+    cuda = runner.is_cuda
+    if kind == "start":
+        if cuda:
+            state["ev0"] = torch.cuda.Event(enable_timing=True)
+            state["ev0"].record()
+        else:
+            state["t0"] = time.perf_counter()
+        return None
+    if cuda:
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev1.record()
+        torch.cuda.synchronize()
+        ms = state["ev0"].elapsed_time(ev1)
+        t = torch.tensor([ms], dtype=torch.float64, device=torch.cuda.current_device())
+    else:
+        t = torch.tensor([(time.perf_counter() - state["t0"]) * 1e3], dtype=torch.float64)
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def stage_plan(runner: ModelRunner, plan) -> Tuple[object, int, int]:
@@ -158,6 +192,7 @@ def stage_plan(runner: ModelRunner, plan) -> Tuple[object, int, int]:
 def worker_loop(runner: ModelRunner, channel: PlanChannel, idle_timeout_s: float = 600.0) -> int:
     """Runs plans until rank 0 sends STOP or closes the ring.  Returns steps run."""
     steps = 0
+    timer_state: dict = {}
     idle_since = time.monotonic()
     while True:
         msg = channel.consume(1.0)
@@ -174,6 +209,9 @@ def worker_loop(runner: ModelRunner, channel: PlanChannel, idle_timeout_s: float
             return steps
         if "capture" in plan:
             runner.capture_graphs(plan["capture"])
+            continue
+        if "timer" in plan:
+            _timer_mark(runner, plan["timer"], timer_state)
             continue
         if plan["sout"]:
             runner.swap_out(plan["sout"])

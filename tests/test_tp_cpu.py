@@ -107,3 +107,23 @@ def test_dead_worker_is_reported_not_hung():
         t1 = time.monotonic()
         launcher.shutdown(timeout=5.0)
         assert time.monotonic() - t1 < 60.0
+
+
+@pytest.mark.timeout(300)
+def test_tp2_timer_is_max_over_ranks():
+    """TPExecutor.timer: the workers mark the window when they consume the control
+    message and join one MAX all-reduce on stop; steps inside the window still run."""
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, 1000, 20).tolist() for _ in range(2)]
+    launcher = TPEngineLauncher(_cfg(2), model_config=MC, device_type="cpu")
+    try:
+        eng = launcher.engine()
+        eng.runner.timer("start")
+        got = _run(eng, prompts, n=4)
+        ms = eng.runner.timer("stop")
+        again = _run(eng, prompts, n=4)       # the plan stream continues after the window
+    finally:
+        launcher.shutdown()
+    assert ms is not None and ms > 0.0
+    assert got == again and all(len(t) == 4 for t in got)
