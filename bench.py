@@ -136,6 +136,15 @@ def make_config(args, device):
     cfg.engine.swap_space_gb = 0
     cfg.engine.cuda_graph_max_batch = args.max_seqs
     cfg.engine.enforce_eager = bool(getattr(args, "eager", False))
+    if args.workload == "shared-prefix":
+        cfg.engine.enable_prefix_caching = True
+    if args.draft:
+        from rusteeze_b200.config.config import SpeculativeSection
+        cfg.engine.speculative = SpeculativeSection(
+            draft_preset=None if args.draft == "self" else args.draft, num_speculative_tokens=args.spec_k)
+        # a verify pass holds max_num_seqs * (k + 1) tokens
+        cfg.engine.max_num_batched_tokens = max(cfg.engine.max_num_batched_tokens,
+                                                args.max_seqs * (args.spec_k + 1))
     return cfg
 
 
@@ -160,9 +169,15 @@ def main():
                     help="dp: one engine replica per GPU (default); tp: one tensor-parallel engine over all GPUs")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="tensor-parallel collectives: fused peer-memory kernels or the NCCL baseline")
-    ap.add_argument("--workload", default="poisson", choices=["poisson", "static"],
+    ap.add_argument("--workload", default="poisson", choices=["poisson", "static", "shared-prefix"],
                     help="poisson: continuous batching (default); static: batches of --batches requests, "
-                         "--static-prompt prompt tokens, --static-output greedy tokens (README table shape)")
+                         "--static-prompt prompt tokens, --static-output greedy tokens (README table shape); "
+                         "shared-prefix: static batches whose prompts share a --shared-prefix token prefix "
+                         "followed by --static-prompt unique tokens (prefix caching on)")
+    ap.add_argument("--shared-prefix", type=int, default=1024)
+    ap.add_argument("--draft", default=None,
+                    help="speculative decoding: random-init draft preset (e.g. llama-3.2-1b), or 'self'")
+    ap.add_argument("--spec-k", type=int, default=4, help="draft tokens per speculative round")
     ap.add_argument("--batches", default="1,8,32,128,256")
     ap.add_argument("--static-prompt", type=int, default=512)
     ap.add_argument("--static-output", type=int, default=128)
@@ -188,12 +203,13 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     device = f"cuda:{local}"
-    if args.workload == "static":
-        return static_batches(args, device, world, rank)
     eng = make_engine(args, device)
-    line = serve(args, eng, device, rank, local, world)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    if args.workload != "poisson":
+        static_batches(args, eng, device, rank, world)
+    else:
+        line = serve(args, eng, device, rank, local, world)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
@@ -220,6 +236,9 @@ def serve_tp(args, world, rank):
             worker_loop(runner, channel)
             return 0
         try:
+            if args.workload != "poisson":
+                static_batches(args, eng, str(info.device), 0, 1, tp_timer=eng.runner.timer)
+                return 0
             line = serve(args, eng, str(info.device), 0, int(os.environ.get("LOCAL_RANK", "0")), 1,
                          tp_timer=eng.runner.timer)
         finally:
@@ -412,54 +431,68 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
     return line
 
 
-def static_batches(args, device, world, rank):
+def static_batches(args, eng, device, rank, world, tp_timer=None):
     """Static batches (all requests admitted together, greedy, EOS ignored):
-    for each batch size B, B prompts of --static-prompt random tokens decode
-    --static-output tokens; output tok/s = B * output / (device time from the
-    first step to the last token), timed with CUDA events, MAX over ranks.
+    for each batch size B, B prompts decode --static-output tokens; output
+    tok/s = B * output / (device time from the first step to the last token),
+    timed with CUDA events, MAX over ranks (DP replicas: `world` > 1; one
+    tensor-parallel engine: `tp_timer`).  Prompts are --static-prompt random
+    tokens, or with `--workload shared-prefix` a common --shared-prefix-token
+    random prefix plus a unique --static-prompt-token suffix (prefix caching on).
     One JSON line per batch size."""
     import numpy as np
     import torch
     import torch.distributed as dist
     from rusteeze_b200.core.sampling_params import SamplingParams
-    eng = make_engine(args, device)
     V = eng.model_config.vocab_size
-    rng = np.random.default_rng(rank)
+    rng = np.random.default_rng(0)
+    prefix = rng.integers(0, V, args.shared_prefix).tolist() if args.workload == "shared-prefix" else []
     stream = torch.cuda.current_stream()
     for B in [int(x) for x in args.batches.split(",")]:
         def run_once():
             for _ in range(B):
                 eng.add_request(None, None, SamplingParams(temperature=0.0, max_tokens=args.static_output,
                                                            ignore_eos=True),
-                                rng.integers(0, V, args.static_prompt).tolist())
+                                prefix + rng.integers(0, V, args.static_prompt).tolist())
             ttft = []
             while eng.has_unfinished_requests():
                 for o in eng.step():
                     if o.finished and o.metrics.ttft is not None:
                         ttft.append(o.metrics.ttft)
             return ttft
-        run_once()                                   # warm-up (graphs, allocator)
+        run_once()                                   # warm-up (graphs, allocator, prefix cache)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if tp_timer is not None:
+            tp_timer("start")
         e0.record(stream)
         ttft = run_once()
         e1.record(stream)
+        tp_ms = tp_timer("stop") if tp_timer is not None else None
         torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+        t = torch.tensor([e0.elapsed_time(e1) if tp_ms is None else tp_ms], dtype=torch.float64, device=device)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
+        n_gpus = world if tp_timer is None else int(os.environ.get("WORLD_SIZE", "1"))
         if rank == 0:
             tok = B * args.static_output * world
-            print(json.dumps({"metric": "output_tokens_per_s", "workload": "static", "batch": B,
-                              "value": round(tok / (ms / 1000.0), 1), "unit": "tokens/s", "n_gpus": world,
-                              "ms_total": round(ms, 2), "ttft_p50_s": round(statistics.median(ttft), 4),
-                              "dtype": args.dtype, "config": {"model": args.model, "prompt": args.static_prompt,
-                                                              "output": args.static_output}}), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+            line = {"metric": "output_tokens_per_s", "workload": args.workload, "batch": B,
+                    "value": round(tok / (ms / 1000.0), 1), "unit": "tokens/s", "n_gpus": n_gpus,
+                    "ms_total": round(ms, 2), "ttft_p50_s": round(statistics.median(ttft), 4) if ttft else None,
+                    "dtype": args.dtype,
+                    "config": {"model": args.model, "prompt": args.static_prompt, "output": args.static_output,
+                               "parallelism": (f"tp{n_gpus} ({args.comm} collectives)" if tp_timer is not None
+                                               else (f"dp{world}" if world > 1 else "tp1"))}}
+            if args.workload == "shared-prefix":
+                line["config"]["shared_prefix"] = args.shared_prefix
+            if getattr(eng, "spec", None) is not None:
+                st = eng.spec.stats
+                line["speculative"] = {"draft": args.draft, "k": args.spec_k, "rounds": st["rounds"],
+                                       "acceptance": round(eng.spec.acceptance_rate(), 4)}
+            print(json.dumps(line), flush=True)
     return 0
 
 

@@ -155,6 +155,11 @@ class LLMEngine:
         budget = total * ec.gpu_memory_utilization - used_by_others
         # activations / logits / graph pools headroom
         budget -= 4 * (1 << 30)
+        # a separate draft model (speculative decoding): its weights, and one draft KV block per block
+        from rusteeze_b200.engine.spec_decode import draft_memory
+        d_w, d_blk = draft_memory(self.model_config, ec.speculative, torch.finfo(self.dtype).bits // 8, BLOCK_SIZE)
+        budget -= d_w
+        bytes_per_block += d_blk
         n = int(budget // bytes_per_block)
         if n < 16:
             raise RuntimeError(f"not enough GPU memory for the KV cache ({budget / 2**30:.1f} GiB left)")

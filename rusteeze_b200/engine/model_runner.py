@@ -244,6 +244,18 @@ class ModelRunner:
         """Eager forward of an explicit token batch (speculative decoding):
         sequence i gets n_new[i] tokens at positions ctx[i].., and the logits
         of its last `logits_per_seq` tokens are returned in sequence order."""
+        meta, T, S = self.stage_arrays(bm, seq_ids, ctx, n_new, toks, logits_per_seq, num_decode)
+        return self.forward_staged(meta, T, S * logits_per_seq)
+
+    def forward_staged(self, meta, T: int, n_rows: int) -> torch.Tensor:
+        """Forward of the staged batch; logits of the rows h_logits_idx[:n_rows]."""
+        h = self.model(self.d_input_ids[:T], self.d_positions[:T], meta, self.kv_layers)
+        idx = self.h_logits_idx[:n_rows].to(h.device, non_blocking=self.is_cuda)
+        return self.model.compute_logits(h.index_select(0, idx))
+
+    def stage_arrays(self, bm, seq_ids, ctx, n_new, toks, logits_per_seq: int, num_decode: int = 0):
+        """Builds and uploads the batch of `forward_arrays` (block tables from `bm`);
+        returns (metadata, T, S)."""
         S = len(seq_ids)
         self._flip_host()
         T = bm.build_batch(np.asarray(seq_ids, dtype=np.int64), np.asarray(ctx, dtype=np.int64),
@@ -269,10 +281,7 @@ class ModelRunner:
             meta.query_start_loc = self.h_qsl[:S + 1].clone()
             meta.seq_lens = self.h_seq_lens[:S].clone()
             meta.block_tables = self.h_block_tables[:S].clone()
-        h = self.model(self.d_input_ids[:T], self.d_positions[:T], meta, self.kv_layers)
-        n_rows = S * logits_per_seq
-        idx = self.h_logits_idx[:n_rows].to(h.device, non_blocking=nb)
-        return self.model.compute_logits(h.index_select(0, idx))
+        return meta, T, S
 
     # ------------------------------------------------------------------ graphs
     def _graph_bucket(self, n: int) -> Optional[int]:

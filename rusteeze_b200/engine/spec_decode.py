@@ -29,7 +29,7 @@ from __future__ import annotations
 import dataclasses
 import logging
 import time
-from typing import Dict
+from typing import Dict, Optional, Tuple
 
 import numpy as np
 import torch
@@ -49,7 +49,7 @@ def _verify_cpu(target: torch.Tensor, draft_logits, draft: torch.Tensor, temps, 
     out = torch.full((B, k + 1), -1, dtype=torch.long)
     acc = torch.zeros(B, dtype=torch.long)
     for b in range(B):
-        g = torch.Generator().manual_seed(int(seeds[b]) * 1000003 + int(offsets[b]))
+        g = torch.Generator().manual_seed((int(seeds[b]) * 1000003 + int(offsets[b])) & ((1 << 63) - 1))
         for j in range(k + 1):
             t = target[b * (k + 1) + j].float()
             if temps[b] <= 0:
@@ -75,19 +75,34 @@ def _verify_cpu(target: torch.Tensor, draft_logits, draft: torch.Tensor, temps, 
     return acc, out
 
 
+def draft_model_config(target: ModelConfig, spec_cfg) -> Optional[ModelConfig]:
+    """The separate draft model's architecture, or None when the target drafts for itself."""
+    if not spec_cfg.draft_model and not spec_cfg.draft_preset:
+        return None
+    dmc = ModelConfig.from_json_file(spec_cfg.draft_model) if spec_cfg.draft_model else \
+        get_preset(spec_cfg.draft_preset)
+    if dmc.vocab_size != target.vocab_size:
+        raise ValueError("draft and target must share the vocabulary")
+    return dataclasses.replace(dmc, max_position_embeddings=max(dmc.max_position_embeddings,
+                                                               target.max_position_embeddings))
+
+
+def draft_memory(target: ModelConfig, spec_cfg, dtype_bytes: int, block_size: int) -> Tuple[int, int]:
+    """(weight bytes, KV bytes per cache block) the draft adds on the GPU that holds
+    it: the draft keeps one KV block per target block (same block tables).  Tensor-
+    parallel engines keep an unsharded draft on rank 0."""
+    dmc = draft_model_config(target, spec_cfg) if spec_cfg is not None else None
+    if dmc is None:
+        return 0, 0
+    return dmc.num_params() * dtype_bytes, dmc.kv_bytes_per_token(dtype_bytes) * block_size
+
+
 class SpecDecoder:
     def __init__(self, engine, spec_cfg):
         self.engine = engine
         self.k = spec_cfg.num_speculative_tokens
         tm = engine.model
-        if spec_cfg.draft_model:
-            dmc = ModelConfig.from_json_file(spec_cfg.draft_model)
-        else:
-            dmc = get_preset(spec_cfg.draft_preset) if spec_cfg.draft_preset else dataclasses.replace(tm.cfg)
-        if dmc.vocab_size != tm.cfg.vocab_size:
-            raise ValueError("draft and target must share the vocabulary")
-        dmc = dataclasses.replace(dmc, max_position_embeddings=max(dmc.max_position_embeddings,
-                                                                   tm.cfg.max_position_embeddings))
+        dmc = draft_model_config(tm.cfg, spec_cfg) or dataclasses.replace(tm.cfg)
         self.self_draft = not spec_cfg.draft_model and not spec_cfg.draft_preset
         if self.self_draft:
             self.draft = tm      # sanity mode: the target drafts for itself (acceptance must be 100% when greedy)

@@ -93,15 +93,8 @@ class TPExecutor:
         self._check_workers()
         r = self.runner
         meta, T, S, sample_rows = r.prepare(so, bm)
-        MB = int(max(1, (int(r.h_seq_lens[:S].max()) + 15) // 16)) if S else 1
-        plan = {
-            "T": T, "S": S, "nd": len(so.decodes), "maxq": meta.max_query_len, "maxs": meta.max_seq_len,
-            "pure": not so.prefills, "rows": sample_rows, "mb": MB,
-            "ids": r.h_input_ids[:T].numpy().copy(), "pos": r.h_positions[:T].numpy().copy(),
-            "slots": r.h_slots[:T].numpy().copy(), "qsl": r.h_qsl[:S + 1].numpy().copy(),
-            "sl": r.h_seq_lens[:S].numpy().copy(), "bt": r.h_block_tables[:S, :MB].numpy().copy(),
-            "copy": so.blocks_to_copy, "sin": so.blocks_to_swap_in, "sout": so.blocks_to_swap_out,
-        }
+        plan = {"pure": not so.prefills, "rows": sample_rows, "copy": so.blocks_to_copy,
+                "sin": so.blocks_to_swap_in, "sout": so.blocks_to_swap_out, **_staged_plan(r, meta, T, S)}
         self.ch.publish(MSG_STEP, plan)
         if so.blocks_to_swap_out:
             r.swap_out(so.blocks_to_swap_out)
@@ -114,6 +107,19 @@ class TPExecutor:
         r.h2d_bytes += r.sampler.last_h2d_bytes
         r.d2h_bytes += r.sampler.last_d2h_bytes
         return res
+
+    @torch.no_grad()
+    def forward_arrays(self, bm, seq_ids, ctx, n_new, toks, logits_per_seq: int,
+                       num_decode: int = 0) -> torch.Tensor:
+        """Speculative-decoding forwards (draft on the target, verify): rank 0 stages
+        the explicit token batch, the plan carries its arrays and logits rows, and
+        every rank runs the same forward on its shard."""
+        self._check_workers()
+        r = self.runner
+        meta, T, S = r.stage_arrays(bm, seq_ids, ctx, n_new, toks, logits_per_seq, num_decode)
+        n_rows = S * logits_per_seq
+        self.ch.publish(MSG_STEP, {"arrays": n_rows, **_staged_plan(r, meta, T, S)})
+        return r.forward_staged(meta, T, n_rows)
 
     def timer(self, kind: str) -> Optional[float]:
         """Device-timed window over every rank: "start" marks it on each rank's stream,
@@ -128,6 +134,18 @@ class TPExecutor:
             self.ch.publish(MSG_STOP, None)
         finally:
             self.ch.close()
+
+
+def _staged_plan(r: ModelRunner, meta, T: int, S: int) -> dict:
+    """The staged host arrays of a batch (rank 0), as the workers' `stage_plan` reads them."""
+    MB = int(max(1, (int(r.h_seq_lens[:S].max()) + 15) // 16)) if S else 1
+    return {
+        "T": T, "S": S, "nd": meta.num_decode_seqs, "maxq": meta.max_query_len, "maxs": meta.max_seq_len,
+        "mb": MB, "ids": r.h_input_ids[:T].numpy().copy(), "pos": r.h_positions[:T].numpy().copy(),
+        "slots": r.h_slots[:T].numpy().copy(), "qsl": r.h_qsl[:S + 1].numpy().copy(),
+        "sl": r.h_seq_lens[:S].numpy().copy(), "bt": r.h_block_tables[:S, :MB].numpy().copy(),
+        "lidx": r.h_logits_idx[:T].numpy().copy(),
+    }
 
 
 def _timer_mark(runner: ModelRunner, kind: str, state: dict) -> Optional[float]:
@@ -212,6 +230,13 @@ def worker_loop(runner: ModelRunner, channel: PlanChannel, idle_timeout_s: float
             continue
         if "timer" in plan:
             _timer_mark(runner, plan["timer"], timer_state)
+            continue
+        if "arrays" in plan:
+            meta, T, S = stage_plan(runner, plan)
+            n_rows = plan["arrays"]
+            runner.h_logits_idx[:n_rows] = torch.from_numpy(plan["lidx"][:n_rows])
+            runner.forward_staged(meta, T, n_rows)
+            steps += 1
             continue
         if plan["sout"]:
             runner.swap_out(plan["sout"])

@@ -59,6 +59,11 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
     ep_rank, ep_size = (info.rank, info.world_size) if mc.is_moe else (0, 1)
     model = build_model(mc, dtype=dtype, device=dev, tp=tp, ep_rank=ep_rank, ep_size=ep_size,
                         model_dir=cfg.model.path, seed=cfg.model.seed)
+    q = cfg.model.quantization
+    if q is not None and q.method != "none":
+        # block-scaled FP8 of this rank's shard (every sharded K / N is a multiple of 128)
+        from rusteeze_b200.models.quant import quantize_model_fp8
+        quantize_model_fp8(model, getattr(q, "scale_format", "ue8m0"))
     if info.device.type == "cuda":
         model.prepare_for_gpu()
     # agree on the KV block count
@@ -68,6 +73,12 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
         free, total = torch.cuda.mem_get_info()
         budget = total * ec.gpu_memory_utilization - (total - free) - 4 * (1 << 30)
         per_block = 2 * mc.num_hidden_layers * model.hkv * mc.head_dim * 16 * torch.finfo(dtype).bits // 8
+        if info.rank == 0:
+            # rank 0 also holds the unsharded draft model of speculative decoding and its KV
+            from rusteeze_b200.engine.spec_decode import draft_memory
+            d_w, d_blk = draft_memory(mc, ec.speculative, torch.finfo(dtype).bits // 8, 16)
+            budget -= d_w
+            per_block += d_blk
         nblocks = int(budget // per_block)
     else:
         nblocks = 256

@@ -127,3 +127,68 @@ def test_tp2_timer_is_max_over_ranks():
         launcher.shutdown()
     assert ms is not None and ms > 0.0
     assert got == again and all(len(t) == 4 for t in got)
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("draft", ["self", "separate"])
+def test_tp2_speculative_decoding_matches_single_process(draft, tmp_path):
+    """Speculative decoding on a tensor-parallel engine: the verify (and self-draft)
+    forwards go through the plan ring so every rank runs them; a separate draft model
+    stays unsharded on rank 0.  Greedy output equals the non-speculative engine's."""
+    import dataclasses
+    from rusteeze_b200.config.config import SpeculativeSection
+    from rusteeze_b200.models.loader import build_model, save_hf_checkpoint
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    rng = np.random.default_rng(2)
+    prompts = [rng.integers(0, 1000, int(n)).tolist() for n in (12, 33)]
+    ref = _run(LLMEngine(_cfg(1), model_config=MC), prompts, n=7)
+    if draft == "self":
+        spec = SpeculativeSection(num_speculative_tokens=3)
+    else:
+        dmc = dataclasses.replace(MC, name="tp-tiny-draft", num_hidden_layers=1)
+        save_hf_checkpoint(build_model(dmc, dtype=__import__("torch").float32, seed=5), str(tmp_path))
+        spec = SpeculativeSection(draft_model=str(tmp_path), num_speculative_tokens=3)
+    cfg = _cfg(2)
+    cfg.engine.speculative = spec
+    launcher = TPEngineLauncher(cfg, model_config=MC, device_type="cpu")
+    try:
+        eng = launcher.engine()
+        got = _run(eng, prompts, n=7)
+        stats = dict(eng.spec.stats)
+    finally:
+        launcher.shutdown()
+    assert got == ref
+    assert stats["rounds"] > 0
+    if draft == "self":
+        assert stats["accepted"] == stats["proposed"]
+
+
+@pytest.mark.timeout(300)
+def test_tp2_fp8_quantises_each_shard_like_the_full_model():
+    """Block-scaled FP8 at TP2: every rank quantises its own shard; with shard
+    boundaries on 128-element blocks that equals quantising the full model, so the
+    greedy tokens match the single-process FP8 engine."""
+    from rusteeze_b200.config.config import QuantizationConfig
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    mc = ModelConfig(name="tp-fp8", hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                     num_attention_heads=8, num_key_value_heads=4, vocab_size=1024, rms_norm_eps=1e-5,
+                     max_position_embeddings=512)
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, 1024, int(n)).tolist() for n in (17, 40)]
+
+    def cfg(tp):
+        c = _cfg(tp)
+        c.model.quantization = QuantizationConfig(method="fp8_block")
+        return c
+
+    single = LLMEngine(cfg(1), model_config=mc)
+    assert getattr(single.model, "fp8", False)
+    ref = _run(single, prompts, n=5)
+    launcher = TPEngineLauncher(cfg(2), model_config=mc, device_type="cpu")
+    try:
+        eng = launcher.engine()
+        assert getattr(eng.model, "fp8", False)
+        got = _run(eng, prompts, n=5)
+    finally:
+        launcher.shutdown()
+    assert got == ref
