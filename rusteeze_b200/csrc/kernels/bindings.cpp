@@ -553,10 +553,93 @@ int64_t gemm_ag(torch::Tensor out, torch::Tensor g, torch::Tensor w, c10::option
   return pl.k_splits > 1 ? 2 : 1;
 }
 
+// MXFP8 row-parallel GEMM whose epilogue reduce-scatters bf16 rows into the owners' slots.
+// Returns n_tiles.
+int64_t gemm_peer_rs_mx(torch::Tensor xq, torch::Tensor sfa, torch::Tensor wq, torch::Tensor wsf,
+                        std::vector<int64_t> slots, std::vector<int64_t> flags, int64_t rank, int64_t rs_rows,
+                        torch::Tensor epoch, int64_t call_idx) {
+  CHECK_CUDA(xq);
+  const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
+  const int world = static_cast<int>(slots.size());
+  TORCH_CHECK(world >= 1 && world <= rz::kMaxTpRanks && flags.size() == slots.size(), "gemm_peer_rs_mx: 1..8 ranks");
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0 && wq.size(1) == K && xq.is_contiguous() && wq.is_contiguous() &&
+                  xq.element_size() == 1 && wq.element_size() == 1,
+              "gemm_peer_rs_mx: contiguous e4m3 [M,K] x [N,K], K and N multiples of 128");
+  TORCH_CHECK(rs_rows % rz::kAgRowBlock == 0 && static_cast<int64_t>(rs_rows) * world >= M, "gemm_peer_rs_mx: rows");
+  const int bn = rz::plan_gemm_mxf8(M, N, K, 0, /*max_splits=*/1).bn;   // the epilogue stores final rows
+  rz::GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.k_splits = 1;
+  p.epi = rz::kEpiPeerRS;
+  p.status = status_ptr();
+  p.sfa = reinterpret_cast<const uint8_t*>(sfa.data_ptr());
+  p.sfb = reinterpret_cast<const uint8_t*>(wsf.data_ptr());
+  for (int i = 0; i < world; ++i) {
+    p.rs_slot[i] = reinterpret_cast<__nv_bfloat16*>(slots[i]);
+    p.rs_flag[i] = reinterpret_cast<uint32_t*>(flags[i]);
+  }
+  p.rs_rows = rs_rows;
+  p.tp_rank = rank; p.tp_world = world;
+  p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  p.call_idx = static_cast<uint32_t>(call_idx);
+  check_rc(rz::gemm_mxf8_launch(p, xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), bn, cur_stream()),
+           "gemm_peer_rs_mx");
+  return (N + bn - 1) / bn;
+}
+
+// MXFP8 GEMM on all-gathered operand rows (e4m3 + scale chunks written by the owners): the
+// TMA producer waits on the all-gather flags per A tile.  silu_q: gate/up with the SiLU
+// epilogue emitting the next MXFP8 operand into (out, sf_out); else bf16 rows into out.
+int64_t gemm_mxf8_ag(torch::Tensor out, c10::optional<torch::Tensor> sf_out, torch::Tensor gq, torch::Tensor gsf,
+                     torch::Tensor wq, torch::Tensor wsf, c10::optional<torch::Tensor> bias, torch::Tensor ag_flag,
+                     torch::Tensor epoch, int64_t call_idx) {
+  CHECK_CUDA(gq);
+  const int M = gq.size(0), K = gq.size(1), N = wq.size(0);
+  const bool silu_q = sf_out.has_value();
+  TORCH_CHECK(K % 128 == 0 && N % (silu_q ? 256 : 128) == 0 && wq.size(1) == K && wq.is_contiguous() &&
+                  gq.element_size() == 1 && wq.element_size() == 1,
+              "gemm_mxf8_ag: e4m3 [M,K] x [N,K], K % 128, N % 128 (256 with silu_q)");
+  rz::GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  int bn = 256;
+  if (silu_q) {
+    TORCH_CHECK(out.size(0) == M && out.size(1) == N / 2 && out.element_size() == 1, "gemm_mxf8_ag: q_out [M, N/2]");
+    p.k_splits = 1;
+    p.epi = rz::kEpiSiluMulMx;
+    p.ldd = out.stride(0);
+    p.q_out = reinterpret_cast<uint8_t*>(out.data_ptr());
+    p.sf_out = reinterpret_cast<uint8_t*>(sf_out->data_ptr());
+  } else {
+    auto pl = rz::plan_gemm_mxf8(M, N, K, 0);
+    bn = pl.bn;
+    p.k_splits = pl.k_splits;
+    p.epi = rz::kEpiNone;
+    p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+    p.ldd = out.stride(0);
+  }
+  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  p.status = status_ptr();
+  p.sfa = reinterpret_cast<const uint8_t*>(gsf.data_ptr());
+  p.sfb = reinterpret_cast<const uint8_t*>(wsf.data_ptr());
+  p.ag_flag = reinterpret_cast<const uint32_t*>(ag_flag.data_ptr());
+  p.ag_rows = M;
+  p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  p.call_idx = static_cast<uint32_t>(call_idx);
+  torch::Tensor ws;
+  if (p.k_splits > 1) {
+    ws = torch::empty({p.k_splits, M, N}, wq.options().dtype(torch::kFloat32));
+    p.partial = ws.data_ptr<float>();
+  }
+  check_rc(rz::gemm_mxf8_launch(p, gq.data_ptr(), gq.stride(0), wq.data_ptr(), wq.stride(0), bn, cur_stream()),
+           "gemm_mxf8_ag");
+  return p.k_splits > 1 ? 2 : 1;
+}
+
 void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10::optional<torch::Tensor> resid_in,
                 torch::Tensor residual, torch::Tensor w, double eps, double offset, std::vector<int64_t> gathers,
                 std::vector<int64_t> ag_flags, int64_t rank, int64_t M, int64_t rs_rows, torch::Tensor epoch,
-                int64_t call_idx, int64_t moe_topk, c10::optional<torch::Tensor> moe_flag) {
+                int64_t call_idx, int64_t moe_topk, c10::optional<torch::Tensor> moe_flag,
+                std::vector<int64_t> gathers_q, std::vector<int64_t> gathers_sf) {
   CHECK_BF16(residual); CHECK_BF16(w);
   const int world = static_cast<int>(gathers.size());
   TORCH_CHECK(world >= 1 && world <= rz::kMaxTpRanks && ag_flags.size() == gathers.size(), "rs_norm_ag: ranks");
@@ -581,6 +664,15 @@ void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10
   if (moe_topk > 0) {
     TORCH_CHECK(moe_flag.has_value(), "rs_norm_ag: MoE mode needs the moe flags");
     p.moe_flag = reinterpret_cast<const uint32_t*>(moe_flag->data_ptr());
+  }
+  p.mx = gathers_q.empty() ? 0 : 1;
+  if (p.mx) {
+    TORCH_CHECK(gathers_q.size() == gathers.size() && gathers_sf.size() == gathers.size(),
+                "rs_norm_ag: one MXFP8 gather buffer pair per rank");
+    for (int i = 0; i < world; ++i) {
+      p.gather_q[i] = reinterpret_cast<uint8_t*>(gathers_q[i]);
+      p.gather_sf[i] = reinterpret_cast<uint8_t*>(gathers_sf[i]);
+    }
   }
   check_rc(rz::rs_norm_ag_launch(p, cur_stream()), "rs_norm_ag");
 }
@@ -667,7 +759,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_peer_rs", &gemm_peer_rs);
   m.def("gemm_ag", &gemm_ag);
-  m.def("rs_norm_ag", &rs_norm_ag);
+  namespace py = pybind11;
+  m.def("rs_norm_ag", &rs_norm_ag, py::arg("slots"), py::arg("rs_flag"), py::arg("n_tiles"), py::arg("resid_in"),
+        py::arg("residual"), py::arg("w"), py::arg("eps"), py::arg("offset"), py::arg("gathers"),
+        py::arg("ag_flags"), py::arg("rank"), py::arg("M"), py::arg("rs_rows"), py::arg("epoch"),
+        py::arg("call_idx"), py::arg("moe_topk"), py::arg("moe_flag"),
+        py::arg("gathers_q") = std::vector<int64_t>{}, py::arg("gathers_sf") = std::vector<int64_t>{});
+  m.def("gemm_peer_rs_mx", &gemm_peer_rs_mx);
+  m.def("gemm_mxf8_ag", &gemm_mxf8_ag);
   m.def("moe_forward_peer", &moe_forward_peer);
   m.def("ag_wait", &ag_wait);
   m.def("tp_epoch_bump", &tp_epoch_bump);

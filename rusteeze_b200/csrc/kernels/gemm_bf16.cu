@@ -50,7 +50,7 @@ constexpr int kSfChunk = 512;   // UE8M0 scales of 128 rows x 4 K-chunks of 32
 constexpr int kSfTmemCol = 256; // TMEM column where the MXFP8 scales live
 constexpr int kGemmThreads = 320;  // warp 0 TMA producer, warp 1 MMA issuer, warps 2..9 epilogue
 
-template <int BN, bool MX>
+template <int BN, bool MX, bool PEER = false>
 struct GemmCfg {
   static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int kABytes = kBM * 128;
@@ -60,8 +60,8 @@ struct GemmCfg {
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // bytes landing per stage
   static constexpr int kAccStages = (MX && BN == 256) ? 1 : 2;
   static constexpr int kTmemCols = MX ? 512 : (2 * BN < 32 ? 32 : 2 * BN);
-  // epilogue transpose for the peer reduce-scatter (bf16 only): 8 warps x 32 rows x 32 bf16
-  static constexpr int kOutStageBytes = MX ? 0 : 8 * 32 * 64;
+  // epilogue transpose of the peer reduce-scatter instances: 8 warps x 32 rows x 32 bf16
+  static constexpr int kOutStageBytes = PEER ? 8 * 32 * 64 : 0;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kOutStageBytes;
   static_assert(!MX || BN >= 128, "MXFP8 tiles cover whole 128-row scale chunks");
   static_assert(kSmemBytes <= 227 * 1024 - 2048, "dynamic + static shared memory must fit one CTA");
@@ -89,11 +89,11 @@ __device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* src, float* v) 
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
-template <int BN, bool MX>
+template <int BN, bool MX, bool PEER>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  GemmParams p) {
-  using C = GemmCfg<BN, MX>;
+  using C = GemmCfg<BN, MX, PEER>;
   constexpr int S = C::kStages;
   constexpr int KS = C::kAccStages;
   extern __shared__ uint8_t smem_raw[];
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
             }
           }
-        } else if (!MX && p.epi == kEpiPeerRS) {   // the MXFP8 launcher rejects this epilogue
+        } else if (PEER) {                        // epilogue kEpiPeerRS (the launcher picks PEER by it)
           // reduce-scatter: each row goes to its owner's slot for this rank, over NVLink.
           // Every 32-column chunk is transposed through shared memory (16-byte units
           // XOR-swizzled by row pair, conflict-free both ways) so that 4 lanes store 64
@@ -558,9 +558,9 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool MX>
-static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B, int ldb, cudaStream_t st) {
-  using C = GemmCfg<BN, MX>;
+template <int BN, bool MX, bool PEER>
+static int launch_inst(const GemmParams& p0, const void* A, int lda, const void* B, int ldb, cudaStream_t st) {
+  using C = GemmCfg<BN, MX, PEER>;
   constexpr int kElems = MX ? kBKMx : kBK;
   const CUtensorMapDataType dt = MX ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int es = MX ? 1 : 2;
@@ -574,7 +574,7 @@ static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B
   const int grid = units < num_sms() ? units : num_sms();
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_tcgen05<BN, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    cudaFuncSetAttribute(gemm_tcgen05<BN, MX, PEER>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     attr_set = true;
   }
   if (p.ag_flag) {
@@ -590,10 +590,10 @@ static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05<BN, MX>, ta, tb, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05<BN, MX, PEER>, ta, tb, p);
     if (e != cudaSuccess) return static_cast<int>(e);
   } else {
-    gemm_tcgen05<BN, MX><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);
+    gemm_tcgen05<BN, MX, PEER><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);
   }
   if (p.k_splits > 1) {
     const int ncols_out = p.epi == kEpiSiluMul ? p.N / 2 : p.N;
@@ -601,6 +601,13 @@ static int launch_bn(const GemmParams& p0, const void* A, int lda, const void* B
     gemm_splitk_reduce<<<static_cast<int>((threads + 255) / 256), 256, 0, st>>>(p);
   }
   return static_cast<int>(cudaGetLastError());
+}
+
+// reduce-scatter GEMMs use the instance with the epilogue transpose buffer
+template <int BN, bool MX>
+static int launch_bn(const GemmParams& p, const void* A, int lda, const void* B, int ldb, cudaStream_t st) {
+  return p.epi == kEpiPeerRS ? launch_inst<BN, MX, true>(p, A, lda, B, ldb, st)
+                             : launch_inst<BN, MX, false>(p, A, lda, B, ldb, st);
 }
 
 GemmPlan plan_gemm(int M, int N, int K, int epi, int max_splits) {
@@ -666,13 +673,14 @@ int gemm_grouped_launch(const GemmParams& p_in, const void* A, int lda, int64_t 
   p.n_tiles = (p.N + bn - 1) / bn;
 #define RZ_GROUPED(BNV, MXV)                                                                                   \
   {                                                                                                           \
-    using C = GemmCfg<BNV, MXV>;                                                                              \
+    using C = GemmCfg<BNV, MXV, false>;                                                                       \
     static bool attr = false;                                                                                 \
     if (!attr) {                                                                                              \
-      cudaFuncSetAttribute(gemm_tcgen05<BNV, MXV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes); \
+      cudaFuncSetAttribute(gemm_tcgen05<BNV, MXV, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,        \
+                           C::kSmemBytes);                                                                    \
       attr = true;                                                                                            \
     }                                                                                                         \
-    gemm_tcgen05<BNV, MXV><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);                             \
+    gemm_tcgen05<BNV, MXV, false><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);                      \
   }
   if (!mx && bn == 256) RZ_GROUPED(256, false)
   else if (!mx && bn == 128) RZ_GROUPED(128, false)
@@ -683,7 +691,7 @@ int gemm_grouped_launch(const GemmParams& p_in, const void* A, int lda, int64_t 
   return static_cast<int>(cudaGetLastError());
 }
 
-GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi) {
+GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi, int max_splits) {
   // Same waves x per-unit cost estimate as the bf16 planner, with the fp8 MMA
   // rate (2x bf16 per SM) and 128-element K blocks.  BN=256 holds a single
   // accumulator (the scale columns take the rest of TMEM), so its epilogue does
@@ -703,7 +711,7 @@ GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi) {
     if (N % bn != 0 && bn == 256) continue;
     const int mt = (M + kBM - 1) / kBM;
     const int nt = (N + bn - 1) / bn;
-    for (int ks = 1; ks <= 16; ks *= 2) {
+    for (int ks = 1; ks <= max_splits; ks *= 2) {
       if (ks > 1 && (kblocks / ks < 4 || mt * nt * 2 > sms)) break;
       const int units = mt * nt * ks;
       const int waves = (units + sms - 1) / sms;
@@ -725,7 +733,7 @@ GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi) {
 int gemm_mxf8_launch(const GemmParams& p_in, const void* A, int lda, const void* B, int ldb, int bn,
                      cudaStream_t st) {
   GemmParams p = p_in;
-  if (p.K % kBKMx != 0 || p.N % 128 != 0 || !p.sfa || !p.sfb || p.epi == kEpiPeerRS) return -4;
+  if (p.K % kBKMx != 0 || p.N % 128 != 0 || !p.sfa || !p.sfb) return -4;
   p.k_blocks = p.K / kBKMx;
   p.kb_per_split = (p.k_blocks + p.k_splits - 1) / p.k_splits;
   p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;

@@ -70,7 +70,7 @@ int gemm_bf16_launch(const GemmParams& p, const void* A, int lda, const void* B,
 int gemm_grouped_launch(const GemmParams& p, const void* A, int lda, int64_t a_rows, const void* B, int ldb,
                         int bn, bool mx, cudaStream_t stream);
 // MXFP8 (e4m3 operands, UE8M0 scales per 32 K-elements): K % 128 == 0, N % 128 == 0, bn in {128, 256}.
-GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi);
+GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi, int max_splits = 16);
 int gemm_mxf8_launch(const GemmParams& p, const void* A, int lda, const void* B, int ldb, int bn,
                      cudaStream_t stream);
 // bf16 [M, K] (row stride ldx) -> e4m3 [M, K] + scale chunks for ceil(M/128) row blocks.

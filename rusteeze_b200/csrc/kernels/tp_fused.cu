@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "gemm_bf16.h"
+#include "mxfp8.cuh"
 #include "tp_fused.h"
 
 namespace rz {
@@ -131,7 +132,50 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
   ss = warp_sum(ss);
   if (lane == 0) s_ss[rr][sub] = ss;
   __syncthreads();
-  if (live) {
+  if (live && p.mx) {
+    // MXFP8 rows: the 16 chunks of a 128-column block belong to one half-warp (chunk
+    // index tr + 64 j), whose lanes reduce the block maximum together; every lane joins
+    // the shuffles (a chunk past H contributes 0)
+    const float inv = rsqrtf((s_ss[rr][0] + s_ss[rr][1]) / p.H + p.eps);
+    const int kbo = p.H / 128;
+    const size_t sf_row = static_cast<size_t>(row / 128) * kbo;
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+      const int c = (tr + j * kRsRowThreads) * 8;
+      const bool ok = c < p.H;
+      float x[8], w[8];
+      float amax = 0.f;
+      if (ok) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xr[j]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h[i]);
+          x[2 * i] = f.x;
+          x[2 * i + 1] = f.y;
+        }
+        ld8f(p.w + c, w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          x[i] = x[i] * inv * (w[i] + p.offset);          // quantised from fp32, as rms_norm_mxf8 does
+          amax = fmaxf(amax, fabsf(x[i]));
+        }
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (ok) {
+        float qinv;
+        const uint32_t e = ue8m0_scale(amax, &qinv);
+        const uint2 q = pack_e4m3x8(x, qinv);
+        const int kb = c / 128;
+        for (int d = 0; d < p.world; ++d) {
+          *reinterpret_cast<uint2*>(p.gather_q[d] + static_cast<size_t>(row) * p.H + c) = q;
+          if ((tr & 15) == 0)
+            *reinterpret_cast<uint32_t*>(p.gather_sf[d] + (sf_row + kb) * kSfChunkBytes + sf_offset(row & 127, 0)) =
+                e * 0x01010101u;
+        }
+      }
+    }
+  } else if (live) {
     const float inv = rsqrtf((s_ss[rr][0] + s_ss[rr][1]) / p.H + p.eps);
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
@@ -221,7 +265,7 @@ int ag_wait_launch(const uint32_t* ag_flag, int M, const uint32_t* epoch_ptr, ui
 
 int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st) {
   if (p.rs_rows % kAgRowBlock != 0 || p.H % 8 != 0 || p.H > kRsNormAgMaxH || p.world > kMaxTpRanks ||
-      kAgRowBlock * p.moe_topk > kRsThreads)
+      kAgRowBlock * p.moe_topk > kRsThreads || (p.mx && p.H % 128 != 0))
     return -1;
   const int own = min(p.M, (p.rank + 1) * p.rs_rows) - p.rank * p.rs_rows;
   if (own <= 0) return 0;

@@ -29,6 +29,12 @@ struct RsNormAgParams {
   // weighted by the gates), each row k-slot released by its own flag moe_flag[k * rs_rows + row]
   int moe_topk;
   const uint32_t* moe_flag;
+  // MXFP8 output (mx != 0): the normalised rows go out as e4m3 with power-of-two 1x128
+  // scales, in the block-scaled GEMM's scale-chunk layout, to every rank's gather_q
+  // [rows, H] and gather_sf [row tiles][H / 128][512] instead of the bf16 gather buffer
+  int mx;
+  uint8_t* gather_q[kMaxTpRanks];
+  uint8_t* gather_sf[kMaxTpRanks];
 };
 
 // Expert-parallel combine: every local (token, slot) pair's weighted expert output row goes

@@ -28,6 +28,7 @@ head/column, row split of o/down, vocab split of embedding and LM head).
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import List, Optional
 
@@ -277,8 +278,15 @@ class DecoderLM(nn.Module):
         F = getattr(self.tp, "fused_tp", None)
         if F is None or self.tp.size == 1 or not F.fits(M) or self.device.type != "cuda":
             return False
-        if self.is_gemma2 or self.act != "silu" or getattr(self, "fp8", False):
+        if self.is_gemma2 or self.act != "silu":
             return False
+        if getattr(self, "fp8", False):
+            # MXFP8 boundary chain (block-scaled GEMMs, quantised all-gather); opt-in with
+            # RZ_FUSED_TP_FP8=1, otherwise FP8 weights take the peer all-reduce path
+            if (os.environ.get("RZ_FUSED_TP_FP8", "0") != "1" or self.cfg.is_moe or not F.mx_ok
+                    or getattr(self, "fp8_format", None) != "ue8m0"):
+                return False
+            return all(L.gate_up_q.shape[0] % 256 == 0 for L in self.layers)
         if self.cfg.is_moe:
             # experts split over the ranks; top-k slots must fit the per-rank slot buffer
             return (self.ep_size == self.tp.size and self.cfg.num_experts_per_tok <= self.tp.size
@@ -301,23 +309,38 @@ class DecoderLM(nn.Module):
         D = cfg.head_dim
         h = self.embed_tokens(input_ids)
         M = h.shape[0]
-        x = F.start(h, self.layers[0].input_norm, eps, off)
+        # MXFP8 weights: every boundary but the last all-gathers the e4m3 operand + scales
+        mx = bool(getattr(self, "fp8", False))
+        x = F.start(h, self.layers[0].input_norm, eps, off, mx=mx)
         n = len(self.layers)
         for li, L in enumerate(self.layers):
             kv = kv_caches[li]
             c_attn, c_mlp = 2 * li + 1, 2 * li + 2
-            qkv = F.gemm_ag(x, L.qkv, 2 * li, L.qkv_bias)
+            if mx:
+                qkv = F.gemm_ag_mx(x, L.qkv_q, L.qkv_sf, 2 * li, L.qkv_bias)
+            else:
+                qkv = F.gemm_ag(x, L.qkv, 2 * li, L.qkv_bias)
             q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
                                    self.hq, self.hkv, D)
             a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
                                     cfg.attn_logit_softcapping)
-            F.gemm_rs(a.view(M, -1), L.o, c_attn)
-            x = F.rs_norm_ag(M, L.post_attn_norm, eps, off, c_attn)
+            if mx:
+                F.gemm_rs_mx(*ops.quant_mxf8_act(a.view(M, -1)), L.o_q, L.o_sf, c_attn)
+            else:
+                F.gemm_rs(a.view(M, -1), L.o, c_attn)
+            x = F.rs_norm_ag(M, L.post_attn_norm, eps, off, c_attn, mx=mx)
             nw = self.layers[li + 1].input_norm if li + 1 < n else self.norm
             if cfg.is_moe:
                 k = cfg.num_experts_per_tok
                 F.moe(x, L.router, L.w13_il, L.w2, k, self.e_lo, c_attn, c_mlp)
                 x = F.rs_norm_ag(M, nw, eps, off, c_mlp, moe_topk=k)
+                continue
+            if mx:
+                # the gate/up epilogue emits the down projection's operand; the final norm
+                # all-gathers bf16 rows for the LM head
+                F.gemm_rs_mx(*F.gemm_ag_mx(x, L.gate_up_q, L.gate_up_sf, c_attn, silu_q=True),
+                             L.down_q, L.down_sf, c_mlp)
+                x = F.rs_norm_ag(M, nw, eps, off, c_mlp, mx=li + 1 < n)
                 continue
             act = F.gemm_ag(x, L.gate_up_il, c_attn, silu_mul=True)
             F.gemm_rs(act, L.down, c_mlp)

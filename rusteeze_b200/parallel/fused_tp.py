@@ -19,10 +19,16 @@ around it (csrc/kernels/tp_fused.cu, gemm_bf16.cu):
                experts and its combine kernel stores every weighted expert
                output row straight into the owner's slot k over NVLink, so the
                owner's rs_norm_ag sums top-k slots instead of world partials.
+  MXFP8        with block-scaled FP8 weights the same chain runs on the
+               block-scaled GEMMs: rs_norm_ag quantises the normalised rows
+               (e4m3 + power-of-two 1x128 scales in the GEMM's scale-chunk
+               layout) before the all-gather, which halves its NVLink bytes,
+               and the gate/up GEMM's SiLU epilogue emits the down projection's
+               operand (gemm_rs_mx / gemm_ag_mx).
 
 One symmetric allocation per rank (torch symmetric memory) holds
-[rs flags | ag flags | slots | gather]; peers' bases come from the
-rendezvous.  The reference has no collective at all
+[rs flags | ag flags | moe flags | slots | gather | gather e4m3 | gather
+scales]; peers' bases come from the rendezvous.  The reference has no collective at all
 (crates/rusteeze-engine/src/tensor_parallel.rs:80-106).
 """
 from __future__ import annotations
@@ -58,7 +64,12 @@ class FusedTP:
         self.off_moe_flag = _up(self.off_ag_flag + 4 * n_ag_flags, _ALIGN)
         self.off_slots = _up(self.off_moe_flag + 4 * n_moe_flags, _ALIGN)
         self.off_gather = _up(self.off_slots + 2 * world * self.max_rs_rows * hidden, _ALIGN)
-        total = _up(self.off_gather + 2 * (max_tokens + 128) * hidden, _ALIGN)
+        # MXFP8 all-gather: e4m3 rows and their UE8M0 scale chunks (block-scaled GEMM layout)
+        self.mx_ok = hidden % 128 == 0
+        self.n_sf_bytes = (self.max_m_tiles + 1) * (hidden // 128) * 512 if self.mx_ok else 0
+        self.off_gather_q = _up(self.off_gather + 2 * (max_tokens + 128) * hidden, _ALIGN)
+        self.off_gather_sf = _up(self.off_gather_q + ((max_tokens + 128) * hidden if self.mx_ok else 0), _ALIGN)
+        total = _up(self.off_gather_sf + self.n_sf_bytes, _ALIGN)
         try:
             symm.enable_symm_mem_for_group(self.group.group_name)
         except Exception:  # noqa: BLE001 -- newer torch enables it implicitly
@@ -73,6 +84,8 @@ class FusedTP:
         self.gather_ptrs = [b + self.off_gather for b in bases]
         self.ag_flag_ptrs = [b + self.off_ag_flag for b in bases]
         self.moe_flag_ptrs = [b + self.off_moe_flag for b in bases]
+        self.gather_q_ptrs = [b + self.off_gather_q for b in bases] if self.mx_ok else []
+        self.gather_sf_ptrs = [b + self.off_gather_sf for b in bases] if self.mx_ok else []
         u8 = self.buf
         self.rs_flag = u8[self.off_rs_flag:self.off_rs_flag + 4 * n_rs_flags].view(torch.int32)
         self.ag_flag = u8[self.off_ag_flag:self.off_ag_flag + 4 * n_ag_flags].view(torch.int32)
@@ -80,6 +93,10 @@ class FusedTP:
         self.slots = u8[self.off_slots:self.off_slots + 2 * world * self.max_rs_rows * hidden].view(torch.bfloat16)
         self.gather = u8[self.off_gather:self.off_gather + 2 * (max_tokens + 128) * hidden].view(
             torch.bfloat16).view(max_tokens + 128, hidden)
+        if self.mx_ok:
+            self.gather_q = u8[self.off_gather_q:self.off_gather_q + (max_tokens + 128) * hidden].view(
+                torch.float8_e4m3fn).view(max_tokens + 128, hidden)
+            self.gather_sf = u8[self.off_gather_sf:self.off_gather_sf + self.n_sf_bytes]
         self.residual = torch.empty(self.max_rs_rows, hidden, dtype=torch.bfloat16, device=device)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
         self.n_tiles = 1
@@ -94,15 +111,26 @@ class FusedTP:
         return 0 < M <= self.max_tokens and self.hidden <= 8192 and self.hidden % 8 == 0
 
     # ------------------------------------------------------------------ ops
-    def start(self, h: torch.Tensor, norm_w: torch.Tensor, eps: float, offset: float) -> torch.Tensor:
+    def _mx_args(self, mx: bool):
+        if mx and not self.mx_ok:
+            raise ValueError("MXFP8 all-gather needs hidden % 128 == 0")
+        return (self.gather_q_ptrs, self.gather_sf_ptrs) if mx else ([], [])
+
+    def _gathered(self, M: int, mx: bool):
+        return (self.gather_q[:M], self.gather_sf) if mx else self.gather[:M]
+
+    def start(self, h: torch.Tensor, norm_w: torch.Tensor, eps: float, offset: float, mx: bool = False):
         """First boundary: x = h (replicated rows), residual shard = own rows,
-        normalised rows all-gathered.  Returns the gathered [M, H] view."""
+        normalised rows all-gathered.  Returns the gathered [M, H] view, or with
+        `mx` the MXFP8 operand (e4m3 [M, H] view, scale chunks)."""
         M = h.shape[0]
         C = ops.cuda_ext()
+        gq, gsf = self._mx_args(mx)
         C.rs_norm_ag(self.slots, self.rs_flag, 1, h.contiguous(), self.residual, norm_w, eps, offset,
-                     self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch, 0, 0, None)
+                     self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch, 0, 0, None,
+                     gq, gsf)
         ops.add_launches(1)
-        return self.gather[:M]
+        return self._gathered(M, mx)
 
     def moe(self, g: torch.Tensor, router: torch.Tensor, w13_il: torch.Tensor, w2: torch.Tensor, topk: int,
             e_lo: int, call_idx_in: int, call_idx: int) -> None:
@@ -124,12 +152,40 @@ class FusedTP:
         ops.add_launches(1)
 
     def rs_norm_ag(self, M: int, norm_w: torch.Tensor, eps: float, offset: float, call_idx: int,
-                   moe_topk: int = 0) -> torch.Tensor:
+                   moe_topk: int = 0, mx: bool = False):
+        gq, gsf = self._mx_args(mx)
         ops.cuda_ext().rs_norm_ag(self.slots, self.rs_flag, self.n_tiles, None, self.residual, norm_w, eps, offset,
                                   self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch,
-                                  call_idx, moe_topk, self.moe_flag if moe_topk else None)
+                                  call_idx, moe_topk, self.moe_flag if moe_topk else None, gq, gsf)
         ops.add_launches(1)
-        return self.gather[:M]
+        return self._gathered(M, mx)
+
+    def gemm_rs_mx(self, xq: torch.Tensor, sfa: torch.Tensor, wq: torch.Tensor, wsf: torch.Tensor,
+                   call_idx: int) -> None:
+        """MXFP8 row-parallel GEMM (operand from `ops.quant_mxf8_act` or a SiLU-quantising
+        epilogue) reduce-scattering its bf16 rows into the owners' slots."""
+        M = xq.shape[0]
+        self.n_tiles = int(ops.cuda_ext().gemm_peer_rs_mx(xq, sfa, wq, wsf, self.slot_ptrs, self.rs_flag_ptrs,
+                                                          self.rank, self.rs_rows(M), self.epoch, call_idx))
+        ops.add_launches(1)
+
+    def gemm_ag_mx(self, g, wq: torch.Tensor, wsf: torch.Tensor, call_idx: int,
+                   bias: Optional[torch.Tensor] = None, silu_q: bool = False):
+        """MXFP8 GEMM on the all-gathered operand `g` = (e4m3 rows, scale chunks):
+        bf16 [M, N] rows, or with `silu_q` (gate/up, rows interleaved in 64-row
+        blocks) SiLU(gate)*up as the next MXFP8 operand (e4m3 [M, N/2], scales)."""
+        gq, gsf = g
+        M, N = gq.shape[0], wq.shape[0]
+        if silu_q:
+            q = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=gq.device)
+            sf = torch.empty((M + 127) // 128, N // 256, 512, dtype=torch.uint8, device=gq.device)
+            ops.add_launches(ops.cuda_ext().gemm_mxf8_ag(q, sf, gq, gsf, wq, wsf, bias, self.ag_flag, self.epoch,
+                                                         call_idx))
+            return q, sf
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=gq.device)
+        ops.add_launches(ops.cuda_ext().gemm_mxf8_ag(out, None, gq, gsf, wq, wsf, bias, self.ag_flag, self.epoch,
+                                                     call_idx))
+        return out
 
     def gemm_ag(self, g: torch.Tensor, w: torch.Tensor, call_idx: int, bias: Optional[torch.Tensor] = None,
                 silu_mul: bool = False) -> torch.Tensor:

@@ -209,3 +209,134 @@ def test_tp2_engine_matches_tp1(backend, arch):
     for (ta, la), (tb, lb) in zip(got, ref):
         assert ta[0] == tb[0]
         assert abs(la - lb) < 0.1
+
+
+# ----------------------------------------------------------------------------- MXFP8 fused boundary
+_FP8_OPT_IN = pytest.mark.skipif(os.environ.get("RZ_FUSED_TP_FP8", "0") != "1",
+                                 reason="MXFP8 fused TP boundary is opt-in (RZ_FUSED_TP_FP8=1)")
+
+
+def _mx_weight(w):
+    from rusteeze_b200.ops import reference as ref
+    q, s = ref.quant_mxf8_weight(w)
+    deq = (q.float().view(-1, 128, w.shape[1] // 128, 128) * s[:, None, :, None]).view(w.shape)
+    return q, ref.pack_block_scales_ue8m0(s), deq
+
+
+def _boundary_mx_worker(rank, world, port, q):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from rusteeze_b200 import ops
+    from rusteeze_b200.ops import reference as ref
+    from rusteeze_b200.parallel.dist import init_distributed
+    from rusteeze_b200.parallel.fused_tp import FusedTP
+    info = init_distributed(timeout_s=60)
+    try:
+        H, K, N = 1024, 512, 512
+        F = FusedTP(dist.group.WORLD, rank, world, info.device, 2048, H)
+        errs = []
+        for step, M in enumerate((1, 37, 300, 1000)):
+            torch.manual_seed(step)                                  # same full tensors on every rank
+            dev = info.device
+            h0 = torch.randn(M, H, device=dev, dtype=torch.bfloat16)
+            xs = [torch.randn(M, K, device=dev, dtype=torch.bfloat16) for _ in range(world)]
+            ws = [_mx_weight(torch.randn(H, K, device=dev) * 0.05) for _ in range(world)]
+            wn = (1 + 0.1 * torch.randn(H, device=dev)).to(torch.bfloat16)
+            wc_q, wc_sf, wc_deq = _mx_weight(torch.randn(N, H, device=dev) * 0.05)
+            F.start(h0, wn, 1e-5, 0.0, mx=True)                       # boundary 0: x = h0
+            F.gemm_rs_mx(*ops.quant_mxf8_act(xs[rank]), ws[rank][0], ws[rank][1], 1)
+            g = F.rs_norm_ag(M, wn, 1e-5, 0.0, 1, mx=True)
+            y = F.gemm_ag_mx(g, wc_q, wc_sf, 1)                      # consumer GEMM on gathered rows
+            F.end_step()
+            torch.cuda.synchronize()
+            gq, gsf = g[0].float().clone(), g[1].clone()
+            dist.barrier()              # the next iteration's all-gather writes into peers' buffers
+            part = torch.zeros(M, H, device=dev)
+            for r in range(world):
+                xq_r, xs_r = ref.quant_mxf8_act(xs[r])
+                x_deq = (xq_r.float().view(M, K // 128, 128) * xs_r.unsqueeze(-1)).view(M, K)
+                part += (x_deq @ ws[r][2].t()).to(torch.bfloat16).float()
+            res = (h0.float() + part).to(torch.bfloat16).float()
+            want = res * torch.rsqrt(res.pow(2).mean(-1, keepdim=True) + 1e-5) * wn.float()
+            g_deq = (gq.view(M, H // 128, 128) * ref.unpack_act_scales_ue8m0(gsf, M, H).unsqueeze(-1)).view(M, H)
+            errs.append(((g_deq - want).norm() / want.norm()).item() / 4)     # e4m3 rounding: ~2-4 %
+            y_want = g_deq @ wc_deq.t()
+            errs.append(((y.float() - y_want).norm() / y_want.norm()).item())
+        q.put((rank, max(errs), int(ops.cuda_ext().status()[0])))
+    except BaseException as e:  # noqa: BLE001
+        q.put((rank, repr(e), -1))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@_FP8_OPT_IN
+@pytest.mark.timeout(300)
+def test_fused_tp_boundary_mxfp8_matches_reference():
+    """MXFP8 chain: block-scaled GEMM reduce-scattering bf16 rows -> add + RMSNorm +
+    quantise + all-gather of e4m3 rows and UE8M0 scale chunks -> block-scaled GEMM on
+    the gathered operand; vs a dequantise-then-matmul fp32 reference."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 4)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_boundary_mx_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(world)]
+    for p in ps:
+        p.join(60)
+    for rank, err, status in res:
+        assert status == 0, f"rank {rank} status {status}: {err}"
+        assert err < 2e-2, f"rank {rank} rel err {err}"
+
+
+def _tp2_fp8_child(q):
+    import faulthandler
+    os.environ["RZ_WORKER_WATCHDOG_S"] = "240"
+    faulthandler.dump_traceback_later(270, exit=True)
+    from rusteeze_b200.config.config import QuantizationConfig
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    try:
+        cfg = _tp_cfg(2, "fused")
+        cfg.model.quantization = QuantizationConfig(method="fp8_block")
+        launcher = TPEngineLauncher(cfg, model_config=_tp_model("llama"))
+        try:
+            eng = launcher.engine()
+            fused = eng.model._fused_tp_ok(1)
+            q.put(("ok", (fused, _tp_run(eng, _tp_prompts()))))
+        finally:
+            launcher.shutdown()
+    except BaseException as e:  # noqa: BLE001
+        q.put(("error", repr(e)))
+        raise
+
+
+@_FP8_OPT_IN
+@pytest.mark.timeout(600)
+def test_tp2_fp8_fused_engine_matches_tp1():
+    """FP8 (MXFP8) Llama at TP2 over the fused MXFP8 boundary chain vs the 1-GPU FP8 engine."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    from rusteeze_b200.config.config import QuantizationConfig
+    from rusteeze_b200.engine.llm_engine import LLMEngine
+    cfg = _tp_cfg(1, "fused")
+    cfg.model.quantization = QuantizationConfig(method="fp8_block")
+    ref = _tp_run(LLMEngine(cfg, model_config=_tp_model("llama")), _tp_prompts())
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_tp2_fp8_child, args=(q,))
+    p.start()
+    status, got = q.get(timeout=420)
+    p.join(60)
+    assert status == "ok", got
+    fused, toks = got
+    assert fused, "the MXFP8 fused boundary chain was not selected"
+    for (ta, la), (tb, lb) in zip(toks, ref):
+        assert ta[0] == tb[0]
+        assert abs(la - lb) < 0.15
