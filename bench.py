@@ -85,22 +85,29 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[4:8]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return summarize_clocks(self.lines)
+
+
+def summarize_clocks(lines) -> dict:
+    """nvidia-smi samples (clocks.sm, clocks.max.sm, power, active mask, then the four
+    throttle reasons as Active / Not Active) -> median SM clock, max clock and every
+    throttle reason seen active."""
+    sm, mx, reasons = [], None, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for ln in lines:
+        parts = [p.strip() for p in ln.split(",")]
+        if len(parts) < 8:
+            continue
+        try:
+            sm.append(float(parts[0]))
+            mx = float(parts[1])
+        except ValueError:
+            continue
+        for n, v in zip(names, parts[4:8]):
+            if v.lower().startswith("active"):
+                reasons.add(n)
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+            "reasons": sorted(reasons), "samples": len(sm)}
 
 
 def build_workload(n, seed, vocab, rate):
