@@ -5,17 +5,17 @@
 //    role of crates/rusteeze-engine/src/memory_pool.rs:13-193.  The engine
 //    registers its buffers as pinned (page-locked) memory through torch so
 //    that H2D/D2H copies of batch metadata and swap blocks are async DMA.
-//  * ShmRing -- a single-producer / multi-consumer broadcast ring in POSIX
-//    shared memory.  Rank 0's scheduler publishes each step's batch plan;
-//    every worker process (one per GPU) reads it without a collective.  It
-//    stands in for the reference's in-process SPSC token ring
-//    (crates/rusteeze-engine/src/zero_copy.rs:34-172), widened to processes
-//    and to N readers.  Every wait is bounded by a timeout and reports it.
+//  * ShmRing (shm_ring.h) -- a single-producer / multi-consumer broadcast
+//    ring in POSIX shared memory.  Rank 0's scheduler publishes each step's
+//    batch plan; every worker process (one per GPU) reads it without a
+//    collective.  Waits release the GIL and are bounded by a timeout.
 //  * NUMA helpers -- node count, CPUs of a node, the NUMA node of a PCI
 //    device, and thread/process CPU affinity; the reference's numa.rs is a
 //    single-node stub (crates/rusteeze-engine/src/numa.rs:14-75).
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
+
+#include "shm_ring.h"
 
 #include <atomic>
 #include <chrono>
@@ -100,131 +100,6 @@ class SizeClassPool {
   int64_t hits_ = 0, misses_ = 0, big_ = 0;
 };
 
-// ---------------------------------------------------------------- shm broadcast ring
-struct RingHeader {
-  uint32_t magic;
-  uint32_t num_slots;
-  uint64_t slot_bytes;
-  uint32_t num_readers;
-  uint32_t pad;
-  std::atomic<uint64_t> write_seq;       // number of messages published
-  std::atomic<uint64_t> closed;
-  std::atomic<uint64_t> read_seq[64];    // per reader: number of messages consumed
-};
-
-constexpr uint32_t kMagic = 0x52425247;  // "RBRG"
-
-class ShmRing {
- public:
-  ShmRing(const std::string& name, bool create, uint32_t num_slots, uint64_t slot_bytes,
-          uint32_t num_readers)
-      : name_(name), owner_(create) {
-    if (num_readers > 64) throw std::invalid_argument("at most 64 readers");
-    size_t hdr = (sizeof(RingHeader) + 63) / 64 * 64;
-    int fd;
-    if (create) {
-      shm_unlink(name.c_str());
-      fd = shm_open(name.c_str(), O_CREAT | O_RDWR | O_EXCL, 0600);
-      if (fd < 0) throw std::runtime_error("shm_open(create) failed for " + name);
-      size_ = hdr + size_t(num_slots) * (slot_bytes + 8);
-      if (ftruncate(fd, static_cast<off_t>(size_)) != 0) {
-        close(fd);
-        throw std::runtime_error("ftruncate failed");
-      }
-    } else {
-      fd = shm_open(name.c_str(), O_RDWR, 0600);
-      if (fd < 0) throw std::runtime_error("shm_open(attach) failed for " + name);
-      struct stat sb;
-      fstat(fd, &sb);
-      size_ = static_cast<size_t>(sb.st_size);
-    }
-    base_ = static_cast<uint8_t*>(mmap(nullptr, size_, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0));
-    close(fd);
-    if (base_ == MAP_FAILED) throw std::runtime_error("mmap failed");
-    h_ = reinterpret_cast<RingHeader*>(base_);
-    if (create) {
-      h_->num_slots = num_slots;
-      h_->slot_bytes = slot_bytes;
-      h_->num_readers = num_readers;
-      h_->write_seq.store(0);
-      h_->closed.store(0);
-      for (auto& r : h_->read_seq) r.store(0);
-      std::atomic_thread_fence(std::memory_order_seq_cst);
-      h_->magic = kMagic;
-    } else {
-      auto t0 = std::chrono::steady_clock::now();
-      while (reinterpret_cast<volatile uint32_t&>(h_->magic) != kMagic) {
-        if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10))
-          throw std::runtime_error("ring header never initialised");
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
-      }
-    }
-    data_ = base_ + hdr;
-  }
-  ~ShmRing() {
-    if (base_ && base_ != MAP_FAILED) munmap(base_, size_);
-    if (owner_) shm_unlink(name_.c_str());
-  }
-
-  uint64_t slot_bytes() const { return h_->slot_bytes; }
-
-  // Returns false on timeout (a reader did not free the slot in time).
-  bool publish(const std::string& s, double timeout_s) {
-    if (s.size() > h_->slot_bytes) throw std::invalid_argument("message larger than ring slot");
-    uint64_t w = h_->write_seq.load(std::memory_order_relaxed);
-    auto deadline = std::chrono::steady_clock::now() + std::chrono::duration<double>(timeout_s);
-    for (;;) {  // slot w % n is free once every reader consumed message w - n
-      uint64_t min_r = UINT64_MAX;
-      for (uint32_t i = 0; i < h_->num_readers; ++i)
-        min_r = std::min<uint64_t>(min_r, h_->read_seq[i].load(std::memory_order_acquire));
-      if (h_->num_readers == 0 || w - min_r < h_->num_slots) break;
-      if (std::chrono::steady_clock::now() > deadline) return false;
-      std::this_thread::yield();
-    }
-    uint8_t* slot = data_ + (w % h_->num_slots) * (h_->slot_bytes + 8);
-    uint64_t len = s.size();
-    std::memcpy(slot, &len, 8);
-    std::memcpy(slot + 8, s.data(), s.size());
-    h_->write_seq.store(w + 1, std::memory_order_release);
-    return true;
-  }
-
-  // Returns None on timeout or when the ring is closed and drained.
-  py::object consume(uint32_t reader, double timeout_s) {
-    if (reader >= h_->num_readers) throw std::invalid_argument("bad reader index");
-    uint64_t r = h_->read_seq[reader].load(std::memory_order_relaxed);
-    bool ready = false;
-    {
-      py::gil_scoped_release nogil;
-      auto deadline = std::chrono::steady_clock::now() + std::chrono::duration<double>(timeout_s);
-      for (;;) {
-        if (h_->write_seq.load(std::memory_order_acquire) > r) { ready = true; break; }
-        if (h_->closed.load() || std::chrono::steady_clock::now() > deadline) break;
-        std::this_thread::yield();
-      }
-    }
-    if (!ready) return py::none();
-    uint8_t* slot = data_ + (r % h_->num_slots) * (h_->slot_bytes + 8);
-    uint64_t len;
-    std::memcpy(&len, slot, 8);
-    py::bytes out(reinterpret_cast<const char*>(slot + 8), len);
-    h_->read_seq[reader].store(r + 1, std::memory_order_release);
-    return out;
-  }
-
-  void close_ring() { h_->closed.store(1); }
-  bool closed() const { return h_->closed.load() != 0; }
-  uint64_t published() const { return h_->write_seq.load(); }
-
- private:
-  std::string name_;
-  bool owner_;
-  size_t size_ = 0;
-  uint8_t* base_ = nullptr;
-  uint8_t* data_ = nullptr;
-  RingHeader* h_ = nullptr;
-};
-
 // ---------------------------------------------------------------- NUMA
 std::string read_file(const std::string& p) {
   std::ifstream f(p);
@@ -303,13 +178,31 @@ void bind_runtime(py::module_& m) {
       .def("release", &SizeClassPool::release)
       .def("stats", &SizeClassPool::stats)
       .def_static("size_class", [](size_t n) { return size_t(1) << SizeClassPool::cls(n); });
+  using rzhost::ShmRing;
   py::class_<ShmRing>(m, "ShmRing")
       .def(py::init<const std::string&, bool, uint32_t, uint64_t, uint32_t>(), py::arg("name"),
            py::arg("create"), py::arg("num_slots") = 8, py::arg("slot_bytes") = 1 << 20,
            py::arg("num_readers") = 1)
-      .def("publish", &ShmRing::publish, py::arg("msg"), py::arg("timeout_s") = 10.0,
-           py::call_guard<py::gil_scoped_release>())
-      .def("consume", &ShmRing::consume, py::arg("reader"), py::arg("timeout_s") = 10.0)
+      .def(
+          "publish",
+          [](ShmRing& r, const std::string& msg, double timeout_s) {
+            py::gil_scoped_release nogil;
+            return r.publish(msg.data(), msg.size(), timeout_s);
+          },
+          py::arg("msg"), py::arg("timeout_s") = 10.0)
+      .def(
+          "consume",
+          [](ShmRing& r, uint32_t reader, double timeout_s) -> py::object {
+            std::string out;
+            bool ok;
+            {
+              py::gil_scoped_release nogil;
+              ok = r.consume(reader, timeout_s, &out);
+            }
+            if (!ok) return py::none();
+            return py::bytes(out);
+          },
+          py::arg("reader"), py::arg("timeout_s") = 10.0)
       .def("close", &ShmRing::close_ring)
       .def_property_readonly("closed", &ShmRing::closed)
       .def_property_readonly("published", &ShmRing::published)
