@@ -103,3 +103,47 @@ def test_abort_frees_blocks():
     assert eng.bm.num_free_gpu_blocks() < 64
     eng.abort_request("x")
     assert eng.bm.num_free_gpu_blocks() == 64 and not eng.has_unfinished_requests()
+
+
+def test_async_engine_stall_watchdog_marks_not_ready_then_recovers():
+    """A step that blocks (a stand-in for a collective waiting on a dead peer) makes the
+    engine not ready after stall_timeout_s; when the step returns, readiness comes back."""
+    import threading
+    import time
+    from rusteeze_b200.engine.async_engine import AsyncLLMEngine
+
+    class _StuckEngine:
+        device = "cpu"
+
+        def __init__(self):
+            self.release = threading.Event()
+            self.entered = threading.Event()
+            self.pending = True
+
+        def has_unfinished_requests(self):
+            return self.pending
+
+        def step(self):
+            self.entered.set()
+            self.release.wait(10.0)
+            self.pending = False
+            return []
+
+        def abort_request(self, rid):
+            pass
+
+    stub = _StuckEngine()
+    ae = AsyncLLMEngine(stub, stall_timeout_s=0.2).start()
+    try:
+        assert stub.entered.wait(5.0)
+        time.sleep(0.4)
+        assert not ae.is_ready and ae.healthy          # stalled, not failed
+        stub.release.set()
+        for _ in range(100):
+            if ae.is_ready:
+                break
+            time.sleep(0.02)
+        assert ae.is_ready
+    finally:
+        stub.release.set()
+        ae.shutdown()
