@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
     }
   }
   __syncthreads();
-  static_assert(kRsThreads / kRsRowThreads == kAgRowBlock, "one row per 128 threads, one flag block per CTA");
+  static_assert(kRsThreads / kRsRowThreads == kAgRowBlock, "one row per 64 threads, one flag block per CTA");
   __shared__ float s_ss[kAgRowBlock][kRsRowThreads / 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rr = warp >> 1, sub = warp & 1;                  // row of the block, warp within the row
