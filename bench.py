@@ -23,7 +23,7 @@ prefill/decode mixes).  Per rank:
      timed with CUDA events on the engine's stream; MAX over ranks.
   value = output tokens produced in the K steps summed over ranks / max time.
   e2e: a separate run through the public `LLMEngine` API (add_request /
-     step) that serves a fresh 256-request set from submission to the last
+     step) that serves a fresh 512-request set from submission to the last
      token; every step copies its inputs from pinned host memory and reads
      the sampled tokens back.
 The inputs (weights + KV working set) are far larger than the 126 MB L2, so
@@ -166,7 +166,7 @@ def main():
     ap.add_argument("--rate", type=float, default=200.0, help="Poisson arrival rate per GPU (req/s)")
     ap.add_argument("--max-seqs", type=int, default=256)
     ap.add_argument("--max-batched-tokens", type=int, default=4096)
-    ap.add_argument("--e2e-requests", type=int, default=256)
+    ap.add_argument("--e2e-requests", type=int, default=512)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--dtype", default="fp8", choices=["fp8", "bf16"],
                     help="fp8: block-scaled e4m3 weights (the Llama-3-8B serving configuration); bf16: unquantised")
