@@ -167,6 +167,22 @@ void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache
 }
 
 // ---------------------------------------------------------------- GEMM
+// Tail split of a plain GEMM (RZ_GEMM_TAIL_SPLIT=1 and a thin last wave): fp32 partial
+// workspace and zeroed arrival counters.  Returns the launches it adds (the counter fill).
+static int64_t setup_tail_split(rz::GemmParams& p, int k_blocks, int bn, const torch::TensorOptions& opt,
+                                torch::Tensor& ws, torch::Tensor& cnt) {
+  if (!rz::tail_split_enabled() || p.k_splits != 1 || p.epi != rz::kEpiNone || p.ag_flag) return 0;
+  const rz::TailPlan tp = rz::plan_tail_split(p.M, p.N, k_blocks, bn);
+  if (tp.tail_split <= 1) return 0;
+  ws = torch::empty({static_cast<int64_t>(tp.tail_tiles) * tp.tail_split * 128 * bn}, opt.dtype(torch::kFloat32));
+  cnt = torch::zeros({static_cast<int64_t>(tp.tail_tiles) * 8}, opt.dtype(torch::kInt32));
+  p.tail_split = tp.tail_split;
+  p.full_units = tp.full_units;
+  p.tail_ws = ws.data_ptr<float>();
+  p.tail_cnt = reinterpret_cast<uint32_t*>(cnt.data_ptr());
+  return 1;
+}
+
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi) {
   auto pl = rz::plan_gemm(M, N, K, epi);
   return {pl.bn, pl.k_splits};
@@ -198,14 +214,15 @@ int64_t gemm_bf16_ex(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::o
   p.ldr = residual.has_value() ? residual->stride(0) : 0;
   p.epi = epi;
   p.status = status_ptr();
-  torch::Tensor ws;
+  torch::Tensor ws, tail_ws, tail_cnt;
   if (k_splits > 1) {
     ws = torch::empty({k_splits, M, N}, x.options().dtype(torch::kFloat32));
     p.partial = ws.data_ptr<float>();
   }
+  const int64_t extra = setup_tail_split(p, (K + 63) / 64, bn, x.options(), tail_ws, tail_cnt);
   check_rc(rz::gemm_bf16_launch(p, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), bn, cur_stream()),
            "gemm_bf16");
-  return k_splits > 1 ? 2 : 1;
+  return (k_splits > 1 ? 2 : 1) + extra;
 }
 
 int64_t gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
@@ -321,14 +338,15 @@ int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch:
   p.status = status_ptr();
   p.sfa = reinterpret_cast<const uint8_t*>(sfa.data_ptr());
   p.sfb = reinterpret_cast<const uint8_t*>(sfb.data_ptr());
-  torch::Tensor ws;
+  torch::Tensor ws, tail_ws, tail_cnt;
   if (k_splits > 1) {
     ws = torch::empty({k_splits, M, N}, xq.options().dtype(torch::kFloat32));
     p.partial = ws.data_ptr<float>();
   }
+  const int64_t extra = setup_tail_split(p, K / 128, bn, xq.options(), tail_ws, tail_cnt);
   check_rc(rz::gemm_mxf8_launch(p, xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), bn, cur_stream()),
            "gemm_mxf8");
-  return k_splits > 1 ? 2 : 1;
+  return (k_splits > 1 ? 2 : 1) + extra;
 }
 
 // gate/up MXFP8 GEMM whose SiLU(gate)*up epilogue writes the down projection's MXFP8 operand.
@@ -766,6 +784,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("call_idx"), py::arg("moe_topk"), py::arg("moe_flag"),
         py::arg("gathers_q") = std::vector<int64_t>{}, py::arg("gathers_sf") = std::vector<int64_t>{});
   m.def("gemm_peer_rs_mx", &gemm_peer_rs_mx);
+  m.def("gemm_tail_plan", [](int64_t M, int64_t N, int64_t k_blocks, int64_t bn, int64_t sms) {
+    const rz::TailPlan t = rz::plan_tail_split(M, N, k_blocks, bn, sms);
+    return std::vector<int64_t>{t.tail_split, t.full_units, t.tail_tiles};
+  });
   m.def("gemm_mxf8_ag", &gemm_mxf8_ag);
   m.def("moe_forward_peer", &moe_forward_peer);
   m.def("ag_wait", &ag_wait);
