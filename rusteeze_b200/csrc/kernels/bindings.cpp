@@ -466,6 +466,11 @@ int64_t moe_forward(torch::Tensor out, torch::Tensor h, torch::Tensor wr, torch:
   return 6;   // zero-fill, route, permute, 2 grouped GEMMs, combine
 }
 
+// Race testing of the flag protocols: random pauses (below this many ns) before the peer
+// stores and flag releases of the communication kernels; 0 (default) disables them.
+static uint32_t g_comm_jitter_ns = 0;
+void set_comm_jitter_ns(int64_t ns) { g_comm_jitter_ns = static_cast<uint32_t>(ns < 0 ? 0 : ns); }
+
 // Expert-parallel MoE block: local experts, then every local (token, slot) output row is sent to
 // the token's owner rank (slot buffers + flags over NVLink) for rs_norm_ag in MoE mode.
 int64_t moe_forward_peer(torch::Tensor h, torch::Tensor wr, torch::Tensor w13, torch::Tensor w2, int64_t topk,
@@ -487,6 +492,7 @@ int64_t moe_forward_peer(torch::Tensor h, torch::Tensor wr, torch::Tensor w13, t
   cp.M = M; cp.H = H; cp.topk = topk; cp.rs_rows = rs_rows;
   cp.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
   cp.call_idx = static_cast<uint32_t>(call_idx);
+  cp.jitter_ns = g_comm_jitter_ns;
   check_rc(rz::moe_combine_peer_launch(cp, cur_stream()), "moe_combine_peer");
   return 6;
 }
@@ -512,6 +518,7 @@ void moe_route(torch::Tensor tw, torch::Tensor tid, torch::Tensor counts, torch:
 }
 
 // ---------------------------------------------------------------- fused tensor-parallel boundary
+
 // Row-parallel GEMM whose epilogue reduce-scatters into the owners' slot buffers.  Returns n_tiles.
 int64_t gemm_peer_rs(torch::Tensor x, torch::Tensor w, std::vector<int64_t> slots, std::vector<int64_t> flags,
                      int64_t rank, int64_t rs_rows, torch::Tensor epoch, int64_t call_idx, int64_t bn) {
@@ -536,6 +543,7 @@ int64_t gemm_peer_rs(torch::Tensor x, torch::Tensor w, std::vector<int64_t> slot
   p.tp_rank = rank; p.tp_world = world;
   p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
   p.call_idx = static_cast<uint32_t>(call_idx);
+  p.jitter_ns = g_comm_jitter_ns;
   check_rc(rz::gemm_bf16_launch(p, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), bn, cur_stream()),
            "gemm_peer_rs");
   return (N + bn - 1) / bn;
@@ -600,6 +608,7 @@ int64_t gemm_peer_rs_mx(torch::Tensor xq, torch::Tensor sfa, torch::Tensor wq, t
   p.tp_rank = rank; p.tp_world = world;
   p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
   p.call_idx = static_cast<uint32_t>(call_idx);
+  p.jitter_ns = g_comm_jitter_ns;
   check_rc(rz::gemm_mxf8_launch(p, xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), bn, cur_stream()),
            "gemm_peer_rs_mx");
   return (N + bn - 1) / bn;
@@ -683,6 +692,7 @@ void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10
     TORCH_CHECK(moe_flag.has_value(), "rs_norm_ag: MoE mode needs the moe flags");
     p.moe_flag = reinterpret_cast<const uint32_t*>(moe_flag->data_ptr());
   }
+  p.jitter_ns = g_comm_jitter_ns;
   p.mx = gathers_q.empty() ? 0 : 1;
   if (p.mx) {
     TORCH_CHECK(gathers_q.size() == gathers.size() && gathers_sf.size() == gathers.size(),
@@ -784,6 +794,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("call_idx"), py::arg("moe_topk"), py::arg("moe_flag"),
         py::arg("gathers_q") = std::vector<int64_t>{}, py::arg("gathers_sf") = std::vector<int64_t>{});
   m.def("gemm_peer_rs_mx", &gemm_peer_rs_mx);
+  m.def("set_comm_jitter_ns", &set_comm_jitter_ns);
   m.def("gemm_tail_plan", [](int64_t M, int64_t N, int64_t k_blocks, int64_t bn, int64_t sms) {
     const rz::TailPlan t = rz::plan_tail_split(M, N, k_blocks, bn, sms);
     return std::vector<int64_t>{t.tail_split, t.full_units, t.tail_tiles};

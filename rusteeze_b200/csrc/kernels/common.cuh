@@ -40,6 +40,17 @@ RZ_DEVICE uint64_t globaltimer() {
   return t;
 }
 
+// Race testing of the flag protocols: a pseudo-random pause below max_ns (0: none) keyed by
+// (a, b, c), so producers publish in shuffled orders and consumers wait at random points.
+RZ_DEVICE void jitter_ns(uint32_t max_ns, uint32_t a, uint32_t b, uint32_t c) {
+  if (max_ns == 0) return;
+  uint32_t h = a * 0x9E3779B1u ^ (b + 0x7F4A7C15u) * 0x85EBCA77u ^ (c + 0x165667B1u) * 0xC2B2AE3Du;
+  h ^= h >> 15;
+  h *= 0x2C1B3C6Du;
+  h ^= h >> 12;
+  __nanosleep(h % max_ns);
+}
+
 RZ_DEVICE float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 RZ_DEVICE __nv_bfloat16 f2bf(float x) { return __float2bfloat16_rn(x); }
 

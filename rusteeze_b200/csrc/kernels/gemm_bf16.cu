@@ -458,6 +458,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // contiguous bytes of one row: 64-byte peer writes instead of 16-byte ones.
           uint4* stg = sm_out + (warp - 2) * 128;
           const int r0 = mb * kBM + quarter * 32;
+          jitter_ns(p.jitter_ns, epoch, static_cast<uint32_t>(t), static_cast<uint32_t>(warp));
 #pragma unroll
           for (int c = 0; c < NC; ++c) {
             const int col0 = colh + c * 32;
@@ -491,6 +492,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // touch (the warp barrier orders all lanes' stores before lane 0's fence + release)
           __syncwarp();
           if (lane == 0 && r0 < p.M) {
+            jitter_ns(p.jitter_ns, epoch + 1u, static_cast<uint32_t>(t), static_cast<uint32_t>(warp));
             __threadfence_system();
             const int r1 = min(p.M, r0 + 32) - 1;
             for (int o = r0 / p.rs_rows; o <= r1 / p.rs_rows; ++o)

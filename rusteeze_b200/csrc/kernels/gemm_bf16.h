@@ -52,6 +52,7 @@ struct GemmParams {
   uint32_t call_idx;
   uint8_t* q_out;              // kEpiSiluMulMx outputs
   uint8_t* sf_out;
+  uint32_t jitter_ns;          // kEpiPeerRS race testing: random pauses before stores and flags (0: off)
   // Tail split (k_splits == 1, kEpiNone, no communication): when the last wave is thin,
   // the tiles after the first full_units (in unit order) run as tail_split K ranges
   // each.  A split stores its fp32 partial of every warp region into

@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
   }
   ss = warp_sum(ss);
   if (lane == 0) s_ss[rr][sub] = ss;
+  jitter_ns(p.jitter_ns, epoch, blockIdx.x, static_cast<uint32_t>(warp));
   __syncthreads();
   if (live && p.mx) {
     // MXFP8 rows: the 16 chunks of a 128-column block belong to one half-warp (chunk
@@ -202,6 +203,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
   // system-scope fence + release (cumulative), so one fence per destination suffices
   __syncthreads();
   if (threadIdx.x < p.world && g0 < p.M) {
+    jitter_ns(p.jitter_ns, epoch + 1u, blockIdx.x, threadIdx.x);
     __threadfence_system();
     st_release_sys_u32(p.ag_flag[threadIdx.x] + g0 / kAgRowBlock, epoch);
   }
@@ -232,6 +234,7 @@ __global__ void __launch_bounds__(256) moe_combine_peer_kernel(MoeCombinePeerPar
     }
     __syncwarp();
     if (lane == 0) {
+      jitter_ns(p.jitter_ns, epoch, static_cast<uint32_t>(i), blockIdx.x);
       __threadfence_system();
       st_release_sys_u32(p.flag[owner] + static_cast<size_t>(k) * p.rs_rows + li, epoch);
     }

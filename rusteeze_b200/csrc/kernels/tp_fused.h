@@ -35,6 +35,7 @@ struct RsNormAgParams {
   int mx;
   uint8_t* gather_q[kMaxTpRanks];
   uint8_t* gather_sf[kMaxTpRanks];
+  uint32_t jitter_ns;                  // race testing: random pauses before stores and flags (0: off)
 };
 
 // Expert-parallel combine: every local (token, slot) pair's weighted expert output row goes
@@ -48,6 +49,7 @@ struct MoeCombinePeerParams {
   int M, H, topk, rs_rows;
   const uint32_t* epoch_ptr;
   uint32_t call_idx;
+  uint32_t jitter_ns;               // race testing: random pause before each flag (0: off)
 };
 
 int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st);

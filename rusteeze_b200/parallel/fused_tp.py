@@ -33,6 +33,7 @@ scales]; peers' bases come from the rendezvous.  The reference has no collective
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -100,6 +101,11 @@ class FusedTP:
         self.residual = torch.empty(self.max_rs_rows, hidden, dtype=torch.bfloat16, device=device)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
         self.n_tiles = 1
+        # race testing of the flag protocols: RZ_TP_JITTER_NS=<ns> makes the communication
+        # kernels pause pseudo-randomly before their peer stores and flag releases
+        jitter = int(os.environ.get("RZ_TP_JITTER_NS", "0") or 0)
+        if jitter:
+            ops.cuda_ext().set_comm_jitter_ns(jitter)
         dist.barrier(group=self.group)
 
     # ------------------------------------------------------------------ shapes

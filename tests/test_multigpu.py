@@ -64,9 +64,9 @@ def test_peer_all_reduce_matches_nccl():
         assert err < 2e-2, f"rank {rank} rel err {err}"
 
 
-def _boundary_worker(rank, world, port, q):
+def _boundary_worker(rank, world, port, q, jitter_ns=0):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
-                      MASTER_PORT=str(port))
+                      MASTER_PORT=str(port), RZ_TP_JITTER_NS=str(jitter_ns))
     import torch.distributed as dist
     from rusteeze_b200 import ops
     from rusteeze_b200.parallel.dist import init_distributed
@@ -104,7 +104,11 @@ def _boundary_worker(rank, world, port, q):
 
 
 @pytest.mark.timeout(300)
-def test_fused_tp_boundary_matches_reference():
+@pytest.mark.parametrize("jitter_ns", [0, pytest.param(20000, marks=pytest.mark.skipif(
+    os.environ.get("RZ_TP_JITTER_TEST", "0") != "1", reason="flag-protocol jitter run is opt-in (RZ_TP_JITTER_TEST=1)"))])
+def test_fused_tp_boundary_matches_reference(jitter_ns):
+    """Fused boundary vs reference; with jitter_ns the producers pause pseudo-randomly
+    (up to 20 us) before their peer stores and flag releases, shuffling arrival orders."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -112,7 +116,7 @@ def test_fused_tp_boundary_matches_reference():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_boundary_worker, args=(r, world, port, q)) for r in range(world)]
+    ps = [ctx.Process(target=_boundary_worker, args=(r, world, port, q, jitter_ns)) for r in range(world)]
     for p in ps:
         p.start()
     res = [q.get(timeout=240) for _ in range(world)]
