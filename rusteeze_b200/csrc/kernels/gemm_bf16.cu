@@ -95,9 +95,10 @@ struct UnitWork {
   int t, kb0, kb1, ks, tail;
 };
 
+template <bool TAIL>
 __device__ __forceinline__ UnitWork unit_work(const GemmParams& p, int u) {
   UnitWork w;
-  if (p.tail_split > 1 && u >= p.full_units) {
+  if (TAIL && u >= p.full_units) {
     const int v = u - p.full_units;
     const int per = (p.k_blocks + p.tail_split - 1) / p.tail_split;
     w.tail = v / p.tail_split;
@@ -115,7 +116,7 @@ __device__ __forceinline__ UnitWork unit_work(const GemmParams& p, int u) {
   return w;
 }
 
-template <int BN, bool MX, bool PEER>
+template <int BN, bool MX, bool PEER, bool TAIL>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  GemmParams p) {
@@ -152,8 +153,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       s_grp[i] = i <= G ? p.grp_off[i] : p.grp_end[i - G - 1];
   }
   const int m_tiles = G ? p.grp_off[G] / kBM : p.m_tiles;
-  const int num_units = p.tail_split > 1 ? p.full_units + (m_tiles * p.n_tiles - p.full_units) * p.tail_split
-                                         : m_tiles * p.n_tiles * p.k_splits;
+  const int num_units = TAIL ? p.full_units + (m_tiles * p.n_tiles - p.full_units) * p.tail_split
+                            : m_tiles * p.n_tiles * p.k_splits;
   const uint32_t epoch =
       p.epoch_ptr ? *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u : 0u;
   // GEMMs that feed or consume a collective finish whole m tiles first: the reduce-scatter
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       uint64_t ag_ready = 0;                 // m tiles whose all-gathered rows were already seen
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        const UnitWork w = unit_work(p, u);
+        const UnitWork w = unit_work<TAIL>(p, u);
         const int t = w.t;
         const int mb = row_major ? t / p.n_tiles : t % m_tiles;
         const int nb = row_major ? t % p.n_tiles : t / m_tiles;
@@ -247,7 +248,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t aph = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        const UnitWork w = unit_work(p, u);
+        const UnitWork w = unit_work<TAIL>(p, u);
         const int kb0 = w.kb0, kb1 = w.kb1;
         if (!mbar_wait(&tempty[acc], aph ^ 1, p.status, kGemmMmaTimeout)) { ok = false; break; }
         tc_fence_after();
@@ -303,7 +304,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t aph = 0;
     uint32_t xph = 0;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
-      const UnitWork w = unit_work(p, u);
+      const UnitWork w = unit_work<TAIL>(p, u);
       const int ks = w.ks;
       const int t = w.t;
       const int mb = row_major ? t / p.n_tiles : t % m_tiles;
@@ -390,7 +391,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_arrive(&tempty[acc]);
         const int colh = nb * BN + half * (BN / 2);
         bool finish = true;                  // this unit stores its region of the tile
-        if (w.tail >= 0) {
+        if (TAIL && w.tail >= 0) {
           // tail split: publish this split's fp32 partial of the warp's region; the split that
           // arrives last sums every partial in split order (reproducible) and stores the tile
           const int S = p.tail_split;
@@ -632,7 +633,7 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool MX, bool PEER>
+template <int BN, bool MX, bool PEER, bool TAIL>
 static int launch_inst(const GemmParams& p0, const void* A, int lda, const void* B, int ldb, cudaStream_t st) {
   using C = GemmCfg<BN, MX, PEER>;
   constexpr int kElems = MX ? kBKMx : kBK;
@@ -644,15 +645,16 @@ static int launch_inst(const GemmParams& p0, const void* A, int lda, const void*
   GemmParams p = p0;
   p.m_tiles = (p.M + kBM - 1) / kBM;
   p.n_tiles = (p.N + BN - 1) / BN;
-  if (p.tail_split > 1 && (p.k_splits != 1 || p.epi != kEpiNone || p.ag_flag || PEER || !p.tail_ws ||
-                           !p.tail_cnt || p.full_units < 0 || p.full_units >= p.m_tiles * p.n_tiles))
+  if (TAIL && (p.tail_split < 2 || p.k_splits != 1 || p.epi != kEpiNone || p.ag_flag || PEER || !p.tail_ws ||
+               !p.tail_cnt || p.full_units < 0 || p.full_units >= p.m_tiles * p.n_tiles))
     return -6;
-  const int units = p.tail_split > 1 ? p.full_units + (p.m_tiles * p.n_tiles - p.full_units) * p.tail_split
-                                     : p.m_tiles * p.n_tiles * p.k_splits;
+  const int units = TAIL ? p.full_units + (p.m_tiles * p.n_tiles - p.full_units) * p.tail_split
+                         : p.m_tiles * p.n_tiles * p.k_splits;
   const int grid = units < num_sms() ? units : num_sms();
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_tcgen05<BN, MX, PEER>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    cudaFuncSetAttribute(gemm_tcgen05<BN, MX, PEER, TAIL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         C::kSmemBytes);
     attr_set = true;
   }
   if (p.ag_flag) {
@@ -668,10 +670,10 @@ static int launch_inst(const GemmParams& p0, const void* A, int lda, const void*
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05<BN, MX, PEER>, ta, tb, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05<BN, MX, PEER, TAIL>, ta, tb, p);
     if (e != cudaSuccess) return static_cast<int>(e);
   } else {
-    gemm_tcgen05<BN, MX, PEER><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);
+    gemm_tcgen05<BN, MX, PEER, TAIL><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);
   }
   if (p.k_splits > 1) {
     const int ncols_out = p.epi == kEpiSiluMul ? p.N / 2 : p.N;
@@ -681,11 +683,13 @@ static int launch_inst(const GemmParams& p0, const void* A, int lda, const void*
   return static_cast<int>(cudaGetLastError());
 }
 
-// reduce-scatter GEMMs use the instance with the epilogue transpose buffer
+// reduce-scatter GEMMs use the instance with the epilogue transpose buffer, tail-split
+// GEMMs the one with the partial-sum path; every other GEMM carries neither
 template <int BN, bool MX>
 static int launch_bn(const GemmParams& p, const void* A, int lda, const void* B, int ldb, cudaStream_t st) {
-  return p.epi == kEpiPeerRS ? launch_inst<BN, MX, true>(p, A, lda, B, ldb, st)
-                             : launch_inst<BN, MX, false>(p, A, lda, B, ldb, st);
+  if (p.epi == kEpiPeerRS) return launch_inst<BN, MX, true, false>(p, A, lda, B, ldb, st);
+  if (p.tail_split > 1) return launch_inst<BN, MX, false, true>(p, A, lda, B, ldb, st);
+  return launch_inst<BN, MX, false, false>(p, A, lda, B, ldb, st);
 }
 
 // RZ_GEMM_TAIL_SPLIT=1 enables the tail split for plain (kEpiNone) GEMMs.
@@ -787,11 +791,11 @@ int gemm_grouped_launch(const GemmParams& p_in, const void* A, int lda, int64_t 
     using C = GemmCfg<BNV, MXV, false>;                                                                       \
     static bool attr = false;                                                                                 \
     if (!attr) {                                                                                              \
-      cudaFuncSetAttribute(gemm_tcgen05<BNV, MXV, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,        \
+      cudaFuncSetAttribute(gemm_tcgen05<BNV, MXV, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                            C::kSmemBytes);                                                                    \
       attr = true;                                                                                            \
     }                                                                                                         \
-    gemm_tcgen05<BNV, MXV, false><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);                      \
+    gemm_tcgen05<BNV, MXV, false, false><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);               \
   }
   if (!mx && bn == 256) RZ_GROUPED(256, false)
   else if (!mx && bn == 128) RZ_GROUPED(128, false)
