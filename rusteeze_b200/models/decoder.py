@@ -345,6 +345,8 @@ class DecoderLM(nn.Module):
             act = F.gemm_ag(x, L.gate_up_il, c_attn, silu_mul=True)
             F.gemm_rs(act, L.down, c_mlp)
             x = F.rs_norm_ag(M, nw, eps, off, c_mlp)
+        # the LM head reads every owner's final rows from the local gather buffer
+        F.wait_gathered(M, 2 * n)
         F.end_step()
         return x
 

@@ -202,6 +202,13 @@ class FusedTP:
                                                 call_idx))
         return out
 
+    def wait_gathered(self, M: int, call_idx: int) -> None:
+        """Waits (bounded, on the device) until every owner's rows of boundary `call_idx`
+        have landed in the local gather buffer; a consumer that is not a flag-waiting
+        GEMM (the LM head reads the final boundary's rows) needs it."""
+        ops.cuda_ext().ag_wait(self.ag_flag, M, self.epoch, call_idx)
+        ops.add_launches(1)
+
     def end_step(self) -> None:
         ops.cuda_ext().tp_epoch_bump(self.epoch)
         ops.add_launches(1)
