@@ -132,9 +132,10 @@ class LLMEngine:
                                "requests_finished": 0, "requests_aborted": 0}
         self.observers: List[Callable] = []
         self.phase_s: Dict[str, float] = {"schedule": 0.0, "postprocess": 0.0}
-        # asynchronous scheduling: single-process CUDA engine without speculation
+        # asynchronous scheduling: CUDA engine without speculation over a runner (or a
+        # tensor-parallel executor) that can pipeline steps
         self._async = (ec.async_scheduling and self.device.startswith("cuda") and spec is None
-                       and hasattr(self.runner, "launch") and executor is None)
+                       and getattr(self.runner, "supports_async", False))
         self._inflight: List[_InFlight] = []
         self._n_sync_only = 0
         self.spec = None

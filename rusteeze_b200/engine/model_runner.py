@@ -74,6 +74,8 @@ def decode_workspace_floats(max_seqs: int, num_q_heads: int, num_kv_heads: int, 
 
 
 class ModelRunner:
+    supports_async = True     # launch / finish: the engine may pipeline steps over this runner
+
     def __init__(self, model: DecoderLM, *, num_gpu_blocks: int, num_cpu_blocks: int,
                  max_num_seqs: int, max_num_batched_tokens: int, max_model_len: int,
                  kv_dtype=None, use_cuda_graph: bool = True, seed: int = 0):
@@ -194,6 +196,7 @@ class ModelRunner:
             toks = np.concatenate(parts)
         else:
             toks = np.zeros(0, dtype=np.int64)
+        self.last_pend = (pend_dst, pend_src)     # the scatter a tensor-parallel worker repeats
         T = bm.build_batch(seq_ids, ctx, n_new, toks, self.h_input_ids.data_ptr(),
                            self.h_positions.data_ptr(), self.h_slots.data_ptr(), self.h_qsl.data_ptr(),
                            self.h_seq_lens.data_ptr(), self.h_block_tables.data_ptr(),

@@ -50,6 +50,7 @@ class AsyncSample:
     host: torch.Tensor            # pinned [2, >=R] float64: token ids, logprobs
     rows: int
     event: "torch.cuda.Event"
+    result: Optional["SampleResult"] = None    # host-sampled rows (CPU engines): already known
 
 
 @dataclass
@@ -114,6 +115,10 @@ class Sampler:
         host memory; `finish` waits for them.  Device rows only."""
         R = logits.shape[0]
         self.last_h2d_bytes = 0
+        if not logits.is_cuda:
+            # CPU engines (tests of the pipelined schedule): sample now, hand back the same handle
+            res = self.sample(logits, rows)
+            return AsyncSample(torch.tensor(res.tokens, dtype=torch.int64), None, R, None, res)
         toks, lp = self._sample_device_async(logits, rows)
         # every host staging buffer is 1-D and only used through contiguous
         # prefixes: a strided pinned slice would make torch stage the copy
@@ -131,6 +136,9 @@ class Sampler:
         return AsyncSample(toks, buf, R, ev)
 
     def finish(self, a: "AsyncSample") -> SampleResult:
+        if a.result is not None:
+            self.last_d2h_bytes = 0
+            return a.result
         a.event.synchronize()
         R = a.rows
         self.last_d2h_bytes = 16 * R

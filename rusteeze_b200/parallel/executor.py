@@ -62,7 +62,15 @@ class PlanChannel:
 
 
 class TPExecutor:
-    """Drop-in for ModelRunner on rank 0 (`LLMEngine(executor=...)`)."""
+    """Drop-in for ModelRunner on rank 0 (`LLMEngine(executor=...)`).
+
+    Pipelined steps (`launch` / `finish`, RZ_TP_ASYNC=1 on GPUs): the next step's plan is
+    published before the previous step's tokens are read back.  Decode inputs still on
+    the device are scattered from the previous step's sample tensor, which rank 0
+    broadcasts to the workers (device to device, one small collective ordered before the
+    step's forward); the plan carries the scatter lists."""
+
+    supports_async = os.environ.get("RZ_TP_ASYNC", "0") == "1"
 
     def __init__(self, runner: ModelRunner, channel: PlanChannel, liveness=None):
         self.runner = runner
@@ -71,6 +79,7 @@ class TPExecutor:
         # checked before every plan so a dead rank is reported instead of stalling a collective
         self.liveness = liveness
         self._tstate: dict = {}
+        self.broadcast_steps = 0     # pipelined steps whose decode inputs came from the previous sample
 
     def __getattr__(self, k):
         return getattr(self.runner, k)
@@ -107,6 +116,36 @@ class TPExecutor:
         r.h2d_bytes += r.sampler.last_h2d_bytes
         r.d2h_bytes += r.sampler.last_d2h_bytes
         return res
+
+    @torch.no_grad()
+    def launch(self, so, bm, rows, prev_tokens):
+        """Enqueues a step on every rank without waiting for the previous one's tokens."""
+        import torch.distributed as dist
+        self._check_workers()
+        r = self.runner
+        if so.blocks_to_swap_out:
+            r.swap_out(so.blocks_to_swap_out)
+        if so.blocks_to_swap_in:
+            r.swap_in(so.blocks_to_swap_in)
+        if so.blocks_to_copy:
+            r.copy_blocks(so.blocks_to_copy)
+        meta, T, S, sample_rows = r.prepare(so, bm, prev_tokens)
+        pend_dst, pend_src = r.last_pend
+        nb = int(prev_tokens.numel()) if pend_dst else 0
+        plan = {"pure": not so.prefills, "rows": sample_rows, "copy": so.blocks_to_copy,
+                "sin": so.blocks_to_swap_in, "sout": so.blocks_to_swap_out, "bcast": nb,
+                "pend": (list(pend_dst), list(pend_src)), **_staged_plan(r, meta, T, S)}
+        self.ch.publish(MSG_STEP, plan)
+        if nb:
+            dist.broadcast(prev_tokens.contiguous(), src=0)
+            self.broadcast_steps += 1
+        logits = r.forward_logits(meta, T, S, sample_rows, pure_decode=not so.prefills)
+        handle = r.sampler.launch(logits, rows)
+        r.h2d_bytes += r.sampler.last_h2d_bytes
+        return handle
+
+    def finish(self, handle) -> SampleResult:
+        return self.runner.finish(handle)
 
     @torch.no_grad()
     def forward_arrays(self, bm, seq_ids, ctx, n_new, toks, logits_per_seq: int,
@@ -244,6 +283,16 @@ def worker_loop(runner: ModelRunner, channel: PlanChannel, idle_timeout_s: float
             runner.swap_in(plan["sin"])
         if plan["copy"]:
             runner.copy_blocks(plan["copy"])
+        prev = None
+        if plan.get("bcast"):
+            # pipelined steps: rank 0's previous sample tensor, for the decode inputs below
+            import torch.distributed as dist
+            prev = torch.empty(plan["bcast"], dtype=torch.int64, device=runner.device)
+            dist.broadcast(prev, src=0)
         meta, T, S = stage_plan(runner, plan)
+        if prev is not None:
+            dst, src = plan["pend"]
+            idx = torch.tensor(dst + src, dtype=torch.int64).to(runner.device, non_blocking=runner.is_cuda)
+            runner.d_input_ids.index_copy_(0, idx[:len(dst)], prev.index_select(0, idx[len(dst):]))
         runner.forward_logits(meta, T, S, plan["rows"], pure_decode=plan["pure"])
         steps += 1
