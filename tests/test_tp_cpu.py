@@ -219,3 +219,27 @@ def test_pipelined_schedule_matches_sync_single_process_and_tp2():
     assert broadcasts > 0                              # decode inputs really came from the device
     assert got == ref
     assert again == [r[:5] for r in ref[:2]]
+
+
+@pytest.mark.timeout(300)
+def test_tp2_prefix_caching_matches_single_process():
+    """Prompts sharing a long prefix on a TP2 engine with prefix caching: cached blocks
+    are reused on every rank (the plan's block tables point at them), and the greedy
+    tokens equal the single-process engine without caching."""
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    rng = np.random.default_rng(5)
+    prefix = rng.integers(0, 1000, 64).tolist()
+    prompts = [prefix + rng.integers(0, 1000, int(n)).tolist() for n in (5, 17, 9)]
+    ref = _run(LLMEngine(_cfg(1), model_config=MC), prompts, n=6)
+    cfg = _cfg(2)
+    cfg.engine.enable_prefix_caching = True
+    launcher = TPEngineLauncher(cfg, model_config=MC, device_type="cpu")
+    try:
+        eng = launcher.engine()
+        first = _run(eng, prompts[:1], n=6)            # fills the cache with the prefix blocks
+        rest = _run(eng, prompts[1:], n=6)
+        hits = eng.bm.stats()["prefix_block_hits"]
+    finally:
+        launcher.shutdown()
+    assert first + rest == ref
+    assert hits > 0                                   # the later prompts reused the prefix blocks
