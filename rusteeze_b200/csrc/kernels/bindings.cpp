@@ -795,6 +795,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gathers_q") = std::vector<int64_t>{}, py::arg("gathers_sf") = std::vector<int64_t>{});
   m.def("gemm_peer_rs_mx", &gemm_peer_rs_mx);
   m.def("set_comm_jitter_ns", &set_comm_jitter_ns);
+  m.def("gemm_tail_split_enabled", &rz::tail_split_enabled);
   m.def("gemm_tail_plan", [](int64_t M, int64_t N, int64_t k_blocks, int64_t bn, int64_t sms) {
     const rz::TailPlan t = rz::plan_tail_split(M, N, k_blocks, bn, sms);
     return std::vector<int64_t>{t.tail_split, t.full_units, t.tail_tiles};

@@ -7,7 +7,9 @@ launching stream (synchronize on both sides), inputs sized above the 126 MB
 L2 where the op is memory-bound (weights / KV caches), and the achieved
 rate divided by the measured peaks in MEASURED_PEAKS.json (HBM copy GB/s and
 cuBLAS bf16 TFLOP/s) when present.  cuBLAS (torch.matmul) is timed on the
-same shapes as the library baseline for the GEMM.
+same shapes as the library baseline for the GEMM.  GEMM rows report the tile plan
+(bn, k_splits) and the tail split in effect: compare a run with RZ_GEMM_TAIL_SPLIT=1
+against one without to see what splitting a thin last wave buys at each shape.
 """
 from __future__ import annotations
 
@@ -75,8 +77,12 @@ def bench_gemm(pk, shapes=None) -> List[dict]:
         tc = time_ms(cublas)
         flops = 2.0 * M * N * K
         bytes_ = (N * K + M * K + M * N) * 2
-        plan = ops.cuda_ext().gemm_plan(M, N, K, 0)
+        C = ops.cuda_ext()
+        plan = C.gemm_plan(M, N, K, 0)
+        tail = C.gemm_tail_plan(M, N, (K + 63) // 64, plan[0], 0)[0] if (C.gemm_tail_split_enabled() and
+                                                                        plan[1] == 1) else 1
         out.append({"kernel": "gemm_bf16_tcgen05", "M": M, "N": N, "K": K, "bn": plan[0], "k_splits": plan[1],
+                    "tail_split": tail,
                     "ms": round(t, 4), "tflops": round(flops / t / 1e9, 1),
                     "frac_of_measured_bf16": round(flops / t / 1e9 / pk["bf16_tflops"], 3),
                     "gbs": round(bytes_ / t / 1e6, 1), "frac_of_measured_hbm": round(bytes_ / t / 1e6 / pk["hbm_gbs"], 3),
@@ -137,7 +143,10 @@ def bench_gemm_mxf8(pk, shapes=None, bns=(0, 128, 256)) -> List[dict]:
             flops = 2.0 * M * N * K
             bytes_ = N * K + M * K * 2 + M * N * 2
             plan = list(C.gemm_plan_mxf8(M, N, K, 0)) if bn == 0 else [bn, 1]
+            tail = C.gemm_tail_plan(M, N, K // 128, plan[0], 0)[0] if (C.gemm_tail_split_enabled() and
+                                                                       plan[1] == 1) else 1
             out.append({"kernel": "gemm_mxf8_tcgen05", "M": M, "N": N, "K": K, "bn": plan[0], "k_splits": plan[1],
+                        "tail_split": tail,
                         "ms": round(t, 4), "tflops": round(flops / t / 1e9, 1), "gbs": round(bytes_ / t / 1e6, 1),
                         "frac_of_measured_hbm": round(bytes_ / t / 1e6 / pk["hbm_gbs"], 3)})
         del ws
