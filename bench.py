@@ -88,6 +88,60 @@ class ClockSampler:
         return summarize_clocks(self.lines)
 
 
+class Device:
+    """The measured device: CUDA events and synchronisation on a GPU; the host clock on
+    CPU, where tiny models exercise the harness itself (those runs are not benchmarks)."""
+
+    def __init__(self, device: str):
+        import torch
+        self.torch = torch
+        self.name = device
+        self.cuda = device.startswith("cuda")
+
+    def sync(self) -> None:
+        if self.cuda:
+            self.torch.cuda.synchronize()
+
+    def stream(self):
+        return self.torch.cuda.current_stream() if self.cuda else None
+
+    def event(self) -> "Event":
+        return Event(self)
+
+    def nvtx(self, name: str = None) -> None:
+        if self.cuda:
+            if name is None:
+                self.torch.cuda.nvtx.range_pop()
+            else:
+                self.torch.cuda.nvtx.range_push(name)
+
+    def kernel_status(self) -> int:
+        if not self.cuda:
+            return 0
+        from rusteeze_b200 import ops
+        return int(ops.cuda_ext().status()[0])
+
+    def pinned(self, values):
+        t = self.torch.tensor(values, dtype=self.torch.int64)
+        return t.pin_memory() if self.cuda else t
+
+
+class Event:
+    def __init__(self, dev: Device):
+        self.dev = dev
+        self.ev = dev.torch.cuda.Event(enable_timing=True) if dev.cuda else None
+        self.t = None
+
+    def record(self, stream=None) -> None:
+        if self.ev is not None:
+            self.ev.record(stream) if stream is not None else self.ev.record()
+        else:
+            self.t = time.perf_counter()
+
+    def elapsed_ms(self, end: "Event") -> float:
+        return self.ev.elapsed_time(end.ev) if self.ev is not None else (end.t - self.t) * 1e3
+
+
 def summarize_clocks(lines) -> dict:
     """nvidia-smi samples (clocks.sm, clocks.max.sm, power, active mask, then the four
     throttle reasons as Active / Not Active) -> median SM clock, max clock and every
@@ -110,11 +164,11 @@ def summarize_clocks(lines) -> dict:
             "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_workload(n, seed, vocab, rate):
+def build_workload(n, seed, vocab, rate, prompt_len=(128, 2048), output_len=(64, 512)):
     import numpy as np
     rng = np.random.default_rng(seed)
-    plen = rng.integers(128, 2049, n)
-    olen = rng.integers(64, 513, n)
+    plen = rng.integers(prompt_len[0], prompt_len[1] + 1, n)
+    olen = rng.integers(output_len[0], output_len[1] + 1, n)
     gaps = rng.exponential(1.0 / rate, n)
     arrivals = np.cumsum(gaps)
     prompts = [rng.integers(0, vocab, int(p)).tolist() for p in plen]
@@ -131,8 +185,10 @@ def make_config(args, device):
     cfg = Config()
     cfg.model.preset = args.model
     cfg.model.device = device
-    cfg.model.dtype = "bfloat16"
+    cfg.model.dtype = "bfloat16" if device.startswith("cuda") else "float32"
     cfg.model.seed = 0
+    if not device.startswith("cuda"):
+        cfg.engine.num_gpu_blocks = 512          # host-memory KV for the tiny harness models
     if args.dtype == "fp8":
         from rusteeze_b200.config.config import QuantizationConfig
         cfg.model.quantization = QuantizationConfig(method="fp8_block")
@@ -186,6 +242,10 @@ def main():
                     help="speculative decoding: random-init draft preset (e.g. llama-3.2-1b), or 'self'")
     ap.add_argument("--spec-k", type=int, default=4, help="draft tokens per speculative round")
     ap.add_argument("--batches", default="1,8,32,128,256")
+    ap.add_argument("--device", default="cuda", choices=["cuda", "cpu"],
+                    help="cpu runs the harness itself on tiny models (gloo ranks, host clock): not a benchmark")
+    ap.add_argument("--prompt-len", default="128,2048", help="prompt length range of the Poisson workload")
+    ap.add_argument("--output-len", default="64,512", help="output length range of the Poisson workload")
     ap.add_argument("--static-prompt", type=int, default=512)
     ap.add_argument("--static-output", type=int, default=128)
     args = ap.parse_args()
@@ -203,13 +263,18 @@ def main():
     import torch
     import torch.distributed as dist
 
-    torch.cuda.set_device(local)
+    cuda = args.device == "cuda"
+    if cuda:
+        torch.cuda.set_device(local)
     if world > 1 and args.parallel == "tp":
         return serve_tp(args, world, rank)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-    device = f"cuda:{local}"
+        if cuda:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=timedelta(seconds=600))
+    device = f"cuda:{local}" if cuda else "cpu"
     eng = make_engine(args, device)
     if args.workload != "poisson":
         static_batches(args, eng, device, rank, world)
@@ -233,7 +298,7 @@ def serve_tp(args, world, rank):
     from rusteeze_b200.parallel.dist import init_distributed
     from rusteeze_b200.parallel.executor import worker_loop
     from rusteeze_b200.parallel.launcher import tp_rank_setup
-    info = init_distributed(timeout_s=600)
+    info = init_distributed(timeout_s=600, device_type=args.device)
     cfg = make_config(args, str(info.device))
     cfg.model.tensor_parallel_size = world
     cfg.engine.comm_backend = args.comm
@@ -258,7 +323,7 @@ def serve_tp(args, world, rank):
         return 0
     finally:
         runner.release_graphs()            # graphs holding NCCL calls go before the process group
-        torch.cuda.synchronize()
+        Device(str(info.device)).sync()
         dist.destroy_process_group()
 
 
@@ -272,9 +337,12 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
     import torch.distributed as dist
     from rusteeze_b200 import ops
     from rusteeze_b200.core.sampling_params import SamplingParams
+    dev = Device(device)
     V = eng.model_config.vocab_size
-    prompts, olens, arrivals = build_workload(args.requests, 1000, V, args.rate)
-    eng_stream = torch.cuda.current_stream()
+    plen = tuple(int(x) for x in args.prompt_len.split(","))
+    olen = tuple(int(x) for x in args.output_len.split(","))
+    prompts, olens, arrivals = build_workload(args.requests, 1000, V, args.rate, plen, olen)
+    eng_stream = dev.stream()
 
     # ---------------------------------------------------------------- steady-state serving
     t0 = time.monotonic()
@@ -322,16 +390,15 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
     launches0 = ops.launch_count()
     if world > 1:
         dist.barrier()
-    torch.cuda.synchronize()
+    dev.sync()
     clk = ClockSampler(local)
     clk.start()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0, ev1 = dev.event(), dev.event()
     if tp_timer is not None:
         tp_timer("start")
     ev0.record(eng_stream)
     ttfts, tpots = [], []
-    torch.cuda.nvtx.range_push("rz_timed")       # lets ncu --nvtx-include select steady-state launches
+    dev.nvtx("rz_timed")       # lets ncu --nvtx-include select steady-state launches
     for _ in range(args.steps):
         for out in step():
             if out.finished and out.metrics is not None:
@@ -339,20 +406,20 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
                     ttfts.append(out.metrics.ttft)
                 if out.metrics.tpot is not None:
                     tpots.append(out.metrics.tpot)
-    torch.cuda.nvtx.range_pop()
+    dev.nvtx()
     ev1.record(eng_stream)
     tp_ms = tp_timer("stop") if tp_timer is not None else None
-    torch.cuda.synchronize()
+    dev.sync()
     if world > 1:
         dist.barrier()
     clocks = clk.stop()
-    ms = ev0.elapsed_time(ev1) if tp_ms is None else tp_ms
+    ms = ev0.elapsed_ms(ev1) if tp_ms is None else tp_ms
     launches = ops.launch_count() - launches0
     gen = eng.stats_counters["generation_tokens"] - gen0
     prompt_toks = eng.stats_counters["prompt_tokens"] - prompt0
     phase1 = eng.host_phase_seconds()
     host_ms = {k: round((phase1[k] - phase0.get(k, 0.0)) * 1e3 / max(1, args.steps), 3) for k in phase1}
-    status = int(ops.cuda_ext().status()[0])
+    status = dev.kernel_status()
 
     t = torch.tensor([ms, float(gen), float(launches)], dtype=torch.float64, device=device)
     if world > 1:
@@ -371,20 +438,20 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
         # drain the steady-state run so the e2e run starts from an empty engine
         for rid in list(eng.requests):
             eng.abort_request(rid)
-        e_prompts, e_olens, _ = build_workload(args.e2e_requests, 5000, V, 1.0)
+        e_prompts, e_olens, _ = build_workload(args.e2e_requests, 5000, V, 1.0, plen, olen)
         h2d0, d2h0, steps0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes, eng.stats_counters["steps"]
         gen_e0 = eng.stats_counters["generation_tokens"]
         if world > 1:
             dist.barrier()
-        torch.cuda.synchronize()
+        dev.sync()
         w0 = time.perf_counter()
         for p, o in zip(e_prompts, e_olens):
-            pin = torch.tensor(p, dtype=torch.int64).pin_memory()      # prompts arrive in pinned host memory
+            pin = dev.pinned(p)                                        # prompts arrive in pinned host memory
             eng.add_request(None, None, SamplingParams(temperature=0.7, top_p=0.9, max_tokens=int(o),
                                                        ignore_eos=True), pin.tolist())
         while eng.has_unfinished_requests():
             eng.step()
-        torch.cuda.synchronize()
+        dev.sync()
         w1 = time.perf_counter()
         if world > 1:
             dist.barrier()
@@ -419,7 +486,7 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
                   "bf16 activations/KV, fp32 accumulate") if args.dtype == "fp8" else "bf16",
         "data": "synthetic requests, random-init N(0,0.02) weights",
         "config": {"model": args.model, "global_batch": args.max_seqs * world,
-                   "seq_len": "prompt U[128,2048] + output U[64,512]",
+                   "seq_len": "prompt U[{},{}] + output U[{},{}]".format(*plen, *olen),
                    "parallelism": f"dp{world}" if world > 1 else "tp1",
                    "workload": f"{args.requests} req/GPU Poisson {args.rate}/s, top_p 0.9 T 0.7, "
                                "continuous batching, paged KV block 16, chunked prefill "
@@ -451,10 +518,11 @@ def static_batches(args, eng, device, rank, world, tp_timer=None):
     import torch
     import torch.distributed as dist
     from rusteeze_b200.core.sampling_params import SamplingParams
+    dev = Device(device)
     V = eng.model_config.vocab_size
     rng = np.random.default_rng(0)
     prefix = rng.integers(0, V, args.shared_prefix).tolist() if args.workload == "shared-prefix" else []
-    stream = torch.cuda.current_stream()
+    stream = dev.stream()
     for B in [int(x) for x in args.batches.split(",")]:
         def run_once():
             for _ in range(B):
@@ -470,16 +538,16 @@ def static_batches(args, eng, device, rank, world, tp_timer=None):
         run_once()                                   # warm-up (graphs, allocator, prefix cache)
         if world > 1:
             dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dev.sync()
+        e0, e1 = dev.event(), dev.event()
         if tp_timer is not None:
             tp_timer("start")
         e0.record(stream)
         ttft = run_once()
         e1.record(stream)
         tp_ms = tp_timer("stop") if tp_timer is not None else None
-        torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) if tp_ms is None else tp_ms], dtype=torch.float64, device=device)
+        dev.sync()
+        t = torch.tensor([e0.elapsed_ms(e1) if tp_ms is None else tp_ms], dtype=torch.float64, device=device)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()

@@ -1,9 +1,13 @@
-"""The benchmark script's host-side contract (no GPU): the reference arm's
-`unavailable` line, the clock-sample summary, and the synthetic workload."""
+"""The benchmark script's contract without a GPU: the reference arm's `unavailable`
+line, the clock-sample summary, the synthetic workload, and every arm of the harness
+(single engine, data-parallel replicas, one tensor-parallel engine with speculative
+decoding over a shared prefix) run on CPU with a tiny model (`--device cpu`)."""
 import json
 import os
 import subprocess
 import sys
+
+import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
@@ -43,3 +47,60 @@ def test_workload_shape_and_determinism():
     assert all(128 <= len(p) <= 2048 for p in p1) and all(64 <= o <= 512 for o in o1)
     assert all(0 <= t < 128256 for p in p1 for t in p)
     assert all(b >= a for a, b in zip(a1, a1[1:]))           # Poisson arrivals are increasing
+
+
+_TINY = ["--device", "cpu", "--model", "tiny-llama", "--dtype", "bf16", "--max-seqs", "4",
+         "--max-batched-tokens", "256"]
+_POISSON = _TINY + ["--requests", "12", "--steps", "3", "--warmup", "3", "--prompt-len", "16,48",
+                    "--output-len", "8,24", "--e2e-requests", "4"]
+
+
+def _json_lines(out):
+    return [json.loads(ln) for ln in out.splitlines() if ln.startswith("{")]
+
+
+def _torchrun(n, port, args):
+    return [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", str(n),
+            "--master-addr", "127.0.0.1", "--master-port", str(port), "bench.py", "--gpus", str(n)] + args
+
+
+def _free_port():
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_bench_line_contract_on_cpu_harness():
+    """One Poisson run of the harness on CPU: the JSON line carries every contract key."""
+    r = subprocess.run([sys.executable, "bench.py"] + _POISSON, cwd=ROOT, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    (d,) = _json_lines(r.stdout)
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+              "scaling", "vs_baseline", "dtype", "data", "config", "clocks", "gpu_launches", "e2e"):
+        assert k in d, k
+    assert d["n_gpus"] == 1 and d["steps"] == 3 and d["warmup"] == 3 and d["value"] > 0
+    assert d["e2e"]["value"] > 0 and d["e2e"]["h2d_bytes_per_step"] > 0
+    assert d["config"]["seq_len"] == "prompt U[16,48] + output U[8,24]"
+
+
+@pytest.mark.timeout(900)
+def test_bench_data_parallel_and_tensor_parallel_runs_on_gloo():
+    """The multi-rank arms of the harness under torchrun with gloo ranks: data-parallel
+    replicas (MAX / SUM over ranks), and one tensor-parallel engine with speculative
+    decoding over a shared prefix (rank 0 drives, the worker follows the plan ring)."""
+    r = subprocess.run(_torchrun(2, _free_port(), _POISSON), cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    (d,) = _json_lines(r.stdout)
+    assert d["n_gpus"] == 2 and d["config"]["parallelism"] == "dp2" and d["e2e"]["requests"] == 8
+    tp = _TINY + ["--parallel", "tp", "--comm", "nccl", "--workload", "shared-prefix", "--shared-prefix", "48",
+                  "--draft", "self", "--spec-k", "3", "--batches", "4", "--static-prompt", "24",
+                  "--static-output", "6"]
+    r = subprocess.run(_torchrun(2, _free_port(), tp), cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    (d,) = _json_lines(r.stdout)
+    assert d["n_gpus"] == 2 and d["config"]["parallelism"].startswith("tp2")
+    assert d["speculative"]["acceptance"] == 1.0 and d["speculative"]["rounds"] > 0
