@@ -51,25 +51,28 @@ __device__ __forceinline__ uint4 pack8f(const float* v) {
   return u;
 }
 
-// 16 warps per block, 2 warps (64 threads) per own row; block b covers rows
-// [row0 + 8b, row0 + 8b + 8).  Thread t of a row owns the 8-column chunks
-// t, t + 64, ...: CH chunks (H <= CH * 512), kept in registers between the
-// sum, the norm and the all-gather so the residual is read once.
+// 16 warps per block.  ROWS = 8: 2 warps (64 threads) per own row, block b covers rows
+// [row0 + 8b, row0 + 8b + 8) and releases their all-gather flag itself.  ROWS = 1 (few
+// own rows): all 16 warps on one row, and the 8 CTAs of a flag block meet on an arrival
+// counter.  Thread t of a row owns the 8-column chunks t, t + 512 / ROWS, ...: CH chunks,
+// kept in registers between the sum, the norm and the all-gather so the residual is read
+// once.
 constexpr int kRsThreads = 512;
-constexpr int kRsRowThreads = 64;
 
-template <int CH>
+template <int CH, int ROWS>
 __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p) {
+  constexpr int kRowThreads = kRsThreads / ROWS;
+  constexpr int kRowWarps = kRowThreads / 32;
   // With reduce, this kernel is a programmatic dependent of the reduce-scatter GEMM: its
   // blocks take the SMs that GEMM CTAs leave and finish rows as their m tiles land (every
   // input is flag-guarded; every output is a persistent buffer no earlier kernel reads).
   pdl_trigger();
   const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u;
   const int own0 = p.rank * p.rs_rows;
-  const int g0 = own0 + blockIdx.x * kAgRowBlock;          // first global row of this block
+  const int g0 = own0 + blockIdx.x * ROWS;                 // first global row of this block
   if (p.reduce && p.moe_topk > 0) {
     // every (row, slot) of this block was written by the rank that owns the slot's expert
-    const int nflags = kAgRowBlock * p.moe_topk;
+    const int nflags = ROWS * p.moe_topk;
     const int f = threadIdx.x;
     if (f < nflags) {
       const int rr = f / p.moe_topk, k = f % p.moe_topk;
@@ -90,10 +93,10 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
     }
   }
   __syncthreads();
-  static_assert(kRsThreads / kRsRowThreads == kAgRowBlock, "one row per 64 threads, one flag block per CTA");
-  __shared__ float s_ss[kAgRowBlock][kRsRowThreads / 32];
+  static_assert(ROWS == 1 || ROWS == kAgRowBlock, "a CTA holds one row or one whole flag block");
+  __shared__ float s_ss[ROWS][kRowWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rr = warp >> 1, sub = warp & 1;                  // row of the block, warp within the row
+  const int rr = warp / kRowWarps, sub = warp % kRowWarps;   // row of the block, warp within the row
   const int tr = sub * 32 + lane;                            // thread within the row
   const int row = g0 + rr;                                   // global row
   const int li = row - own0;                                 // row within this rank's shard
@@ -105,7 +108,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
     const int nsrc = p.reduce ? (p.moe_topk > 0 ? p.moe_topk : p.world) : 0;
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
-      const int c = (tr + j * kRsRowThreads) * 8;
+      const int c = (tr + j * kRowThreads) * 8;
       if (c < p.H) {
         float x[8], t[8];
         if (p.reduce) {
@@ -137,12 +140,15 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
     // MXFP8 rows: the 16 chunks of a 128-column block belong to one half-warp (chunk
     // index tr + 64 j), whose lanes reduce the block maximum together; every lane joins
     // the shuffles (a chunk past H contributes 0)
-    const float inv = rsqrtf((s_ss[rr][0] + s_ss[rr][1]) / p.H + p.eps);
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRowWarps; ++i) tot += s_ss[rr][i];
+    const float inv = rsqrtf(tot / p.H + p.eps);
     const int kbo = p.H / 128;
     const size_t sf_row = static_cast<size_t>(row / 128) * kbo;
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
-      const int c = (tr + j * kRsRowThreads) * 8;
+      const int c = (tr + j * kRowThreads) * 8;
       const bool ok = c < p.H;
       float x[8], w[8];
       float amax = 0.f;
@@ -177,10 +183,13 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
       }
     }
   } else if (live) {
-    const float inv = rsqrtf((s_ss[rr][0] + s_ss[rr][1]) / p.H + p.eps);
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRowWarps; ++i) tot += s_ss[rr][i];
+    const float inv = rsqrtf(tot / p.H + p.eps);
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
-      const int c = (tr + j * kRsRowThreads) * 8;
+      const int c = (tr + j * kRowThreads) * 8;
       if (c < p.H) {
         float x[8], w[8];
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xr[j]);
@@ -202,10 +211,24 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
   // publish: the block barrier orders every thread's stores before the flag thread's
   // system-scope fence + release (cumulative), so one fence per destination suffices
   __syncthreads();
-  if (threadIdx.x < p.world && g0 < p.M) {
-    jitter_ns(p.jitter_ns, epoch + 1u, blockIdx.x, threadIdx.x);
+  if (ROWS == kAgRowBlock) {
+    if (threadIdx.x < p.world && g0 < p.M) {
+      jitter_ns(p.jitter_ns, epoch + 1u, blockIdx.x, threadIdx.x);
+      __threadfence_system();
+      st_release_sys_u32(p.ag_flag[threadIdx.x] + g0 / kAgRowBlock, epoch);
+    }
+  } else if (threadIdx.x == 0 && g0 < p.M) {
+    // one-row CTAs: the last of the flag block's live rows to arrive releases its flags
+    const int fb = g0 / kAgRowBlock, fb0 = fb * kAgRowBlock;
+    const int live_rows = min(min(p.M, own0 + p.rs_rows), fb0 + kAgRowBlock) - fb0;
+    jitter_ns(p.jitter_ns, epoch + 1u, blockIdx.x, 0u);
     __threadfence_system();
-    st_release_sys_u32(p.ag_flag[threadIdx.x] + g0 / kAgRowBlock, epoch);
+    const uint32_t prev = atomicAdd(p.ag_cnt + fb, 1u);
+    if (prev == static_cast<uint32_t>(live_rows - 1)) {
+      __threadfence_system();
+      for (int d = 0; d < p.world; ++d) st_release_sys_u32(p.ag_flag[d] + fb, epoch);
+      atomicExch(p.ag_cnt + fb, 0u);                       // ready for the next call
+    }
   }
   pdl_wait();   // complete only after the primary grid
 }
@@ -266,18 +289,37 @@ int ag_wait_launch(const uint32_t* ag_flag, int M, const uint32_t* epoch_ptr, ui
   return static_cast<int>(cudaGetLastError());
 }
 
+static int device_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
 int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st) {
   if (p.rs_rows % kAgRowBlock != 0 || p.H % 8 != 0 || p.H > kRsNormAgMaxH || p.world > kMaxTpRanks ||
       kAgRowBlock * p.moe_topk > kRsThreads || (p.mx && p.H % 128 != 0))
     return -1;
   const int own = min(p.M, (p.rank + 1) * p.rs_rows) - p.rank * p.rs_rows;
   if (own <= 0) return 0;
-  const int ch = (p.H / 8 + kRsRowThreads - 1) / kRsRowThreads;
-  void (*k)(RsNormAgParams) = ch <= 4 ? rs_norm_ag_kernel<4>
-                              : ch <= 8 ? rs_norm_ag_kernel<8>
-                              : ch <= 12 ? rs_norm_ag_kernel<12> : rs_norm_ag_kernel<16>;
+  // few own rows (decode at high TP): one row per CTA spreads the row blocks over the SMs
+  const bool fine = p.ag_cnt != nullptr && (own + kAgRowBlock - 1) / kAgRowBlock < device_sms();
+  void (*k)(RsNormAgParams);
+  if (fine) {
+    const int ch = (p.H / 8 + kRsThreads - 1) / kRsThreads;
+    k = ch <= 1 ? rs_norm_ag_kernel<1, 1> : rs_norm_ag_kernel<2, 1>;
+  } else {
+    const int ch = (p.H / 8 + kRsThreads / kAgRowBlock - 1) / (kRsThreads / kAgRowBlock);
+    k = ch <= 4 ? rs_norm_ag_kernel<4, kAgRowBlock>
+               : ch <= 8 ? rs_norm_ag_kernel<8, kAgRowBlock>
+                         : ch <= 12 ? rs_norm_ag_kernel<12, kAgRowBlock> : rs_norm_ag_kernel<16, kAgRowBlock>;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((own + kAgRowBlock - 1) / kAgRowBlock);
+  cfg.gridDim = dim3(fine ? own : (own + kAgRowBlock - 1) / kAgRowBlock);
   cfg.blockDim = dim3(kRsThreads);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -64,9 +64,9 @@ def test_peer_all_reduce_matches_nccl():
         assert err < 2e-2, f"rank {rank} rel err {err}"
 
 
-def _boundary_worker(rank, world, port, q, jitter_ns=0):
+def _boundary_worker(rank, world, port, q, jitter_ns=0, fine=0):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
-                      MASTER_PORT=str(port), RZ_TP_JITTER_NS=str(jitter_ns))
+                      MASTER_PORT=str(port), RZ_TP_JITTER_NS=str(jitter_ns), RZ_RSN_FINE=str(fine))
     import torch.distributed as dist
     from rusteeze_b200 import ops
     from rusteeze_b200.parallel.dist import init_distributed
@@ -103,12 +103,18 @@ def _boundary_worker(rank, world, port, q, jitter_ns=0):
         dist.destroy_process_group()
 
 
+_OPTIN = pytest.mark.skipif(os.environ.get("RZ_TP_OPTIN_TESTS", "0") != "1",
+                            reason="not yet run on GPUs: opt-in (RZ_TP_OPTIN_TESTS=1)")
+
+
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("jitter_ns", [0, pytest.param(20000, marks=pytest.mark.skipif(
-    os.environ.get("RZ_TP_JITTER_TEST", "0") != "1", reason="flag-protocol jitter run is opt-in (RZ_TP_JITTER_TEST=1)"))])
-def test_fused_tp_boundary_matches_reference(jitter_ns):
-    """Fused boundary vs reference; with jitter_ns the producers pause pseudo-randomly
-    (up to 20 us) before their peer stores and flag releases, shuffling arrival orders."""
+@pytest.mark.parametrize("jitter_ns,fine", [(0, 0), pytest.param(20000, 0, marks=_OPTIN),
+                                            pytest.param(0, 1, marks=_OPTIN), pytest.param(20000, 1, marks=_OPTIN)])
+def test_fused_tp_boundary_matches_reference(jitter_ns, fine):
+    """Fused boundary vs reference.  jitter_ns: the producers pause pseudo-randomly (up to
+    20 us) before their peer stores and flag releases, shuffling arrival orders.  fine: the
+    add+RMSNorm+all-gather runs one row per CTA where the rank owns few rows (flag blocks
+    released by an arrival counter)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -116,7 +122,7 @@ def test_fused_tp_boundary_matches_reference(jitter_ns):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_boundary_worker, args=(r, world, port, q, jitter_ns)) for r in range(world)]
+    ps = [ctx.Process(target=_boundary_worker, args=(r, world, port, q, jitter_ns, fine)) for r in range(world)]
     for p in ps:
         p.start()
     res = [q.get(timeout=240) for _ in range(world)]
