@@ -180,6 +180,54 @@ def _moe_grouped():
     return lambda: ops.moe_forward(h, router, w13, w2, 2)
 
 
+_TP1 = {}
+
+
+def _fused_tp_one_rank(M=4096, H=4096, K=2048, N=3072):
+    """A one-rank FusedTP group (Llama-3-8B TP2 shapes per rank): the fused boundary
+    kernels run as they do at TP > 1, with every peer store landing locally -- ncu never
+    wraps a multi-rank command, so this is how their tensor / DRAM counters are read."""
+    if not _TP1:
+        import os
+        import socket
+        import torch.distributed as dist
+        from rusteeze_b200.parallel.fused_tp import FusedTP
+        if not dist.is_initialized():
+            sk = socket.socket()
+            sk.bind(("127.0.0.1", 0))
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", str(sk.getsockname()[1]))
+            sk.close()
+            dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+        F = FusedTP(dist.group.WORLD, 0, 1, torch.device("cuda", 0), M, H)
+        x, w_o, w_qkv, h0 = _bf(M, K), _bf(H, K, scale=0.02), _bf(N, H, scale=0.02), _bf(M, H)
+        w_n = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+        F.start(h0, w_n, 1e-5, 0.0)
+        F.gemm_rs(x, w_o, 1)                       # flags of boundary 1 carry this step's epoch
+        g = F.rs_norm_ag(M, w_n, 1e-5, 0.0, 1)
+        torch.cuda.synchronize()
+        _TP1.update(F=F, x=x, w_o=w_o, w_qkv=w_qkv, w_n=w_n, g=g, M=M)
+    return _TP1
+
+
+@case("gemm_peer_rs_1rank", "gemm_tcgen05")
+def _gemm_peer_rs():
+    t = _fused_tp_one_rank()
+    return lambda: t["F"].gemm_rs(t["x"], t["w_o"], 1)
+
+
+@case("rs_norm_ag_1rank", "rs_norm_ag_kernel")
+def _rs_norm_ag():
+    t = _fused_tp_one_rank()
+    return lambda: t["F"].rs_norm_ag(t["M"], t["w_n"], 1e-5, 0.0, 1)
+
+
+@case("gemm_ag_1rank", "gemm_tcgen05")
+def _gemm_ag():
+    t = _fused_tp_one_rank()
+    return lambda: t["F"].gemm_ag(t["g"], t["w_qkv"], 1)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None)
@@ -196,6 +244,10 @@ def main() -> int:
     torch.cuda.synchronize()
     status = int(ops.cuda_ext().status()[0])
     print(f"{a.case}: ok status={status}")
+    if _TP1:
+        import torch.distributed as dist
+        _TP1.clear()
+        dist.destroy_process_group()
     return 0 if status == 0 else 1
 
 
