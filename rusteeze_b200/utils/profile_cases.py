@@ -186,7 +186,9 @@ _TP1 = {}
 def _fused_tp_one_rank(M=4096, H=4096, K=2048, N=3072):
     """A one-rank FusedTP group (Llama-3-8B TP2 shapes per rank): the fused boundary
     kernels run as they do at TP > 1, with every peer store landing locally -- ncu never
-    wraps a multi-rank command, so this is how their tensor / DRAM counters are read."""
+    wraps a multi-rank command, so this is how their tensor / DRAM counters are read.
+    The setup launches one GEMM and one rs_norm_ag of its own: skip 2 matching launches
+    (`-s 2`) to capture the timed one."""
     if not _TP1:
         import os
         import socket
