@@ -114,6 +114,17 @@ class AsyncLLMEngine:
         return d
 
     # ------------------------------------------------------------------ engine thread
+    @staticmethod
+    def _push(sub: _Submit, item) -> bool:
+        """Hands an item to the request's asyncio queue; False when the client's event loop
+        is gone (its stream is then dropped), so one vanished client cannot stop the
+        engine thread."""
+        try:
+            sub.loop.call_soon_threadsafe(sub.q.put_nowait, item)
+            return True
+        except RuntimeError:            # event loop closed
+            return False
+
     def _drain_inbox(self) -> None:
         while True:
             try:
@@ -127,7 +138,7 @@ class AsyncLLMEngine:
                     self._streams[item.request_id] = item
                     self._deadlines[item.request_id] = time.monotonic() + self.request_timeout_s
                 except BaseException as e:  # noqa: BLE001 -- delivered to the caller
-                    item.loop.call_soon_threadsafe(item.q.put_nowait, e)
+                    self._push(item, e)
             elif kind == "abort":
                 if item in self._streams:
                     self.engine.abort_request(item)
@@ -142,8 +153,7 @@ class AsyncLLMEngine:
                 self._deadlines.pop(rid, None)
                 self.engine.abort_request(rid)
                 if sub is not None:
-                    sub.loop.call_soon_threadsafe(sub.q.put_nowait,
-                                                  RequestTimeoutError(f"request {rid} timed out"))
+                    self._push(sub, RequestTimeoutError(f"request {rid} timed out"))
 
     def _check_device_status(self) -> None:
         """Kernels report protocol errors (an expired bounded wait, a corrupt
@@ -183,7 +193,7 @@ class AsyncLLMEngine:
                 self.last_error = f"engine step failed: {e!r}"
                 log.error("engine step failed:\n%s", traceback.format_exc())
                 for sub in self._streams.values():
-                    sub.loop.call_soon_threadsafe(sub.q.put_nowait, ServiceUnavailableError(self.last_error))
+                    self._push(sub, ServiceUnavailableError(self.last_error))
                 self._streams.clear()
                 return
             finally:
@@ -192,7 +202,13 @@ class AsyncLLMEngine:
                 sub = self._streams.get(o.request_id)
                 if sub is None:
                     continue
-                sub.loop.call_soon_threadsafe(sub.q.put_nowait, o)
+                if not self._push(sub, o):
+                    # the client is gone: stop generating for it
+                    self._streams.pop(o.request_id, None)
+                    self._deadlines.pop(o.request_id, None)
+                    if not o.finished:
+                        self.engine.abort_request(o.request_id)
+                    continue
                 if o.finished:
                     self._streams.pop(o.request_id, None)
                     self._deadlines.pop(o.request_id, None)

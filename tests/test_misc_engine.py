@@ -147,3 +147,70 @@ def test_async_engine_stall_watchdog_marks_not_ready_then_recovers():
     finally:
         stub.release.set()
         ae.shutdown()
+
+
+def test_closing_a_stream_aborts_the_request_in_the_engine():
+    """A client that stops reading (SSE disconnect closes the async generator) must not
+    leave its request generating: the engine drops it at its next loop iteration."""
+    import asyncio
+    from rusteeze_b200.engine.async_engine import AsyncLLMEngine
+    eng = _tiny_engine()
+    ae = AsyncLLMEngine(eng).start()
+
+    async def client():
+        sp = SamplingParams(temperature=0.0, max_tokens=10_000, ignore_eos=True)
+        gen = ae.generate(None, sp, "r-disconnect", prompt_token_ids=list(range(5, 25)))
+        got = 0
+        async for _ in gen:
+            got += 1
+            if got == 2:
+                break
+        await gen.aclose()
+        for _ in range(200):                    # the loop stays alive while the engine drops it
+            if not eng.has_unfinished_requests():
+                break
+            await asyncio.sleep(0.02)
+        return got
+
+    try:
+        assert asyncio.run(client()) == 2
+        assert not eng.has_unfinished_requests()
+        assert eng.stats_counters["requests_aborted"] >= 1
+        assert ae.healthy and ae._thread.is_alive()
+    finally:
+        ae.shutdown()
+
+
+def test_a_vanished_client_loop_does_not_stop_the_engine_thread():
+    """Outputs for a client whose event loop has closed are dropped and its request
+    aborted; the engine thread keeps serving the next client."""
+    import asyncio
+    from rusteeze_b200.engine.async_engine import AsyncLLMEngine
+    eng = _tiny_engine()
+    ae = AsyncLLMEngine(eng).start()
+
+    async def first():
+        sp = SamplingParams(temperature=0.0, max_tokens=10_000, ignore_eos=True)
+        gen = ae.generate(None, sp, "r-gone", prompt_token_ids=list(range(5, 25)))
+        async for _ in gen:
+            return                              # the loop closes with the stream still open
+
+    async def second():
+        sp = SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True)
+        last = None
+        async for out in ae.generate(None, sp, "r-next", prompt_token_ids=list(range(30, 40))):
+            last = out
+        return last
+
+    try:
+        asyncio.run(first())
+        out = asyncio.run(second())
+        assert out.finished and len(out.outputs[0].token_ids) == 4
+        assert ae._thread.is_alive()
+        for _ in range(200):
+            if not eng.has_unfinished_requests():
+                break
+            time.sleep(0.02)
+        assert not eng.has_unfinished_requests()
+    finally:
+        ae.shutdown()
