@@ -241,7 +241,10 @@ class Scheduler:
                 seq = self.waiting[0]
                 if seq.pending:
                     break                   # preempted this step with a token still in flight
-                if seq.total_len > cfg.max_model_len:
+                if (seq.total_len > cfg.max_model_len or
+                        bm.blocks_for(seq.total_len + 1) > bm.num_gpu_blocks):
+                    # longer than the model, or its KV (with the first sampled token) could
+                    # never fit the whole GPU cache: report it instead of waiting forever
                     self.waiting.popleft()
                     seq.status = RequestStatus.FINISHED_IGNORED
                     seq.finish_reason = "length"

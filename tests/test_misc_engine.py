@@ -214,3 +214,26 @@ def test_a_vanished_client_loop_does_not_stop_the_engine_thread():
         assert not eng.has_unfinished_requests()
     finally:
         ae.shutdown()
+
+
+def test_requests_larger_than_the_kv_cache_are_reported_not_stuck():
+    """A prompt that fits the model's context but not the whole KV cache (64 blocks of 16
+    tokens here) finishes at once with finish_reason "length" instead of waiting forever;
+    one that outgrows the cache while generating ends the same way; other requests are
+    unaffected."""
+    eng = _tiny_engine()                       # 64 GPU blocks = 1024 tokens of KV
+    eng.add_request("big", None, SamplingParams(max_tokens=4, temperature=0.0), list(range(1100)))
+    eng.add_request("grows", None, SamplingParams(max_tokens=200, temperature=0.0, ignore_eos=True),
+                    list(range(900)))
+    eng.add_request("small", None, SamplingParams(max_tokens=3, temperature=0.0, ignore_eos=True), list(range(20)))
+    done = {}
+    for _ in range(400):
+        if not eng.has_unfinished_requests():
+            break
+        for o in eng.step():
+            if o.finished:
+                done[o.request_id] = o.outputs[0]
+    assert not eng.has_unfinished_requests()
+    assert done["big"].finish_reason == "length" and done["big"].token_ids == []
+    assert done["grows"].finish_reason == "length" and 0 < len(done["grows"].token_ids) < 200
+    assert done["small"].finish_reason == "length" and len(done["small"].token_ids) == 3
