@@ -157,6 +157,14 @@ class Scheduler:
             seq.reset_for_recompute()
             self.waiting.appendleft(seq)
 
+    def _drop_too_long(self, seq: Sequence) -> None:
+        """A running sequence whose next step would need more KV blocks than the GPU
+        cache has: free it and report it finished by length."""
+        self.bm.free(seq.seq_id)
+        seq.status = RequestStatus.FINISHED_IGNORED
+        seq.finish_reason = "length"
+        self.ignored.append(seq)
+
     def _finishes_with_pending(self, seq: Sequence) -> bool:
         p = seq.request.params
         n = seq.num_generated + seq.pending
@@ -192,6 +200,10 @@ class Scheduler:
                     self._preempt(seq, out)
                     continue
             target = seq.num_computed + n + self._lookahead(seq)
+            if bm.blocks_for(target) > bm.num_gpu_blocks:
+                # its KV can never fit the whole cache: the sequence ends here ("length")
+                self._drop_too_long(seq)
+                continue
             while bm.blocks_to_grow(seq.seq_id, target, seq.num_computed) > bm.num_free_gpu_blocks():
                 if queue:
                     self._preempt(queue.pop(), out)   # lowest priority goes first
@@ -214,7 +226,9 @@ class Scheduler:
         if not out.preempted:
             while self.swapped and seq_budget > 0 and token_budget > 0:
                 seq = self.swapped[0]
-                need = len(bm.block_table(seq.seq_id)) + self._watermark_blocks
+                held = len(bm.block_table(seq.seq_id))
+                # the watermark reserve only applies while there is room for it
+                need = held + (self._watermark_blocks if held + self._watermark_blocks <= bm.num_gpu_blocks else 0)
                 if need > bm.num_free_gpu_blocks():
                     break
                 self.swapped.popleft()

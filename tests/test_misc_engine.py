@@ -58,7 +58,10 @@ def _tiny_engine(**kw):
     cfg.model.dtype = "float32"
     cfg.engine.num_gpu_blocks = 64
     for k, v in kw.items():
-        setattr(cfg.engine, k, v)
+        if k == "preemption_mode":
+            cfg.engine.scheduling.preemption_mode = v
+        else:
+            setattr(cfg.engine, k, v)
     return LLMEngine(cfg)
 
 
@@ -216,12 +219,13 @@ def test_a_vanished_client_loop_does_not_stop_the_engine_thread():
         ae.shutdown()
 
 
-def test_requests_larger_than_the_kv_cache_are_reported_not_stuck():
+@pytest.mark.parametrize("mode", ["recompute", "swap"])
+def test_requests_larger_than_the_kv_cache_are_reported_not_stuck(mode):
     """A prompt that fits the model's context but not the whole KV cache (64 blocks of 16
     tokens here) finishes at once with finish_reason "length" instead of waiting forever;
-    one that outgrows the cache while generating ends the same way; other requests are
-    unaffected."""
-    eng = _tiny_engine()                       # 64 GPU blocks = 1024 tokens of KV
+    one that outgrows the cache while generating ends the same way (in swap mode it used
+    to be swapped out and never fit back); other requests are unaffected."""
+    eng = _tiny_engine(swap_space_gb=0.01, preemption_mode=mode)     # 64 GPU blocks = 1024 tokens of KV
     eng.add_request("big", None, SamplingParams(max_tokens=4, temperature=0.0), list(range(1100)))
     eng.add_request("grows", None, SamplingParams(max_tokens=200, temperature=0.0, ignore_eos=True),
                     list(range(900)))
