@@ -367,6 +367,8 @@ class LLMEngine:
         ign, self.scheduler.ignored = self.scheduler.ignored, []
         for s in ign:
             req = s.request
+            # ignored before its best_of samples were forked: there will be no children
+            req.forked = True
             if req.request_id in self.requests and req.is_finished():
                 outs.append(req.to_output(delta=True))
                 self._retire(req)

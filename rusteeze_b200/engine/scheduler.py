@@ -241,7 +241,9 @@ class Scheduler:
                     continue
                 out.blocks_to_copy.extend(bm.ensure_capacity(seq.seq_id, target, seq.num_computed))
                 done_prompt = seq.num_computed + n >= seq.total_len
-                ss = ScheduledSeq(seq, seq.num_computed, n, sample=done_prompt)
+                # a prompt swapped out mid-prefill forks its best_of samples here like anywhere else
+                ss = ScheduledSeq(seq, seq.num_computed, n, sample=done_prompt,
+                                  num_samples=self._num_samples(seq) if done_prompt else 1)
                 (out.prefills if n > 1 or seq.is_prefill else out.decodes).append(ss)
                 token_budget -= n
                 seq_budget -= 1
