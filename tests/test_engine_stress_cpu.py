@@ -1,6 +1,7 @@
 """Randomised engine stress on CPU (seeded): request mixes with varied prompt and output
 lengths, sampling modes, n / best_of, random aborts, tight KV caches, recompute and
-swap preemption, prefix caching and chunked prefill on and off.  Every request must end
+swap preemption, prefix caching and chunked prefill on and off, the synchronous and the
+pipelined schedule.  Every request must end
 (finished or aborted) within a step cap -- no livelock -- every finished request must be
 reported, and the block manager's invariants must hold after every step.
 RZ_STRESS_SEEDS=<n> widens the search (default 8 seeds, plus the seeds of past bugs)."""
@@ -56,6 +57,10 @@ def test_random_request_mixes_always_drain(seed):
     rng = np.random.default_rng(1000 + seed)
     mode = ["recompute", "swap"][seed % 2]
     eng = _engine(rng, mode, prefix=bool(seed & 2), chunked=bool(seed % 3 != 1))
+    if seed & 4:
+        # the pipelined schedule (step n+1 enqueued before step n's tokens are applied;
+        # ineligible requests drain it into synchronous steps)
+        eng._async = True
     shared = rng.integers(0, 300, 48).tolist()
     live = set()
     n_req = 24
@@ -82,3 +87,32 @@ def test_random_request_mixes_always_drain(seed):
     assert submitted == n_req
     assert not eng.has_unfinished_requests(), f"livelock: {eng.stats()}"
     assert not live, f"requests that ended without a finished output: {sorted(live)}"
+
+
+@pytest.mark.timeout(900)
+@pytest.mark.parametrize("seed", range(int(os.environ.get("RZ_STRESS_SEEDS", "4"))))
+def test_pipelined_schedule_emits_the_synchronous_tokens(seed):
+    """Greedy request mixes under a tight cache (preemption by recompute, prefix caching
+    on odd seeds): the pipelined schedule must emit exactly the synchronous one's tokens
+    for every request."""
+    def run(pipelined):
+        rng = np.random.default_rng(2000 + seed)
+        eng = _engine(rng, "recompute", prefix=bool(seed & 1), chunked=True)
+        eng._async = pipelined
+        shared = rng.integers(0, 300, 40).tolist()
+        for i in range(16):
+            toks = (shared[: int(rng.integers(0, 40))] if rng.random() < 0.5 else []) + \
+                rng.integers(0, 300, int(rng.integers(1, 120))).tolist()
+            eng.add_request(f"g{i}", None, SamplingParams(temperature=0.0, max_tokens=int(rng.integers(1, 30)),
+                                                          ignore_eos=True), toks)
+        done = {}
+        for _ in range(3000):
+            for o in eng.step():
+                if o.finished:
+                    done[o.request_id] = (o.outputs[0].token_ids, o.outputs[0].finish_reason)
+            if not eng.has_unfinished_requests():
+                break
+        return done
+
+    sync, pipe = run(False), run(True)
+    assert len(sync) == 16 and sync == pipe
