@@ -60,6 +60,20 @@ def _dtype(name: str, device: str) -> torch.dtype:
             "fp16": torch.float16}[name]
 
 
+def swap_blocks(ec, model_config, dtype: torch.dtype, device: str) -> int:
+    """Host swap-space blocks for swap preemption.  Every tensor-parallel rank computes
+    the same count from the same config (the engine's block manager on rank 0 and each
+    rank's host KV cache must agree)."""
+    cuda = str(device).startswith("cuda")
+    bytes_per_block = model_config.kv_bytes_per_token(torch.finfo(dtype).bits // 8) * BLOCK_SIZE
+    n = int(ec.swap_space_gb * (1 << 30) // bytes_per_block)
+    if not cuda:
+        n = min(n, 1024)
+    if ec.scheduling.preemption_mode != "swap" and cuda:
+        n = 0
+    return n
+
+
 def resolve_device(name: str) -> str:
     if name == "auto":
         return "cuda:0" if torch.cuda.is_available() else "cpu"
@@ -103,11 +117,7 @@ class LLMEngine:
                                                                if self.tokenizer.eos_token_id is not None else []))
         # KV cache sizing
         num_gpu_blocks = ec.num_gpu_blocks or self._profile_num_blocks()
-        bytes_per_block = self.model_config.kv_bytes_per_token(torch.finfo(self.dtype).bits // 8) * BLOCK_SIZE
-        num_cpu_blocks = int(ec.swap_space_gb * (1 << 30) // bytes_per_block) if self.device.startswith("cuda") \
-            else min(int(ec.swap_space_gb * (1 << 30) // bytes_per_block), 1024)
-        if ec.scheduling.preemption_mode != "swap":
-            num_cpu_blocks = min(num_cpu_blocks, 0 if self.device.startswith("cuda") else num_cpu_blocks)
+        num_cpu_blocks = swap_blocks(ec, self.model_config, self.dtype, self.device)
         self.bm = make_block_manager(BLOCK_SIZE, num_gpu_blocks, num_cpu_blocks, ec.enable_prefix_caching)
         spec = ec.speculative
         self.sched_cfg = SchedulerConfig(

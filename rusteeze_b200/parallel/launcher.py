@@ -86,7 +86,9 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
         t = torch.tensor([nblocks], dtype=torch.int64, device=info.device if info.backend == "nccl" else "cpu")
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
         nblocks = int(t.item())
-    runner = ModelRunner(model, num_gpu_blocks=nblocks, num_cpu_blocks=0, max_num_seqs=ec.max_num_seqs,
+    from rusteeze_b200.engine.llm_engine import swap_blocks
+    n_swap = swap_blocks(ec, mc, dtype, dev)     # the same count on every rank and in rank 0's engine
+    runner = ModelRunner(model, num_gpu_blocks=nblocks, num_cpu_blocks=n_swap, max_num_seqs=ec.max_num_seqs,
                          max_num_batched_tokens=ec.max_num_batched_tokens, max_model_len=max_len,
                          use_cuda_graph=not ec.enforce_eager, seed=cfg.model.seed)
     channel = None
@@ -99,7 +101,6 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
         dist.barrier()
     ecfg = copy.deepcopy(cfg)
     ecfg.engine.num_gpu_blocks = nblocks
-    ecfg.engine.swap_space_gb = 0.0
     ecfg.model.device = dev
     if info.rank == 0:
         executor = TPExecutor(runner, channel, liveness) if channel is not None else runner

@@ -116,3 +116,55 @@ def test_pipelined_schedule_emits_the_synchronous_tokens(seed):
 
     sync, pipe = run(False), run(True)
     assert len(sync) == 16 and sync == pipe
+
+
+@pytest.mark.timeout(900)
+@pytest.mark.parametrize("mode", ["swap", "recompute"])
+def test_tp2_engine_under_preemption_matches_single_process(mode):
+    """A TP2 engine (gloo ranks; plans carry the swap and copy-on-write block lists to the
+    worker, which swaps its own KV shard) under a tight KV cache with prefix caching:
+    greedy tokens equal the single-process engine's, and preemptions (swaps in swap
+    mode) really happened."""
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+
+    def cfg(tp):
+        c = Config()
+        c.model.device = "cpu"
+        c.model.dtype = "float32"
+        c.model.tensor_parallel_size = tp
+        c.engine.num_gpu_blocks = 20
+        c.engine.max_num_seqs = 6
+        c.engine.max_num_batched_tokens = 96
+        c.engine.enable_chunked_prefill = True
+        c.engine.enable_prefix_caching = True
+        c.engine.swap_space_gb = 0.002
+        c.engine.scheduling.preemption_mode = mode
+        c.engine.comm_backend = "nccl"
+        return c
+
+    rng = np.random.default_rng(7)
+    shared = rng.integers(0, 300, 40).tolist()
+    reqs = [((shared[: int(rng.integers(8, 40))] if i % 2 else []) + rng.integers(0, 300, int(rng.integers(4, 60))).tolist(),
+             int(rng.integers(8, 40))) for i in range(10)]
+
+    def run(eng):
+        for i, (toks, mx) in enumerate(reqs):
+            eng.add_request(f"t{i}", None, SamplingParams(temperature=0.0, max_tokens=mx, ignore_eos=True), toks)
+        done = {}
+        for _ in range(3000):
+            for o in eng.step():
+                if o.finished:
+                    done[o.request_id] = o.outputs[0].token_ids
+            if not eng.has_unfinished_requests():
+                break
+        return done, eng.scheduler.num_preemptions, eng.bm.stats()["swap_outs"]
+
+    ref, _, _ = run(LLMEngine(cfg(1), model_config=MC))
+    launcher = TPEngineLauncher(cfg(2), model_config=MC, device_type="cpu")
+    try:
+        got, preemptions, swap_outs = run(launcher.engine())
+    finally:
+        launcher.shutdown()
+    assert preemptions > 0
+    assert (swap_outs > 0) == (mode == "swap")        # swap mode moves KV to every rank's host cache
+    assert len(ref) == 10 and got == ref
