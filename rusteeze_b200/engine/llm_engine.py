@@ -252,6 +252,8 @@ class LLMEngine:
             so = self.scheduler.schedule()
         outputs: List[RequestOutput] = []
         if so.is_empty():
+            # nothing to run, but a swap-in or swap-out decided this step must still happen
+            self.runner.apply_block_ops(so)
             return self._collect_ignored()
         rows, owners = self._sample_rows(so)
         t0 = time.monotonic()
@@ -294,7 +296,9 @@ class LLMEngine:
         with nvtx_range("rz.step.schedule"):
             so = self.scheduler.schedule()
         launched = False
-        if not so.is_empty():
+        if so.is_empty():
+            self.runner.apply_block_ops(so)        # block moves of a step with nothing to run
+        else:
             prev = self._inflight[-1] if self._inflight else None
             for ss in so.scheduled:
                 if ss.seq.pending:

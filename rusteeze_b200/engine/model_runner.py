@@ -197,6 +197,7 @@ class ModelRunner:
         else:
             toks = np.zeros(0, dtype=np.int64)
         self.last_pend = (pend_dst, pend_src)     # the scatter a tensor-parallel worker repeats
+        self._check_capacity(S, int(n_new.sum()))
         T = bm.build_batch(seq_ids, ctx, n_new, toks, self.h_input_ids.data_ptr(),
                            self.h_positions.data_ptr(), self.h_slots.data_ptr(), self.h_qsl.data_ptr(),
                            self.h_seq_lens.data_ptr(), self.h_block_tables.data_ptr(),
@@ -260,6 +261,7 @@ class ModelRunner:
         """Builds and uploads the batch of `forward_arrays` (block tables from `bm`);
         returns (metadata, T, S)."""
         S = len(seq_ids)
+        self._check_capacity(S, int(np.sum(n_new)) if S else 0)
         self._flip_host()
         T = bm.build_batch(np.asarray(seq_ids, dtype=np.int64), np.asarray(ctx, dtype=np.int64),
                            np.asarray(n_new, dtype=np.int64), np.asarray(toks, dtype=np.int64),
@@ -349,17 +351,29 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ execute
     @torch.no_grad()
-    # ------------------------------------------------------------------ asynchronous steps
-    @torch.no_grad()
-    def launch(self, so: SchedulerOutput, bm, rows: List[SampleRow], prev_tokens: Optional[torch.Tensor]):
-        """Enqueues a whole step (copies, forward, sampling, result readback)
-        without waiting for the GPU; `finish` returns its SampleResult."""
+    def _check_capacity(self, S: int, T: int) -> None:
+        """The batch builder writes into the fixed-size staging buffers: refuse a batch
+        that does not fit them instead of writing past their ends."""
+        if S > self.max_num_seqs or T > self.max_tokens:
+            raise ValueError(f"batch of {S} sequences / {T} tokens exceeds this runner's staging capacity "
+                             f"({self.max_num_seqs} sequences / {self.max_tokens} tokens)")
+
+    def apply_block_ops(self, so: SchedulerOutput) -> None:
+        """The step's KV block moves: swap-outs first (their GPU blocks may be handed to
+        swap-ins and copies of the same step), then swap-ins, then copy-on-write copies."""
         if so.blocks_to_swap_out:
             self.swap_out(so.blocks_to_swap_out)
         if so.blocks_to_swap_in:
             self.swap_in(so.blocks_to_swap_in)
         if so.blocks_to_copy:
             self.copy_blocks(so.blocks_to_copy)
+
+    # ------------------------------------------------------------------ asynchronous steps
+    @torch.no_grad()
+    def launch(self, so: SchedulerOutput, bm, rows: List[SampleRow], prev_tokens: Optional[torch.Tensor]):
+        """Enqueues a whole step (copies, forward, sampling, result readback)
+        without waiting for the GPU; `finish` returns its SampleResult."""
+        self.apply_block_ops(so)
         t0 = time.perf_counter()
         meta, T, S, sample_rows = self.prepare(so, bm, prev_tokens)
         t1 = time.perf_counter()
@@ -380,12 +394,7 @@ class ModelRunner:
         return res
 
     def execute(self, so: SchedulerOutput, bm, rows: List[SampleRow]) -> SampleResult:
-        if so.blocks_to_swap_out:
-            self.swap_out(so.blocks_to_swap_out)
-        if so.blocks_to_swap_in:
-            self.swap_in(so.blocks_to_swap_in)
-        if so.blocks_to_copy:
-            self.copy_blocks(so.blocks_to_copy)
+        self.apply_block_ops(so)
         t0 = time.perf_counter()
         meta, T, S, sample_rows = self.prepare(so, bm)
         t1 = time.perf_counter()

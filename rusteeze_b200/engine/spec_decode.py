@@ -128,7 +128,15 @@ class SpecDecoder:
     def step(self):
         eng = self.engine
         so = eng.scheduler.schedule()
+        # preempted sequences lose their draft KV (swapped or freed): the draft recomputes it
+        for s in so.preempted:
+            if not self.self_draft:
+                self.draft_computed[s.seq_id] = 0
+        if not self.self_draft and so.blocks_to_copy:
+            self.drunner.copy_blocks(so.blocks_to_copy)      # the draft's own copy-on-write copies
         if so.is_empty():
+            # a step may only move blocks (preemptions with nothing left to run)
+            self.runner.apply_block_ops(so)
             return eng._collect_ignored()
         spec_ok = not so.prefills and all(
             s.seq.request.params.top_k <= 0 and s.seq.request.params.top_p >= 1.0 and
@@ -175,6 +183,7 @@ class SpecDecoder:
     @torch.no_grad()
     def _spec_round(self, so):
         eng, k, bm = self.engine, self.k, self.engine.bm
+        self.runner.apply_block_ops(so)          # the target's swaps and copies of this step
         seqs = [s.seq for s in so.decodes]
         S = len(seqs)
         ids = [s.seq_id for s in seqs]
@@ -186,6 +195,12 @@ class SpecDecoder:
         if self.self_draft:
             dc = list(cs)
         n1 = [c - d + 1 for c, d in zip(cs, dc)]
+        if not self.self_draft and sum(n1) > drunner.max_tokens:
+            # a long catch-up (a preempted sequence recomputes its draft KV): feed the tokens
+            # before each sequence's current one in chunks that fit the draft runner
+            self._draft_catch_up(seqs, dc, cs, drunner)
+            dc = list(cs)
+            n1 = [1] * S
         toks = np.concatenate([s.tokens_np()[d:c + 1] for s, d, c in zip(seqs, dc, cs)])
         draft_tokens = torch.empty(S, k, dtype=torch.long)
         draft_logits = []
@@ -259,6 +274,28 @@ class SpecDecoder:
             if req.is_finished():
                 eng._retire(req)
         return outs
+
+    def _draft_catch_up(self, seqs, dc, cs, drunner) -> None:
+        """Draft KV for positions [dc[i], cs[i]) of every sequence, in batches of at most
+        the draft runner's token capacity (logits are not needed)."""
+        cap = drunner.max_tokens
+        todo = [(s, d, c) for s, d, c in zip(seqs, dc, cs) if c > d]
+        while todo:
+            ids, ctx, nn, parts, used, rest = [], [], [], [], 0, []
+            for s, d, c in todo:
+                take = min(c - d, cap - used)
+                if take <= 0 or len(ids) == drunner.max_num_seqs:
+                    rest.append((s, d, c))
+                    continue
+                ids.append(s.seq_id)
+                ctx.append(d)
+                nn.append(take)
+                parts.append(s.tokens_np()[d:d + take])
+                used += take
+                if d + take < c:
+                    rest.append((s, d + take, c))
+            drunner.forward_arrays(self.engine.bm, ids, ctx, nn, np.concatenate(parts), 1, num_decode=0)
+            todo = rest
 
     def _propose(self, logits: torch.Tensor, temps: torch.Tensor, seqs, i: int) -> torch.Tensor:
         """Greedy argmax, or a temperature sample (Gumbel-max) per row."""

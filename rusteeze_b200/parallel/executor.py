@@ -147,6 +147,14 @@ class TPExecutor:
     def finish(self, handle) -> SampleResult:
         return self.runner.finish(handle)
 
+    def apply_block_ops(self, so) -> None:
+        """A step's swap / copy-on-write block moves outside a step plan (speculative
+        rounds run their forwards as explicit batches): every rank moves its own KV shard."""
+        if so.blocks_to_swap_out or so.blocks_to_swap_in or so.blocks_to_copy:
+            self._check_workers()
+            self.ch.publish(MSG_STEP, {"blockops": (so.blocks_to_swap_out, so.blocks_to_swap_in, so.blocks_to_copy)})
+            self.runner.apply_block_ops(so)
+
     @torch.no_grad()
     def forward_arrays(self, bm, seq_ids, ctx, n_new, toks, logits_per_seq: int,
                        num_decode: int = 0) -> torch.Tensor:
@@ -269,6 +277,15 @@ def worker_loop(runner: ModelRunner, channel: PlanChannel, idle_timeout_s: float
             continue
         if "timer" in plan:
             _timer_mark(runner, plan["timer"], timer_state)
+            continue
+        if "blockops" in plan:
+            sout, sin, copy = plan["blockops"]
+            if sout:
+                runner.swap_out(sout)
+            if sin:
+                runner.swap_in(sin)
+            if copy:
+                runner.copy_blocks(copy)
             continue
         if "arrays" in plan:
             meta, T, S = stage_plan(runner, plan)

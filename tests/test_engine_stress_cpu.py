@@ -19,7 +19,7 @@ MC = ModelConfig(name="stress", hidden_size=64, intermediate_size=128, num_hidde
                  num_key_value_heads=1, vocab_size=300, max_position_embeddings=512)
 
 
-def _engine(rng, mode, prefix, chunked):
+def _engine(rng, mode, prefix, chunked, spec=None):
     cfg = Config()
     cfg.model.device = "cpu"
     cfg.model.dtype = "float32"
@@ -30,6 +30,11 @@ def _engine(rng, mode, prefix, chunked):
     cfg.engine.enable_prefix_caching = prefix
     cfg.engine.swap_space_gb = 0.002
     cfg.engine.scheduling.preemption_mode = mode
+    if spec is not None:
+        cfg.engine.speculative = spec
+        # a verify pass holds max_num_seqs * (k + 1) tokens
+        cfg.engine.max_num_batched_tokens = max(cfg.engine.max_num_batched_tokens,
+                                                cfg.engine.max_num_seqs * (spec.num_speculative_tokens + 1))
     return LLMEngine(cfg, model_config=MC)
 
 
@@ -168,3 +173,77 @@ def test_tp2_engine_under_preemption_matches_single_process(mode):
     assert preemptions > 0
     assert (swap_outs > 0) == (mode == "swap")        # swap mode moves KV to every rank's host cache
     assert len(ref) == 10 and got == ref
+
+
+# seeds 22, 31, 59: speculative rounds skipped the step's swap / copy block moves;
+# seed 71: a preempted sequence's draft catch-up overflowed the draft runner's buffers
+_SPEC_SEEDS = sorted(set(range(int(os.environ.get("RZ_STRESS_SEEDS", "4")))) | {22, 31, 59, 71})
+
+
+@pytest.mark.timeout(900)
+@pytest.mark.parametrize("seed", _SPEC_SEEDS)
+def test_speculative_decoding_under_random_mixes(seed):
+    """Speculative decoding (self-draft on even seeds, a separate 1-layer draft on odd
+    ones) under tight caches, both preemption modes, random aborts and mixed sampling:
+    every request ends and is reported, invariants hold, and greedy requests emit exactly
+    the tokens of a non-speculative engine."""
+    import dataclasses
+    from rusteeze_b200.config.config import SpeculativeSection
+    rng = np.random.default_rng(3000 + seed)
+    mode = ["recompute", "swap"][(seed >> 1) % 2]
+    draft_dir = None
+    if seed % 2:
+        import tempfile
+        from rusteeze_b200.models.loader import build_model, save_hf_checkpoint
+        draft_dir = tempfile.mkdtemp(prefix="rz_draft_")
+        save_hf_checkpoint(build_model(dataclasses.replace(MC, name="draft", num_hidden_layers=1),
+                                       dtype=__import__("torch").float32, seed=11), draft_dir)
+    reqs = []
+    for i in range(14):
+        greedy = rng.random() < 0.6
+        p = (SamplingParams(temperature=0.0, max_tokens=int(rng.integers(1, 30)), ignore_eos=True) if greedy else
+             SamplingParams(temperature=0.9, top_p=0.95, max_tokens=int(rng.integers(1, 30)),
+                            seed=int(rng.integers(1 << 30))))
+        reqs.append((f"s{i}", rng.integers(0, 300, int(rng.integers(1, 90))).tolist(), p, greedy))
+    aborts = {int(x) for x in rng.integers(0, 14, 2)}
+
+    def run(spec):
+        r2 = np.random.default_rng(4000 + seed)
+        eng = _engine(r2, mode, prefix=bool(seed & 4), chunked=True,
+                      spec=SpeculativeSection(draft_model=draft_dir, num_speculative_tokens=3) if spec else None)
+        done = {}
+        for i, (rid, toks, p, _) in enumerate(reqs):
+            eng.add_request(rid, None, p, toks)
+        for step in range(3000):
+            if step == 5:
+                for i in sorted(aborts):
+                    eng.abort_request(reqs[i][0])
+            for o in eng.step():
+                if o.finished:
+                    done[o.request_id] = o.outputs[0].token_ids
+            assert eng.bm.check_invariants()
+            if not eng.has_unfinished_requests():
+                break
+        assert not eng.has_unfinished_requests()
+        return done
+
+    base, spec = run(False), run(True)
+    for i, (rid, _, _, greedy) in enumerate(reqs):
+        if i in aborts:
+            continue
+        assert rid in spec, f"{rid} never reported"
+        if greedy and rid in base:
+            assert spec[rid] == base[rid], rid
+
+
+def test_a_batch_beyond_the_staging_buffers_is_refused():
+    """The batch builder writes into fixed-size pinned staging buffers: a batch larger than
+    the runner's capacity raises instead of writing past them."""
+    rng = np.random.default_rng(0)
+    eng = _engine(rng, "recompute", prefix=False, chunked=True)
+    r = eng.runner
+    eng.add_request("x", None, SamplingParams(max_tokens=2), list(range(10)))
+    seq = eng.requests["x"].seqs[0]
+    eng.bm.allocate_prompt(seq.seq_id, seq.tokens_np())
+    with pytest.raises(ValueError, match="staging capacity"):
+        r.forward_arrays(eng.bm, [seq.seq_id], [0], [r.max_tokens + 1], np.zeros(r.max_tokens + 1, np.int64), 1)
