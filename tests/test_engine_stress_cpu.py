@@ -124,8 +124,8 @@ def test_pipelined_schedule_emits_the_synchronous_tokens(seed):
 
 
 @pytest.mark.timeout(900)
-@pytest.mark.parametrize("mode", ["swap", "recompute"])
-def test_tp2_engine_under_preemption_matches_single_process(mode):
+@pytest.mark.parametrize("mode,spec", [("swap", False), ("recompute", False), ("swap", True)])
+def test_tp2_engine_under_preemption_matches_single_process(mode, spec):
     """A TP2 engine (gloo ranks; plans carry the swap and copy-on-write block lists to the
     worker, which swaps its own KV shard) under a tight KV cache with prefix caching:
     greedy tokens equal the single-process engine's, and preemptions (swaps in swap
@@ -137,7 +137,7 @@ def test_tp2_engine_under_preemption_matches_single_process(mode):
         c.model.device = "cpu"
         c.model.dtype = "float32"
         c.model.tensor_parallel_size = tp
-        c.engine.num_gpu_blocks = 20
+        c.engine.num_gpu_blocks = 10 if spec else 20
         c.engine.max_num_seqs = 6
         c.engine.max_num_batched_tokens = 96
         c.engine.enable_chunked_prefill = True
@@ -145,6 +145,10 @@ def test_tp2_engine_under_preemption_matches_single_process(mode):
         c.engine.swap_space_gb = 0.002
         c.engine.scheduling.preemption_mode = mode
         c.engine.comm_backend = "nccl"
+        if spec:        # speculative rounds: block moves travel as their own plan messages
+            from rusteeze_b200.config.config import SpeculativeSection
+            c.engine.speculative = SpeculativeSection(num_speculative_tokens=2)
+            c.engine.max_num_batched_tokens = max(c.engine.max_num_batched_tokens, 6 * 3)
         return c
 
     rng = np.random.default_rng(7)
