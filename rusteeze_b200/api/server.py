@@ -150,15 +150,19 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
         try:
             for pi, (text, ids) in enumerate(prompts):
                 final = None
-                async for out in async_engine.generate(text, sp, f"{rid}-{pi}", ids, priority=req.priority):
-                    final = out
-                    for c, delta in zip(out.outputs, out.delta_text):
-                        if delta or c.finish_reason:
-                            chunk = S.CompletionResponse(
-                                id=rid, model=model_name, usage=S.Usage(),
-                                choices=[S.CompletionChoice(index=pi * sp.n + c.index, text=delta,
-                                                            finish_reason=c.finish_reason)])
-                            yield "data: " + chunk.model_dump_json(exclude={"usage"}, exclude_none=True) + "\n\n"
+                agen = async_engine.generate(text, sp, f"{rid}-{pi}", ids, priority=req.priority)
+                try:
+                    async for out in agen:
+                        final = out
+                        for c, delta in zip(out.outputs, out.delta_text):
+                            if delta or c.finish_reason:
+                                chunk = S.CompletionResponse(
+                                    id=rid, model=model_name, usage=S.Usage(),
+                                    choices=[S.CompletionChoice(index=pi * sp.n + c.index, text=delta,
+                                                                finish_reason=c.finish_reason)])
+                                yield "data: " + chunk.model_dump_json(exclude={"usage"}, exclude_none=True) + "\n\n"
+                finally:
+                    await agen.aclose()           # a stream closed early aborts its request now, not at GC
                 metrics.on_request_finished(final, "completions")
                 usage.prompt_tokens += len(final.prompt_token_ids)
                 usage.completion_tokens += sum(len(c.token_ids) for c in final.outputs)
@@ -202,16 +206,21 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
             yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
                 S.ChatChunkChoice(index=i, delta=S.ChatDelta(role="assistant", content=""))]))
         final = None
+        agen = async_engine.generate(None, sp, rid, ids, priority=req.priority)
         try:
-            async for out in async_engine.generate(None, sp, rid, ids, priority=req.priority):
-                final = out
-                for c, delta in zip(out.outputs, out.delta_text):
-                    if delta:
-                        yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
-                            S.ChatChunkChoice(index=c.index, delta=S.ChatDelta(content=delta))]))
-                    if c.finish_reason:
-                        yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
-                            S.ChatChunkChoice(index=c.index, delta=S.ChatDelta(), finish_reason=c.finish_reason)]))
+            try:
+                async for out in agen:
+                    final = out
+                    for c, delta in zip(out.outputs, out.delta_text):
+                        if delta:
+                            yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
+                                S.ChatChunkChoice(index=c.index, delta=S.ChatDelta(content=delta))]))
+                        if c.finish_reason:
+                            yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
+                                S.ChatChunkChoice(index=c.index, delta=S.ChatDelta(),
+                                                  finish_reason=c.finish_reason)]))
+            finally:
+                await agen.aclose()               # a stream closed early aborts its request now, not at GC
             metrics.on_request_finished(final, "chat")
             if req.stream_options and req.stream_options.include_usage and final is not None:
                 n_out = sum(len(c.token_ids) for c in final.outputs)
