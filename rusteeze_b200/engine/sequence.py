@@ -21,6 +21,17 @@ from rusteeze_b200.core.types import RequestMetrics, RequestStatus
 _seq_ids = itertools.count(1)
 
 
+def _stop_prefix_len(text: str, stops) -> int:
+    """Length of the longest suffix of `text` that is a proper prefix of a stop string."""
+    best = 0
+    for st in stops:
+        for k in range(min(len(st) - 1, len(text)), best, -1):
+            if text.endswith(st[:k]):
+                best = k
+                break
+    return best
+
+
 class Sequence:
     __slots__ = ("seq_id", "request", "prompt_len", "token_ids", "status", "num_computed",
                  "num_cached", "logprobs", "cumulative_logprob", "output_text", "stop_reason",
@@ -155,9 +166,14 @@ class Request:
                                          logprobs=s.logprobs if p.logprobs is not None else None,
                                          finish_reason=s.finish_reason, stop_reason=s.stop_reason))
             prev = self.sent_text_len.get(s.index, 0)
-            deltas.append(text[prev:])
+            # a running sequence's text may end in the start of a stop string, which the next
+            # token could complete (and the stop string is then cut from the output): hold
+            # that suffix back so a stream never sends text it would have to retract
+            end = len(text) if s.is_finished() or not p.stop else len(text) - _stop_prefix_len(text, p.stop)
+            end = max(end, prev)
+            deltas.append(text[prev:end])
             if delta:
-                self.sent_text_len[s.index] = len(text)
+                self.sent_text_len[s.index] = end
         return RequestOutput(request_id=self.request_id, prompt=self.prompt,
                              prompt_token_ids=self.prompt_token_ids, outputs=outs,
                              finished=self.is_finished(), metrics=self.metrics,
