@@ -151,6 +151,7 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
             for pi, (text, ids) in enumerate(prompts):
                 final = None
                 agen = async_engine.generate(text, sp, f"{rid}-{pi}", ids, priority=req.priority)
+                completed = False
                 try:
                     async for out in agen:
                         final = out
@@ -161,8 +162,11 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                                     choices=[S.CompletionChoice(index=pi * sp.n + c.index, text=delta,
                                                                 finish_reason=c.finish_reason)])
                                 yield "data: " + chunk.model_dump_json(exclude={"usage"}, exclude_none=True) + "\n\n"
+                    completed = True
                 finally:
                     await agen.aclose()           # a stream closed early aborts its request now, not at GC
+                    if not completed:
+                        metrics.on_request_finished(final, "completions", status="aborted")
                 metrics.on_request_finished(final, "completions")
                 usage.prompt_tokens += len(final.prompt_token_ids)
                 usage.completion_tokens += sum(len(c.token_ids) for c in final.outputs)
@@ -207,6 +211,7 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                 S.ChatChunkChoice(index=i, delta=S.ChatDelta(role="assistant", content=""))]))
         final = None
         agen = async_engine.generate(None, sp, rid, ids, priority=req.priority)
+        completed = False
         try:
             try:
                 async for out in agen:
@@ -219,8 +224,11 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                             yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
                                 S.ChatChunkChoice(index=c.index, delta=S.ChatDelta(),
                                                   finish_reason=c.finish_reason)]))
+                completed = True
             finally:
                 await agen.aclose()               # a stream closed early aborts its request now, not at GC
+                if not completed:
+                    metrics.on_request_finished(final, "chat", status="aborted")
             metrics.on_request_finished(final, "chat")
             if req.stream_options and req.stream_options.include_usage and final is not None:
                 n_out = sum(len(c.token_ids) for c in final.outputs)

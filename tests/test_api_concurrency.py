@@ -101,6 +101,13 @@ def test_concurrent_streams_with_disconnects_over_http():
                                          [dropped(client, i) for i in range(4)]))
             assert all(res), res
             ready = (await client.get(f"{base}/health/ready")).status_code
+            for _ in range(100):                  # the dropped streams are counted once their generators close
+                text = (await client.get(f"{base}/metrics")).text
+                if 'requests_total{status="aborted"} 4.0' in text:
+                    break
+                await asyncio.sleep(0.05)
+            assert 'requests_total{status="aborted"} 4.0' in text, [ln for ln in text.splitlines()
+                                                                     if "requests_total" in ln]
         return ready
 
     try:
