@@ -52,6 +52,10 @@ class CallNode:
     finished: Optional[float] = None
 
 
+_TERMINAL = (CallState.DONE, CallState.FAILED, CallState.CANCELLED, CallState.TIMED_OUT)
+_DEAD = (CallState.FAILED, CallState.CANCELLED, CallState.TIMED_OUT)
+
+
 class RecursiveScheduler:
     def __init__(self, limits: Optional[SchedulerLimits] = None):
         self.limits = limits or SchedulerLimits()
@@ -69,9 +73,23 @@ class RecursiveScheduler:
         if self.num_pending() >= self.limits.max_pending:
             raise RuntimeError(f"too many pending sub-calls ({self.limits.max_pending})")
         cid = next(self._ids)
-        self.nodes[cid] = CallNode(cid, parent, depth, prompt, instruction, self.limits.priority_decay ** depth)
+        node = CallNode(cid, parent, depth, prompt, instruction, self.limits.priority_decay ** depth)
+        if self._under_dead(parent):
+            # a call on the path to the root already failed, was cancelled or timed out (its
+            # model output can still arrive and ask for sub-calls): born cancelled, never run
+            node.state = CallState.CANCELLED
+            node.finished = time.monotonic()
+        self.nodes[cid] = node
         p.children.append(cid)
         return cid
+
+    def _under_dead(self, cid: Optional[int]) -> bool:
+        while cid is not None:
+            n = self.nodes[cid]
+            if n.state in _DEAD:
+                return True
+            cid = n.parent
+        return False
 
     def spawn_batch(self, parent: int, items: List[tuple]) -> List[int]:
         return [self.spawn(parent, pr, ins) for pr, ins in items]
@@ -97,19 +115,23 @@ class RecursiveScheduler:
 
     def start(self, cid: int) -> None:
         n = self.nodes[cid]
+        if n.state != CallState.PENDING:
+            return                     # only pending calls start (a cancelled one stays cancelled)
         n.state = CallState.RUNNING
         n.started = time.monotonic()
 
     def complete(self, cid: int, result: str) -> None:
         n = self.nodes[cid]
-        if n.state in (CallState.CANCELLED, CallState.TIMED_OUT):
-            return
+        if n.state in _TERMINAL:
+            return                     # terminal states are final
         n.state = CallState.DONE
         n.result = result
         n.finished = time.monotonic()
 
     def fail(self, cid: int, error: str) -> None:
         n = self.nodes[cid]
+        if n.state in _TERMINAL:
+            return
         n.state = CallState.FAILED
         n.error = error
         n.finished = time.monotonic()
@@ -117,11 +139,13 @@ class RecursiveScheduler:
             self.cancel(c)
 
     def cancel(self, cid: int) -> None:
+        """Cancels a call and everything still pending or running below it; calls that
+        already ended keep their state, but the cascade goes through them (a finished
+        call can have sub-calls still queued)."""
         n = self.nodes[cid]
-        if n.state in (CallState.DONE, CallState.FAILED, CallState.CANCELLED, CallState.TIMED_OUT):
-            return
-        n.state = CallState.CANCELLED
-        n.finished = time.monotonic()
+        if n.state not in _TERMINAL:
+            n.state = CallState.CANCELLED
+            n.finished = time.monotonic()
         for c in list(n.children):
             self.cancel(c)
 
