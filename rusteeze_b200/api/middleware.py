@@ -54,9 +54,24 @@ class SlidingWindowLimiter:
         self.per_day = per_day
         self.hits: Dict[str, Deque[float]] = collections.defaultdict(collections.deque)
         self.day: Dict[str, Deque[float]] = collections.defaultdict(collections.deque)
+        self._checks = 0
+        self._sweep_at = 4096          # table size that triggers the next sweep (doubles as it grows)
+
+    def _forget_idle(self, now: float) -> None:
+        """Drops keys with no admission inside their windows: keyed by client address, the
+        tables would otherwise grow with every client ever seen."""
+        for k in [k for k, q in self.hits.items() if not q or now - q[-1] >= 60.0]:
+            d = self.day.get(k)
+            if d is None or not d or now - d[-1] >= 86400.0:
+                self.hits.pop(k, None)
+                self.day.pop(k, None)
+        self._sweep_at = max(4096, 2 * len(self.hits))     # amortised O(1) per check
 
     def check(self, key: str, now: Optional[float] = None):
         now = time.monotonic() if now is None else now
+        self._checks += 1
+        if self._checks % 1024 == 0 or len(self.hits) > self._sweep_at:
+            self._forget_idle(now)
         q = self.hits[key]
         while q and now - q[0] >= 60.0:
             q.popleft()
