@@ -127,6 +127,10 @@ class SpecDecoder:
     # ------------------------------------------------------------------ main
     def step(self):
         eng = self.engine
+        self._steps = getattr(self, "_steps", 0) + 1
+        if self._steps % 256 == 0 and len(self.draft_computed) > len(eng.seq_to_request):
+            # sequences of aborted requests never reach the finish path that drops their entry
+            self.draft_computed = {k: v for k, v in self.draft_computed.items() if k in eng.seq_to_request}
         so = eng.scheduler.schedule()
         # preempted sequences lose their draft KV (swapped or freed): the draft recomputes it
         for s in so.preempted:

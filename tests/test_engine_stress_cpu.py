@@ -251,3 +251,29 @@ def test_a_batch_beyond_the_staging_buffers_is_refused():
     eng.bm.allocate_prompt(seq.seq_id, seq.tokens_np())
     with pytest.raises(ValueError, match="staging capacity"):
         r.forward_arrays(eng.bm, [seq.seq_id], [0], [r.max_tokens + 1], np.zeros(r.max_tokens + 1, np.int64), 1)
+
+
+def test_speculative_decoder_forgets_aborted_sequences():
+    """Aborted requests leave no per-sequence draft state behind in a long-running engine."""
+    from rusteeze_b200.config.config import SpeculativeSection
+    rng = np.random.default_rng(1)
+    eng = _engine(rng, "recompute", prefix=False, chunked=True,
+                  spec=SpeculativeSection(draft_preset=None, num_speculative_tokens=2))
+    import dataclasses
+    from rusteeze_b200.models.loader import build_model
+    sd = eng.spec                          # a separate draft, so per-sequence draft state is kept
+    sd.self_draft = False
+    sd.draft = build_model(dataclasses.replace(MC, num_hidden_layers=1), dtype=__import__("torch").float32, seed=3)
+    from rusteeze_b200.engine.model_runner import ModelRunner
+    r = eng.runner
+    sd.drunner = ModelRunner(sd.draft, num_gpu_blocks=r.num_gpu_blocks, num_cpu_blocks=0,
+                             max_num_seqs=r.max_num_seqs, max_num_batched_tokens=r.max_tokens,
+                             max_model_len=eng.max_model_len, use_cuda_graph=False)
+    for i in range(300):
+        eng.add_request(f"a{i}", None, SamplingParams(temperature=0.0, max_tokens=50, ignore_eos=True),
+                        rng.integers(0, 300, 8).tolist())
+        eng.step()
+        eng.abort_request(f"a{i}")
+    for _ in range(300):
+        eng.step()
+    assert len(sd.draft_computed) <= len(eng.seq_to_request) + 1
