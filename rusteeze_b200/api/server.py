@@ -308,15 +308,20 @@ def _chat_logprobs(tok, c) -> S.ChatLogProbs:
 
 
 def serve(config, engine=None, host: Optional[str] = None, port: Optional[int] = None) -> None:
-    """Builds the engine (unless given), starts the engine thread and runs uvicorn
+    """Builds the engine (unless given; D replicas behind a router when
+    model.data_parallel_size = D > 1), starts the engine thread(s) and runs uvicorn
     with graceful SIGINT/SIGTERM shutdown (crates/rusteeze-api/src/server.rs:304-330).
     TLS is real when cert/key are configured (the reference falls back to
     plaintext, server.rs:185-192)."""
     import uvicorn
     from rusteeze_b200.engine.async_engine import AsyncLLMEngine
     from rusteeze_b200.engine.llm_engine import LLMEngine
-    eng = engine or LLMEngine(config)
-    ae = AsyncLLMEngine(eng, request_timeout_s=config.engine.request_timeout_seconds).start()
+    if engine is None and config.model.data_parallel_size > 1:
+        from rusteeze_b200.engine.dp_engine import ReplicatedAsyncEngine
+        ae = ReplicatedAsyncEngine.from_config(config).start()
+    else:
+        eng = engine or LLMEngine(config)
+        ae = AsyncLLMEngine(eng, request_timeout_s=config.engine.request_timeout_seconds).start()
     metrics = EngineMetrics(model_name=config.model.served_name())
     app = create_app(ae, config, metrics)
     if config.server.metrics_port:

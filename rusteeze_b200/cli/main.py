@@ -32,6 +32,9 @@ def _model_args(p: argparse.ArgumentParser, required: bool = True) -> None:
     p.add_argument("--device", default="auto")
     p.add_argument("--dtype", default="auto")
     p.add_argument("--tensor-parallel-size", type=int, default=1)
+    p.add_argument("--data-parallel-size", type=int, default=1,
+                   help="serve: D engine replicas (one GPU each) behind a request router")
+    p.add_argument("--router-policy", default="least_loaded", choices=["least_loaded", "round_robin", "random"])
     p.add_argument("--max-model-len", type=int, default=None)
     p.add_argument("--gpu-memory-utilization", type=float, default=0.9)
     p.add_argument("--quantization", default=None, choices=[None, "fp8_block", "fp8"])
@@ -41,7 +44,7 @@ def _model_args(p: argparse.ArgumentParser, required: bool = True) -> None:
 
 def _overrides(a) -> dict:
     model = {"device": a.device, "dtype": a.dtype, "tensor_parallel_size": a.tensor_parallel_size,
-             "max_model_len": a.max_model_len, "seed": a.seed}
+             "data_parallel_size": a.data_parallel_size, "max_model_len": a.max_model_len, "seed": a.seed}
     if a.model:
         if os.path.isdir(a.model):
             model["path"] = a.model
@@ -50,7 +53,7 @@ def _overrides(a) -> dict:
     if getattr(a, "quantization", None):
         model["quantization"] = {"method": "fp8_block"}
     eng = {"gpu_memory_utilization": a.gpu_memory_utilization, "enforce_eager": a.enforce_eager}
-    return {"model": model, "engine": eng}
+    return {"model": model, "engine": eng, "server": {"router_policy": a.router_policy}}
 
 
 def _load_config(a, extra: Optional[dict] = None):
@@ -87,8 +90,8 @@ def cmd_serve(a) -> int:
     if not a.json:
         print(BANNER, file=sys.stderr)
         print(f"serving {cfg.model.served_name()} on {cfg.server.host}:{cfg.server.port} "
-              f"(tp={cfg.model.tensor_parallel_size})", file=sys.stderr)
-    serve(cfg, engine=_engine(cfg))
+              f"(tp={cfg.model.tensor_parallel_size}, dp={cfg.model.data_parallel_size})", file=sys.stderr)
+    serve(cfg, engine=None if cfg.model.data_parallel_size > 1 else _engine(cfg))
     return 0
 
 

@@ -94,6 +94,7 @@ class ServerSection:
     tls: Optional[TlsConfig] = None
     rate_limit: Optional[RateLimitConfig] = None
     metrics_port: Optional[int] = None
+    router_policy: str = "least_loaded"    # data-parallel replicas: least_loaded | round_robin | random
 
 
 @dataclass

@@ -24,10 +24,18 @@ def collect_errors(cfg) -> List[str]:
         e.append(f"model.dtype must be one of {sorted(_DTYPES)}, got {m.dtype!r}")
     if not _DEVICE_RE.match(m.device):
         e.append(f"model.device must be auto|cpu|cuda|cuda:N (metal/vulkan are not supported), got {m.device!r}")
-    for k in ("tensor_parallel_size", "expert_parallel_size", "data_parallel_size"):
+    for k in ("tensor_parallel_size", "expert_parallel_size"):
         v = getattr(m, k)
         if v < 1 or v & (v - 1):
             e.append(f"model.{k} must be a power of two >= 1, got {v}")
+    if m.data_parallel_size < 1:
+        e.append(f"model.data_parallel_size must be >= 1, got {m.data_parallel_size}")
+    if m.data_parallel_size > 1 and m.tensor_parallel_size > 1:
+        e.append("model.data_parallel_size > 1 serves tensor_parallel_size 1 replicas (one GPU each)")
+    if m.data_parallel_size > 1 and m.device.startswith("cuda:"):
+        e.append("model.device must be auto|cuda|cpu with data_parallel_size > 1 (replica i runs on cuda:i)")
+    if s.router_policy not in ("least_loaded", "round_robin", "random"):
+        e.append(f"server.router_policy must be least_loaded|round_robin|random, got {s.router_policy!r}")
     if m.pipeline_parallel_size != 1:
         e.append("model.pipeline_parallel_size > 1 is not supported: one NVSwitch domain serves these "
                  "models with tensor/expert parallelism")

@@ -140,10 +140,14 @@ class AsyncLLMEngine:
                 except BaseException as e:  # noqa: BLE001 -- delivered to the caller
                     self._push(item, e)
             elif kind == "abort":
-                if item in self._streams:
+                sub = self._streams.pop(item, None)
+                if sub is not None:
+                    req = self.engine.requests.get(item)
                     self.engine.abort_request(item)
-                    self._streams.pop(item, None)
                     self._deadlines.pop(item, None)
+                    if req is not None:
+                        # a caller still iterating the stream gets its final (aborted) output
+                        self._push(sub, req.to_output(delta=True))
 
     def _expire(self) -> None:
         now = time.monotonic()
@@ -177,6 +181,10 @@ class AsyncLLMEngine:
             log.error("device kernel reported status %d; engine marked unhealthy", code)
 
     def _loop(self) -> None:
+        dev = str(getattr(self.engine, "device", "cpu"))
+        if dev.startswith("cuda"):
+            import torch
+            torch.cuda.set_device(torch.device(dev))   # the current device is per thread
         while not self._stop.is_set():
             self._drain_inbox()
             self._expire()

@@ -4,8 +4,9 @@ Counterpart of crates/rusteeze-engine/src/router.rs (least-loaded /
 round-robin / random selection over N backends, manual health flags, a
 log2 latency histogram with p50/p99; :13-274), which nothing in the
 reference calls.  Here a `ReplicaRouter` fronts several engine replicas
-(e.g. 8 x TP1 on one box, one process per GPU) and is used by the DP
-serving front end; health can be driven by a prober callback.
+(8 x TP1 on one box, one GPU each) for the data-parallel serving front end
+(`engine.dp_engine.ReplicatedAsyncEngine`); health is driven by a prober
+callback (the replica engine's readiness).
 """
 from __future__ import annotations
 
@@ -39,7 +40,7 @@ class LatencyHistogram:
     def percentile(self, q: float) -> Optional[float]:
         if self.n == 0:
             return None
-        target = q / 100.0 * self.n
+        target = max(1, math.ceil(q / 100.0 * self.n))     # rank of the q-th percentile sample
         c = 0
         for i, k in enumerate(self.counts):
             c += k
@@ -84,6 +85,8 @@ class ReplicaRouter:
         for r in self.replicas:
             if r.name == name:
                 r.healthy = healthy
+                return
+        raise KeyError(f"no replica named {name!r}")
 
     def select(self) -> Replica:
         with self._lock:
