@@ -8,6 +8,8 @@ the GPU sampler packs into a per-row parameter tensor (see
 """
 from __future__ import annotations
 
+import math
+
 import enum
 from dataclasses import dataclass, field, asdict
 from typing import Dict, List, Optional
@@ -101,8 +103,20 @@ class SamplingParams:
         def bad(msg: str) -> None:
             raise InvalidRequestError(msg, param="sampling_params")
 
+        for name in ("temperature", "top_p", "min_p", "typical_p", "frequency_penalty", "presence_penalty",
+                     "repetition_penalty", "length_penalty", "eta_cutoff", "epsilon_cutoff", "mirostat_tau",
+                     "mirostat_eta"):
+            v = getattr(self, name)
+            if not math.isfinite(v):
+                bad(f"{name} must be a finite number, got {v}")
         if self.temperature < 0.0:
             bad(f"temperature must be >= 0, got {self.temperature}")
+        if not 0.0 <= self.epsilon_cutoff < 1.0:
+            bad(f"epsilon_cutoff must be in [0, 1), got {self.epsilon_cutoff}")
+        if not 0.0 <= self.eta_cutoff < 1.0:
+            bad(f"eta_cutoff must be in [0, 1), got {self.eta_cutoff}")
+        if self.mirostat_tau < 0.0:
+            bad(f"mirostat_tau must be >= 0, got {self.mirostat_tau}")
         if not 0.0 <= self.top_p <= 1.0:
             bad(f"top_p must be in [0, 1], got {self.top_p}")
         if self.top_k == 0 or self.top_k < -1:

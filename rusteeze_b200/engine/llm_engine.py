@@ -190,6 +190,10 @@ class LLMEngine:
         V = self.model_config.vocab_size
         if min(prompt_token_ids) < 0 or max(prompt_token_ids) >= V:
             raise InvalidRequestError(f"prompt token ids must be in [0, {V})")
+        # token ids the sampler indexes logits with: out of range they would fail inside step()
+        for what, ids in (("logit_bias", params.logit_bias.keys()), ("stop_token_ids", params.stop_token_ids)):
+            if any(not 0 <= int(t) < V for t in ids):
+                raise InvalidRequestError(f"{what} token ids must be in [0, {V})")
         if len(prompt_token_ids) >= self.max_model_len:
             raise ContextLengthExceededError(
                 f"prompt has {len(prompt_token_ids)} tokens; the model context is {self.max_model_len}")
