@@ -16,6 +16,12 @@ from typing import Dict, List, Optional
 
 from rusteeze_b200.core.errors import InvalidRequestError
 
+# Upper bounds the reference does not have (sampling.rs:357-383 checks only the lower
+# ones): one request must not be able to make the engine build an unbounded number of
+# sequences, or return a vocabulary-sized logprob table for every token.
+MAX_BEST_OF = 256
+MAX_LOGPROBS = 20
+
 
 class SamplingStrategy(str, enum.Enum):
     GREEDY = "greedy"
@@ -135,14 +141,18 @@ class SamplingParams:
             bad(f"n must be >= 1, got {self.n}")
         if self.best_of < self.n:
             bad(f"best_of ({self.best_of}) must be >= n ({self.n})")
+        if self.best_of > MAX_BEST_OF:
+            bad(f"best_of / n must be <= {MAX_BEST_OF}, got {self.best_of}")
         if self.max_tokens is not None and self.max_tokens < 1:
             bad(f"max_tokens must be >= 1, got {self.max_tokens}")
         if self.min_tokens < 0:
             bad(f"min_tokens must be >= 0, got {self.min_tokens}")
         if self.max_tokens is not None and self.min_tokens > self.max_tokens:
             bad(f"min_tokens ({self.min_tokens}) must be <= max_tokens ({self.max_tokens})")
-        if self.logprobs is not None and self.logprobs < 0:
-            bad("logprobs must be >= 0")
+        for name in ("logprobs", "prompt_logprobs"):
+            v = getattr(self, name)
+            if v is not None and not 0 <= v <= MAX_LOGPROBS:
+                bad(f"{name} must be in [0, {MAX_LOGPROBS}], got {v}")
         if self.mirostat_mode not in (0, 1, 2):
             bad(f"mirostat_mode must be 0, 1 or 2, got {self.mirostat_mode}")
         if self.use_beam_search:

@@ -1,0 +1,111 @@
+"""HTTP request fuzzing on the tiny CPU model: random JSON bodies for the completion
+and chat endpoints -- wrong types, missing fields, edge numbers, token ids outside
+the vocabulary, odd chat content -- get a 2xx or a 4xx with an OpenAI error body,
+never a 500, and the engine stays ready and serves a plain request afterwards."""
+import json
+import random
+
+import pytest
+from fastapi.testclient import TestClient
+
+from rusteeze_b200.api.server import create_app
+from rusteeze_b200.config.config import Config
+from rusteeze_b200.engine.async_engine import AsyncLLMEngine
+from rusteeze_b200.engine.llm_engine import LLMEngine
+
+_VALUES = [None, True, 0, 1, -1, 3, 2 ** 31, 2 ** 63, -2 ** 63, 0.5, -0.5, 1e308, "x", "", [], {}, [1, 2],
+           ["a"], {"a": 1}]
+_NUM_FIELDS = ["max_tokens", "temperature", "top_p", "top_k", "min_p", "n", "best_of", "presence_penalty",
+               "frequency_penalty", "repetition_penalty", "seed", "priority", "min_tokens", "logprobs",
+               "top_logprobs", "max_completion_tokens"]
+
+
+def _cfg():
+    cfg = Config()
+    cfg.model.preset = "tiny-llama"
+    cfg.model.device = "cpu"
+    cfg.model.dtype = "float32"
+    cfg.model.max_model_len = 96
+    cfg.engine.num_gpu_blocks = 48
+    cfg.engine.max_num_seqs = 4
+    cfg.engine.max_num_batched_tokens = 128
+    cfg.server.timeout_seconds = 30
+    cfg.logging.request_logging = False
+    return cfg
+
+
+def _body(rng, chat, V):
+    b = {}
+    if chat:
+        msgs = rng.choice([
+            [{"role": "user", "content": "hi"}],
+            [{"role": "system", "content": "s"}, {"role": "user", "content": [{"type": "text", "text": "a"}]}],
+            [{"role": "user"}], [], [{"content": "no role"}], "hello", [{"role": "tool", "content": None}],
+            [{"role": "user", "content": [{"type": "image_url", "image_url": {"url": "x"}}]}],
+        ])
+        if rng.random() < 0.95:
+            b["messages"] = msgs
+    else:
+        p = rng.choice(["abc", "", ["a", "b"], [1, 2, 3], [[1, 2], [3]], [V, 1], [-1], [[]], [], 5, None,
+                        "word " * 200])
+        if rng.random() < 0.95:
+            b["prompt"] = p
+    for k in rng.sample(_NUM_FIELDS, rng.randint(0, 6)):
+        b[k] = rng.choice(_VALUES) if rng.random() < 0.5 else rng.choice([0, 1, 2, 4])
+    if rng.random() < 0.2:
+        b["logit_bias"] = rng.choice([{"5": 1.0}, {str(V + 1): 1.0}, {"-2": 3.0}, {"x": 1.0}, {"5": 1e6}, []])
+    if rng.random() < 0.2:
+        b["stop_token_ids"] = rng.choice([[1], [V], [-1], ["a"], None])
+    if rng.random() < 0.2:
+        b["stop"] = rng.choice(["\n", ["a", "b"], "", [""], 5, ["x"] * 10])
+    if rng.random() < 0.3:
+        b["stream"] = rng.choice([True, False, "yes"])
+    if rng.random() < 0.1:
+        b["stream_options"] = rng.choice([{"include_usage": True}, {"include_usage": "no"}, 1])
+    if rng.random() < 0.1:
+        b["model"] = rng.choice(["tiny-llama", "other", 7])
+    if rng.random() < 0.1:
+        b["response_format"] = rng.choice([{"type": "json_object"}, {"type": "nope"}, "x"])
+    b.setdefault("max_tokens", rng.choice([1, 3, 5]))
+    return b
+
+
+@pytest.fixture(scope="module")
+def client():
+    cfg = _cfg()
+    ae = AsyncLLMEngine(LLMEngine(cfg)).start()
+    c = TestClient(create_app(ae, cfg), raise_server_exceptions=False)
+    yield c, ae
+    ae.shutdown()
+
+
+def _post(c, url, body):
+    if body.get("stream") is True:
+        with c.stream("POST", url, json=body) as r:
+            return r.status_code, "".join(r.iter_text())
+    r = c.post(url, json=body)
+    return r.status_code, r.text
+
+
+@pytest.mark.parametrize("seed", range(3))
+def test_random_bodies_never_get_a_server_error(client, seed):
+    c, ae = client
+    V = ae.engine.model_config.vocab_size
+    rng = random.Random(seed)
+    codes = {}
+    for _ in range(60):
+        chat = rng.random() < 0.5
+        body = _body(rng, chat, V)
+        url = "/v1/chat/completions" if chat else "/v1/completions"
+        code, text = _post(c, url, body)
+        codes[code] = codes.get(code, 0) + 1
+        assert code < 500, (body, code, text[:400])
+        if code == 200 and body.get("stream") is True:
+            assert text.rstrip().endswith("data: [DONE]"), (body, text[-300:])
+        if code >= 400:
+            err = json.loads(text)
+            assert "error" in err or "detail" in err, text[:300]
+        assert ae.is_ready, (body, ae.last_error)
+    assert codes.get(200, 0) > 0 and sum(v for k, v in codes.items() if k >= 400) > 0, codes
+    code, text = _post(c, "/v1/completions", {"prompt": "fine", "max_tokens": 2, "ignore_eos": True})
+    assert code == 200 and json.loads(text)["usage"]["completion_tokens"] == 2
