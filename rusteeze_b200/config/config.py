@@ -186,7 +186,7 @@ def _from_dict(cls, data: Any):
     for k, v in data.items():
         if k not in hints:
             raise ConfigError(f"unknown config key {cls.__name__}.{k}")
-        kw[k] = _convert(hints[k].type, v)
+        kw[k] = _convert(hints[k].type, v, f"{cls.__name__}.{k}")
     return cls(**kw)
 
 
@@ -199,11 +199,50 @@ _SECTION_TYPES = {
 }
 
 
-def _convert(tp, v):
+def _convert(tp, v, where: str = "value"):
+    """Checks a file or override value against the field's annotation: sections
+    recurse; int / float / bool / str / List[...] fields get that type or a
+    ConfigError naming the key (numeric strings, as environment variables give them,
+    are accepted for numbers)."""
     t = tp if isinstance(tp, str) else getattr(tp, "__name__", str(tp))
     for name, cls in _SECTION_TYPES.items():
         if name in t:
             return _from_dict(cls, v)
+    optional = t.startswith("Optional[")
+    base = t[len("Optional["):-1] if optional else t
+    if v is None:
+        if optional:
+            return None
+        raise ConfigError(f"{where} must not be null")
+    if base.startswith("List["):
+        if not isinstance(v, (list, tuple)):
+            raise ConfigError(f"{where} must be a list, got {type(v).__name__}")
+        return [_convert(base[5:-1], x, f"{where}[{i}]") for i, x in enumerate(v)]
+    if base == "bool":
+        if isinstance(v, bool):
+            return v
+        if isinstance(v, str) and v.lower() in ("true", "false", "1", "0", "yes", "no"):
+            return v.lower() in ("true", "1", "yes")
+        raise ConfigError(f"{where} must be true or false, got {v!r}")
+    if base in ("int", "float"):
+        if isinstance(v, str):
+            try:
+                v = float(v) if base == "float" or any(c in v for c in ".eE") else int(v)
+            except ValueError:
+                raise ConfigError(f"{where} must be a number, got {v!r}") from None
+        if isinstance(v, bool) or not isinstance(v, (int, float)):
+            raise ConfigError(f"{where} must be a number, got {v!r}")
+        if base == "int":
+            if isinstance(v, float) and not v.is_integer():
+                raise ConfigError(f"{where} must be an integer, got {v!r}")
+            return int(v)
+        return float(v)
+    if base == "str":
+        if isinstance(v, str):
+            return v
+        if isinstance(v, (int, float)) and not isinstance(v, bool):
+            return str(v)              # e.g. an all-digit API key written unquoted
+        raise ConfigError(f"{where} must be a string, got {v!r}")
     return v
 
 

@@ -56,15 +56,22 @@ def detect_format(path: str) -> str:
 
 
 def parse_text(text: str, fmt: str) -> Dict[str, Any]:
-    if fmt == "yaml":
-        import yaml
-        return yaml.safe_load(text) or {}
-    if fmt == "toml":
-        import tomllib
-        return tomllib.loads(text)
-    if fmt == "json":
-        return json.loads(text)
-    raise ConfigError(f"unknown format {fmt}")
+    if fmt not in ("yaml", "toml", "json"):
+        raise ConfigError(f"unknown format {fmt}")
+    try:
+        if fmt == "yaml":
+            import yaml
+            d = yaml.safe_load(text) or {}
+        elif fmt == "toml":
+            import tomllib
+            d = tomllib.loads(text)
+        else:
+            d = json.loads(text)
+    except Exception as e:  # noqa: BLE001 -- yaml / toml / json parse errors
+        raise ConfigError(f"cannot parse the {fmt} config: {e}") from None
+    if not isinstance(d, dict):
+        raise ConfigError(f"a {fmt} config must be a mapping of sections, got {type(d).__name__}")
+    return d
 
 
 def load_file(path: str) -> Dict[str, Any]:

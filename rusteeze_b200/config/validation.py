@@ -49,6 +49,16 @@ def collect_errors(cfg) -> List[str]:
         e.append("server.timeout_seconds must be > 0")
     if s.tls is not None and (not s.tls.cert_path or not s.tls.key_path):
         e.append("server.tls needs cert_path and key_path")
+    rl = s.rate_limit
+    if rl is not None and rl.enabled:
+        if rl.requests_per_minute < 1:
+            e.append(f"server.rate_limit.requests_per_minute must be >= 1, got {rl.requests_per_minute}")
+        if rl.by not in ("api_key", "ip"):
+            e.append(f"server.rate_limit.by must be api_key|ip, got {rl.by!r}")
+        if rl.burst < 0:
+            e.append(f"server.rate_limit.burst must be >= 0, got {rl.burst}")
+        if rl.requests_per_day is not None and rl.requests_per_day < 1:
+            e.append(f"server.rate_limit.requests_per_day must be >= 1, got {rl.requests_per_day}")
     if g.max_num_seqs < 1:
         e.append("engine.max_num_seqs must be >= 1")
     if g.max_num_batched_tokens < g.max_num_seqs:
