@@ -12,8 +12,9 @@ crates/rusteeze-engine/src/recursive_engine.rs:591-754:
   DECOMPOSE(chunk, overlap)     prompt -> __chunks__ (sentence/paragraph aware)
   SEARCH(pattern)               regex search over the prompt (the reference
                                 does a case-insensitive substring match,
-                                prompt_env.rs:823-831; invalid regexes fall
-                                back to that)
+                                prompt_env.rs:823-831; invalid regexes and
+                                ones at risk of catastrophic backtracking
+                                fall back to that)
   SET_VAR(name, value) / GET_VAR(name)
   SUBCALL(text, instruction)    one sub-model call on literal text
   SUBCALL_VAR(var, instruction) one sub-model call on a variable
@@ -109,6 +110,68 @@ def parse_model_output(text: str) -> Op:
             return Op("DECOMPOSE", (int(m.group(1)), 200))
     t = text.strip()
     return Op("THINK", (t[:200] + "..." if len(t) > 200 else t,))
+
+
+# ----------------------------------------------------------------------------- model-written regexes
+_MAX_PATTERN = 512
+
+
+_REGEX_WORKER = (
+    "import json,re,sys\n"
+    "d=json.loads(sys.stdin.read())\n"
+    "rx=re.compile(d['p'],d['f'])\n"
+    "if d['lines']:\n"
+    "    out=[k for k,ln in enumerate(d['t'].splitlines()) if rx.search(ln)]\n"
+    "else:\n"
+    "    out=[]\n"
+    "    for m in rx.finditer(d['t']):\n"
+    "        out.append([m.start(),m.group(0)])\n"
+    "        if len(out)>=d['k']:\n"
+    "            break\n"
+    "sys.stdout.write(json.dumps(out))\n")
+REGEX_TIMEOUT_S = 2.0
+
+
+def _repeats(pat: str) -> bool:
+    """Repetition, alternation, several optional items or a backreference: the
+    constructs whose backtracking can take super-linear time."""
+    optional = len(re.findall(r"(?<!\()\?", pat))
+    return any(ch in pat for ch in "*+{|") or optional > 4 or bool(re.search(r"\\[1-9]", pat))
+
+
+def model_regex(pat: str, text: str, flags: int, lines: bool = False, limit: int = 20):
+    """Runs a regex written by the model over `text`: the first `limit` matches as
+    (position, match) pairs, or with `lines` the indices of the matching lines.
+    Returns None when the pattern is invalid, longer than 512 characters or did not
+    finish within REGEX_TIMEOUT_S (the caller then matches it as a plain substring).
+
+    Python's `re` backtracks and has no time limit: nested repeats ((a+)+) take
+    exponential time and even `a*a*b` takes minutes over a 20k-character prompt, which
+    would stall the engine thread.  Patterns without any repetition or alternation run
+    here; the others run in a child interpreter that is killed at the time limit."""
+    if len(pat) > _MAX_PATTERN:
+        return None
+    try:
+        rx = re.compile(pat, flags)
+    except re.error:
+        return None
+    if not _repeats(pat):
+        if lines:
+            return [k for k, ln in enumerate(text.splitlines()) if rx.search(ln)]
+        return [(m.start(), m.group(0)) for _, m in zip(range(limit), rx.finditer(text))]
+    import json
+    import subprocess
+    import sys
+    try:
+        r = subprocess.run([sys.executable, "-I", "-S", "-c", _REGEX_WORKER],
+                           input=json.dumps({"p": pat, "f": int(flags), "t": text, "lines": lines, "k": limit}),
+                           capture_output=True, text=True, timeout=REGEX_TIMEOUT_S)
+    except (subprocess.TimeoutExpired, OSError):
+        return None
+    if r.returncode != 0:
+        return None
+    out = json.loads(r.stdout)
+    return out if lines else [(int(a), str(b)) for a, b in out]
 
 
 # ----------------------------------------------------------------------------- chunking
@@ -221,17 +284,16 @@ class PromptEnvironment:
                 return ExecResult(stdout=f"{len(chunks)} chunks stored in {self.CHUNKS_VAR}")
             if k == "SEARCH":
                 pat = a[0]
-                try:
-                    rx = re.compile(pat, re.IGNORECASE | re.MULTILINE)
-                    hits = [(m.start(), m.group(0)) for _, m in zip(range(self.limits.max_search_results),
-                                                                  rx.finditer(self.prompt))]
-                except re.error:
+                hits = model_regex(pat, self.prompt, re.IGNORECASE | re.MULTILINE,
+                                   limit=self.limits.max_search_results)
+                if hits is None:
                     low, lp = self.prompt.lower(), pat.lower()
                     hits, i = [], low.find(lp)
                     while i >= 0 and len(hits) < self.limits.max_search_results:
                         hits.append((i, self.prompt[i:i + len(pat)]))
                         i = low.find(lp, i + 1)
-                lines = [f"@{pos}: ...{self.prompt[max(0, pos - 60):pos + len(g) + 60]!r}..." for pos, g in hits]
+                lines = [f"@{pos}: ...{self.prompt[max(0, pos - 60):pos + min(len(g), 200) + 60]!r}..."
+                         for pos, g in hits]
                 return ExecResult(stdout=f"{len(hits)} match(es)\n" + "\n".join(lines))
             if k == "SET_VAR":
                 st.set(a[0], a[1])
@@ -308,8 +370,13 @@ class PromptEnvironment:
             n = int(arg) if arg and arg.isdigit() else 1000
             res = str(v)[:n] if not isinstance(v, list) else v[:n]
         elif name == "grep":
-            rx = re.compile(arg or "", re.IGNORECASE)
-            res = "\n".join(ln for ln in str(v).splitlines() if rx.search(ln))
+            text_lines = str(v).splitlines()
+            idx = model_regex(arg or "", str(v), re.IGNORECASE, lines=True)
+            if idx is not None:
+                res = "\n".join(text_lines[k] for k in idx)
+            else:
+                kw = (arg or "").lower()
+                res = "\n".join(ln for ln in text_lines if kw in ln.lower())
         else:
             return ExecResult(error=f"unknown transform {op!r}")
         st.set(dst, res)
