@@ -183,8 +183,17 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
     async def chat(req: S.ChatCompletionRequest, request: Request):
         _check_model(req.model)
         msgs = [m.model_dump() for m in req.messages]
+        if req.chat_template and not sc.trust_request_chat_template:
+            raise InvalidRequestError("a per-request chat_template is disabled on this server "
+                                      "(server.trust_request_chat_template)", param="chat_template")
         tmpl = template if not req.chat_template else ChatTemplate(jinja=req.chat_template)
-        prompt = tmpl.apply(msgs, add_generation_prompt=req.add_generation_prompt)
+        try:
+            prompt = tmpl.apply(msgs, add_generation_prompt=req.add_generation_prompt)
+        except RusteezeError:
+            raise
+        except Exception as e:  # noqa: BLE001 -- template syntax errors, raise_exception(), bad messages
+            raise InvalidRequestError(f"chat template could not render these messages: {e}",
+                                      param="messages") from None
         ids = eng.tokenizer.encode(prompt, add_special_tokens=False) or eng.tokenizer.encode(prompt)
         lp = (req.top_logprobs or 0) if req.logprobs else None
         sp = _sampling_params(req, defaults, defaults.max_tokens, lp)

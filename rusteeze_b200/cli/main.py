@@ -77,7 +77,8 @@ def _engine(cfg):
 def cmd_serve(a) -> int:
     from rusteeze_b200.api.server import serve
     extra = {"server": {"host": a.host, "port": a.port, "api_key": a.api_key, "metrics_port": a.metrics_port,
-                        "cors": {"enabled": bool(a.cors)}},
+                        "cors": {"enabled": bool(a.cors)},
+                        "trust_request_chat_template": a.trust_request_chat_template or None},
              "engine": {"max_num_seqs": a.max_num_seqs, "block_size": a.block_size, "swap_space_gb": a.swap_space,
                         "enable_prefix_caching": a.enable_prefix_caching,
                         "enable_chunked_prefill": a.enable_chunked_prefill,
@@ -336,6 +337,8 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--cors", action="store_true")
     s.add_argument("--metrics-port", type=int, default=None)
     s.add_argument("--chat-template", default=None)
+    s.add_argument("--trust-request-chat-template", action="store_true",
+                   help="render a chat request's own Jinja chat_template (off: refused with 400)")
     s.add_argument("--trust-remote-code", action="store_true")
     s.add_argument("--pipeline-parallel-size", type=int, default=1)
     s.add_argument("--speculative-model", default=None)

@@ -109,3 +109,27 @@ def test_random_bodies_never_get_a_server_error(client, seed):
     assert codes.get(200, 0) > 0 and sum(v for k, v in codes.items() if k >= 400) > 0, codes
     code, text = _post(c, "/v1/completions", {"prompt": "fine", "max_tokens": 2, "ignore_eos": True})
     assert code == 200 and json.loads(text)["usage"]["completion_tokens"] == 2
+
+
+def test_request_chat_templates_need_the_operator_s_consent():
+    """A chat request's own Jinja template is refused unless the server trusts request
+    templates; a trusted template that fails to render is the client's error (400)."""
+    body = {"messages": [{"role": "user", "content": "hi"}], "max_tokens": 2, "ignore_eos": True,
+            "chat_template": "{% for i in range(99999) %}{% for j in range(99999) %}x{% endfor %}{% endfor %}"}
+    for trusted in (False, True):
+        cfg = _cfg()
+        cfg.server.trust_request_chat_template = trusted
+        ae = AsyncLLMEngine(LLMEngine(cfg)).start()
+        c = TestClient(create_app(ae, cfg), raise_server_exceptions=False)
+        try:
+            if not trusted:
+                r = c.post("/v1/chat/completions", json=body)
+                assert r.status_code == 400 and "chat_template" in r.text
+                continue
+            ok = {**body, "chat_template": "{% for m in messages %}<{{ m.role }}>{{ m.content }}{% endfor %}"}
+            assert c.post("/v1/chat/completions", json=ok).status_code == 200
+            for bad in ("{% if %}", "{{ raise_exception('roles must alternate') }}", "{{ messages[5].content }}x"):
+                r = c.post("/v1/chat/completions", json={**body, "chat_template": bad})
+                assert r.status_code == 400, (bad, r.status_code, r.text)
+        finally:
+            ae.shutdown()
