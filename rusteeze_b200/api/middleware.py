@@ -10,6 +10,8 @@ rate-limit, request-id and timeout layers but never installs them
 """
 from __future__ import annotations
 
+import json
+
 import asyncio
 import collections
 import hmac
@@ -31,6 +33,60 @@ OPEN_PATHS = {"/health", "/health/live", "/health/ready", "/metrics", "/version"
 
 def error_response(err) -> JSONResponse:
     return JSONResponse(err.to_openai(), status_code=err.http_status)
+
+
+class BodyLimitMiddleware:
+    """Refuses request bodies above `max_bytes` (server.max_body_bytes) with 413:
+    by the Content-Length header before anything is read, and, for a body sent
+    without one (chunked), by reading it here up to the limit -- the read stops
+    there, so at most max_body_bytes are ever buffered -- and replaying it to the app."""
+
+    def __init__(self, app, max_bytes: int):
+        self.app = app
+        self.max_bytes = max_bytes
+
+    async def _reject(self, send) -> None:
+        from rusteeze_b200.core.errors import PayloadTooLargeError
+        err = PayloadTooLargeError(f"request body exceeds {self.max_bytes} bytes")
+        body = json.dumps(err.to_openai()).encode()
+        await send({"type": "http.response.start", "status": err.http_status,
+                    "headers": [(b"content-type", b"application/json"),
+                                (b"content-length", str(len(body)).encode())]})
+        await send({"type": "http.response.body", "body": body})
+
+    async def __call__(self, scope, receive, send):
+        if scope["type"] != "http" or self.max_bytes <= 0:
+            return await self.app(scope, receive, send)
+        for k, v in scope.get("headers", []):
+            if k == b"content-length":
+                try:
+                    n = int(v)
+                except ValueError:
+                    n = self.max_bytes + 1
+                if n > self.max_bytes:
+                    return await self._reject(send)
+        if any(k == b"content-length" for k, _ in scope.get("headers", [])):
+            return await self.app(scope, receive, send)
+        # no length given (chunked): read up to the limit here, then replay it to the app
+        chunks, seen, more = [], 0, True
+        while more:
+            msg = await receive()
+            if msg["type"] != "http.request":
+                return                       # the client went away
+            chunks.append(msg.get("body", b""))
+            seen += len(chunks[-1])
+            if seen > self.max_bytes:
+                return await self._reject(send)
+            more = msg.get("more_body", False)
+        replayed = False
+
+        async def replay():
+            nonlocal replayed
+            if not replayed:
+                replayed = True
+                return {"type": "http.request", "body": b"".join(chunks), "more_body": False}
+            return await receive()
+        await self.app(scope, replay, send)
 
 
 class AuthMiddleware(BaseHTTPMiddleware):

@@ -29,7 +29,7 @@ from fastapi.responses import JSONResponse, PlainTextResponse, Response, Streami
 
 from rusteeze_b200 import __version__
 from rusteeze_b200.api import schemas as S
-from rusteeze_b200.api.middleware import (AuthMiddleware, RateLimitMiddleware, RequestIdMiddleware,
+from rusteeze_b200.api.middleware import (AuthMiddleware, BodyLimitMiddleware, RateLimitMiddleware, RequestIdMiddleware,
                                           SlidingWindowLimiter, TimeoutMiddleware, error_response)
 from rusteeze_b200.core.errors import InvalidRequestError, RusteezeError
 from rusteeze_b200.core.sampling_params import SamplingParams
@@ -93,6 +93,7 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                            allow_methods=sc.cors.allowed_methods, allow_headers=sc.cors.allowed_headers,
                            max_age=sc.cors.max_age)
     app.add_middleware(RequestIdMiddleware, log_requests=cfg.logging.request_logging)
+    app.add_middleware(BodyLimitMiddleware, max_bytes=sc.max_body_bytes)
 
     @app.exception_handler(RusteezeError)
     async def _err(_request: Request, exc: RusteezeError):

@@ -42,6 +42,12 @@ class ContextLengthExceededError(InvalidRequestError):
     code = "context_length_exceeded"
 
 
+class PayloadTooLargeError(RusteezeError):
+    http_status = 413
+    error_type = "invalid_request_error"
+    code = "payload_too_large"
+
+
 class AuthenticationError(RusteezeError):
     http_status = 401
     error_type = "authentication_error"

@@ -133,3 +133,30 @@ def test_request_chat_templates_need_the_operator_s_consent():
                 assert r.status_code == 400, (bad, r.status_code, r.text)
         finally:
             ae.shutdown()
+
+
+def test_request_bodies_above_the_limit_get_413():
+    cfg = _cfg()
+    cfg.server.max_body_bytes = 4096
+    ae = AsyncLLMEngine(LLMEngine(cfg)).start()
+    c = TestClient(create_app(ae, cfg), raise_server_exceptions=False)
+    try:
+        ok = {"prompt": "small", "max_tokens": 1}
+        assert c.post("/v1/completions", json=ok).status_code == 200
+        big = {"prompt": "x" * 10000, "max_tokens": 1}
+        r = c.post("/v1/completions", json=big)                    # Content-Length over the limit
+        assert r.status_code == 413 and r.json()["error"]["code"] == "payload_too_large"
+        data = json.dumps(big).encode()
+
+        def chunks():                                              # no Content-Length: counted
+            for i in range(0, len(data), 1000):
+                yield data[i:i + 1000]
+        r = c.post("/v1/completions", content=chunks(), headers={"content-type": "application/json"})
+        assert r.status_code == 413
+        small = json.dumps(ok).encode()
+        r = c.post("/v1/completions", content=iter([small[:5], small[5:]]),
+                   headers={"content-type": "application/json"})
+        assert r.status_code == 200
+        assert ae.is_ready
+    finally:
+        ae.shutdown()
