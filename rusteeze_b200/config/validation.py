@@ -77,6 +77,22 @@ def collect_errors(cfg) -> List[str]:
         e.append("engine.comm_backend must be nccl|fused")
     if g.speculative is not None and not 1 <= g.speculative.num_speculative_tokens <= 16:
         e.append("engine.speculative.num_speculative_tokens must be in [1, 16]")
+    # fields kept for config-file parity whose non-default values this engine does not
+    # implement: refused instead of silently ignored
+    if m.expert_parallel_size not in (1, m.tensor_parallel_size):
+        e.append("model.expert_parallel_size must be 1 or equal tensor_parallel_size (experts are split over "
+                 "the tensor-parallel ranks)")
+    if m.quantization is not None and m.quantization.group_size != 128:
+        e.append(f"model.quantization.group_size must be 128 (the FP8 GEMM's block), got {m.quantization.group_size}")
+    if g.kv_cache_dtype not in ("auto", m.dtype):
+        e.append(f"engine.kv_cache_dtype must be auto (the model dtype), got {g.kv_cache_dtype!r}")
+    if not g.scheduling.enable_preemption:
+        e.append("engine.scheduling.enable_preemption: false is not supported (a full KV cache preempts by "
+                 "engine.scheduling.preemption_mode)")
+    if g.scheduling.delay_factor != 0.0:
+        e.append("engine.scheduling.delay_factor must be 0 (prompts are scheduled as soon as blocks allow)")
+    if s.rate_limit is not None and s.rate_limit.enabled and s.rate_limit.tokens_per_minute is not None:
+        e.append("server.rate_limit.tokens_per_minute is not supported (limits count requests)")
     if cfg.logging.level.lower() not in ("trace", "debug", "info", "warn", "warning", "error"):
         e.append(f"logging.level invalid: {cfg.logging.level!r}")
     if cfg.logging.format not in ("pretty", "compact", "json"):

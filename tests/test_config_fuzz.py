@@ -82,3 +82,19 @@ def test_numbers_written_as_strings_are_accepted(tmp_path):
     cfg = ConfigLoader(str(p)).load({})
     assert cfg.server.port == 9001 and cfg.server.api_key == "12345"
     assert cfg.engine.gpu_memory_utilization == 0.5 and cfg.model.max_model_len == 1000
+
+
+@pytest.mark.parametrize("text,needle", [
+    ("model:\n  expert_parallel_size: 2\n", "expert_parallel_size"),
+    ("model:\n  quantization: {method: fp8_block, group_size: 64}\n", "group_size"),
+    ("engine:\n  kv_cache_dtype: fp8\n", "kv_cache_dtype"),
+    ("engine:\n  scheduling: {enable_preemption: false}\n", "enable_preemption"),
+    ("engine:\n  scheduling: {delay_factor: 0.5}\n", "delay_factor"),
+    ("server:\n  rate_limit: {enabled: true, tokens_per_minute: 1000}\n", "tokens_per_minute"),
+])
+def test_settings_this_engine_does_not_implement_are_refused(tmp_path, text, needle):
+    p = tmp_path / "c.yaml"
+    p.write_text(text)
+    with pytest.raises(ConfigError) as ei:
+        ConfigLoader(str(p)).load({})
+    assert needle in str(ei.value)
