@@ -13,19 +13,27 @@ architecture; no network for checkpoints or datasets):
     (1024 requests per GPU), served with continuous batching, paged KV
     (block 16), chunked prefill, max 256 running sequences.
 
-One engine replica per GPU (data parallel: every rank serves the same seeded
-synthetic request stream as the 1-GPU run, so per-GPU work is identical at
-every N: weak scaling, and the MAX over ranks is not a max over different
-prefill/decode mixes).  Per rank:
-  1. ramp: engine steps until the running batch is full (untimed)
+N GPUs (torchrun, one rank per GPU) run ONE tensor-parallel engine over all of
+them (`--parallel tp`, the default at N > 1): rank 0 schedules and samples,
+every rank runs the forward on its weight shard, and the layer boundaries are
+the fused GEMM + reduce-scatter / add + RMSNorm + all-gather kernels over
+NVLink (`--comm fused`; `--comm nccl` is the NCCL baseline).  Scaling is weak
+by default: the engine serves N x 1024 requests at N x the arrival rate with
+N x 256 running sequences and N x the prefill budget, so every GPU carries the
+1-GPU run's per-GPU load (`--scaling strong` keeps the 1-GPU workload).
+`--parallel dp` runs one independent replica per GPU instead.
+  1. ramp: engine steps until the running batch is full and half a batch of
+     requests has finished (untimed)
   2. W warm-up engine steps (untimed)
   3. K timed engine steps, bracketed by a barrier + cuda synchronize and
-     timed with CUDA events on the engine's stream; MAX over ranks.
-  value = output tokens produced in the K steps summed over ranks / max time.
+     timed with CUDA events on the engine's stream on every rank; MAX over ranks.
+  value = output tokens produced in the K steps / max time over ranks.
   e2e: a separate run through the public `LLMEngine` API (add_request /
-     step) that serves a fresh 512-request set from submission to the last
-     token; every step copies its inputs from pinned host memory and reads
-     the sampled tokens back.
+     step) that serves a fresh request stream of the same shape (same count,
+     lengths and Poisson arrival rate; each request is submitted when its
+     arrival time has passed) from the first submission to the last token;
+     every step copies its inputs from pinned host memory and reads the
+     sampled tokens back.
 The inputs (weights + KV working set) are far larger than the 126 MB L2, so
 no L2 flush is needed between steps.
 
@@ -44,6 +52,9 @@ import threading
 import time
 
 REFERENCE_PUBLISHED_TOK_S = 32000.0   # the reference README's output tok/s at batch 256 (A100, Llama-2-7B)
+REFERENCE_PUBLISHED_BASIS = ("reference README claim: 32,000 output tok/s, Llama-2-7B static batch 256 on one "
+                             "A100 80GB (README.md:88); a different model, workload and GPU, and not reproducible "
+                             "by the reference's own code")
 
 
 def reference_unavailable() -> str:
@@ -222,14 +233,19 @@ def main():
     ap.add_argument("--rate", type=float, default=200.0, help="Poisson arrival rate per GPU (req/s)")
     ap.add_argument("--max-seqs", type=int, default=256)
     ap.add_argument("--max-batched-tokens", type=int, default=4096)
-    ap.add_argument("--e2e-requests", type=int, default=512)
+    ap.add_argument("--e2e-requests", type=int, default=None,
+                    help="requests of the end-to-end run (default: --requests, scaled like it)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--dtype", default="fp8", choices=["fp8", "bf16"],
                     help="fp8: block-scaled e4m3 weights (the Llama-3-8B serving configuration); bf16: unquantised")
     ap.add_argument("--fp8", action="store_true", help="same as --dtype fp8 (the default)")
     ap.add_argument("--eager", action="store_true", help="disable CUDA graphs (profiling runs)")
-    ap.add_argument("--parallel", default="dp", choices=["dp", "tp"],
-                    help="dp: one engine replica per GPU (default); tp: one tensor-parallel engine over all GPUs")
+    ap.add_argument("--parallel", default=None, choices=["dp", "tp"],
+                    help="tp: one tensor-parallel engine over all GPUs (default with N > 1); dp: one engine "
+                         "replica per GPU")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="tp: weak = requests, arrival rate, running sequences and prefill budget x N "
+                         "(per-GPU load of the 1-GPU run); strong = the 1-GPU workload on N GPUs")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="tensor-parallel collectives: fused peer-memory kernels or the NCCL baseline")
     ap.add_argument("--workload", default="poisson", choices=["poisson", "static", "shared-prefix"],
@@ -266,6 +282,10 @@ def main():
     cuda = args.device == "cuda"
     if cuda:
         torch.cuda.set_device(local)
+    if args.parallel is None:
+        args.parallel = "tp" if world > 1 else "dp"
+    if args.e2e_requests is None:
+        args.e2e_requests = args.requests
     if world > 1 and args.parallel == "tp":
         return serve_tp(args, world, rank)
     if world > 1:
@@ -299,6 +319,14 @@ def serve_tp(args, world, rank):
     from rusteeze_b200.parallel.executor import worker_loop
     from rusteeze_b200.parallel.launcher import tp_rank_setup
     info = init_distributed(timeout_s=600, device_type=args.device)
+    if args.scaling == "weak":
+        # every GPU carries the 1-GPU run's load: N x the requests, arrival rate, running
+        # sequences and prefill budget on the one N-GPU engine
+        args.requests *= world
+        args.e2e_requests *= world
+        args.rate *= world
+        args.max_seqs *= world
+        args.max_batched_tokens *= world
     cfg = make_config(args, str(info.device))
     cfg.model.tensor_parallel_size = world
     cfg.engine.comm_backend = args.comm
@@ -315,10 +343,11 @@ def serve_tp(args, world, rank):
                          tp_timer=eng.runner.timer)
         finally:
             eng.runner.shutdown()
-        line.update(n_gpus=world, scaling="strong", gpu_launches_scope="rank 0")
+        line.update(n_gpus=world, scaling=args.scaling, gpu_launches_scope="rank 0")
         line["config"]["parallelism"] = f"tp{world} ({args.comm} collectives)"
         line["config"]["global_batch"] = args.max_seqs
-        line["config"]["workload"] = line["config"]["workload"].replace("req/GPU", "req")
+        line["config"]["workload"] = line["config"]["workload"].replace("req/GPU", "req").replace(
+            "/s,", "/s in total,")
         print(json.dumps(line), flush=True)
         return 0
     finally:
@@ -438,19 +467,28 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
         # drain the steady-state run so the e2e run starts from an empty engine
         for rid in list(eng.requests):
             eng.abort_request(rid)
-        e_prompts, e_olens, _ = build_workload(args.e2e_requests, 5000, V, 1.0, plen, olen)
+        e_prompts, e_olens, e_arr = build_workload(args.e2e_requests, 5000, V, args.rate, plen, olen)
         h2d0, d2h0, steps0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes, eng.stats_counters["steps"]
         gen_e0 = eng.stats_counters["generation_tokens"]
         if world > 1:
             dist.barrier()
         dev.sync()
         w0 = time.perf_counter()
-        for p, o in zip(e_prompts, e_olens):
-            pin = dev.pinned(p)                                        # prompts arrive in pinned host memory
-            eng.add_request(None, None, SamplingParams(temperature=0.7, top_p=0.9, max_tokens=int(o),
-                                                       ignore_eos=True), pin.tolist())
-        while eng.has_unfinished_requests():
-            eng.step()
+        e_next = 0
+        e_ttft = []
+        while e_next < len(e_prompts) or eng.has_unfinished_requests():
+            now = time.perf_counter() - w0
+            while e_next < len(e_prompts) and e_arr[e_next] <= now:   # Poisson arrivals, as in config 3
+                eng.add_request(None, None, SamplingParams(temperature=0.7, top_p=0.9,
+                                                           max_tokens=int(e_olens[e_next]), ignore_eos=True),
+                                e_prompts[e_next])
+                e_next += 1
+            if not eng.has_unfinished_requests():
+                time.sleep(max(0.0, min(0.05, e_arr[e_next] - now)))
+                continue
+            for out in eng.step():
+                if out.finished and out.metrics is not None and out.metrics.ttft is not None:
+                    e_ttft.append(out.metrics.ttft)
         dev.sync()
         w1 = time.perf_counter()
         if world > 1:
@@ -469,7 +507,11 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
         e2e = {"value": e_gen / e_s, "unit": "output_tokens/s",
                "h2d_bytes_per_step": int((eng.runner.h2d_bytes - h2d0) / esteps),
                "d2h_bytes_per_step": int((eng.runner.d2h_bytes - d2h0) / esteps),
-               "requests": args.e2e_requests * world, "wall_s": round(e_s, 3)}
+               "requests": args.e2e_requests * world, "wall_s": round(e_s, 3),
+               "workload": f"{args.e2e_requests} requests per engine, Poisson {args.rate}/s arrivals, same "
+                           "length ranges and sampling as the timed run, submitted through LLMEngine.add_request "
+                           "as they arrive; wall clock from the first submission to the last token",
+               "ttft_p50_s": round(statistics.median(e_ttft), 4) if e_ttft else None}
 
     line = {
         "metric": "output_tokens_per_s",
@@ -482,6 +524,7 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": round(value / REFERENCE_PUBLISHED_TOK_S, 4),
+        "vs_baseline_basis": REFERENCE_PUBLISHED_BASIS,
         "dtype": ("fp8_e4m3 weights (128x128 UE8M0 block scales), 1x128 UE8M0 activation scales, "
                   "bf16 activations/KV, fp32 accumulate") if args.dtype == "fp8" else "bf16",
         "data": "synthetic requests, random-init N(0,0.02) weights",

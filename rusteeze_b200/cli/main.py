@@ -26,25 +26,31 @@ BANNER = f"rusteeze_b200 {__version__} -- Blackwell (sm_100a) LLM inference engi
 
 
 def _model_args(p: argparse.ArgumentParser, required: bool = True) -> None:
-    p.add_argument("-m", "--model", default=os.environ.get("RUSTEEZE_MODEL"), required=required and
-                   not os.environ.get("RUSTEEZE_MODEL"),
+    # Every default is None: an option the user did not give leaves the config file's (or the
+    # environment's) value in place, so precedence stays defaults < file < env < CLI.  The model
+    # may come from -m, RUSTEEZE_MODEL or model.path / model.preset in the config file; commands
+    # that need one check after the config is loaded.
+    p.add_argument("-m", "--model", default=None,
                    help="HF-layout model directory or a random-init preset name")
-    p.add_argument("--device", default="auto")
-    p.add_argument("--dtype", default="auto")
-    p.add_argument("--tensor-parallel-size", type=int, default=1)
-    p.add_argument("--data-parallel-size", type=int, default=1,
+    p.add_argument("--device", default=None)
+    p.add_argument("--dtype", default=None)
+    p.add_argument("--tensor-parallel-size", type=int, default=None)
+    p.add_argument("--data-parallel-size", type=int, default=None,
                    help="serve: D engine replicas (one GPU each) behind a request router")
-    p.add_argument("--router-policy", default="least_loaded", choices=["least_loaded", "round_robin", "random"])
+    p.add_argument("--router-policy", default=None, choices=["least_loaded", "round_robin", "random"])
     p.add_argument("--max-model-len", type=int, default=None)
-    p.add_argument("--gpu-memory-utilization", type=float, default=0.9)
+    p.add_argument("--gpu-memory-utilization", type=float, default=None)
     p.add_argument("--quantization", default=None, choices=[None, "fp8_block", "fp8"])
-    p.add_argument("--enforce-eager", action="store_true")
-    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--enforce-eager", action="store_true", default=None)
+    p.add_argument("--seed", type=int, default=None)
+    p.set_defaults(model_required=required)
 
 
 def _overrides(a) -> dict:
     model = {"device": a.device, "dtype": a.dtype, "tensor_parallel_size": a.tensor_parallel_size,
              "data_parallel_size": a.data_parallel_size, "max_model_len": a.max_model_len, "seed": a.seed}
+    if a.model is None and os.environ.get("RUSTEEZE_MODEL"):
+        a.model = os.environ["RUSTEEZE_MODEL"]       # a directory or a preset name
     if a.model:
         if os.path.isdir(a.model):
             model["path"] = a.model
@@ -62,7 +68,11 @@ def _load_config(a, extra: Optional[dict] = None):
     ov = _overrides(a) if hasattr(a, "device") else {}
     if extra:
         ov = merge_dict(ov, extra)
-    return ConfigLoader(a.config).load(ov)
+    cfg = ConfigLoader(a.config).load(ov)
+    if getattr(a, "model_required", False) and not (cfg.model.path or cfg.model.preset):
+        raise SystemExit("rusteeze: a model is required: -m/--model, RUSTEEZE_MODEL, or model.path / "
+                         "model.preset in the config file")
+    return cfg
 
 
 def _engine(cfg):
@@ -77,7 +87,7 @@ def _engine(cfg):
 def cmd_serve(a) -> int:
     from rusteeze_b200.api.server import serve
     extra = {"server": {"host": a.host, "port": a.port, "api_key": a.api_key, "metrics_port": a.metrics_port,
-                        "cors": {"enabled": bool(a.cors)},
+                        "cors": {"enabled": True} if a.cors else None,
                         "trust_request_chat_template": a.trust_request_chat_template or None},
              "engine": {"max_num_seqs": a.max_num_seqs, "block_size": a.block_size, "swap_space_gb": a.swap_space,
                         "enable_prefix_caching": a.enable_prefix_caching,
@@ -325,16 +335,16 @@ def build_parser() -> argparse.ArgumentParser:
 
     s = sub.add_parser("serve", help="start the OpenAI-compatible server")
     _model_args(s)
-    s.add_argument("--host", default=os.environ.get("RUSTEEZE_HOST", "0.0.0.0"))
-    s.add_argument("-p", "--port", type=int, default=int(os.environ.get("RUSTEEZE_PORT", "8000")))
-    s.add_argument("--api-key", default=os.environ.get("RUSTEEZE_API_KEY"))
-    s.add_argument("--max-num-seqs", type=int, default=256)
-    s.add_argument("--max-num-batched-tokens", type=int, default=8192)
-    s.add_argument("--enable-prefix-caching", action="store_true")
-    s.add_argument("--enable-chunked-prefill", action="store_true")
-    s.add_argument("--block-size", type=int, default=16)
-    s.add_argument("--swap-space", type=float, default=4.0)
-    s.add_argument("--cors", action="store_true")
+    s.add_argument("--host", default=None)
+    s.add_argument("-p", "--port", type=int, default=None)
+    s.add_argument("--api-key", default=None)
+    s.add_argument("--max-num-seqs", type=int, default=None)
+    s.add_argument("--max-num-batched-tokens", type=int, default=None)
+    s.add_argument("--enable-prefix-caching", action="store_true", default=None)
+    s.add_argument("--enable-chunked-prefill", action="store_true", default=None)
+    s.add_argument("--block-size", type=int, default=None)
+    s.add_argument("--swap-space", type=float, default=None)
+    s.add_argument("--cors", action="store_true", default=None)
     s.add_argument("--metrics-port", type=int, default=None)
     s.add_argument("--chat-template", default=None)
     s.add_argument("--trust-request-chat-template", action="store_true",

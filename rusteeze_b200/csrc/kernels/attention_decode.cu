@@ -276,11 +276,7 @@ __global__ void decode_combine_kernel(DecodeAttnParams p) {
 template <int D>
 static int launch_dec(const DecodeAttnParams& p, cudaStream_t st) {
   using C = DecCfg<D>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(decode_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    attr = true;
-  }
+  opt_in_smem<decode_attn_kernel<D>>(C::kSmem);
   const int items = p.num_seqs * p.num_kv_heads * p.num_splits;
   decode_attn_kernel<D><<<(items + C::kWarps - 1) / C::kWarps, C::kWarps * 32, C::kSmem, st>>>(p);
   if (p.num_splits > 1) decode_combine_kernel<D><<<dim3(p.num_q_heads, p.num_seqs), 128, 0, st>>>(p);

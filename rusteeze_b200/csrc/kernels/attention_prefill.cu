@@ -245,11 +245,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnParams p) 
 template <int D>
 static int launch_prefill(const PrefillAttnParams& p, cudaStream_t st) {
   constexpr int smem = kPBQ * D * 2 + 4 * kPBKV * D * 2;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(prefill_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  opt_in_smem<prefill_attn_kernel<D>>(smem);
   dim3 grid((p.max_q_len + kPBQ - 1) / kPBQ, p.num_q_heads, p.num_seqs);
   prefill_attn_kernel<D><<<grid, 128, smem, st>>>(p);
   return static_cast<int>(cudaGetLastError());

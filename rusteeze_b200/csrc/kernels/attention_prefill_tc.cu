@@ -382,11 +382,7 @@ int prefill_tc_launch(const PrefillAttnParams& p, cudaStream_t st) {
   dim3 grid(p.num_seqs * a.tiles_per_seq, p.num_kv_heads);
 #define RZ_PF(SC, WIN)                                                                                    \
   {                                                                                                       \
-    static bool attr = false;                                                                             \
-    if (!attr) {                                                                                          \
-      cudaFuncSetAttribute(prefill_tc_kernel<SC, WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem); \
-      attr = true;                                                                                        \
-    }                                                                                                     \
+    opt_in_smem<prefill_tc_kernel<SC, WIN>>(kPfSmem);                                                     \
     prefill_tc_kernel<SC, WIN><<<grid, kPfThreads, kPfSmem, st>>>(tk, tv, a);                             \
   }
   const bool sc = p.softcap > 0.f, win = p.window > 0;

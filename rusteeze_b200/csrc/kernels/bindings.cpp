@@ -2,6 +2,8 @@
 // launches on the current CUDA stream, and raises on a launch error.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+
+#include <mutex>
 #include <torch/extension.h>
 
 #include "attention.h"
@@ -26,8 +28,12 @@ inline void check_rc(int rc, const char* what) {
 }
 
 // One status word per device for the bounded device-side waits.
+// Created on first use under a lock: replicas on several host threads may make their
+// first launches at the same time.
 torch::Tensor& status_tensor(int dev) {
   static torch::Tensor t[64];
+  static std::mutex init;
+  std::lock_guard<std::mutex> g(init);
   if (!t[dev].defined())
     t[dev] = torch::zeros({4}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, dev));
   return t[dev];
@@ -39,6 +45,7 @@ int* status_ptr() {
 }
 
 void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps, double offset) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w);
   TORCH_CHECK(x.is_contiguous() && out.is_contiguous(), "rms_norm: contiguous tensors required");
   const int H = x.size(-1);
@@ -52,6 +59,7 @@ void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps, d
 
 void fused_add_rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor residual, torch::Tensor w, double eps,
                         double offset) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(residual); CHECK_BF16(w);
   TORCH_CHECK(x.is_contiguous() && residual.is_contiguous() && out.is_contiguous(), "contiguous tensors required");
   const int H = x.size(-1);
@@ -66,6 +74,7 @@ void fused_add_rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor residu
 
 void rope_and_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin, torch::Tensor k_cache,
                     torch::Tensor v_cache, torch::Tensor slots, int64_t Hq, int64_t Hkv, int64_t D) {
+  const at::cuda::CUDAGuard rz_guard(qkv.device());
   CHECK_CUDA(qkv); CHECK_BF16(qkv); CHECK_LAST(qkv);
   TORCH_CHECK(positions.scalar_type() == at::kLong && slots.scalar_type() == at::kLong, "int64 positions/slots");
   TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "fp32 contiguous cos_sin");
@@ -80,6 +89,7 @@ void rope_and_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor co
 }
 
 void act_mul(torch::Tensor out, torch::Tensor x, int64_t kind) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(x); CHECK_BF16(x);
   TORCH_CHECK(x.is_contiguous() && out.is_contiguous(), "contiguous tensors required");
   check_rc(rz::act_mul_launch(reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
@@ -91,6 +101,7 @@ void act_mul(torch::Tensor out, torch::Tensor x, int64_t kind) {
 void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                       torch::Tensor seq_lens, torch::Tensor block_tables, c10::optional<torch::Tensor> workspace,
                       int64_t num_seqs, double scale, int64_t window, double softcap, int64_t num_splits) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(q); CHECK_BF16(q);
   rz::DecodeAttnParams p{};
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
@@ -127,6 +138,7 @@ void prefill_attention_impl(torch::Tensor out, torch::Tensor q, torch::Tensor k_
                             torch::Tensor qsl, torch::Tensor seq_lens, torch::Tensor block_tables, int64_t seq_offset,
                             int64_t num_seqs, int64_t max_q_len, double scale, int64_t window, double softcap,
                             int64_t impl) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(q); CHECK_BF16(q);
   rz::PrefillAttnParams p{};
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
@@ -162,6 +174,7 @@ void prefill_attention_impl(torch::Tensor out, torch::Tensor q, torch::Tensor k_
 void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                        torch::Tensor qsl, torch::Tensor seq_lens, torch::Tensor block_tables, int64_t seq_offset,
                        int64_t num_seqs, int64_t max_q_len, double scale, int64_t window, double softcap) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   prefill_attention_impl(out, q, k_cache, v_cache, qsl, seq_lens, block_tables, seq_offset, num_seqs, max_q_len,
                          scale, window, softcap, 0);
 }
@@ -191,6 +204,7 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi) {
 // Returns the number of kernels launched (1, or 2 with a split-K reduction).
 int64_t gemm_bf16_ex(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                      c10::optional<torch::Tensor> residual, int64_t epi, int64_t bn, int64_t k_splits) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_LAST(x); CHECK_LAST(w);
   const int M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K, "gemm: K mismatch");
@@ -227,11 +241,13 @@ int64_t gemm_bf16_ex(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::o
 
 int64_t gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                   c10::optional<torch::Tensor> residual) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   return gemm_bf16_ex(out, x, w, bias, residual, 0, 0, 0);
 }
 
 // ---------------------------------------------------------------- FP8
 void quant_fp8_act(torch::Tensor xq, torch::Tensor xs, torch::Tensor x) {
+  const at::cuda::CUDAGuard rz_guard(xq.device());
   CHECK_CUDA(x); CHECK_BF16(x);
   TORCH_CHECK(x.size(1) % 128 == 0, "K must be a multiple of 128");
   check_rc(rz::quant_fp8_act_launch(xq.data_ptr(), xs.data_ptr<float>(),
@@ -244,6 +260,7 @@ void quant_fp8_act(torch::Tensor xq, torch::Tensor xs, torch::Tensor x) {
 int64_t gemm_fp8_block(torch::Tensor out, torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws,
                        c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual, int64_t epi,
                        int64_t k_splits) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
   TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "fp8 gemm: K and N must be multiples of 128");
   TORCH_CHECK(wq.size(1) == K, "fp8 gemm: K mismatch");
@@ -277,6 +294,7 @@ int64_t gemm_fp8_block(torch::Tensor out, torch::Tensor xq, torch::Tensor xs, to
 
 // ---------------------------------------------------------------- MXFP8 (UE8M0 block scales)
 void quant_mxf8_act(torch::Tensor xq, torch::Tensor sfa, torch::Tensor x) {
+  const at::cuda::CUDAGuard rz_guard(xq.device());
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_LAST(x);
   const int M = x.size(0), K = x.size(1);
   TORCH_CHECK(K % 128 == 0, "K must be a multiple of 128");
@@ -291,6 +309,7 @@ void quant_mxf8_act(torch::Tensor xq, torch::Tensor sfa, torch::Tensor x) {
 
 void rms_norm_mxf8(torch::Tensor xq, torch::Tensor sfa, torch::Tensor x, c10::optional<torch::Tensor> residual,
                    torch::Tensor w, double eps, double offset) {
+  const at::cuda::CUDAGuard rz_guard(xq.device());
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w);
   TORCH_CHECK(x.is_contiguous() && xq.is_contiguous() && sfa.is_contiguous(), "rms_norm_mxf8: contiguous tensors");
   const int M = x.size(0), H = x.size(1);
@@ -312,6 +331,7 @@ void rms_norm_mxf8(torch::Tensor xq, torch::Tensor sfa, torch::Tensor x, c10::op
 int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch::Tensor wq, torch::Tensor sfb,
                   c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual, int64_t epi, int64_t bn,
                   int64_t k_splits) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(xq);
   const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
   TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "mxf8 gemm: K and N must be multiples of 128");
@@ -352,6 +372,7 @@ int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch:
 // gate/up MXFP8 GEMM whose SiLU(gate)*up epilogue writes the down projection's MXFP8 operand.
 int64_t gemm_mxf8_silu_q(torch::Tensor q_out, torch::Tensor sf_out, torch::Tensor xq, torch::Tensor sfa,
                          torch::Tensor wq, torch::Tensor sfb, c10::optional<torch::Tensor> bias) {
+  const at::cuda::CUDAGuard rz_guard(q_out.device());
   CHECK_CUDA(xq);
   const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
   TORCH_CHECK(K % 128 == 0 && N % 256 == 0 && wq.size(1) == K, "mxf8 silu_q: K % 128, N % 256");
@@ -383,6 +404,7 @@ std::vector<int64_t> gemm_plan_mxf8(int64_t M, int64_t N, int64_t K, int64_t epi
 // Grouped GEMM over 128-aligned expert segments: x [rows, K], w [G, N, K] -> out [rows, N or N/2].
 int64_t gemm_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor grp_off,
                      torch::Tensor grp_end, int64_t epi, int64_t bn) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w);
   TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "grouped gemm: contiguous tensors");
   TORCH_CHECK(w.dim() == 3 && w.size(2) == x.size(1), "grouped gemm: w [G, N, K]");
@@ -416,6 +438,7 @@ struct MoeExpertOut {
 };
 MoeExpertOut moe_experts(torch::Tensor h, torch::Tensor wr, torch::Tensor w13, torch::Tensor w2, int64_t topk,
                          int64_t e_lo, bool renormalize) {
+  const at::cuda::CUDAGuard rz_guard(h.device());
   CHECK_CUDA(h); CHECK_BF16(h); CHECK_BF16(wr); CHECK_BF16(w13); CHECK_BF16(w2); CHECK_LAST(h);
   const int M = h.size(0), H = h.size(1), E = wr.size(0), ne = w13.size(0), I = w13.size(1) / 2;
   TORCH_CHECK(wr.size(1) == H && w13.size(2) == H && w2.size(0) == ne && w2.size(1) == H && w2.size(2) == I,
@@ -453,6 +476,7 @@ MoeExpertOut moe_experts(torch::Tensor h, torch::Tensor wr, torch::Tensor w13, t
 // Returns the number of kernels launched.
 int64_t moe_forward(torch::Tensor out, torch::Tensor h, torch::Tensor wr, torch::Tensor w13, torch::Tensor w2,
                     int64_t topk, int64_t e_lo, bool renormalize, c10::optional<torch::Tensor> residual) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   const int M = h.size(0), H = h.size(1);
   TORCH_CHECK(out.is_contiguous() && out.size(0) == M && out.size(1) == H, "moe: out [M, H]");
   auto e = moe_experts(h, wr, w13, w2, topk, e_lo, renormalize);
@@ -476,6 +500,7 @@ void set_comm_jitter_ns(int64_t ns) { g_comm_jitter_ns = static_cast<uint32_t>(n
 int64_t moe_forward_peer(torch::Tensor h, torch::Tensor wr, torch::Tensor w13, torch::Tensor w2, int64_t topk,
                          int64_t e_lo, bool renormalize, std::vector<int64_t> slots, std::vector<int64_t> flags,
                          int64_t rs_rows, torch::Tensor epoch, int64_t call_idx) {
+  const at::cuda::CUDAGuard rz_guard(h.device());
   const int M = h.size(0), H = h.size(1);
   const int world = static_cast<int>(slots.size());
   TORCH_CHECK(world >= 1 && world <= rz::kMaxTpRanks && flags.size() == slots.size() && topk <= world &&
@@ -498,6 +523,7 @@ int64_t moe_forward_peer(torch::Tensor h, torch::Tensor wr, torch::Tensor w13, t
 }
 
 void ag_wait(torch::Tensor ag_flag, int64_t M, torch::Tensor epoch, int64_t call_idx) {
+  const at::cuda::CUDAGuard rz_guard(ag_flag.device());
   check_rc(rz::ag_wait_launch(reinterpret_cast<const uint32_t*>(ag_flag.data_ptr()), M,
                               reinterpret_cast<const uint32_t*>(epoch.data_ptr()), static_cast<uint32_t>(call_idx),
                               status_ptr(), cur_stream()),
@@ -507,6 +533,7 @@ void ag_wait(torch::Tensor ag_flag, int64_t M, torch::Tensor epoch, int64_t call
 // Routing only (tests): fills topk weights / ids and the local expert counts.
 void moe_route(torch::Tensor tw, torch::Tensor tid, torch::Tensor counts, torch::Tensor h, torch::Tensor wr,
                int64_t topk, int64_t e_lo, int64_t ne, bool renormalize) {
+  const at::cuda::CUDAGuard rz_guard(tw.device());
   CHECK_CUDA(h); CHECK_BF16(h); CHECK_BF16(wr);
   rz::MoeRouteParams rp{};
   rp.h = reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()); rp.ldh = h.stride(0);
@@ -522,6 +549,7 @@ void moe_route(torch::Tensor tw, torch::Tensor tid, torch::Tensor counts, torch:
 // Row-parallel GEMM whose epilogue reduce-scatters into the owners' slot buffers.  Returns n_tiles.
 int64_t gemm_peer_rs(torch::Tensor x, torch::Tensor w, std::vector<int64_t> slots, std::vector<int64_t> flags,
                      int64_t rank, int64_t rs_rows, torch::Tensor epoch, int64_t call_idx, int64_t bn) {
+  const at::cuda::CUDAGuard rz_guard(x.device());
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_LAST(x); CHECK_LAST(w);
   const int M = x.size(0), K = x.size(1), N = w.size(0);
   const int world = static_cast<int>(slots.size());
@@ -552,6 +580,7 @@ int64_t gemm_peer_rs(torch::Tensor x, torch::Tensor w, std::vector<int64_t> slot
 // GEMM whose A rows are all-gathered by peers: waits on the local all-gather flags per A tile.
 int64_t gemm_ag(torch::Tensor out, torch::Tensor g, torch::Tensor w, c10::optional<torch::Tensor> bias, int64_t epi,
                 torch::Tensor ag_flag, torch::Tensor epoch, int64_t call_idx) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(g); CHECK_BF16(g); CHECK_BF16(w); CHECK_LAST(g); CHECK_LAST(w);
   const int M = g.size(0), K = g.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && K % 8 == 0 && N % 8 == 0, "gemm_ag: shapes");
@@ -584,6 +613,7 @@ int64_t gemm_ag(torch::Tensor out, torch::Tensor g, torch::Tensor w, c10::option
 int64_t gemm_peer_rs_mx(torch::Tensor xq, torch::Tensor sfa, torch::Tensor wq, torch::Tensor wsf,
                         std::vector<int64_t> slots, std::vector<int64_t> flags, int64_t rank, int64_t rs_rows,
                         torch::Tensor epoch, int64_t call_idx) {
+  const at::cuda::CUDAGuard rz_guard(xq.device());
   CHECK_CUDA(xq);
   const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
   const int world = static_cast<int>(slots.size());
@@ -620,6 +650,7 @@ int64_t gemm_peer_rs_mx(torch::Tensor xq, torch::Tensor sfa, torch::Tensor wq, t
 int64_t gemm_mxf8_ag(torch::Tensor out, c10::optional<torch::Tensor> sf_out, torch::Tensor gq, torch::Tensor gsf,
                      torch::Tensor wq, torch::Tensor wsf, c10::optional<torch::Tensor> bias, torch::Tensor ag_flag,
                      torch::Tensor epoch, int64_t call_idx) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(gq);
   const int M = gq.size(0), K = gq.size(1), N = wq.size(0);
   const bool silu_q = sf_out.has_value();
@@ -668,6 +699,7 @@ void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10
                 int64_t call_idx, int64_t moe_topk, c10::optional<torch::Tensor> moe_flag,
                 std::vector<int64_t> gathers_q, std::vector<int64_t> gathers_sf,
                 c10::optional<torch::Tensor> ag_cnt) {
+  const at::cuda::CUDAGuard rz_guard(slots.device());
   CHECK_BF16(residual); CHECK_BF16(w);
   const int world = static_cast<int>(gathers.size());
   TORCH_CHECK(world >= 1 && world <= rz::kMaxTpRanks && ag_flags.size() == gathers.size(), "rs_norm_ag: ranks");
@@ -708,11 +740,13 @@ void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10
 }
 
 void tp_epoch_bump(torch::Tensor epoch) {
+  const at::cuda::CUDAGuard rz_guard(epoch.device());
   check_rc(rz::tp_epoch_bump_launch(reinterpret_cast<uint32_t*>(epoch.data_ptr()), cur_stream()), "tp_epoch_bump");
 }
 
 // ---------------------------------------------------------------- sampling
 void argmax_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, bool want_lp) {
+  const at::cuda::CUDAGuard rz_guard(tok.device());
   CHECK_CUDA(logits);
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "fp32 logits");
   check_rc(rz::argmax_sample_launch(logits.data_ptr<float>(), logits.size(0), logits.size(1), logits.stride(0),
@@ -723,6 +757,7 @@ void argmax_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, bo
 void topk_topp_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, torch::Tensor temp,
                       torch::Tensor topk, torch::Tensor topp, torch::Tensor minp, torch::Tensor seeds,
                       torch::Tensor offsets, bool want_lp) {
+  const at::cuda::CUDAGuard rz_guard(tok.device());
   CHECK_CUDA(logits);
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "fp32 logits");
   (void)want_lp;
@@ -737,6 +772,7 @@ void topk_topp_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits,
 void spec_verify(torch::Tensor out_tokens, torch::Tensor n_acc, torch::Tensor target_logits,
                  c10::optional<torch::Tensor> draft_logits, torch::Tensor draft_tokens, torch::Tensor temp,
                  torch::Tensor seeds, torch::Tensor offsets) {
+  const at::cuda::CUDAGuard rz_guard(out_tokens.device());
   const int B = draft_tokens.size(0), k = draft_tokens.size(1);
   const int V = target_logits.size(1);
   TORCH_CHECK(target_logits.size(0) == B * (k + 1), "target logits must have B*(k+1) rows");
@@ -753,6 +789,7 @@ void spec_verify(torch::Tensor out_tokens, torch::Tensor n_acc, torch::Tensor ta
 }
 
 void copy_blocks(torch::Tensor cache, torch::Tensor pairs) {
+  const at::cuda::CUDAGuard rz_guard(cache.device());
   TORCH_CHECK(pairs.scalar_type() == at::kInt && pairs.is_cuda(), "int32 CUDA pairs");
   const int64_t block_bytes = cache.stride(0) * cache.element_size();
   check_rc(rz::copy_blocks_launch(cache.data_ptr(), pairs.data_ptr<int32_t>(), pairs.size(0), block_bytes,

@@ -26,6 +26,7 @@
 // the kernel finishes without blocking (the result is then garbage, and the
 // host reports the engine unhealthy).
 #include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
 #include "comm.h"
@@ -162,6 +163,7 @@ namespace {
 // x (local, bf16, numel n) -> out (local) = sum over ranks.  bufs: symmetric buffer bases (one per rank).
 int64_t peer_all_reduce(torch::Tensor out, torch::Tensor x, std::vector<int64_t> bufs, int64_t rank,
                         int64_t half_bytes, torch::Tensor epoch, torch::Tensor status, bool two_shot) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() && out.is_contiguous(), "contiguous CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16, "bf16 all-reduce");
   const int world = static_cast<int>(bufs.size());

@@ -13,9 +13,27 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #define RZ_DEVICE __device__ __forceinline__
 
 namespace rz {
+
+// Opts kernel `Kernel` in to `bytes` of dynamic shared memory on the current device.
+// The attribute belongs to a device's context, so a process that launches on several
+// GPUs (one engine replica per GPU, each on its own thread) needs it once per device; a
+// bit per device records which have it.  Two threads racing on a device's first launch
+// both set the attribute, which is idempotent.
+template <auto Kernel>
+inline void opt_in_smem(int bytes) {
+  static std::atomic<uint64_t> devices{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (devices.load(std::memory_order_acquire) & bit) return;
+  cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  devices.fetch_or(bit, std::memory_order_acq_rel);
+}
 
 constexpr uint64_t kWaitTimeoutNs = 1000ull * 1000ull * 1000ull;  // 1 s
 

@@ -4,6 +4,9 @@
 #include "attention.h"
 #include "decode_noalloc.h"
 
+#include <atomic>
+#include <mutex>
+
 namespace {
 
 // The scratch array and the status word live in the library image: nothing
@@ -16,25 +19,32 @@ static __device__ int g_noalloc_status;
 constexpr int kMaxDevices = 64;
 
 struct DeviceSymbols {
-  bool ready = false;
+  std::atomic<bool> ready{false};
   float* scratch = nullptr;
   int* status = nullptr;
 };
 
 // One lookup per device, performed by the first call on that device with it current.
+// Host threads making their first call on one device at the same time serialise on the
+// mutex; `ready` is published with release ordering after both addresses are written, so
+// a thread that sees it set (acquire) also sees the addresses.
 int symbols_for_current_device(DeviceSymbols** out) {
   static DeviceSymbols table[kMaxDevices];
+  static std::mutex lookup;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kRzNoAllocSymbolError;
   DeviceSymbols& s = table[dev];
-  if (!s.ready) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return kRzNoAllocSymbolError;
-    s.scratch = static_cast<float*>(p);
-    p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_status) != cudaSuccess || p == nullptr) return kRzNoAllocSymbolError;
-    s.status = static_cast<int*>(p);
-    s.ready = true;
+  if (!s.ready.load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> g(lookup);
+    if (!s.ready.load(std::memory_order_relaxed)) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return kRzNoAllocSymbolError;
+      void* q = nullptr;
+      if (cudaGetSymbolAddress(&q, g_noalloc_status) != cudaSuccess || q == nullptr) return kRzNoAllocSymbolError;
+      s.scratch = static_cast<float*>(p);
+      s.status = static_cast<int*>(q);
+      s.ready.store(true, std::memory_order_release);
+    }
   }
   *out = &s;
   return kRzNoAllocOk;
@@ -92,7 +102,8 @@ extern "C" __attribute__((visibility("default"))) int rz_decode_attention_noallo
     return kRzNoAllocSymbolError;
   if (cudaStreamSynchronize(stream) != cudaSuccess) return kRzNoAllocSymbolError;
   const int zero = 0;
-  cudaMemcpyAsync(sym->status, &zero, sizeof(int), cudaMemcpyHostToDevice, stream);
-  cudaStreamSynchronize(stream);
+  if (cudaMemcpyAsync(sym->status, &zero, sizeof(int), cudaMemcpyHostToDevice, stream) != cudaSuccess)
+    return kRzNoAllocSymbolError;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return kRzNoAllocSymbolError;
   return v;
 }

@@ -33,7 +33,14 @@
 //     rejected with kRzNoAllocTooLarge before anything is launched.
 //   * A bad page id or sequence length found by the kernel's bounds checks is
 //     recorded in a device status word; rz_decode_attention_noalloc_status()
-//     copies it to the host and clears it.
+//     copies it to the host and clears it.  Like the scratch array, the status
+//     word is one per device and shared by every call on it: a code it reports
+//     may come from any call since the last read, including an overlapping one.
+//     If clearing it fails, kRzNoAllocSymbolError is returned instead of the
+//     code, so a stale code is not reported again as new.
+//   * The per-device address lookup is safe to run from several host threads
+//     at once (it is serialised); the calls themselves still race on the GPU
+//     as described above.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>

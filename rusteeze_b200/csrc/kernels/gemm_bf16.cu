@@ -651,12 +651,7 @@ static int launch_inst(const GemmParams& p0, const void* A, int lda, const void*
   const int units = TAIL ? p.full_units + (p.m_tiles * p.n_tiles - p.full_units) * p.tail_split
                          : p.m_tiles * p.n_tiles * p.k_splits;
   const int grid = units < num_sms() ? units : num_sms();
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemm_tcgen05<BN, MX, PEER, TAIL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         C::kSmemBytes);
-    attr_set = true;
-  }
+  opt_in_smem<gemm_tcgen05<BN, MX, PEER, TAIL>>(C::kSmemBytes);
   if (p.ag_flag) {
     // the A rows are guarded by all-gather flags: start while the previous kernel (the
     // add+RMSNorm+all-gather) is still running, as soon as all of its CTAs are resident
@@ -789,12 +784,7 @@ int gemm_grouped_launch(const GemmParams& p_in, const void* A, int lda, int64_t 
 #define RZ_GROUPED(BNV, MXV)                                                                                   \
   {                                                                                                           \
     using C = GemmCfg<BNV, MXV, false>;                                                                       \
-    static bool attr = false;                                                                                 \
-    if (!attr) {                                                                                              \
-      cudaFuncSetAttribute(gemm_tcgen05<BNV, MXV, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                           C::kSmemBytes);                                                                    \
-      attr = true;                                                                                            \
-    }                                                                                                         \
+    opt_in_smem<gemm_tcgen05<BNV, MXV, false, false>>(C::kSmemBytes);                                       \
     gemm_tcgen05<BNV, MXV, false, false><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);               \
   }
   if (!mx && bn == 256) RZ_GROUPED(256, false)

@@ -284,11 +284,7 @@ int gemm_fp8_launch(const Fp8GemmParams& p_in, const void* A, int lda, const voi
   CUtensorMap ta, tb;
   if (make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.M, p.K, lda, kF8BM, kF8BK)) return -2;
   if (make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.N, p.K, ldb, kF8BN, kF8BK)) return -3;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(gemm_fp8_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, kF8Smem);
-    attr = true;
-  }
+  opt_in_smem<gemm_fp8_tcgen05>(kF8Smem);
   const int units = p.m_tiles * p.n_tiles * p.k_splits;
   const int grid = units < num_sms() ? units : num_sms();
   gemm_fp8_tcgen05<<<grid, kF8Threads, kF8Smem, st>>>(ta, tb, p);

@@ -92,10 +92,18 @@ def test_bench_data_parallel_and_tensor_parallel_runs_on_gloo():
     """The multi-rank arms of the harness under torchrun with gloo ranks: data-parallel
     replicas (MAX / SUM over ranks), and one tensor-parallel engine with speculative
     decoding over a shared prefix (rank 0 drives, the worker follows the plan ring)."""
-    r = subprocess.run(_torchrun(2, _free_port(), _POISSON), cwd=ROOT, capture_output=True, text=True, timeout=600)
+    r = subprocess.run(_torchrun(2, _free_port(), _POISSON + ["--parallel", "dp"]), cwd=ROOT, capture_output=True,
+                       text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-3000:]
     (d,) = _json_lines(r.stdout)
     assert d["n_gpus"] == 2 and d["config"]["parallelism"] == "dp2" and d["e2e"]["requests"] == 8
+    # the default at N > 1: one tensor-parallel engine, weak scaling (N x requests and running sequences)
+    r = subprocess.run(_torchrun(2, _free_port(), _POISSON + ["--comm", "nccl"]), cwd=ROOT, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    (d,) = _json_lines(r.stdout)
+    assert d["n_gpus"] == 2 and d["config"]["parallelism"].startswith("tp2") and d["scaling"] == "weak"
+    assert d["config"]["global_batch"] == 8 and d["e2e"]["requests"] == 8 and d["value"] > 0
     tp = _TINY + ["--parallel", "tp", "--comm", "nccl", "--workload", "shared-prefix", "--shared-prefix", "48",
                   "--draft", "self", "--spec-k", "3", "--batches", "4", "--static-prompt", "24",
                   "--static-output", "6"]

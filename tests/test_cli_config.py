@@ -97,3 +97,35 @@ def test_cli_generate_and_benchmark_tiny():
 def test_cli_rejects_pipeline_parallel():
     r = _cli("serve", "-m", "tiny-llama", "--pipeline-parallel-size", "2")
     assert r.returncode == 2 and "pipeline_parallel_size" in r.stderr
+
+
+def test_serve_options_not_given_keep_the_config_file_values(tmp_path, monkeypatch):
+    """`rusteeze -c file serve` with no flags: the file's values stand (argparse defaults used
+    to override them); flags given on the command line still win."""
+    from rusteeze_b200.cli.main import _load_config, build_parser
+    p = tmp_path / "c.yaml"
+    p.write_text("model:\n  preset: tiny-llama\n  tensor_parallel_size: 2\n  dtype: float32\n"
+                 "engine:\n  max_num_seqs: 96\n  max_num_batched_tokens: 2048\n  swap_space_gb: 1.5\n"
+                 "server:\n  port: 9001\n  router_policy: round_robin\n")
+    for k in ("RUSTEEZE_MODEL", "RUSTEEZE_PORT", "RUSTEEZE_MAX_SEQS", "RUSTEEZE_CONFIG"):
+        monkeypatch.delenv(k, raising=False)
+    a = build_parser().parse_args(["-c", str(p), "serve"])
+    cfg = _load_config(a, {"server": {"port": a.port}, "engine": {"max_num_seqs": a.max_num_seqs,
+                                                                   "swap_space_gb": a.swap_space}})
+    assert (cfg.model.tensor_parallel_size, cfg.model.dtype, cfg.engine.max_num_seqs) == (2, "float32", 96)
+    assert (cfg.engine.max_num_batched_tokens, cfg.engine.swap_space_gb, cfg.server.port) == (2048, 1.5, 9001)
+    assert cfg.server.router_policy == "round_robin"
+    a = build_parser().parse_args(["-c", str(p), "serve", "--max-num-seqs", "8", "-p", "9100"])
+    cfg = _load_config(a, {"server": {"port": a.port}, "engine": {"max_num_seqs": a.max_num_seqs}})
+    assert (cfg.engine.max_num_seqs, cfg.server.port, cfg.model.tensor_parallel_size) == (8, 9100, 2)
+
+
+def test_a_model_is_required_from_somewhere(tmp_path, monkeypatch):
+    import pytest
+    from rusteeze_b200.cli.main import _load_config, build_parser
+    for k in ("RUSTEEZE_MODEL", "RUSTEEZE_CONFIG", "RUSTEEZE_MODEL_PATH", "RUSTEEZE_MODEL_PRESET"):
+        monkeypatch.delenv(k, raising=False)
+    with pytest.raises(SystemExit):
+        _load_config(build_parser().parse_args(["serve"]))
+    monkeypatch.setenv("RUSTEEZE_MODEL", "tiny-llama")
+    assert _load_config(build_parser().parse_args(["serve"])).model.preset == "tiny-llama"

@@ -355,6 +355,40 @@ def test_prefill_tcgen05_matches_mma_sync_and_oracle(Hq, Hkv, window, softcap):
     assert int(C().status()[0]) == 0
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs a second GPU")
+def test_kernels_on_a_second_device_after_the_first():
+    """Kernels that opt in to more than 48 KB of shared memory do so per device: one process
+    that launches on cuda:0 and then on cuda:1 (data-parallel replicas on threads) must get
+    correct results on both."""
+    D, Hq, Hkv = 128, 32, 8
+    specs = [(300, 300), (700, 1), (90, 1)]
+    cache, bt, q, qsl, sl = _paged_setup([s for s, _ in specs], [x for _, x in specs], Hq, Hkv, D, seed=31)
+    r_pf = ref.paged_attention(q, cache[:, 0, 0], cache[:, 0, 1], qsl, sl, bt, D ** -0.5)
+    dq, dsl = q[300:], sl[1:]
+    r_dec = ref.paged_attention(dq, cache[:, 0, 0], cache[:, 0, 1], torch.arange(3, dtype=torch.int32), dsl,
+                                bt[1:], D ** -0.5)
+    torch.manual_seed(3)
+    x = torch.randn(300, 4096, dtype=torch.bfloat16)
+    w = torch.randn(1024, 4096, dtype=torch.bfloat16) * 0.02
+    r_mm = x.float() @ w.float().t()
+    for dev in ("cuda:0", "cuda:1"):
+        with torch.cuda.device(dev):
+            cd = cache.to(dev)
+            out = torch.zeros(q.shape, device=dev, dtype=torch.bfloat16)
+            C().prefill_attention(out, q.to(dev), cd[:, 0, 0], cd[:, 0, 1], qsl.to(dev), sl.to(dev), bt.to(dev), 0,
+                                  1, 300, D ** -0.5, 0, 0.0)
+            ws = torch.empty(2 * Hq * 4 * (D + 2), device=dev)
+            dout = torch.empty(dq.shape, device=dev, dtype=torch.bfloat16)
+            C().decode_attention(dout, dq.to(dev), cd[:, 0, 0], cd[:, 0, 1], dsl.to(dev), bt[1:].to(dev), ws, 2,
+                                 D ** -0.5, 0, 0.0, 4)
+            y = ops.linear(x.to(dev), w.to(dev))
+            torch.cuda.synchronize(dev)
+            assert rel_err(out[:300], r_pf[:300]) < 1.5e-2
+            assert rel_err(dout, r_dec) < 1e-2
+            assert rel_err(y, r_mm) < 1e-2
+            assert int(C().status()[0]) == 0
+
+
 def test_bounded_peer_wait_reports_timeout_and_context_survives():
     """Failure detection on the device without a fault: the fused TP boundary
     kernel waits for reduce-scatter flags that nothing sets (two 'ranks' whose

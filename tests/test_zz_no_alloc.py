@@ -77,6 +77,50 @@ def test_noalloc_matches_regular_entry_point_twice(Hq, Hkv, D, splits):
     assert status(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
 
 
+def _compare_twice(fn, seq_lens, Hq, Hkv, D, splits, seed):
+    from rusteeze_b200 import ops
+    cache, bt, q, sl = _inputs(seq_lens, Hq, Hkv, D, seed=seed)
+    kc, vc = cache[:, 1, 0], cache[:, 1, 1]
+    scale = D ** -0.5
+    ws = torch.empty(len(seq_lens) * Hq * splits * (D + 2), device=q.device)
+    ref = torch.empty_like(q)
+    ops.cuda_ext().decode_attention(ref, q, kc, vc, sl, bt, ws, len(seq_lens), scale, 0, 0.0, splits)
+    torch.cuda.synchronize(q.device)
+    for _ in range(2):
+        out = torch.full_like(q, float("nan"))
+        assert _call(fn, out, q, kc, vc, sl, bt, Hkv, splits, scale) == 0
+        torch.cuda.synchronize(q.device)
+        a, b = out.float().cpu(), ref.float().cpu()
+        assert torch.isfinite(a).all()
+        assert ((a - b).norm() / b.norm()).item() < 1e-2
+
+
+def test_noalloc_largest_accepted_size():
+    """16 sequences x 32 heads x 63 splits x (128 + 2) = 4,193,280 floats: the largest
+    split count that fits for this shape (head_dim + 2 never divides the power-of-two
+    array size, so no size ends exactly at its last float; this one ends 1,024 floats
+    before it).  One more split is rejected."""
+    fn, _ = _lib()
+    Hq, Hkv, D, S = 32, 8, 128, 16
+    splits = SCRATCH_FLOATS // (S * Hq * (D + 2))
+    assert splits == 63 and S * Hq * splits * (D + 2) > SCRATCH_FLOATS - Hq * (D + 2)
+    _compare_twice(fn, [1100 + 37 * i for i in range(S)], Hq, Hkv, D, splits, seed=7)
+    cache, bt, q, sl = _inputs([64] * S, Hq, Hkv, D, seed=8)
+    out = torch.empty_like(q)
+    assert _call(fn, out, q, cache[:, 0, 0], cache[:, 0, 1], sl, bt, Hkv, splits + 1, 0.1) == TOO_LARGE
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs a second GPU")
+def test_noalloc_on_a_second_device_after_the_first():
+    """The scratch address is looked up per device and kernels opt in to their shared
+    memory per device, so a call on cuda:1 after calls on cuda:0 must work."""
+    fn, status = _lib()
+    _compare_twice(fn, [5, 200, 777], 32, 8, 128, 4, seed=11)
+    with torch.cuda.device(1):
+        _compare_twice(fn, [5, 200, 777, 1500], 32, 8, 128, 4, seed=12)
+        assert status(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+
+
 def test_noalloc_rejects_sizes_beyond_scratch():
     fn, _ = _lib()
     Hq, Hkv, D = 32, 8, 128
