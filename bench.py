@@ -381,7 +381,8 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
     def admit(now):
         nonlocal nxt
         while nxt < len(prompts) and arrivals[nxt] <= now:
-            sp = SamplingParams(temperature=0.7, top_p=0.9, max_tokens=int(olens[nxt]), ignore_eos=True)
+            sp = SamplingParams(temperature=0.7, top_p=0.9, max_tokens=int(olens[nxt]), ignore_eos=True,
+                                output_kind="final_only")
             r = eng.add_request(None, None, sp, prompts[nxt])
             req_ids[r.request_id] = nxt
             nxt += 1
@@ -480,7 +481,8 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
             now = time.perf_counter() - w0
             while e_next < len(e_prompts) and e_arr[e_next] <= now:   # Poisson arrivals, as in config 3
                 eng.add_request(None, None, SamplingParams(temperature=0.7, top_p=0.9,
-                                                           max_tokens=int(e_olens[e_next]), ignore_eos=True),
+                                                           max_tokens=int(e_olens[e_next]), ignore_eos=True,
+                                                           output_kind="final_only"),
                                 e_prompts[e_next])
                 e_next += 1
             if not eng.has_unfinished_requests():
@@ -510,7 +512,8 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
                "requests": args.e2e_requests * world, "wall_s": round(e_s, 3),
                "workload": f"{args.e2e_requests} requests per engine, Poisson {args.rate}/s arrivals, same "
                            "length ranges and sampling as the timed run, submitted through LLMEngine.add_request "
-                           "as they arrive; wall clock from the first submission to the last token",
+                           "as they arrive (output_kind final_only: one output with its detokenised text per "
+                           "request); wall clock from the first submission to the last token",
                "ttft_p50_s": round(statistics.median(e_ttft), 4) if e_ttft else None}
 
     line = {
@@ -570,7 +573,7 @@ def static_batches(args, eng, device, rank, world, tp_timer=None):
         def run_once():
             for _ in range(B):
                 eng.add_request(None, None, SamplingParams(temperature=0.0, max_tokens=args.static_output,
-                                                           ignore_eos=True),
+                                                           ignore_eos=True, output_kind="final_only"),
                                 prefix + rng.integers(0, V, args.static_prompt).tolist())
             ttft = []
             while eng.has_unfinished_requests():

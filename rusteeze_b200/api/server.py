@@ -53,7 +53,9 @@ def _sampling_params(req, defaults, max_tokens_default: int, logprobs: Optional[
         logit_bias={int(k): v for k, v in (req.logit_bias or {}).items()},
         logprobs=logprobs, ignore_eos=req.ignore_eos, min_tokens=req.min_tokens,
         skip_special_tokens=req.skip_special_tokens,
-        include_stop_str_in_output=req.include_stop_str_in_output)
+        include_stop_str_in_output=req.include_stop_str_in_output,
+        # a non-streaming response is built from the final output only
+        output_kind="delta" if getattr(req, "stream", False) else "final_only")
 
 
 def _sse(obj) -> str:

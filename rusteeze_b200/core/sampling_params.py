@@ -85,6 +85,11 @@ class SamplingParams:
     mirostat_tau: float = 5.0
     mirostat_eta: float = 0.1
     guided_decoding: Optional[GuidedDecodingParams] = None
+    # "delta": the engine returns an output for the request after every step (streaming);
+    # "final_only": one output when it finishes, and its text is detokenised once then
+    # (unless stop strings need it token by token) -- offline batches and non-streaming
+    # API requests read nothing in between
+    output_kind: str = "delta"
 
     def __post_init__(self) -> None:
         if isinstance(self.stop, str):
@@ -153,6 +158,8 @@ class SamplingParams:
             v = getattr(self, name)
             if v is not None and not 0 <= v <= MAX_LOGPROBS:
                 bad(f"{name} must be in [0, {MAX_LOGPROBS}], got {v}")
+        if self.output_kind not in ("delta", "final_only"):
+            bad(f"output_kind must be 'delta' or 'final_only', got {self.output_kind!r}")
         if self.mirostat_mode not in (0, 1, 2):
             bad(f"mirostat_mode must be 0, 1 or 2, got {self.mirostat_mode}")
         if self.use_beam_search:

@@ -193,6 +193,17 @@ class BlockManager {
     return extra;
   }
 
+  // One call per scheduled sequence: grows `sid` to hold `num_tokens` (copy-on-write of
+  // shared blocks from `write_from` on) when the free pool allows it and returns the copy
+  // pairs (usually none); returns None and changes nothing when it does not fit.
+  py::object try_grow(int64_t sid, int64_t num_tokens, int64_t write_from) {
+    if (blocks_to_grow(sid, num_tokens, write_from) > num_free_gpu_blocks()) return py::none();
+    auto cow = ensure_capacity(sid, num_tokens, write_from);
+    py::list out;
+    for (const auto& c : cow) out.append(py::make_tuple(c.first, c.second));
+    return std::move(out);
+  }
+
   // After a step wrote KV for positions < num_computed, publish newly
   // completed full blocks to the prefix cache.
   void commit(int64_t sid, py::array_t<int64_t, py::array::c_style> tokens, int64_t num_computed) {
@@ -484,6 +495,7 @@ void bind_block_manager(py::module_& m) {
       .def("allocate_prompt", &BlockManager::allocate_prompt)
       .def("ensure_capacity", &BlockManager::ensure_capacity)
       .def("blocks_to_grow", &BlockManager::blocks_to_grow)
+      .def("try_grow", &BlockManager::try_grow)
       .def("commit", &BlockManager::commit)
       .def("free", &BlockManager::free)
       .def("fork", &BlockManager::fork)

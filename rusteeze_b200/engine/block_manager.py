@@ -67,6 +67,10 @@ class PyBlockManager:
     def num_gpu_blocks(self):
         return self.ngpu
 
+    @property
+    def block_size(self):
+        return self.bs
+
     def num_free_gpu_blocks(self):
         return len(self.gpu_free) + len(self.lru)
 
@@ -161,6 +165,11 @@ class PyBlockManager:
             if self.gpu_ref[st.blocks[b]] > 1:
                 extra += 1
         return extra
+
+    def try_grow(self, sid, num_tokens, write_from):
+        if self.blocks_to_grow(sid, num_tokens, write_from) > self.num_free_gpu_blocks():
+            return None
+        return self.ensure_capacity(sid, num_tokens, write_from)
 
     def commit(self, sid, toks, num_computed):
         if not self.prefix:

@@ -141,6 +141,7 @@ class LLMEngine:
         self.stats_counters = {"steps": 0, "prompt_tokens": 0, "generation_tokens": 0,
                                "requests_finished": 0, "requests_aborted": 0}
         self.observers: List[Callable] = []
+        self._prefix_caching = bool(ec.enable_prefix_caching)
         self.phase_s: Dict[str, float] = {"schedule": 0.0, "postprocess": 0.0}
         # asynchronous scheduling: CUDA engine without speculation over a runner (or a
         # tensor-parallel executor) that can pipeline steps
@@ -270,10 +271,7 @@ class LLMEngine:
         touched = self._apply_results(so, res, owners, now)
         for obs in self.observers:
             obs(self, so, now - t0)
-        for req in touched:
-            outputs.append(req.to_output(delta=True))
-            if req.is_finished():
-                self._retire(req)
+        outputs += self._emit(touched)
         outputs += self._collect_ignored()
         ph = self.phase_s
         ph["schedule"] += h1 - h0
@@ -358,18 +356,27 @@ class LLMEngine:
                 seen.add(id(req))
                 touched.append(req)
         # publish the now-known full blocks to the prefix cache
-        for ss in done.so.scheduled:
-            s = ss.seq
-            if not s.is_finished() and self.bm.has_seq(s.seq_id):
-                self.bm.commit(s.seq_id, s.tokens_np(), min(s.num_computed, len(s.token_ids)))
+        if self._prefix_caching:
+            for ss in done.so.scheduled:
+                s = ss.seq
+                if not s.is_finished() and self.bm.has_seq(s.seq_id):
+                    self.bm.commit(s.seq_id, s.tokens_np(), min(s.num_computed, len(s.token_ids)))
         for obs in self.observers:
             obs(self, done.so, now - done.t_launch)
+        outputs = self._emit(touched)
+        self.phase_s["postprocess"] += time.perf_counter() - h2
+        return outputs
+
+    def _emit(self, touched) -> List[RequestOutput]:
+        """Outputs of the requests a step advanced: every step for streaming requests,
+        only the last one for final-only requests; finished requests are retired."""
         outputs = []
         for req in touched:
-            outputs.append(req.to_output(delta=True))
-            if req.is_finished():
+            fin = req.is_finished()
+            if fin or req.stream:
+                outputs.append(req.to_output(delta=True))
+            if fin:
                 self._retire(req)
-        self.phase_s["postprocess"] += time.perf_counter() - h2
         return outputs
 
     def _drain_inflight(self) -> List[RequestOutput]:
@@ -459,9 +466,14 @@ class LLMEngine:
         return touched
 
     def _check_stop(self, s: Sequence, tok: int) -> None:
-        p = s.request.params
-        delta = s.detok.step(tok) if s.detok is not None else ""
-        s.output_text += delta
+        req = s.request
+        p = req.params
+        if req.defer_text or s.detok is None:
+            delta = ""
+        else:
+            delta = s.detok.step(tok)
+            s.detok_n += 1
+            s.output_text += delta
         reason = None
         n = s.num_generated
         if n >= p.min_tokens:
@@ -541,6 +553,9 @@ class LLM:
         n = len(prompts) if prompts is not None else len(prompt_token_ids)
         if not isinstance(sampling_params, list):
             sampling_params = [sampling_params or SamplingParams()] * n
+        # offline batches read only the finished outputs
+        sampling_params = [sp if sp.output_kind == "final_only" else sp.clone(output_kind="final_only")
+                           for sp in sampling_params]
         ids = []
         for i in range(n):
             req = self.engine.add_request(

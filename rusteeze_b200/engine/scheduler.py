@@ -56,14 +56,22 @@ class SchedulerConfig:
     max_prefill_seqs: int = 64          # bound on prefill chunks per step
 
 
-@dataclass
 class ScheduledSeq:
-    seq: Sequence
-    ctx: int            # tokens with KV before this step
-    num_new: int        # tokens computed this step
-    sample: bool        # logits of the last new token are sampled
-    num_samples: int = 1
-    pend_row: int = -1  # async scheduling: row of the previous step's samples that is this step's input
+    """One sequence's share of a step (a plain slotted class: thousands are built per step)."""
+    __slots__ = ("seq", "ctx", "num_new", "sample", "num_samples", "pend_row")
+
+    def __init__(self, seq: Sequence, ctx: int, num_new: int, sample: bool, num_samples: int = 1,
+                 pend_row: int = -1):
+        self.seq = seq
+        self.ctx = ctx                  # tokens with KV before this step
+        self.num_new = num_new          # tokens computed this step
+        self.sample = sample            # logits of the last new token are sampled
+        self.num_samples = num_samples
+        self.pend_row = pend_row        # async scheduling: row of the previous step's samples that is this step's input
+
+    def __repr__(self) -> str:
+        return (f"ScheduledSeq(seq={self.seq.seq_id}, ctx={self.ctx}, num_new={self.num_new}, "
+                f"sample={self.sample}, num_samples={self.num_samples}, pend_row={self.pend_row})")
 
 
 @dataclass
@@ -84,6 +92,16 @@ class SchedulerOutput:
         return not self.decodes and not self.prefills
 
 
+def _sched_key(s: Sequence):
+    """Running order: highest priority, then oldest request, then sequence id (fixed for a
+    sequence's life, so it is computed once)."""
+    k = s.sched_key
+    if k is None:
+        r = s.request
+        k = s.sched_key = (-r.priority, r.arrival_time, s.seq_id)
+    return k
+
+
 class Scheduler:
     def __init__(self, cfg: SchedulerConfig, block_manager):
         self.cfg = cfg
@@ -94,6 +112,7 @@ class Scheduler:
         self.num_preemptions = 0
         self.ignored: List[Sequence] = []      # too long to ever run; the engine reports and drops them
         self._watermark_blocks = max(1, int(cfg.watermark * self.bm.num_gpu_blocks))
+        self._bs = self.bm.block_size
 
     # ------------------------------------------------------------------ queue ops
     def add(self, seq: Sequence) -> None:
@@ -132,8 +151,7 @@ class Scheduler:
 
     # ------------------------------------------------------------------ helpers
     def _key(self, s: Sequence):
-        r = s.request
-        return (-r.priority, r.arrival_time, s.seq_id)
+        return _sched_key(s)
 
     def _sort_waiting(self) -> None:
         pol = self.cfg.policy
@@ -180,44 +198,55 @@ class Scheduler:
         token_budget = cfg.max_num_batched_tokens
         seq_budget = cfg.max_num_seqs
 
-        # 1. running sequences, highest priority / oldest first
-        self.running.sort(key=self._key)
+        # 1. running sequences, highest priority / oldest first.  running[i:end] is the
+        # queue still to visit; preemption takes the lowest priority one from its end.
+        running = self.running
+        running.sort(key=_sched_key)
         kept: List[Sequence] = []
-        queue = list(self.running)
-        while queue:
-            seq = queue.pop(0)
+        bs, ngpu = self._bs, bm.num_gpu_blocks
+        la_decode = cfg.num_lookahead_slots
+        decodes, prefills = out.decodes, out.prefills
+        i, end = 0, len(running)
+        while i < end:
+            seq = running[i]
+            i += 1
             if seq.pending and self._finishes_with_pending(seq):
                 kept.append(seq)            # its in-flight token is its last: nothing to schedule
                 continue
-            if seq.is_prefill:
-                n = min(seq.remaining, token_budget)
+            total = len(seq.token_ids) + seq.pending
+            nc = seq.num_computed
+            prefill = total - nc > 1
+            if prefill:
+                n = min(total - nc, token_budget)
                 if n <= 0 or seq_budget <= 0:
                     kept.append(seq)        # keeps its blocks, continues next step
                     continue
+                la = 0
             else:
                 n = 1
-                if token_budget < 1 + self._lookahead(seq) or seq_budget <= 0:
+                la = la_decode
+                if token_budget < 1 + la or seq_budget <= 0:
                     self._preempt(seq, out)
                     continue
-            target = seq.num_computed + n + self._lookahead(seq)
-            if bm.blocks_for(target) > bm.num_gpu_blocks:
+            target = nc + n + la
+            if (target + bs - 1) // bs > ngpu:
                 # its KV can never fit the whole cache: the sequence ends here ("length")
                 self._drop_too_long(seq)
                 continue
-            while bm.blocks_to_grow(seq.seq_id, target, seq.num_computed) > bm.num_free_gpu_blocks():
-                if queue:
-                    self._preempt(queue.pop(), out)   # lowest priority goes first
-                else:
-                    break
-            if bm.blocks_to_grow(seq.seq_id, target, seq.num_computed) > bm.num_free_gpu_blocks():
+            cow = bm.try_grow(seq.seq_id, target, nc)
+            while cow is None and i < end:
+                end -= 1
+                self._preempt(running[end], out)  # lowest priority goes first
+                cow = bm.try_grow(seq.seq_id, target, nc)
+            if cow is None:
                 self._preempt(seq, out)
                 continue
-            out.blocks_to_copy.extend(bm.ensure_capacity(seq.seq_id, target, seq.num_computed))
-            done_prompt = seq.num_computed + n >= seq.total_len
-            ss = ScheduledSeq(seq, seq.num_computed, n, sample=done_prompt,
-                              num_samples=self._num_samples(seq) if done_prompt else 1)
-            (out.prefills if n > 1 or seq.is_prefill else out.decodes).append(ss)
-            token_budget -= n + (self._lookahead(seq) if n == 1 else 0)
+            if cow:
+                out.blocks_to_copy.extend(cow)
+            done_prompt = nc + n >= total
+            ss = ScheduledSeq(seq, nc, n, done_prompt, self._num_samples(seq) if done_prompt else 1)
+            (prefills if n > 1 or prefill else decodes).append(ss)
+            token_budget -= n + (la if n == 1 else 0)
             seq_budget -= 1
             kept.append(seq)
         self.running = kept

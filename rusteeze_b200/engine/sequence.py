@@ -36,7 +36,7 @@ class Sequence:
     __slots__ = ("seq_id", "request", "prompt_len", "token_ids", "status", "num_computed",
                  "num_cached", "logprobs", "cumulative_logprob", "output_text", "stop_reason",
                  "detok", "_buf", "index", "finish_reason", "rng_offset",
-                 "mirostat_mu", "spec_draft", "pending")
+                 "mirostat_mu", "spec_draft", "pending", "detok_n", "sched_key")
 
     def __init__(self, request: "Request", prompt_token_ids: List[int], index: int = 0):
         self.seq_id = next(_seq_ids)
@@ -53,6 +53,8 @@ class Sequence:
         self.stop_reason = None
         self.finish_reason: Optional[str] = None
         self.detok = None
+        self.detok_n = 0               # output tokens already fed to the detokenizer
+        self.sched_key = None          # running-queue order, set by the scheduler
         # int64 mirror of token_ids with room to grow: batch building slices it
         # without converting the Python list every step
         self._buf = np.empty(max(16, self.prompt_len + min(request.params.max_tokens or 256, 4096) + 8
@@ -111,6 +113,14 @@ class Sequence:
     def is_finished(self) -> bool:
         return self.status.is_finished
 
+    def materialize_text(self) -> None:
+        """Detokenises the output tokens not yet fed to the detokenizer (outputs whose
+        text is deferred until it is read)."""
+        n = len(self.token_ids) - self.prompt_len
+        if self.detok is not None and self.detok_n < n:
+            self.output_text += self.detok.extend(self.token_ids[self.prompt_len + self.detok_n:])
+            self.detok_n = n
+
     def reset_for_recompute(self) -> None:
         """Preemption by recompute: drop all KV; prompt+generated get re-prefilled."""
         self.num_computed = 0
@@ -138,6 +148,10 @@ class Request:
             self.metrics = RequestMetrics(arrival_time=self.arrival_time)
         if not self.seqs:
             self.seqs = [Sequence(self, self.prompt_token_ids, 0)]
+        # per-step outputs for streaming consumers; final-only requests without stop
+        # strings detokenise once, when their output is built
+        self.stream = self.params.output_kind == "delta"
+        self.defer_text = not self.stream and not self.params.stop
 
     @property
     def num_target_seqs(self) -> int:
@@ -160,6 +174,8 @@ class Request:
         outs = []
         deltas = []
         for s in seqs:
+            if self.defer_text:
+                s.materialize_text()
             text = s.output_text
             outs.append(CompletionOutput(index=s.index, text=text, token_ids=s.output_token_ids,
                                          cumulative_logprob=s.cumulative_logprob if p.logprobs is not None else None,

@@ -165,12 +165,7 @@ class SpecDecoder:
             self.draft_computed[ss.seq.seq_id] = ss.ctx + ss.num_new
         for obs in eng.observers:
             obs(eng, so, now - t0)
-        outs = []
-        for req in touched:
-            outs.append(req.to_output(delta=True))
-            if req.is_finished():
-                eng._retire(req)
-        return outs + eng._collect_ignored()
+        return eng._emit(touched) + eng._collect_ignored()
 
     def _draft_follow(self, so) -> None:
         if self.self_draft:
@@ -272,12 +267,7 @@ class SpecDecoder:
         eng.stats_counters["steps"] += 1
         for obs in eng.observers:
             obs(eng, so, now - t0)
-        outs = []
-        for req in touched:
-            outs.append(req.to_output(delta=True))
-            if req.is_finished():
-                eng._retire(req)
-        return outs
+        return eng._emit(touched)
 
     def _draft_catch_up(self, seqs, dc, cs, drunner) -> None:
         """Draft KV for positions [dc[i], cs[i]) of every sequence, in batches of at most

@@ -28,7 +28,6 @@ head/column, row split of o/down, vocab split of embedding and LM head).
 """
 from __future__ import annotations
 
-import os
 from dataclasses import dataclass
 from typing import List, Optional
 
@@ -281,10 +280,9 @@ class DecoderLM(nn.Module):
         if self.is_gemma2 or self.act != "silu":
             return False
         if getattr(self, "fp8", False):
-            # MXFP8 boundary chain (block-scaled GEMMs, quantised all-gather); opt-in with
-            # RZ_FUSED_TP_FP8=1, otherwise FP8 weights take the peer all-reduce path
-            if (os.environ.get("RZ_FUSED_TP_FP8", "0") != "1" or self.cfg.is_moe or not F.mx_ok
-                    or getattr(self, "fp8_format", None) != "ue8m0"):
+            # MXFP8 boundary chain (block-scaled GEMMs, quantised all-gather); fp32-scale FP8
+            # checkpoints and FP8 MoE take the peer all-reduce path
+            if self.cfg.is_moe or not F.mx_ok or getattr(self, "fp8_format", None) != "ue8m0":
                 return False
             return all(L.gate_up_q.shape[0] % 256 == 0 for L in self.layers)
         if self.cfg.is_moe:

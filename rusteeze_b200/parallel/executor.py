@@ -18,7 +18,6 @@ on the survivors (the engine then reports unhealthy).
 from __future__ import annotations
 
 import logging
-import os
 import pickle
 import time
 from typing import Optional, Tuple
@@ -64,13 +63,13 @@ class PlanChannel:
 class TPExecutor:
     """Drop-in for ModelRunner on rank 0 (`LLMEngine(executor=...)`).
 
-    Pipelined steps (`launch` / `finish`, RZ_TP_ASYNC=1 on GPUs): the next step's plan is
+    Pipelined steps (`launch` / `finish`, on with `engine.async_scheduling`): the next step's plan is
     published before the previous step's tokens are read back.  Decode inputs still on
     the device are scattered from the previous step's sample tensor, which rank 0
     broadcasts to the workers (device to device, one small collective ordered before the
     step's forward); the plan carries the scatter lists."""
 
-    supports_async = os.environ.get("RZ_TP_ASYNC", "0") == "1"
+    supports_async = True
 
     def __init__(self, runner: ModelRunner, channel: PlanChannel, liveness=None):
         self.runner = runner
@@ -226,6 +225,10 @@ def stage_plan(runner: ModelRunner, plan) -> Tuple[object, int, int]:
     from rusteeze_b200.models.decoder import AttentionMetadata
     r = runner
     T, S, MB = plan["T"], plan["S"], plan["mb"]
+    # alternate the pinned staging sets as rank 0 does: with pipelined steps this plan
+    # arrives while the previous step's host->device copies (and its sample-row index
+    # copy) may still be queued on the stream, reading the other set
+    r._flip_host()
     r.h_input_ids[:T] = torch.from_numpy(plan["ids"])
     r.h_positions[:T] = torch.from_numpy(plan["pos"])
     r.h_slots[:T] = torch.from_numpy(plan["slots"])

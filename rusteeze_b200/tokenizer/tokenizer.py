@@ -161,3 +161,30 @@ class IncrementalDetokenizer:
                 self.prefix_offset = 0
             return delta
         return ""
+
+    def extend(self, new_ids) -> str:
+        """Feeds many tokens at once and returns the text they add: the concatenation
+        of what `step` would have returned for them one by one, with one decode of the
+        window instead of two per token.  Used for outputs whose text nobody reads
+        until the request finishes.  Where the window ends in an incomplete character
+        the tokens go through `step` so the held-back tail is handled exactly."""
+        new_ids = [int(t) for t in new_ids]
+        if not new_ids:
+            return ""
+        n0 = len(self.ids)
+        self.ids.extend(new_ids)
+        prefix = self.tok.decode(self.ids[self.prefix_offset:self.read_offset], self.skip)
+        full = self.tok.decode(self.ids[self.prefix_offset:], self.skip)
+        if full.endswith("�") or "�" in full[len(prefix):] or not full.startswith(prefix):
+            del self.ids[n0:]
+            return "".join(self.step(t) for t in new_ids)
+        delta = full[len(prefix):]
+        self.prefix_offset = max(self.read_offset, len(self.ids) - 6)
+        self.read_offset = len(self.ids)
+        self.text += delta
+        if self.prefix_offset > 64:
+            cut = self.prefix_offset
+            self.ids = self.ids[cut:]
+            self.read_offset -= cut
+            self.prefix_offset = 0
+        return delta

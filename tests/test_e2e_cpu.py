@@ -100,3 +100,32 @@ def test_shared_prefix_different_suffixes():
     assert run(eng, ps[:1], 8) == ref[:1]
     assert run(eng, ps[1:], 8) == ref[1:]
     assert eng.bm.stats()["prefix_block_hits"] >= 6
+
+
+def test_final_only_outputs_match_streamed_outputs():
+    """output_kind="final_only": one output per request, at the end, with the same tokens and
+    text as the per-step (delta) outputs; stop strings still end the request on time."""
+    from rusteeze_b200.config.config import Config
+    from rusteeze_b200.core.sampling_params import SamplingParams
+    from rusteeze_b200.engine.llm_engine import LLMEngine
+    cfg = Config()
+    cfg.model.preset = "tiny-llama"
+    cfg.model.device = "cpu"
+    cfg.model.dtype = "float32"
+    cfg.engine.num_gpu_blocks = 256
+    res = {}
+    for kind in ("delta", "final_only"):
+        eng = LLMEngine(cfg)
+        counts, final = {}, {}
+        for i, stop in enumerate(([], [], ["e"])):
+            sp = SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True, stop=stop, output_kind=kind)
+            eng.add_request(f"r{i}", None, sp, list(range(5 + i, 40 + 3 * i)))
+        while eng.has_unfinished_requests():
+            for o in eng.step():
+                counts[o.request_id] = counts.get(o.request_id, 0) + 1
+                if o.finished:
+                    final[o.request_id] = (o.outputs[0].token_ids, o.outputs[0].text, o.outputs[0].finish_reason)
+        res[kind] = (counts, final)
+    assert res["delta"][1] == res["final_only"][1]
+    assert all(c == 1 for c in res["final_only"][0].values()) and len(res["final_only"][0]) == 3
+    assert all(c > 1 for c in res["delta"][0].values())

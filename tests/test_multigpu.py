@@ -9,6 +9,14 @@ import torch
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
+WORLDS = [2, 4, 8]
+
+
+def _need(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
 def _port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -45,11 +53,10 @@ def _ar_worker(rank, world, port, q):
 
 
 @pytest.mark.timeout(300)
-def test_peer_all_reduce_matches_nccl():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", WORLDS)
+def test_peer_all_reduce_matches_nccl(world):
+    _need(world)
     import torch.multiprocessing as mp
-    world = min(torch.cuda.device_count(), 4)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
@@ -103,22 +110,16 @@ def _boundary_worker(rank, world, port, q, jitter_ns=0, fine=0):
         dist.destroy_process_group()
 
 
-_OPTIN = pytest.mark.skipif(os.environ.get("RZ_TP_OPTIN_TESTS", "0") != "1",
-                            reason="not yet run on GPUs: opt-in (RZ_TP_OPTIN_TESTS=1)")
-
-
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("jitter_ns,fine", [(0, 0), pytest.param(20000, 0, marks=_OPTIN),
-                                            pytest.param(0, 1, marks=_OPTIN), pytest.param(20000, 1, marks=_OPTIN)])
-def test_fused_tp_boundary_matches_reference(jitter_ns, fine):
+@pytest.mark.parametrize("world", WORLDS)
+@pytest.mark.parametrize("jitter_ns,fine", [(0, 0), (20000, 0), (0, 1), (20000, 1)])
+def test_fused_tp_boundary_matches_reference(jitter_ns, fine, world):
     """Fused boundary vs reference.  jitter_ns: the producers pause pseudo-randomly (up to
     20 us) before their peer stores and flag releases, shuffling arrival orders.  fine: the
     add+RMSNorm+all-gather runs one row per CTA where the rank owns few rows (flag blocks
     released by an arrival counter)."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    _need(world)
     import torch.multiprocessing as mp
-    world = min(torch.cuda.device_count(), 4)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
@@ -136,12 +137,12 @@ def test_fused_tp_boundary_matches_reference(jitter_ns, fine):
 def _tp_model(arch):
     from rusteeze_b200.models.config import ModelArchitecture, ModelConfig
     if arch == "llama":
-        return ModelConfig(name="tp-mid", hidden_size=1024, intermediate_size=2816, num_hidden_layers=2,
+        return ModelConfig(name="tp-mid", hidden_size=1024, intermediate_size=3072, num_hidden_layers=2,
                            num_attention_heads=8, num_key_value_heads=2, vocab_size=32000,
                            max_position_embeddings=2048)
     return ModelConfig(name="ep-mid", architecture=ModelArchitecture.MIXTRAL, hidden_size=1024,
                        intermediate_size=1792, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
-                       vocab_size=32000, max_position_embeddings=2048, num_local_experts=4, num_experts_per_tok=2)
+                       vocab_size=32000, max_position_embeddings=2048, num_local_experts=8, num_experts_per_tok=2)
 
 
 def _tp_cfg(tp, backend):
@@ -164,19 +165,23 @@ def _tp_prompts():
     return [rng.integers(0, 32000, int(n)).tolist() for n in (50, 130, 20)]
 
 
-def _tp_run(eng, prompts):
+def _tp_run(eng, prompts, top=1):
+    """Greedy run: per prompt (tokens, logprob of the first token) or, with top > 1,
+    (tokens, the first step's top-`top` logprobs)."""
     from rusteeze_b200.core.sampling_params import SamplingParams
-    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True, logprobs=1)
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True, logprobs=top)
     ids = [eng.add_request(None, None, sp, p).request_id for p in prompts]
     done = {}
     while eng.has_unfinished_requests():
         for o in eng.step():
             if o.finished:
                 done[o.request_id] = o.outputs[0]
+    if top > 1:
+        return [(done[i].token_ids, dict(done[i].logprobs[0])) for i in ids]
     return [(done[i].token_ids, done[i].logprobs[0][done[i].token_ids[0]]) for i in ids]
 
 
-def _tp2_child(backend, arch, q):
+def _tp_child(backend, arch, q, world=2):
     """Rank 0 of a TP2 engine in a fresh process (torch symmetric memory keys
     its buffers by a per-process allocation count, so every launch starts clean)."""
     import faulthandler
@@ -184,7 +189,7 @@ def _tp2_child(backend, arch, q):
     faulthandler.dump_traceback_later(270, exit=True)
     from rusteeze_b200.parallel.launcher import TPEngineLauncher
     try:
-        launcher = TPEngineLauncher(_tp_cfg(2, backend), model_config=_tp_model(arch))
+        launcher = TPEngineLauncher(_tp_cfg(world, backend), model_config=_tp_model(arch))
         try:
             q.put(("ok", _tp_run(launcher.engine(), _tp_prompts())))
         finally:
@@ -195,21 +200,21 @@ def _tp2_child(backend, arch, q):
 
 
 @pytest.mark.timeout(600)
+@pytest.mark.parametrize("world", WORLDS)
 @pytest.mark.parametrize("backend,arch", [("nccl", "llama"), ("fused", "llama"), ("nccl", "mixtral"),
                                           ("fused", "mixtral")])
-def test_tp2_engine_matches_tp1(backend, arch):
-    """TP2 engine (rank 0 schedules, worker process over the plan ring) vs the
-    single-GPU engine.  Mixtral: attention TP2 + experts EP2; with the fused
-    backend the MoE dispatch is the fused all-gather and the combine stores
-    expert rows straight into the owners' slots."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def test_tp_engine_matches_tp1(backend, arch, world):
+    """TP engine at 2, 4 and 8 GPUs (rank 0 schedules, worker processes over the plan
+    ring) vs the single-GPU engine.  Mixtral: attention TP + experts EP (8 experts);
+    with the fused backend the MoE dispatch is the fused all-gather and the combine
+    stores expert rows straight into the owners' slots."""
+    _need(world)
     import torch.multiprocessing as mp
     from rusteeze_b200.engine.llm_engine import LLMEngine
     ref = _tp_run(LLMEngine(_tp_cfg(1, backend), model_config=_tp_model(arch)), _tp_prompts())
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    p = ctx.Process(target=_tp2_child, args=(backend, arch, q))
+    p = ctx.Process(target=_tp_child, args=(backend, arch, q, world))
     p.start()
     status, got = q.get(timeout=420)
     p.join(60)
@@ -222,10 +227,6 @@ def test_tp2_engine_matches_tp1(backend, arch):
 
 
 # ----------------------------------------------------------------------------- MXFP8 fused boundary
-_FP8_OPT_IN = pytest.mark.skipif(os.environ.get("RZ_FUSED_TP_FP8", "0") != "1",
-                                 reason="MXFP8 fused TP boundary is opt-in (RZ_FUSED_TP_FP8=1)")
-
-
 def _mx_weight(w):
     from rusteeze_b200.ops import reference as ref
     q, s = ref.quant_mxf8_weight(w)
@@ -281,16 +282,14 @@ def _boundary_mx_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@_FP8_OPT_IN
 @pytest.mark.timeout(300)
-def test_fused_tp_boundary_mxfp8_matches_reference():
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_tp_boundary_mxfp8_matches_reference(world):
     """MXFP8 chain: block-scaled GEMM reduce-scattering bf16 rows -> add + RMSNorm +
     quantise + all-gather of e4m3 rows and UE8M0 scale chunks -> block-scaled GEMM on
     the gathered operand; vs a dequantise-then-matmul fp32 reference."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    _need(world)
     import torch.multiprocessing as mp
-    world = min(torch.cuda.device_count(), 4)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
@@ -305,20 +304,20 @@ def test_fused_tp_boundary_mxfp8_matches_reference():
         assert err < 2e-2, f"rank {rank} rel err {err}"
 
 
-def _tp2_fp8_child(q):
+def _tp_fp8_child(q, world):
     import faulthandler
     os.environ["RZ_WORKER_WATCHDOG_S"] = "240"
     faulthandler.dump_traceback_later(270, exit=True)
     from rusteeze_b200.config.config import QuantizationConfig
     from rusteeze_b200.parallel.launcher import TPEngineLauncher
     try:
-        cfg = _tp_cfg(2, "fused")
+        cfg = _tp_cfg(world, "fused")
         cfg.model.quantization = QuantizationConfig(method="fp8_block")
         launcher = TPEngineLauncher(cfg, model_config=_tp_model("llama"))
         try:
             eng = launcher.engine()
             fused = eng.model._fused_tp_ok(1)
-            q.put(("ok", (fused, _tp_run(eng, _tp_prompts()))))
+            q.put(("ok", (fused, _tp_run(eng, _tp_prompts(), top=5))))
         finally:
             launcher.shutdown()
     except BaseException as e:  # noqa: BLE001
@@ -326,27 +325,29 @@ def _tp2_fp8_child(q):
         raise
 
 
-@_FP8_OPT_IN
 @pytest.mark.timeout(600)
-def test_tp2_fp8_fused_engine_matches_tp1():
-    """FP8 (MXFP8) Llama at TP2 over the fused MXFP8 boundary chain vs the 1-GPU FP8 engine."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_fp8_fused_engine_matches_tp1(world):
+    """FP8 (MXFP8) Llama at TP 2/4/8 over the fused MXFP8 boundary chain vs the 1-GPU FP8 engine."""
+    _need(world)
     import torch.multiprocessing as mp
     from rusteeze_b200.config.config import QuantizationConfig
     from rusteeze_b200.engine.llm_engine import LLMEngine
     cfg = _tp_cfg(1, "fused")
     cfg.model.quantization = QuantizationConfig(method="fp8_block")
-    ref = _tp_run(LLMEngine(cfg, model_config=_tp_model("llama")), _tp_prompts())
+    ref = _tp_run(LLMEngine(cfg, model_config=_tp_model("llama")), _tp_prompts(), top=5)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    p = ctx.Process(target=_tp2_fp8_child, args=(q,))
+    p = ctx.Process(target=_tp_fp8_child, args=(q, world))
     p.start()
     status, got = q.get(timeout=420)
     p.join(60)
     assert status == "ok", got
     fused, toks = got
     assert fused, "the MXFP8 fused boundary chain was not selected"
-    for (ta, la), (tb, lb) in zip(toks, ref):
-        assert ta[0] == tb[0]
-        assert abs(la - lb) < 0.15
+    # e4m3 activations are re-quantised after a differently rounded reduction at TP > 1, so
+    # near-tied greedy choices of a random-init model may flip: each engine's first token must
+    # be among the other's top 5 with a close logprob
+    for (ta, top_a), (tb, top_b) in zip(toks, ref):
+        assert tb[0] in top_a and abs(top_a[tb[0]] - top_b[tb[0]]) < 0.15, (tb[0], top_a, top_b)
+        assert ta[0] in top_b and abs(top_b[ta[0]] - top_a[ta[0]]) < 0.15, (ta[0], top_a, top_b)
