@@ -262,6 +262,10 @@ def main():
                     help="cpu runs the harness itself on tiny models (gloo ranks, host clock): not a benchmark")
     ap.add_argument("--prompt-len", default="128,2048", help="prompt length range of the Poisson workload")
     ap.add_argument("--output-len", default="64,512", help="output length range of the Poisson workload")
+    ap.add_argument("--op-split", type=int, default=0,
+                    help="after the timed window, run this many more steps with per-section CUDA events "
+                         "(GEMMs with their collectives, attention, norms, sampling; MAX over ranks) and "
+                         "report ms per step per section; not part of the timed value")
     ap.add_argument("--static-prompt", type=int, default=512)
     ap.add_argument("--static-output", type=int, default=128)
     args = ap.parse_args()
@@ -462,6 +466,32 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
         ms_max, gen_sum, launches_sum = ms, float(gen), float(launches)
     value = gen_sum / (ms_max / 1000.0)
 
+    # ---------------------------------------------------------------- per-section split (separate window)
+    op_split = None
+    if args.op_split > 0 and dev.cuda:
+        from rusteeze_b200.utils.op_timer import OP_TIMER, SECTIONS
+        if tp_timer is not None:
+            tp_timer("ops_start")
+        else:
+            OP_TIMER.start()
+        sg0 = eng.stats_counters["steps"]
+        for _ in range(args.op_split):
+            step()
+        dev.sync()
+        if tp_timer is not None:
+            rep = tp_timer("ops_stop")
+        else:
+            OP_TIMER.stop()
+            rep = OP_TIMER.report()
+            if world > 1:
+                tv = torch.tensor([rep.get(k, 0.0) for k in SECTIONS], dtype=torch.float64, device=device)
+                dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+                rep = dict(zip(SECTIONS, tv.tolist()))
+        n_st = max(1, eng.stats_counters["steps"] - sg0)
+        op_split = {"steps": n_st, "ms_per_step": {k: round(v / n_st, 3) for k, v in rep.items() if v > 0},
+                    "note": "CUDA events around each section on the engine stream, MAX over ranks; the "
+                            "events break the overlap between fused sections, so the sum exceeds ms_per_step"}
+
     # ---------------------------------------------------------------- end-to-end through the public API
     e2e = None
     if not args.no_e2e:
@@ -548,6 +578,8 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
         "kernel_status": status,
         "e2e": e2e,
     }
+    if op_split is not None:
+        line["op_split"] = op_split
     return line
 
 

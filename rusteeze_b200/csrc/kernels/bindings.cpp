@@ -180,21 +180,6 @@ void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache
 }
 
 // ---------------------------------------------------------------- GEMM
-// Tail split of a plain GEMM (RZ_GEMM_TAIL_SPLIT=1 and a thin last wave): fp32 partial
-// workspace and zeroed arrival counters.  Returns the launches it adds (the counter fill).
-static int64_t setup_tail_split(rz::GemmParams& p, int k_blocks, int bn, const torch::TensorOptions& opt,
-                                torch::Tensor& ws, torch::Tensor& cnt) {
-  if (!rz::tail_split_enabled() || p.k_splits != 1 || p.epi != rz::kEpiNone || p.ag_flag) return 0;
-  const rz::TailPlan tp = rz::plan_tail_split(p.M, p.N, k_blocks, bn);
-  if (tp.tail_split <= 1) return 0;
-  ws = torch::empty({static_cast<int64_t>(tp.tail_tiles) * tp.tail_split * 128 * bn}, opt.dtype(torch::kFloat32));
-  cnt = torch::zeros({static_cast<int64_t>(tp.tail_tiles) * 8}, opt.dtype(torch::kInt32));
-  p.tail_split = tp.tail_split;
-  p.full_units = tp.full_units;
-  p.tail_ws = ws.data_ptr<float>();
-  p.tail_cnt = reinterpret_cast<uint32_t*>(cnt.data_ptr());
-  return 1;
-}
 
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi) {
   auto pl = rz::plan_gemm(M, N, K, epi);
@@ -228,15 +213,14 @@ int64_t gemm_bf16_ex(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::o
   p.ldr = residual.has_value() ? residual->stride(0) : 0;
   p.epi = epi;
   p.status = status_ptr();
-  torch::Tensor ws, tail_ws, tail_cnt;
+  torch::Tensor ws;
   if (k_splits > 1) {
     ws = torch::empty({k_splits, M, N}, x.options().dtype(torch::kFloat32));
     p.partial = ws.data_ptr<float>();
   }
-  const int64_t extra = setup_tail_split(p, (K + 63) / 64, bn, x.options(), tail_ws, tail_cnt);
   check_rc(rz::gemm_bf16_launch(p, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), bn, cur_stream()),
            "gemm_bf16");
-  return (k_splits > 1 ? 2 : 1) + extra;
+  return k_splits > 1 ? 2 : 1;
 }
 
 int64_t gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
@@ -358,15 +342,14 @@ int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch:
   p.status = status_ptr();
   p.sfa = reinterpret_cast<const uint8_t*>(sfa.data_ptr());
   p.sfb = reinterpret_cast<const uint8_t*>(sfb.data_ptr());
-  torch::Tensor ws, tail_ws, tail_cnt;
+  torch::Tensor ws;
   if (k_splits > 1) {
     ws = torch::empty({k_splits, M, N}, xq.options().dtype(torch::kFloat32));
     p.partial = ws.data_ptr<float>();
   }
-  const int64_t extra = setup_tail_split(p, K / 128, bn, xq.options(), tail_ws, tail_cnt);
   check_rc(rz::gemm_mxf8_launch(p, xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), bn, cur_stream()),
            "gemm_mxf8");
-  return (k_splits > 1 ? 2 : 1) + extra;
+  return k_splits > 1 ? 2 : 1;
 }
 
 // gate/up MXFP8 GEMM whose SiLU(gate)*up epilogue writes the down projection's MXFP8 operand.
@@ -745,28 +728,81 @@ void tp_epoch_bump(torch::Tensor epoch) {
 }
 
 // ---------------------------------------------------------------- sampling
-void argmax_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, bool want_lp) {
-  const at::cuda::CUDAGuard rz_guard(tok.device());
-  CHECK_CUDA(logits);
-  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "fp32 logits");
-  check_rc(rz::argmax_sample_launch(logits.data_ptr<float>(), logits.size(0), logits.size(1), logits.stride(0),
-                                    tok.data_ptr<int64_t>(), lp.data_ptr<float>(), want_lp, cur_stream()),
-           "argmax_sample");
+// ----------------------------------------------------------------------------- cluster sampler
+// Slot tables, in order: f32 [S,8], i32 [S,8], n_gen [S], seed [S], cnt [P, ceil(V/2)] (may be
+// empty), seen [P, ceil(V/32)] (may be empty), bias_tok [S, kSampMaxBias], bias_val, stop_ids.
+static rz::SampleSlotTables slot_tables(const std::vector<torch::Tensor>& t) {
+  TORCH_CHECK(t.size() == 9, "nine slot tables expected");
+  rz::SampleSlotTables st{};
+  st.f32 = t[0].data_ptr<float>();
+  st.i32 = t[1].data_ptr<int32_t>();
+  st.n_gen = t[2].data_ptr<int32_t>();
+  st.seed = t[3].data_ptr<int64_t>();
+  st.cnt = t[4].numel() ? reinterpret_cast<uint32_t*>(t[4].data_ptr<int32_t>()) : nullptr;
+  st.seen = t[5].numel() ? reinterpret_cast<uint32_t*>(t[5].data_ptr<int32_t>()) : nullptr;
+  st.bias_tok = t[6].data_ptr<int32_t>();
+  st.bias_val = t[7].data_ptr<float>();
+  st.stop_ids = t[8].data_ptr<int32_t>();
+  return st;
 }
 
-void topk_topp_sample(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, torch::Tensor temp,
-                      torch::Tensor topk, torch::Tensor topp, torch::Tensor minp, torch::Tensor seeds,
-                      torch::Tensor offsets, bool want_lp) {
-  const at::cuda::CUDAGuard rz_guard(tok.device());
+static rz::SampleClusterArgs cluster_args(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits) {
   CHECK_CUDA(logits);
-  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "fp32 logits");
-  (void)want_lp;
-  check_rc(rz::topk_topp_sample_launch(logits.data_ptr<float>(), logits.size(0), logits.size(1), logits.stride(0),
-                                       temp.data_ptr<float>(), topk.data_ptr<int32_t>(), topp.data_ptr<float>(),
-                                       minp.data_ptr<float>(), seeds.data_ptr<int64_t>(),
-                                       offsets.data_ptr<int64_t>(), tok.data_ptr<int64_t>(), lp.data_ptr<float>(),
-                                       cur_stream()),
-           "topk_topp_sample");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits [R, V] with unit column stride");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16, "fp32 or bf16 logits");
+  rz::SampleClusterArgs a{};
+  a.logits = logits.data_ptr();
+  a.ld = logits.stride(0);
+  a.R = static_cast<int>(logits.size(0));
+  a.V = static_cast<int>(logits.size(1));
+  a.tok = tok.data_ptr<int64_t>();
+  a.lp = lp.data_ptr<float>();
+  return a;
+}
+
+// Per-row parameters (every row greedy when temp <= 0).
+void sample_rows(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, torch::Tensor temp, torch::Tensor topk,
+                 torch::Tensor topp, torch::Tensor minp, torch::Tensor seeds, torch::Tensor offsets) {
+  const at::cuda::CUDAGuard rz_guard(tok.device());
+  rz::SampleClusterArgs a = cluster_args(tok, lp, logits);
+  a.temp = temp.data_ptr<float>();
+  a.topk = topk.data_ptr<int32_t>();
+  a.topp = topp.data_ptr<float>();
+  a.minp = minp.data_ptr<float>();
+  a.seeds = seeds.data_ptr<int64_t>();
+  a.offsets = offsets.data_ptr<int64_t>();
+  check_rc(rz::sample_cluster_launch(a, logits.scalar_type() == at::kBFloat16, false, cur_stream()), "sample_rows");
+}
+
+// Slot mode: row_info[r] = slot | (sample index << 16); penalties, bias and min_tokens from the
+// tables; the kernel advances each slot's generated count and penalty counts.
+void sample_slots(torch::Tensor tok, torch::Tensor lp, torch::Tensor logits, torch::Tensor row_info,
+                  std::vector<torch::Tensor> tables) {
+  const at::cuda::CUDAGuard rz_guard(tok.device());
+  rz::SampleClusterArgs a = cluster_args(tok, lp, logits);
+  TORCH_CHECK(row_info.scalar_type() == at::kInt && row_info.numel() >= a.R, "row_info int32 [R]");
+  a.row_info = row_info.data_ptr<int32_t>();
+  a.st = slot_tables(tables);
+  check_rc(rz::sample_cluster_launch(a, logits.scalar_type() == at::kBFloat16, true, cur_stream()), "sample_slots");
+}
+
+void sample_slot_init(std::vector<torch::Tensor> tables, int64_t n, int64_t V, torch::Tensor slot, torch::Tensor f32,
+                      torch::Tensor i32, torch::Tensor n_gen, torch::Tensor seed, torch::Tensor bias_tok,
+                      torch::Tensor bias_val, torch::Tensor stop_ids, torch::Tensor tok_off, torch::Tensor toks) {
+  const at::cuda::CUDAGuard rz_guard(slot.device());
+  rz::SampleSlotInit u{};
+  u.slot = slot.data_ptr<int32_t>();
+  u.f32 = f32.data_ptr<float>();
+  u.i32 = i32.data_ptr<int32_t>();
+  u.n_gen = n_gen.data_ptr<int32_t>();
+  u.seed = seed.data_ptr<int64_t>();
+  u.bias_tok = bias_tok.data_ptr<int32_t>();
+  u.bias_val = bias_val.data_ptr<float>();
+  u.stop_ids = stop_ids.data_ptr<int32_t>();
+  u.tok_off = tok_off.data_ptr<int32_t>();
+  u.toks = toks.data_ptr<int32_t>();
+  check_rc(rz::sample_slot_init_launch(u, static_cast<int>(n), slot_tables(tables), static_cast<int>(V), cur_stream()),
+           "sample_slot_init");
 }
 
 void spec_verify(torch::Tensor out_tokens, torch::Tensor n_acc, torch::Tensor target_logits,
@@ -835,11 +871,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ag_cnt") = py::none());
   m.def("gemm_peer_rs_mx", &gemm_peer_rs_mx);
   m.def("set_comm_jitter_ns", &set_comm_jitter_ns);
-  m.def("gemm_tail_split_enabled", &rz::tail_split_enabled);
-  m.def("gemm_tail_plan", [](int64_t M, int64_t N, int64_t k_blocks, int64_t bn, int64_t sms) {
-    const rz::TailPlan t = rz::plan_tail_split(M, N, k_blocks, bn, sms);
-    return std::vector<int64_t>{t.tail_split, t.full_units, t.tail_tiles};
-  });
   m.def("gemm_mxf8_ag", &gemm_mxf8_ag);
   m.def("moe_forward_peer", &moe_forward_peer);
   m.def("ag_wait", &ag_wait);
@@ -849,9 +880,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_mxf8", &gemm_mxf8);
   m.def("gemm_plan_mxf8", &gemm_plan_mxf8);
   m.def("gemm_mxf8_silu_q", &gemm_mxf8_silu_q);
-  m.def("argmax_sample", &argmax_sample);
-  m.def("topk_topp_sample", &topk_topp_sample);
   m.def("spec_verify", &spec_verify);
+  m.def("sample_rows", &sample_rows);
+  m.def("sample_slots", &sample_slots);
+  m.def("sample_slot_init", &sample_slot_init);
+  m.attr("SAMPLE_MAX_BIAS") = rz::kSampMaxBias;
+  m.attr("SAMPLE_MAX_STOP") = rz::kSampMaxStop;
   m.def("copy_blocks", &copy_blocks);
   m.def("status", &read_status);
   bind_comm(m);

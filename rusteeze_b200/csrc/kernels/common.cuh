@@ -14,25 +14,31 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <mutex>
 
 #define RZ_DEVICE __device__ __forceinline__
 
 namespace rz {
 
-// Opts kernel `Kernel` in to `bytes` of dynamic shared memory on the current device.
-// The attribute belongs to a device's context, so a process that launches on several
-// GPUs (one engine replica per GPU, each on its own thread) needs it once per device; a
-// bit per device records which have it.  Two threads racing on a device's first launch
-// both set the attribute, which is idempotent.
+// Opts kernel `Kernel` in to at least `bytes` of dynamic shared memory on the current
+// device.  The attribute belongs to a device's context, so a process that launches on
+// several GPUs (one engine replica per GPU, each on its own thread) needs it once per
+// device; and a kernel whose shared memory depends on its arguments (the sampler's row
+// slice grows with the vocabulary) must raise it when a larger launch comes: the
+// largest size granted per device is recorded, and raising it is serialised so that a
+// smaller request can never overwrite a larger grant.
 template <auto Kernel>
 inline void opt_in_smem(int bytes) {
-  static std::atomic<uint64_t> devices{0};
+  static std::atomic<int> granted[64];
+  static std::mutex raise;
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint64_t bit = 1ull << (dev & 63);
-  if (devices.load(std::memory_order_acquire) & bit) return;
+  dev &= 63;
+  if (granted[dev].load(std::memory_order_acquire) >= bytes) return;
+  std::lock_guard<std::mutex> g(raise);
+  if (granted[dev].load(std::memory_order_relaxed) >= bytes) return;
   cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  devices.fetch_or(bit, std::memory_order_acq_rel);
+  granted[dev].store(bytes, std::memory_order_release);
 }
 
 constexpr uint64_t kWaitTimeoutNs = 1000ull * 1000ull * 1000ull;  // 1 s

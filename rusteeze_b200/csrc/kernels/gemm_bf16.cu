@@ -89,34 +89,22 @@ __device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* src, float* v) 
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
-// What a work unit computes: tile index t (in unit order), K blocks [kb0, kb1), the split
-// index ks of a split-K unit, and the tail tile index (-1 unless it is a tail-split unit).
+// What a work unit computes: tile index t (in unit order), K blocks [kb0, kb1) and the split
+// index ks of a split-K unit.
 struct UnitWork {
-  int t, kb0, kb1, ks, tail;
+  int t, kb0, kb1, ks;
 };
 
-template <bool TAIL>
 __device__ __forceinline__ UnitWork unit_work(const GemmParams& p, int u) {
   UnitWork w;
-  if (TAIL && u >= p.full_units) {
-    const int v = u - p.full_units;
-    const int per = (p.k_blocks + p.tail_split - 1) / p.tail_split;
-    w.tail = v / p.tail_split;
-    w.ks = v % p.tail_split;
-    w.t = p.full_units + w.tail;
-    w.kb0 = w.ks * per;
-    w.kb1 = min(p.k_blocks, w.kb0 + per);
-  } else {
-    w.tail = -1;
-    w.ks = u % p.k_splits;
-    w.t = u / p.k_splits;
-    w.kb0 = w.ks * p.kb_per_split;
-    w.kb1 = min(p.k_blocks, w.kb0 + p.kb_per_split);
-  }
+  w.ks = u % p.k_splits;
+  w.t = u / p.k_splits;
+  w.kb0 = w.ks * p.kb_per_split;
+  w.kb1 = min(p.k_blocks, w.kb0 + p.kb_per_split);
   return w;
 }
 
-template <int BN, bool MX, bool PEER, bool TAIL>
+template <int BN, bool MX, bool PEER>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  GemmParams p) {
@@ -153,8 +141,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       s_grp[i] = i <= G ? p.grp_off[i] : p.grp_end[i - G - 1];
   }
   const int m_tiles = G ? p.grp_off[G] / kBM : p.m_tiles;
-  const int num_units = TAIL ? p.full_units + (m_tiles * p.n_tiles - p.full_units) * p.tail_split
-                            : m_tiles * p.n_tiles * p.k_splits;
+  const int num_units = m_tiles * p.n_tiles * p.k_splits;
   const uint32_t epoch =
       p.epoch_ptr ? *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u : 0u;
   // GEMMs that feed or consume a collective finish whole m tiles first: the reduce-scatter
@@ -195,7 +182,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       uint64_t ag_ready = 0;                 // m tiles whose all-gathered rows were already seen
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        const UnitWork w = unit_work<TAIL>(p, u);
+        const UnitWork w = unit_work(p, u);
         const int t = w.t;
         const int mb = row_major ? t / p.n_tiles : t % m_tiles;
         const int nb = row_major ? t % p.n_tiles : t / m_tiles;
@@ -248,7 +235,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t aph = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        const UnitWork w = unit_work<TAIL>(p, u);
+        const UnitWork w = unit_work(p, u);
         const int kb0 = w.kb0, kb1 = w.kb1;
         if (!mbar_wait(&tempty[acc], aph ^ 1, p.status, kGemmMmaTimeout)) { ok = false; break; }
         tc_fence_after();
@@ -304,7 +291,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t aph = 0;
     uint32_t xph = 0;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
-      const UnitWork w = unit_work<TAIL>(p, u);
+      const UnitWork w = unit_work(p, u);
       const int ks = w.ks;
       const int t = w.t;
       const int mb = row_major ? t / p.n_tiles : t % m_tiles;
@@ -390,53 +377,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
         const int colh = nb * BN + half * (BN / 2);
-        bool finish = true;                  // this unit stores its region of the tile
-        if (TAIL && w.tail >= 0) {
-          // tail split: publish this split's fp32 partial of the warp's region; the split that
-          // arrives last sums every partial in split order (reproducible) and stores the tile
-          const int S = p.tail_split;
-          const size_t tile0 = static_cast<size_t>(w.tail) * S;
-          const size_t roff = static_cast<size_t>(row_in_tile) * BN + half * (BN / 2);
-          float* mine = p.tail_ws + (tile0 + w.ks) * (kBM * BN) + roff;
-#pragma unroll
-          for (int c = 0; c < NC; ++c)
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(mine + c * 32 + j) =
-                  make_float4(__uint_as_float(r[c][j]), __uint_as_float(r[c][j + 1]), __uint_as_float(r[c][j + 2]),
-                              __uint_as_float(r[c][j + 3]));
-          __threadfence();
-          __syncwarp();
-          uint32_t* cnt = p.tail_cnt + w.tail * 8 + quarter * 2 + half;
-          uint32_t prev = 0;
-          if (lane == 0) prev = atomicAdd(cnt, 1u);
-          prev = __shfl_sync(0xffffffffu, prev, 0);
-          finish = prev == static_cast<uint32_t>(S - 1);
-          if (finish) {
-            __threadfence();
-#pragma unroll
-            for (int c = 0; c < NC; ++c)
-#pragma unroll
-              for (int j = 0; j < 32; ++j) r[c][j] = 0u;     // +0.0f
-            for (int sp = 0; sp < S; ++sp) {
-              const float* part = p.tail_ws + (tile0 + sp) * (kBM * BN) + roff;
-#pragma unroll
-              for (int c = 0; c < NC; ++c)
-#pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                  const float4 v = __ldcg(reinterpret_cast<const float4*>(part + c * 32 + j));
-                  r[c][j] = __float_as_uint(__uint_as_float(r[c][j]) + v.x);
-                  r[c][j + 1] = __float_as_uint(__uint_as_float(r[c][j + 1]) + v.y);
-                  r[c][j + 2] = __float_as_uint(__uint_as_float(r[c][j + 2]) + v.z);
-                  r[c][j + 3] = __float_as_uint(__uint_as_float(r[c][j + 3]) + v.w);
-                }
-            }
-            if (lane == 0) *cnt = 0u;                       // ready for the next launch
-          }
-        }
-        if (!finish) {
-          // another split of this tail tile stores it
-        } else if (p.k_splits > 1) {
+        if (p.k_splits > 1) {
           float* dst = p.partial + (static_cast<size_t>(ks) * p.M + row) * p.N;
 #pragma unroll
           for (int c = 0; c < NC; ++c) {
@@ -633,7 +574,7 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool MX, bool PEER, bool TAIL>
+template <int BN, bool MX, bool PEER>
 static int launch_inst(const GemmParams& p0, const void* A, int lda, const void* B, int ldb, cudaStream_t st) {
   using C = GemmCfg<BN, MX, PEER>;
   constexpr int kElems = MX ? kBKMx : kBK;
@@ -645,13 +586,9 @@ static int launch_inst(const GemmParams& p0, const void* A, int lda, const void*
   GemmParams p = p0;
   p.m_tiles = (p.M + kBM - 1) / kBM;
   p.n_tiles = (p.N + BN - 1) / BN;
-  if (TAIL && (p.tail_split < 2 || p.k_splits != 1 || p.epi != kEpiNone || p.ag_flag || PEER || !p.tail_ws ||
-               !p.tail_cnt || p.full_units < 0 || p.full_units >= p.m_tiles * p.n_tiles))
-    return -6;
-  const int units = TAIL ? p.full_units + (p.m_tiles * p.n_tiles - p.full_units) * p.tail_split
-                         : p.m_tiles * p.n_tiles * p.k_splits;
+  const int units = p.m_tiles * p.n_tiles * p.k_splits;
   const int grid = units < num_sms() ? units : num_sms();
-  opt_in_smem<gemm_tcgen05<BN, MX, PEER, TAIL>>(C::kSmemBytes);
+  opt_in_smem<gemm_tcgen05<BN, MX, PEER>>(C::kSmemBytes);
   if (p.ag_flag) {
     // the A rows are guarded by all-gather flags: start while the previous kernel (the
     // add+RMSNorm+all-gather) is still running, as soon as all of its CTAs are resident
@@ -665,10 +602,10 @@ static int launch_inst(const GemmParams& p0, const void* A, int lda, const void*
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05<BN, MX, PEER, TAIL>, ta, tb, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05<BN, MX, PEER>, ta, tb, p);
     if (e != cudaSuccess) return static_cast<int>(e);
   } else {
-    gemm_tcgen05<BN, MX, PEER, TAIL><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);
+    gemm_tcgen05<BN, MX, PEER><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);
   }
   if (p.k_splits > 1) {
     const int ncols_out = p.epi == kEpiSiluMul ? p.N / 2 : p.N;
@@ -678,46 +615,16 @@ static int launch_inst(const GemmParams& p0, const void* A, int lda, const void*
   return static_cast<int>(cudaGetLastError());
 }
 
-// reduce-scatter GEMMs use the instance with the epilogue transpose buffer, tail-split
-// GEMMs the one with the partial-sum path; every other GEMM carries neither
+// reduce-scatter GEMMs use the instance with the epilogue transpose buffer; every other
+// GEMM is built without it
 template <int BN, bool MX>
 static int launch_bn(const GemmParams& p, const void* A, int lda, const void* B, int ldb, cudaStream_t st) {
-  if (p.epi == kEpiPeerRS) return launch_inst<BN, MX, true, false>(p, A, lda, B, ldb, st);
-  if (p.tail_split > 1) return launch_inst<BN, MX, false, true>(p, A, lda, B, ldb, st);
-  return launch_inst<BN, MX, false, false>(p, A, lda, B, ldb, st);
+  if (p.epi == kEpiPeerRS) return launch_inst<BN, MX, true>(p, A, lda, B, ldb, st);
+  return launch_inst<BN, MX, false>(p, A, lda, B, ldb, st);
 }
 
-// RZ_GEMM_TAIL_SPLIT=1 enables the tail split for plain (kEpiNone) GEMMs.
-bool tail_split_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("RZ_GEMM_TAIL_SPLIT");
-    return v && v[0] == '1';
-  }();
-  return on;
-}
-
-TailPlan plan_tail_split(int M, int N, int k_blocks, int bn, int sms) {
-  TailPlan tp{1, 0, 0};
-  if (sms <= 0) sms = num_sms();
-  if (sms <= 0 || k_blocks < 2) return tp;
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
-  const int rem = tiles % sms;
-  // a thin last wave (at most half the SMs busy): split its tiles' K over the idle SMs
-  if (tiles <= sms || rem == 0 || rem * 2 > sms) return tp;
-  const int want = sms / rem;
-  const int per = (k_blocks + want - 1) / want;
-  const int S = (k_blocks + per - 1) / per;    // no empty split
-  if (S < 2) return tp;
-  return TailPlan{S, tiles - rem, rem};
-}
-
-// Waves of a ks == 1 grid of `units` tiles, counting a tail-split last wave as its share.
-static double effective_waves(int units, int sms, bool tail) {
-  const int full = units / sms, rem = units % sms;
-  if (rem == 0) return full;
-  if (tail && full > 0 && rem * 2 <= sms) return full + 1.0 / (sms / rem) + 0.1;   // + fix-up
-  return full + 1;
-}
+// Waves of a grid of `units` tiles on `sms` SMs.
+static double effective_waves(int units, int sms) { return static_cast<double>((units + sms - 1) / sms); }
 
 GemmPlan plan_gemm(int M, int N, int K, int epi, int max_splits) {
   // Pick (BN, k_splits <= max_splits) minimising an estimate of waves x per-unit cost.
@@ -732,8 +639,7 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int max_splits) {
     for (int ks = 1; ks <= max_splits; ks *= 2) {
       if (ks > 1 && kblocks / ks < 4) break;
       const int units = mt * nt * ks;
-      const double waves = ks == 1 ? effective_waves(units, sms, tail_split_enabled() && epi == kEpiNone)
-                                   : static_cast<double>((units + sms - 1) / sms);
+      const double waves = effective_waves(units, sms);
       const double kb = static_cast<double>((kblocks + ks - 1) / ks);
       // per unit: MMA time ~ 128*bn*64*2 flop per k-block at ~8.2 TFLOP/s/SM; load time ~ (128+bn)*128 B per
       // k-block at ~40 GB/s/SM (HBM share) -- whichever dominates
@@ -784,8 +690,8 @@ int gemm_grouped_launch(const GemmParams& p_in, const void* A, int lda, int64_t 
 #define RZ_GROUPED(BNV, MXV)                                                                                   \
   {                                                                                                           \
     using C = GemmCfg<BNV, MXV, false>;                                                                       \
-    opt_in_smem<gemm_tcgen05<BNV, MXV, false, false>>(C::kSmemBytes);                                       \
-    gemm_tcgen05<BNV, MXV, false, false><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);               \
+    opt_in_smem<gemm_tcgen05<BNV, MXV, false>>(C::kSmemBytes);                                       \
+    gemm_tcgen05<BNV, MXV, false><<<grid, kGemmThreads, C::kSmemBytes, st>>>(ta, tb, p);               \
   }
   if (!mx && bn == 256) RZ_GROUPED(256, false)
   else if (!mx && bn == 128) RZ_GROUPED(128, false)
@@ -819,8 +725,7 @@ GemmPlan plan_gemm_mxf8(int M, int N, int K, int epi, int max_splits) {
     for (int ks = 1; ks <= max_splits; ks *= 2) {
       if (ks > 1 && (kblocks / ks < 4 || mt * nt * 2 > sms)) break;
       const int units = mt * nt * ks;
-      const double waves = ks == 1 ? effective_waves(units, sms, tail_split_enabled() && epi == kEpiNone)
-                                   : static_cast<double>((units + sms - 1) / sms);
+      const double waves = effective_waves(units, sms);
       const double kb = static_cast<double>((kblocks + ks - 1) / ks);
       // 128x128 fp8 tiles are shared-memory bound (~10.5 vs ~14 TFLOP/s/SM measured)
       const double t_mma = kb * (128.0 * bn * 128 * 2) / (bn == 256 ? 14e12 : 10.5e12);

@@ -53,16 +53,6 @@ struct GemmParams {
   uint8_t* q_out;              // kEpiSiluMulMx outputs
   uint8_t* sf_out;
   uint32_t jitter_ns;          // kEpiPeerRS race testing: random pauses before stores and flags (0: off)
-  // Tail split (k_splits == 1, kEpiNone, no communication): when the last wave is thin,
-  // the tiles after the first full_units (in unit order) run as tail_split K ranges
-  // each.  A split stores its fp32 partial of every warp region into
-  // tail_ws [tail tile][tail_split][128][BN] and bumps tail_cnt [tail tile][8]; the
-  // split that arrives last sums all partials in split order and runs the epilogue,
-  // then resets the counter (no split ever waits for another).
-  int tail_split;              // <= 1: off
-  int full_units;
-  float* tail_ws;
-  uint32_t* tail_cnt;
 };
 
 constexpr int kMaxGemmGroups = 64;
@@ -74,14 +64,6 @@ struct GemmPlan {
 };
 
 GemmPlan plan_gemm(int M, int N, int K, int epi, int max_splits = 16);
-// Tail split of an (M, N, K) GEMM with BN-column tiles: {tail_split, full_units, tail_tiles},
-// tail_split <= 1 when the last wave is not thin enough to pay.  k_blocks = K blocks of the
-// operand format (K / 64 bf16, K / 128 MXFP8).
-struct TailPlan {
-  int tail_split, full_units, tail_tiles;
-};
-TailPlan plan_tail_split(int M, int N, int k_blocks, int bn, int sms = 0);   // sms <= 0: this device's
-bool tail_split_enabled();   // RZ_GEMM_TAIL_SPLIT=1
 __global__ void gemm_splitk_reduce(GemmParams p);
 int gemm_bf16_launch(const GemmParams& p, const void* A, int lda, const void* B, int ldb, int bn,
                      cudaStream_t stream);

@@ -142,6 +142,10 @@ class LLMEngine:
                                "requests_finished": 0, "requests_aborted": 0}
         self.observers: List[Callable] = []
         self._prefix_caching = bool(ec.enable_prefix_caching)
+        # device sampling slots (one per live sequence) of the rank that samples
+        self._sampler = getattr(self.runner, "sampler", None)
+        if self._sampler is not None and self.device.startswith("cuda"):
+            self._sampler.max_slots = ec.max_num_seqs + 64
         self.phase_s: Dict[str, float] = {"schedule": 0.0, "postprocess": 0.0}
         # asynchronous scheduling: CUDA engine without speculation over a runner (or a
         # tensor-parallel executor) that can pipeline steps
@@ -255,6 +259,8 @@ class LLMEngine:
         h0 = time.perf_counter()
         with nvtx_range("rz.step.schedule"):
             so = self.scheduler.schedule()
+        if so.preempted:
+            self._release_slots(so.preempted)
         outputs: List[RequestOutput] = []
         if so.is_empty():
             # nothing to run, but a swap-in or swap-out decided this step must still happen
@@ -297,6 +303,8 @@ class LLMEngine:
         h0 = time.perf_counter()
         with nvtx_range("rz.step.schedule"):
             so = self.scheduler.schedule()
+        if so.preempted:
+            self._release_slots(so.preempted)
         launched = False
         if so.is_empty():
             self.runner.apply_block_ops(so)        # block moves of a step with nothing to run
@@ -408,14 +416,10 @@ class LLMEngine:
             s = ss.seq
             req = s.request
             p = req.params
-            # token histories are only materialised for the rows that read them
-            pen = p.has_penalties()
-            prompt_ids = s.token_ids[:s.prompt_len] if pen else ()
-            output_ids = s.output_token_ids if (pen or p.min_tokens > s.num_generated) else ()
+            # token histories are read from the sequence only by rows that need them
             for j in range(ss.num_samples):
-                rows.append(SampleRow(p, prompt_ids, output_ids,
-                                      seed=req.seed + 7919 * (s.index + j), offset=s.num_generated + s.pending,
-                                      eos_ids=self.eos_ids, mirostat_mu=s.mirostat_mu))
+                rows.append(SampleRow(p, None, None, req.seed + 7919 * (s.index + j), s.num_generated + s.pending,
+                                      self.eos_ids, s.mirostat_mu, s, j))
             owners.append((ss, ss.num_samples))
         return rows, owners
 
@@ -500,8 +504,15 @@ class LLMEngine:
             self.scheduler.remove(s)
             self.bm.free(s.seq_id)
 
+    def _release_slots(self, seqs) -> None:
+        sm = self._sampler
+        if sm is not None:
+            for s in seqs:
+                sm.release(s.seq_id)
+
     def _retire(self, req: Request) -> None:
         import time as _t
+        self._release_slots(req.seqs)
         if req.request_id in self.requests:
             if not getattr(req, "async_ok", True):
                 self._n_sync_only -= 1

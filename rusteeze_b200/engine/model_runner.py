@@ -33,6 +33,7 @@ from rusteeze_b200.engine.sampler import SampleRow, Sampler, SampleResult
 from rusteeze_b200.engine.scheduler import SchedulerOutput
 from rusteeze_b200.models.decoder import AttentionMetadata, DecoderLM
 from rusteeze_b200.ops import BLOCK_SIZE
+from rusteeze_b200.utils.op_timer import OP_TIMER
 
 _ZERO1 = np.zeros(1, dtype=np.int64)
 
@@ -421,7 +422,8 @@ class ModelRunner:
                 self.d_input_ids[S:B].fill_(0)
                 self.d_positions[S:B].fill_(0)
             g, out, _ = self.graphs[B]
-            g.replay()
+            with OP_TIMER.section("decode_graph"):
+                g.replay()
             from rusteeze_b200 import ops as _ops
             _ops.add_launches(self.graph_launches.get(B, 0))
             return out.index_select(0, self._sample_index(sample_rows))

@@ -27,21 +27,168 @@ import numpy as np
 import torch
 
 from rusteeze_b200 import ops
+from rusteeze_b200.utils.op_timer import OP_TIMER
 from rusteeze_b200.core.sampling_params import SamplingParams
 from rusteeze_b200.ops import reference as ref
 
 _MASK = -1e30
 
 
-@dataclass
 class SampleRow:
-    params: SamplingParams
-    prompt_ids: Seq[int]
-    output_ids: Seq[int]
-    seed: int
-    offset: int
-    eos_ids: Tuple[int, ...] = ()
-    mirostat_mu: Optional[float] = None
+    """One row of logits to sample.  `seq` (the engine's Sequence, when there is one) and
+    `sub` (the sample index of a best_of prompt row) key the row's device slot; the token
+    histories that penalties read are taken from the sequence only when they are needed."""
+    __slots__ = ("params", "_prompt_ids", "_output_ids", "seed", "offset", "eos_ids", "mirostat_mu", "seq", "sub")
+
+    def __init__(self, params: SamplingParams, prompt_ids: Optional[Seq[int]] = None,
+                 output_ids: Optional[Seq[int]] = None, seed: int = 0, offset: int = 0,
+                 eos_ids: Tuple[int, ...] = (), mirostat_mu: Optional[float] = None, seq=None, sub: int = 0):
+        self.params = params
+        self._prompt_ids = prompt_ids
+        self._output_ids = output_ids
+        self.seed, self.offset, self.eos_ids, self.mirostat_mu = seed, offset, eos_ids, mirostat_mu
+        self.seq, self.sub = seq, sub
+
+    @property
+    def prompt_ids(self) -> Seq[int]:
+        if self._prompt_ids is None:
+            self._prompt_ids = self.seq.token_ids[:self.seq.prompt_len] if self.seq is not None else ()
+        return self._prompt_ids
+
+    @property
+    def output_ids(self) -> Seq[int]:
+        if self._output_ids is None:
+            self._output_ids = self.seq.output_token_ids if self.seq is not None else ()
+        return self._output_ids
+
+
+class SlotTable:
+    """Device-resident sampling state, one slot per live sequence (see
+    csrc/kernels/sampling_cluster.cu): parameters uploaded once when a sequence is first
+    sampled (or again after a preemption), the generated-token counter the kernel
+    advances, and for sequences with penalties a prompt bitmask and 16-bit output
+    counts the kernel updates after each draw.  A step then only uploads one int32 per
+    row (slot | sample index << 16).
+
+    Slots are released when a sequence finishes or is preempted; the next owner's
+    parameters are written by a kernel launched after every step that could still
+    touch the old owner, so stream order protects the hand-over."""
+
+    def __init__(self, max_slots: int, vocab: int, device: torch.device):
+        C = ops.cuda_ext()
+        self.MAXB, self.MAXS = int(C.SAMPLE_MAX_BIAS), int(C.SAMPLE_MAX_STOP)
+        S, self.V, self.dev = max_slots, vocab, device
+        z = lambda *sh, dt=torch.int32: torch.zeros(*sh, dtype=dt, device=device)  # noqa: E731
+        self.f32 = z(S, 8, dt=torch.float32)
+        self.i32 = z(S, 8)
+        self.n_gen = z(S)
+        self.seed = z(S, dt=torch.int64)
+        self.cnt = z(0)
+        self.seen = z(0)
+        self.bias_tok = z(S, self.MAXB)
+        self.bias_val = z(S, self.MAXB, dt=torch.float32)
+        self.stop_ids = z(S, self.MAXS)
+        self.free = list(range(S - 1, -1, -1))
+        self.of: Dict[int, int] = {}            # seq id -> slot
+        self.pen_of: Dict[int, int] = {}        # slot -> penalty row
+        self.pen_free: List[int] = []
+        self._pin_info = [torch.empty(1 << 14, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._pk = 0
+        self.uploads = 0
+
+    def tables(self) -> List[torch.Tensor]:
+        return [self.f32, self.i32, self.n_gen, self.seed, self.cnt, self.seen, self.bias_tok, self.bias_val,
+                self.stop_ids]
+
+    def fits(self, row: SampleRow) -> bool:
+        p = row.params
+        return (len(p.logit_bias) <= self.MAXB and len(row.eos_ids) + len(p.stop_token_ids) <= self.MAXS)
+
+    def release(self, seq_id: int) -> None:
+        slot = self.of.pop(seq_id, None)
+        if slot is None:
+            return
+        pr = self.pen_of.pop(slot, None)
+        if pr is not None:
+            self.pen_free.append(pr)
+        self.free.append(slot)
+
+    def _pen_row(self, slot: int) -> int:
+        if self.cnt.numel() == 0:
+            P = self.f32.shape[0]
+            self.cnt = torch.zeros(P, (self.V + 1) // 2, dtype=torch.int32, device=self.dev)
+            self.seen = torch.zeros(P, (self.V + 31) // 32, dtype=torch.int32, device=self.dev)
+            self.pen_free = list(range(P - 1, -1, -1))
+        pr = self.pen_free.pop()
+        self.pen_of[slot] = pr
+        return pr
+
+    def row_info(self, rows: List[SampleRow]) -> torch.Tensor:
+        """Slot of every row (assigning and uploading new ones); returns the device int32
+        row-info vector for `ops.sample_slots`."""
+        R = len(rows)
+        info = np.empty(R, dtype=np.int32)
+        new: List[Tuple[int, SampleRow]] = []
+        for i, r in enumerate(rows):
+            key = r.seq.seq_id
+            slot = self.of.get(key)
+            if slot is None:
+                if not self.free:
+                    raise RuntimeError("no free sampling slot (more live sequences than slots)")
+                slot = self.free.pop()
+                self.of[key] = slot
+                new.append((slot, r))
+            info[i] = slot | (r.sub << 16)
+        if new:
+            self._upload(new)
+        buf = self._pin_info[self._pk]
+        self._pk ^= 1
+        if R > buf.numel():
+            raise ValueError("too many sample rows for the row-info buffer")
+        buf[:R].copy_(torch.from_numpy(info))
+        return buf[:R].to(self.dev, non_blocking=True)
+
+    def _upload(self, new: List[Tuple[int, SampleRow]]) -> None:
+        n = len(new)
+        B, S = self.MAXB, self.MAXS
+        slot = np.empty(n, dtype=np.int32)
+        f32 = np.zeros((n, 8), dtype=np.float32)
+        i32 = np.zeros((n, 8), dtype=np.int32)
+        n_gen = np.empty(n, dtype=np.int32)
+        seed = np.empty(n, dtype=np.int64)
+        btok = np.zeros((n, B), dtype=np.int32)
+        bval = np.zeros((n, B), dtype=np.float32)
+        stops = np.zeros((n, S), dtype=np.int32)
+        off = [0]
+        toks: List[int] = []
+        for i, (sl, r) in enumerate(new):
+            p = r.params
+            slot[i] = sl
+            f32[i, :6] = (0.0 if p.is_greedy else p.temperature, p.top_p, p.min_p, p.repetition_penalty,
+                          p.frequency_penalty, p.presence_penalty)
+            pen = self._pen_row(sl) if p.has_penalties() else -1
+            st = list(r.eos_ids) + list(p.stop_token_ids)
+            i32[i, :5] = (p.top_k, p.min_tokens, pen, len(p.logit_bias), len(st))
+            n_gen[i] = r.offset
+            seed[i] = (r.seed - 7919 * r.sub) & ((1 << 63) - 1)    # the row adds 7919 * sub back
+            if p.logit_bias:
+                btok[i, :len(p.logit_bias)] = list(p.logit_bias.keys())
+                bval[i, :len(p.logit_bias)] = list(p.logit_bias.values())
+            if st:
+                stops[i, :len(st)] = st
+            if pen >= 0:
+                toks += list(r.prompt_ids)
+                off.append(len(toks))
+                toks += list(r.output_ids)
+                off.append(len(toks))
+            else:
+                off += [len(toks), len(toks)]
+        d = lambda a: torch.from_numpy(a).pin_memory().to(self.dev, non_blocking=True)  # noqa: E731
+        tk = d(np.asarray(toks if toks else [0], dtype=np.int32))
+        ops.cuda_ext().sample_slot_init(self.tables(), n, self.V, d(slot), d(f32), d(i32), d(n_gen), d(seed),
+                                        d(btok), d(bval), d(stops), d(np.asarray(off, dtype=np.int32)), tk)
+        ops.add_launches(1)
+        self.uploads += n
 
 
 @dataclass
@@ -104,11 +251,32 @@ class Sampler:
     # ------------------------------------------------------------------ asynchronous entry
     @staticmethod
     def async_eligible(params: SamplingParams) -> bool:
-        """Rows whose sampling runs entirely in the GPU kernel with nothing to
-        read back but (token, logprob): no penalties / logit bias / min_tokens
-        masks (they index with host lists), no host samplers, no top logprobs."""
-        return (not params.has_penalties() and not params.logit_bias and not params.min_tokens
-                and not params.needs_host_sampling() and params.logprobs is None)
+        """Rows whose sampling runs entirely in the GPU kernel with nothing to read back
+        but (token, logprob): penalties, logit bias (up to the slot table's 320 entries)
+        and min_tokens (up to 32 stop ids with EOS) live in the device slot tables; host
+        samplers and top logprobs do not."""
+        return (not params.needs_host_sampling() and params.logprobs is None
+                and len(params.logit_bias) <= 320 and len(params.stop_token_ids) <= 48)
+
+    def slots(self, device, max_slots: int) -> SlotTable:
+        if getattr(self, "_slots", None) is None:
+            self._slots = SlotTable(max_slots, self.vocab_size, device)
+        return self._slots
+
+    def release(self, seq_id: int) -> None:
+        """A sequence finished, was aborted or preempted: its device slot is free."""
+        st = getattr(self, "_slots", None)
+        if st is not None:
+            st.release(seq_id)
+
+    def _drop_slots(self) -> None:
+        """A synchronous step samples with host-built parameters and advances no slot
+        counters: every slot is released, so the next pipelined step re-uploads fresh
+        state (generated counts, penalty histories) for the sequences it samples."""
+        st = getattr(self, "_slots", None)
+        if st is not None and st.of:
+            for k in list(st.of):
+                st.release(k)
 
     def launch(self, logits: torch.Tensor, rows: List[SampleRow]) -> "AsyncSample":
         """Enqueues the sampling kernel and the copy of its results into pinned
@@ -119,7 +287,14 @@ class Sampler:
             # CPU engines (tests of the pipelined schedule): sample now, hand back the same handle
             res = self.sample(logits, rows)
             return AsyncSample(torch.tensor(res.tokens, dtype=torch.int64), None, R, None, res)
-        toks, lp = self._sample_device_async(logits, rows)
+        with OP_TIMER.section("sample"):
+            st = self.slots(logits.device, self.max_slots) if getattr(self, "max_slots", 0) else None
+            if st is not None and all(r.seq is not None and st.fits(r) for r in rows):
+                info = st.row_info(rows)
+                self.last_h2d_bytes += 4 * R
+                toks, lp = ops.sample_slots(logits, info, st.tables())
+            else:
+                toks, lp = self._sample_device_async(logits, rows)
         # every host staging buffer is 1-D and only used through contiguous
         # prefixes: a strided pinned slice would make torch stage the copy
         # through a blocking temporary
@@ -180,6 +355,7 @@ class Sampler:
         assert R == len(rows)
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
+        self._drop_slots()
         logits = self._process_logits(logits, rows)
         host_rows = [i for i, r in enumerate(rows) if r.params.needs_host_sampling()]
         tokens: List[int] = [0] * R
@@ -188,7 +364,8 @@ class Sampler:
         dev_rows = [i for i in range(R) if i not in set(host_rows)] if host_rows else list(range(R))
         if dev_rows:
             sub = logits if len(dev_rows) == R else logits[dev_rows]
-            t, lp = self._sample_device(sub, [rows[i] for i in dev_rows])
+            with OP_TIMER.section("sample"):
+                t, lp = self._sample_device(sub, [rows[i] for i in dev_rows])
             for j, i in enumerate(dev_rows):
                 tokens[i] = t[j]
                 lps[i] = lp[j]

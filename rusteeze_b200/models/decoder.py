@@ -35,6 +35,7 @@ import torch
 import torch.nn as nn
 
 from rusteeze_b200 import ops
+from rusteeze_b200.utils.op_timer import OP_TIMER
 from rusteeze_b200.core.types import ModelArchitecture
 from rusteeze_b200.models.config import ModelConfig
 from rusteeze_b200.ops import reference as ref
@@ -227,50 +228,74 @@ class DecoderLM(nn.Module):
         cfg = self.cfg
         eps, off = cfg.rms_norm_eps, cfg.norm_offset
         D = cfg.head_dim
-        h = self.embed_tokens(input_ids)
+        sec = OP_TIMER.section
+        with sec("embed"):
+            h = self.embed_tokens(input_ids)
         residual = None
         # MXFP8 weights: the norms emit the GEMM operand (e4m3 + UE8M0 scales) directly
         mx = h.is_cuda and getattr(self, "fp8_format", None) == "ue8m0" and not self.is_gemma2
         for li, L in enumerate(self.layers):
             kv = kv_caches[li]
             if mx:
-                if residual is None:
-                    residual = h
-                    xq = ops.rms_norm_mxf8(h, L.input_norm, eps, off)
-                else:
-                    xq = ops.rms_norm_mxf8(h, L.input_norm, eps, off, residual=residual)
-                qkv = ops.linear_mxf8_q(*xq, L.qkv_q, L.qkv_sf, L.qkv_bias)
+                with sec("norm_ag"):
+                    if residual is None:
+                        residual = h
+                        xq = ops.rms_norm_mxf8(h, L.input_norm, eps, off)
+                    else:
+                        xq = ops.rms_norm_mxf8(h, L.input_norm, eps, off, residual=residual)
+                with sec("qkv_gemm"):
+                    qkv = ops.linear_mxf8_q(*xq, L.qkv_q, L.qkv_sf, L.qkv_bias)
             else:
-                if residual is None:
-                    residual = h
-                    x = ops.rms_norm(h, L.input_norm, eps, off)
-                else:
-                    x, residual = ops.fused_add_rms_norm(h, residual, L.input_norm, eps, off)
-                qkv = self._lin(x, L, "qkv", L.qkv_bias)
-            q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
-                                   self.hq, self.hkv, D)
-            a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
-                                    cfg.attn_logit_softcapping)
-            h = self._row_parallel(a.view(a.shape[0], -1), L, "o")
+                with sec("norm_ag"):
+                    if residual is None:
+                        residual = h
+                        x = ops.rms_norm(h, L.input_norm, eps, off)
+                    else:
+                        x, residual = ops.fused_add_rms_norm(h, residual, L.input_norm, eps, off)
+                with sec("qkv_gemm"):
+                    qkv = self._lin(x, L, "qkv", L.qkv_bias)
+            with sec("rope_kv"):
+                q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
+                                       self.hq, self.hkv, D)
+            with sec("attention"):
+                a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
+                                        cfg.attn_logit_softcapping)
+            with sec("o_gemm_rs"):
+                h = self._row_parallel(a.view(a.shape[0], -1), L, "o")
             if self.is_gemma2:
-                h = ops.rms_norm(h, L.post_attn_norm, eps, off)
-                x, residual = ops.fused_add_rms_norm(h, residual, L.pre_ff_norm, eps, off)
-                h = self._mlp(L, x)
-                h = ops.rms_norm(h, L.post_ff_norm, eps, off)
+                with sec("norm_ag"):
+                    h = ops.rms_norm(h, L.post_attn_norm, eps, off)
+                    x, residual = ops.fused_add_rms_norm(h, residual, L.pre_ff_norm, eps, off)
+                with sec("down_gemm_rs"):
+                    h = self._mlp(L, x)
+                with sec("norm_ag"):
+                    h = ops.rms_norm(h, L.post_ff_norm, eps, off)
                 continue
             if mx and not cfg.is_moe:
-                xq = ops.rms_norm_mxf8(h, L.post_attn_norm, eps, off, residual=residual)
+                with sec("norm_ag"):
+                    xq = ops.rms_norm_mxf8(h, L.post_attn_norm, eps, off, residual=residual)
                 if L.gate_up_q.shape[0] % 256 == 0:
                     # the SiLU epilogue emits the down projection's fp8 operand directly
-                    aq = ops.linear_mxf8_silu_q(*xq, L.gate_up_q, L.gate_up_sf)
-                    h = self.tp.all_reduce(ops.linear_mxf8_q(*aq, L.down_q, L.down_sf))
+                    with sec("gate_up_gemm"):
+                        aq = ops.linear_mxf8_silu_q(*xq, L.gate_up_q, L.gate_up_sf)
+                    with sec("down_gemm_rs"):
+                        h = self.tp.all_reduce(ops.linear_mxf8_q(*aq, L.down_q, L.down_sf))
                 else:
-                    a = ops.linear_mxf8_q(*xq, L.gate_up_q, L.gate_up_sf, silu_mul=True)
-                    h = self._row_parallel(a, L, "down")
+                    with sec("gate_up_gemm"):
+                        a = ops.linear_mxf8_q(*xq, L.gate_up_q, L.gate_up_sf, silu_mul=True)
+                    with sec("down_gemm_rs"):
+                        h = self._row_parallel(a, L, "down")
                 continue
-            x, residual = ops.fused_add_rms_norm(h, residual, L.post_attn_norm, eps, off)
-            h = self._moe(L, x) if cfg.is_moe else self._mlp(L, x)
-        h, _ = ops.fused_add_rms_norm(h, residual, self.norm, eps, off)
+            with sec("norm_ag"):
+                x, residual = ops.fused_add_rms_norm(h, residual, L.post_attn_norm, eps, off)
+            if cfg.is_moe:
+                with sec("moe"):
+                    h = self._moe(L, x)
+            else:
+                with sec("down_gemm_rs"):
+                    h = self._mlp(L, x)
+        with sec("final_norm"):
+            h, _ = ops.fused_add_rms_norm(h, residual, self.norm, eps, off)
         return h
 
     def _fused_tp_ok(self, M: int) -> bool:
@@ -305,51 +330,72 @@ class DecoderLM(nn.Module):
         cfg = self.cfg
         eps, off = cfg.rms_norm_eps, cfg.norm_offset
         D = cfg.head_dim
-        h = self.embed_tokens(input_ids)
+        sec = OP_TIMER.section
+        with sec("embed"):
+            h = self.embed_tokens(input_ids)
         M = h.shape[0]
         # MXFP8 weights: every boundary but the last all-gathers the e4m3 operand + scales
         mx = bool(getattr(self, "fp8", False))
-        x = F.start(h, self.layers[0].input_norm, eps, off, mx=mx)
+        with sec("norm_ag"):
+            x = F.start(h, self.layers[0].input_norm, eps, off, mx=mx)
         n = len(self.layers)
         for li, L in enumerate(self.layers):
             kv = kv_caches[li]
             c_attn, c_mlp = 2 * li + 1, 2 * li + 2
-            if mx:
-                qkv = F.gemm_ag_mx(x, L.qkv_q, L.qkv_sf, 2 * li, L.qkv_bias)
-            else:
-                qkv = F.gemm_ag(x, L.qkv, 2 * li, L.qkv_bias)
-            q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
-                                   self.hq, self.hkv, D)
-            a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
-                                    cfg.attn_logit_softcapping)
-            if mx:
-                F.gemm_rs_mx(*ops.quant_mxf8_act(a.view(M, -1)), L.o_q, L.o_sf, c_attn)
-            else:
-                F.gemm_rs(a.view(M, -1), L.o, c_attn)
-            x = F.rs_norm_ag(M, L.post_attn_norm, eps, off, c_attn, mx=mx)
+            with sec("qkv_gemm"):
+                if mx:
+                    qkv = F.gemm_ag_mx(x, L.qkv_q, L.qkv_sf, 2 * li, L.qkv_bias)
+                else:
+                    qkv = F.gemm_ag(x, L.qkv, 2 * li, L.qkv_bias)
+            with sec("rope_kv"):
+                q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
+                                       self.hq, self.hkv, D)
+            with sec("attention"):
+                a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
+                                        cfg.attn_logit_softcapping)
+            with sec("o_gemm_rs"):
+                if mx:
+                    F.gemm_rs_mx(*ops.quant_mxf8_act(a.view(M, -1)), L.o_q, L.o_sf, c_attn)
+                else:
+                    F.gemm_rs(a.view(M, -1), L.o, c_attn)
+            with sec("norm_ag"):
+                x = F.rs_norm_ag(M, L.post_attn_norm, eps, off, c_attn, mx=mx)
             nw = self.layers[li + 1].input_norm if li + 1 < n else self.norm
             if cfg.is_moe:
                 k = cfg.num_experts_per_tok
-                F.moe(x, L.router, L.w13_il, L.w2, k, self.e_lo, c_attn, c_mlp)
-                x = F.rs_norm_ag(M, nw, eps, off, c_mlp, moe_topk=k)
+                with sec("moe"):
+                    F.moe(x, L.router, L.w13_il, L.w2, k, self.e_lo, c_attn, c_mlp)
+                with sec("norm_ag"):
+                    x = F.rs_norm_ag(M, nw, eps, off, c_mlp, moe_topk=k)
                 continue
             if mx:
                 # the gate/up epilogue emits the down projection's operand; the final norm
                 # all-gathers bf16 rows for the LM head
-                F.gemm_rs_mx(*F.gemm_ag_mx(x, L.gate_up_q, L.gate_up_sf, c_attn, silu_q=True),
-                             L.down_q, L.down_sf, c_mlp)
-                x = F.rs_norm_ag(M, nw, eps, off, c_mlp, mx=li + 1 < n)
+                with sec("gate_up_gemm"):
+                    aq = F.gemm_ag_mx(x, L.gate_up_q, L.gate_up_sf, c_attn, silu_q=True)
+                with sec("down_gemm_rs"):
+                    F.gemm_rs_mx(*aq, L.down_q, L.down_sf, c_mlp)
+                with sec("norm_ag"):
+                    x = F.rs_norm_ag(M, nw, eps, off, c_mlp, mx=li + 1 < n)
                 continue
-            act = F.gemm_ag(x, L.gate_up_il, c_attn, silu_mul=True)
-            F.gemm_rs(act, L.down, c_mlp)
-            x = F.rs_norm_ag(M, nw, eps, off, c_mlp)
+            with sec("gate_up_gemm"):
+                act = F.gemm_ag(x, L.gate_up_il, c_attn, silu_mul=True)
+            with sec("down_gemm_rs"):
+                F.gemm_rs(act, L.down, c_mlp)
+            with sec("norm_ag"):
+                x = F.rs_norm_ag(M, nw, eps, off, c_mlp)
         # the LM head reads every owner's final rows from the local gather buffer
-        F.wait_gathered(M, 2 * n)
-        F.end_step()
+        with sec("final_norm"):
+            F.wait_gathered(M, 2 * n)
+            F.end_step()
         return x
 
     def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
         """h [n, H] -> fp32 logits [n, vocab] (gathered over TP ranks)."""
+        with OP_TIMER.section("lm_head"):
+            return self._compute_logits(h)
+
+    def _compute_logits(self, h: torch.Tensor) -> torch.Tensor:
         if getattr(self, "lm_head_q", None) is not None:
             logits = ops.linear_fp8(h, self.lm_head_q, self.lm_head_s, wsf=getattr(self, "lm_head_sf", None))
         else:

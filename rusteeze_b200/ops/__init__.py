@@ -338,9 +338,36 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
     tokens = torch.empty(B, dtype=torch.int64, device=logits.device)
     lp = torch.empty(B, dtype=torch.float32, device=logits.device)
     if greedy_all:
-        C.argmax_sample(tokens, lp, logits, bool(want_logprobs))
+        z = _greedy_params(B, logits.device)
+        C.sample_rows(tokens, lp, logits, *z)
     else:
-        C.topk_topp_sample(tokens, lp, logits, temperature, top_k, top_p, min_p, seeds, offsets,
-                           bool(want_logprobs))
+        C.sample_rows(tokens, lp, logits, temperature, top_k, top_p, min_p, seeds, offsets)
+    _LAUNCHES[0] += 1
+    return tokens, lp
+
+
+_GREEDY: dict = {}
+
+
+def _greedy_params(B: int, device) -> tuple:
+    """Per-row parameter vectors of an all-greedy batch (temperature 0), cached by size."""
+    key = (B, str(device))
+    z = _GREEDY.get(key)
+    if z is None:
+        f = torch.zeros(B, dtype=torch.float32, device=device)
+        i = torch.zeros(B, dtype=torch.int32, device=device)
+        l = torch.zeros(B, dtype=torch.int64, device=device)
+        z = _GREEDY[key] = (f, i, f, f, l, l)
+    return z
+
+
+def sample_slots(logits: torch.Tensor, row_info: torch.Tensor, tables) -> tuple:
+    """Samples every row with the parameters of its device slot (`engine.sampler.SlotTable`):
+    penalties, logit bias and min_tokens applied in the kernel, which then advances the
+    slot's generated-token counter and penalty counts.  Returns (ids int64 [R], logprob fp32 [R])."""
+    B = logits.shape[0]
+    tokens = torch.empty(B, dtype=torch.int64, device=logits.device)
+    lp = torch.empty(B, dtype=torch.float32, device=logits.device)
+    cuda_ext().sample_slots(tokens, lp, logits, row_info, list(tables))
     _LAUNCHES[0] += 1
     return tokens, lp

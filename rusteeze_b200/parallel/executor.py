@@ -167,7 +167,7 @@ class TPExecutor:
         self.ch.publish(MSG_STEP, {"arrays": n_rows, **_staged_plan(r, meta, T, S)})
         return r.forward_staged(meta, T, n_rows)
 
-    def timer(self, kind: str) -> Optional[float]:
+    def timer(self, kind: str):
         """Device-timed window over every rank: "start" marks it on each rank's stream,
         "stop" returns its length in ms, the MAX over ranks (one all-reduce that the
         workers join when they consume the stop message, after their last step)."""
@@ -194,11 +194,25 @@ def _staged_plan(r: ModelRunner, meta, T: int, S: int) -> dict:
     }
 
 
-def _timer_mark(runner: ModelRunner, kind: str, state: dict) -> Optional[float]:
+def _timer_mark(runner: ModelRunner, kind: str, state: dict):
     """One rank's side of `TPExecutor.timer`: CUDA events on the runner's stream (host
-    clock on CPU ranks); "stop" all-reduces the elapsed ms with MAX over ranks."""
+    clock on CPU ranks); "stop" all-reduces the elapsed ms with MAX over ranks.
+    "ops_start" / "ops_stop" switch the per-section op timer on every rank; "ops_stop"
+    returns ms per section, the MAX over ranks."""
     import torch.distributed as dist
+    from rusteeze_b200.utils.op_timer import OP_TIMER, SECTIONS
     cuda = runner.is_cuda
+    if kind == "ops_start":
+        OP_TIMER.start()
+        return None
+    if kind == "ops_stop":
+        OP_TIMER.stop()
+        rep = OP_TIMER.report() if cuda else {}
+        t = torch.tensor([rep.get(k, 0.0) for k in SECTIONS], dtype=torch.float64,
+                         device=torch.cuda.current_device() if cuda else "cpu")
+        if dist.is_initialized() and dist.get_world_size() > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return dict(zip(SECTIONS, t.tolist()))
     if kind == "start":
         if cuda:
             state["ev0"] = torch.cuda.Event(enable_timing=True)

@@ -8,8 +8,7 @@ L2 where the op is memory-bound (weights / KV caches), and the achieved
 rate divided by the measured peaks in MEASURED_PEAKS.json (HBM copy GB/s and
 cuBLAS bf16 TFLOP/s) when present.  cuBLAS (torch.matmul) is timed on the
 same shapes as the library baseline for the GEMM.  GEMM rows report the tile plan
-(bn, k_splits) and the tail split in effect: compare a run with RZ_GEMM_TAIL_SPLIT=1
-against one without to see what splitting a thin last wave buys at each shape.
+(bn, k_splits).
 """
 from __future__ import annotations
 
@@ -79,10 +78,7 @@ def bench_gemm(pk, shapes=None) -> List[dict]:
         bytes_ = (N * K + M * K + M * N) * 2
         C = ops.cuda_ext()
         plan = C.gemm_plan(M, N, K, 0)
-        tail = C.gemm_tail_plan(M, N, (K + 63) // 64, plan[0], 0)[0] if (C.gemm_tail_split_enabled() and
-                                                                        plan[1] == 1) else 1
         out.append({"kernel": "gemm_bf16_tcgen05", "M": M, "N": N, "K": K, "bn": plan[0], "k_splits": plan[1],
-                    "tail_split": tail,
                     "ms": round(t, 4), "tflops": round(flops / t / 1e9, 1),
                     "frac_of_measured_bf16": round(flops / t / 1e9 / pk["bf16_tflops"], 3),
                     "gbs": round(bytes_ / t / 1e6, 1), "frac_of_measured_hbm": round(bytes_ / t / 1e6 / pk["hbm_gbs"], 3),
@@ -143,10 +139,7 @@ def bench_gemm_mxf8(pk, shapes=None, bns=(0, 128, 256)) -> List[dict]:
             flops = 2.0 * M * N * K
             bytes_ = N * K + M * K * 2 + M * N * 2
             plan = list(C.gemm_plan_mxf8(M, N, K, 0)) if bn == 0 else [bn, 1]
-            tail = C.gemm_tail_plan(M, N, K // 128, plan[0], 0)[0] if (C.gemm_tail_split_enabled() and
-                                                                       plan[1] == 1) else 1
             out.append({"kernel": "gemm_mxf8_tcgen05", "M": M, "N": N, "K": K, "bn": plan[0], "k_splits": plan[1],
-                        "tail_split": tail,
                         "ms": round(t, 4), "tflops": round(flops / t / 1e9, 1), "gbs": round(bytes_ / t / 1e6, 1),
                         "frac_of_measured_hbm": round(bytes_ / t / 1e6 / pk["hbm_gbs"], 3)})
         del ws
@@ -223,17 +216,31 @@ def bench_norm(pk) -> List[dict]:
 
 
 def bench_sample(pk) -> List[dict]:
+    """Cluster sampler, top-p 0.9 at T 0.7 and greedy, fp32 and bf16 logits.  Four logit
+    buffers are used in turn, so every launch reads its rows from DRAM (L2 is 126 MB)."""
     out = []
-    for B in (1, 64, 256):
-        V = 128256
-        logits = torch.randn(B, V, device="cuda")
-        f = lambda v, dt: torch.full((B,), v, dtype=dt, device="cuda")  # noqa: E731
-        args = (f(0.7, torch.float32), f(-1, torch.int32), f(0.9, torch.float32), f(0.0, torch.float32),
-                torch.arange(B, device="cuda"), f(0, torch.int64))
-        t = time_ms(lambda: ops.sample(logits, *args, greedy_all=False))
-        tg = time_ms(lambda: ops.sample(logits, None, None, None, None, None, None, greedy_all=True))
-        out.append({"kernel": "topk_topp_sample", "B": B, "V": V, "ms": round(t, 4), "argmax_ms": round(tg, 4),
-                    "gbs_per_pass": round(B * V * 4 / t / 1e6, 1)})
+    for dt in (torch.float32, torch.bfloat16):
+        for B in (1, 64, 256):
+            V = 128256
+            bufs = [(torch.randn(B, V, device="cuda") * 3).to(dt) for _ in range(4)]
+            f = lambda v, t: torch.full((B,), v, dtype=t, device="cuda")  # noqa: E731
+            args = (f(0.7, torch.float32), f(-1, torch.int32), f(0.9, torch.float32), f(0.0, torch.float32),
+                    torch.arange(B, device="cuda"), f(0, torch.int64))
+            it = [0]
+
+            def run(greedy):
+                it[0] += 1
+                x = bufs[it[0] % 4]
+                if greedy:
+                    ops.sample(x, None, None, None, None, None, None, greedy_all=True)
+                else:
+                    ops.sample(x, *args, greedy_all=False)
+            t = time_ms(lambda: run(False))
+            tg = time_ms(lambda: run(True))
+            nbytes = B * V * bufs[0].element_size()
+            out.append({"kernel": "sample_cluster", "dtype": str(dt).split(".")[-1], "B": B, "V": V,
+                        "ms": round(t, 4), "greedy_ms": round(tg, 4), "gbs": round(nbytes / t / 1e6, 1),
+                        "frac_of_measured_hbm": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
     return out
 
 

@@ -137,7 +137,7 @@ def _prefill():
                                                     D ** -0.5, 0, 0.0)
 
 
-@case("sample_topk_topp", "topk_topp_kernel")
+@case("sample_topk_topp", "sample_cluster_kernel")
 def _sample():
     B, V = 256, 128256
     logits = torch.randn(B, V, device="cuda") * 3
