@@ -2,7 +2,7 @@
 //
 // The row (bf16 or fp32, up to ~400K entries) is split over the 8 CTAs of a
 // cluster; each CTA reads its slice from HBM exactly once into shared memory,
-// and every later pass (penalties, max, normaliser, two histogram levels,
+// and every later pass (penalties, max, normaliser, the rejection rounds of
 // the draw) runs on shared memory.  The CTAs combine their partial results
 // through distributed shared memory (DSMEM) at cluster barriers, so a row
 // costs one HBM read instead of one per pass.  Semantics are those of the
@@ -16,28 +16,34 @@
 //   min_tokens the stop ids (EOS + stop_token_ids) are -inf while fewer than
 //              min_tokens tokens were generated;
 //   greedy     T <= 0 or top_k == 1: argmax, logprob from the raw softmax;
-//   otherwise  e = exp((x - max) / T) = p / p_max; keep the top-k, then the
-//              tokens whose preceding (un-renormalised) mass is < top_p, and
-//              e >= min_p; draw one token from the kept mass by inverse CDF with
-//              one uniform number from a counter-based Philox4x32-10 stream keyed
-//              by (seed, tokens generated so far).
+//   otherwise  e = exp((x - max) / T) = p / p_max; the kept set K holds the
+//              tokens t with fewer than k tokens strictly more likely, with the
+//              mass of strictly more likely tokens < top_p, and with e_t >=
+//              min_p (the most likely token is always kept); one token is drawn
+//              from K with probability proportional to e.
 //
-// The top-k / top-p threshold is found without a sort by radix selection on
-// the IEEE bits of e (a positive float's bit pattern orders like its value):
-// a 2048-bucket histogram of count and mass on bits [30:20] (exponent + 3
-// mantissa bits), then a second 2048-bucket level on bits [19:9] inside the
-// bucket where the running count or mass crosses the target.  Tokens whose
-// first 22 key bits tie with the boundary are kept or dropped together.  Every
-// token of a bucket shares its exponent, so a bucket's mass is accumulated as
-// an integer sum of 21-bit mantissas: lanes of a warp that hit the same bucket
-// are combined with one match and one integer warp reduction, and their
-// leader does one shared-memory add.
+// K is never materialised.  The draw is exact rejection sampling with a pivot
+// (no sort, no histogram): draw a candidate c from the tokens above the pivot
+// in proportion to e (inverse CDF with one uniform from a counter-based
+// Philox4x32-10 stream keyed by (seed, tokens generated so far, round)); one
+// pass then counts the tokens and the mass strictly above e_c.  If c meets
+// every rule it is in K and is returned: conditioned on acceptance it is
+// distributed like e over K.  Otherwise every token at or below e_c fails too
+// (the count and the mass above a token only grow as e falls), so the pivot
+// rises to e_c, and the mass just computed is the next round's total.  For
+// top-p at 0.9 the first candidate is accepted nine times in ten; top-k over a
+// flat distribution halves the candidate set per round in expectation.  A
+// round costs one pass over shared memory and two cluster barriers.
 //
-// The draw walks the kept mass in (thread, stride) order rather than token
-// order: thread t of a CTA owns tokens t, t + 512, ...; per-thread kept sums,
-// a CTA total per cluster rank, and one uniform u pick the CTA, then the
-// thread, then the token where the running mass crosses u times the total.
-// Any fixed order gives the same distribution.
+// The draw walks the mass in (thread, stride) order rather than token order:
+// thread t of a CTA owns tokens t, t + 512, ...; per-thread sums, a total per
+// cluster rank, and the uniform pick the CTA, the thread, then the token where
+// the running mass crosses u times the total.  Any fixed order gives the same
+// distribution.
+//
+// The returned logprob is that of the drawn token under the temperature-scaled
+// softmax over the whole vocabulary (log e_c - log sum e), the greedy one under
+// the raw softmax.
 //
 // Parameters come either from per-row arrays, or (slot mode) from
 // device-resident per-sequence tables indexed by a slot id per row: the host
@@ -59,7 +65,7 @@ namespace {
 
 constexpr int kCl = 8;        // CTAs per row (portable cluster size)
 constexpr int kThr = 512;     // threads per CTA
-constexpr int kHB = 2048;     // histogram buckets per level
+constexpr int kMaxRounds = 64; // rejection rounds before the most likely token is returned
 
 struct P4 {
   uint32_t x, y, z, w;
@@ -115,123 +121,34 @@ __device__ __forceinline__ float block_sum(float v, float* rv) {
   return warp_sum(v);
 }
 
-// Histogram add: lanes of a warp with the same bucket are combined (count by popcount,
-// mass as an integer sum of mantissas) and their leader adds once.  `mfx` is the token's
-// 21-bit mantissa with the implicit 1 (1.m * 2^20); a bucket's tokens share an exponent.
-__device__ __forceinline__ void hist_add(int* cnt, unsigned long long* mass, int b, uint32_t mfx) {
-  const unsigned grp = __match_any_sync(__activemask(), b);
-  const uint32_t tot = __reduce_add_sync(grp, mfx);
-  if ((threadIdx.x & 31) == __ffs(grp) - 1) {
-    atomicAdd(&cnt[b], __popc(grp));
-    atomicAdd(&mass[b], static_cast<unsigned long long>(tot));
-  }
-}
-__device__ __forceinline__ uint32_t mant_fx(uint32_t u) { return ((u & 0x7fffffu) >> 3) | (1u << 20); }
-
-// CTA 0 only: sums the cluster's histograms into its own, then warp 0 walks the buckets
-// from the largest key down and finds the first one where the running count reaches
-// k_target or the running mass reaches m_target.  `scale(b)` turns bucket b's integer
-// mass into e units.  Writes (bucket or -1, count before) and (mass before) to sel.
-template <typename Scale>
-__device__ void merge_and_scan(cg::cluster_group& cl, int* hcnt, unsigned long long* hm, float* hf, long k_target,
-                               float m_target, Scale scale, int* sel_i, float* sel_f) {
-  for (int b = threadIdx.x; b < kHB; b += kThr) {
-    int c = 0;
-    unsigned long long m = 0;
-#pragma unroll
-    for (int r = 0; r < kCl; ++r) {
-      c += *cl.map_shared_rank(hcnt + b, r);
-      m += *cl.map_shared_rank(hm + b, r);
-    }
-    hcnt[b] = c;
-    hf[b] = static_cast<float>(m) * scale(b);
-  }
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    constexpr int per = kHB / 32;
-    // lane l owns the descending-order range [l*per, (l+1)*per): bucket kHB-1-i
-    long c = 0;
-    float m = 0.f;
-    for (int i = 0; i < per; ++i) {
-      const int b = kHB - 1 - (lane * per + i);
-      c += hcnt[b];
-      m += hf[b];
-    }
-    long ci = c;
-    float mi = m;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const long oc = __shfl_up_sync(0xffffffffu, ci, o);
-      const float om = __shfl_up_sync(0xffffffffu, mi, o);
-      if (lane >= o) {
-        ci += oc;
-        mi += om;
-      }
-    }
-    const unsigned hit = __ballot_sync(0xffffffffu, ci >= k_target || mi >= m_target);
-    if (lane == 0) {
-      sel_i[0] = -1;
-      sel_i[1] = 0;
-      sel_f[0] = 0.f;
-    }
-    __syncwarp();
-    if (hit) {
-      const int first = __ffs(hit) - 1;
-      if (lane == first) {
-        long cc = ci - c;
-        float mm = mi - m;
-        int bsel = kHB - 1 - (lane * per + per - 1);
-        for (int i = 0; i < per; ++i) {
-          const int b = kHB - 1 - (lane * per + i);
-          // the lane total said the target is reached in this range; rounding of the
-          // per-bucket sums may differ, so the range's last bucket is the fallback
-          if (cc + hcnt[b] >= k_target || mm + hf[b] >= m_target || i == per - 1) {
-            bsel = b;
-            break;
-          }
-          cc += hcnt[b];
-          mm += hf[b];
-        }
-        sel_i[0] = bsel;
-        sel_i[1] = static_cast<int>(cc);
-        sel_f[0] = mm;
-      }
-    }
-  }
-  __syncthreads();
-}
-
 template <bool BF16>
 __device__ __forceinline__ float load1(const void* row, int64_t i) {
   if (BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(row)[i]);
   return static_cast<const float*>(row)[i];
 }
 
-// 2^k for an integer exponent (the mass scale of a histogram bucket)
-__device__ __forceinline__ float pow2i(int k) { return ldexpf(1.f, k); }
-
 }  // namespace
 
 template <bool BF16, bool SLOTS>
-__global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kThr) sample_cluster_kernel(SampleClusterArgs a) {
+__global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kThr, 3) sample_cluster_kernel(SampleClusterArgs a) {
   cg::cluster_group cl = cg::this_cluster();
   const int cr = static_cast<int>(cl.block_rank());
   const int row = blockIdx.x / kCl;
   const int tid = threadIdx.x;
   extern __shared__ __align__(16) float xs[];
-  __shared__ int hcnt[kHB];
-  __shared__ unsigned long long hm[kHB];
-  __shared__ float hf[kHB];
   __shared__ float tsum[kThr];
   __shared__ float rv[32];
   __shared__ int ri[32];
-  // per-CTA partial results that the other CTAs read through DSMEM
-  __shared__ float c_max, c_sum, c_kept;
+  __shared__ float wsum[kThr / 32];
+  // per-CTA partial results that the other CTAs read through DSMEM (double-buffered by
+  // round parity, so a round's values are never overwritten while a peer may read them)
+  __shared__ float c_max, c_sum;
   __shared__ int c_arg;
-  // CTA 0's threshold selections (one set per level), read by every CTA
-  __shared__ int sel_i[2][2];
-  __shared__ float sel_f[2][1];
+  __shared__ float c_mass[2];
+  __shared__ int c_cnt[2];
+  __shared__ float cand_e[2];
+  __shared__ int cand_t[2];
+  __shared__ int last_t;
 
   // ---------------------------------------------------------------- parameters
   float T, top_p, min_p, rep = 1.f, freq = 0.f, pres = 0.f;
@@ -365,6 +282,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kThr) sample_clust
       xs[i] = e;
       z += e;
     }
+    tsum[tid] = z;
   }
   z = block_sum(z, rv);
   if (tid == 0) c_sum = z;
@@ -393,154 +311,135 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kThr) sample_clust
     return;
   }
 
-  // ---------------------------------------------------------------- 4. top-k / top-p threshold (radix select on e)
+  // ---------------------------------------------------------------- 4. rejection rounds with a rising pivot
+  // tsum holds each thread's mass above the pivot (initially all of it: the Z partials)
   const int k = top_k > 0 ? min(top_k, V) : V;
-  const bool trunc = k < V || top_p < 1.f;
-  int kb1 = -1, kb2 = 0;   // kept: key1 > kb1, or key1 == kb1 and key2 >= kb2 (kb1 < 0: all)
-  if (trunc) {
-    const float m_target = top_p < 1.f ? top_p * Z : INFINITY;
-    for (int b = tid; b < kHB; b += kThr) {
-      hcnt[b] = 0;
-      hm[b] = 0ull;
-    }
-    __syncthreads();
-    for (int i = tid; i < n; i += kThr) {
-      const uint32_t u = __float_as_uint(xs[i]);
-      if (u >= 0x00800000u) hist_add(hcnt, hm, static_cast<int>(u >> 20), mant_fx(u));   // normal e > 0
-    }
-    __syncthreads();
-    cl.sync();
-    // bucket b holds exponent b >> 3: mass = sum(1.m * 2^20) * 2^(E - 127 - 20)
-    if (cr == 0)
-      merge_and_scan(cl, hcnt, hm, hf, k, m_target, [](int b) { return pow2i((b >> 3) - 147); }, sel_i[0],
-                     sel_f[0]);
-    cl.sync();
-    const int b1 = *cl.map_shared_rank(&sel_i[0][0], 0);
-    const long cb = *cl.map_shared_rank(&sel_i[0][1], 0);
-    const float mb = *cl.map_shared_rank(&sel_f[0][0], 0);
-    if (b1 >= 0) {
-      for (int b = tid; b < kHB; b += kThr) {
-        hcnt[b] = 0;
-        hm[b] = 0ull;
-      }
-      __syncthreads();
-      for (int i = tid; i < n; i += kThr) {
-        const uint32_t u = __float_as_uint(xs[i]);
-        if (static_cast<int>(u >> 20) == b1) hist_add(hcnt, hm, static_cast<int>((u >> 9) & 0x7ffu), mant_fx(u));
-      }
-      __syncthreads();
-      cl.sync();
-      const float sc = pow2i((b1 >> 3) - 147);
-      if (cr == 0)
-        merge_and_scan(cl, hcnt, hm, hf, k - cb, m_target - mb, [sc](int) { return sc; }, sel_i[1], sel_f[1]);
-      cl.sync();
-      const int b2 = *cl.map_shared_rank(&sel_i[1][0], 0);
-      kb1 = b1;
-      kb2 = b2 < 0 ? 0 : b2;
-    }
-  }
-
-  // ---------------------------------------------------------------- 5. draw by inverse CDF over the kept mass
-  auto kept_e = [&](int i) -> float {
-    const float e = xs[i];
-    const uint32_t u = __float_as_uint(e);
-    bool keep = e > 0.f;
-    if (kb1 >= 0) {
-      const int key1 = static_cast<int>(u >> 20);
-      keep = keep && (key1 > kb1 || (key1 == kb1 && static_cast<int>((u >> 9) & 0x7ffu) >= kb2));
-    }
-    keep = (keep && e >= min_p) || e == 1.f;   // the most likely token is always kept
-    return keep ? e : 0.f;
-  };
-  float ts = 0.f;
-  for (int i = tid; i < n; i += kThr) ts += kept_e(i);
-  tsum[tid] = ts;
-  const float kept = block_sum(ts, rv);   // starts with a barrier: tsum is complete after it
-  if (tid == 0) {
-    c_kept = kept;
-    c_arg = arg;                           // replaced by the drawn token in the owning CTA
-    if (cr == 0) {
-      a.tok[row] = arg;                    // (nothing kept at all: the argmax stands)
-      a.lp[row] = 0.f;
-    }
-  }
-  cl.sync();
+  const float pZ = top_p < 1.f ? top_p * Z : INFINITY;
   float ctot[kCl];
-  float total = 0.f;
 #pragma unroll
-  for (int r = 0; r < kCl; ++r) {
-    ctot[r] = *cl.map_shared_rank(&c_kept, r);
-    total += ctot[r];
-  }
-  // one uniform per row and step
-  const P4 rnd = philox10(P4{0x53414D50u, static_cast<uint32_t>(off), static_cast<uint32_t>(off >> 32), 0x5A4D504Cu},
-                          static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
-  const float target = unit_open(rnd.x) * total;
-  // the CTA whose running total crosses the target (the last CTA with mass takes rounding)
-  int owner = -1, last = -1;
-  float before = 0.f, acc = 0.f;
+  for (int r = 0; r < kCl; ++r) ctot[r] = *cl.map_shared_rank(&c_sum, r);
+  float pivot = -1.f;       // candidates: e > pivot
+  float total = Z;
+  int tok = arg;
+  float etok = 1.f;
+  for (int round = 0; round < kMaxRounds; ++round) {
+    const int par = round & 1;
+    // -- draw a candidate above the pivot: the CTA, then the thread, then the token
+    const P4 rnd = philox10(P4{static_cast<uint32_t>(round), static_cast<uint32_t>(off),
+                               static_cast<uint32_t>(off >> 32), 0x5A4D504Cu},
+                            static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
+    const float target = unit_open(rnd.x) * total;
+    int owner = -1, last = -1;
+    float before = 0.f, acc = 0.f;
 #pragma unroll
-  for (int r = 0; r < kCl; ++r) {
-    if (ctot[r] > 0.f) {
-      last = r;
-      if (owner < 0 && acc + ctot[r] > target) {
-        owner = r;
-        before = acc;
-      }
-    }
-    acc += ctot[r];
-  }
-  if (owner < 0 && last >= 0) {
-    owner = last;
-    before = acc - ctot[last];
-  }
-  if (owner < 0) owner = 0;                    // nothing kept: the argmax below
-  if (cr == owner) {
-    // inclusive prefix of the per-thread sums in thread order; thread i's range is
-    // [P(i-1), P(i)) with P(i-1) taken from its neighbour, so ranges neither overlap nor gap
-    __shared__ float wsum[kThr / 32];
-    __shared__ int last_t;
-    const int w = tid >> 5, l = tid & 31;
-    const float mine_sum = tsum[tid];
-    if (tid == 0) last_t = -1;
-    float v = mine_sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float t = __shfl_up_sync(0xffffffffu, v, o);
-      if (l >= o) v += t;
-    }
-    const float prev_in_warp = __shfl_up_sync(0xffffffffu, v, 1);
-    if (l == 31) wsum[w] = v;
-    __syncthreads();
-    if (mine_sum > 0.f) atomicMax(&last_t, tid);
-    float wpre = before;
-    for (int j = 0; j < w; ++j) wpre += wsum[j];
-    __syncthreads();
-    const float incl = wpre + v;
-    const float excl = l == 0 ? wpre : wpre + prev_in_warp;
-    // the last thread with mass also takes a target at or past its end (rounding)
-    const bool claim = mine_sum > 0.f && excl <= target && (target < incl || tid == last_t);
-    if (claim) {
-      float run = excl;
-      int pick = -1, lastk = -1;
-      for (int i = tid; i < n; i += kThr) {
-        const float e = kept_e(i);
-        if (e > 0.f) {
-          lastk = i;
-          run += e;
-          if (pick < 0 && run > target) pick = i;
+    for (int r = 0; r < kCl; ++r) {
+      if (ctot[r] > 0.f) {
+        last = r;
+        if (owner < 0 && acc + ctot[r] > target) {
+          owner = r;
+          before = acc;
         }
       }
-      if (pick < 0) pick = lastk;
-      const int tok = lo + pick;
-      a.tok[row] = tok;
-      a.lp[row] = __logf(xs[pick]) - __logf(total);
-      c_arg = tok;                             // CTA 0 reads the pick for the slot update
+      acc += ctot[r];
+    }
+    if (owner < 0) {            // rounding past the end: the last CTA with mass
+      owner = last < 0 ? 0 : last;
+      before = acc - (last < 0 ? 0.f : ctot[last]);
+    }
+    if (cr == owner) {
+      // inclusive prefix of the per-thread sums in thread order; thread i owns
+      // [P(i-1), P(i)), with P(i-1) taken from its neighbour so ranges neither overlap nor gap
+      const int w = tid >> 5, l = tid & 31;
+      const float mine = tsum[tid];
+      float v = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float t = __shfl_up_sync(0xffffffffu, v, o);
+        if (l >= o) v += t;
+      }
+      const float prev = __shfl_up_sync(0xffffffffu, v, 1);
+      if (l == 31) wsum[w] = v;
+      if (tid == 0) {
+        cand_t[par] = arg;      // replaced below; kept if rounding leaves no claimant
+        cand_e[par] = 1.f;
+        last_t = -1;
+      }
+      __syncthreads();
+      float wpre = before;
+      for (int j = 0; j < w; ++j) wpre += wsum[j];
+      if (mine > 0.f) atomicMax(&last_t, tid);   // the last thread with mass also takes a target past its end
+      __syncthreads();
+      const float incl = wpre + v;
+      const float excl = l == 0 ? wpre : wpre + prev;
+      if (mine > 0.f && excl <= target && (target < incl || tid == last_t)) {
+        float run = excl;
+        int pick = -1, lastk = -1;
+        for (int i = tid; i < n; i += kThr) {
+          const float e = xs[i];
+          if (e > pivot) {
+            lastk = i;
+            run += e;
+            if (pick < 0 && run > target) pick = i;
+          }
+        }
+        if (pick < 0) pick = lastk;
+        if (pick >= 0) {
+          cand_t[par] = lo + pick;
+          cand_e[par] = xs[pick];
+        }
+      }
+    }
+    cl.sync();
+    const int c = *cl.map_shared_rank(&cand_t[par], owner);
+    const float ec = *cl.map_shared_rank(&cand_e[par], owner);
+    // -- count and mass strictly above the candidate (the next round's sums if it fails)
+    float ms = 0.f;
+    int cn = 0;
+    for (int i = tid; i < n; i += kThr) {
+      const float e = xs[i];
+      if (e > ec) {
+        ms += e;
+        ++cn;
+      }
+    }
+    tsum[tid] = ms;
+    const float cms = block_sum(ms, rv);
+    const int ccn = static_cast<int>(block_sum(static_cast<float>(cn), rv));
+    if (tid == 0) {
+      c_mass[par] = cms;
+      c_cnt[par] = ccn;
+    }
+    cl.sync();
+    float above = 0.f;
+    long nabove = 0;
+#pragma unroll
+    for (int r = 0; r < kCl; ++r) {
+      ctot[r] = *cl.map_shared_rank(&c_mass[par], r);
+      above += ctot[r];
+      nabove += *cl.map_shared_rank(&c_cnt[par], r);
+    }
+    tok = c;
+    etok = ec;
+    // (the most likely token, e = 1, has nothing above it and always passes)
+    if ((nabove < k && above < pZ && ec >= min_p) || ec >= 1.f) break;
+    if (!(above > 0.f)) {       // nothing left above the candidate: the most likely token
+      tok = arg;
+      etok = 1.f;
+      break;
+    }
+    pivot = ec;
+    total = above;
+    if (round == kMaxRounds - 1) {
+      tok = arg;
+      etok = 1.f;
     }
   }
-  cl.sync();
-  if (SLOTS && cr == 0 && tid == 0) post_update(*cl.map_shared_rank(&c_arg, owner));
-  cl.sync();   // no CTA leaves while CTA 0 may still read its shared memory
+  if (cr == 0 && tid == 0) {
+    a.tok[row] = tok;
+    a.lp[row] = __logf(etok) - __logf(Z);
+    post_update(tok);
+  }
+  cl.sync();   // no CTA leaves while a peer may still read its shared memory
 }
 
 int sample_cluster_chunk(int V) {

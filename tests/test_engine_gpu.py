@@ -150,9 +150,9 @@ def test_async_falls_back_for_host_sampling_and_aborts():
     b = eng.add_request(None, None, SamplingParams(temperature=0.0, max_tokens=40, ignore_eos=True), ps[1])
     for _ in range(3):
         eng.step()
-    # a penalised request forces the synchronous path (after draining the pipeline)
+    # a request that wants top logprobs is sampled on the host path: the pipeline drains
     c = eng.add_request(None, None, SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True,
-                                                   repetition_penalty=1.2), ps[2])
+                                                   logprobs=2), ps[2])
     eng.step()
     assert not eng._inflight
     eng.abort_request(b.request_id)
@@ -164,6 +164,31 @@ def test_async_falls_back_for_host_sampling_and_aborts():
     assert len(done[a.request_id].outputs[0].token_ids) == 12
     assert len(done[c.request_id].outputs[0].token_ids) == 8
     assert eng._n_sync_only == 0
+
+
+def test_penalties_bias_and_min_tokens_stay_pipelined_and_match_the_synchronous_path():
+    """Penalties, logit bias and min_tokens live in the device slot tables: such requests
+    keep the pipelined schedule, and their greedy tokens equal those of the synchronous
+    engine, which applies the same rules with host-built index tensors."""
+    ps = prompts(3, seed=12)
+    sps = [SamplingParams(temperature=0.0, max_tokens=14, ignore_eos=True, repetition_penalty=1.3),
+           SamplingParams(temperature=0.0, max_tokens=14, ignore_eos=True, frequency_penalty=0.8,
+                          presence_penalty=0.5, logit_bias={17: 2.0, 123: -5.0}),
+           SamplingParams(temperature=0.0, max_tokens=14, min_tokens=10, stop_token_ids=[5, 9])]
+    outs = []
+    for flag in (False, True):
+        eng = _engine_async(flag)
+        ids = [eng.add_request(None, None, sp, p).request_id for sp, p in zip(sps, ps)]
+        if flag:
+            assert eng._n_sync_only == 0
+        done = {}
+        while eng.has_unfinished_requests():
+            for o in eng.step():
+                if o.finished:
+                    done[o.request_id] = o.outputs[0].token_ids
+        outs.append([done[i] for i in ids])
+    assert outs[0] == outs[1]
+    assert len(outs[1][2]) >= 10
 
 
 def test_async_launch_never_synchronises():
