@@ -23,7 +23,7 @@ import traceback
 from dataclasses import dataclass
 from typing import AsyncIterator, Dict, List, Optional
 
-from rusteeze_b200.core.errors import RequestTimeoutError, ServiceUnavailableError
+from rusteeze_b200.core.errors import DistributedError, RequestTimeoutError, ServiceUnavailableError
 from rusteeze_b200.core.outputs import RequestOutput
 from rusteeze_b200.core.sampling_params import SamplingParams
 
@@ -42,8 +42,11 @@ class _Submit:
 
 
 class AsyncLLMEngine:
-    def __init__(self, engine, request_timeout_s: float = 600.0, stall_timeout_s: float = 120.0):
+    def __init__(self, engine, request_timeout_s: float = 600.0, stall_timeout_s: float = 120.0,
+                 max_worker_recoveries: int = 3):
         self.engine = engine
+        self.max_worker_recoveries = max_worker_recoveries
+        self.recovering = False
         self.request_timeout_s = request_timeout_s
         self.stall_timeout_s = stall_timeout_s
         self._inbox: "queue.Queue" = queue.Queue()
@@ -74,7 +77,7 @@ class AsyncLLMEngine:
 
     @property
     def is_ready(self) -> bool:
-        if not self.healthy or self._thread is None or not self._thread.is_alive():
+        if not self.healthy or self.recovering or self._thread is None or not self._thread.is_alive():
             return False
         t = self.last_step_start
         return t is None or time.monotonic() - t < self.stall_timeout_s
@@ -180,6 +183,30 @@ class AsyncLLMEngine:
             self.last_error = f"device kernel status {code}"
             log.error("device kernel reported status %d; engine marked unhealthy", code)
 
+    def _fail(self, e: BaseException) -> None:
+        self.healthy = False
+        self.last_error = f"engine step failed: {e!r}"
+        log.error("engine step failed:\n%s", traceback.format_exc())
+        for sub in self._streams.values():
+            self._push(sub, ServiceUnavailableError(self.last_error))
+        self._streams.clear()
+
+    def _recover(self, launcher, err: BaseException) -> bool:
+        """Worker-group recovery; returns False (engine unhealthy) when it fails too or when
+        the engine has already been recovered `max_worker_recoveries` times."""
+        if launcher.recoveries >= self.max_worker_recoveries:
+            return False
+        log.error("engine step failed with %r; replacing the tensor-parallel worker group", err)
+        self.recovering = True            # /health/ready answers 503 meanwhile
+        try:
+            launcher.recover()
+        except BaseException:  # noqa: BLE001
+            log.error("worker-group recovery failed:\n%s", traceback.format_exc())
+            return False
+        finally:
+            self.recovering = False
+        return True
+
     def _loop(self) -> None:
         dev = str(getattr(self.engine, "device", "cpu"))
         if dev.startswith("cuda"):
@@ -196,13 +223,16 @@ class AsyncLLMEngine:
             self.last_step_start = time.monotonic()
             try:
                 outs = self.engine.step()
+            except DistributedError as e:
+                # a tensor-parallel worker died: replace the worker group and keep serving
+                # (the engine re-queues its live sequences as recompute preemptions)
+                launcher = getattr(self.engine, "tp_launcher", None)
+                if launcher is not None and self._recover(launcher, e):
+                    continue
+                self._fail(e)
+                return
             except BaseException as e:  # noqa: BLE001
-                self.healthy = False
-                self.last_error = f"engine step failed: {e!r}"
-                log.error("engine step failed:\n%s", traceback.format_exc())
-                for sub in self._streams.values():
-                    self._push(sub, ServiceUnavailableError(self.last_error))
-                self._streams.clear()
+                self._fail(e)
                 return
             finally:
                 self.last_step_start = None

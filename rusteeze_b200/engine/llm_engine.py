@@ -522,6 +522,45 @@ class LLMEngine:
                 self.seq_to_request.pop(s.seq_id, None)
             self.stats_counters["requests_finished"] += 1
 
+    # ------------------------------------------------------------------ recovery
+    def recover_from_worker_failure(self, executor, num_gpu_blocks: int) -> int:
+        """A tensor-parallel worker died and the group was restarted (the launcher's
+        `recover`): the KV cache is gone.  Steps in flight never completed, so their samples
+        are dropped; every running or swapped sequence is reset for recompute and queued
+        ahead of the waiting prompts in its old order, with a fresh block manager and the
+        new executor.  Returns the number of sequences re-queued."""
+        from collections import deque
+        for fl in self._inflight:
+            for ss, _k in fl.owners:
+                ss.seq.pending = max(0, ss.seq.pending - 1)
+        self._inflight = []
+        live = [s for s in list(self.scheduler.running) + list(self.scheduler.swapped) if not s.is_finished()]
+        waiting = [s for s in self.scheduler.waiting if not s.is_finished()]
+        ec = self.config.engine
+        num_cpu_blocks = swap_blocks(ec, self.model_config, self.dtype, self.device)
+        self.bm = make_block_manager(BLOCK_SIZE, num_gpu_blocks, num_cpu_blocks, ec.enable_prefix_caching)
+        n_pre = self.scheduler.num_preemptions
+        self.scheduler = Scheduler(self.sched_cfg, self.bm)
+        self.scheduler.num_preemptions = n_pre + len(live)
+        for s in live:
+            s.reset_for_recompute()
+            s.pending = 0
+        for s in waiting:
+            if s.num_computed:
+                s.reset_for_recompute()
+        self.scheduler.waiting = deque(live + waiting)
+        self.runner = executor
+        self._sampler = getattr(executor, "sampler", None)
+        if self._sampler is not None and self.device.startswith("cuda"):
+            self._sampler.max_slots = ec.max_num_seqs + 64
+        if self.device.startswith("cuda") and not ec.enforce_eager and hasattr(self.runner, "capture_graphs"):
+            from rusteeze_b200.engine.model_runner import decode_graph_buckets
+            mx = min(ec.cuda_graph_max_batch or ec.max_num_seqs, ec.max_num_seqs)
+            self.runner.capture_graphs(decode_graph_buckets(mx))
+        self.stats_counters["worker_recoveries"] = self.stats_counters.get("worker_recoveries", 0) + 1
+        log.warning("worker group replaced: %d sequences re-queued for recompute", len(live))
+        return len(live)
+
     # ------------------------------------------------------------------ stats
     def stats(self) -> dict:
         d = dict(self.stats_counters)

@@ -44,7 +44,10 @@ def _model_config(cfg: Config) -> ModelConfig:
 
 
 def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfig] = None, tag: str = "0",
-                  liveness=None):
+                  liveness=None, build_engine: bool = True):
+    """Builds this rank's shard, runner and plan channel.  Rank 0 returns (engine, runner,
+    channel); with build_engine=False (worker-group recovery) it returns (executor, runner,
+    channel) for an engine that already exists."""
     from rusteeze_b200.engine.llm_engine import LLMEngine, _dtype
     mc = model_config or _model_config(cfg)
     ec = cfg.engine
@@ -104,6 +107,8 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
     ecfg.model.device = dev
     if info.rank == 0:
         executor = TPExecutor(runner, channel, liveness) if channel is not None else runner
+        if not build_engine:
+            return executor, runner, channel
         engine = LLMEngine(ecfg, model=model, executor=executor)
         return engine, runner, channel
     return None, runner, channel
@@ -139,27 +144,43 @@ def _spawned_worker(rank: int, world: int, port: int, cfg_dict: dict, mc_dict: O
 
 
 class TPEngineLauncher:
-    """Spawns ranks 1..N-1 and builds rank 0's engine in this process."""
+    """Spawns ranks 1..N-1 and builds rank 0's engine in this process.
+
+    Worker-group recovery: when a worker process dies (the engine's next step raises
+    DistributedError before it publishes a plan), `recover()` tears the group down,
+    spawns a fresh set of workers on a new rendezvous, rebuilds rank 0's shard, runner and
+    plan channel, and hands them to the existing engine, which re-queues every live
+    sequence as a recompute preemption (the KV cache went with the old group).  Requests
+    in flight then complete as if they had been preempted.  The reference handles
+    failures only by request timeout, abort and shutdown
+    (crates/rusteeze-engine/src/engine.rs:295,575-603)."""
 
     def __init__(self, cfg: Config, model_config: Optional[ModelConfig] = None, device_type: Optional[str] = None):
-        import torch.multiprocessing as mp
         self.cfg = cfg
+        self.model_config = model_config
         self.world = cfg.model.tensor_parallel_size
         self.device_type = device_type or ("cuda" if torch.cuda.is_available() else "cpu")
+        self.recoveries = 0
+        info = self._spawn()
+        self._engine, self.runner, self.channel = tp_rank_setup(cfg, info, model_config, self.tag,
+                                                                liveness=self.dead_workers)
+        self._engine.tp_launcher = self
+
+    def _spawn(self) -> DistInfo:
+        import torch.multiprocessing as mp
         port = free_port()
         self.tag = f"{os.getpid()}_{port}"
         ctx = mp.get_context("spawn")
-        mc_dict = model_config.to_dict() if model_config else None
-        self.procs = [ctx.Process(target=_spawned_worker, args=(r, self.world, port, cfg.to_dict(), mc_dict,
+        mc_dict = self.model_config.to_dict() if self.model_config else None
+        self.procs = [ctx.Process(target=_spawned_worker, args=(r, self.world, port, self.cfg.to_dict(), mc_dict,
                                                                  self.tag, self.device_type), daemon=True)
                       for r in range(1, self.world)]
         for p in self.procs:
             p.start()
         os.environ.update(RANK="0", WORLD_SIZE=str(self.world), LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
                           MASTER_PORT=str(port))
-        info = init_distributed(device_type=self.device_type, timeout_s=float(os.environ.get("RZ_PG_TIMEOUT_S", "120")))
-        self._engine, self.runner, self.channel = tp_rank_setup(cfg, info, model_config, self.tag,
-                                                                liveness=self.dead_workers)
+        return init_distributed(device_type=self.device_type,
+                                timeout_s=float(os.environ.get("RZ_PG_TIMEOUT_S", "120")))
 
     def dead_workers(self):
         """Ranks whose worker process has exited."""
@@ -168,13 +189,46 @@ class TPEngineLauncher:
     def engine(self):
         return self._engine
 
+    def _teardown(self, timeout: float) -> None:
+        for p in self.procs:
+            p.join(timeout)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout)
+        if self.channel is not None:
+            try:
+                self.channel.close()
+            except Exception:  # noqa: BLE001 -- already closed
+                pass
+        # graphs holding collectives must go before the process group, on every rank
+        self.runner.release_graphs()
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception as e:  # noqa: BLE001 -- a group with a dead member may not close cleanly
+                log.warning("process group teardown after a worker failure: %r", e)
+
+    def recover(self) -> None:
+        """Replaces the worker group after a worker died (see the class docstring)."""
+        dead = self.dead_workers()
+        log.error("tensor-parallel worker rank(s) %s died; restarting the worker group", dead)
+        try:
+            self.channel.ring.close()          # surviving workers see the closed ring and exit
+        except Exception:  # noqa: BLE001
+            pass
+        self._teardown(timeout=10.0)
+        info = self._spawn()
+        executor, self.runner, self.channel = tp_rank_setup(self.cfg, info, self.model_config, self.tag,
+                                                            liveness=self.dead_workers, build_engine=False)
+        self._engine.recover_from_worker_failure(executor, self.runner.num_gpu_blocks)
+        self.recoveries += 1
+
     def shutdown(self, timeout: float = 30.0) -> None:
         if self.channel is not None:
             try:
                 self._engine.runner.shutdown()
             except Exception:  # noqa: BLE001 -- a dead worker cannot consume the stop message
                 pass
-        # graphs holding NCCL calls must go before the process group, on every rank
         self.runner.release_graphs()
         for p in self.procs:
             p.join(timeout)

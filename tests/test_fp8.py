@@ -261,3 +261,58 @@ def test_gemm_mxf8_silu_emits_mxf8_operand(M):
     want = qr.float().view(M, I // 128, 128) * sr.unsqueeze(-1)
     assert ((deq - want).norm() / want.norm()).item() < 2e-2
     assert int(ops.cuda_ext().status()[0]) == 0
+
+
+_ORACLE = {}
+
+
+def _llama3_oracle(mc, prompt):
+    """fp32 CPU logits of the last prompt position on the unquantised random-init weights
+    (the same seed every engine below starts from)."""
+    key = (mc.num_hidden_layers, tuple(prompt))
+    if key not in _ORACLE:
+        from rusteeze_b200.models.loader import build_model, to_cpu_fp32
+        from rusteeze_b200.models.naive import naive_logits
+        m = build_model(mc, dtype=torch.bfloat16, device="cuda:0", seed=0)
+        _ORACLE[key] = torch.log_softmax(naive_logits(to_cpu_fp32(m), prompt)[-1].double(), -1)
+        del m
+        torch.cuda.empty_cache()
+    return _ORACLE[key]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt,tol", [("none", 0.05), ("ue8m0", 0.25), ("fp32", 0.25)])
+def test_fp8_engine_logprobs_track_the_fp32_oracle(fmt, tol):
+    """Llama-3-8B shapes (2 layers, random init): the first step's top-20 logprobs of the bf16
+    engine, the MXFP8 engine (power-of-two UE8M0 block scales applied in the MMA) and the
+    fp32-scale FP8 engine (per-K-block promotion) against the fp32 oracle on the unquantised
+    weights.  The bound covers weight and activation quantisation together."""
+    from rusteeze_b200.config.config import Config, QuantizationConfig
+    from rusteeze_b200.core.sampling_params import SamplingParams
+    from rusteeze_b200.engine.llm_engine import LLMEngine
+    from rusteeze_b200.models.config import get_preset
+    mc = dataclasses.replace(get_preset("llama-3-8b"), num_hidden_layers=2)
+    prompt = list(range(1000, 1100))
+    ref_lsm = _llama3_oracle(mc, prompt)
+    cfg = Config()
+    cfg.model.device = "cuda:0"
+    cfg.model.seed = 0
+    if fmt != "none":
+        cfg.model.quantization = QuantizationConfig(method="fp8_block", scale_format=fmt)
+    cfg.engine.num_gpu_blocks = 64
+    cfg.engine.max_num_seqs = 4
+    cfg.engine.max_num_batched_tokens = 256
+    eng = LLMEngine(cfg, model_config=mc)
+    eng.add_request("r", None, SamplingParams(temperature=0.0, max_tokens=1, ignore_eos=True, logprobs=20), prompt)
+    out = None
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            out = o
+    top = out.outputs[0].logprobs[0]
+    err = max(abs(lp - float(ref_lsm[t])) for t, lp in top.items())
+    # the oracle's own top 5 must appear among the engine's top 20
+    ref_top5 = set(torch.topk(ref_lsm, 5).indices.tolist())
+    overlap = len(ref_top5 & set(top))
+    print(f"{fmt}: max |logprob - oracle| over the top 20 = {err:.4f}, oracle top-5 overlap {overlap}/5")
+    assert err < tol, (fmt, err)
+    assert overlap >= 3, (fmt, overlap)
