@@ -230,6 +230,35 @@ def _gemm_ag():
     return lambda: t["F"].gemm_ag(t["g"], t["w_qkv"], 1)
 
 
+@case("moe_combine_peer_1rank", "moe_combine_peer_kernel")
+def _moe_combine_peer():
+    """Mixtral-8x7B expert layer on a one-rank FusedTP group (all 8 experts local, 2048
+    tokens): route, grouped expert GEMMs and the combine kernel that stores every weighted
+    expert row into its owner's slot -- the capture selects the combine."""
+    t = _fused_tp_one_rank(M=2048, H=4096, K=4096, N=4096)
+    if "moe" not in t:
+        E, I = 8, 14336
+        router = _bf(E, 4096, scale=0.05)
+        w13 = ops.interleave_gate_up_experts(_bf(E, 2 * I, 4096, scale=0.02))
+        w2 = _bf(E, 4096, I, scale=0.02)
+        t["moe"] = (router, w13, w2)
+    router, w13, w2 = t["moe"]
+    return lambda: t["F"].moe(t["g"], router, w13, w2, 2, 0, 1, 2)
+
+
+@case("peer_all_reduce_1rank", "peer_all_reduce_kernel")
+def _peer_all_reduce():
+    """The peer all-reduce on a one-rank group (the 256 x 4096 decode message of
+    Llama-3-8B and its two-shot path at 4096 x 4096 share the kernel)."""
+    t = _fused_tp_one_rank()
+    if "ar" not in t:
+        import torch.distributed as dist
+        from rusteeze_b200.parallel.comm import PeerAllReduce
+        t["ar"] = PeerAllReduce(dist.group.WORLD, 0, 1, torch.device("cuda", 0), 4096 * 4096)
+        t["ar_x"] = _bf(4096, 4096)
+    return lambda: t["ar"].all_reduce(t["ar_x"])
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None)
