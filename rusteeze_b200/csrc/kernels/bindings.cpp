@@ -88,6 +88,36 @@ void rope_and_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor co
            "rope_and_cache");
 }
 
+// Vocab-parallel embedding rows: table holds rows [lo, hi) of the vocabulary.
+void embedding(torch::Tensor out, torch::Tensor table, torch::Tensor ids, int64_t lo, int64_t hi, int64_t vocab,
+               double scale) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
+  CHECK_CUDA(table); CHECK_BF16(table); CHECK_LAST(table);
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "embedding: int64 ids");
+  TORCH_CHECK(out.is_contiguous() && out.size(1) == table.size(1) && out.size(0) == ids.numel(), "embedding: out [M, H]");
+  TORCH_CHECK(table.stride(0) == table.size(1), "embedding: contiguous table rows");
+  check_rc(rz::embedding_launch(reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), ids.data_ptr<int64_t>(),
+                                static_cast<int>(ids.numel()), static_cast<int>(table.size(1)), lo, hi, vocab,
+                                static_cast<float>(scale), status_ptr(), cur_stream()),
+           "embedding");
+}
+
+void layer_norm(torch::Tensor out, torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w,
+                c10::optional<torch::Tensor> b, double eps) {
+  const at::cuda::CUDAGuard rz_guard(out.device());
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w);
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous(), "layer_norm: contiguous rows");
+  const int rows = x.size(0), H = x.size(1);
+  check_rc(rz::layer_norm_launch(reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                 reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                 residual.has_value() ? reinterpret_cast<__nv_bfloat16*>(residual->data_ptr()) : nullptr,
+                                 reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+                                 b.has_value() ? reinterpret_cast<const __nv_bfloat16*>(b->data_ptr()) : nullptr, rows, H,
+                                 static_cast<float>(eps), cur_stream()),
+           "layer_norm");
+}
+
 void act_mul(torch::Tensor out, torch::Tensor x, int64_t kind) {
   const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(x); CHECK_BF16(x);
@@ -197,9 +227,9 @@ int64_t gemm_bf16_ex(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::o
   TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "gemm: row strides must be 16-byte aligned");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
               "gemm: operands must be 16-byte aligned");
-  if (epi == rz::kEpiSiluMul) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "silu epilogue: N % 128, out N/2");
+  if ((epi & 0xff) == rz::kEpiSiluMul) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "silu epilogue: N % 128, out N/2");
   if (bn <= 0 || k_splits <= 0) {
-    auto pl = rz::plan_gemm(M, N, K, epi);
+    auto pl = rz::plan_gemm(M, N, K, static_cast<int>(epi & 0xff));
     bn = pl.bn;
     k_splits = pl.k_splits;
   }
@@ -211,7 +241,8 @@ int64_t gemm_bf16_ex(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::o
   p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
   p.residual = residual.has_value() ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
   p.ldr = residual.has_value() ? residual->stride(0) : 0;
-  p.epi = epi;
+  p.epi = static_cast<int>(epi & 0xff);
+  p.gate_act = static_cast<int>((epi >> 8) & 1);   // kGateGelu: GELU(tanh) gate
   p.status = status_ptr();
   torch::Tensor ws;
   if (k_splits > 1) {
@@ -324,9 +355,9 @@ int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch:
   TORCH_CHECK(sfa.numel() >= static_cast<int64_t>((M + 127) / 128) * (K / 128) * 512 &&
                   sfb.numel() >= static_cast<int64_t>(N / 128) * (K / 128) * 512,
               "mxf8 gemm: scale chunk buffers too small");
-  if (epi == rz::kEpiSiluMul) TORCH_CHECK(out.size(1) == N / 2, "silu epilogue: out has N/2 columns");
+  if ((epi & 0xff) == rz::kEpiSiluMul) TORCH_CHECK(out.size(1) == N / 2, "silu epilogue: out has N/2 columns");
   if (bn <= 0 || k_splits <= 0) {
-    auto pl = rz::plan_gemm_mxf8(M, N, K, epi);
+    auto pl = rz::plan_gemm_mxf8(M, N, K, static_cast<int>(epi & 0xff));
     bn = pl.bn;
     k_splits = pl.k_splits;
   }
@@ -338,7 +369,8 @@ int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch:
   p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
   p.residual = residual.has_value() ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
   p.ldr = residual.has_value() ? residual->stride(0) : 0;
-  p.epi = epi;
+  p.epi = static_cast<int>(epi & 0xff);
+  p.gate_act = static_cast<int>((epi >> 8) & 1);   // kGateGelu: GELU(tanh) gate
   p.status = status_ptr();
   p.sfa = reinterpret_cast<const uint8_t*>(sfa.data_ptr());
   p.sfb = reinterpret_cast<const uint8_t*>(sfb.data_ptr());
@@ -354,7 +386,7 @@ int64_t gemm_mxf8(torch::Tensor out, torch::Tensor xq, torch::Tensor sfa, torch:
 
 // gate/up MXFP8 GEMM whose SiLU(gate)*up epilogue writes the down projection's MXFP8 operand.
 int64_t gemm_mxf8_silu_q(torch::Tensor q_out, torch::Tensor sf_out, torch::Tensor xq, torch::Tensor sfa,
-                         torch::Tensor wq, torch::Tensor sfb, c10::optional<torch::Tensor> bias) {
+                         torch::Tensor wq, torch::Tensor sfb, c10::optional<torch::Tensor> bias, int64_t gate_act) {
   const at::cuda::CUDAGuard rz_guard(q_out.device());
   CHECK_CUDA(xq);
   const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
@@ -368,6 +400,7 @@ int64_t gemm_mxf8_silu_q(torch::Tensor q_out, torch::Tensor sf_out, torch::Tenso
   p.ldd = q_out.stride(0);
   p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
   p.epi = rz::kEpiSiluMulMx;
+  p.gate_act = static_cast<int>(gate_act);
   p.status = status_ptr();
   p.sfa = reinterpret_cast<const uint8_t*>(sfa.data_ptr());
   p.sfb = reinterpret_cast<const uint8_t*>(sfb.data_ptr());
@@ -395,14 +428,15 @@ int64_t gemm_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch:
   TORCH_CHECK(grp_off.numel() == G + 1 && grp_end.numel() == G && grp_off.scalar_type() == at::kInt,
               "grouped gemm: int32 grp_off [G+1], grp_end [G]");
   TORCH_CHECK(G <= rz::kMaxGemmGroups && K % 64 == 0 && N % 64 == 0, "grouped gemm: G <= 64, K/N multiples of 64");
-  if (epi == rz::kEpiSiluMul) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "silu epilogue: N % 128, out N/2");
+  if ((epi & 0xff) == rz::kEpiSiluMul) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "silu epilogue: N % 128, out N/2");
   if (bn <= 0) bn = (static_cast<int64_t>((x.size(0) + 127) / 128) * (N / 256) >= 2 * rz::num_sms()) ? 256 : 128;
   rz::GemmParams p{};
   p.N = N; p.K = K;
   p.k_splits = 1;
   p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.ldd = out.stride(0);
-  p.epi = epi;
+  p.epi = static_cast<int>(epi & 0xff);
+  p.gate_act = static_cast<int>((epi >> 8) & 1);   // kGateGelu: GELU(tanh) gate
   p.status = status_ptr();
   p.grp_off = grp_off.data_ptr<int>();
   p.grp_end = grp_end.data_ptr<int>();
@@ -567,15 +601,16 @@ int64_t gemm_ag(torch::Tensor out, torch::Tensor g, torch::Tensor w, c10::option
   CHECK_CUDA(g); CHECK_BF16(g); CHECK_BF16(w); CHECK_LAST(g); CHECK_LAST(w);
   const int M = g.size(0), K = g.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && K % 8 == 0 && N % 8 == 0, "gemm_ag: shapes");
-  if (epi == rz::kEpiSiluMul) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "silu epilogue: N % 128, out N/2");
-  auto pl = rz::plan_gemm(M, N, K, epi);
+  if ((epi & 0xff) == rz::kEpiSiluMul) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "silu epilogue: N % 128, out N/2");
+  auto pl = rz::plan_gemm(M, N, K, static_cast<int>(epi & 0xff));
   rz::GemmParams p{};
   p.M = M; p.N = N; p.K = K;
   p.k_splits = pl.k_splits;
   p.D = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.ldd = out.stride(0);
   p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
-  p.epi = epi;
+  p.epi = static_cast<int>(epi & 0xff);
+  p.gate_act = static_cast<int>((epi >> 8) & 1);   // kGateGelu: GELU(tanh) gate
   p.status = status_ptr();
   p.ag_flag = reinterpret_cast<const uint32_t*>(ag_flag.data_ptr());
   p.ag_rows = M;
@@ -849,6 +884,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_add_rms_norm", &fused_add_rms_norm);
   m.def("rope_and_cache", &rope_and_cache);
   m.def("act_mul", &act_mul);
+  m.def("embedding", &embedding);
+  m.def("layer_norm", &layer_norm);
   m.def("decode_attention", &decode_attention);
   m.def("prefill_attention", &prefill_attention);
   m.def("prefill_attention_impl", &prefill_attention_impl);
@@ -879,7 +916,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &moe_route);
   m.def("gemm_mxf8", &gemm_mxf8);
   m.def("gemm_plan_mxf8", &gemm_plan_mxf8);
-  m.def("gemm_mxf8_silu_q", &gemm_mxf8_silu_q);
+  m.def("gemm_mxf8_silu_q", &gemm_mxf8_silu_q, py::arg("q_out"), py::arg("sf_out"), py::arg("xq"), py::arg("sfa"),
+        py::arg("wq"), py::arg("sfb"), py::arg("bias"), py::arg("gate_act") = 0);
   m.def("spec_verify", &spec_verify);
   m.def("sample_rows", &sample_rows);
   m.def("sample_slots", &sample_slots);

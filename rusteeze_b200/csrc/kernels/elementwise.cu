@@ -278,6 +278,131 @@ int act_mul_launch(__nv_bfloat16* out, const __nv_bfloat16* x, int rows, int I, 
   return static_cast<int>(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------------------- embedding
+// out[m] = table[ids[m] - lo] * scale when lo <= ids[m] < hi, else zeros (the rows another
+// rank of a vocab-parallel embedding owns; the caller sums the ranks).  Ids outside the
+// whole vocabulary are recorded in the status word and give zeros.  One warp per row,
+// 16-byte vectors.
+__global__ void embedding_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ table,
+                                 const int64_t* __restrict__ ids, int M, int H, int64_t lo, int64_t hi, int64_t vocab,
+                                 float scale, int* status) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t id = ids[row];
+  if ((id < 0 || id >= vocab) && lane == 0) set_status(status, kBadArgument);
+  const bool own = id >= lo && id < hi && id < vocab && id >= 0;
+  const __nv_bfloat16* src = table + (own ? (id - lo) : 0) * static_cast<int64_t>(H);
+  __nv_bfloat16* dst = out + static_cast<int64_t>(row) * H;
+  for (int c = lane * 8; c < H; c += 32 * 8) {
+    float v[8];
+    if (own) {
+      ld8(src + c, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] *= scale;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    st8(dst + c, v);
+  }
+}
+
+int embedding_launch(__nv_bfloat16* out, const __nv_bfloat16* table, const int64_t* ids, int M, int H, int64_t lo,
+                     int64_t hi, int64_t vocab, float scale, int* status, cudaStream_t st) {
+  if (M == 0) return 0;
+  if (H % 8) return -1;
+  const int warps = 8;
+  embedding_kernel<<<(M + warps - 1) / warps, warps * 32, 0, st>>>(out, table, ids, M, H, lo, hi, vocab, scale,
+                                                                    status);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------- LayerNorm
+// y = (x - mean) * rsqrt(var + eps) * w + b (b optional), fp32 statistics; with a residual,
+// r += x first (in place) and the rounded sum is normalised, as in fused_add_rms_norm.
+// One CTA per row; blockDim = H / (8 * NV).
+template <int NV, bool ADD>
+__global__ void layer_norm_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
+                                  __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w,
+                                  const __nv_bfloat16* __restrict__ b, int H, float eps) {
+  __shared__ float red[33];
+  const size_t row = blockIdx.x;
+  const int c0 = threadIdx.x * 8 * NV;
+  float v[NV][8];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = c0 + j * 8;
+    if (c < H) {
+      ld8(x + row * H + c, v[j]);
+      if (ADD) {
+        float r[8];
+        ld8(residual + row * H + c, r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] += r[i];
+        st8(residual + row * H + c, v[j]);
+        ld8(residual + row * H + c, v[j]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += v[j][i];
+    }
+  }
+  const float mean = block_sum<NV>(s, red) / H;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = c0 + j * 8;
+    if (c < H) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[j][i] - mean;
+        ss += d * d;
+      }
+    }
+  }
+  __syncthreads();   // red is reused by the second reduction
+  const float inv = rsqrtf(block_sum<NV>(ss, red) / H + eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = c0 + j * 8;
+    if (c < H) {
+      float g[8], bb[8], o[8];
+      ld8(w + c, g);
+      if (b) {
+        ld8(b + c, bb);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bb[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = (v[j][i] - mean) * inv * g[i] + bb[i];
+      st8(out + row * H + c, o);
+    }
+  }
+}
+
+int layer_norm_launch(__nv_bfloat16* out, const __nv_bfloat16* x, __nv_bfloat16* residual, const __nv_bfloat16* w,
+                      const __nv_bfloat16* b, int rows, int H, float eps, cudaStream_t st) {
+  if (rows == 0) return 0;
+  if (H % 8 || H > 16384) return -1;
+  int nv = 1;
+  while (H / (8 * nv) > 1024) nv *= 2;
+  const int threads = (H / 8 + nv - 1) / nv;
+#define RZ_LN(NV)                                                                                           \
+  if (residual)                                                                                             \
+    layer_norm_kernel<NV, true><<<rows, threads, 0, st>>>(out, x, residual, w, b, H, eps);                  \
+  else                                                                                                      \
+    layer_norm_kernel<NV, false><<<rows, threads, 0, st>>>(out, x, residual, w, b, H, eps);
+  if (nv == 1) {
+    RZ_LN(1)
+  } else {
+    RZ_LN(2)
+  }
+#undef RZ_LN
+  return static_cast<int>(cudaGetLastError());
+}
+
 // ---------------------------------------------------------------------------- KV block copy
 // Copies whole KV blocks (all layers) src -> dst inside one cache tensor (copy-on-write).
 __global__ void copy_blocks_kernel(uint4* __restrict__ cache, const int32_t* __restrict__ pairs, int64_t vec_per_block) {

@@ -14,5 +14,9 @@ int rope_cache_launch(__nv_bfloat16* qkv, int qkv_stride, const int64_t* pos, co
                       __nv_bfloat16* kc, __nv_bfloat16* vc, int64_t block_stride, const int64_t* slots, int T,
                       int Hq, int Hkv, int D, cudaStream_t st);
 int act_mul_launch(__nv_bfloat16* out, const __nv_bfloat16* x, int rows, int I, int kind, cudaStream_t st);
+int embedding_launch(__nv_bfloat16* out, const __nv_bfloat16* table, const int64_t* ids, int M, int H, int64_t lo,
+                     int64_t hi, int64_t vocab, float scale, int* status, cudaStream_t st);
+int layer_norm_launch(__nv_bfloat16* out, const __nv_bfloat16* x, __nv_bfloat16* residual, const __nv_bfloat16* w,
+                      const __nv_bfloat16* b, int rows, int H, float eps, cudaStream_t st);
 int copy_blocks_launch(void* cache, const int32_t* pairs, int npairs, int64_t block_bytes, cudaStream_t st);
 }  // namespace rz

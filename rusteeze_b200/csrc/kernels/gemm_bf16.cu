@@ -88,6 +88,11 @@ __device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* src, float* v) 
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+// GELU with the tanh approximation (Gemma's GeGLU): 0.5 x (1 + tanh(sqrt(2/pi)(x + 0.044715 x^3)))
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+__device__ __forceinline__ float gate_act(float x, int act) { return act ? gelu_tanh_f(x) : silu(x); }
 
 // What a work unit computes: tile index t (in unit order), K blocks [kb0, kb1) and the split
 // index ks of a split-K unit.
@@ -328,7 +333,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               a += bf2f(p.bias[gcol + j]);
               b += bf2f(p.bias[gcol + 64 + j]);
             }
-            o[it][j] = silu(a) * b;
+            o[it][j] = gate_act(a, p.gate_act) * b;
             amax = fmaxf(amax, fabsf(o[it][j]));
           }
         }
@@ -511,7 +516,7 @@ __global__ void gemm_splitk_reduce(GemmParams p) {
         g[i] += bf2f(p.bias[gc + i]);
         v[i] += bf2f(p.bias[gc + 64 + i]);
       }
-      o[i] = silu(g[i]) * v[i];
+      o[i] = gate_act(g[i], p.gate_act) * v[i];
     }
   } else {
     for (int i = 0; i < 8; ++i) o[i] = 0.f;

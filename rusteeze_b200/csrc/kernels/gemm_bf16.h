@@ -10,6 +10,9 @@ namespace rz {
 // kEpiSiluMulMx: SiLU(gate)*up written as e4m3 (q_out, row stride ldd) plus UE8M0 1x128
 // scales (sf_out, [ceil(M/128)][N/256] chunks); BN = 256 only.
 enum GemmEpilogue : int { kEpiNone = 0, kEpiSiluMul = 1, kEpiPeerRS = 2, kEpiSiluMulMx = 3 };
+// The bindings take the epilogue with the gate activation in bit 8 of the same argument:
+// epi | kGateGelu makes the gated epilogues compute GELU(tanh)(gate) * up instead of SiLU.
+constexpr int kGateGelu = 1 << 8;
 
 constexpr int kMaxTpRanks = 8;
 constexpr int kAgRowBlock = 8;    // rows per all-gather flag
@@ -27,6 +30,7 @@ struct GemmParams {
   const __nv_bfloat16* residual;  // [M][ldr] or nullptr (kEpiNone only)
   int ldr;
   int epi;
+  int gate_act;        // gated epilogues (kEpiSiluMul / kEpiSiluMulMx): 0 SiLU, 1 GELU (tanh)
   int* status;
   const uint8_t* sfa;  // MXFP8 only: A scales, [ceil(M/128)][K/128] chunks of 512 bytes
   const uint8_t* sfb;  // MXFP8 only: B scales, [N/128][K/128] chunks of 512 bytes

@@ -194,7 +194,7 @@ class SlotTable:
 @dataclass
 class AsyncSample:
     tokens: torch.Tensor          # device int64 [R]: next step's pending input ids
-    host: torch.Tensor            # pinned [2, >=R] float64: token ids, logprobs
+    host: object                  # pinned (int64 token ids, fp32 logprobs), each >= R long
     rows: int
     event: "torch.cuda.Event"
     result: Optional["SampleResult"] = None    # host-sampled rows (CPU engines): already known
@@ -299,16 +299,19 @@ class Sampler:
         # prefixes: a strided pinned slice would make torch stage the copy
         # through a blocking temporary
         if not hasattr(self, "_pinned"):
-            self._pinned = [torch.empty(2 << 14, dtype=torch.float64, pin_memory=True) for _ in range(2)]
+            # (token ids, logprobs) per set: two plain device-to-host copies, no packing kernel
+            self._pinned = [(torch.empty(1 << 15, dtype=torch.int64, pin_memory=True),
+                             torch.empty(1 << 15, dtype=torch.float32, pin_memory=True)) for _ in range(2)]
             self._pk = 0
-        buf = self._pinned[self._pk]
+        bt, bl = self._pinned[self._pk]
         self._pk ^= 1
-        if 2 * R > buf.numel():
+        if R > bt.numel():
             raise ValueError("too many sample rows for the async readback buffer")
-        buf[:2 * R].copy_(torch.cat([toks.double(), lp.double()]), non_blocking=True)
+        bt[:R].copy_(toks, non_blocking=True)
+        bl[:R].copy_(lp, non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
-        return AsyncSample(toks, buf, R, ev)
+        return AsyncSample(toks, (bt, bl), R, ev)
 
     def finish(self, a: "AsyncSample") -> SampleResult:
         if a.result is not None:
@@ -316,9 +319,9 @@ class Sampler:
             return a.result
         a.event.synchronize()
         R = a.rows
-        self.last_d2h_bytes = 16 * R
-        vals = a.host[:2 * R].tolist()
-        return SampleResult([int(x) for x in vals[:R]], vals[R:], [None] * R, [None] * R)
+        self.last_d2h_bytes = 12 * R
+        bt, bl = a.host
+        return SampleResult(bt[:R].tolist(), bl[:R].tolist(), [None] * R, [None] * R)
 
     def _sample_device_async(self, logits: torch.Tensor, rows: List[SampleRow]):
         greedy = [r.params.is_greedy for r in rows]
@@ -356,6 +359,8 @@ class Sampler:
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
         self._drop_slots()
+        # the host-side rules index the logits in place: fp32 (the GPU path hands bf16 views)
+        logits = logits.float()
         logits = self._process_logits(logits, rows)
         host_rows = [i for i, r in enumerate(rows) if r.params.needs_host_sampling()]
         tokens: List[int] = [0] * R

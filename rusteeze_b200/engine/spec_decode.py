@@ -226,7 +226,8 @@ class SpecDecoder:
             dev = tlogits.device
             out = torch.empty(S, k + 1, dtype=torch.int64, device=dev)
             nacc = torch.empty(S, dtype=torch.int32, device=dev)
-            ops.cuda_ext().spec_verify(out, nacc, tlogits.contiguous(), dl.contiguous(), draft_tokens.to(dev),
+            ops.cuda_ext().spec_verify(out, nacc, tlogits.float().contiguous(), dl.float().contiguous(),
+                                       draft_tokens.to(dev),
                                        temps.to(dev), seeds.to(dev), offs.to(dev))
             ops.add_launches(1)
             both = torch.cat([out.cpu(), nacc.cpu().long().view(-1, 1)], dim=1)

@@ -152,15 +152,12 @@ class DecoderLM(nn.Module):
         return self.embed if self.lm_head is None else self.lm_head
 
     def embed_tokens(self, ids: torch.Tensor) -> torch.Tensor:
-        if self.tp.size == 1:
-            h = self.embed[ids]
-        else:
-            local = ids - self.vocab_lo
-            ok = (local >= 0) & (local < self.embed.shape[0])
-            h = self.embed[local.clamp(0, self.embed.shape[0] - 1)] * ok.unsqueeze(1).to(self.dtype)
+        """Embedding rows (vocab-parallel at TP > 1: each rank gathers the rows of its
+        vocabulary shard and zeros elsewhere, one kernel with Gemma's scale folded in, and
+        the ranks' rows are summed)."""
+        h = ops.embedding(ids, self.embed, self.vocab_lo, self.cfg.vocab_size, self.cfg.embed_scale)
+        if self.tp.size > 1:
             h = self.tp.all_reduce(h)
-        if self.cfg.embed_scale != 1.0:
-            h = h * torch.tensor(self.cfg.embed_scale, dtype=self.dtype)
         return h
 
     def _lin(self, x: torch.Tensor, owner, name: str, bias=None) -> torch.Tensor:
@@ -178,10 +175,12 @@ class DecoderLM(nn.Module):
 
     def _mlp(self, L, h: torch.Tensor) -> torch.Tensor:
         if getattr(L, "gate_up_q", None) is not None:
-            a = ops.linear_fp8(h, L.gate_up_q, L.gate_up_s, silu_mul=True, wsf=getattr(L, "gate_up_sf", None))
+            a = ops.linear_fp8(h, L.gate_up_q, L.gate_up_s, silu_mul=True, wsf=getattr(L, "gate_up_sf", None),
+                               act=self.act)
             return self._row_parallel(a, L, "down")
         if getattr(L, "gate_up_il", None) is not None and h.is_cuda:
-            a = ops.linear_silu_mul(h, L.gate_up_il)      # SiLU(gate)*up fused in the GEMM epilogue
+            # act(gate)*up fused in the GEMM epilogue (SwiGLU, or Gemma's GeGLU)
+            a = ops.linear_silu_mul(h, L.gate_up_il, act=self.act)
         else:
             gu = ops.linear(h, L.gate_up)
             a = ops.silu_mul(gu) if self.act == "silu" else ops.gelu_tanh_mul(gu)
@@ -190,11 +189,13 @@ class DecoderLM(nn.Module):
     @torch.no_grad()
     def prepare_for_gpu(self) -> None:
         """Re-lays weights for the GPU kernels: gate/up rows interleaved in
-        64-row blocks for the fused SiLU epilogue (the [gate | up] copy is
-        dropped to save HBM)."""
-        if not self.device.type == "cuda" or self.act != "silu" or getattr(self, "fp8", False):
+        64-row blocks for the fused gated epilogue, SiLU or GELU-tanh (the
+        [gate | up] copy is dropped to save HBM)."""
+        if not self.device.type == "cuda" or getattr(self, "fp8", False):
             return
         if self.cfg.is_moe:
+            if self.act != "silu":
+                return
             if self.cfg.intermediate_size % 64 or self.cfg.hidden_size % 256:
                 return
             for L in self.layers:
@@ -277,12 +278,12 @@ class DecoderLM(nn.Module):
                 if L.gate_up_q.shape[0] % 256 == 0:
                     # the SiLU epilogue emits the down projection's fp8 operand directly
                     with sec("gate_up_gemm"):
-                        aq = ops.linear_mxf8_silu_q(*xq, L.gate_up_q, L.gate_up_sf)
+                        aq = ops.linear_mxf8_silu_q(*xq, L.gate_up_q, L.gate_up_sf, act=self.act)
                     with sec("down_gemm_rs"):
                         h = self.tp.all_reduce(ops.linear_mxf8_q(*aq, L.down_q, L.down_sf))
                 else:
                     with sec("gate_up_gemm"):
-                        a = ops.linear_mxf8_q(*xq, L.gate_up_q, L.gate_up_sf, silu_mul=True)
+                        a = ops.linear_mxf8_q(*xq, L.gate_up_q, L.gate_up_sf, silu_mul=True, act=self.act)
                     with sec("down_gemm_rs"):
                         h = self._row_parallel(a, L, "down")
                 continue
@@ -302,9 +303,11 @@ class DecoderLM(nn.Module):
         F = getattr(self.tp, "fused_tp", None)
         if F is None or self.tp.size == 1 or not F.fits(M) or self.device.type != "cuda":
             return False
-        if self.is_gemma2 or self.act != "silu":
+        if self.is_gemma2:
             return False
         if getattr(self, "fp8", False):
+            if self.act != "silu":
+                return False
             # MXFP8 boundary chain (block-scaled GEMMs, quantised all-gather); fp32-scale FP8
             # checkpoints and FP8 MoE take the peer all-reduce path
             if self.cfg.is_moe or not F.mx_ok or getattr(self, "fp8_format", None) != "ue8m0":
@@ -379,7 +382,7 @@ class DecoderLM(nn.Module):
                     x = F.rs_norm_ag(M, nw, eps, off, c_mlp, mx=li + 1 < n)
                 continue
             with sec("gate_up_gemm"):
-                act = F.gemm_ag(x, L.gate_up_il, c_attn, silu_mul=True)
+                act = F.gemm_ag(x, L.gate_up_il, c_attn, silu_mul=True, act=self.act)
             with sec("down_gemm_rs"):
                 F.gemm_rs(act, L.down, c_mlp)
             with sec("norm_ag"):
@@ -391,7 +394,8 @@ class DecoderLM(nn.Module):
         return x
 
     def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
-        """h [n, H] -> fp32 logits [n, vocab] (gathered over TP ranks)."""
+        """h [n, H] -> logits [n, vocab] (gathered over TP ranks): bf16 on the GPU (fp32
+        with a final softcap), fp32 on the CPU."""
         with OP_TIMER.section("lm_head"):
             return self._compute_logits(h)
 
@@ -402,10 +406,14 @@ class DecoderLM(nn.Module):
             logits = ops.linear(h, self.lm_head_weight)
         if self.tp.size > 1:
             logits = self.tp.all_gather_last_dim(logits)
-        logits = logits[:, : self.cfg.vocab_size].float()
+        logits = logits[:, : self.cfg.vocab_size]
         cap = self.cfg.final_logit_softcapping
         if cap:
-            logits = cap * torch.tanh(logits / cap)
+            logits = cap * torch.tanh(logits.float() / cap)
+        elif not logits.is_cuda:
+            logits = logits.float()
+        # on the GPU the logits stay in the GEMM's bf16 (a strided view past a padded
+        # vocabulary): the sampling kernel reads bf16 rows directly, host-side paths cast
         return logits
 
 

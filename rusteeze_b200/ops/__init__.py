@@ -110,6 +110,41 @@ def rope_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Te
 
 
 # ----------------------------------------------------------------------------- activations
+def embedding(ids: torch.Tensor, table: torch.Tensor, lo: int = 0, vocab: Optional[int] = None,
+              scale: float = 1.0) -> torch.Tensor:
+    """Rows of a (vocab-parallel) embedding table: table holds vocabulary rows [lo, lo +
+    rows); ids outside that range give zero rows (another rank's share), every row is
+    multiplied by `scale` (Gemma's sqrt(hidden))."""
+    hi = lo + table.shape[0]
+    vocab = hi if vocab is None else vocab
+    if not ids.is_cuda:
+        local = ids - lo
+        ok = (local >= 0) & (local < table.shape[0])
+        h = table[local.clamp(0, table.shape[0] - 1)] * ok.unsqueeze(1).to(table.dtype)
+        return h * torch.tensor(scale, dtype=table.dtype) if scale != 1.0 else h
+    out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    if ids.numel():
+        cuda_ext().embedding(out, table, ids.contiguous().view(-1), lo, hi, vocab, float(scale))
+        _LAUNCHES[0] += 1
+    return out
+
+
+def layer_norm(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], eps: float,
+               residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """LayerNorm with fp32 statistics (bias optional); with `residual`, residual += x first
+    (in place) and the sum is normalised."""
+    if not x.is_cuda:
+        if residual is not None:
+            residual.add_(x)
+            x = residual
+        return ref.layer_norm(x, w, b, eps).to(x.dtype)
+    out = torch.empty_like(x)
+    if x.shape[0]:
+        cuda_ext().layer_norm(out, x.contiguous(), residual, w, b, float(eps))
+        _LAUNCHES[0] += 1
+    return out
+
+
 def silu_mul(x: torch.Tensor) -> torch.Tensor:
     if not x.is_cuda:
         return ref.silu_mul(x)
@@ -195,13 +230,36 @@ def deinterleave_gate_up(w_il: torch.Tensor, block: int = 64) -> torch.Tensor:
     return torch.cat([v[:, 0].reshape(I, K), v[:, 1].reshape(I, K)], dim=0)
 
 
-def linear_silu_mul(x: torch.Tensor, w_il: torch.Tensor) -> torch.Tensor:
-    """silu(x @ Wg.T) * (x @ Wu.T) in one GEMM; w_il from interleave_gate_up."""
+GATE_GELU = 1 << 8     # epilogue flag: GELU(tanh) instead of SiLU as the gate activation
+
+
+def _gate(act: str) -> int:
+    if act in ("silu", "swiglu"):
+        return 0
+    if act in ("gelu_tanh", "gelu", "gelu_pytorch_tanh", "geglu"):
+        return GATE_GELU
+    raise ValueError(f"unsupported gate activation {act!r}")
+
+
+def linear_silu_mul(x: torch.Tensor, w_il: torch.Tensor, act: str = "silu") -> torch.Tensor:
+    """act(x @ Wg.T) * (x @ Wu.T) in one GEMM (act: SiLU, or GELU-tanh for GeGLU MLPs);
+    w_il from interleave_gate_up."""
     M = x.shape[0]
     out = torch.empty(M, w_il.shape[0] // 2, dtype=x.dtype, device=x.device)
     if M == 0:
         return out
-    _LAUNCHES[0] += cuda_ext().gemm_bf16_ex(out, x, w_il, None, None, 1, 0, 0)
+    _LAUNCHES[0] += cuda_ext().gemm_bf16_ex(out, x, w_il, None, None, 1 | _gate(act), 0, 0)
+    return out
+
+
+def _act_mul_interleaved(y: torch.Tensor, act: str) -> torch.Tensor:
+    """act(gate) * up on GEMM output whose columns are interleaved [gate 64 | up 64] blocks:
+    every 128-column block is one [gate | up] row of the activation kernel."""
+    M, N = y.shape
+    out = torch.empty(M, N // 2, dtype=y.dtype, device=y.device)
+    if M:
+        cuda_ext().act_mul(out.view(M * (N // 128), 64), y.view(M * (N // 128), 128), 0 if _gate(act) == 0 else 1)
+        _LAUNCHES[0] += 1
     return out
 
 
@@ -246,37 +304,39 @@ def rms_norm_mxf8(x: torch.Tensor, w: torch.Tensor, eps: float, offset: float = 
 
 def linear_mxf8_q(xq: torch.Tensor, sfa: torch.Tensor, wq: torch.Tensor, wsf: torch.Tensor,
                   bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
-                  silu_mul: bool = False) -> torch.Tensor:
-    """MXFP8 GEMM on an already quantised operand (e.g. from rms_norm_mxf8)."""
+                  silu_mul: bool = False, act: str = "silu") -> torch.Tensor:
+    """MXFP8 GEMM on an already quantised operand (e.g. from rms_norm_mxf8); with
+    silu_mul the gated epilogue applies `act` (SiLU or GELU-tanh) to the gate."""
     M, N = xq.shape[0], wq.shape[0]
     out = torch.empty(M, N // 2 if silu_mul else N, dtype=torch.bfloat16, device=xq.device)
     if M:
-        _LAUNCHES[0] += cuda_ext().gemm_mxf8(out, xq, sfa, wq, wsf, bias, residual, 1 if silu_mul else 0, 0, 0)
+        epi = (1 | _gate(act)) if silu_mul else 0
+        _LAUNCHES[0] += cuda_ext().gemm_mxf8(out, xq, sfa, wq, wsf, bias, residual, epi, 0, 0)
     return out
 
 
 def linear_mxf8_silu_q(xq: torch.Tensor, sfa: torch.Tensor, wq: torch.Tensor, wsf: torch.Tensor,
-                       bias: Optional[torch.Tensor] = None):
+                       bias: Optional[torch.Tensor] = None, act: str = "silu"):
     """gate/up MXFP8 GEMM (rows interleaved in 64-row blocks) whose epilogue
-    emits SiLU(gate)*up directly as the next MXFP8 operand (e4m3 + scales)."""
+    emits act(gate)*up directly as the next MXFP8 operand (e4m3 + scales)."""
     M, N = xq.shape[0], wq.shape[0]
     q = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=xq.device)
     sf = torch.empty((M + 127) // 128, N // 256, 512, dtype=torch.uint8, device=xq.device)
     if M:
-        _LAUNCHES[0] += cuda_ext().gemm_mxf8_silu_q(q, sf, xq, sfa, wq, wsf, bias)
+        _LAUNCHES[0] += cuda_ext().gemm_mxf8_silu_q(q, sf, xq, sfa, wq, wsf, bias, _gate(act) >> 8)
     return q, sf
 
 
 def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
                bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
-               silu_mul: bool = False, wsf: Optional[torch.Tensor] = None) -> torch.Tensor:
+               silu_mul: bool = False, wsf: Optional[torch.Tensor] = None, act: str = "silu") -> torch.Tensor:
     """Block-scaled fp8 GEMM: x bf16 [M,K] is quantised 1x128 on the fly (one
     kernel), wq e4m3 [N,K] carries fp32 128x128 scales ws [N/128, K/128].
     With `wsf` (the same scales as power-of-two UE8M0 chunks) the GEMM applies
     the scales inside the tensor-core MMA (kind::mxf8f6f4.block_scale);
     without it, fp32 scales are applied per 128-K block in the epilogue.
     With silu_mul the weight rows are gate/up interleaved in 64-row blocks and
-    the output is silu(gate) * up with N/2 columns."""
+    the output is act(gate) * up with N/2 columns (act: SiLU or GELU-tanh)."""
     M, N = x.shape[0], wq.shape[0]
     n_out = N // 2 if silu_mul else N
     if not x.is_cuda:
@@ -290,7 +350,9 @@ def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
             y = y + bias.float()
         if silu_mul:
             v = y.view(M, N // 128, 2, 64)
-            y = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(M, n_out)
+            g = (torch.nn.functional.silu(v[:, :, 0]) if _gate(act) == 0
+                 else torch.nn.functional.gelu(v[:, :, 0], approximate="tanh"))
+            y = (g * v[:, :, 1]).reshape(M, n_out)
         if residual is not None:
             y = y + residual.float()
         return y.to(x.dtype)
@@ -299,9 +361,15 @@ def linear_fp8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
         return out
     if wsf is not None:
         xq, sfa = quant_mxf8_act(x)
-        _LAUNCHES[0] += cuda_ext().gemm_mxf8(out, xq, sfa, wq, wsf, bias, residual, 1 if silu_mul else 0, 0, 0)
+        epi = (1 | _gate(act)) if silu_mul else 0
+        _LAUNCHES[0] += cuda_ext().gemm_mxf8(out, xq, sfa, wq, wsf, bias, residual, epi, 0, 0)
         return out
     xq, xs = quant_fp8_act(x)
+    if silu_mul and _gate(act):
+        # the fp32-scale kernel's gated epilogue is SiLU: GELU gates run on the full output
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+        _LAUNCHES[0] += cuda_ext().gemm_fp8_block(y, xq, xs, wq, ws, bias, residual, 0, 0)
+        return _act_mul_interleaved(y, act)
     _LAUNCHES[0] += cuda_ext().gemm_fp8_block(out, xq, xs, wq, ws, bias, residual, 1 if silu_mul else 0, 0)
     return out
 

@@ -198,12 +198,14 @@ class FusedTP:
         return out
 
     def gemm_ag(self, g: torch.Tensor, w: torch.Tensor, call_idx: int, bias: Optional[torch.Tensor] = None,
-                silu_mul: bool = False) -> torch.Tensor:
+                silu_mul: bool = False, act: str = "silu") -> torch.Tensor:
+        """GEMM on the gathered rows; with silu_mul the gated epilogue applies `act`
+        (SiLU, or GELU-tanh for GeGLU MLPs) to interleaved gate/up weight rows."""
         M = g.shape[0]
         n_out = w.shape[0] // 2 if silu_mul else w.shape[0]
         out = torch.empty(M, n_out, dtype=torch.bfloat16, device=g.device)
-        ops.add_launches(ops.cuda_ext().gemm_ag(out, g, w, bias, 1 if silu_mul else 0, self.ag_flag, self.epoch,
-                                                call_idx))
+        epi = (1 | ops._gate(act)) if silu_mul else 0
+        ops.add_launches(ops.cuda_ext().gemm_ag(out, g, w, bias, epi, self.ag_flag, self.epoch, call_idx))
         return out
 
     def wait_gathered(self, M: int, call_idx: int) -> None:

@@ -234,7 +234,8 @@ def _gemm_ag():
 def _moe_combine_peer():
     """Mixtral-8x7B expert layer on a one-rank FusedTP group (all 8 experts local, 2048
     tokens): route, grouped expert GEMMs and the combine kernel that stores every weighted
-    expert row into its owner's slot -- the capture selects the combine."""
+    expert row into its owner's slot -- the capture selects the combine.  A one-rank group
+    has one slot per row, so the case routes top-1 (the combine kernel is the same)."""
     t = _fused_tp_one_rank(M=2048, H=4096, K=4096, N=4096)
     if "moe" not in t:
         E, I = 8, 14336
@@ -243,7 +244,7 @@ def _moe_combine_peer():
         w2 = _bf(E, 4096, I, scale=0.02)
         t["moe"] = (router, w13, w2)
     router, w13, w2 = t["moe"]
-    return lambda: t["F"].moe(t["g"], router, w13, w2, 2, 0, 1, 2)
+    return lambda: t["F"].moe(t["g"], router, w13, w2, 1, 0, 1, 2)
 
 
 @case("peer_all_reduce_1rank", "peer_all_reduce_kernel")

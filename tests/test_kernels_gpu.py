@@ -404,3 +404,62 @@ def test_bounded_peer_wait_reports_timeout_and_context_survives():
     C().status().zero_()
     x = torch.randn(64, 64, device=DEV)
     assert torch.allclose((x @ x.t()).cpu(), x.cpu() @ x.cpu().t(), atol=1e-3)
+
+
+# ----------------------------------------------------------------------------- embedding / LayerNorm / GeGLU
+def test_embedding_vocab_shard_and_scale():
+    torch.manual_seed(21)
+    V, H, lo, rows = 1000, 512, 300, 250
+    full = torch.randn(V, H, dtype=torch.bfloat16)
+    ids = torch.randint(0, V, (77,))
+    out = ops.embedding(ids.to(DEV), full[lo:lo + rows].to(DEV), lo, V, 7.5)
+    own = (ids >= lo) & (ids < lo + rows)
+    want = full.float()[ids] * 7.5 * own.unsqueeze(1).float()
+    assert rel_err(out, want) < 5e-3
+    assert (out.float().cpu()[~own] == 0).all()
+
+
+@pytest.mark.parametrize("H,bias,res", [(512, True, False), (4096, False, True), (5120, True, True)])
+def test_layer_norm(H, bias, res):
+    torch.manual_seed(22)
+    x = torch.randn(37, H, dtype=torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H)).to(torch.bfloat16)
+    b = (0.1 * torch.randn(H)).to(torch.bfloat16) if bias else None
+    r = torch.randn(37, H, dtype=torch.bfloat16) if res else None
+    want_x = (x.float() + r.float()).to(torch.bfloat16) if res else x
+    want = ref.layer_norm(want_x, w, b, 1e-5)
+    rd = r.to(DEV) if res else None
+    y = ops.layer_norm(x.to(DEV), w.to(DEV), b.to(DEV) if bias else None, 1e-5, residual=rd)
+    assert rel_err(y, want) < 1e-2
+    if res:
+        assert torch.equal(rd.cpu(), want_x)
+
+
+@pytest.mark.parametrize("M", [7, 300])
+def test_gelu_gated_epilogue_bf16_and_mxfp8(M):
+    """GELU(tanh)(gate) * up in the GEMM epilogue (Gemma's GeGLU), bf16 and MXFP8 (bf16
+    output and the re-quantised MXFP8 operand) vs the fp32 oracle."""
+    torch.manual_seed(23)
+    K, I = 1024, 512
+    x = torch.randn(M, K, dtype=torch.bfloat16, device=DEV)
+    wg = (torch.randn(I, K) * 0.05).to(torch.bfloat16)
+    wu = (torch.randn(I, K) * 0.05).to(torch.bfloat16)
+    w_il = ops.interleave_gate_up(torch.cat([wg, wu]).to(DEV))
+    g, u = x.float() @ wg.to(DEV).float().t(), x.float() @ wu.to(DEV).float().t()
+    want = torch.nn.functional.gelu(g, approximate="tanh") * u
+    assert rel_err(ops.linear_silu_mul(x, w_il, act="gelu_tanh"), want) < 1.5e-2
+    assert rel_err(ops.linear_silu_mul(x, w_il, act="silu"), torch.nn.functional.silu(g) * u) < 1.5e-2
+    # MXFP8: weights and activations quantised, compare against the dequantised oracle
+    q, s = ref.quant_mxf8_weight(w_il.float().cpu())
+    wsf = ref.pack_block_scales_ue8m0(s).to(DEV)
+    wdq = (q.float().view(-1, 128, K // 128, 128) * s[:, None, :, None]).view(2 * I, K)
+    xq, sfa = ops.quant_mxf8_act(x)
+    xr_q, xr_s = ref.quant_mxf8_act(x.cpu())
+    xdq = (xr_q.float().view(M, K // 128, 128) * xr_s.unsqueeze(-1)).view(M, K)
+    y = (xdq @ wdq.t()).view(M, I // 64, 2, 64)
+    want_mx = (torch.nn.functional.gelu(y[:, :, 0], approximate="tanh") * y[:, :, 1]).reshape(M, I)
+    out = ops.linear_mxf8_q(xq, sfa, q.to(DEV), wsf, silu_mul=True, act="gelu_tanh")
+    assert rel_err(out, want_mx) < 2e-2
+    oq, osf = ops.linear_mxf8_silu_q(xq, sfa, q.to(DEV), wsf, act="gelu_tanh")
+    o_deq = (oq.float().cpu().view(M, I // 128, 128) * ref.unpack_act_scales_ue8m0(osf.cpu(), M, I).unsqueeze(-1))
+    assert rel_err(o_deq.view(M, I), want_mx) < 6e-2
