@@ -715,8 +715,7 @@ void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10
                 torch::Tensor residual, torch::Tensor w, double eps, double offset, std::vector<int64_t> gathers,
                 std::vector<int64_t> ag_flags, int64_t rank, int64_t M, int64_t rs_rows, torch::Tensor epoch,
                 int64_t call_idx, int64_t moe_topk, c10::optional<torch::Tensor> moe_flag,
-                std::vector<int64_t> gathers_q, std::vector<int64_t> gathers_sf,
-                c10::optional<torch::Tensor> ag_cnt) {
+                std::vector<int64_t> gathers_q, std::vector<int64_t> gathers_sf) {
   const at::cuda::CUDAGuard rz_guard(slots.device());
   CHECK_BF16(residual); CHECK_BF16(w);
   const int world = static_cast<int>(gathers.size());
@@ -744,7 +743,6 @@ void rs_norm_ag(torch::Tensor slots, torch::Tensor rs_flag, int64_t n_tiles, c10
     p.moe_flag = reinterpret_cast<const uint32_t*>(moe_flag->data_ptr());
   }
   p.jitter_ns = g_comm_jitter_ns;
-  p.ag_cnt = ag_cnt.has_value() ? reinterpret_cast<uint32_t*>(ag_cnt->data_ptr()) : nullptr;
   p.mx = gathers_q.empty() ? 0 : 1;
   if (p.mx) {
     TORCH_CHECK(gathers_q.size() == gathers.size() && gathers_sf.size() == gathers.size(),
@@ -904,8 +902,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("residual"), py::arg("w"), py::arg("eps"), py::arg("offset"), py::arg("gathers"),
         py::arg("ag_flags"), py::arg("rank"), py::arg("M"), py::arg("rs_rows"), py::arg("epoch"),
         py::arg("call_idx"), py::arg("moe_topk"), py::arg("moe_flag"),
-        py::arg("gathers_q") = std::vector<int64_t>{}, py::arg("gathers_sf") = std::vector<int64_t>{},
-        py::arg("ag_cnt") = py::none());
+        py::arg("gathers_q") = std::vector<int64_t>{}, py::arg("gathers_sf") = std::vector<int64_t>{});
   m.def("gemm_peer_rs_mx", &gemm_peer_rs_mx);
   m.def("set_comm_jitter_ns", &set_comm_jitter_ns);
   m.def("gemm_mxf8_ag", &gemm_mxf8_ag);

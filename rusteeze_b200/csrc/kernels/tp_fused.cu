@@ -51,15 +51,13 @@ __device__ __forceinline__ uint4 pack8f(const float* v) {
   return u;
 }
 
-// 16 warps per block.  ROWS = 8: 2 warps (64 threads) per own row, block b covers rows
-// [row0 + 8b, row0 + 8b + 8) and releases their all-gather flag itself.  ROWS = 1 (few
-// own rows): all 16 warps on one row, and the 8 CTAs of a flag block meet on an arrival
-// counter.  Thread t of a row owns the 8-column chunks t, t + 512 / ROWS, ...: CH chunks,
-// kept in registers between the sum, the norm and the all-gather so the residual is read
-// once.
+// 16 warps per block, 2 warps (64 threads) per own row: block b covers rows
+// [row0 + 8b, row0 + 8b + 8) (one all-gather flag block) and releases their flag itself.
+// Thread t of a row owns the 8-column chunks t, t + 64, ...: CH chunks, kept in registers
+// between the sum, the norm and the all-gather so the residual is read once.
 constexpr int kRsThreads = 512;
 
-template <int CH, int ROWS>
+template <int CH, int ROWS = kAgRowBlock>
 __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p) {
   constexpr int kRowThreads = kRsThreads / ROWS;
   constexpr int kRowWarps = kRowThreads / 32;
@@ -93,7 +91,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
     }
   }
   __syncthreads();
-  static_assert(ROWS == 1 || ROWS == kAgRowBlock, "a CTA holds one row or one whole flag block");
+  static_assert(ROWS == kAgRowBlock, "a CTA holds one whole flag block");
   __shared__ float s_ss[ROWS][kRowWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rr = warp / kRowWarps, sub = warp % kRowWarps;   // row of the block, warp within the row
@@ -106,28 +104,61 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
   if (live) {
     __nv_bfloat16* res = p.residual + static_cast<size_t>(li) * p.H;
     const int nsrc = p.reduce ? (p.moe_topk > 0 ? p.moe_topk : p.world) : 0;
+    // chunks in groups of G with every load of a group issued before the first add, so a
+    // thread keeps G (then G per source) 16-byte loads in flight instead of one
+    constexpr int G = CH < 4 ? CH : 4;
 #pragma unroll
-    for (int j = 0; j < CH; ++j) {
-      const int c = (tr + j * kRowThreads) * 8;
-      if (c < p.H) {
-        float x[8], t[8];
-        if (p.reduce) {
-          ld8f(res + c, x);
-          for (int s = 0; s < nsrc; ++s) {
-            ld8f(p.slots + (static_cast<size_t>(s) * p.rs_rows + li) * p.H + c, t);
+    for (int j0 = 0; j0 < CH; j0 += G) {
+      float x[G][8];
+      uint4 raw[G];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) x[i] += t[i];
-          }
-        } else {
-          ld8f(p.resid_in + static_cast<size_t>(row) * p.H + c, x);
-        }
-        xr[j] = pack8f(x);
-        *reinterpret_cast<uint4*>(res + c) = xr[j];
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xr[j]);
+      for (int q = 0; q < G; ++q) {
+        const int c = (tr + (j0 + q) * kRowThreads) * 8;
+        raw[q] = make_uint4(0u, 0u, 0u, 0u);
+        if (c < p.H)
+          raw[q] = *reinterpret_cast<const uint4*>(p.reduce ? res + c : p.resid_in + static_cast<size_t>(row) * p.H + c);
+      }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {                        // normalise the rounded residual
+      for (int q = 0; q < G; ++q) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
           const float2 f = __bfloat1622float2(h[i]);
-          ss += f.x * f.x + f.y * f.y;
+          x[q][2 * i] = f.x;
+          x[q][2 * i + 1] = f.y;
+        }
+      }
+      for (int s = 0; s < nsrc; ++s) {
+        const __nv_bfloat16* slot = p.slots + (static_cast<size_t>(s) * p.rs_rows + li) * p.H;
+#pragma unroll
+        for (int q = 0; q < G; ++q) {
+          const int c = (tr + (j0 + q) * kRowThreads) * 8;
+          raw[q] = c < p.H ? *reinterpret_cast<const uint4*>(slot + c) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int q = 0; q < G; ++q) {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            x[q][2 * i] += f.x;
+            x[q][2 * i + 1] += f.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < G; ++q) {
+        const int j = j0 + q;
+        const int c = (tr + j * kRowThreads) * 8;
+        if (c < p.H) {
+          xr[j] = pack8f(x[q]);
+          *reinterpret_cast<uint4*>(res + c) = xr[j];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xr[j]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {                      // normalise the rounded residual
+            const float2 f = __bfloat1622float2(h[i]);
+            ss += f.x * f.x + f.y * f.y;
+          }
         }
       }
     }
@@ -211,55 +242,57 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgParams p
   // publish: the block barrier orders every thread's stores before the flag thread's
   // system-scope fence + release (cumulative), so one fence per destination suffices
   __syncthreads();
-  if (ROWS == kAgRowBlock) {
-    if (threadIdx.x < p.world && g0 < p.M) {
-      jitter_ns(p.jitter_ns, epoch + 1u, blockIdx.x, threadIdx.x);
-      __threadfence_system();
-      st_release_sys_u32(p.ag_flag[threadIdx.x] + g0 / kAgRowBlock, epoch);
-    }
-  } else if (threadIdx.x == 0 && g0 < p.M) {
-    // one-row CTAs: the last of the flag block's live rows to arrive releases its flags
-    const int fb = g0 / kAgRowBlock, fb0 = fb * kAgRowBlock;
-    const int live_rows = min(min(p.M, own0 + p.rs_rows), fb0 + kAgRowBlock) - fb0;
-    jitter_ns(p.jitter_ns, epoch + 1u, blockIdx.x, 0u);
+  if (threadIdx.x < p.world && g0 < p.M) {
+    jitter_ns(p.jitter_ns, epoch + 1u, blockIdx.x, threadIdx.x);
     __threadfence_system();
-    const uint32_t prev = atomicAdd(p.ag_cnt + fb, 1u);
-    if (prev == static_cast<uint32_t>(live_rows - 1)) {
-      __threadfence_system();
-      for (int d = 0; d < p.world; ++d) st_release_sys_u32(p.ag_flag[d] + fb, epoch);
-      atomicExch(p.ag_cnt + fb, 0u);                       // ready for the next call
-    }
+    st_release_sys_u32(p.ag_flag[threadIdx.x] + g0 / kAgRowBlock, epoch);
   }
   pdl_wait();   // complete only after the primary grid
 }
 
 __global__ void tp_epoch_bump_kernel(uint32_t* ep) { *ep += 1u; }
 
-// one warp per (token, slot) pair
+// One warp per group of 8 consecutive (token, slot) pairs: the warp stores the group's
+// weighted rows, then one lane fences once (system scope) and releases the group's flags.
+// A fence per row made the kernel fence-bound (membar stalls dominated); the owner still
+// waits per (row, slot) flag.
+constexpr int kMoePairsPerWarp = 8;
 __global__ void __launch_bounds__(256) moe_combine_peer_kernel(MoeCombinePeerParams p) {
   const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) * 256u + p.call_idx + 1u;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int pairs = p.M * p.topk;
-  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < pairs; i += gridDim.x * warps) {
-    const int pos = p.pos_of[i];
-    if (pos < 0) continue;                                   // warp-uniform: the expert is on another rank
-    const int t = i / p.topk, k = i % p.topk;
-    const int owner = t / p.rs_rows, li = t - owner * p.rs_rows;
-    const float w = p.topk_w[i];
-    const __nv_bfloat16* src = p.y + static_cast<size_t>(pos) * p.H;
-    __nv_bfloat16* dst = p.slot[owner] + (static_cast<size_t>(k) * p.rs_rows + li) * p.H;
-    for (int c = lane * 8; c < p.H; c += 256) {
-      float v[8];
-      ld8f(src + c, v);
+  const int groups = (pairs + kMoePairsPerWarp - 1) / kMoePairsPerWarp;
+  for (int gi = blockIdx.x * warps + (threadIdx.x >> 5); gi < groups; gi += gridDim.x * warps) {
+    const int i0 = gi * kMoePairsPerWarp;
+    const int i1 = min(pairs, i0 + kMoePairsPerWarp);
+    bool any = false;
+    for (int i = i0; i < i1; ++i) {
+      const int pos = p.pos_of[i];
+      if (pos < 0) continue;                                 // warp-uniform: the expert is on another rank
+      any = true;
+      const int t = i / p.topk, k = i % p.topk;
+      const int owner = t / p.rs_rows, li = t - owner * p.rs_rows;
+      const float w = p.topk_w[i];
+      const __nv_bfloat16* src = p.y + static_cast<size_t>(pos) * p.H;
+      __nv_bfloat16* dst = p.slot[owner] + (static_cast<size_t>(k) * p.rs_rows + li) * p.H;
+      for (int c = lane * 8; c < p.H; c += 256) {
+        float v[8];
+        ld8f(src + c, v);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] *= w;
-      *reinterpret_cast<uint4*>(dst + c) = pack8f(v);
+        for (int j = 0; j < 8; ++j) v[j] *= w;
+        *reinterpret_cast<uint4*>(dst + c) = pack8f(v);
+      }
     }
     __syncwarp();
-    if (lane == 0) {
-      jitter_ns(p.jitter_ns, epoch, static_cast<uint32_t>(i), blockIdx.x);
-      __threadfence_system();
-      st_release_sys_u32(p.flag[owner] + static_cast<size_t>(k) * p.rs_rows + li, epoch);
+    if (lane == 0 && any) {
+      jitter_ns(p.jitter_ns, epoch, static_cast<uint32_t>(gi), blockIdx.x);
+      __threadfence_system();      // orders the whole warp's row stores (after the warp barrier)
+      for (int i = i0; i < i1; ++i) {
+        if (p.pos_of[i] < 0) continue;
+        const int t = i / p.topk, k = i % p.topk;
+        const int owner = t / p.rs_rows, li = t - owner * p.rs_rows;
+        st_release_sys_u32(p.flag[owner] + static_cast<size_t>(k) * p.rs_rows + li, epoch);
+      }
     }
   }
 }
@@ -275,7 +308,8 @@ int moe_combine_peer_launch(const MoeCombinePeerParams& p, cudaStream_t st) {
   if (p.H % 8 != 0) return -1;
   const int pairs = p.M * p.topk;
   if (pairs == 0) return 0;
-  int blocks = (pairs + 7) / 8;
+  const int groups = (pairs + kMoePairsPerWarp - 1) / kMoePairsPerWarp;
+  int blocks = (groups + 7) / 8;
   blocks = blocks > 1024 ? 1024 : blocks;
   moe_combine_peer_kernel<<<blocks, 256, 0, st>>>(p);
   return static_cast<int>(cudaGetLastError());
@@ -289,16 +323,6 @@ int ag_wait_launch(const uint32_t* ag_flag, int M, const uint32_t* epoch_ptr, ui
   return static_cast<int>(cudaGetLastError());
 }
 
-static int device_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
 
 int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st) {
   if (p.rs_rows % kAgRowBlock != 0 || p.H % 8 != 0 || p.H > kRsNormAgMaxH || p.world > kMaxTpRanks ||
@@ -306,20 +330,13 @@ int rs_norm_ag_launch(const RsNormAgParams& p, cudaStream_t st) {
     return -1;
   const int own = min(p.M, (p.rank + 1) * p.rs_rows) - p.rank * p.rs_rows;
   if (own <= 0) return 0;
-  // few own rows (decode at high TP): one row per CTA spreads the row blocks over the SMs
-  const bool fine = p.ag_cnt != nullptr && (own + kAgRowBlock - 1) / kAgRowBlock < device_sms();
-  void (*k)(RsNormAgParams);
-  if (fine) {
-    const int ch = (p.H / 8 + kRsThreads - 1) / kRsThreads;
-    k = ch <= 1 ? rs_norm_ag_kernel<1, 1> : rs_norm_ag_kernel<2, 1>;
-  } else {
-    const int ch = (p.H / 8 + kRsThreads / kAgRowBlock - 1) / (kRsThreads / kAgRowBlock);
-    k = ch <= 4 ? rs_norm_ag_kernel<4, kAgRowBlock>
-               : ch <= 8 ? rs_norm_ag_kernel<8, kAgRowBlock>
-                         : ch <= 12 ? rs_norm_ag_kernel<12, kAgRowBlock> : rs_norm_ag_kernel<16, kAgRowBlock>;
-  }
+  const int ch = (p.H / 8 + kRsThreads / kAgRowBlock - 1) / (kRsThreads / kAgRowBlock);
+  void (*k)(RsNormAgParams) = ch <= 4    ? rs_norm_ag_kernel<4>
+                              : ch <= 8  ? rs_norm_ag_kernel<8>
+                              : ch <= 12 ? rs_norm_ag_kernel<12>
+                                         : rs_norm_ag_kernel<16>;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(fine ? own : (own + kAgRowBlock - 1) / kAgRowBlock);
+  cfg.gridDim = dim3((own + kAgRowBlock - 1) / kAgRowBlock);
   cfg.blockDim = dim3(kRsThreads);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -36,9 +36,6 @@ struct RsNormAgParams {
   uint8_t* gather_q[kMaxTpRanks];
   uint8_t* gather_sf[kMaxTpRanks];
   uint32_t jitter_ns;                  // race testing: random pauses before stores and flags (0: off)
-  // one row per CTA (few own rows): the CTAs of a flag block meet on ag_cnt[flag block]
-  // (local, zeroed, reset by the last arrival), which releases the all-gather flags
-  uint32_t* ag_cnt;
 };
 
 // Expert-parallel combine: every local (token, slot) pair's weighted expert output row goes

@@ -106,10 +106,6 @@ class FusedTP:
         jitter = int(os.environ.get("RZ_TP_JITTER_NS", "0") or 0)
         if jitter:
             ops.cuda_ext().set_comm_jitter_ns(jitter)
-        # RZ_RSN_FINE=1: with few own rows the add+RMSNorm+all-gather runs one row per CTA,
-        # whose flag blocks meet on these (local, self-resetting) arrival counters
-        self.ag_cnt = (torch.zeros(n_ag_flags, dtype=torch.int32, device=device)
-                       if os.environ.get("RZ_RSN_FINE", "0") == "1" else None)
         dist.barrier(group=self.group)
 
     # ------------------------------------------------------------------ shapes
@@ -138,7 +134,7 @@ class FusedTP:
         gq, gsf = self._mx_args(mx)
         C.rs_norm_ag(self.slots, self.rs_flag, 1, h.contiguous(), self.residual, norm_w, eps, offset,
                      self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch, 0, 0, None,
-                     gq, gsf, self.ag_cnt)
+                     gq, gsf)
         ops.add_launches(1)
         return self._gathered(M, mx)
 
@@ -166,7 +162,7 @@ class FusedTP:
         gq, gsf = self._mx_args(mx)
         ops.cuda_ext().rs_norm_ag(self.slots, self.rs_flag, self.n_tiles, None, self.residual, norm_w, eps, offset,
                                   self.gather_ptrs, self.ag_flag_ptrs, self.rank, M, self.rs_rows(M), self.epoch,
-                                  call_idx, moe_topk, self.moe_flag if moe_topk else None, gq, gsf, self.ag_cnt)
+                                  call_idx, moe_topk, self.moe_flag if moe_topk else None, gq, gsf)
         ops.add_launches(1)
         return self._gathered(M, mx)
 
