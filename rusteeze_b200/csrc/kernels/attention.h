@@ -22,6 +22,7 @@ struct DecodeAttnParams {
   float scale;
   int window;                     // sliding window (0 = none)
   float softcap;                  // 0 = none
+  const float* alibi;             // [Hq] ALiBi slopes (nullptr = none): logit += slope * (k_pos - q_pos)
   int* status;
 };
 
@@ -45,12 +46,14 @@ struct PrefillAttnParams {
   float scale;
   int window;
   float softcap;
+  const float* alibi;             // [Hq] ALiBi slopes (nullptr = none)
   int* status;
 };
 
 int decode_attention_launch(const DecodeAttnParams& p, cudaStream_t st);
 int prefill_attention_launch(const PrefillAttnParams& p, cudaStream_t st);
-// tcgen05 FlashAttention prefill (head_dim 128, query heads per kv head dividing 128)
+// tcgen05 FlashAttention prefill (head_dim 128, query heads per kv head dividing 128; not
+// ALiBi together with a soft-cap)
 bool prefill_tc_supported(const PrefillAttnParams& p);
 int prefill_tc_launch(const PrefillAttnParams& p, cudaStream_t st);
 

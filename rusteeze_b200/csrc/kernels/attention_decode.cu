@@ -69,7 +69,7 @@ __device__ __forceinline__ uint32_t dswz(int row, int chunk) {
   return static_cast<uint32_t>(row * D * 2 + ((chunk ^ (row & 7)) << 4));
 }
 
-template <int D>
+template <int D, bool ALIBI>
 __global__ void __launch_bounds__(DecCfg<D>::kWarps * 32) decode_attn_kernel(DecodeAttnParams p) {
   using C = DecCfg<D>;
   constexpr int kChunks = D / 8;
@@ -139,6 +139,15 @@ __global__ void __launch_bounds__(DecCfg<D>::kWarps * 32) decode_attn_kernel(Dec
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
   const float sl2 = p.scale * 1.4426950408889634f;
+  // ALiBi slope of the thread's two head rows (lane/4, lane/4 + 8), log2 domain
+  float ab[2] = {0.f, 0.f};
+  if (ALIBI) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = (lane >> 2) + 8 * h;
+      ab[h] = r < G ? p.alibi[kvh * G + r] * 1.4426950408889634f : 0.f;
+    }
+  }
   const int kv_end = min(L, b1 * 16);
 
   for (int j = 0; j < npages; ++j) {
@@ -170,6 +179,7 @@ __global__ void __launch_bounds__(DecCfg<D>::kWarps * 32) decode_attn_kernel(Dec
         float v = s[nt][e];
         if (p.softcap > 0.f) v = p.softcap * tanhf(v * p.scale / p.softcap) * 1.4426950408889634f;
         else v *= sl2;
+        if (ALIBI) v += ab[e >> 1] * static_cast<float>(pos - (L - 1));
         const bool valid = pos < kv_end && (p.window <= 0 || pos > L - 1 - p.window);
         v = valid ? v : -INFINITY;
         s[nt][e] = v;
@@ -273,12 +283,18 @@ __global__ void decode_combine_kernel(DecodeAttnParams p) {
   }
 }
 
+template <int D, bool ALIBI>
+static void launch_dec_main(const DecodeAttnParams& p, cudaStream_t st) {
+  using C = DecCfg<D>;
+  opt_in_smem<decode_attn_kernel<D, ALIBI>>(C::kSmem);
+  const int items = p.num_seqs * p.num_kv_heads * p.num_splits;
+  decode_attn_kernel<D, ALIBI><<<(items + C::kWarps - 1) / C::kWarps, C::kWarps * 32, C::kSmem, st>>>(p);
+}
+
 template <int D>
 static int launch_dec(const DecodeAttnParams& p, cudaStream_t st) {
-  using C = DecCfg<D>;
-  opt_in_smem<decode_attn_kernel<D>>(C::kSmem);
-  const int items = p.num_seqs * p.num_kv_heads * p.num_splits;
-  decode_attn_kernel<D><<<(items + C::kWarps - 1) / C::kWarps, C::kWarps * 32, C::kSmem, st>>>(p);
+  if (p.alibi != nullptr) launch_dec_main<D, true>(p, st);
+  else launch_dec_main<D, false>(p, st);
   if (p.num_splits > 1) decode_combine_kernel<D><<<dim3(p.num_q_heads, p.num_seqs), 128, 0, st>>>(p);
   return static_cast<int>(cudaGetLastError());
 }

@@ -128,6 +128,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnParams p) 
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
   const float sl2 = p.scale * 1.4426950408889634f;  // scale * log2(e)
+  const float ab = p.alibi != nullptr ? p.alibi[qh] * 1.4426950408889634f : 0.f;  // ALiBi slope, log2
   const int row_a = warp * 16 + (lane >> 2);          // this thread's rows: row_a, row_a + 8
   const int qpos_a = qpos_lo + row_a;
 
@@ -170,6 +171,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnParams p) 
         float v = s[nt][e];
         if (p.softcap > 0.f) v = p.softcap * tanhf(v * p.scale / p.softcap) * 1.4426950408889634f;
         else v *= sl2;
+        v += ab * static_cast<float>(kpos - qpos);
         bool masked = kpos > qpos || (p.window > 0 && kpos <= qpos - p.window);
         v = masked ? -INFINITY : v;
         s[nt][e] = v;

@@ -44,7 +44,7 @@ struct PfTcArgs {
   int tiles_per_seq;
 };
 
-template <bool SOFTCAP, bool WINDOW>
+template <bool SOFTCAP, bool WINDOW, bool ALIBI>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       const PfTcArgs a) {
@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int lo = WINDOW ? pos - p.window + 1 : -0x40000000;   // valid kv positions: [lo, pos]
     const float l2e = 1.4426950408889634f;
     const float sc = p.scale * l2e;
+    const float ab = ALIBI ? p.alibi[kvh * a.G + g] * l2e : 0.f;   // ALiBi slope, log2 domain
     float m_use = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_arrive(&s_empty[s]);
       const int c0 = kv_beg + j * 128 + hc * 64;     // kv position of x[0]
       float mx = -INFINITY;
-      if (!SOFTCAP && c0 >= lo && c0 + 63 <= pos) {  // interior tile: nothing masked
+      if (!SOFTCAP && !ALIBI && c0 >= lo && c0 + 63 <= pos) {  // interior tile: nothing masked
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           x[c] *= sc;
@@ -243,6 +244,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           if (SOFTCAP) v = p.softcap * tanhf(v * p.scale / p.softcap) * l2e;
           else v *= sc;
           const int kp = c0 + c;
+          if (ALIBI) v += ab * static_cast<float>(kp - pos);
           v = (kp >= lo && kp <= pos) ? v : -INFINITY;
           x[c] = v;
           mx = fmaxf(mx, v);
@@ -364,6 +366,7 @@ static int make_tmap_paged(CUtensorMap* m, const void* cache, int num_blocks, in
 
 bool prefill_tc_supported(const PrefillAttnParams& p) {
   if (p.head_dim != 128 || p.num_kv_heads <= 0 || p.num_q_heads % p.num_kv_heads) return false;
+  if (p.alibi != nullptr && p.softcap > 0.f) return false;
   const int G = p.num_q_heads / p.num_kv_heads;
   return G >= 1 && G <= 128 && 128 % G == 0 && (p.block_stride * 2) % 16 == 0 &&
          (reinterpret_cast<uintptr_t>(p.k_cache) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.v_cache) & 15) == 0;
@@ -380,16 +383,18 @@ int prefill_tc_launch(const PrefillAttnParams& p, cudaStream_t st) {
   if (make_tmap_paged(&tk, p.k_cache, p.num_blocks, p.num_kv_heads, p.block_stride)) return -2;
   if (make_tmap_paged(&tv, p.v_cache, p.num_blocks, p.num_kv_heads, p.block_stride)) return -3;
   dim3 grid(p.num_seqs * a.tiles_per_seq, p.num_kv_heads);
-#define RZ_PF(SC, WIN)                                                                                    \
+#define RZ_PF(SC, WIN, AL)                                                                                \
   {                                                                                                       \
-    opt_in_smem<prefill_tc_kernel<SC, WIN>>(kPfSmem);                                                     \
-    prefill_tc_kernel<SC, WIN><<<grid, kPfThreads, kPfSmem, st>>>(tk, tv, a);                             \
+    opt_in_smem<prefill_tc_kernel<SC, WIN, AL>>(kPfSmem);                                                 \
+    prefill_tc_kernel<SC, WIN, AL><<<grid, kPfThreads, kPfSmem, st>>>(tk, tv, a);                         \
   }
-  const bool sc = p.softcap > 0.f, win = p.window > 0;
-  if (sc && win) RZ_PF(true, true)
-  else if (sc) RZ_PF(true, false)
-  else if (win) RZ_PF(false, true)
-  else RZ_PF(false, false)
+  const bool sc = p.softcap > 0.f, win = p.window > 0, al = p.alibi != nullptr;
+  if (al && win) RZ_PF(false, true, true)
+  else if (al) RZ_PF(false, false, true)
+  else if (sc && win) RZ_PF(true, true, false)
+  else if (sc) RZ_PF(true, false, false)
+  else if (win) RZ_PF(false, true, false)
+  else RZ_PF(false, false, false)
 #undef RZ_PF
   return static_cast<int>(cudaGetLastError());
 }

@@ -128,9 +128,19 @@ void act_mul(torch::Tensor out, torch::Tensor x, int64_t kind) {
            "act_mul");
 }
 
+// ALiBi slopes: fp32 on the device, one per query head of this rank
+static const float* alibi_ptr(const c10::optional<torch::Tensor>& a, int64_t heads) {
+  if (!a.has_value()) return nullptr;
+  CHECK_CUDA(*a);
+  TORCH_CHECK(a->scalar_type() == at::kFloat && a->is_contiguous() && a->numel() == heads,
+              "alibi slopes must be a contiguous fp32 tensor with one slope per query head");
+  return a->data_ptr<float>();
+}
+
 void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                       torch::Tensor seq_lens, torch::Tensor block_tables, c10::optional<torch::Tensor> workspace,
-                      int64_t num_seqs, double scale, int64_t window, double softcap, int64_t num_splits) {
+                      int64_t num_seqs, double scale, int64_t window, double softcap, int64_t num_splits,
+                      c10::optional<torch::Tensor> alibi) {
   const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(q); CHECK_BF16(q);
   rz::DecodeAttnParams p{};
@@ -154,6 +164,7 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   p.scale = scale;
   p.window = window;
   p.softcap = softcap;
+  p.alibi = alibi_ptr(alibi, p.num_q_heads);
   p.status = status_ptr();
   if (num_splits > 1) {
     TORCH_CHECK(workspace.has_value() &&
@@ -167,7 +178,7 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
 void prefill_attention_impl(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                             torch::Tensor qsl, torch::Tensor seq_lens, torch::Tensor block_tables, int64_t seq_offset,
                             int64_t num_seqs, int64_t max_q_len, double scale, int64_t window, double softcap,
-                            int64_t impl) {
+                            int64_t impl, c10::optional<torch::Tensor> alibi) {
   const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(q); CHECK_BF16(q);
   rz::PrefillAttnParams p{};
@@ -192,6 +203,7 @@ void prefill_attention_impl(torch::Tensor out, torch::Tensor q, torch::Tensor k_
   p.scale = scale;
   p.window = window;
   p.softcap = softcap;
+  p.alibi = alibi_ptr(alibi, p.num_q_heads);
   p.status = status_ptr();
   // impl: 0 = tensor-core kernel when the shape allows it (head_dim 128), else mma.sync;
   //       1 = mma.sync kernel; 2 = tensor-core kernel (error if the shape is not supported)
@@ -203,10 +215,11 @@ void prefill_attention_impl(torch::Tensor out, torch::Tensor q, torch::Tensor k_
 
 void prefill_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                        torch::Tensor qsl, torch::Tensor seq_lens, torch::Tensor block_tables, int64_t seq_offset,
-                       int64_t num_seqs, int64_t max_q_len, double scale, int64_t window, double softcap) {
+                       int64_t num_seqs, int64_t max_q_len, double scale, int64_t window, double softcap,
+                       c10::optional<torch::Tensor> alibi) {
   const at::cuda::CUDAGuard rz_guard(out.device());
   prefill_attention_impl(out, q, k_cache, v_cache, qsl, seq_lens, block_tables, seq_offset, num_seqs, max_q_len,
-                         scale, window, softcap, 0);
+                         scale, window, softcap, 0, alibi);
 }
 
 // ---------------------------------------------------------------- GEMM
@@ -884,9 +897,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("act_mul", &act_mul);
   m.def("embedding", &embedding);
   m.def("layer_norm", &layer_norm);
-  m.def("decode_attention", &decode_attention);
-  m.def("prefill_attention", &prefill_attention);
-  m.def("prefill_attention_impl", &prefill_attention_impl);
+  m.def("decode_attention", &decode_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("seq_lens"), py::arg("block_tables"), py::arg("workspace"),
+        py::arg("num_seqs"), py::arg("scale"), py::arg("window"), py::arg("softcap"), py::arg("num_splits"),
+        py::arg("alibi") = py::none());
+  m.def("prefill_attention", &prefill_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("qsl"), py::arg("seq_lens"), py::arg("block_tables"), py::arg("seq_offset"),
+        py::arg("num_seqs"), py::arg("max_q_len"), py::arg("scale"), py::arg("window"), py::arg("softcap"),
+        py::arg("alibi") = py::none());
+  m.def("prefill_attention_impl", &prefill_attention_impl, py::arg("out"), py::arg("q"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("qsl"), py::arg("seq_lens"), py::arg("block_tables"), py::arg("seq_offset"),
+        py::arg("num_seqs"), py::arg("max_q_len"), py::arg("scale"), py::arg("window"), py::arg("softcap"),
+        py::arg("impl"), py::arg("alibi") = py::none());
   m.def("gemm_plan", &gemm_plan);
   m.def("gemm_bf16", &gemm_bf16);
   m.def("gemm_bf16_ex", &gemm_bf16_ex);

@@ -59,6 +59,9 @@ class ModelConfig:
     final_logit_softcapping: Optional[float] = None
     query_pre_attn_scalar: Optional[float] = None
     sliding_window_pattern: int = 0    # gemma2: every 2nd layer (even index) is local
+    # positions: "rope" (rotary q/k) or "alibi" (no rotation; a per-head linear bias on the
+    # attention logits, crates/rusteeze-tensor/src/attention.rs:33-34,341-390)
+    position_embedding: str = "rope"
     name: str = "custom"
 
     def __post_init__(self) -> None:
@@ -131,6 +134,12 @@ class ModelConfig:
             raise ConfigError(f"head_dim {self.head_dim} must be a multiple of 16")
         if self.is_moe and not 0 < self.num_experts_per_tok <= self.num_local_experts:
             raise ConfigError("num_experts_per_tok must be in [1, num_local_experts]")
+        if self.position_embedding not in ("rope", "alibi"):
+            raise ConfigError(f"position_embedding must be rope or alibi, got {self.position_embedding!r}")
+
+    @property
+    def use_alibi(self) -> bool:
+        return self.position_embedding == "alibi"
 
     def to_dict(self) -> dict:
         d = asdict(self)
@@ -172,6 +181,8 @@ class ModelConfig:
             attn_logit_softcapping=d.get("attn_logit_softcapping"),
             final_logit_softcapping=d.get("final_logit_softcapping"),
             query_pre_attn_scalar=d.get("query_pre_attn_scalar"),
+            position_embedding=("alibi" if d.get("alibi") or d.get("position_embedding_type") == "alibi"
+                                else "rope"),
             name=d.get("_name_or_path", "hf"),
         )
         if arch == ModelArchitecture.QWEN2 and not d.get("use_sliding_window", False):
@@ -215,6 +226,8 @@ class ModelConfig:
         for k in ("attn_logit_softcapping", "final_logit_softcapping", "query_pre_attn_scalar"):
             if getattr(self, k) is not None:
                 d[k] = getattr(self, k)
+        if self.use_alibi:
+            d["alibi"] = True
         return d
 
 

@@ -141,9 +141,19 @@ class DecoderLM(nn.Module):
         self.norm = nn.Parameter(e(H), requires_grad=False)
         self.lm_head = (None if cfg.tie_word_embeddings
                         else nn.Parameter(e(self.vocab_hi - self.vocab_lo, H), requires_grad=False))
-        self.register_buffer("cos_sin", ref.rope_cos_sin_cache(
-            D, cfg.max_position_embeddings, cfg.rope_theta, cfg.rope_scaling, device=device),
-            persistent=False)
+        if cfg.use_alibi:
+            # no rotation: the fused RoPE + KV-write kernel runs with a zero-angle table (a
+            # plain cache write) and the attention kernels add slope * (k_pos - q_pos); this
+            # rank's query heads are [tpr * hq, (tpr + 1) * hq)
+            self.register_buffer("cos_sin", ref.identity_cos_sin(D, cfg.max_position_embeddings, device=device),
+                                 persistent=False)
+            self.register_buffer("alibi", ref.alibi_slopes(cfg.num_attention_heads)[
+                tpr * self.hq:(tpr + 1) * self.hq].contiguous().to(device), persistent=False)
+        else:
+            self.register_buffer("cos_sin", ref.rope_cos_sin_cache(
+                D, cfg.max_position_embeddings, cfg.rope_theta, cfg.rope_scaling, device=device),
+                persistent=False)
+            self.alibi = None
         self.moe_impl = None   # set by parallel.moe for EP / fused dispatch
 
     # ------------------------------------------------------------------ helpers
@@ -260,7 +270,7 @@ class DecoderLM(nn.Module):
                                        self.hq, self.hkv, D)
             with sec("attention"):
                 a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
-                                        cfg.attn_logit_softcapping)
+                                        cfg.attn_logit_softcapping, self.alibi)
             with sec("o_gemm_rs"):
                 h = self._row_parallel(a.view(a.shape[0], -1), L, "o")
             if self.is_gemma2:
@@ -355,7 +365,7 @@ class DecoderLM(nn.Module):
                                        self.hq, self.hkv, D)
             with sec("attention"):
                 a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
-                                        cfg.attn_logit_softcapping)
+                                        cfg.attn_logit_softcapping, self.alibi)
             with sec("o_gemm_rs"):
                 if mx:
                     F.gemm_rs_mx(*ops.quant_mxf8_act(a.view(M, -1)), L.o_q, L.o_sf, c_attn)

@@ -43,6 +43,8 @@ def naive_logits(model: DecoderLM, ids) -> torch.Tensor:
         if cfg.attn_logit_softcapping:
             c = cfg.attn_logit_softcapping
             s = c * torch.tanh(s / c)
+        if model.alibi is not None:
+            s = s + ref.alibi_bias(model.alibi.float().cpu(), pos, pos)
         mask = torch.ones(n, n, dtype=torch.bool).triu(1)
         w = L.sliding_window
         if w:

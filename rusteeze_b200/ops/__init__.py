@@ -166,11 +166,13 @@ def gelu_tanh_mul(x: torch.Tensor) -> torch.Tensor:
 # ----------------------------------------------------------------------------- attention
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, meta,
                     scale: float, sliding_window: Optional[int] = None,
-                    softcap: Optional[float] = None) -> torch.Tensor:
-    """q [T, Hq, D] -> out [T, Hq, D].  `meta` is an AttentionMetadata."""
+                    softcap: Optional[float] = None,
+                    alibi: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q [T, Hq, D] -> out [T, Hq, D].  `meta` is an AttentionMetadata; `alibi` holds
+    one fp32 ALiBi slope per query head (None: no positional bias)."""
     if not q.is_cuda:
         return ref.paged_attention(q, k_cache, v_cache, meta.query_start_loc, meta.seq_lens,
-                                   meta.block_tables, scale, sliding_window, softcap)
+                                   meta.block_tables, scale, sliding_window, softcap, alibi)
     out = torch.empty_like(q)
     C = cuda_ext()
     nd = meta.num_decode_seqs
@@ -179,12 +181,12 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     if nd > 0:
         C.decode_attention(out, q, k_cache, v_cache, meta.seq_lens, meta.block_tables,
                            meta.decode_workspace, nd, float(scale), win, cap,
-                           meta.decode_num_splits)
+                           meta.decode_num_splits, alibi)
         _LAUNCHES[0] += 2 if meta.decode_num_splits > 1 else 1
     if meta.num_seqs > nd:
         C.prefill_attention(out, q, k_cache, v_cache, meta.query_start_loc, meta.seq_lens,
                             meta.block_tables, nd, meta.num_seqs - nd, meta.max_query_len,
-                            float(scale), win, cap)
+                            float(scale), win, cap, alibi)
         _LAUNCHES[0] += 1
     return out
 

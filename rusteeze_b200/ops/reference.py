@@ -65,6 +65,37 @@ def rope_cos_sin_cache(head_dim: int, max_pos: int, theta: float, scaling=None,
     return torch.cat([freqs.cos(), freqs.sin()], dim=-1).float().to(device)
 
 
+def identity_cos_sin(head_dim: int, max_pos: int, device=None) -> torch.Tensor:
+    """The cos/sin table of a zero rotation (cos 1, sin 0): models without RoPE (ALiBi)
+    run the fused RoPE + KV-write kernel with it, which then only writes the cache."""
+    t = torch.zeros(max_pos, head_dim, dtype=torch.float32, device=device)
+    t[:, : head_dim // 2] = 1.0
+    return t
+
+
+def alibi_slopes(num_heads: int) -> torch.Tensor:
+    """ALiBi head slopes (Press et al., "Train Short, Test Long", 2022): for n a power of
+    two, head i (1-based) gets 2^(-8 i / n).  Otherwise the n' = 2^floor(log2 n) slopes of
+    that geometric sequence come first, followed by the odd-indexed terms 2^(-8 (2j - 1) /
+    (2 n')), j = 1, 2, ... of the sequence for 2 n' heads (the interleaving the paper's
+    reference code uses).  The reference library's `get_alibi_slopes`
+    (crates/rusteeze-tensor/src/attention.rs:342-368) agrees for powers of two."""
+    def geometric(n: int):
+        return [2.0 ** (-8.0 * i / n) for i in range(1, n + 1)]
+    p = 1 << (max(1, num_heads).bit_length() - 1)
+    slopes = geometric(p)
+    if p < num_heads:
+        slopes += [2.0 ** (-8.0 * (2 * j - 1) / (2 * p)) for j in range(1, num_heads - p + 1)]
+    return torch.tensor(slopes, dtype=torch.float32)
+
+
+def alibi_bias(slopes: torch.Tensor, q_pos: torch.Tensor, k_pos: torch.Tensor) -> torch.Tensor:
+    """[H, q, k] additive logit bias slope_h * (k_pos - q_pos): 0 on the diagonal, more
+    negative the further back the key."""
+    rel = (k_pos.view(1, -1) - q_pos.view(-1, 1)).float()
+    return slopes.float().view(-1, 1, 1) * rel.unsqueeze(0)
+
+
 def rope(q: torch.Tensor, k: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor):
     """Neox (rotate-half) RoPE, in place on q [T,Hq,D] and k [T,Hkv,D]."""
     d = q.shape[-1]
@@ -120,11 +151,13 @@ def gather_kv(cache: torch.Tensor, block_table: torch.Tensor, seq_len: int) -> t
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                     query_start_loc: torch.Tensor, seq_lens: torch.Tensor, block_tables: torch.Tensor,
                     scale: float, sliding_window: Optional[int] = None,
-                    softcap: Optional[float] = None) -> torch.Tensor:
+                    softcap: Optional[float] = None,
+                    alibi: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Varlen causal GQA attention over a paged KV cache.
 
     q: [T, Hq, D]; sequence i owns query rows query_start_loc[i]:query_start_loc[i+1],
-    which are the LAST q_len positions of its seq_lens[i]-long context.
+    which are the LAST q_len positions of its seq_lens[i]-long context.  alibi: [Hq]
+    slopes, added as slope * (k_pos - q_pos) after the soft-cap.
     """
     out = torch.empty_like(q)
     hq, hkv = q.shape[1], k_cache.shape[1]
@@ -143,6 +176,8 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
             s = softcap * torch.tanh(s / softcap)
         qpos = torch.arange(L - ql, L).unsqueeze(1)
         kpos = torch.arange(L).unsqueeze(0)
+        if alibi is not None:
+            s = s + alibi_bias(alibi.cpu(), qpos.view(-1), kpos.view(-1)).to(s.device)
         mask = kpos > qpos
         if sliding_window:
             mask |= kpos <= qpos - sliding_window

@@ -344,6 +344,39 @@ def test_prefill_tcgen05_matches_mma_sync_and_oracle(Hq, Hkv, window, softcap):
     assert int(C().status()[0]) == 0
 
 
+@pytest.mark.parametrize("Hq,Hkv", [(8, 8), (32, 8), (12, 4)])
+@pytest.mark.parametrize("window", [0, 60])
+def test_attention_alibi_matches_oracle(Hq, Hkv, window):
+    """ALiBi slopes (power-of-two and interleaved non-power-of-two head counts) in the decode
+    kernel (1 and 4 splits), the mma.sync prefill kernel and the tcgen05 prefill kernel (where
+    the query heads per kv head divide 128) against the fp32 oracle."""
+    D = 128
+    slopes = ref.alibi_slopes(Hq)
+    specs = [(77, 77), (300, 100), (130, 1), (700, 700), (16, 16)]
+    cache, bt, q, qsl, sl = _paged_setup([s for s, _ in specs], [x for _, x in specs], Hq, Hkv, D, seed=31)
+    kc, vc = cache[:, 0, 0], cache[:, 0, 1]
+    r = ref.paged_attention(q, kc, vc, qsl, sl, bt, D ** -0.5, window or None, None, slopes)
+    cd = cache.to(DEV)
+    al = slopes.to(DEV)
+    for impl in (1, 0):
+        out = torch.zeros(q.shape, device=DEV, dtype=torch.bfloat16)
+        C().prefill_attention_impl(out, q.to(DEV), cd[:, 0, 0], cd[:, 0, 1], qsl.to(DEV), sl.to(DEV), bt.to(DEV),
+                                   0, len(specs), max(x for _, x in specs), D ** -0.5, window, 0.0, impl, al)
+        assert rel_err(out, r) < 1.5e-2, impl
+    # decode: one query row per sequence (the last position)
+    dq_rows = [int(qsl[i + 1]) - 1 for i in range(len(specs))]
+    dq = q[dq_rows].contiguous()
+    dqsl = torch.arange(len(specs) + 1, dtype=torch.int32)
+    rd = ref.paged_attention(dq, kc, vc, dqsl, sl, bt, D ** -0.5, window or None, None, slopes)
+    for splits in (1, 4):
+        ws = torch.empty(len(specs) * Hq * splits * (D + 2), device=DEV)
+        out = torch.zeros(dq.shape, device=DEV, dtype=torch.bfloat16)
+        C().decode_attention(out, dq.to(DEV), cd[:, 0, 0], cd[:, 0, 1], sl.to(DEV), bt.to(DEV), ws, len(specs),
+                             D ** -0.5, window, 0.0, splits, al)
+        assert rel_err(out, rd) < 1e-2, splits
+    assert int(C().status()[0]) == 0
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs a second GPU")
 def test_kernels_on_a_second_device_after_the_first():
     """Kernels that opt in to more than 48 KB of shared memory do so per device: one process

@@ -16,6 +16,8 @@ from rusteeze_b200.models.loader import build_model, load_hf_weights, save_hf_ch
 from rusteeze_b200.models.naive import naive_greedy, naive_logits
 
 ARCHS = [A.LLAMA, A.MISTRAL, A.MIXTRAL, A.QWEN2, A.PHI3, A.GEMMA, A.GEMMA2]
+# GPU oracle cases: every architecture, plus Llama with ALiBi instead of RoPE
+GPU_CASES = [(a, {}) for a in ARCHS] + [(A.LLAMA, {"position_embedding": "alibi"})]
 
 
 def _engine(mc, **kw):
@@ -46,6 +48,55 @@ def test_arch_engine_matches_naive(arch):
                 done[o.request_id] = o.outputs[0].token_ids
     for rid, p in zip(ids, prompts):
         assert done[rid] == naive_greedy(eng.model, p, 10), arch
+
+
+def test_alibi_slopes_follow_the_paper():
+    from rusteeze_b200.ops import reference as ref
+    s8 = ref.alibi_slopes(8)
+    assert torch.allclose(s8, torch.tensor([2.0 ** -i for i in range(1, 9)]))
+    s32 = ref.alibi_slopes(32)
+    assert abs(float(s32[0]) - 2 ** -0.25) < 1e-7 and abs(float(s32[-1]) - 2 ** -8) < 1e-9
+    # 12 heads: the 8 power-of-two slopes, then odd terms of the 16-head sequence
+    s12 = ref.alibi_slopes(12)
+    assert torch.allclose(s12[:8], s8)
+    assert torch.allclose(s12[8:], torch.tensor([2.0 ** (-0.5 * k) for k in (1, 3, 5, 7)]))
+    b = ref.alibi_bias(torch.tensor([0.5]), torch.arange(3, 5), torch.arange(5))
+    assert b.shape == (1, 2, 5) and float(b[0, 1, 4]) == 0.0 and float(b[0, 0, 0]) == -1.5
+
+
+@pytest.mark.parametrize("non_pow2", [False, True])
+def test_alibi_engine_matches_naive(non_pow2):
+    """ALiBi position encoding (no rotation, per-head linear logit bias) through the paged,
+    chunked-prefill engine equals the dense oracle; 8 heads (or 6, a non-power of two)."""
+    mc = tiny_variant(A.LLAMA, position_embedding="alibi", num_attention_heads=6 if non_pow2 else 8,
+                      num_key_value_heads=2, head_dim=32)
+    eng = _engine(mc)
+    assert eng.model.alibi is not None and eng.model.alibi.numel() == mc.num_attention_heads
+    rng = np.random.default_rng(2)
+    prompts = [rng.integers(0, mc.vocab_size, int(n)).tolist() for n in (50, 130, 7)]
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+    ids = [eng.add_request(None, None, sp, p).request_id for p in prompts]
+    done = {}
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            if o.finished:
+                done[o.request_id] = o.outputs[0].token_ids
+    for rid, p in zip(ids, prompts):
+        assert done[rid] == naive_greedy(eng.model, p, 8)
+    # the bias matters: the same weights without it give other logits
+    m = build_model(mc, dtype=torch.float32, seed=4)
+    m_rope = build_model(dataclasses.replace(mc, position_embedding="rope"), dtype=torch.float32, seed=4)
+    assert not torch.allclose(naive_logits(m, prompts[0])[-1], naive_logits(m_rope, prompts[0])[-1], atol=1e-3)
+
+
+def test_alibi_config_roundtrip():
+    mc = tiny_variant(A.LLAMA, position_embedding="alibi")
+    d = mc.to_hf_dict()
+    assert d["alibi"] is True
+    assert ModelConfig.from_hf_dict(d).use_alibi
+    assert not ModelConfig.from_hf_dict({k: v for k, v in d.items() if k != "alibi"}).use_alibi
+    with pytest.raises(Exception):
+        tiny_variant(A.LLAMA, position_embedding="learned")
 
 
 def test_sliding_window_changes_output():
@@ -134,8 +185,8 @@ def test_model_config_parsing_variants():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("arch", ARCHS, ids=[a.value for a in ARCHS])
-def test_arch_gpu_logprobs_match_fp32_oracle(arch):
+@pytest.mark.parametrize("arch,extra", GPU_CASES, ids=[a.value + ("-alibi" if e else "") for a, e in GPU_CASES])
+def test_arch_gpu_logprobs_match_fp32_oracle(arch, extra):
     """Every architecture on the sm_100a kernels (SwiGLU and Gemma's GeGLU in the GEMM's
     gated epilogue, MoE grouped GEMMs, biases, softcaps, windows): the first step's top-5
     logprobs against the dense fp32 CPU oracle on the same weights."""
@@ -144,6 +195,7 @@ def test_arch_gpu_logprobs_match_fp32_oracle(arch):
               head_dim=128, vocab_size=32000)
     if arch == A.GEMMA2:
         kw.update(query_pre_attn_scalar=128)
+    kw.update(extra)
     mc = tiny_variant(arch, **kw)
     cfg = Config()
     cfg.model.device = "cuda:0"
