@@ -205,6 +205,7 @@ def make_config(args, device):
         cfg.model.quantization = QuantizationConfig(method="fp8_block")
     cfg.engine.max_num_seqs = args.max_seqs
     cfg.engine.max_num_batched_tokens = args.max_batched_tokens
+    cfg.engine.kv_cache_dtype = getattr(args, "kv_cache_dtype", "auto")
     cfg.engine.enable_chunked_prefill = True
     cfg.engine.gpu_memory_utilization = 0.88
     cfg.engine.swap_space_gb = 0
@@ -239,6 +240,8 @@ def main():
     ap.add_argument("--dtype", default="fp8", choices=["fp8", "bf16"],
                     help="fp8: block-scaled e4m3 weights (the Llama-3-8B serving configuration); bf16: unquantised")
     ap.add_argument("--fp8", action="store_true", help="same as --dtype fp8 (the default)")
+    ap.add_argument("--kv-cache-dtype", default="auto", choices=["auto", "fp8_e4m3", "fp8_e5m2"],
+                    help="paged KV cache element type (auto: bf16, the configuration the headline is quoted on)")
     ap.add_argument("--eager", action="store_true", help="disable CUDA graphs (profiling runs)")
     ap.add_argument("--parallel", default=None, choices=["dp", "tp"],
                     help="tp: one tensor-parallel engine over all GPUs (default with N > 1); dp: one engine "
@@ -558,8 +561,9 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
         "scaling": "weak",
         "vs_baseline": round(value / REFERENCE_PUBLISHED_TOK_S, 4),
         "vs_baseline_basis": REFERENCE_PUBLISHED_BASIS,
-        "dtype": ("fp8_e4m3 weights (128x128 UE8M0 block scales), 1x128 UE8M0 activation scales, "
-                  "bf16 activations/KV, fp32 accumulate") if args.dtype == "fp8" else "bf16",
+        "dtype": (("fp8_e4m3 weights (128x128 UE8M0 block scales), 1x128 UE8M0 activation scales, "
+                   "bf16 activations, fp32 accumulate") if args.dtype == "fp8" else "bf16")
+                 + (", bf16 KV cache" if args.kv_cache_dtype == "auto" else f", {args.kv_cache_dtype} KV cache"),
         "data": "synthetic requests, random-init N(0,0.02) weights",
         "config": {"model": args.model, "global_batch": args.max_seqs * world,
                    "seq_len": "prompt U[{},{}] + output U[{},{}]".format(*plen, *olen),

@@ -42,6 +42,8 @@ def _model_args(p: argparse.ArgumentParser, required: bool = True) -> None:
     p.add_argument("--gpu-memory-utilization", type=float, default=None)
     p.add_argument("--quantization", default=None, choices=[None, "fp8_block", "fp8"])
     p.add_argument("--enforce-eager", action="store_true", default=None)
+    p.add_argument("--kv-cache-dtype", default=None, choices=["auto", "fp8", "fp8_e4m3", "fp8_e5m2"],
+                   help="paged KV cache element type (fp8: half the bytes per token)")
     p.add_argument("--seed", type=int, default=None)
     p.set_defaults(model_required=required)
 
@@ -58,7 +60,8 @@ def _overrides(a) -> dict:
             model["preset"] = a.model
     if getattr(a, "quantization", None):
         model["quantization"] = {"method": "fp8_block"}
-    eng = {"gpu_memory_utilization": a.gpu_memory_utilization, "enforce_eager": a.enforce_eager}
+    eng = {"gpu_memory_utilization": a.gpu_memory_utilization, "enforce_eager": a.enforce_eager,
+           "kv_cache_dtype": a.kv_cache_dtype}
     return {"model": model, "engine": eng, "server": {"router_policy": a.router_policy}}
 
 

@@ -134,7 +134,7 @@ class EngineSection:
     gpu_memory_utilization: float = 0.9
     num_gpu_blocks: Optional[int] = None      # override the memory-derived count
     swap_space_gb: float = 4.0
-    kv_cache_dtype: str = "auto"              # auto (= model dtype) | bfloat16 | float16
+    kv_cache_dtype: str = "auto"              # auto (= model dtype) | fp8 (= fp8_e4m3) | fp8_e4m3 | fp8_e5m2
     enable_prefix_caching: bool = False
     enable_chunked_prefill: bool = False
     enforce_eager: bool = False               # disable CUDA graphs

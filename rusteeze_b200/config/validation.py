@@ -84,8 +84,9 @@ def collect_errors(cfg) -> List[str]:
                  "the tensor-parallel ranks)")
     if m.quantization is not None and m.quantization.group_size != 128:
         e.append(f"model.quantization.group_size must be 128 (the FP8 GEMM's block), got {m.quantization.group_size}")
-    if g.kv_cache_dtype not in ("auto", m.dtype):
-        e.append(f"engine.kv_cache_dtype must be auto (the model dtype), got {g.kv_cache_dtype!r}")
+    if g.kv_cache_dtype not in ("auto", m.dtype, "fp8", "fp8_e4m3", "fp8_e5m2"):
+        e.append(f"engine.kv_cache_dtype must be auto (the model dtype), fp8, fp8_e4m3 or fp8_e5m2, "
+                 f"got {g.kv_cache_dtype!r}")
     if not g.scheduling.enable_preemption:
         e.append("engine.scheduling.enable_preemption: false is not supported (a full KV cache preempts by "
                  "engine.scheduling.preemption_mode)")

@@ -24,7 +24,13 @@ struct DecodeAttnParams {
   float softcap;                  // 0 = none
   const float* alibi;             // [Hq] ALiBi slopes (nullptr = none): logit += slope * (k_pos - q_pos)
   int* status;
+  // cache element format: kKvBf16, or fp8 (kKvE4m3 / kKvE5m2) with k_cache / v_cache pointing
+  // at bytes, an element holding value / scale (scales are ignored for bf16)
+  int kv_fmt;
+  float k_scale, v_scale;
 };
+
+constexpr int kKvBf16 = 0, kKvE4m3 = 1, kKvE5m2 = 2;
 
 struct PrefillAttnParams {
   __nv_bfloat16* out;             // [T, Hq, D] (row stride out_stride)
@@ -51,6 +57,15 @@ struct PrefillAttnParams {
 };
 
 int decode_attention_launch(const DecodeAttnParams& p, cudaStream_t st);
+// fp8 cache -> bf16 scratch for the prefill kernels: the blocks of sequences
+// [seq_offset, seq_offset + num_seqs) are written densely (sequence by sequence) into
+// k_out / v_out [blocks, Hkv, 16, D], and row seq of bt_out [*, bt_out_stride] maps
+// each of its pages to its scratch block.  Row offsets are prefix sums of ceil(len / 16).
+int kv_dequant_gather_launch(__nv_bfloat16* k_out, __nv_bfloat16* v_out, int32_t* bt_out, int64_t bt_out_stride,
+                             const uint8_t* k_cache, const uint8_t* v_cache, int64_t block_stride, int num_blocks,
+                             const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens,
+                             int seq_offset, int num_seqs, int Hkv, int D, int kv_fmt, float k_scale,
+                             float v_scale, int64_t out_blocks, int* status, cudaStream_t st);
 int prefill_attention_launch(const PrefillAttnParams& p, cudaStream_t st);
 // tcgen05 FlashAttention prefill (head_dim 128, query heads per kv head dividing 128; not
 // ALiBi together with a soft-cap)

@@ -253,6 +253,99 @@ static int launch_prefill(const PrefillAttnParams& p, cudaStream_t st) {
   return static_cast<int>(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------------------- fp8 cache -> bf16
+// Grid (num_seqs, kGatherSplit): CTA (i, y) takes pages y, y + kGatherSplit, ... of sequence
+// seq_offset + i.  Its scratch row offset is the sum of ceil(len / 16) over the earlier
+// sequences, summed by the CTA itself (a few hundred lengths at most).
+constexpr int kGatherSplit = 16;
+constexpr int kGatherThreads = 256;
+
+template <int KVF>
+__device__ __forceinline__ void fp8x8_to_bf16(uint2 raw, float scale, __nv_bfloat16* dst) {
+  const __nv_fp8_interpretation_t fmt = KVF == kKvE4m3 ? __NV_E4M3 : __NV_E5M2;
+  const uint32_t w[2] = {raw.x, raw.y};
+  __align__(16) __nv_bfloat162 out[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(
+        static_cast<__nv_fp8x2_storage_t>((w[k >> 1] >> (16 * (k & 1))) & 0xffffu), fmt);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+    out[k] = __floats2bfloat162_rn(f.x * scale, f.y * scale);
+  }
+  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(out);
+}
+
+template <int KVF>
+__global__ void __launch_bounds__(kGatherThreads) kv_dequant_gather_kernel(
+    __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out, int32_t* __restrict__ bt_out,
+    int64_t bt_out_stride, const uint8_t* __restrict__ k_cache, const uint8_t* __restrict__ v_cache,
+    int64_t block_stride, int num_blocks, const int32_t* __restrict__ block_tables, int64_t bt_stride,
+    const int32_t* __restrict__ seq_lens, int seq_offset, int Hkv, int D, float k_scale, float v_scale,
+    int64_t out_blocks, int* status) {
+  __shared__ int64_t red[kGatherThreads / 32];
+  const int i = blockIdx.x;
+  const int seq = seq_offset + i;
+  int64_t part = 0;
+  for (int k = threadIdx.x; k < i; k += blockDim.x) part += (max(seq_lens[seq_offset + k], 0) + 15) / 16;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+  __syncthreads();
+  int64_t base = 0;
+#pragma unroll
+  for (int w = 0; w < kGatherThreads / 32; ++w) base += red[w];
+  int L = seq_lens[seq];
+  if (L < 0 || L > bt_stride * 16 || L > bt_out_stride * 16) {
+    if (threadIdx.x == 0) set_status(status, kBadArgument);
+    L = 0;
+  }
+  const int nblk = (L + 15) / 16;
+  const int64_t page_elems = static_cast<int64_t>(Hkv) * 16 * D;   // one block of one layer
+  const int chunks = static_cast<int>(page_elems / 8);
+  for (int b = blockIdx.y; b < nblk; b += gridDim.y) {
+    const int64_t dst_blk = base + b;
+    if (dst_blk >= out_blocks) {          // scratch sized by the caller from the same lengths
+      if (threadIdx.x == 0) set_status(status, kBadArgument);
+      return;
+    }
+    int64_t pid = block_tables[static_cast<int64_t>(seq) * bt_stride + b];
+    if (pid < 0 || pid >= num_blocks) {
+      if (threadIdx.x == 0) set_status(status, kBadArgument);
+      pid = 0;
+    }
+    if (threadIdx.x == 0) bt_out[static_cast<int64_t>(seq) * bt_out_stride + b] = static_cast<int32_t>(dst_blk);
+    const uint8_t* ks = k_cache + pid * block_stride;
+    const uint8_t* vs = v_cache + pid * block_stride;
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+      fp8x8_to_bf16<KVF>(*reinterpret_cast<const uint2*>(ks + c * 8), k_scale, k_out + dst_blk * page_elems + c * 8);
+      fp8x8_to_bf16<KVF>(*reinterpret_cast<const uint2*>(vs + c * 8), v_scale, v_out + dst_blk * page_elems + c * 8);
+    }
+  }
+}
+
+int kv_dequant_gather_launch(__nv_bfloat16* k_out, __nv_bfloat16* v_out, int32_t* bt_out, int64_t bt_out_stride,
+                             const uint8_t* k_cache, const uint8_t* v_cache, int64_t block_stride, int num_blocks,
+                             const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens,
+                             int seq_offset, int num_seqs, int Hkv, int D, int kv_fmt, float k_scale,
+                             float v_scale, int64_t out_blocks, int* status, cudaStream_t st) {
+  if (num_seqs == 0) return 0;
+  if (D % 16 || block_stride % 8 || (reinterpret_cast<uintptr_t>(k_cache) & 7) ||
+      (reinterpret_cast<uintptr_t>(v_cache) & 7))
+    return -1;
+  const dim3 grid(num_seqs, kGatherSplit);
+  if (kv_fmt == kKvE4m3)
+    kv_dequant_gather_kernel<kKvE4m3><<<grid, kGatherThreads, 0, st>>>(
+        k_out, v_out, bt_out, bt_out_stride, k_cache, v_cache, block_stride, num_blocks, block_tables, bt_stride,
+        seq_lens, seq_offset, Hkv, D, k_scale, v_scale, out_blocks, status);
+  else if (kv_fmt == kKvE5m2)
+    kv_dequant_gather_kernel<kKvE5m2><<<grid, kGatherThreads, 0, st>>>(
+        k_out, v_out, bt_out, bt_out_stride, k_cache, v_cache, block_stride, num_blocks, block_tables, bt_stride,
+        seq_lens, seq_offset, Hkv, D, k_scale, v_scale, out_blocks, status);
+  else
+    return -1;
+  return static_cast<int>(cudaGetLastError());
+}
+
 int prefill_attention_launch(const PrefillAttnParams& p, cudaStream_t st) {
   if (p.num_seqs == 0) return 0;
   switch (p.head_dim) {

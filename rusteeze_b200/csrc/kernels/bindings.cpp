@@ -72,20 +72,61 @@ void fused_add_rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor residu
            "fused_add_rms_norm");
 }
 
+// KV cache element format from the cache tensor's dtype: bf16, or fp8 e4m3 / e5m2
+static int kv_format(const torch::Tensor& c) {
+  switch (c.scalar_type()) {
+    case at::kBFloat16: return rz::kKvBf16;
+    case at::kFloat8_e4m3fn: return rz::kKvE4m3;
+    case at::kFloat8_e5m2: return rz::kKvE5m2;
+    default: TORCH_CHECK(false, "KV cache must be bfloat16, float8_e4m3fn or float8_e5m2");
+  }
+  return -1;
+}
+
 void rope_and_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin, torch::Tensor k_cache,
-                    torch::Tensor v_cache, torch::Tensor slots, int64_t Hq, int64_t Hkv, int64_t D) {
+                    torch::Tensor v_cache, torch::Tensor slots, int64_t Hq, int64_t Hkv, int64_t D, double k_scale,
+                    double v_scale) {
   const at::cuda::CUDAGuard rz_guard(qkv.device());
   CHECK_CUDA(qkv); CHECK_BF16(qkv); CHECK_LAST(qkv);
   TORCH_CHECK(positions.scalar_type() == at::kLong && slots.scalar_type() == at::kLong, "int64 positions/slots");
   TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "fp32 contiguous cos_sin");
   TORCH_CHECK(k_cache.stride(0) == v_cache.stride(0), "k/v caches must share the block stride");
   TORCH_CHECK(k_cache.stride(1) == 16 * D && k_cache.stride(2) == D, "cache page layout [blocks, Hkv, 16, D]");
+  const int fmt = kv_format(k_cache);
+  TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "k/v caches must share the dtype");
+  TORCH_CHECK(k_scale > 0 && v_scale > 0, "KV cache scales must be positive");
   check_rc(rz::rope_cache_launch(reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0),
-                                 positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(),
-                                 reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
-                                 reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), k_cache.stride(0),
-                                 slots.data_ptr<int64_t>(), qkv.size(0), Hq, Hkv, D, cur_stream()),
+                                 positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(), k_cache.data_ptr(),
+                                 v_cache.data_ptr(), k_cache.stride(0), slots.data_ptr<int64_t>(), qkv.size(0), Hq,
+                                 Hkv, D, fmt, static_cast<float>(k_scale), static_cast<float>(v_scale),
+                                 cur_stream()),
            "rope_and_cache");
+}
+
+// fp8 cache blocks of sequences [seq_offset, seq_offset + num_seqs) -> bf16 scratch pages and
+// the scratch block table (rows indexed like block_tables)
+void kv_dequant_gather(torch::Tensor k_out, torch::Tensor v_out, torch::Tensor bt_out, torch::Tensor k_cache,
+                       torch::Tensor v_cache, torch::Tensor block_tables, torch::Tensor seq_lens, int64_t seq_offset,
+                       int64_t num_seqs, double k_scale, double v_scale) {
+  const at::cuda::CUDAGuard rz_guard(k_out.device());
+  CHECK_CUDA(k_out); CHECK_BF16(k_out); CHECK_BF16(v_out);
+  TORCH_CHECK(k_out.is_contiguous() && v_out.is_contiguous() && k_out.sizes() == v_out.sizes(),
+              "scratch pages [blocks, Hkv, 16, D], contiguous");
+  TORCH_CHECK(bt_out.scalar_type() == at::kInt && bt_out.stride(1) == 1, "int32 scratch block table");
+  TORCH_CHECK(bt_out.size(0) >= seq_offset + num_seqs, "scratch block table has too few rows");
+  const int fmt = kv_format(k_cache);
+  TORCH_CHECK(fmt != rz::kKvBf16 && v_cache.scalar_type() == k_cache.scalar_type(), "fp8 k/v caches");
+  TORCH_CHECK(k_cache.stride(0) == v_cache.stride(0) && k_cache.size(1) == k_out.size(1) &&
+                  k_cache.size(3) == k_out.size(3) && k_cache.stride(1) == 16 * k_cache.size(3),
+              "cache and scratch page layouts differ");
+  check_rc(rz::kv_dequant_gather_launch(
+               reinterpret_cast<__nv_bfloat16*>(k_out.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v_out.data_ptr()),
+               bt_out.data_ptr<int32_t>(), bt_out.stride(0), reinterpret_cast<const uint8_t*>(k_cache.data_ptr()),
+               reinterpret_cast<const uint8_t*>(v_cache.data_ptr()), k_cache.stride(0), k_cache.size(0),
+               block_tables.data_ptr<int32_t>(), block_tables.stride(0), seq_lens.data_ptr<int32_t>(), seq_offset,
+               num_seqs, k_cache.size(1), k_cache.size(3), fmt, static_cast<float>(k_scale),
+               static_cast<float>(v_scale), k_out.size(0), status_ptr(), cur_stream()),
+           "kv_dequant_gather");
 }
 
 // Vocab-parallel embedding rows: table holds rows [lo, hi) of the vocabulary.
@@ -140,7 +181,7 @@ static const float* alibi_ptr(const c10::optional<torch::Tensor>& a, int64_t hea
 void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                       torch::Tensor seq_lens, torch::Tensor block_tables, c10::optional<torch::Tensor> workspace,
                       int64_t num_seqs, double scale, int64_t window, double softcap, int64_t num_splits,
-                      c10::optional<torch::Tensor> alibi) {
+                      c10::optional<torch::Tensor> alibi, double k_scale, double v_scale) {
   const at::cuda::CUDAGuard rz_guard(out.device());
   CHECK_CUDA(q); CHECK_BF16(q);
   rz::DecodeAttnParams p{};
@@ -165,6 +206,11 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   p.window = window;
   p.softcap = softcap;
   p.alibi = alibi_ptr(alibi, p.num_q_heads);
+  p.kv_fmt = kv_format(k_cache);
+  TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "k/v caches must share the dtype");
+  TORCH_CHECK(k_scale > 0 && v_scale > 0, "KV cache scales must be positive");
+  p.k_scale = static_cast<float>(k_scale);
+  p.v_scale = static_cast<float>(v_scale);
   p.status = status_ptr();
   if (num_splits > 1) {
     TORCH_CHECK(workspace.has_value() &&
@@ -204,6 +250,8 @@ void prefill_attention_impl(torch::Tensor out, torch::Tensor q, torch::Tensor k_
   p.window = window;
   p.softcap = softcap;
   p.alibi = alibi_ptr(alibi, p.num_q_heads);
+  TORCH_CHECK(k_cache.scalar_type() == at::kBFloat16 && v_cache.scalar_type() == at::kBFloat16,
+              "prefill attention reads bf16 pages (gather an fp8 cache with kv_dequant_gather first)");
   p.status = status_ptr();
   // impl: 0 = tensor-core kernel when the shape allows it (head_dim 128), else mma.sync;
   //       1 = mma.sync kernel; 2 = tensor-core kernel (error if the shape is not supported)
@@ -893,14 +941,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rusteeze_b200 sm_100a kernels";
   m.def("rms_norm", &rms_norm);
   m.def("fused_add_rms_norm", &fused_add_rms_norm);
-  m.def("rope_and_cache", &rope_and_cache);
+  m.def("rope_and_cache", &rope_and_cache, py::arg("qkv"), py::arg("positions"), py::arg("cos_sin"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("slots"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"),
+        py::arg("k_scale") = 1.0, py::arg("v_scale") = 1.0);
   m.def("act_mul", &act_mul);
   m.def("embedding", &embedding);
   m.def("layer_norm", &layer_norm);
   m.def("decode_attention", &decode_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("seq_lens"), py::arg("block_tables"), py::arg("workspace"),
         py::arg("num_seqs"), py::arg("scale"), py::arg("window"), py::arg("softcap"), py::arg("num_splits"),
-        py::arg("alibi") = py::none());
+        py::arg("alibi") = py::none(), py::arg("k_scale") = 1.0, py::arg("v_scale") = 1.0);
+  m.def("kv_dequant_gather", &kv_dequant_gather);
   m.def("prefill_attention", &prefill_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("qsl"), py::arg("seq_lens"), py::arg("block_tables"), py::arg("seq_offset"),
         py::arg("num_seqs"), py::arg("max_q_len"), py::arg("scale"), py::arg("window"), py::arg("softcap"),

@@ -8,6 +8,7 @@
 // architectures/common.rs:33-45), rotate-half RoPE (common.rs:142-170),
 // SwiGLU (common.rs:354-361); the reference's KV write is a no-op
 // (crates/rusteeze-tensor/src/cache.rs:484-505).
+#include "attention.h"
 #include "common.cuh"
 #include "elementwise.h"
 #include "mxfp8.cuh"
@@ -180,12 +181,34 @@ int rms_norm_launch(__nv_bfloat16* out, const __nv_bfloat16* x, __nv_bfloat16* r
 // ---------------------------------------------------------------------------- RoPE + KV write
 // One CTA per token.  Work items: (Hq + Hkv) heads x (D/2)/8 rotation vectors (8 elements of the
 // first half with the matching 8 of the second half, 16-byte loads), plus Hkv x D/8 v vectors.
+// KVF: cache element format (kKvBf16, or fp8 e4m3 / e5m2 holding value * inv_scale, converted
+// with saturation to the largest finite value).
+template <int KVF>
+__device__ __forceinline__ void st8_kv(void* cache, int64_t elem, const float* v, float inv_scale) {
+  if constexpr (KVF == kKvBf16) {
+    st8(reinterpret_cast<__nv_bfloat16*>(cache) + elem, v);
+  } else {
+    const __nv_fp8_interpretation_t fmt = KVF == kKvE4m3 ? __NV_E4M3 : __NV_E5M2;
+    uint32_t w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * k] * inv_scale, v[4 * k + 1] * inv_scale),
+                                                   __NV_SATFINITE, fmt);
+      const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * k + 2] * inv_scale, v[4 * k + 3] * inv_scale),
+                                                   __NV_SATFINITE, fmt);
+      w[k] = (lo & 0xffffu) | (hi << 16);
+    }
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(cache) + elem) = make_uint2(w[0], w[1]);
+  }
+}
+
+template <int KVF>
 __global__ void __launch_bounds__(128) rope_cache_kernel(__nv_bfloat16* __restrict__ qkv, int qkv_stride,
                                                          const int64_t* __restrict__ pos,
-                                                         const float* __restrict__ cos_sin,
-                                                         __nv_bfloat16* __restrict__ kc,
-                                                         __nv_bfloat16* __restrict__ vc, int64_t block_stride,
-                                                         const int64_t* __restrict__ slots, int Hq, int Hkv, int D) {
+                                                         const float* __restrict__ cos_sin, void* __restrict__ kc,
+                                                         void* __restrict__ vc, int64_t block_stride,
+                                                         const int64_t* __restrict__ slots, int Hq, int Hkv, int D,
+                                                         float k_inv_scale, float v_inv_scale) {
   const int t = blockIdx.x;
   __nv_bfloat16* row = qkv + static_cast<size_t>(t) * qkv_stride;
   const int64_t p = pos[t];
@@ -215,9 +238,9 @@ __global__ void __launch_bounds__(128) rope_cache_kernel(__nv_bfloat16* __restri
       st8(base + j, y1);
       st8(base + j + half, y2);
     } else if (slot >= 0) {
-      __nv_bfloat16* dst = kc + blk * block_stride + (static_cast<int64_t>(h - Hq) * 16 + off) * D;
-      st8(dst + j, y1);
-      st8(dst + j + half, y2);
+      const int64_t dst = blk * block_stride + (static_cast<int64_t>(h - Hq) * 16 + off) * D;
+      st8_kv<KVF>(kc, dst + j, y1, k_inv_scale);
+      st8_kv<KVF>(kc, dst + j + half, y2, k_inv_scale);
     }
   }
   if (slot >= 0) {
@@ -225,18 +248,35 @@ __global__ void __launch_bounds__(128) rope_cache_kernel(__nv_bfloat16* __restri
     const __nv_bfloat16* vsrc = row + (Hq + Hkv) * D;
     for (int i = threadIdx.x; i < nv; i += blockDim.x) {
       const int h = (i * 8) / D, d = (i * 8) % D;
-      *reinterpret_cast<uint4*>(vc + blk * block_stride + (static_cast<int64_t>(h) * 16 + off) * D + d) =
-          *reinterpret_cast<const uint4*>(vsrc + h * D + d);
+      const int64_t dst = blk * block_stride + (static_cast<int64_t>(h) * 16 + off) * D + d;
+      if constexpr (KVF == kKvBf16) {
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(vc) + dst) =
+            *reinterpret_cast<const uint4*>(vsrc + h * D + d);
+      } else {
+        float x[8];
+        ld8(vsrc + h * D + d, x);
+        st8_kv<KVF>(vc, dst, x, v_inv_scale);
+      }
     }
   }
 }
 
-int rope_cache_launch(__nv_bfloat16* qkv, int qkv_stride, const int64_t* pos, const float* cos_sin,
-                      __nv_bfloat16* kc, __nv_bfloat16* vc, int64_t block_stride, const int64_t* slots, int T,
-                      int Hq, int Hkv, int D, cudaStream_t st) {
+int rope_cache_launch(__nv_bfloat16* qkv, int qkv_stride, const int64_t* pos, const float* cos_sin, void* kc,
+                      void* vc, int64_t block_stride, const int64_t* slots, int T, int Hq, int Hkv, int D,
+                      int kv_fmt, float k_scale, float v_scale, cudaStream_t st) {
   if (T == 0) return 0;
   if (D % 16 != 0 || qkv_stride % 8 != 0) return -1;
-  rope_cache_kernel<<<T, 128, 0, st>>>(qkv, qkv_stride, pos, cos_sin, kc, vc, block_stride, slots, Hq, Hkv, D);
+  if (kv_fmt == kKvBf16)
+    rope_cache_kernel<kKvBf16><<<T, 128, 0, st>>>(qkv, qkv_stride, pos, cos_sin, kc, vc, block_stride, slots, Hq,
+                                                  Hkv, D, 1.f, 1.f);
+  else if (kv_fmt == kKvE4m3)
+    rope_cache_kernel<kKvE4m3><<<T, 128, 0, st>>>(qkv, qkv_stride, pos, cos_sin, kc, vc, block_stride, slots, Hq,
+                                                  Hkv, D, 1.f / k_scale, 1.f / v_scale);
+  else if (kv_fmt == kKvE5m2)
+    rope_cache_kernel<kKvE5m2><<<T, 128, 0, st>>>(qkv, qkv_stride, pos, cos_sin, kc, vc, block_stride, slots, Hq,
+                                                  Hkv, D, 1.f / k_scale, 1.f / v_scale);
+  else
+    return -1;
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -60,6 +60,17 @@ def _dtype(name: str, device: str) -> torch.dtype:
             "fp16": torch.float16}[name]
 
 
+def kv_cache_dtype(name: str, model_dtype: torch.dtype) -> torch.dtype:
+    """Element type of the paged KV cache: the model dtype ("auto" or its own name), or fp8
+    ("fp8" / "fp8_e4m3": float8_e4m3fn, "fp8_e5m2": float8_e5m2)."""
+    n = (name or "auto").lower()
+    if n in ("fp8", "fp8_e4m3"):
+        return torch.float8_e4m3fn
+    if n == "fp8_e5m2":
+        return torch.float8_e5m2
+    return model_dtype
+
+
 def swap_blocks(ec, model_config, dtype: torch.dtype, device: str) -> int:
     """Host swap-space blocks for swap preemption.  Every tensor-parallel rank computes
     the same count from the same config (the engine's block manager on rank 0 and each
@@ -116,8 +127,9 @@ class LLMEngine:
         self.eos_ids = tuple(self.model_config.eos_token_id or ([self.tokenizer.eos_token_id]
                                                                if self.tokenizer.eos_token_id is not None else []))
         # KV cache sizing
+        self.kv_dtype = kv_cache_dtype(ec.kv_cache_dtype, self.dtype)
         num_gpu_blocks = ec.num_gpu_blocks or self._profile_num_blocks()
-        num_cpu_blocks = swap_blocks(ec, self.model_config, self.dtype, self.device)
+        num_cpu_blocks = swap_blocks(ec, self.model_config, self.kv_dtype, self.device)
         self.bm = make_block_manager(BLOCK_SIZE, num_gpu_blocks, num_cpu_blocks, ec.enable_prefix_caching)
         spec = ec.speculative
         self.sched_cfg = SchedulerConfig(
@@ -130,7 +142,8 @@ class LLMEngine:
         self.runner = executor or ModelRunner(
             model, num_gpu_blocks=num_gpu_blocks, num_cpu_blocks=num_cpu_blocks,
             max_num_seqs=ec.max_num_seqs, max_num_batched_tokens=ec.max_num_batched_tokens,
-            max_model_len=self.max_model_len, use_cuda_graph=not ec.enforce_eager, seed=mc.seed)
+            max_model_len=self.max_model_len, kv_dtype=self.kv_dtype, use_cuda_graph=not ec.enforce_eager,
+            seed=mc.seed)
         if self.device.startswith("cuda") and not ec.enforce_eager and hasattr(self.runner, "capture_graphs"):
             from rusteeze_b200.engine.model_runner import decode_graph_buckets
             mx = min(ec.cuda_graph_max_batch or ec.max_num_seqs, ec.max_num_seqs)
@@ -161,7 +174,7 @@ class LLMEngine:
     # ------------------------------------------------------------------ sizing
     def _profile_num_blocks(self) -> int:
         ec = self.config.engine
-        bytes_per_block = self.model_config.kv_bytes_per_token(torch.finfo(self.dtype).bits // 8) * BLOCK_SIZE
+        bytes_per_block = self.model_config.kv_bytes_per_token(torch.finfo(self.kv_dtype).bits // 8) * BLOCK_SIZE
         bytes_per_block //= max(1, getattr(self.model.tp, "size", 1)) if self.model_config.num_key_value_heads >= \
             getattr(self.model.tp, "size", 1) else 1
         if not self.device.startswith("cuda"):

@@ -33,6 +33,7 @@ from rusteeze_b200.engine.sampler import SampleRow, Sampler, SampleResult
 from rusteeze_b200.engine.scheduler import SchedulerOutput
 from rusteeze_b200.models.decoder import AttentionMetadata, DecoderLM
 from rusteeze_b200.ops import BLOCK_SIZE
+from rusteeze_b200.ops import reference as ref
 from rusteeze_b200.utils.op_timer import OP_TIMER
 
 _ZERO1 = np.zeros(1, dtype=np.int64)
@@ -90,13 +91,16 @@ class ModelRunner:
         self.kv_dtype = kv_dtype or model.dtype
         L, D, hkv = self.cfg.num_hidden_layers, self.cfg.head_dim, model.hkv
         self.num_gpu_blocks = num_gpu_blocks
-        self.kv_cache = torch.zeros(num_gpu_blocks, L, 2, hkv, BLOCK_SIZE, D, dtype=self.kv_dtype,
-                                    device=self.device)
+        # fp8 caches are allocated and moved as bytes (block copies, swaps) and viewed as
+        # their float8 dtype by the attention ops
+        store = torch.uint8 if ref.is_fp8(self.kv_dtype) else self.kv_dtype
+        self.kv_cache = torch.zeros(num_gpu_blocks, L, 2, hkv, BLOCK_SIZE, D, dtype=store,
+                                    device=self.device).view(self.kv_dtype)
         self.kv_layers = [(self.kv_cache[:, l, 0], self.kv_cache[:, l, 1]) for l in range(L)]
         self.cpu_cache = None
         if num_cpu_blocks > 0:
-            self.cpu_cache = torch.zeros(num_cpu_blocks, L, 2, hkv, BLOCK_SIZE, D, dtype=self.kv_dtype,
-                                         pin_memory=self.is_cuda)
+            self.cpu_cache = torch.zeros(num_cpu_blocks, L, 2, hkv, BLOCK_SIZE, D, dtype=store,
+                                         pin_memory=self.is_cuda).view(self.kv_dtype)
         pin = self.is_cuda
         T, S, MB = self.max_tokens, max_num_seqs, self.max_blocks
         # two sets of pinned staging buffers, alternated per step: with
@@ -143,6 +147,12 @@ class ModelRunner:
         self.h_logits_idx_np = self.h_logits_idx.numpy()
         self.h_seq_lens_np = self.h_seq_lens.numpy()
 
+    def prefill_kv_blocks(self, nd: int, S: int) -> int:
+        """KV blocks of sequences [nd, S) of the staged batch (host lengths)."""
+        if S <= nd or not ref.is_fp8(self.kv_dtype):
+            return 0
+        return int(((self.h_seq_lens_np[nd:S].astype(np.int64) + BLOCK_SIZE - 1) // BLOCK_SIZE).sum())
+
     def _flip_host(self) -> None:
         self._host_k ^= 1
         self._bind_host(self._host_k)
@@ -156,7 +166,8 @@ class ModelRunner:
             self.device, non_blocking=True)
         dst = torch.tensor([p[1] for p in pairs], dtype=torch.long, pin_memory=self.is_cuda).to(
             self.device, non_blocking=True)
-        self.kv_cache.index_copy_(0, dst, self.kv_cache.index_select(0, src))
+        kv = self.kv_cache.view(torch.uint8) if ref.is_fp8(self.kv_dtype) else self.kv_cache
+        kv.index_copy_(0, dst, kv.index_select(0, src))
 
     @torch.no_grad()
     def swap_out(self, pairs: List[Tuple[int, int]]) -> None:
@@ -235,7 +246,7 @@ class ModelRunner:
             seq_lens=self.d_seq_lens[:S], block_tables=self.d_block_tables[:S],
             slot_mapping=self.d_slots[:T], max_query_len=max_q, max_seq_len=max_s,
             decode_num_splits=choose_num_splits(max(nd, 1), self.model.hkv, self.max_blocks),
-            decode_workspace=self.decode_ws)
+            decode_workspace=self.decode_ws, prefill_kv_blocks=self.prefill_kv_blocks(nd, S))
         if not self.is_cuda:
             # host oracle path reads the metadata on the host
             meta.query_start_loc = self.h_qsl[:S + 1].clone()
@@ -282,7 +293,7 @@ class ModelRunner:
             seq_lens=self.d_seq_lens[:S], block_tables=self.d_block_tables[:S], slot_mapping=self.d_slots[:T],
             max_query_len=int(max(n_new)) if S else 1, max_seq_len=int(self.h_seq_lens[:S].max()) if S else 0,
             decode_num_splits=choose_num_splits(max(num_decode, 1), self.model.hkv, self.max_blocks),
-            decode_workspace=self.decode_ws)
+            decode_workspace=self.decode_ws, prefill_kv_blocks=self.prefill_kv_blocks(num_decode, S))
         if not self.is_cuda:
             meta.query_start_loc = self.h_qsl[:S + 1].clone()
             meta.seq_lens = self.h_seq_lens[:S].clone()

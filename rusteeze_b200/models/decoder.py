@@ -64,6 +64,9 @@ class AttentionMetadata:
     # rows of the hidden state whose logits are needed (last token of each seq,
     # or every verify position for speculative decoding)
     logits_indices: Optional[torch.Tensor] = None
+    # KV blocks of the non-decode sequences (sum of ceil(seq_len / 16) over [num_decode_seqs,
+    # num_seqs)): the size of the bf16 scratch an fp8 cache is gathered into for prefill
+    prefill_kv_blocks: int = 0
 
 
 class TPGroup:
@@ -155,6 +158,9 @@ class DecoderLM(nn.Module):
                 persistent=False)
             self.alibi = None
         self.moe_impl = None   # set by parallel.moe for EP / fused dispatch
+        # an fp8 KV cache holds k / k_scale and v / v_scale (1.0: the values as they are,
+        # saturated at the format's largest finite value)
+        self.kv_scales = (1.0, 1.0)
 
     # ------------------------------------------------------------------ helpers
     @property
@@ -267,10 +273,10 @@ class DecoderLM(nn.Module):
                     qkv = self._lin(x, L, "qkv", L.qkv_bias)
             with sec("rope_kv"):
                 q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
-                                       self.hq, self.hkv, D)
+                                       self.hq, self.hkv, D, *self.kv_scales)
             with sec("attention"):
                 a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
-                                        cfg.attn_logit_softcapping, self.alibi)
+                                        cfg.attn_logit_softcapping, self.alibi, *self.kv_scales)
             with sec("o_gemm_rs"):
                 h = self._row_parallel(a.view(a.shape[0], -1), L, "o")
             if self.is_gemma2:
@@ -362,10 +368,10 @@ class DecoderLM(nn.Module):
                     qkv = F.gemm_ag(x, L.qkv, 2 * li, L.qkv_bias)
             with sec("rope_kv"):
                 q = ops.rope_and_cache(qkv, positions, self.cos_sin, kv[0], kv[1], meta.slot_mapping,
-                                       self.hq, self.hkv, D)
+                                       self.hq, self.hkv, D, *self.kv_scales)
             with sec("attention"):
                 a = ops.paged_attention(q, kv[0], kv[1], meta, cfg.attn_scale, L.sliding_window,
-                                        cfg.attn_logit_softcapping, self.alibi)
+                                        cfg.attn_logit_softcapping, self.alibi, *self.kv_scales)
             with sec("o_gemm_rs"):
                 if mx:
                     F.gemm_rs_mx(*ops.quant_mxf8_act(a.view(M, -1)), L.o_q, L.o_sf, c_attn)

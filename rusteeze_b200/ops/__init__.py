@@ -88,10 +88,12 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
 # ----------------------------------------------------------------------------- rope + kv write
 def rope_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
                    k_cache: torch.Tensor, v_cache: torch.Tensor, slot_mapping: torch.Tensor,
-                   num_q_heads: int, num_kv_heads: int, head_dim: int) -> torch.Tensor:
+                   num_q_heads: int, num_kv_heads: int, head_dim: int, k_scale: float = 1.0,
+                   v_scale: float = 1.0) -> torch.Tensor:
     """Applies neox RoPE to the q and k parts of the fused qkv [T, (Hq+2Hkv)*D]
     output (q in place), writes rotated k and v into the paged caches at
-    slot_mapping, and returns q as a [T, Hq, D] view."""
+    slot_mapping, and returns q as a [T, Hq, D] view.  fp8 caches (float8_e4m3fn /
+    float8_e5m2) store k / k_scale and v / v_scale, saturated."""
     T = qkv.shape[0]
     qs, kvs = num_q_heads * head_dim, num_kv_heads * head_dim
     if not qkv.is_cuda:
@@ -101,10 +103,10 @@ def rope_and_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Te
         qq = q.clone()
         ref.rope(qq, k, positions, cos_sin)
         q.copy_(qq)
-        ref.reshape_and_cache(k, v, k_cache, v_cache, slot_mapping)
+        ref.reshape_and_cache(k, v, k_cache, v_cache, slot_mapping, k_scale, v_scale)
         return q
     cuda_ext().rope_and_cache(qkv, positions, cos_sin, k_cache, v_cache, slot_mapping,
-                              num_q_heads, num_kv_heads, head_dim)
+                              num_q_heads, num_kv_heads, head_dim, float(k_scale), float(v_scale))
     _LAUNCHES[0] += 1
     return qkv[:, :qs].view(T, num_q_heads, head_dim)
 
@@ -167,12 +169,16 @@ def gelu_tanh_mul(x: torch.Tensor) -> torch.Tensor:
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, meta,
                     scale: float, sliding_window: Optional[int] = None,
                     softcap: Optional[float] = None,
-                    alibi: Optional[torch.Tensor] = None) -> torch.Tensor:
+                    alibi: Optional[torch.Tensor] = None, k_scale: float = 1.0,
+                    v_scale: float = 1.0) -> torch.Tensor:
     """q [T, Hq, D] -> out [T, Hq, D].  `meta` is an AttentionMetadata; `alibi` holds
-    one fp32 ALiBi slope per query head (None: no positional bias)."""
+    one fp32 ALiBi slope per query head (None: no positional bias).  With an fp8 cache the
+    decode rows read it directly (f16 tensor-core variant) and the other rows read a bf16
+    scratch copy of their sequences' blocks (`kv_dequant_gather`)."""
     if not q.is_cuda:
         return ref.paged_attention(q, k_cache, v_cache, meta.query_start_loc, meta.seq_lens,
-                                   meta.block_tables, scale, sliding_window, softcap, alibi)
+                                   meta.block_tables, scale, sliding_window, softcap, alibi,
+                                   k_scale, v_scale)
     out = torch.empty_like(q)
     C = cuda_ext()
     nd = meta.num_decode_seqs
@@ -181,14 +187,36 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     if nd > 0:
         C.decode_attention(out, q, k_cache, v_cache, meta.seq_lens, meta.block_tables,
                            meta.decode_workspace, nd, float(scale), win, cap,
-                           meta.decode_num_splits, alibi)
+                           meta.decode_num_splits, alibi, float(k_scale), float(v_scale))
         _LAUNCHES[0] += 2 if meta.decode_num_splits > 1 else 1
     if meta.num_seqs > nd:
-        C.prefill_attention(out, q, k_cache, v_cache, meta.query_start_loc, meta.seq_lens,
-                            meta.block_tables, nd, meta.num_seqs - nd, meta.max_query_len,
+        kc, vc, bt = k_cache, v_cache, meta.block_tables
+        if ref.is_fp8(k_cache.dtype):
+            kc, vc, bt = _gather_fp8_kv(k_cache, v_cache, meta, nd, k_scale, v_scale)
+        C.prefill_attention(out, q, kc, vc, meta.query_start_loc, meta.seq_lens,
+                            bt, nd, meta.num_seqs - nd, meta.max_query_len,
                             float(scale), win, cap, alibi)
         _LAUNCHES[0] += 1
     return out
+
+
+def _gather_fp8_kv(k_cache: torch.Tensor, v_cache: torch.Tensor, meta, nd: int, k_scale: float,
+                   v_scale: float):
+    """bf16 scratch pages [prefill_kv_blocks, Hkv, 16, D] for the non-decode sequences and
+    their block table (rows indexed like meta.block_tables)."""
+    nblk = max(int(meta.prefill_kv_blocks), 1)
+    shape = (nblk,) + tuple(k_cache.shape[1:])
+    scr = getattr(meta, "_fp8_scratch", None)      # reused by every layer of the forward
+    if scr is None or scr[0].shape != shape:
+        scr = (torch.empty(shape, dtype=torch.bfloat16, device=k_cache.device),
+               torch.empty(shape, dtype=torch.bfloat16, device=k_cache.device),
+               torch.zeros_like(meta.block_tables))
+        meta._fp8_scratch = scr
+    kc, vc, bt = scr
+    cuda_ext().kv_dequant_gather(kc, vc, bt, k_cache, v_cache, meta.block_tables, meta.seq_lens, nd,
+                                 meta.num_seqs - nd, float(k_scale), float(v_scale))
+    _LAUNCHES[0] += 1
+    return kc, vc, bt
 
 
 # ----------------------------------------------------------------------------- gemm

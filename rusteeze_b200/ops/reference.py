@@ -112,15 +112,32 @@ def rope(q: torch.Tensor, k: torch.Tensor, positions: torch.Tensor, cos_sin: tor
     return q, k
 
 
+FP8_KV_DTYPES = (torch.float8_e4m3fn, torch.float8_e5m2)
+
+
+def is_fp8(dtype: torch.dtype) -> bool:
+    return dtype in FP8_KV_DTYPES
+
+
+def to_kv(x: torch.Tensor, dtype: torch.dtype, scale: float = 1.0) -> torch.Tensor:
+    """Cache encoding: bf16/f16/f32 as is; fp8 holds x / scale rounded to nearest even and
+    saturated to the largest finite value (448 for e4m3, 57344 for e5m2), NaN kept."""
+    if not is_fp8(dtype):
+        return x.to(dtype)
+    m = torch.finfo(dtype).max
+    y = x.float() / scale
+    return torch.where(torch.isnan(y), y, y.clamp(-m, m)).to(dtype)
+
+
 def reshape_and_cache(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                      slot_mapping: torch.Tensor) -> None:
+                      slot_mapping: torch.Tensor, k_scale: float = 1.0, v_scale: float = 1.0) -> None:
     """k,v: [T, Hkv, D]; caches: [num_blocks, Hkv, BLOCK, D]; slot<0 is skipped."""
     sm = slot_mapping.long()
     keep = sm >= 0
     sm = sm[keep]
     blk, off = sm // BLOCK_SIZE, sm % BLOCK_SIZE
-    k_cache[blk, :, off, :] = k[keep].to(k_cache.dtype)
-    v_cache[blk, :, off, :] = v[keep].to(v_cache.dtype)
+    k_cache[blk, :, off, :] = to_kv(k[keep], k_cache.dtype, k_scale)
+    v_cache[blk, :, off, :] = to_kv(v[keep], v_cache.dtype, v_scale)
 
 
 def silu_mul(x: torch.Tensor) -> torch.Tensor:
@@ -142,9 +159,13 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
 
 
 def gather_kv(cache: torch.Tensor, block_table: torch.Tensor, seq_len: int) -> torch.Tensor:
-    """cache [nb, Hkv, BLOCK, D] -> [seq_len, Hkv, D] for one sequence."""
+    """cache [nb, Hkv, BLOCK, D] -> [seq_len, Hkv, D] for one sequence (fp8 caches are
+    gathered as bytes and keep their dtype)."""
     nblk = (seq_len + BLOCK_SIZE - 1) // BLOCK_SIZE
-    blocks = cache[block_table[:nblk].long()]                 # [nblk, Hkv, BLOCK, D]
+    src = cache.view(torch.uint8) if is_fp8(cache.dtype) else cache
+    blocks = src[block_table[:nblk].long()]                   # [nblk, Hkv, BLOCK, D]
+    if src is not cache:
+        blocks = blocks.view(cache.dtype)
     return blocks.permute(0, 2, 1, 3).reshape(-1, cache.shape[1], cache.shape[3])[:seq_len]
 
 
@@ -152,12 +173,14 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                     query_start_loc: torch.Tensor, seq_lens: torch.Tensor, block_tables: torch.Tensor,
                     scale: float, sliding_window: Optional[int] = None,
                     softcap: Optional[float] = None,
-                    alibi: Optional[torch.Tensor] = None) -> torch.Tensor:
+                    alibi: Optional[torch.Tensor] = None, k_scale: float = 1.0,
+                    v_scale: float = 1.0) -> torch.Tensor:
     """Varlen causal GQA attention over a paged KV cache.
 
     q: [T, Hq, D]; sequence i owns query rows query_start_loc[i]:query_start_loc[i+1],
     which are the LAST q_len positions of its seq_lens[i]-long context.  alibi: [Hq]
-    slopes, added as slope * (k_pos - q_pos) after the soft-cap.
+    slopes, added as slope * (k_pos - q_pos) after the soft-cap.  fp8 caches hold
+    k / k_scale and v / v_scale.
     """
     out = torch.empty_like(q)
     hq, hkv = q.shape[1], k_cache.shape[1]
@@ -168,8 +191,8 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         ql = b - a
         if ql == 0:
             continue
-        K = gather_kv(k_cache, block_tables[i], L).float().repeat_interleave(g, dim=1)  # [L,Hq,D]
-        V = gather_kv(v_cache, block_tables[i], L).float().repeat_interleave(g, dim=1)
+        K = (gather_kv(k_cache, block_tables[i], L).float() * k_scale).repeat_interleave(g, dim=1)  # [L,Hq,D]
+        V = (gather_kv(v_cache, block_tables[i], L).float() * v_scale).repeat_interleave(g, dim=1)
         Q = q[a:b].float()
         s = torch.einsum("qhd,khd->hqk", Q, K) * scale
         if softcap:

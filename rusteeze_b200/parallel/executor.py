@@ -262,7 +262,7 @@ def stage_plan(runner: ModelRunner, plan) -> Tuple[object, int, int]:
         seq_lens=r.d_seq_lens[:S], block_tables=r.d_block_tables[:S], slot_mapping=r.d_slots[:T],
         max_query_len=plan["maxq"], max_seq_len=plan["maxs"],
         decode_num_splits=choose_num_splits(max(plan["nd"], 1), r.model.hkv, r.max_blocks),
-        decode_workspace=r.decode_ws)
+        decode_workspace=r.decode_ws, prefill_kv_blocks=r.prefill_kv_blocks(plan["nd"], S))
     if not r.is_cuda:
         meta.query_start_loc = r.h_qsl[:S + 1].clone()
         meta.seq_lens = r.h_seq_lens[:S].clone()

@@ -48,11 +48,12 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
     """Builds this rank's shard, runner and plan channel.  Rank 0 returns (engine, runner,
     channel); with build_engine=False (worker-group recovery) it returns (executor, runner,
     channel) for an engine that already exists."""
-    from rusteeze_b200.engine.llm_engine import LLMEngine, _dtype
+    from rusteeze_b200.engine.llm_engine import LLMEngine, _dtype, kv_cache_dtype
     mc = model_config or _model_config(cfg)
     ec = cfg.engine
     dev = str(info.device)
     dtype = _dtype(cfg.model.dtype, dev)
+    kv_dtype = kv_cache_dtype(ec.kv_cache_dtype, dtype)
     max_len = min(cfg.model.max_model_len or mc.max_position_embeddings, mc.max_position_embeddings)
     tp = TPComm(info.rank, info.world_size, group=dist.group.WORLD if info.world_size > 1 else None,
                 mode=ec.comm_backend if info.device.type == "cuda" else "nccl", device=info.device,
@@ -75,7 +76,7 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
     elif info.device.type == "cuda":
         free, total = torch.cuda.mem_get_info()
         budget = total * ec.gpu_memory_utilization - (total - free) - 4 * (1 << 30)
-        per_block = 2 * mc.num_hidden_layers * model.hkv * mc.head_dim * 16 * torch.finfo(dtype).bits // 8
+        per_block = 2 * mc.num_hidden_layers * model.hkv * mc.head_dim * 16 * torch.finfo(kv_dtype).bits // 8
         if info.rank == 0:
             # rank 0 also holds the unsharded draft model of speculative decoding and its KV
             from rusteeze_b200.engine.spec_decode import draft_memory
@@ -90,10 +91,10 @@ def tp_rank_setup(cfg: Config, info: DistInfo, model_config: Optional[ModelConfi
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
         nblocks = int(t.item())
     from rusteeze_b200.engine.llm_engine import swap_blocks
-    n_swap = swap_blocks(ec, mc, dtype, dev)     # the same count on every rank and in rank 0's engine
+    n_swap = swap_blocks(ec, mc, kv_dtype, dev)     # the same count on every rank and in rank 0's engine
     runner = ModelRunner(model, num_gpu_blocks=nblocks, num_cpu_blocks=n_swap, max_num_seqs=ec.max_num_seqs,
                          max_num_batched_tokens=ec.max_num_batched_tokens, max_model_len=max_len,
-                         use_cuda_graph=not ec.enforce_eager, seed=cfg.model.seed)
+                         kv_dtype=kv_dtype, use_cuda_graph=not ec.enforce_eager, seed=cfg.model.seed)
     channel = None
     if info.world_size > 1:
         if info.rank == 0:

@@ -1,6 +1,6 @@
 """Kernel microbenchmarks with CUDA-event timing and roofline fractions.
 
-    python -m rusteeze_b200.utils.kernel_bench [--only gemm,decode,prefill,norm,sample] [--json out.json]
+    python -m rusteeze_b200.utils.kernel_bench [--only gemm,decode,decode_fp8,prefill,norm,sample] [--json out.json]
 
 Each case: warm-up launches, then N timed launches bracketed by events on the
 launching stream (synchronize on both sides), inputs sized above the 126 MB
@@ -146,15 +146,20 @@ def bench_gemm_mxf8(pk, shapes=None, bns=(0, 128, 256)) -> List[dict]:
     return out
 
 
-def bench_decode(pk, cases=None) -> List[dict]:
+def bench_decode(pk, cases=None, kv: str = "bf16") -> List[dict]:
+    """Split-KV decode attention over a paged cache of bf16 or fp8 (e4m3) pages; bytes are
+    the KV bytes the step must read (half for fp8)."""
     cases = cases or [(1, 1024, 32, 8), (16, 1024, 32, 8), (64, 2048, 32, 8), (256, 1232, 32, 8),
                       (256, 4096, 32, 8)]
     out = []
     D = 128
+    esz = 1 if kv == "fp8" else 2
     for B, ctx, Hq, Hkv in cases:
         nblk = (ctx + 15) // 16
         nb = B * nblk + 16
         cache = torch.randn(nb, 1, 2, Hkv, 16, D, device="cuda", dtype=torch.bfloat16)
+        if kv == "fp8":
+            cache = cache.to(torch.float8_e4m3fn)
         bt = torch.randperm(nb, device="cuda")[: B * nblk].view(B, nblk).int().contiguous()
         sl = torch.full((B,), ctx, device="cuda", dtype=torch.int32)
         q = torch.randn(B, Hq, D, device="cuda", dtype=torch.bfloat16)
@@ -168,11 +173,16 @@ def bench_decode(pk, cases=None) -> List[dict]:
                                             sp)
 
         t = time_ms(fn)
-        bytes_ = B * ctx * Hkv * D * 2 * 2
-        out.append({"kernel": "decode_attention", "B": B, "ctx": ctx, "Hq": Hq, "Hkv": Hkv, "splits": sp,
+        bytes_ = B * ctx * Hkv * D * 2 * esz
+        out.append({"kernel": "decode_attention" + ("_fp8kv" if kv == "fp8" else ""), "B": B, "ctx": ctx,
+                    "Hq": Hq, "Hkv": Hkv, "splits": sp,
                     "ms": round(t, 4), "gbs": round(bytes_ / t / 1e6, 1),
                     "frac_of_measured_hbm": round(bytes_ / t / 1e6 / pk["hbm_gbs"], 3)})
     return out
+
+
+def bench_decode_fp8(pk, cases=None) -> List[dict]:
+    return bench_decode(pk, cases, kv="fp8")
 
 
 def bench_prefill(pk, cases=None) -> List[dict]:
@@ -257,7 +267,8 @@ def main():
     ITERS[0], ITERS[1] = a.iters, a.warmup
     pk = peaks()
     res = {"peaks": pk}
-    cases = {"gemm": a.gemm, "gemm_fp8": a.gemm, "gemm_mxf8": a.gemm, "decode": a.decode, "prefill": a.prefill}
+    cases = {"gemm": a.gemm, "gemm_fp8": a.gemm, "gemm_mxf8": a.gemm, "decode": a.decode, "decode_fp8": a.decode,
+             "prefill": a.prefill}
     for name in a.only.split(","):
         c = cases.get(name)
         if c:

@@ -87,7 +87,7 @@ def test_numbers_written_as_strings_are_accepted(tmp_path):
 @pytest.mark.parametrize("text,needle", [
     ("model:\n  expert_parallel_size: 2\n", "expert_parallel_size"),
     ("model:\n  quantization: {method: fp8_block, group_size: 64}\n", "group_size"),
-    ("engine:\n  kv_cache_dtype: fp8\n", "kv_cache_dtype"),
+    ("engine:\n  kv_cache_dtype: int8\n", "kv_cache_dtype"),
     ("engine:\n  scheduling: {enable_preemption: false}\n", "enable_preemption"),
     ("engine:\n  scheduling: {delay_factor: 0.5}\n", "delay_factor"),
     ("server:\n  rate_limit: {enabled: true, tokens_per_minute: 1000}\n", "tokens_per_minute"),
