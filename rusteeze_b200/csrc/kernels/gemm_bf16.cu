@@ -569,13 +569,19 @@ int make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int el
   return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
 }
 
+// SM count of the current device for grid sizing and tile planning; B200's 148 when the
+// query fails (no device: plans are still computed, e.g. on a build host)
 int num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  static std::atomic<int> cached{0};
+  int n = cached.load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return 148;
   }
+  cached.store(n, std::memory_order_relaxed);
   return n;
 }
 

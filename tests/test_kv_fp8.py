@@ -234,12 +234,15 @@ def test_fp8_kv_engine_on_gpu_tracks_the_fp32_oracle(kv, fmt, tol):
     top-5 logprobs against the dense fp32 oracle on the unquantised weights, then greedy
     decoding through the CUDA graphs."""
     from rusteeze_b200.config.config import QuantizationConfig
-    from rusteeze_b200.models.loader import build_model
+    from rusteeze_b200.models.loader import build_model, to_cpu_fp32
     from rusteeze_b200.models.naive import naive_logits
     mc = tiny_variant(A.LLAMA, hidden_size=512, intermediate_size=1024, num_attention_heads=4,
                       num_key_value_heads=2, head_dim=128, vocab_size=32000)
     p = np.random.default_rng(3).integers(0, mc.vocab_size, 50).tolist()
-    want = torch.log_softmax(naive_logits(build_model(mc, dtype=torch.float32, seed=0), p)[-1].double(), -1)
+    # the engine's own random init (bf16 on the device, seed 0), run in fp32 on the CPU
+    m = build_model(mc, dtype=torch.bfloat16, device=DEV, seed=0)
+    want = torch.log_softmax(naive_logits(to_cpu_fp32(m), p)[-1].double(), -1)
+    del m
     cfg = Config()
     cfg.model.device = DEV
     cfg.model.seed = 0
