@@ -16,8 +16,10 @@
 //               tcgen05.ld the S row, causal / sliding-window / soft-cap masks
 //               in registers, exp2 online softmax with the running maximum
 //               updated only when it grows by more than 2^8 (then O is
-//               rescaled in TMEM with tcgen05.ld/st), P written as bf16 into
-//               the 128-byte-swizzled shared-memory A operand of the PV MMA;
+//               rescaled in TMEM with tcgen05.ld/st), P written as bf16 pairs
+//               back into the thread's own S columns in TMEM (tcgen05.st), from
+//               where the PV MMA takes its A operand: softmax of tile j+1 runs
+//               while PV_j reads P_j, and waits for PV_j only to rescale O;
 //               finally O / l -> bf16 rows.
 // V stays in its natural [position][d] layout and is consumed as an MN-major
 // B operand, so no transpose is needed.  Every wait is bounded; page ids
@@ -33,7 +35,7 @@ namespace {
 
 constexpr int kTile = 16 * 1024;        // one 128-row x 128-byte swizzled half tile
 constexpr int kPfThreads = 320;   // producer, MMA, 8 softmax warps (2 per TMEM lane quarter)
-constexpr int kPfSmem = 12 * kTile + 1024 + 256 + 3072;   // Q(2) P(2) K(2x2) V(2x2) halves, barriers, exchange
+constexpr int kPfSmem = 10 * kTile + 1024 + 256 + 3072;   // Q(2) K(2x2) V(2x2) halves, barriers, exchange
 
 }  // namespace
 
@@ -70,22 +72,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t base = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (base & 1023)) & 1023);
   uint8_t* sQ = smem;                    // 2 halves (d 0-63, 64-127)
-  uint8_t* sP = smem + 2 * kTile;        // 2 halves (kv 0-63, 64-127)
-  uint8_t* sK = smem + 4 * kTile;        // [stage][half]
-  uint8_t* sV = smem + 8 * kTile;        // [stage][d half]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 12 * kTile);
+  uint8_t* sK = smem + 2 * kTile;        // [stage][half]
+  uint8_t* sV = smem + 6 * kTile;        // [stage][d half]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 10 * kTile);
   uint64_t* k_full = bars;               // [2]
   uint64_t* v_full = bars + 2;           // [2]
   uint64_t* kv_empty = bars + 4;         // [2]
   uint64_t* s_full = bars + 6;           // [2]
-  uint64_t* s_empty = bars + 8;          // [2]
-  uint64_t* p_full = bars + 10;
-  uint64_t* p_empty = bars + 11;
+  uint64_t* s_empty = bars + 8;          // [2] S/P slot free again (PV of its tile completed)
+  uint64_t* p_full = bars + 10;          // [2] P of the slot's tile stored in TMEM
+  uint64_t* pv_done = bars + 16;         // the last issued PV completed (O may be rescaled)
   uint64_t* o_full = bars + 12;
   uint64_t* mx_bar = bars + 13;          // the two threads of a row exchange their half-row maxima
   uint64_t* fin_bar = bars + 14;         // ... and their half-row sums at the end
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
-  float* xch = reinterpret_cast<float*>(bars + 16);   // maxima [2 tile parities][2 halves][128 rows]
+  float* xch = reinterpret_cast<float*>(bars + 17);   // maxima [2 tile parities][2 halves][128 rows]
   float* xsum = xch + 512;                              // sums [2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -95,10 +96,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 256);
+      mbar_init(&s_empty[i], 1);
+      mbar_init(&p_full[i], 256);
     }
-    mbar_init(p_full, 256);
-    mbar_init(p_empty, 1);
+    mbar_init(pv_done, 1);
     mbar_init(o_full, 1);
     mbar_init(mx_bar, 256);
     mbar_init(fin_bar, 256);
@@ -185,17 +186,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       for (int j = 0; j < ntiles && ok; ++j) {
         if (j + 1 < ntiles && !(ok = issue_s(j + 1))) break;
         const int s = j & 1;
-        if (!mbar_wait(p_full, j & 1, p.status, kAttnTimeout)) { ok = false; break; }
+        if (!mbar_wait(&p_full[s], (j >> 1) & 1, p.status, kAttnTimeout)) { ok = false; break; }
         if (!mbar_wait(&v_full[s], (j >> 1) & 1, p.status, kAttnTimeout)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t dp = smem_desc_k_sw128(smem_u32(sP + (kk >> 2) * kTile)) + 2 * (kk & 3);
+          // P of kv positions [16 kk, 16 kk + 16): bf16 pairs in TMEM, the first 64 kv in
+          // columns [0, 32) of the slot, the second 64 in [64, 96) (each softmax thread's half)
+          const uint32_t tp = tmem_base + s * 128 + (kk >> 2) * 64 + (kk & 3) * 8;
           const uint64_t dv = smem_desc_mn_sw128(smem_u32(sV + (s * 2) * kTile + kk * 2048), kTile);
-          umma_f16(tO, dp, dv, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tO, tp, dv, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&kv_empty[s]);
-        umma_commit(p_empty);
+        umma_commit(&s_empty[s]);
+        umma_commit(pv_done);
       }
       umma_commit(o_full);
     }
@@ -227,8 +231,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(u[i]);
       }
-      tc_fence_before();
-      mbar_arrive(&s_empty[s]);
       const int c0 = kv_beg + j * 128 + hc * 64;     // kv position of x[0]
       float mx = -INFINITY;
       if (!SOFTCAP && !ALIBI && c0 >= lo && c0 + 63 <= pos) {  // interior tile: nothing masked
@@ -277,11 +279,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
       l = l * alpha + rs;
-      // P / O may be touched only after the previous PV MMA finished
-      if (j > 0 && !mbar_wait(p_empty, (j - 1) & 1, p.status, kAttnTimeout)) { ok = false; break; }
-      tc_fence_after();
-      // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows needs it
+      // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows needs it,
+      // after the previous PV (which accumulates into O) completed
       if (__any_sync(0xffffffffu, rescale)) {
+        if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, p.status, kAttnTimeout)) { ok = false; break; }
+        tc_fence_after();
         if (!rescale) alpha = 1.f;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
@@ -295,13 +297,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         tmem_st_wait();
       }
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(sP + hc * kTile + r * 128 + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_proxy_async_smem();
+      // P into this thread's own S columns (already read into x): the PV MMA's A operand
+      tmem_st_32x32b_x32(tmem_base + lane_off + s * 128 + hc * 64, pk);
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[s]);
     }
     // row sum = sum of the two half rows
     xsum[hc * 128 + r] = l;

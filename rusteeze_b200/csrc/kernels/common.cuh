@@ -247,6 +247,17 @@ RZ_DEVICE void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: A (M = 128 rows = TMEM lanes) holds two
+// bf16 K-elements per 32-bit column, K-ascending from tmem_a
+RZ_DEVICE void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // kind::f8f6f4 (both operands e4m3), fp32 accumulate
 RZ_DEVICE void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
