@@ -178,7 +178,11 @@ def discover_weight_files(model_dir: str):
 
 
 class _TensorIndex:
-    def __init__(self, files):
+    """Checkpoint tensors by name.  With `quant` (an integer `quantization_config`: gptq, awq,
+    int8 weight-only), a layer's `<prefix>.weight` is rebuilt from its integer tensors."""
+
+    def __init__(self, files, quant: Optional[dict] = None):
+        self.quant = quant
         self.handles = []
         for f in files:
             if f.endswith(".safetensors"):
@@ -193,13 +197,23 @@ class _TensorIndex:
                 self.where[k] = i
 
     def has(self, k: str) -> bool:
-        return k in self.where
+        if k in self.where:
+            return True
+        return bool(self.quant) and k.endswith(".weight") and k[:-7] + ".qweight" in self.where
 
-    def get(self, k: str) -> torch.Tensor:
+    def _raw(self, k: str) -> torch.Tensor:
         if k not in self.where:
             raise ModelLoadError(f"missing weight {k}")
         h = self.handles[self.where[k]]
         return h[k] if isinstance(h, dict) else h.get_tensor(k)
+
+    def get(self, k: str) -> torch.Tensor:
+        if self.quant and k.endswith(".weight"):
+            from rusteeze_b200.models.int_quant import dequantize_checkpoint_tensor
+            w = dequantize_checkpoint_tensor(self._raw, lambda n: n in self.where, k[:-7], self.quant)
+            if w is not None:
+                return w
+        return self._raw(k)
 
 
 def _hf_full(ix: _TensorIndex, cfg: ModelConfig, name: str) -> torch.Tensor:
@@ -247,9 +261,20 @@ def _hf_full(ix: _TensorIndex, cfg: ModelConfig, name: str) -> torch.Tensor:
     raise ModelLoadError(f"no HF mapping for {name} ({arch.value})")
 
 
+def checkpoint_quantization(model_dir: str) -> Optional[dict]:
+    """The integer `quantization_config` of a checkpoint's config.json (gptq, awq, int8), if
+    any: such layers are dequantized to the model dtype while loading."""
+    path = os.path.join(model_dir, "config.json")
+    if not os.path.exists(path):
+        return None
+    from rusteeze_b200.models.int_quant import checkpoint_quant_config
+    with open(path) as f:
+        return checkpoint_quant_config(json.load(f))
+
+
 @torch.no_grad()
 def load_hf_weights(model: DecoderLM, model_dir: str) -> DecoderLM:
-    ix = _TensorIndex(discover_weight_files(model_dir))
+    ix = _TensorIndex(discover_weight_files(model_dir), checkpoint_quantization(model_dir))
     for name, shape, slicer, _kind in logical_params(model):
         full = _hf_full(ix, model.cfg, name)
         if tuple(full.shape) != tuple(shape):

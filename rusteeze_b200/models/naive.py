@@ -17,8 +17,11 @@ from rusteeze_b200.ops import reference as ref
 
 
 @torch.no_grad()
-def naive_logits(model: DecoderLM, ids) -> torch.Tensor:
+def naive_logits(model: DecoderLM, ids, observer=None) -> torch.Tensor:
+    """`observer(name, x)`, when given, sees the input of every attention / MLP linear under
+    its HF name (calibration for integer quantization)."""
     cfg = model.cfg
+    obs = observer or (lambda name, x: None)
     assert model.tp.size == 1
     ids = torch.as_tensor(ids, dtype=torch.long)
     n = ids.numel()
@@ -30,6 +33,9 @@ def naive_logits(model: DecoderLM, ids) -> torch.Tensor:
     cs = model.cos_sin.float().cpu()
     for li, L in enumerate(model.layers):
         x = ref.rms_norm(h, f(L.input_norm), eps, off)
+        pre = f"model.layers.{li}."
+        for nm in ("q_proj", "k_proj", "v_proj"):
+            obs(pre + "self_attn." + nm, x)
         qkv = x @ f(L.qkv).t()
         if L.qkv_bias is not None:
             qkv = qkv + f(L.qkv_bias)
@@ -51,6 +57,7 @@ def naive_logits(model: DecoderLM, ids) -> torch.Tensor:
             mask |= torch.ones(n, n, dtype=torch.bool).tril(-w)
         s = s.masked_fill(mask, float("-inf"))
         a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv).reshape(n, hq * D)
+        obs(pre + "self_attn.o_proj", a)
         o = a @ f(L.o).t()
         if model.is_gemma2:
             o = ref.rms_norm(o, f(L.post_attn_norm), eps, off)
@@ -70,9 +77,12 @@ def naive_logits(model: DecoderLM, ids) -> torch.Tensor:
                     g, u = gu.chunk(2)
                     y[t] += wts[t, j] * ((F.silu(g) * u) @ f(L.w2[e]).t())
         else:
+            obs(pre + "mlp.gate_proj", x)
+            obs(pre + "mlp.up_proj", x)
             gu = x @ f(L.gate_up).t()
             g, u = gu.chunk(2, dim=-1)
             act = F.gelu(g, approximate="tanh") if model.act == "gelu_tanh" else F.silu(g)
+            obs(pre + "mlp.down_proj", act * u)
             y = (act * u) @ f(L.down).t()
         if model.is_gemma2:
             y = ref.rms_norm(y, f(L.post_ff_norm), eps, off)
