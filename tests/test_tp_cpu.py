@@ -1,4 +1,4 @@
-"""Tensor parallelism on CPU gloo ranks (world 2): the rank-0 engine with a
+"""Tensor parallelism on CPU gloo ranks (worlds 2, 4 and 8): the rank-0 engine with
 worker process must produce the same greedy tokens as the single-process
 engine; plan broadcast goes over the shared-memory ring."""
 import numpy as np
@@ -333,3 +333,50 @@ def test_async_engine_recovers_from_a_dead_worker():
         assert eng.tp_launcher.recoveries == 1 and ae.healthy and ae.is_ready
     finally:
         ae.shutdown()
+
+
+MC8 = ModelConfig(name="tp-tiny8", hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                  num_attention_heads=8, num_key_value_heads=4, vocab_size=1000, rms_norm_eps=1e-5,
+                  max_position_embeddings=512)
+
+
+@pytest.mark.timeout(600)
+@pytest.mark.parametrize("world", [4, 8])
+def test_tp4_tp8_gloo_match_single_process_sync_and_pipelined(world):
+    """The host side of wider tensor parallelism: the plan ring with 3 or 7 readers, weights
+    and vocabulary split 4 or 8 ways, kv heads split (4 kv heads at TP4) or replicated (TP8),
+    and the pipelined schedule's device-to-device broadcast of the sampled tokens to every
+    worker.  Greedy tokens equal the single-process engine's."""
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    rng = np.random.default_rng(7)
+    prompts = [rng.integers(0, 1000, int(n)).tolist() for n in (33, 8, 61)]
+    ref = _run(LLMEngine(_cfg(1), model_config=MC8), prompts, n=6)
+    launcher = TPEngineLauncher(_cfg(world), model_config=MC8, device_type="cpu")
+    try:
+        eng = launcher.engine()
+        got = _run(eng, prompts, n=6)
+        eng._async = True
+        piped = _run(eng, prompts, n=6)
+    finally:
+        launcher.shutdown()
+    assert got == ref
+    assert piped == ref
+
+
+@pytest.mark.timeout(600)
+def test_tp4_gloo_mixtral_expert_parallel_matches_single_process():
+    from rusteeze_b200.models.config import ModelArchitecture
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    mc = ModelConfig(name="ep4-tiny", architecture=ModelArchitecture.MIXTRAL, hidden_size=128,
+                     intermediate_size=192, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=4,
+                     vocab_size=1000, rms_norm_eps=1e-5, max_position_embeddings=512, num_local_experts=8,
+                     num_experts_per_tok=2)
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, 1000, int(n)).tolist() for n in (25, 50)]
+    ref = _run(LLMEngine(_cfg(1), model_config=mc), prompts)
+    launcher = TPEngineLauncher(_cfg(4), model_config=mc, device_type="cpu")
+    try:
+        got = _run(launcher.engine(), prompts)
+    finally:
+        launcher.shutdown()
+    assert got == ref
