@@ -1,6 +1,6 @@
-"""Tensor parallelism on CPU gloo ranks (worlds 2, 4 and 8): the rank-0 engine with
-worker process must produce the same greedy tokens as the single-process
-engine; plan broadcast goes over the shared-memory ring."""
+"""Tensor parallelism on CPU gloo ranks (worlds 2, 4 and 8): the rank-0 engine with its
+worker processes must produce the same greedy tokens as the single-process engine; plan
+broadcast goes over the shared-memory ring."""
 import numpy as np
 import pytest
 
