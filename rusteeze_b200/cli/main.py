@@ -317,6 +317,43 @@ def cmd_validate(a) -> int:
     return 0 if not errs else 1
 
 
+def cmd_quantize(a) -> int:
+    """Writes an INT8 (per-channel), GPTQ or AWQ (grouped 4-bit) copy of a checkpoint or
+    preset; GPTQ and AWQ calibrate on random token sequences unless a file of token-id
+    lists (one JSON list per line) is given."""
+    import numpy as np
+    import torch
+    from rusteeze_b200.models import int_quant as iq
+    from rusteeze_b200.models.config import ModelConfig, get_preset
+    from rusteeze_b200.models.loader import build_model
+    is_dir = os.path.isdir(a.model)
+    mc = ModelConfig.from_json_file(a.model) if is_dir else get_preset(a.model)
+    if mc.is_moe:
+        raise SystemExit("rusteeze quantize: MoE checkpoints are not quantized to integer formats")
+    model = build_model(mc, dtype=torch.float32, model_dir=a.model if is_dir else None, seed=a.seed)
+    if a.calibration:
+        with open(a.calibration) as f:
+            prompts = [json.loads(line) for line in f if line.strip()]
+    else:
+        rng = np.random.default_rng(a.seed)
+        prompts = [rng.integers(0, mc.vocab_size, a.calibration_len).tolist() for _ in range(a.calibration_samples)]
+    cfg = (iq.QuantConfig.int8() if a.method == "int8" else
+           iq.QuantConfig(method=a.method, bits=4, group_size=a.group_size, act_order=a.act_order))
+    cfg.exclude(a.exclude or [])
+    stats = iq.QuantStats()
+    iq.quantize_model_checkpoint(model, a.output, cfg, prompts, stats)
+    if is_dir:                                    # keep the tokenizer with the weights
+        import shutil
+        for f in os.listdir(a.model):
+            if f.startswith(("tokenizer", "special_tokens", "generation_config")):
+                shutil.copy(os.path.join(a.model, f), os.path.join(a.output, f))
+    d = {"output": a.output, "method": a.method, "layers": stats.layers_quantized,
+         "compression": round(stats.compression_ratio(), 3), "mean_abs_error": stats.mean_error,
+         "max_abs_error": stats.max_error}
+    print(json.dumps(d) if a.json else "\n".join(f"{k}: {v}" for k, v in d.items()))
+    return 0
+
+
 def cmd_version(a) -> int:
     import platform
     d = {"version": __version__, "python": platform.python_version()}
@@ -412,6 +449,19 @@ def build_parser() -> argparse.ArgumentParser:
     v = sub.add_parser("validate", help="validate a config file")
     v.add_argument("file", nargs="?")
     v.set_defaults(fn=cmd_validate)
+
+    qz = sub.add_parser("quantize", help="write an INT8 / GPTQ / AWQ copy of a checkpoint")
+    qz.add_argument("-m", "--model", required=True, help="HF-layout model directory or a preset name")
+    qz.add_argument("-o", "--output", required=True)
+    qz.add_argument("--method", default="gptq", choices=["int8", "gptq", "awq"])
+    qz.add_argument("--group-size", type=int, default=128)
+    qz.add_argument("--act-order", action="store_true", help="GPTQ: columns by decreasing Hessian diagonal")
+    qz.add_argument("--calibration", default=None, help="file with one JSON list of token ids per line")
+    qz.add_argument("--calibration-samples", type=int, default=32)
+    qz.add_argument("--calibration-len", type=int, default=256)
+    qz.add_argument("--exclude", nargs="*", help="layer names kept in full precision")
+    qz.add_argument("--seed", type=int, default=0)
+    qz.set_defaults(fn=cmd_quantize)
 
     ve = sub.add_parser("version")
     ve.set_defaults(fn=cmd_version)

@@ -202,3 +202,23 @@ def test_quantized_checkpoint_loads_through_the_engine(tmp_path, method, tol):
             if o.finished:
                 toks = o.outputs[0].token_ids
     assert toks is not None and len(toks) == 6
+
+
+def test_cli_quantize_writes_a_servable_checkpoint(tmp_path):
+    """`rusteeze quantize` on a preset: a GPTQ checkpoint that `rusteeze info` reads and the
+    engine generates from."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PYTHONPATH=root)
+    out = tmp_path / "q"
+    r = subprocess.run([sys.executable, "-m", "rusteeze_b200", "--json", "quantize", "-m", "tiny-llama", "-o",
+                        str(out), "--method", "gptq", "--group-size", "64", "--calibration-samples", "2",
+                        "--calibration-len", "32"], capture_output=True, text=True, timeout=600, cwd=root, env=env)
+    assert r.returncode == 0, r.stderr
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    assert d["method"] == "gptq" and d["layers"] == 14 and d["compression"] > 2
+    r = subprocess.run([sys.executable, "-m", "rusteeze_b200", "generate", "-m", str(out), "--device", "cpu",
+                        "--dtype", "float32", "-p", "hello", "--max-tokens", "4"], capture_output=True, text=True,
+                       timeout=600, cwd=root, env=env)
+    assert r.returncode == 0, r.stderr
