@@ -264,3 +264,70 @@ def test_fp8_kv_engine_on_gpu_tracks_the_fp32_oracle(kv, fmt, tol):
         outs += [o for o in eng.step() if o.finished]
     assert len(outs) == 3 and all(len(o.outputs[0].token_ids) == 24 for o in outs)
     assert int(ops.cuda_ext().status()[0]) == 0
+
+
+def test_fp8_kv_with_speculative_decoding_matches_the_plain_fp8_engine():
+    """Speculative verify reads the fp8 cache through the multi-token (prefill) path; greedy
+    output equals the non-speculative engine on the same fp8 cache, and a self-draft
+    accepts every proposal."""
+    from rusteeze_b200.config.config import SpeculativeSection
+    mc = tiny_variant(A.LLAMA)
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, mc.vocab_size, int(n)).tolist() for n in (20, 45)]
+
+    def run(eng):
+        sp = SamplingParams(temperature=0.0, max_tokens=9, ignore_eos=True)
+        ids = [eng.add_request(None, None, sp, p).request_id for p in prompts]
+        done = {}
+        while eng.has_unfinished_requests():
+            for o in eng.step():
+                if o.finished:
+                    done[o.request_id] = o.outputs[0].token_ids
+        return [done[i] for i in ids]
+
+    plain = run(_engine("fp8_e4m3", mc=mc))
+    eng = _engine("fp8_e4m3", mc=mc, speculative=SpeculativeSection(num_speculative_tokens=3))
+    assert run(eng) == plain
+    assert eng.spec.stats["accepted"] == eng.spec.stats["proposed"] > 0
+
+
+@pytest.mark.timeout(300)
+def test_fp8_kv_tp2_gloo_matches_single_process():
+    """fp8 caches in every rank's runner (the worker's included): a TP2 engine's greedy
+    tokens equal the single-process engine's on the same fp8 cache format."""
+    from rusteeze_b200.models.config import ModelConfig
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    mc = ModelConfig(name="tp-tiny", hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                     num_attention_heads=4, num_key_value_heads=2, vocab_size=1000, rms_norm_eps=1e-5,
+                     max_position_embeddings=512)
+
+    def cfg(tp):
+        c = Config()
+        c.model.device, c.model.dtype, c.model.tensor_parallel_size = "cpu", "float32", tp
+        c.engine.num_gpu_blocks, c.engine.max_num_seqs, c.engine.max_num_batched_tokens = 96, 4, 128
+        c.engine.enable_chunked_prefill, c.engine.comm_backend = True, "nccl"
+        c.engine.kv_cache_dtype = "fp8_e5m2"
+        return c
+
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, 1000, int(n)).tolist() for n in (30, 70)]
+    sp = SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True)
+
+    def run(eng):
+        ids = [eng.add_request(None, None, sp, p).request_id for p in prompts]
+        done = {}
+        while eng.has_unfinished_requests():
+            for o in eng.step():
+                if o.finished:
+                    done[o.request_id] = o.outputs[0].token_ids
+        return [done[i] for i in ids]
+
+    ref = run(LLMEngine(cfg(1), model_config=mc))
+    launcher = TPEngineLauncher(cfg(2), model_config=mc, device_type="cpu")
+    try:
+        eng = launcher.engine()
+        assert eng.runner.runner.kv_cache.dtype == torch.float8_e5m2     # rank 0's runner under the executor
+        got = run(eng)
+    finally:
+        launcher.shutdown()
+    assert got == ref
