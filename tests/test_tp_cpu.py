@@ -380,3 +380,21 @@ def test_tp4_gloo_mixtral_expert_parallel_matches_single_process():
     finally:
         launcher.shutdown()
     assert got == ref
+
+
+@pytest.mark.timeout(300)
+def test_tp2_alibi_slopes_follow_each_rank_s_heads():
+    """ALiBi at TP2: every rank adds the slopes of its own query heads (a slice of the
+    model's slopes); greedy tokens equal the single-process engine's."""
+    import dataclasses
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    mc = dataclasses.replace(MC8, name="tp-alibi", position_embedding="alibi")
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, 1000, int(n)).tolist() for n in (44, 13)]
+    ref = _run(LLMEngine(_cfg(1), model_config=mc), prompts)
+    launcher = TPEngineLauncher(_cfg(2), model_config=mc, device_type="cpu")
+    try:
+        got = _run(launcher.engine(), prompts)
+    finally:
+        launcher.shutdown()
+    assert got == ref
