@@ -210,6 +210,19 @@ def cmd_benchmark(a) -> int:
     where the engine runs on CUDA.  Reports output tok/s, TTFT/TPOT p50/p99."""
     import numpy as np
     from rusteeze_b200.core.sampling_params import SamplingParams
+    if a.url:
+        # a running server over HTTP (streamed /v1/completions), no engine in this process
+        import asyncio
+        from rusteeze_b200.utils.http_bench import run_http_benchmark
+        res = asyncio.run(run_http_benchmark(a.url, a.served_model or a.model or "default", a.vocab_size,
+                                             a.num_prompts, a.input_len, a.output_len, a.concurrency,
+                                             a.request_rate, a.seed or 0))
+        s = json.dumps(res, indent=None if a.json else 1)
+        print(s)
+        if a.output:
+            with open(a.output, "w") as f:
+                f.write(s)
+        return 0 if res["failed"] == 0 else 1
     cfg = _load_config(a, {"engine": {"max_num_seqs": max(a.concurrency, 1),
                                       "max_num_batched_tokens": max(8192, a.concurrency)}})
     eng = _engine(cfg)
@@ -429,6 +442,11 @@ def build_parser() -> argparse.ArgumentParser:
     b.add_argument("--concurrency", type=int, default=1)
     b.add_argument("--warmup", type=int, default=3)
     b.add_argument("-o", "--output")
+    b.add_argument("--url", default=None,
+                   help="benchmark a running OpenAI-compatible server at this base URL over HTTP instead")
+    b.add_argument("--request-rate", type=float, default=None, help="--url: Poisson arrivals per second")
+    b.add_argument("--served-model", default=None, help="--url: the model name sent in requests")
+    b.add_argument("--vocab-size", type=int, default=32000, help="--url: range of the random prompt token ids")
     b.set_defaults(fn=cmd_benchmark)
 
     d = sub.add_parser("download", help="download an HF model snapshot (needs network)")
