@@ -57,12 +57,15 @@ def init_logging(level: Optional[str] = None, fmt: Optional[str] = None, file: O
 
 
 class nvtx_range:
-    """NVTX range around an engine phase (no-op when CUDA/NVTX is unavailable)."""
+    """NVTX range around an engine phase (no-op when CUDA/NVTX is unavailable); with host
+    tracing on (`RUSTEEZE_TRACE`, metrics/trace.py) it also records a trace span."""
 
     def __init__(self, name: str):
         self.name = name
 
     def __enter__(self):
+        from rusteeze_b200.metrics import trace
+        self.t = time.perf_counter_ns() if trace.enabled() else 0
         try:
             import torch
             if torch.cuda.is_available():
@@ -78,4 +81,7 @@ class nvtx_range:
         if self.on:
             import torch
             torch.cuda.nvtx.range_pop()
+        if self.t:
+            from rusteeze_b200.metrics import trace
+            trace.record(self.name, self.t, time.perf_counter_ns())
         return False
