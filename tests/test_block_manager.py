@@ -3,7 +3,6 @@ operation sequences (refcount conservation, no double free, CoW, swap,
 prefix-cache accounting), plus the reference's seed scenarios
 (crates/rusteeze-engine/src/block_manager.rs:250-294)."""
 import numpy as np
-import pytest
 from hypothesis import given, settings, strategies as st
 
 from rusteeze_b200.engine.block_manager import PyBlockManager, make_block_manager

@@ -6,7 +6,7 @@ import sys
 
 import pytest
 
-from rusteeze_b200.config.loader import ConfigLoader, env_overrides, load_file
+from rusteeze_b200.config.loader import ConfigLoader, env_overrides
 from rusteeze_b200.config.validation import collect_errors
 from rusteeze_b200.core.errors import ConfigError
 

@@ -2,9 +2,7 @@
 incremental detokenizer, chat templates, sampler host paths, abort/timeout."""
 import time
 
-import numpy as np
 import pytest
-import torch
 
 from rusteeze_b200.core.sampling_params import SamplingParams
 from rusteeze_b200.engine.batch_optimizer import BatchOptimizer, BatchOptimizerConfig

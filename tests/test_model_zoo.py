@@ -12,7 +12,7 @@ from rusteeze_b200.core.types import ModelArchitecture as A
 from rusteeze_b200.engine.llm_engine import LLMEngine
 from rusteeze_b200.models.config import ModelConfig, tiny_variant
 from rusteeze_b200.models.decoder import TPGroup
-from rusteeze_b200.models.loader import build_model, load_hf_weights, save_hf_checkpoint
+from rusteeze_b200.models.loader import build_model, save_hf_checkpoint
 from rusteeze_b200.models.naive import naive_greedy, naive_logits
 
 ARCHS = [A.LLAMA, A.MISTRAL, A.MIXTRAL, A.QWEN2, A.PHI3, A.GEMMA, A.GEMMA2]

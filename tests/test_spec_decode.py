@@ -1,7 +1,6 @@
 """Speculative decoding: greedy output must equal plain greedy decoding
 exactly, whatever the draft; a self-draft accepts everything."""
 import numpy as np
-import pytest
 
 from rusteeze_b200.config.config import Config, SpeculativeSection
 from rusteeze_b200.core.sampling_params import SamplingParams
@@ -50,8 +49,6 @@ def test_independent_draft_greedy_matches_target():
     ref = _run(_engine(), PROMPTS)
     eng = _engine(SpeculativeSection(draft_preset=None, num_speculative_tokens=3))
     # an independent draft: same architecture, different random weights
-    import dataclasses
-    from rusteeze_b200.engine.spec_decode import SpecDecoder
     from rusteeze_b200.models.loader import build_model
     sd = eng.spec
     sd.self_draft = False
