@@ -258,6 +258,11 @@ PRESETS = {
                                   num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
                                   vocab_size=32000, rms_norm_eps=1e-5, rope_theta=10000.0,
                                   max_position_embeddings=2048),
+    # Mixtral-shaped MoE for harness tests: 2 layers, 4 experts (top-2), 4q/2kv
+    "tiny-mixtral": lambda: _preset(name="tiny-mixtral", architecture=ModelArchitecture.MIXTRAL, hidden_size=256,
+                                    intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+                                    num_key_value_heads=2, vocab_size=32000, rms_norm_eps=1e-5, rope_theta=1e6,
+                                    num_local_experts=4, num_experts_per_tok=2, max_position_embeddings=2048),
     "llama-2-7b": lambda: _preset(name="llama-2-7b", hidden_size=4096, intermediate_size=11008,
                                   num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=32,
                                   vocab_size=32000, rms_norm_eps=1e-5, rope_theta=10000.0,

@@ -112,3 +112,21 @@ def test_bench_data_parallel_and_tensor_parallel_runs_on_gloo():
     (d,) = _json_lines(r.stdout)
     assert d["n_gpus"] == 2 and d["config"]["parallelism"].startswith("tp2")
     assert d["speculative"]["acceptance"] == 1.0 and d["speculative"]["rounds"] > 0
+
+
+@pytest.mark.timeout(900)
+def test_bench_moe_static_batches_one_process_and_tp2_on_gloo():
+    """The shape of the Mixtral configuration on the CPU harness: static batches through a
+    MoE model, in one process and as one TP2 engine with the experts split over the ranks."""
+    moe = ["--device", "cpu", "--model", "tiny-mixtral", "--dtype", "bf16", "--max-seqs", "4",
+           "--max-batched-tokens", "256", "--workload", "static", "--batches", "4", "--static-prompt", "24",
+           "--static-output", "6"]
+    r = subprocess.run([sys.executable, "bench.py"] + moe, cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    lines = _json_lines(r.stdout)
+    assert lines and all(d["value"] > 0 for d in lines)
+    r = subprocess.run(_torchrun(2, _free_port(), moe + ["--parallel", "tp", "--comm", "nccl"]), cwd=ROOT,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    lines = _json_lines(r.stdout)
+    assert lines and lines[-1]["n_gpus"] == 2 and lines[-1]["value"] > 0
