@@ -6,7 +6,8 @@ the legacy completions request follows crates/rusteeze-core/src/request.rs:
 525-594 (prompt as string / list of strings / token ids / list of token id
 lists, echo, best_of, logprobs) plus the `RusteezeExtensions` fields
 (request.rs:489-523: priority, min_tokens, stop_token_ids, ignore_eos,
-use_prefix_cache) accepted at top level as vLLM does.
+use_prefix_cache) and beam search (`use_beam_search`, `length_penalty`,
+`early_stopping`, sampling.rs:76-80) accepted at top level as vLLM does.
 """
 from __future__ import annotations
 
@@ -59,6 +60,10 @@ class _SamplingFields(BaseModel):
     ignore_eos: bool = False
     skip_special_tokens: bool = True
     include_stop_str_in_output: bool = False
+    # beam search (sampling.rs:76-80): `best_of` (or `n`) is the width
+    use_beam_search: bool = False
+    length_penalty: float = 1.0
+    early_stopping: Union[bool, Literal["never"]] = False
 
 
 class ChatCompletionRequest(_SamplingFields):

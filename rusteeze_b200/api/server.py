@@ -6,8 +6,8 @@ Routes (crates/rusteeze-api/src/routes.rs:19-43): POST /v1/chat/completions
 reference documents (crates/rusteeze-api/src/lib.rs:8) but never routes.
 Chat prompts are rendered with the model's chat template (the reference
 joins "role: content" lines, handlers.rs:222-229).  `stop`, `n`,
-`best_of`, logprobs and `stream_options.include_usage` are honoured (the
-reference ignores stop and n, handlers.rs:232-245).  SSE framing follows
+`best_of`, beam search, logprobs and `stream_options.include_usage` are honoured
+(the reference ignores stop and n, handlers.rs:232-245).  SSE framing follows
 handlers.rs:143-182: a role chunk, content deltas, a finish chunk, then
 `data: [DONE]`.
 
@@ -32,7 +32,7 @@ from rusteeze_b200.api import schemas as S
 from rusteeze_b200.api.middleware import (AuthMiddleware, BodyLimitMiddleware, RateLimitMiddleware, RequestIdMiddleware,
                                           SlidingWindowLimiter, TimeoutMiddleware, error_response)
 from rusteeze_b200.core.errors import InvalidRequestError, RusteezeError
-from rusteeze_b200.core.sampling_params import SamplingParams
+from rusteeze_b200.core.sampling_params import EarlyStoppingMode, SamplingParams
 from rusteeze_b200.metrics.registry import CONTENT_TYPE, EngineMetrics
 from rusteeze_b200.tokenizer.chat_template import ChatTemplate
 
@@ -40,11 +40,17 @@ from rusteeze_b200.tokenizer.chat_template import ChatTemplate
 def _sampling_params(req, defaults, max_tokens_default: int, logprobs: Optional[int]) -> SamplingParams:
     stop = req.stop if isinstance(req.stop, list) else ([req.stop] if req.stop else [])
     mt = getattr(req, "max_completion_tokens", None) or req.max_tokens or max_tokens_default
+    beam = req.use_beam_search
+    # beam search is deterministic: unset temperature / top_p / top_k take its values,
+    # not the server's sampling defaults
+    es = req.early_stopping
     return SamplingParams(
         n=req.n, best_of=req.best_of or req.n, max_tokens=mt,
-        temperature=req.temperature if req.temperature is not None else defaults.temperature,
-        top_p=req.top_p if req.top_p is not None else defaults.top_p,
-        top_k=req.top_k if req.top_k is not None else defaults.top_k,
+        temperature=req.temperature if req.temperature is not None else (0.0 if beam else defaults.temperature),
+        top_p=req.top_p if req.top_p is not None else (1.0 if beam else defaults.top_p),
+        top_k=req.top_k if req.top_k is not None else (-1 if beam else defaults.top_k),
+        use_beam_search=beam, length_penalty=req.length_penalty,
+        early_stopping=EarlyStoppingMode(es if isinstance(es, str) else ("true" if es else "false")),
         min_p=req.min_p or 0.0,
         presence_penalty=req.presence_penalty or 0.0, frequency_penalty=req.frequency_penalty or 0.0,
         repetition_penalty=req.repetition_penalty if req.repetition_penalty is not None

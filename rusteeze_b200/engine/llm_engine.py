@@ -30,6 +30,7 @@ from rusteeze_b200.core.errors import ContextLengthExceededError, InvalidRequest
 from rusteeze_b200.core.outputs import RequestOutput
 from rusteeze_b200.core.sampling_params import SamplingParams
 from rusteeze_b200.core.types import RequestStatus, new_request_id
+from rusteeze_b200.engine.beam_search import BeamSearcher
 from rusteeze_b200.engine.block_manager import make_block_manager
 from rusteeze_b200.engine.model_runner import ModelRunner
 from rusteeze_b200.engine.sampler import SampleRow, Sampler
@@ -166,6 +167,7 @@ class LLMEngine:
                        and getattr(self.runner, "supports_async", False))
         self._inflight: List[_InFlight] = []
         self._n_sync_only = 0
+        self._beams = BeamSearcher(self)
         self.spec = None
         if spec is not None:
             from rusteeze_b200.engine.spec_decode import SpecDecoder
@@ -216,7 +218,11 @@ class LLMEngine:
             raise ContextLengthExceededError(
                 f"prompt has {len(prompt_token_ids)} tokens; the model context is {self.max_model_len}")
         if params.use_beam_search:
-            raise InvalidRequestError("beam search is not supported; use best_of/n sampling")
+            if self.spec is not None:
+                raise InvalidRequestError("beam search cannot be combined with speculative decoding")
+            if params.best_of > self.scheduler.cfg.max_num_seqs:
+                raise InvalidRequestError(f"beam width {params.best_of} exceeds max_num_seqs "
+                                          f"({self.scheduler.cfg.max_num_seqs}): the beams could never step together")
         rid = request_id or new_request_id("cmpl")
         if rid in self.requests:
             raise InvalidRequestError(f"duplicate request id {rid}")
@@ -226,6 +232,8 @@ class LLMEngine:
             req.seed = int(self._rng.integers(0, 2 ** 62))
         else:
             req.seed = int(params.seed)
+        if params.use_beam_search:
+            self._beams.start(req)
         for s in req.seqs:
             self._register_seq(req, s)
             self.scheduler.add(s)
@@ -236,7 +244,8 @@ class LLMEngine:
         return req
 
     def _register_seq(self, req: Request, s: Sequence) -> None:
-        s.detok = IncrementalDetokenizer(self.tokenizer, req.prompt_token_ids, req.params.skip_special_tokens)
+        if s.detok is None:
+            s.detok = IncrementalDetokenizer(self.tokenizer, req.prompt_token_ids, req.params.skip_special_tokens)
         self.seq_to_request[s.seq_id] = req
 
     def abort_request(self, request_id: str) -> bool:
@@ -394,7 +403,7 @@ class LLMEngine:
         outputs = []
         for req in touched:
             fin = req.is_finished()
-            if fin or req.stream:
+            if fin or (req.stream and req.beam is None):
                 outputs.append(req.to_output(delta=True))
             if fin:
                 self._retire(req)
@@ -429,6 +438,11 @@ class LLMEngine:
             s = ss.seq
             req = s.request
             p = req.params
+            if req.beam is not None:
+                rows.append(SampleRow(req.beam.row_params, None, None, req.seed, s.num_generated + s.pending,
+                                      self.eos_ids, None, s, 0))
+                owners.append((ss, 1))
+                continue
             # token histories are read from the sequence only by rows that need them
             for j in range(ss.num_samples):
                 rows.append(SampleRow(p, None, None, req.seed + 7919 * (s.index + j), s.num_generated + s.pending,
@@ -447,9 +461,14 @@ class LLMEngine:
             if s.num_generated == 0:
                 self.stats_counters["prompt_tokens"] += ss.num_new
         i = 0
+        beams = {}
         for ss, k in owners:
             s = ss.seq
             req = s.request
+            if req.beam is not None:
+                beams.setdefault(id(req), (req, []))[1].append((s, ss, res.top_logprobs[i]))
+                i += k
+                continue
             toks = res.tokens[i:i + k]
             lps = res.logprobs[i:i + k]
             tops = res.top_logprobs[i:i + k]
@@ -479,6 +498,11 @@ class LLMEngine:
                 self._check_stop(t, tok)
             if id(req) not in seen:
                 seen.add(id(req))
+                touched.append(req)
+        for key, (req, entries) in beams.items():
+            self._beams.step(req, entries, now)
+            if key not in seen:
+                seen.add(key)
                 touched.append(req)
         return touched
 

@@ -330,6 +330,7 @@ class Scheduler:
 
     def _num_samples(self, seq: Sequence) -> int:
         r = seq.request
-        if r.forked or r.num_target_seqs == 1 or seq.num_generated > 0:
+        # beam search samples one row per beam; its search forks the beams
+        if r.forked or r.num_target_seqs == 1 or seq.num_generated > 0 or r.beam is not None:
             return 1
         return r.num_target_seqs

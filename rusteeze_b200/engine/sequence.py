@@ -36,7 +36,7 @@ class Sequence:
     __slots__ = ("seq_id", "request", "prompt_len", "token_ids", "status", "num_computed",
                  "num_cached", "logprobs", "cumulative_logprob", "output_text", "stop_reason",
                  "detok", "_buf", "index", "finish_reason", "rng_offset",
-                 "mirostat_mu", "spec_draft", "pending", "detok_n", "sched_key")
+                 "mirostat_mu", "spec_draft", "pending", "detok_n", "sched_key", "pruned")
 
     def __init__(self, request: "Request", prompt_token_ids: List[int], index: int = 0):
         self.seq_id = next(_seq_ids)
@@ -67,6 +67,27 @@ class Sequence:
         # scheduling): their KV position is already reserved, their value is
         # only on the device until the step's results are applied
         self.pending = 0
+        self.pruned = False            # a beam that left the search: never reported
+
+    def fork_copy(self, index: int, with_kv: bool) -> "Sequence":
+        """A new sequence with this one's tokens, logprobs, text and detokenizer state
+        (beam search); `with_kv` also copies the KV counters, for a child that shares the
+        parent's blocks through the block manager's fork."""
+        c = Sequence(self.request, self.token_ids[:self.prompt_len], index)
+        n = len(self.token_ids)
+        if c._buf.shape[0] < self._buf.shape[0]:
+            c._buf = np.empty_like(self._buf)
+        c._buf[:n] = self._buf[:n]
+        c.token_ids = list(self.token_ids)
+        c.logprobs = list(self.logprobs)
+        c.cumulative_logprob = self.cumulative_logprob
+        c.output_text = self.output_text
+        c.detok = self.detok.clone() if self.detok is not None else None
+        c.detok_n = self.detok_n
+        c.mirostat_mu = self.mirostat_mu
+        if with_kv:
+            c.num_computed, c.num_cached = self.num_computed, self.num_cached
+        return c
 
     # ------------------------------------------------------------------
     @property
@@ -140,6 +161,7 @@ class Request:
     metrics: RequestMetrics = None
     forked: bool = False
     lora: Optional[str] = None
+    beam: Optional[object] = None          # beam search state (engine/beam_search.py)
     # streaming state
     sent_text_len: Dict[int, int] = field(default_factory=dict)
 
@@ -158,6 +180,8 @@ class Request:
         return self.params.best_of
 
     def is_finished(self) -> bool:
+        if self.beam is not None:
+            return all(s.is_finished() for s in self.seqs)
         # with best_of > 1 the children are forked when the prompt's last
         # chunk is sampled; until then the request cannot be finished
         return (self.forked or self.num_target_seqs == 1) and all(s.is_finished() for s in self.seqs)
@@ -165,23 +189,39 @@ class Request:
     def live_seqs(self) -> List[Sequence]:
         return [s for s in self.seqs if not s.is_finished()]
 
+    def _beam_outputs(self) -> List[Sequence]:
+        """The n best finished hypotheses (or, while the search runs, the n best live beams),
+        best first."""
+        n = self.params.n
+        if self.is_finished():
+            seqs = [s for _, s in self.beam.finished][:n]
+            return seqs or [s for s in self.seqs if not s.pruned][:n]
+        return sorted(self.live_seqs(), key=lambda s: -s.cumulative_logprob)[:n]
+
     def to_output(self, delta: bool = False) -> RequestOutput:
         p = self.params
         seqs = self.seqs
-        if self.is_finished() and len(seqs) > p.n:
+        if self.beam is not None:
+            seqs = self._beam_outputs()
+        elif self.is_finished() and len(seqs) > p.n:
             # best_of > n: keep the n sequences with the highest cumulative logprob
             seqs = sorted(seqs, key=lambda s: s.cumulative_logprob, reverse=True)[: p.n]
         outs = []
         deltas = []
-        for s in seqs:
+        beam_fin = self.beam is not None and self.is_finished()
+        for rank, s in enumerate(seqs):
             if self.defer_text:
                 s.materialize_text()
             text = s.output_text
-            outs.append(CompletionOutput(index=s.index, text=text, token_ids=s.output_token_ids,
+            idx = rank if self.beam is not None else s.index
+            outs.append(CompletionOutput(index=idx, text=text, token_ids=s.output_token_ids,
                                          cumulative_logprob=s.cumulative_logprob if p.logprobs is not None else None,
                                          logprobs=s.logprobs if p.logprobs is not None else None,
                                          finish_reason=s.finish_reason, stop_reason=s.stop_reason))
-            prev = self.sent_text_len.get(s.index, 0)
+            prev = self.sent_text_len.get(idx, 0)
+            if self.beam is not None and not beam_fin:
+                deltas.append("")          # beams are re-ranked every step: text goes out at the end
+                continue
             # a running sequence's text may end in the start of a stop string, which the next
             # token could complete (and the stop string is then cut from the output): hold
             # that suffix back so a stream never sends text it would have to retract
@@ -189,7 +229,7 @@ class Request:
             end = max(end, prev)
             deltas.append(text[prev:end])
             if delta:
-                self.sent_text_len[s.index] = end
+                self.sent_text_len[idx] = end
         return RequestOutput(request_id=self.request_id, prompt=self.prompt,
                              prompt_token_ids=self.prompt_token_ids, outputs=outs,
                              finished=self.is_finished(), metrics=self.metrics,

@@ -141,6 +141,12 @@ class IncrementalDetokenizer:
         self.read_offset = len(self.ids)
         self.text = ""
 
+    def clone(self) -> "IncrementalDetokenizer":
+        c = IncrementalDetokenizer.__new__(IncrementalDetokenizer)
+        c.tok, c.skip, c.ids = self.tok, self.skip, list(self.ids)
+        c.prefix_offset, c.read_offset, c.text = self.prefix_offset, self.read_offset, self.text
+        return c
+
     def step(self, new_id: int) -> str:
         self.ids.append(int(new_id))
         prefix = self.tok.decode(self.ids[self.prefix_offset:self.read_offset], self.skip)
