@@ -178,10 +178,22 @@ class TPEngineLauncher:
                       for r in range(1, self.world)]
         for p in self.procs:
             p.start()
-        os.environ.update(RANK="0", WORLD_SIZE=str(self.world), LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
-                          MASTER_PORT=str(port))
-        return init_distributed(device_type=self.device_type,
-                                timeout_s=float(os.environ.get("RZ_PG_TIMEOUT_S", "120")))
+        # the rendezvous variables are set for the process group's creation only: left in
+        # this process's environment they would make every later child (a tool, a test's
+        # subprocess) believe it is rank 0 of this group
+        env = dict(RANK="0", WORLD_SIZE=str(self.world), LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(port))
+        saved = {k: os.environ.get(k) for k in env}
+        os.environ.update(env)
+        try:
+            return init_distributed(device_type=self.device_type,
+                                    timeout_s=float(os.environ.get("RZ_PG_TIMEOUT_S", "120")))
+        finally:
+            for k, v in saved.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = v
 
     def dead_workers(self):
         """Ranks whose worker process has exited."""
