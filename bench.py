@@ -215,8 +215,11 @@ def make_config(args, device):
         cfg.engine.enable_prefix_caching = True
     if args.draft:
         from rusteeze_b200.config.config import SpeculativeSection
-        cfg.engine.speculative = SpeculativeSection(
-            draft_preset=None if args.draft == "self" else args.draft, num_speculative_tokens=args.spec_k)
+        if args.draft == "ngram":
+            cfg.engine.speculative = SpeculativeSection(method="ngram", num_speculative_tokens=args.spec_k)
+        else:
+            cfg.engine.speculative = SpeculativeSection(
+                draft_preset=None if args.draft == "self" else args.draft, num_speculative_tokens=args.spec_k)
         # a verify pass holds max_num_seqs * (k + 1) tokens
         cfg.engine.max_num_batched_tokens = max(cfg.engine.max_num_batched_tokens,
                                                 args.max_seqs * (args.spec_k + 1))
@@ -258,7 +261,8 @@ def main():
                          "followed by --static-prompt unique tokens (prefix caching on)")
     ap.add_argument("--shared-prefix", type=int, default=1024)
     ap.add_argument("--draft", default=None,
-                    help="speculative decoding: random-init draft preset (e.g. llama-3.2-1b), or 'self'")
+                    help="speculative decoding: random-init draft preset (e.g. llama-3.2-1b), 'self', or 'ngram' "
+                         "(prompt lookup, no draft model)")
     ap.add_argument("--spec-k", type=int, default=4, help="draft tokens per speculative round")
     ap.add_argument("--batches", default="1,8,32,128,256")
     ap.add_argument("--device", default="cuda", choices=["cuda", "cpu"],

@@ -97,7 +97,10 @@ def cmd_serve(a) -> int:
                         "enable_chunked_prefill": a.enable_chunked_prefill,
                         "max_num_batched_tokens": a.max_num_batched_tokens},
              "model": {"chat_template": a.chat_template, "trust_remote_code": a.trust_remote_code}}
-    if a.speculative_model:
+    if a.speculative_method == "ngram":
+        extra["engine"]["speculative"] = {"method": "ngram", "num_speculative_tokens": a.num_speculative_tokens,
+                                          "ngram_max": a.ngram_max, "ngram_min": a.ngram_min}
+    elif a.speculative_model:
         extra["engine"]["speculative"] = {"draft_preset" if not os.path.isdir(a.speculative_model) else "draft_model":
                                           a.speculative_model, "num_speculative_tokens": a.num_speculative_tokens}
     cfg = _load_config(a, extra)
@@ -405,7 +408,11 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--trust-remote-code", action="store_true")
     s.add_argument("--pipeline-parallel-size", type=int, default=1)
     s.add_argument("--speculative-model", default=None)
+    s.add_argument("--speculative-method", default="draft", choices=["draft", "ngram"],
+                   help="ngram: prompt-lookup proposals, no draft model")
     s.add_argument("--num-speculative-tokens", type=int, default=4)
+    s.add_argument("--ngram-max", type=int, default=4, help="longest suffix the ngram proposer looks up")
+    s.add_argument("--ngram-min", type=int, default=1, help="shortest suffix the ngram proposer looks up")
     s.set_defaults(fn=cmd_serve)
 
     g = sub.add_parser("generate", help="offline generation")

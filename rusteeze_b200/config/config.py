@@ -120,9 +120,14 @@ class SamplingDefaults:
 
 @dataclass
 class SpeculativeSection:
+    # proposer (crates/rusteeze-core/src/config.rs:635-645): "draft" (a draft model, or the
+    # target itself when neither field below is set) | "ngram" (prompt lookup: no model)
+    method: str = "draft"
     draft_model: Optional[str] = None    # HF dir of the draft model
     draft_preset: Optional[str] = None   # or a random-init preset (e.g. llama-3.2-1b)
     num_speculative_tokens: int = 4
+    ngram_max: int = 4                   # longest suffix the n-gram proposer looks up
+    ngram_min: int = 1                   # shortest
     acceptance_threshold: float = 0.9    # accepted for config parity; verification is exact
 
 

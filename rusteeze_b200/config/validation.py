@@ -77,6 +77,18 @@ def collect_errors(cfg) -> List[str]:
         e.append("engine.comm_backend must be nccl|fused")
     if g.speculative is not None and not 1 <= g.speculative.num_speculative_tokens <= 16:
         e.append("engine.speculative.num_speculative_tokens must be in [1, 16]")
+    if g.speculative is not None:
+        sp = g.speculative
+        if sp.method in ("medusa", "mlp"):
+            e.append(f"engine.speculative.method {sp.method!r} needs trained speculator heads, which this engine "
+                     "does not load; use 'draft' or 'ngram'")
+        elif sp.method not in ("draft", "ngram"):
+            e.append(f"engine.speculative.method must be draft|ngram, got {sp.method!r}")
+        if sp.method == "ngram":
+            if sp.draft_model or sp.draft_preset:
+                e.append("engine.speculative: the ngram proposer takes no draft model")
+            if not 1 <= sp.ngram_min <= sp.ngram_max <= 16:
+                e.append("engine.speculative: need 1 <= ngram_min <= ngram_max <= 16")
     # fields kept for config-file parity whose non-default values this engine does not
     # implement: refused instead of silently ignored
     if m.expert_parallel_size not in (1, m.tensor_parallel_size):

@@ -23,6 +23,16 @@ The reference ships an unused tree-speculation module whose acceptance rule
     draft processes the same tokens to stay in sync.
 Sampled speculation applies temperature only (top-k/top-p requests fall
 back to plain decoding).
+
+`method: ngram` replaces the draft model by prompt lookup (the n-gram method the
+reference's configuration names, crates/rusteeze-core/src/config.rs:635-645, without
+an implementation): each sequence proposes the k tokens that followed the most recent
+earlier occurrence of its last n tokens (C++ `_host.ngram_propose`, longest n first).
+There is no draft KV and no draft forward; the target pass and the greedy verify are
+the same as above, so the emitted tokens equal plain greedy decoding.  A proposal is a
+point mass, not a distribution, so n-gram rounds run for greedy batches only (sampled
+requests decode normally), and a step in which no sequence has a proposal runs as a
+plain step.
 """
 from __future__ import annotations
 
@@ -101,6 +111,8 @@ class SpecDecoder:
     def __init__(self, engine, spec_cfg):
         self.engine = engine
         self.k = spec_cfg.num_speculative_tokens
+        self.ngram = getattr(spec_cfg, "method", "draft") == "ngram"
+        self.ngram_range = (getattr(spec_cfg, "ngram_max", 4), getattr(spec_cfg, "ngram_min", 1))
         tm = engine.model
         dmc = draft_model_config(tm.cfg, spec_cfg) or dataclasses.replace(tm.cfg)
         self.self_draft = not spec_cfg.draft_model and not spec_cfg.draft_preset
@@ -113,7 +125,7 @@ class SpecDecoder:
                 self.draft.prepare_for_gpu()
         r = engine.runner
         self.runner: ModelRunner = r
-        self.drunner = ModelRunner(self.draft, num_gpu_blocks=r.num_gpu_blocks, num_cpu_blocks=0,
+        self.drunner = None if self.ngram else ModelRunner(self.draft, num_gpu_blocks=r.num_gpu_blocks, num_cpu_blocks=0,
                                    max_num_seqs=r.max_num_seqs, max_num_batched_tokens=max(
                                        r.max_tokens, r.max_num_seqs * (self.k + 2)),
                                    max_model_len=engine.max_model_len, use_cuda_graph=False)
@@ -146,10 +158,23 @@ class SpecDecoder:
             s.seq.request.params.top_k <= 0 and s.seq.request.params.top_p >= 1.0 and
             s.seq.request.params.min_p == 0.0 and not s.seq.request.params.needs_host_sampling()
             and not s.seq.request.params.has_penalties() and s.seq.request.params.logprobs is None
+            and (not self.ngram or s.seq.request.params.is_greedy)
             for s in so.decodes)
         if not spec_ok:
             return self._plain_step(so)
-        return self._spec_round(so)
+        props = None
+        if self.ngram:
+            props = self._ngram_proposals([s.seq for s in so.decodes])
+            if not props[1].any():
+                return self._plain_step(so)
+        return self._spec_round(so, props)
+
+    def _ngram_proposals(self, seqs):
+        """(int64 [S, k] proposals, int32 [S] how many of each row are real) by prompt lookup."""
+        from rusteeze_b200 import _host
+        n_max, n_min = self.ngram_range
+        props, counts = _host.ngram_propose([s.tokens_np() for s in seqs], self.k, n_max, n_min)
+        return torch.from_numpy(props), counts
 
     def _plain_step(self, so):
         """Normal engine step on the target; the draft processes the same tokens."""
@@ -180,7 +205,7 @@ class SpecDecoder:
         self.drunner.forward_arrays(self.engine.bm, ids, ctx, nn, toks, 1, num_decode=0)
 
     @torch.no_grad()
-    def _spec_round(self, so):
+    def _spec_round(self, so, props=None):
         eng, k, bm = self.engine, self.k, self.engine.bm
         self.runner.apply_block_ops(so)          # the target's swaps and copies of this step
         seqs = [s.seq for s in so.decodes]
@@ -188,45 +213,26 @@ class SpecDecoder:
         ids = [s.seq_id for s in seqs]
         cs = [s.num_computed for s in seqs]             # KV exists for positions < c; token at c is new
         t0 = time.monotonic()
-        drunner = self.runner if self.self_draft else self.drunner
-        # ---- draft proposals
-        dc = [self.draft_computed.get(s.seq_id, s.num_computed) for s in seqs]
-        if self.self_draft:
-            dc = list(cs)
-        n1 = [c - d + 1 for c, d in zip(cs, dc)]
-        if not self.self_draft and sum(n1) > drunner.max_tokens:
-            # a long catch-up (a preempted sequence recomputes its draft KV): feed the tokens
-            # before each sequence's current one in chunks that fit the draft runner
-            self._draft_catch_up(seqs, dc, cs, drunner)
-            dc = list(cs)
-            n1 = [1] * S
-        toks = np.concatenate([s.tokens_np()[d:c + 1] for s, d, c in zip(seqs, dc, cs)])
-        draft_tokens = torch.empty(S, k, dtype=torch.long)
-        draft_logits = []
         temps = torch.tensor([s.request.params.temperature if not s.request.params.is_greedy else 0.0
                               for s in seqs], dtype=torch.float32)
-        cur = None
-        for i in range(k):
-            if i == 0:
-                logits = drunner.forward_arrays(bm, ids, dc, n1, toks, 1, num_decode=0)
-            else:
-                logits = drunner.forward_arrays(bm, ids, [c + i for c in cs], [1] * S, cur, 1, num_decode=S)
-            draft_logits.append(logits)
-            nxt = self._propose(logits, temps, seqs, i)
-            draft_tokens[:, i] = nxt
-            cur = nxt.numpy()
+        if props is not None:
+            draft_tokens, n_real = props
+            dl = None                  # greedy verification reads no draft distribution
+        else:
+            draft_tokens, dl = self._draft_proposals(seqs, cs, temps)
+            n_real = None
         # ---- one target pass over k+1 positions per sequence
         vt = np.concatenate([np.concatenate([[s.token_ids[c]], draft_tokens[j].numpy()])
                              for j, (s, c) in enumerate(zip(seqs, cs))]).astype(np.int64)
         tlogits = self.runner.forward_arrays(bm, ids, cs, [k + 1] * S, vt, k + 1, num_decode=0)
-        dl = torch.stack(draft_logits, dim=1).reshape(S * k, -1)     # row b*k + j
         seeds = torch.tensor([(s.request.seed + 7919 * s.index) & ((1 << 62) - 1) for s in seqs], dtype=torch.int64)
         offs = torch.tensor([s.num_generated for s in seqs], dtype=torch.int64)
         if tlogits.is_cuda:
             dev = tlogits.device
             out = torch.empty(S, k + 1, dtype=torch.int64, device=dev)
             nacc = torch.empty(S, dtype=torch.int32, device=dev)
-            ops.cuda_ext().spec_verify(out, nacc, tlogits.float().contiguous(), dl.float().contiguous(),
+            ops.cuda_ext().spec_verify(out, nacc, tlogits.float().contiguous(),
+                                       dl.float().contiguous() if dl is not None else None,
                                        draft_tokens.to(dev),
                                        temps.to(dev), seeds.to(dev), offs.to(dev))
             ops.add_launches(1)
@@ -241,8 +247,10 @@ class SpecDecoder:
             a = int(nacc[j])
             emitted = [int(x) for x in out[j, :a + 1].tolist()]
             c = cs[j]
-            self.stats["proposed"] += k
-            self.stats["accepted"] += a
+            # n-gram rows pad their proposals; only the real ones count
+            real = k if n_real is None else int(n_real[j])
+            self.stats["proposed"] += real
+            self.stats["accepted"] += min(a, real)
             req = s.request
             for tok in emitted:
                 s.append_token(tok)
@@ -269,6 +277,37 @@ class SpecDecoder:
         for obs in eng.observers:
             obs(eng, so, now - t0)
         return eng._emit(touched)
+
+    def _draft_proposals(self, seqs, cs, temps):
+        """k batched draft-model steps: (int64 [S, k] proposals, [S*k, V] draft logits,
+        row b*k + j)."""
+        k, bm, S = self.k, self.engine.bm, len(seqs)
+        ids = [s.seq_id for s in seqs]
+        drunner = self.runner if self.self_draft else self.drunner
+        dc = [self.draft_computed.get(s.seq_id, s.num_computed) for s in seqs]
+        if self.self_draft:
+            dc = list(cs)
+        n1 = [c - d + 1 for c, d in zip(cs, dc)]
+        if not self.self_draft and sum(n1) > drunner.max_tokens:
+            # a long catch-up (a preempted sequence recomputes its draft KV): feed the tokens
+            # before each sequence's current one in chunks that fit the draft runner
+            self._draft_catch_up(seqs, dc, cs, drunner)
+            dc = list(cs)
+            n1 = [1] * S
+        toks = np.concatenate([s.tokens_np()[d:c + 1] for s, d, c in zip(seqs, dc, cs)])
+        draft_tokens = torch.empty(S, k, dtype=torch.long)
+        draft_logits = []
+        cur = None
+        for i in range(k):
+            if i == 0:
+                logits = drunner.forward_arrays(bm, ids, dc, n1, toks, 1, num_decode=0)
+            else:
+                logits = drunner.forward_arrays(bm, ids, [c + i for c in cs], [1] * S, cur, 1, num_decode=S)
+            draft_logits.append(logits)
+            nxt = self._propose(logits, temps, seqs, i)
+            draft_tokens[:, i] = nxt
+            cur = nxt.numpy()
+        return draft_tokens, torch.stack(draft_logits, dim=1).reshape(S * k, -1)
 
     def _draft_catch_up(self, seqs, dc, cs, drunner) -> None:
         """Draft KV for positions [dc[i], cs[i]) of every sequence, in batches of at most
