@@ -16,6 +16,7 @@ import asyncio
 import collections
 import hmac
 import logging
+import math
 import time
 import uuid
 from typing import Deque, Dict, Optional
@@ -103,13 +104,39 @@ class AuthMiddleware(BaseHTTPMiddleware):
         return await call_next(request)
 
 
+class _TokenWindow:
+    """(time, tokens) charges of one key inside a window, with their running sum."""
+    __slots__ = ("log", "total")
+
+    def __init__(self):
+        self.log: Deque = collections.deque()
+        self.total = 0
+
+    def expire(self, now: float, span: float) -> None:
+        while self.log and now - self.log[0][0] >= span:
+            self.total -= self.log.popleft()[1]
+
+
 class SlidingWindowLimiter:
-    def __init__(self, per_minute: int, burst: int = 0, per_day: Optional[int] = None):
+    """Per-key sliding windows: requests per minute (+ burst) and per day, and, when set,
+    tokens per minute and per day.  The server configuration declares all four
+    (crates/rusteeze-config/src/server.rs:207-244); the reference's middleware counts
+    requests only.  Tokens (prompt + completion) are charged when a generation ends
+    (`charge`); a key whose charges inside a window have reached its token limit is
+    refused until enough of them age out, so one request may overshoot the limit, never
+    a second."""
+
+    def __init__(self, per_minute: int, burst: int = 0, per_day: Optional[int] = None,
+                 tokens_per_minute: Optional[int] = None, tokens_per_day: Optional[int] = None):
         self.per_minute = per_minute
         self.burst = burst
         self.per_day = per_day
+        self.tokens_per_minute = tokens_per_minute
+        self.tokens_per_day = tokens_per_day
         self.hits: Dict[str, Deque[float]] = collections.defaultdict(collections.deque)
         self.day: Dict[str, Deque[float]] = collections.defaultdict(collections.deque)
+        self.tok_min: Dict[str, _TokenWindow] = collections.defaultdict(_TokenWindow)
+        self.tok_day: Dict[str, _TokenWindow] = collections.defaultdict(_TokenWindow)
         self._checks = 0
         self._sweep_at = 4096          # table size that triggers the next sweep (doubles as it grows)
 
@@ -121,7 +148,52 @@ class SlidingWindowLimiter:
             if d is None or not d or now - d[-1] >= 86400.0:
                 self.hits.pop(k, None)
                 self.day.pop(k, None)
+        for tab, span in ((self.tok_min, 60.0), (self.tok_day, 86400.0)):
+            for k in [k for k, w in tab.items() if not w.log or now - w.log[-1][0] >= span]:
+                tab.pop(k, None)
         self._sweep_at = max(4096, 2 * len(self.hits))     # amortised O(1) per check
+
+    def charge(self, key: str, tokens: int, now: Optional[float] = None) -> None:
+        """Records the tokens a finished (or aborted) generation of `key` used."""
+        if tokens <= 0 or (self.tokens_per_minute is None and self.tokens_per_day is None):
+            return
+        now = time.monotonic() if now is None else now
+        for tab in (self.tok_min, self.tok_day):
+            w = tab[key]
+            w.log.append((now, int(tokens)))
+            w.total += int(tokens)
+
+    def tokens_remaining(self, key: str, now: Optional[float] = None) -> Optional[int]:
+        """Tokens `key` may still use in the current minute (None: no per-minute token limit)."""
+        if self.tokens_per_minute is None:
+            return None
+        now = time.monotonic() if now is None else now
+        w = self.tok_min.get(key)
+        if w is None:
+            return self.tokens_per_minute
+        w.expire(now, 60.0)
+        return max(0, self.tokens_per_minute - w.total)
+
+    def _token_block(self, key: str, now: float) -> Optional[float]:
+        """Seconds until `key` is under its token limits again, or None when it is now."""
+        for tab, limit, span in ((self.tok_min, self.tokens_per_minute, 60.0),
+                                 (self.tok_day, self.tokens_per_day, 86400.0)):
+            if limit is None:
+                continue
+            w = tab.get(key)
+            if w is None:
+                continue
+            w.expire(now, span)
+            if w.total >= limit:
+                # the earliest time the window's sum drops below the limit
+                need, t = w.total - limit + 1, span
+                for ts, n in w.log:
+                    need -= n
+                    if need <= 0:
+                        t = span - (now - ts)
+                        break
+                return t
+        return None
 
     def check(self, key: str, now: Optional[float] = None):
         now = time.monotonic() if now is None else now
@@ -134,6 +206,9 @@ class SlidingWindowLimiter:
         limit = self.per_minute + self.burst
         if len(q) >= limit:
             return False, limit, 0, 60.0 - (now - q[0])
+        wait = self._token_block(key, now)
+        if wait is not None:
+            return False, limit, limit - len(q), wait
         if self.per_day is not None:
             d = self.day[key]
             while d and now - d[0] >= 86400.0:
@@ -164,15 +239,22 @@ class RateLimitMiddleware(BaseHTTPMiddleware):
     async def dispatch(self, request: Request, call_next):
         if request.url.path in OPEN_PATHS:
             return await call_next(request)
-        ok, limit, remaining, reset = self.limiter.check(self._key(request))
+        key = self._key(request)
+        # the handlers charge the tokens of each finished generation to this key
+        request.state.rate_key = key
+        ok, limit, remaining, reset = self.limiter.check(key)
         if not ok:
             resp = error_response(RateLimitError("rate limit exceeded"))
-            resp.headers["Retry-After"] = str(max(1, int(reset)))
+            resp.headers["Retry-After"] = str(max(1, int(math.ceil(reset))))
         else:
             resp = await call_next(request)
         resp.headers["X-RateLimit-Limit"] = str(limit)
         resp.headers["X-RateLimit-Remaining"] = str(max(0, remaining))
         resp.headers["X-RateLimit-Reset"] = str(max(0, int(reset)))
+        toks = self.limiter.tokens_remaining(key)
+        if toks is not None:
+            resp.headers["X-RateLimit-Limit-Tokens"] = str(self.limiter.tokens_per_minute)
+            resp.headers["X-RateLimit-Remaining-Tokens"] = str(toks)
         return resp
 
 

@@ -88,11 +88,13 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
     app.state.metrics = metrics
     sc = cfg.server
     app.add_middleware(TimeoutMiddleware, timeout_s=sc.timeout_seconds)
+    limiter = None
     if sc.rate_limit is not None and sc.rate_limit.enabled:
-        app.add_middleware(RateLimitMiddleware,
-                           limiter=SlidingWindowLimiter(sc.rate_limit.requests_per_minute, sc.rate_limit.burst,
-                                                        sc.rate_limit.requests_per_day),
-                           by=sc.rate_limit.by)
+        rl = sc.rate_limit
+        limiter = SlidingWindowLimiter(rl.requests_per_minute, rl.burst, rl.requests_per_day,
+                                       tokens_per_minute=rl.tokens_per_minute, tokens_per_day=rl.tokens_per_day)
+        app.add_middleware(RateLimitMiddleware, limiter=limiter, by=rl.by)
+    app.state.rate_limiter = limiter
     app.add_middleware(AuthMiddleware, api_key=sc.api_key)
     if sc.compression:
         app.add_middleware(GZipMiddleware, minimum_size=1024)
@@ -111,6 +113,11 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
     @app.exception_handler(ValueError)
     async def _verr(_request: Request, exc: ValueError):
         return error_response(InvalidRequestError(str(exc)))
+
+    def _charge(key: Optional[str], final) -> None:
+        """Token limits: a generation's prompt + completion tokens go to its client's key."""
+        if limiter is not None and key is not None and final is not None:
+            limiter.charge(key, len(final.prompt_token_ids) + sum(len(c.token_ids) for c in final.outputs))
 
     def _check_model(name: str) -> None:
         if name and name != model_name and not cfg.model.path == name:
@@ -136,14 +143,16 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
         sp = _sampling_params(req, defaults, 16, req.logprobs)
         metrics.on_request_params(sp)
         rid = "cmpl-" + uuid.uuid4().hex
+        key = getattr(request.state, "rate_key", None)
         if req.stream:
-            return StreamingResponse(_stream_completion(rid, prompts, sp, req), media_type="text/event-stream")
+            return StreamingResponse(_stream_completion(rid, prompts, sp, req, key), media_type="text/event-stream")
         choices, usage = [], S.Usage()
         for pi, (text, ids) in enumerate(prompts):
             final = None
             async for out in async_engine.generate(text, sp, f"{rid}-{pi}", ids, priority=req.priority):
                 final = out
             metrics.on_request_finished(final, "completions")
+            _charge(key, final)
             usage.prompt_tokens += len(final.prompt_token_ids)
             for c in final.outputs:
                 usage.completion_tokens += len(c.token_ids)
@@ -154,7 +163,7 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
         usage.total_tokens = usage.prompt_tokens + usage.completion_tokens
         return S.CompletionResponse(id=rid, model=model_name, choices=choices, usage=usage)
 
-    async def _stream_completion(rid, prompts, sp, req) -> AsyncIterator[str]:
+    async def _stream_completion(rid, prompts, sp, req, key) -> AsyncIterator[str]:
         usage = S.Usage()
         try:
             for pi, (text, ids) in enumerate(prompts):
@@ -174,6 +183,7 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                     completed = True
                 finally:
                     await agen.aclose()           # a stream closed early aborts its request now, not at GC
+                    _charge(key, final)
                     if not completed:
                         metrics.on_request_finished(final, "completions", status="aborted")
                 metrics.on_request_finished(final, "completions")
@@ -208,12 +218,14 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
         sp = _sampling_params(req, defaults, defaults.max_tokens, lp)
         metrics.on_request_params(sp)
         rid = "chatcmpl-" + uuid.uuid4().hex
+        key = getattr(request.state, "rate_key", None)
         if req.stream:
-            return StreamingResponse(_stream_chat(rid, ids, sp, req), media_type="text/event-stream")
+            return StreamingResponse(_stream_chat(rid, ids, sp, req, key), media_type="text/event-stream")
         final = None
         async for out in async_engine.generate(None, sp, rid, ids, priority=req.priority):
             final = out
         metrics.on_request_finished(final, "chat")
+        _charge(key, final)
         choices = [S.ChatChoice(index=c.index, message=S.ChatMessage(role="assistant", content=c.text),
                                 finish_reason=c.finish_reason,
                                 logprobs=_chat_logprobs(eng.tokenizer, c) if req.logprobs else None)
@@ -223,7 +235,7 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                                         usage=S.Usage(prompt_tokens=len(ids), completion_tokens=n_out,
                                                       total_tokens=len(ids) + n_out))
 
-    async def _stream_chat(rid, ids, sp, req) -> AsyncIterator[str]:
+    async def _stream_chat(rid, ids, sp, req, key) -> AsyncIterator[str]:
         for i in range(sp.n):
             yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
                 S.ChatChunkChoice(index=i, delta=S.ChatDelta(role="assistant", content=""))]))
@@ -245,6 +257,7 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                 completed = True
             finally:
                 await agen.aclose()               # a stream closed early aborts its request now, not at GC
+                _charge(key, final)
                 if not completed:
                     metrics.on_request_finished(final, "chat", status="aborted")
             metrics.on_request_finished(final, "chat")

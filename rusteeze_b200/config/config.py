@@ -74,7 +74,8 @@ class RateLimitConfig:
     enabled: bool = False
     requests_per_minute: int = 60
     requests_per_day: Optional[int] = None
-    tokens_per_minute: Optional[int] = None
+    tokens_per_minute: Optional[int] = None   # prompt + completion tokens per key
+    tokens_per_day: Optional[int] = None
     burst: int = 10
     by: str = "api_key"                 # api_key | ip
 

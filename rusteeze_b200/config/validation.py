@@ -59,6 +59,10 @@ def collect_errors(cfg) -> List[str]:
             e.append(f"server.rate_limit.burst must be >= 0, got {rl.burst}")
         if rl.requests_per_day is not None and rl.requests_per_day < 1:
             e.append(f"server.rate_limit.requests_per_day must be >= 1, got {rl.requests_per_day}")
+        for name in ("tokens_per_minute", "tokens_per_day"):
+            v = getattr(rl, name)
+            if v is not None and v < 1:
+                e.append(f"server.rate_limit.{name} must be >= 1, got {v}")
     if g.max_num_seqs < 1:
         e.append("engine.max_num_seqs must be >= 1")
     if g.max_num_batched_tokens < g.max_num_seqs:
@@ -104,8 +108,6 @@ def collect_errors(cfg) -> List[str]:
                  "engine.scheduling.preemption_mode)")
     if g.scheduling.delay_factor != 0.0:
         e.append("engine.scheduling.delay_factor must be 0 (prompts are scheduled as soon as blocks allow)")
-    if s.rate_limit is not None and s.rate_limit.enabled and s.rate_limit.tokens_per_minute is not None:
-        e.append("server.rate_limit.tokens_per_minute is not supported (limits count requests)")
     if cfg.logging.level.lower() not in ("trace", "debug", "info", "warn", "warning", "error"):
         e.append(f"logging.level invalid: {cfg.logging.level!r}")
     if cfg.logging.format not in ("pretty", "compact", "json"):

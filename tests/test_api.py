@@ -145,6 +145,48 @@ def test_rate_limit_headers(engine):
     ae.shutdown()
 
 
+def test_token_limiter_windows():
+    """Token charges age out of the minute and day windows; a key at its limit waits until
+    enough of its charges have aged out; keys are independent."""
+    from rusteeze_b200.api.middleware import SlidingWindowLimiter
+    lim = SlidingWindowLimiter(1000, 0, tokens_per_minute=100, tokens_per_day=250)
+    assert lim.check("a", now=0.0)[0]
+    lim.charge("a", 60, now=1.0)
+    assert lim.check("a", now=2.0)[0] and lim.tokens_remaining("a", now=2.0) == 40
+    lim.charge("a", 50, now=3.0)                       # 110 >= 100: the next request waits
+    ok, _, _, wait = lim.check("a", now=4.0)
+    assert not ok and wait == 57.0                     # the 60-token charge leaves at t = 61
+    assert lim.check("b", now=4.0)[0]                  # another key is not affected
+    assert lim.check("a", now=61.5)[0]                 # 50 tokens left in the minute window
+    lim.charge("a", 90, now=62.0)
+    lim.charge("a", 60, now=130.0)                     # day: 60 + 50 + 90 + 60 = 260 >= 250
+    ok, _, _, wait = lim.check("a", now=131.0)
+    assert not ok and wait == 86400.0 - 130.0          # until the first charge (t = 1) leaves the day
+    assert lim.check("a", now=86402.0)[0]
+
+
+def test_tokens_per_minute_limit_through_the_api(engine):
+    cfg = _cfg()
+    cfg.server.rate_limit = RateLimitConfig(enabled=True, requests_per_minute=100, burst=0, tokens_per_minute=30)
+    ae = AsyncLLMEngine(engine).start()
+    try:
+        c = TestClient(create_app(ae, cfg))
+        body = {"prompt": [1, 2, 3, 4, 5, 6, 7, 8, 9, 10], "max_tokens": 8, "ignore_eos": True}
+        r = c.post("/v1/completions", json=body, headers={"x-api-key": "alice"})
+        assert r.status_code == 200 and r.json()["usage"]["total_tokens"] == 18
+        assert r.headers["x-ratelimit-limit-tokens"] == "30"
+        r = c.post("/v1/completions", json=dict(body, stream=True), headers={"x-api-key": "alice"})
+        assert r.status_code == 200                    # 18 < 30: admitted; charged 18 more when it ends
+        r = c.post("/v1/completions", json=body, headers={"x-api-key": "alice"})
+        assert r.status_code == 429 and int(r.headers["retry-after"]) >= 1
+        assert r.headers["x-ratelimit-remaining-tokens"] == "0"
+        r = c.post("/v1/chat/completions", headers={"x-api-key": "bob"},
+                   json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 4})
+        assert r.status_code == 200                    # another key has its own budget
+    finally:
+        ae.shutdown()
+
+
 def test_ready_reports_unhealthy_after_engine_failure():
     cfg = _cfg()
     eng = LLMEngine(cfg)

@@ -90,7 +90,6 @@ def test_numbers_written_as_strings_are_accepted(tmp_path):
     ("engine:\n  kv_cache_dtype: int8\n", "kv_cache_dtype"),
     ("engine:\n  scheduling: {enable_preemption: false}\n", "enable_preemption"),
     ("engine:\n  scheduling: {delay_factor: 0.5}\n", "delay_factor"),
-    ("server:\n  rate_limit: {enabled: true, tokens_per_minute: 1000}\n", "tokens_per_minute"),
 ])
 def test_settings_this_engine_does_not_implement_are_refused(tmp_path, text, needle):
     p = tmp_path / "c.yaml"
