@@ -358,6 +358,11 @@ def serve(config, engine=None, host: Optional[str] = None, port: Optional[int] =
     if config.server.metrics_port:
         from rusteeze_b200.metrics.exporter import start_exporter
         start_exporter(metrics, config.server.metrics_port)
+    pusher = None
+    pg = config.metrics.push_gateway
+    if pg is not None and pg.url:
+        from rusteeze_b200.metrics.exporter import PushGatewayPusher
+        pusher = PushGatewayPusher(metrics, pg.url, pg.job, pg.instance, pg.interval_seconds).start()
     tls = config.server.tls
     kw = {}
     if tls is not None and tls.cert_path:
@@ -371,6 +376,8 @@ def serve(config, engine=None, host: Optional[str] = None, port: Optional[int] =
         server.run()
     finally:
         ae.shutdown()
+        if pusher is not None:
+            pusher.stop()
 
 
 def serve_from_env() -> None:

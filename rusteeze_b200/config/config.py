@@ -162,12 +162,21 @@ class LoggingSection:
 
 
 @dataclass
+class PushGatewaySection:
+    url: str = ""                        # e.g. http://pushgateway:9091
+    job: str = "rusteeze"
+    instance: Optional[str] = None
+    interval_seconds: float = 15.0
+
+
+@dataclass
 class MetricsSection:
     enabled: bool = True
     path: str = "/metrics"
     prometheus: bool = True
     latency_buckets: List[float] = field(default_factory=lambda: [
         0.005, 0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1.0, 2.5, 5.0, 10.0, 30.0, 60.0])
+    push_gateway: Optional[PushGatewaySection] = None
 
 
 @dataclass
@@ -204,7 +213,7 @@ _SECTION_TYPES = {
     "RateLimitConfig": RateLimitConfig, "SchedulingSection": SchedulingSection,
     "SamplingDefaults": SamplingDefaults, "SpeculativeSection": SpeculativeSection,
     "ModelSection": ModelSection, "ServerSection": ServerSection, "EngineSection": EngineSection,
-    "LoggingSection": LoggingSection, "MetricsSection": MetricsSection,
+    "LoggingSection": LoggingSection, "MetricsSection": MetricsSection, "PushGatewaySection": PushGatewaySection,
 }
 
 

@@ -112,6 +112,14 @@ def collect_errors(cfg) -> List[str]:
         e.append(f"logging.level invalid: {cfg.logging.level!r}")
     if cfg.logging.format not in ("pretty", "compact", "json"):
         e.append("logging.format must be pretty|compact|json")
+    pg = cfg.metrics.push_gateway
+    if pg is not None:
+        if not pg.url.startswith(("http://", "https://")):
+            e.append(f"metrics.push_gateway.url must be an http(s) URL, got {pg.url!r}")
+        if not pg.job:
+            e.append("metrics.push_gateway.job must not be empty")
+        if not pg.interval_seconds > 0:
+            e.append(f"metrics.push_gateway.interval_seconds must be > 0, got {pg.interval_seconds}")
     return e
 
 
