@@ -64,6 +64,12 @@ class _SamplingFields(BaseModel):
     use_beam_search: bool = False
     length_penalty: float = 1.0
     early_stopping: Union[bool, Literal["never"]] = False
+    # structured output: OpenAI `response_format` ({"type": "json_object"} or
+    # {"type": "json_schema", "json_schema": {"schema": ...}}) and vLLM's guided_* fields
+    response_format: Optional[Dict[str, Any]] = None
+    guided_json: Optional[Union[Dict[str, Any], str]] = None
+    guided_regex: Optional[str] = None
+    guided_choice: Optional[List[str]] = None
 
 
 class ChatCompletionRequest(_SamplingFields):
@@ -73,7 +79,6 @@ class ChatCompletionRequest(_SamplingFields):
     max_completion_tokens: Optional[int] = None
     add_generation_prompt: bool = True
     chat_template: Optional[str] = None
-    response_format: Optional[Dict[str, Any]] = None
     tools: Optional[List[Dict[str, Any]]] = None
     tool_choice: Optional[Any] = None
 

@@ -32,9 +32,35 @@ from rusteeze_b200.api import schemas as S
 from rusteeze_b200.api.middleware import (AuthMiddleware, BodyLimitMiddleware, RateLimitMiddleware, RequestIdMiddleware,
                                           SlidingWindowLimiter, TimeoutMiddleware, error_response)
 from rusteeze_b200.core.errors import InvalidRequestError, RusteezeError
-from rusteeze_b200.core.sampling_params import EarlyStoppingMode, SamplingParams
+from rusteeze_b200.core.sampling_params import EarlyStoppingMode, GuidedDecodingParams, SamplingParams
 from rusteeze_b200.metrics.registry import CONTENT_TYPE, EngineMetrics
 from rusteeze_b200.tokenizer.chat_template import ChatTemplate
+
+
+def _guided(req) -> Optional[GuidedDecodingParams]:
+    """The request's structured-output constraint, if any."""
+    rf = req.response_format or {}
+    t = rf.get("type") if isinstance(rf, dict) else None
+    if t not in (None, "text", "json_object", "json_schema"):
+        raise InvalidRequestError(f"response_format type {t!r} is not supported", param="response_format")
+    g = GuidedDecodingParams()
+    if t == "json_object":
+        g.json_object = True
+    elif t == "json_schema":
+        js = rf.get("json_schema") or {}
+        schema = js.get("schema", js) if isinstance(js, dict) else None
+        if not isinstance(schema, dict):
+            raise InvalidRequestError("response_format json_schema needs a schema object", param="response_format")
+        g.json_schema = schema
+    if req.guided_json is not None:
+        g.json_schema = json.loads(req.guided_json) if isinstance(req.guided_json, str) else req.guided_json
+    if req.guided_regex is not None:
+        g.regex = req.guided_regex
+    if req.guided_choice is not None:
+        g.choice = list(req.guided_choice)
+    if g.json_schema is None and g.regex is None and not g.choice and not g.json_object:
+        return None
+    return g
 
 
 def _sampling_params(req, defaults, max_tokens_default: int, logprobs: Optional[int]) -> SamplingParams:
@@ -49,7 +75,7 @@ def _sampling_params(req, defaults, max_tokens_default: int, logprobs: Optional[
         temperature=req.temperature if req.temperature is not None else (0.0 if beam else defaults.temperature),
         top_p=req.top_p if req.top_p is not None else (1.0 if beam else defaults.top_p),
         top_k=req.top_k if req.top_k is not None else (-1 if beam else defaults.top_k),
-        use_beam_search=beam, length_penalty=req.length_penalty,
+        use_beam_search=beam, length_penalty=req.length_penalty, guided_decoding=_guided(req),
         early_stopping=EarlyStoppingMode(es if isinstance(es, str) else ("true" if es else "false")),
         min_p=req.min_p or 0.0,
         presence_penalty=req.presence_penalty or 0.0, frequency_penalty=req.frequency_penalty or 0.0,

@@ -43,13 +43,15 @@ class EarlyStoppingMode(str, enum.Enum):
 
 @dataclass
 class GuidedDecodingParams:
-    """Structured-output constraints. Only `choice` and `regex` over token
-    strings are enforced (as a logit mask); `json_schema` is accepted and
-    carried for API parity."""
+    """Structured-output constraints (crates/rusteeze-core/src/sampling.rs:148, declared
+    there and not applied): exactly one of `choice`, `regex`, `json_schema` or
+    `json_object` (any JSON object) is enforced as a per-step token mask
+    (engine/guided); `grammar` is refused."""
     json_schema: Optional[dict] = None
     regex: Optional[str] = None
     choice: Optional[List[str]] = None
     grammar: Optional[str] = None
+    json_object: bool = False
 
 
 @dataclass

@@ -1,0 +1,165 @@
+"""Guided (structured) decoding: which tokens may come next.
+
+`GuidedDecodingParams` (choice, regex, JSON schema, JSON object) compiles to one regex
+and its lazily built DFA (`regex_fsm.RegexFSM`, cached per pattern).  A `TokenIndex`
+holds, per tokenizer, the text of every token and a character trie over those texts.
+The tokens allowed in a DFA state are found by walking the trie and the DFA together,
+cutting a branch as soon as the DFA dies, so shared token prefixes are stepped once; the
+resulting boolean mask is cached per (pattern, state).  A `Guide` is one sequence's
+position in its DFA: the sampler masks the row's logits with `guide.mask()`, and the
+engine advances the guide with every token the sequence takes.
+
+End of output: where the DFA accepts, the EOS ids are allowed too; where it accepts and
+cannot continue, only EOS is.  A request with `ignore_eos` ends ("stop") when its guide
+can no longer continue.
+
+Tokens whose text is empty (special tokens) or not whole characters (a byte-level
+tokenizer's partial UTF-8 bytes) are never allowed, so guided outputs are spelled with
+whole-character tokens.
+"""
+from __future__ import annotations
+
+import threading
+from collections import OrderedDict
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from rusteeze_b200.engine.guided.json_schema import any_object, schema_to_regex
+from rusteeze_b200.engine.guided.regex_fsm import RegexFSM
+
+MASK_CACHE_STATES = 2048
+
+
+def guide_pattern(g) -> str:
+    """The regex of a `GuidedDecodingParams` (exactly one constraint must be set)."""
+    import re
+    kinds = [k for k in ("choice", "regex", "json_schema", "json_object", "grammar")
+             if getattr(g, k, None) not in (None, False, [], "")]
+    if len(kinds) != 1:
+        raise ValueError(f"guided decoding needs exactly one of choice / regex / json_schema / json_object, "
+                         f"got {kinds or 'none'}")
+    k = kinds[0]
+    if k == "choice":
+        return "(" + "|".join(re.escape(str(c)) for c in g.choice) + ")"
+    if k == "regex":
+        return g.regex
+    if k == "json_schema":
+        return schema_to_regex(g.json_schema)
+    if k == "json_object":
+        return any_object()
+    raise ValueError("grammar-guided decoding is not supported; use regex, choice or json_schema")
+
+
+class TokenIndex:
+    """Token texts and the character trie over them, for one tokenizer."""
+
+    def __init__(self, tokenizer, vocab_size: int):
+        self.vocab_size = vocab_size
+        texts: List[str] = []
+        for i in range(vocab_size):
+            try:
+                t = tokenizer.decode([i], True)
+            except Exception:  # noqa: BLE001 -- ids the tokenizer does not know
+                t = ""
+            texts.append("" if "�" in t else t)
+        self.texts = texts
+        # trie: node = [children dict, token ids ending here]
+        root: list = [{}, []]
+        for i, t in enumerate(texts):
+            if not t:
+                continue
+            node = root
+            for ch in t:
+                nxt = node[0].get(ch)
+                if nxt is None:
+                    nxt = node[0][ch] = [{}, []]
+                node = nxt
+            node[1].append(i)
+        self.root = root
+
+    def allowed(self, fsm: RegexFSM, state: int) -> np.ndarray:
+        """Bool mask [vocab]: tokens whose whole text keeps the DFA alive from `state`."""
+        mask = np.zeros(self.vocab_size, dtype=bool)
+        stack = [(self.root, state)]
+        step = fsm.step
+        while stack:
+            node, st = stack.pop()
+            for ch, child in node[0].items():
+                ns = step(st, ch)
+                if ns < 0:
+                    continue
+                if child[1]:
+                    mask[child[1]] = True
+                if child[0]:
+                    stack.append((child, ns))
+        return mask
+
+
+_lock = threading.Lock()
+_fsms: Dict[str, RegexFSM] = {}
+_indexes: Dict[Tuple[int, int], TokenIndex] = {}
+_masks: "OrderedDict[Tuple[str, int, int], np.ndarray]" = OrderedDict()
+
+
+def fsm_for(pattern: str) -> RegexFSM:
+    with _lock:
+        f = _fsms.get(pattern)
+        if f is None:
+            f = _fsms[pattern] = RegexFSM(pattern)
+        return f
+
+
+def index_for(tokenizer, vocab_size: int) -> TokenIndex:
+    key = (id(tokenizer), vocab_size)
+    with _lock:
+        ix = _indexes.get(key)
+    if ix is None:
+        ix = TokenIndex(tokenizer, vocab_size)
+        with _lock:
+            _indexes[key] = ix
+    return ix
+
+
+class Guide:
+    """One sequence's position in its constraint's DFA."""
+
+    __slots__ = ("fsm", "index", "state", "eos_ids")
+
+    def __init__(self, fsm: RegexFSM, index: TokenIndex, eos_ids: Sequence[int], state: Optional[int] = None):
+        self.fsm, self.index, self.eos_ids = fsm, index, tuple(eos_ids)
+        self.state = fsm.start if state is None else state
+
+    def copy(self) -> "Guide":
+        return Guide(self.fsm, self.index, self.eos_ids, self.state)
+
+    @property
+    def complete(self) -> bool:
+        """The output matches and nothing can follow."""
+        return self.fsm.accepting(self.state) and not self.fsm.can_continue(self.state)
+
+    def mask(self, allow_eos: bool = True) -> np.ndarray:
+        key = (self.fsm.pattern, id(self.index), self.state)
+        with _lock:
+            m = _masks.get(key)
+            if m is not None:
+                _masks.move_to_end(key)
+        if m is None:
+            m = self.index.allowed(self.fsm, self.state) if self.state >= 0 else \
+                np.zeros(self.index.vocab_size, dtype=bool)
+            with _lock:
+                _masks[key] = m
+                while len(_masks) > MASK_CACHE_STATES:
+                    _masks.popitem(last=False)
+        if allow_eos and self.fsm.accepting(self.state):
+            m = m.copy()
+            for e in self.eos_ids:
+                if 0 <= e < m.shape[0]:
+                    m[e] = True
+        return m
+
+    def advance(self, tok: int) -> None:
+        if tok in self.eos_ids:
+            return
+        t = self.index.texts[tok] if 0 <= tok < len(self.index.texts) else ""
+        self.state = self.fsm.walk(self.state, t) if t else -1

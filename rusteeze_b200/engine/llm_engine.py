@@ -217,6 +217,16 @@ class LLMEngine:
         if len(prompt_token_ids) >= self.max_model_len:
             raise ContextLengthExceededError(
                 f"prompt has {len(prompt_token_ids)} tokens; the model context is {self.max_model_len}")
+        guide = None
+        if params.guided_decoding is not None:
+            if params.use_beam_search:
+                raise InvalidRequestError("beam search cannot be combined with guided decoding")
+            from rusteeze_b200.engine.guided import Guide, fsm_for, guide_pattern, index_for
+            try:
+                fsm = fsm_for(guide_pattern(params.guided_decoding))
+            except ValueError as e:
+                raise InvalidRequestError(f"guided decoding: {e}", param="guided_decoding") from None
+            guide = Guide(fsm, index_for(self.tokenizer, V), self.eos_ids)
         if params.use_beam_search:
             if self.spec is not None:
                 raise InvalidRequestError("beam search cannot be combined with speculative decoding")
@@ -234,6 +244,8 @@ class LLMEngine:
             req.seed = int(params.seed)
         if params.use_beam_search:
             self._beams.start(req)
+        if guide is not None:
+            req.seqs[0].guide = guide
         for s in req.seqs:
             self._register_seq(req, s)
             self.scheduler.add(s)
@@ -444,9 +456,11 @@ class LLMEngine:
                 owners.append((ss, 1))
                 continue
             # token histories are read from the sequence only by rows that need them
+            mask = s.guide.mask(allow_eos=not p.ignore_eos) if s.guide is not None else None
             for j in range(ss.num_samples):
                 rows.append(SampleRow(p, None, None, req.seed + 7919 * (s.index + j), s.num_generated + s.pending,
                                       self.eos_ids, s.mirostat_mu, s, j))
+                rows[-1].allowed = mask
             owners.append((ss, ss.num_samples))
         return rows, owners
 
@@ -480,6 +494,7 @@ class LLMEngine:
                     c = Sequence(req, req.prompt_token_ids, index=j)
                     c.num_computed = s.num_computed
                     c.num_cached = s.num_cached
+                    c.guide = s.guide.copy() if s.guide is not None else None
                     self.bm.fork(s.seq_id, c.seq_id)
                     req.seqs.append(c)
                     self._register_seq(req, c)
@@ -517,6 +532,8 @@ class LLMEngine:
             s.output_text += delta
         reason = None
         n = s.num_generated
+        if s.guide is not None:
+            s.guide.advance(tok)
         if n >= p.min_tokens:
             if not p.ignore_eos and tok in self.eos_ids:
                 reason = "stop"
@@ -535,6 +552,9 @@ class LLMEngine:
         if reason is None and ((p.max_tokens is not None and n >= p.max_tokens)
                                or len(s.token_ids) >= self.max_model_len):
             reason = "length"
+        if (reason is None and s.guide is not None and (p.ignore_eos or not self.eos_ids)
+                and (s.guide.complete or s.guide.state < 0)):
+            reason = "stop"               # the constrained output is complete and no EOS will come
         if reason is not None:
             s.finish_reason = reason
             s.status = RequestStatus.FINISHED_STOPPED if reason == "stop" else RequestStatus.FINISHED_LENGTH

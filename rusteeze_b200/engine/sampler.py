@@ -38,7 +38,8 @@ class SampleRow:
     """One row of logits to sample.  `seq` (the engine's Sequence, when there is one) and
     `sub` (the sample index of a best_of prompt row) key the row's device slot; the token
     histories that penalties read are taken from the sequence only when they are needed."""
-    __slots__ = ("params", "_prompt_ids", "_output_ids", "seed", "offset", "eos_ids", "mirostat_mu", "seq", "sub")
+    __slots__ = ("params", "_prompt_ids", "_output_ids", "seed", "offset", "eos_ids", "mirostat_mu", "seq", "sub",
+                 "allowed")
 
     def __init__(self, params: SamplingParams, prompt_ids: Optional[Seq[int]] = None,
                  output_ids: Optional[Seq[int]] = None, seed: int = 0, offset: int = 0,
@@ -48,6 +49,7 @@ class SampleRow:
         self._output_ids = output_ids
         self.seed, self.offset, self.eos_ids, self.mirostat_mu = seed, offset, eos_ids, mirostat_mu
         self.seq, self.sub = seq, sub
+        self.allowed = None            # guided decoding: bool mask [vocab] of the tokens that may come next
 
     @property
     def prompt_ids(self) -> Seq[int]:
@@ -462,9 +464,15 @@ def _cpu_sample(logits: torch.Tensor, rows: List[SampleRow]):
 
 
 def _host_sample(x: torch.Tensor, r: SampleRow):
-    """Mirostat v1/v2, typical-p, eta/epsilon cutoffs, guided choice."""
+    """Rows the GPU kernel does not cover: guided decoding (the row's `allowed` mask,
+    applied to the logits first, like a logits processor), Mirostat v1/v2, typical-p,
+    eta / epsilon cutoffs; then top-k / top-p / min-p of the remaining distribution."""
     p = r.params
     g = _row_generator(r.seed, r.offset)
+    if r.allowed is not None:
+        allowed = torch.from_numpy(r.allowed[:x.shape[0]])
+        if bool(allowed.any()):
+            x = x.masked_fill(~allowed, float("-inf"))
     if p.temperature > 0:
         x = x / p.temperature
     probs = torch.softmax(x, -1)
@@ -485,7 +493,7 @@ def _host_sample(x: torch.Tensor, r: SampleRow):
         surprise = -math.log(max(pr, 1e-10))
         mu = mu + p.mirostat_eta * (p.mirostat_tau - surprise)
         return tok, math.log(max(pr, 1e-45)), mu
-    keep = torch.ones_like(probs, dtype=torch.bool)
+    keep = torch.isfinite(x)
     if p.typical_p > 0:
         ent = -(probs * torch.log(probs.clamp_min(1e-30))).sum()
         dev = (-torch.log(probs.clamp_min(1e-30)) - ent).abs()
@@ -501,13 +509,18 @@ def _host_sample(x: torch.Tensor, r: SampleRow):
         ent = -(probs * torch.log(probs.clamp_min(1e-30))).sum()
         eps = min(p.eta_cutoff, math.sqrt(p.eta_cutoff) * math.exp(-float(ent)))
         keep &= probs >= eps
-    if p.guided_decoding is not None and getattr(r, "allowed", None) is not None:
-        m = torch.zeros_like(keep)
-        m[list(r.allowed)] = True
-        keep &= m
+    if p.temperature > 0 and (p.top_k > 0 or p.top_p < 1.0 or p.min_p > 0.0):
+        fp = ref.topk_topp_minp_probs(x.unsqueeze(0), torch.ones(1), torch.tensor([p.top_k]),
+                                      torch.tensor([p.top_p]), torch.tensor([p.min_p]))[0]
+        keep &= fp > 0
     if not keep.any():
-        keep[int(probs.argmax())] = True
+        keep[int(x.argmax())] = True
     pr = torch.where(keep, probs, torch.zeros_like(probs))
+    if float(pr.sum()) <= 0.0:
+        # every kept token's probability underflowed (or was masked, e.g. EOS before
+        # min_tokens when the constraint allows nothing else): the best kept logit
+        tok = int(torch.where(keep, x, torch.full_like(x, -float("inf"))).argmax())
+        return tok, math.log(max(float(probs[tok]), 1e-45)), None
     if p.temperature == 0:
         tok = int(pr.argmax())
     else:

@@ -36,7 +36,7 @@ class Sequence:
     __slots__ = ("seq_id", "request", "prompt_len", "token_ids", "status", "num_computed",
                  "num_cached", "logprobs", "cumulative_logprob", "output_text", "stop_reason",
                  "detok", "_buf", "index", "finish_reason", "rng_offset",
-                 "mirostat_mu", "spec_draft", "pending", "detok_n", "sched_key", "pruned")
+                 "mirostat_mu", "spec_draft", "pending", "detok_n", "sched_key", "pruned", "guide")
 
     def __init__(self, request: "Request", prompt_token_ids: List[int], index: int = 0):
         self.seq_id = next(_seq_ids)
@@ -68,6 +68,7 @@ class Sequence:
         # only on the device until the step's results are applied
         self.pending = 0
         self.pruned = False            # a beam that left the search: never reported
+        self.guide = None              # guided decoding: position in the constraint's automaton
 
     def fork_copy(self, index: int, with_kv: bool) -> "Sequence":
         """A new sequence with this one's tokens, logprobs, text and detokenizer state
@@ -85,6 +86,7 @@ class Sequence:
         c.detok = self.detok.clone() if self.detok is not None else None
         c.detok_n = self.detok_n
         c.mirostat_mu = self.mirostat_mu
+        c.guide = self.guide.copy() if self.guide is not None else None
         if with_kv:
             c.num_computed, c.num_cached = self.num_computed, self.num_cached
         return c

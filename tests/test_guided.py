@@ -1,0 +1,200 @@
+"""Guided (structured) decoding: the regex automaton against Python's `re` (full matches)
+and the `regex` module (partial matches: a prefix keeps the automaton alive exactly when
+it can still be completed), JSON Schema compilation against instances, token masks
+against a brute-force check of every token, and constrained generation through the
+engine and the HTTP API with random weights: every output satisfies its constraint."""
+import json
+import re
+
+import numpy as np
+import pytest
+import regex as regex_mod
+from hypothesis import given, settings, strategies as st
+
+from rusteeze_b200.config.config import Config
+from rusteeze_b200.core.errors import InvalidRequestError
+from rusteeze_b200.core.sampling_params import GuidedDecodingParams, SamplingParams
+from rusteeze_b200.engine.guided.guide import TokenIndex, fsm_for
+from rusteeze_b200.engine.guided.json_schema import any_object, schema_to_regex
+from rusteeze_b200.engine.guided.regex_fsm import RegexError, RegexFSM
+from rusteeze_b200.engine.llm_engine import LLMEngine
+from rusteeze_b200.tokenizer.tokenizer import ByteTokenizer
+
+PATTERNS = [r"[0-9]{3}-[a-c]+", r"(ab|ba)*c?", r"a{2,4}b{0,2}", r"(x|yz)+(\.[xy]{1,2})?", r"[^abc]b*",
+            r"\d\w\s?", r"(?:a|b)(?P<n>c|d)e?", r"a.c", r"[a-c-]+", r"^ab+$"]
+ALPHA = "abcxyz0123-. \n"
+
+
+@settings(max_examples=400, deadline=None)
+@given(st.sampled_from(PATTERNS), st.text(alphabet=ALPHA, max_size=8))
+def test_fsm_matches_python_re_and_partial_matches(pat, s):
+    f = fsm_for(pat)
+    assert f.fullmatch(s) == bool(re.fullmatch(pat, s))
+    alive = f.walk(f.start, s) >= 0
+    assert alive == (regex_mod.fullmatch(pat, s, partial=True) is not None)
+
+
+def test_unsupported_patterns_are_refused():
+    for p in (r"(a)\1", r"(?=a)b", r"a{5,2}", "[abc", "(ab", "*a"):
+        with pytest.raises(RegexError):
+            RegexFSM(p)
+
+
+SCHEMA = {"type": "object",
+          "properties": {"name": {"type": "string", "maxLength": 6},
+                         "age": {"type": "integer"},
+                         "tags": {"type": "array", "items": {"enum": ["a", "b"]}, "maxItems": 2},
+                         "kind": {"$ref": "#/$defs/kind"},
+                         "score": {"type": ["number", "null"]}},
+          "required": ["name", "age"],
+          "$defs": {"kind": {"enum": ["x", "y"]}}}
+
+
+def _valid(d) -> bool:
+    if not isinstance(d, dict) or set(d) - set(SCHEMA["properties"]) or not {"name", "age"} <= set(d):
+        return False
+    if not (isinstance(d["name"], str) and len(d["name"]) <= 6) or type(d["age"]) is not int:
+        return False
+    if "tags" in d and not (isinstance(d["tags"], list) and len(d["tags"]) <= 2 and set(d["tags"]) <= {"a", "b"}):
+        return False
+    if "kind" in d and d["kind"] not in ("x", "y"):
+        return False
+    return "score" not in d or d["score"] is None or type(d["score"]) in (int, float)
+
+
+def test_schema_regex_accepts_instances_and_rejects_others():
+    f = RegexFSM(schema_to_regex(SCHEMA))
+    good = [{"name": "bo", "age": 3}, {"name": "", "age": -12, "tags": ["a", "b"], "kind": "y", "score": 1.5},
+            {"name": "ab\"c", "age": 0, "score": None}, {"name": "x", "age": 7, "kind": "x"}]
+    for d in good:
+        assert _valid(d)
+        for sep in ((",", ":"), (", ", ": ")):
+            assert f.fullmatch(json.dumps(d, separators=sep)), d
+    bad = ['{"age": 3}', '{"name": "toolongname", "age": 3}', '{"name": "a", "age": 1.5}',
+           '{"name": "a", "age": 1, "tags": ["c"]}', '{"name": "a", "age": 1, "extra": 1}',
+           '{"age": 1, "name": "a"}']                     # properties come in the schema's order
+    for t in bad:
+        assert not f.fullmatch(t), t
+    assert RegexFSM(any_object()).fullmatch('{"a": [1, {"b": null}], "c": "x"}')
+
+
+def test_token_masks_equal_a_brute_force_check():
+    tok = ByteTokenizer(300)
+    ix = TokenIndex(tok, 300)
+    f = fsm_for(r'"[a-c]{0,3}"|[0-9]+')
+    rng = np.random.default_rng(0)
+    states = {f.start}
+    for s in ('"', '"ab', '"abc', "12", '"abc"'):
+        states.add(f.walk(f.start, s))
+    for _ in range(5):
+        states.add(f.walk(f.start, "".join(rng.choice(list('"abc0123'), 2))))
+    for stt in states:
+        if stt < 0:
+            continue
+        m = ix.allowed(f, stt)
+        want = np.array([bool(t) and f.walk(stt, t) >= 0 for t in ix.texts])
+        assert (m == want).all()
+
+
+def _engine(preset="tiny-llama"):
+    cfg = Config()
+    cfg.model.preset, cfg.model.device, cfg.model.dtype = preset, "cpu", "float32"
+    cfg.engine.num_gpu_blocks = 128
+    cfg.engine.max_num_seqs = 8
+    return LLMEngine(cfg)
+
+
+def _gen(eng, g, n=1, temp=0.9, max_tokens=80, seed=1, **kw):
+    eng.add_request(None, "hello", SamplingParams(n=n, temperature=temp, max_tokens=max_tokens, guided_decoding=g,
+                                                  seed=seed, **kw))
+    fin = None
+    while eng.has_unfinished_requests():
+        for o in eng.step():
+            if o.finished:
+                fin = o
+    return fin.outputs
+
+
+@pytest.fixture(scope="module")
+def eng():
+    return _engine()
+
+
+def test_choice_regex_and_schema_outputs_satisfy_their_constraints(eng):
+    for seed in range(3):
+        outs = _gen(eng, GuidedDecodingParams(choice=["yes", "no", "maybe not"]), n=3, seed=seed)
+        assert all(o.text in ("yes", "no", "maybe not") and o.finish_reason == "stop" for o in outs)
+        outs = _gen(eng, GuidedDecodingParams(regex=r"[0-9]{3}-[a-z]{2,5}"), n=2, seed=seed)
+        assert all(re.fullmatch(r"[0-9]{3}-[a-z]{2,5}", o.text) for o in outs)
+        outs = _gen(eng, GuidedDecodingParams(json_schema=SCHEMA), max_tokens=200, seed=seed,
+                    logit_bias={ord("}") + 3: 4.0, ord(",") + 3: 2.0, ord('"') + 3: 3.0})
+        for o in outs:
+            assert o.finish_reason == "stop", o.text
+            assert _valid(json.loads(o.text)), o.text
+    greedy = _gen(eng, GuidedDecodingParams(regex=r"(ab|cd){2}x?"), temp=0.0)
+    assert re.fullmatch(r"(ab|cd){2}x?", greedy[0].text)
+
+
+def test_top_k_applies_to_the_constrained_distribution(eng):
+    """Guided rows are sampled on the host: top_k=1 at temperature 1 must give the greedy
+    constrained output whatever the seed."""
+    g = GuidedDecodingParams(regex=r"[a-z]{4}")
+    greedy = _gen(eng, g, temp=0.0)[0].text
+    assert {_gen(eng, g, temp=1.0, top_k=1, seed=s)[0].text for s in range(4)} == {greedy}
+    assert len({_gen(eng, g, temp=1.0, seed=s)[0].text for s in range(4)}) > 1
+
+
+def test_json_object_mode_prefixes_stay_valid(eng):
+    f = fsm_for(any_object())
+    for seed in range(3):
+        o = _gen(eng, GuidedDecodingParams(json_object=True), max_tokens=120, seed=seed,
+                 logit_bias={ord("}") + 3: 6.0, ord("]") + 3: 4.0, ord('"') + 3: 3.0})[0]
+        assert f.walk(f.start, o.text) >= 0, o.text
+        if o.finish_reason == "stop":
+            assert isinstance(json.loads(o.text), dict)
+
+
+def test_ignore_eos_stops_when_the_constraint_is_complete(eng):
+    outs = _gen(eng, GuidedDecodingParams(choice=["alpha", "beta"]), n=2, ignore_eos=True)
+    assert all(o.text in ("alpha", "beta") and o.finish_reason == "stop" for o in outs)
+
+
+def test_invalid_constraints_are_refused(eng):
+    for g in (GuidedDecodingParams(), GuidedDecodingParams(regex="a", choice=["a"]),
+              GuidedDecodingParams(grammar="root ::= 'a'"), GuidedDecodingParams(regex="(a")):
+        with pytest.raises(InvalidRequestError):
+            eng.add_request(None, "x", SamplingParams(guided_decoding=g))
+    with pytest.raises(InvalidRequestError):
+        eng.add_request(None, "x", SamplingParams(best_of=2, use_beam_search=True, temperature=0.0,
+                                                  guided_decoding=GuidedDecodingParams(regex="a+")))
+
+
+def test_structured_output_through_the_api():
+    from fastapi.testclient import TestClient
+
+    from rusteeze_b200.api.server import create_app
+    from rusteeze_b200.engine.async_engine import AsyncLLMEngine
+    cfg = Config()
+    cfg.logging.request_logging = False
+    ae = AsyncLLMEngine(_engine()).start()
+    try:
+        c = TestClient(create_app(ae, cfg))
+        schema = {"type": "object", "properties": {"ok": {"type": "boolean"}, "n": {"type": "integer"}},
+                  "required": ["ok", "n"]}
+        r = c.post("/v1/chat/completions", json={
+            "messages": [{"role": "user", "content": "answer in JSON"}], "max_tokens": 60, "temperature": 0.7,
+            "seed": 4, "logit_bias": {str(ord("}") + 3): 5.0},
+            "response_format": {"type": "json_schema", "json_schema": {"name": "a", "schema": schema}}})
+        assert r.status_code == 200, r.text
+        d = json.loads(r.json()["choices"][0]["message"]["content"])
+        assert type(d["ok"]) is bool and type(d["n"]) is int
+        r = c.post("/v1/completions", json={"prompt": "pick", "max_tokens": 10, "n": 3, "temperature": 1.0,
+                                            "guided_choice": ["red", "green"]})
+        assert r.status_code == 200 and {x["text"] for x in r.json()["choices"]} <= {"red", "green"}
+        r = c.post("/v1/completions", json={"prompt": "x", "guided_regex": "(a"})
+        assert r.status_code == 400
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                 "response_format": {"type": "xml"}})
+        assert r.status_code == 400
+    finally:
+        ae.shutdown()
