@@ -15,6 +15,7 @@ refused (they are not regular).
 from __future__ import annotations
 
 import bisect
+import threading
 from typing import Dict, FrozenSet, List, Optional, Tuple
 
 MAX_CP = 0x10FFFF
@@ -317,6 +318,9 @@ class RegexFSM:
         self._trans: List[Dict[str, int]] = []
         self._accept: List[bool] = []
         self._live: List[bool] = []
+        # states and transitions are added on first use; engines on several threads (data-
+        # parallel replicas in one process) may share one automaton
+        self._lock = threading.Lock()
         self.start = self._state(self._closure([s]))
 
     def _closure(self, states) -> FrozenSet[int]:
@@ -354,9 +358,12 @@ class RegexFSM:
             return nxt
         cp = ord(ch)
         sets, edges = self._nfa.sets, self._nfa.edges
-        targets = [y for x in self._sets[state] for sid, y in edges[x] if _contains(sets[sid], cp)]
-        nxt = self._state(self._closure(targets)) if targets else -1
-        t[ch] = nxt
+        with self._lock:
+            nxt = t.get(ch)
+            if nxt is None:
+                targets = [y for x in self._sets[state] for sid, y in edges[x] if _contains(sets[sid], cp)]
+                nxt = self._state(self._closure(targets)) if targets else -1
+                t[ch] = nxt
         return nxt
 
     def walk(self, state: int, text: str) -> int:

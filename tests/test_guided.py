@@ -96,6 +96,29 @@ def test_token_masks_equal_a_brute_force_check():
         assert (m == want).all()
 
 
+class _WordTokenizer:
+    """A large synthetic vocabulary (multi-character tokens), to reach the self-loop path."""
+
+    def __init__(self, n, seed=0):
+        rng = np.random.default_rng(seed)
+        alpha = list('abcdefxyz0123456789 .,:"{}[]-\\')
+        self.t = ["".join(rng.choice(alpha, int(rng.integers(1, 6)))) for _ in range(n)]
+
+    def decode(self, ids, skip=True):
+        return "".join(self.t[i] for i in ids)
+
+
+def test_large_vocabulary_masks_equal_a_brute_force_check():
+    ix = TokenIndex(_WordTokenizer(6000), 6000)
+    f = fsm_for(any_object())
+    for text in ("", "{", '{"a', '{"a\\', '{"ab": "x y', '{"a": [1, 2', '{"a": {"b": 1}'):
+        stt = f.walk(f.start, text)
+        assert stt >= 0
+        m = ix.allowed(f, stt)
+        want = np.array([bool(t) and f.walk(stt, t) >= 0 for t in ix.texts])
+        assert (m == want).all(), text
+
+
 def _engine(preset="tiny-llama"):
     cfg = Config()
     cfg.model.preset, cfg.model.device, cfg.model.dtype = preset, "cpu", "float32"
