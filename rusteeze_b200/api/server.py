@@ -167,6 +167,8 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
         if not prompts:
             raise InvalidRequestError("prompt must not be empty")
         sp = _sampling_params(req, defaults, 16, req.logprobs)
+        if req.echo and req.logprobs is not None:
+            sp.prompt_logprobs = req.logprobs        # echoed prompt tokens carry logprobs too
         metrics.on_request_params(sp)
         rid = "cmpl-" + uuid.uuid4().hex
         key = getattr(request.state, "rate_key", None)
@@ -183,9 +185,11 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
             for c in final.outputs:
                 usage.completion_tokens += len(c.token_ids)
                 t = ((final.prompt or eng.tokenizer.decode(final.prompt_token_ids)) if req.echo else "") + c.text
+                echo_lp = (final.prompt_token_ids, final.prompt_logprobs) if (
+                    req.echo and final.prompt_logprobs is not None) else None
                 choices.append(S.CompletionChoice(index=pi * sp.n + c.index, text=t, finish_reason=c.finish_reason,
-                                                  logprobs=_cmpl_logprobs(eng.tokenizer, c) if req.logprobs is not None
-                                                  else None))
+                                                  logprobs=_cmpl_logprobs(eng.tokenizer, c, echo_lp)
+                                                  if req.logprobs is not None else None))
         usage.total_tokens = usage.prompt_tokens + usage.completion_tokens
         return S.CompletionResponse(id=rid, model=model_name, choices=choices, usage=usage)
 
@@ -341,9 +345,20 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
     return app
 
 
-def _cmpl_logprobs(tok, c) -> S.CompletionLogProbs:
+def _cmpl_logprobs(tok, c, prompt=None) -> S.CompletionLogProbs:
+    """OpenAI completion logprobs; with `echo`, the prompt's tokens come first (the first
+    one without a logprob, as it has no context)."""
     lp = S.CompletionLogProbs()
     off = 0
+    if prompt is not None:
+        ids, plp = prompt
+        for tid, d in zip(ids, plp):
+            s = tok.decode([tid])
+            lp.tokens.append(s)
+            lp.token_logprobs.append(None if d is None else d.get(tid))
+            lp.top_logprobs.append(None if d is None else {tok.decode([k]): v for k, v in d.items()})
+            lp.text_offset.append(off)
+            off += len(s)
     for tid, d in zip(c.token_ids, c.logprobs or []):
         s = tok.decode([tid])
         lp.tokens.append(s)

@@ -37,3 +37,6 @@ class RequestOutput:
     num_cached_tokens: int = 0
     # text appended since the previous RequestOutput for this request (streaming)
     delta_text: List[str] = field(default_factory=list)
+    # per prompt token: None for the first, else {token id: logprob} with the prompt's own
+    # token and the `prompt_logprobs` most likely ones (when the request asked for them)
+    prompt_logprobs: Optional[List[Optional[Dict[int, float]]]] = None

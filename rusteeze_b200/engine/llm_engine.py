@@ -479,6 +479,8 @@ class LLMEngine:
         for ss, k in owners:
             s = ss.seq
             req = s.request
+            if req.params.prompt_logprobs is not None and req.prompt_lp is None and s.num_generated == 0:
+                req.prompt_lp = self._score_prompt(s, req.params.prompt_logprobs)
             if req.beam is not None:
                 beams.setdefault(id(req), (req, []))[1].append((s, ss, res.top_logprobs[i]))
                 i += k
@@ -520,6 +522,35 @@ class LLMEngine:
                 seen.add(key)
                 touched.append(req)
         return touched
+
+    @torch.no_grad()
+    def _score_prompt(self, s: Sequence, k: int) -> List[Optional[Dict[int, float]]]:
+        """Prompt logprobs (`prompt_logprobs` = k): one extra forward over the prompt, whose
+        KV is already in the cache, in chunks that fit the runner's staging buffers; the
+        logits at position j - 1 score prompt token j.  The batched step computes logits
+        for sampled positions only, so scoring runs apart from it, once per request."""
+        P = s.prompt_len
+        toks = np.asarray(s.token_ids[:P], dtype=np.int64)
+        runner = self.runner
+        cap = getattr(runner, "max_tokens", None) or getattr(getattr(runner, "runner", None), "max_tokens", P)
+        out: List[Optional[Dict[int, float]]] = [None]
+        c0 = 0
+        while c0 < P - 1:
+            n = min(cap, P - c0)
+            logits = runner.forward_arrays(self.bm, [s.seq_id], [c0], [n], toks[c0:c0 + n], n, 0)
+            lsm = torch.log_softmax(logits.float(), -1).cpu()
+            for r in range(n):
+                j = c0 + r + 1
+                if j >= P:
+                    break
+                d: Dict[int, float] = {}
+                if k:
+                    v, ix = lsm[r].topk(min(k, lsm.shape[1]))
+                    d = dict(zip(ix.tolist(), v.tolist()))
+                d[int(toks[j])] = float(lsm[r, toks[j]])
+                out.append(d)
+            c0 += n
+        return out
 
     def _check_stop(self, s: Sequence, tok: int) -> None:
         req = s.request

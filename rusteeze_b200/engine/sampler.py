@@ -257,7 +257,7 @@ class Sampler:
         but (token, logprob): penalties, logit bias (up to the slot table's 320 entries)
         and min_tokens (up to 32 stop ids with EOS) live in the device slot tables; host
         samplers and top logprobs do not."""
-        return (not params.needs_host_sampling() and params.logprobs is None
+        return (not params.needs_host_sampling() and params.logprobs is None and params.prompt_logprobs is None
                 and len(params.logit_bias) <= 320 and len(params.stop_token_ids) <= 48)
 
     def slots(self, device, max_slots: int) -> SlotTable:

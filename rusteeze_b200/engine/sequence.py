@@ -164,6 +164,7 @@ class Request:
     forked: bool = False
     lora: Optional[str] = None
     beam: Optional[object] = None          # beam search state (engine/beam_search.py)
+    prompt_lp: Optional[list] = None       # prompt logprobs, once scored
     # streaming state
     sent_text_len: Dict[int, int] = field(default_factory=dict)
 
@@ -236,4 +237,4 @@ class Request:
                              prompt_token_ids=self.prompt_token_ids, outputs=outs,
                              finished=self.is_finished(), metrics=self.metrics,
                              num_cached_tokens=max((s.num_cached for s in self.seqs), default=0),
-                             delta_text=deltas)
+                             delta_text=deltas, prompt_logprobs=self.prompt_lp)

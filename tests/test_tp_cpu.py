@@ -398,3 +398,40 @@ def test_tp2_alibi_slopes_follow_each_rank_s_heads():
     finally:
         launcher.shutdown()
     assert got == ref
+
+
+@pytest.mark.timeout(300)
+def test_tp2_prompt_logprobs_beam_search_and_guided_decoding_match_single_process():
+    """Host-side request features on a TP2 engine: prompt scoring (the executor's explicit
+    forward), beam search (forked beams' block tables and copy-on-write copies reach the
+    workers through the plans) and guided decoding (rank 0's sampler masks the logits)
+    give what the single-process engine gives."""
+    from rusteeze_b200.core.sampling_params import GuidedDecodingParams
+    from rusteeze_b200.parallel.launcher import TPEngineLauncher
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, 1000, int(n)).tolist() for n in (40, 9)]
+    reqs = [SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True, prompt_logprobs=2),
+            SamplingParams(n=2, best_of=3, use_beam_search=True, temperature=0.0, max_tokens=6, ignore_eos=True),
+            SamplingParams(temperature=0.0, max_tokens=12, guided_decoding=GuidedDecodingParams(regex=r"[a-f]{3,6}"))]
+
+    def run(eng):
+        ids = [eng.add_request(None, None, sp, p).request_id for sp in reqs for p in prompts]
+        done = {}
+        while eng.has_unfinished_requests():
+            for o in eng.step():
+                if o.finished:
+                    done[o.request_id] = o
+        return [done[i] for i in ids]
+
+    ref = run(LLMEngine(_cfg(1), model_config=MC))
+    launcher = TPEngineLauncher(_cfg(2), model_config=MC, device_type="cpu")
+    try:
+        got = run(launcher.engine())
+    finally:
+        launcher.shutdown()
+    for a, b in zip(got, ref):
+        assert [c.token_ids for c in a.outputs] == [c.token_ids for c in b.outputs]
+        if b.prompt_logprobs is not None:
+            assert len(a.prompt_logprobs) == len(b.prompt_logprobs)
+            for x, y in zip(a.prompt_logprobs[1:], b.prompt_logprobs[1:]):
+                assert x.keys() == y.keys() and max(abs(x[t] - y[t]) for t in x) < 1e-4
