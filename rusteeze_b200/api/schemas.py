@@ -32,6 +32,9 @@ class ChatMessage(BaseModel):
     role: str
     content: Optional[Union[str, List[ContentPart]]] = ""
     name: Optional[str] = None
+    # assistant turns that called tools, and the id a tool result answers
+    tool_calls: Optional[List[Dict[str, Any]]] = None
+    tool_call_id: Optional[str] = None
 
 
 class _SamplingFields(BaseModel):
@@ -130,6 +133,7 @@ class ChatCompletionResponse(BaseModel):
 class ChatDelta(BaseModel):
     role: Optional[str] = None
     content: Optional[str] = None
+    tool_calls: Optional[List[Dict[str, Any]]] = None
 
 
 class ChatChunkChoice(BaseModel):

@@ -63,6 +63,63 @@ def _guided(req) -> Optional[GuidedDecodingParams]:
     return g
 
 
+def _tool_setup(req):
+    """(tools to render, function definitions, mode, JSON schema that forces a call or
+    None).  mode: "none" (no tools, or tool_choice none), "auto" (the reply may be a call,
+    parsed afterwards), "forced" (tool_choice required or a named function: the reply is
+    constrained to {"name": ..., "arguments": ...} by guided decoding)."""
+    tools = req.tools or []
+    choice = req.tool_choice
+    if not tools:
+        if choice not in (None, "none", "auto"):
+            raise InvalidRequestError("tool_choice needs tools", param="tool_choice")
+        return None, [], "none", None
+    fns = []
+    for t in tools:
+        f = t.get("function") if isinstance(t, dict) else None
+        if not isinstance(t, dict) or t.get("type", "function") != "function" or not isinstance(f, dict) \
+                or not f.get("name"):
+            raise InvalidRequestError("each tool must be {type: function, function: {name, parameters}}",
+                                      param="tools")
+        fns.append(f)
+    if choice in (None, "auto"):
+        return tools, fns, "auto", None
+    if choice == "none":
+        return None, fns, "none", None
+    if choice == "required":
+        chosen = fns
+    elif isinstance(choice, dict) and choice.get("type") == "function":
+        name = (choice.get("function") or {}).get("name")
+        chosen = [f for f in fns if f["name"] == name]
+        if not chosen:
+            raise InvalidRequestError(f"tool_choice names an unknown function {name!r}", param="tool_choice")
+    else:
+        raise InvalidRequestError("tool_choice must be none, auto, required or {type: function, function: {name}}",
+                                  param="tool_choice")
+    alts = [{"type": "object", "properties": {"name": {"const": f["name"]},
+                                              "arguments": f.get("parameters") or {"type": "object"}},
+             "required": ["name", "arguments"]} for f in chosen]
+    return tools, fns, "forced", (alts[0] if len(alts) == 1 else {"anyOf": alts})
+
+
+def _parse_tool_call(text: str, fns) -> Optional[dict]:
+    """A reply that is exactly one JSON call of a known function, as an OpenAI tool call."""
+    t = text.strip()
+    if not t.startswith("{"):
+        return None
+    try:
+        d = json.loads(t)
+    except ValueError:
+        return None
+    if not isinstance(d, dict):
+        return None
+    args = d.get("arguments", d.get("parameters"))
+    if d.get("name") not in {f["name"] for f in fns} or not isinstance(args, dict):
+        return None
+    return {"id": "call_" + uuid.uuid4().hex[:24], "type": "function",
+            "function": {"name": d["name"], "arguments": json.dumps(args)}}
+
+
 def _sampling_params(req, defaults, max_tokens_default: int, logprobs: Optional[int]) -> SamplingParams:
     stop = req.stop if isinstance(req.stop, list) else ([req.stop] if req.stop else [])
     mt = getattr(req, "max_completion_tokens", None) or req.max_tokens or max_tokens_default
@@ -232,12 +289,13 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
     async def chat(req: S.ChatCompletionRequest, request: Request):
         _check_model(req.model)
         msgs = [m.model_dump() for m in req.messages]
+        tools, fns, tool_mode, call_schema = _tool_setup(req)
         if req.chat_template and not sc.trust_request_chat_template:
             raise InvalidRequestError("a per-request chat_template is disabled on this server "
                                       "(server.trust_request_chat_template)", param="chat_template")
         tmpl = template if not req.chat_template else ChatTemplate(jinja=req.chat_template)
         try:
-            prompt = tmpl.apply(msgs, add_generation_prompt=req.add_generation_prompt)
+            prompt = tmpl.apply(msgs, add_generation_prompt=req.add_generation_prompt, tools=tools)
         except RusteezeError:
             raise
         except Exception as e:  # noqa: BLE001 -- template syntax errors, raise_exception(), bad messages
@@ -246,26 +304,36 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
         ids = eng.tokenizer.encode(prompt, add_special_tokens=False) or eng.tokenizer.encode(prompt)
         lp = (req.top_logprobs or 0) if req.logprobs else None
         sp = _sampling_params(req, defaults, defaults.max_tokens, lp)
+        if call_schema is not None:
+            if sp.guided_decoding is not None:
+                raise InvalidRequestError("tool_choice required / named cannot be combined with response_format "
+                                          "or guided decoding", param="tool_choice")
+            sp.guided_decoding = GuidedDecodingParams(json_schema=call_schema)
         metrics.on_request_params(sp)
         rid = "chatcmpl-" + uuid.uuid4().hex
         key = getattr(request.state, "rate_key", None)
         if req.stream:
-            return StreamingResponse(_stream_chat(rid, ids, sp, req, key), media_type="text/event-stream")
+            return StreamingResponse(_stream_chat(rid, ids, sp, req, key, tool_mode, fns),
+                                     media_type="text/event-stream")
         final = None
         async for out in async_engine.generate(None, sp, rid, ids, priority=req.priority):
             final = out
         metrics.on_request_finished(final, "chat")
         _charge(key, final)
-        choices = [S.ChatChoice(index=c.index, message=S.ChatMessage(role="assistant", content=c.text),
-                                finish_reason=c.finish_reason,
-                                logprobs=_chat_logprobs(eng.tokenizer, c) if req.logprobs else None)
-                   for c in final.outputs]
+        choices = []
+        for c in final.outputs:
+            call = _parse_tool_call(c.text, fns) if tool_mode != "none" and c.finish_reason == "stop" else None
+            msg = (S.ChatMessage(role="assistant", content=None, tool_calls=[call]) if call is not None
+                   else S.ChatMessage(role="assistant", content=c.text))
+            choices.append(S.ChatChoice(index=c.index, message=msg,
+                                        finish_reason="tool_calls" if call is not None else c.finish_reason,
+                                        logprobs=_chat_logprobs(eng.tokenizer, c) if req.logprobs else None))
         n_out = sum(len(c.token_ids) for c in final.outputs)
         return S.ChatCompletionResponse(id=rid, model=model_name, choices=choices,
                                         usage=S.Usage(prompt_tokens=len(ids), completion_tokens=n_out,
                                                       total_tokens=len(ids) + n_out))
 
-    async def _stream_chat(rid, ids, sp, req, key) -> AsyncIterator[str]:
+    async def _stream_chat(rid, ids, sp, req, key, tool_mode="none", fns=()) -> AsyncIterator[str]:
         for i in range(sp.n):
             yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
                 S.ChatChunkChoice(index=i, delta=S.ChatDelta(role="assistant", content=""))]))
@@ -274,16 +342,39 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
         completed = False
         try:
             try:
+                # with tools, a reply that opens with "{" is held back until it is known
+                # whether it is a call (sent as one tool_calls delta) or text
+                held: dict = {}
+                passthrough: dict = {}
                 async for out in agen:
                     final = out
                     for c, delta in zip(out.outputs, out.delta_text):
+                        i = c.index
+                        if tool_mode != "none" and not passthrough.get(i):
+                            held[i] = held.get(i, "") + delta
+                            lead = held[i].lstrip()
+                            if lead and not lead.startswith("{") and tool_mode == "auto":
+                                passthrough[i] = True
+                                delta, held[i] = held[i], ""
+                            else:
+                                delta = ""
                         if delta:
                             yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
-                                S.ChatChunkChoice(index=c.index, delta=S.ChatDelta(content=delta))]))
+                                S.ChatChunkChoice(index=i, delta=S.ChatDelta(content=delta))]))
                         if c.finish_reason:
+                            reason = c.finish_reason
+                            if held.get(i):
+                                call = _parse_tool_call(held[i], fns) if reason == "stop" else None
+                                if call is not None:
+                                    reason = "tool_calls"
+                                    d = S.ChatDelta(tool_calls=[{"index": 0, **call}])
+                                else:
+                                    d = S.ChatDelta(content=held[i])
+                                held[i] = ""
+                                yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
+                                    S.ChatChunkChoice(index=i, delta=d)]))
                             yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
-                                S.ChatChunkChoice(index=c.index, delta=S.ChatDelta(),
-                                                  finish_reason=c.finish_reason)]))
+                                S.ChatChunkChoice(index=i, delta=S.ChatDelta(), finish_reason=reason)]))
                 completed = True
             finally:
                 await agen.aclose()               # a stream closed early aborts its request now, not at GC

@@ -69,7 +69,11 @@ class ChatTemplate:
         eos = getattr(tokenizer, "eos_token", "") if tokenizer else ""
         return cls(fmt, bos, eos, jinja)
 
-    def apply(self, messages: List[Dict], add_generation_prompt: bool = True) -> str:
+    def apply(self, messages: List[Dict], add_generation_prompt: bool = True,
+              tools: Optional[List[Dict]] = None) -> str:
+        """Renders the conversation.  `tools` (OpenAI function definitions) go to a Jinja
+        template as its `tools` variable; the built-in formats get them as a system note
+        asking for a JSON call, and see tool results and earlier calls as plain turns."""
         if self.jinja:
             try:
                 from jinja2.sandbox import ImmutableSandboxedEnvironment
@@ -78,10 +82,11 @@ class ChatTemplate:
                 return env.from_string(self.jinja).render(
                     messages=[{**m, "content": _content(m)} for m in messages],
                     add_generation_prompt=add_generation_prompt,
-                    bos_token=self.bos, eos_token=self.eos)
+                    bos_token=self.bos, eos_token=self.eos, tools=tools)
             except ImportError:
                 pass
-        return getattr(self, f"_{self.fmt.value}")(messages, add_generation_prompt)
+        msgs = _flatten_tool_turns(messages, tools, self.fmt)
+        return getattr(self, f"_{self.fmt.value}")(msgs, add_generation_prompt)
 
     # ---- built-in formats (public prompt conventions of each model family) ----
     def _llama(self, msgs, gen):
@@ -172,3 +177,35 @@ class ChatTemplate:
 
 def _raise(msg):
     raise ValueError(msg)
+
+
+_ROLE_FORMATS = ("chatml", "llama3", "zephyr", "phi3")
+
+
+def _flatten_tool_turns(messages: List[Dict], tools: Optional[List[Dict]], fmt) -> List[Dict]:
+    """Tool definitions, calls and results as ordinary turns for the built-in formats:
+    the definitions as a system note, an assistant's calls as JSON in its content, a tool
+    result under the `tool` role where the format has named roles (else as a user turn)."""
+    import json
+    out: List[Dict] = []
+    if tools:
+        fns = [t.get("function", t) for t in tools]
+        note = ("You can call these functions. To call one, answer with only a JSON object "
+                '{"name": <function name>, "arguments": <arguments object>}.\n' + json.dumps(fns))
+        out.append({"role": "system", "content": note})
+    for m in messages:
+        m = dict(m)
+        calls = m.get("tool_calls")
+        if m.get("role") == "assistant" and calls:
+            parts = [_content(m)] if _content(m) else []
+            for c in calls:
+                f = c.get("function", {})
+                args = f.get("arguments", "{}")
+                parts.append(json.dumps({"name": f.get("name"),
+                                         "arguments": json.loads(args) if isinstance(args, str) else args}))
+            m["content"] = "\n".join(parts)
+        if m.get("role") == "tool" and getattr(fmt, "value", fmt) not in _ROLE_FORMATS:
+            m["role"] = "user"
+            m["content"] = f"Tool result: {_content(m)}"
+        out.append(m)
+    return out
