@@ -11,6 +11,11 @@ joins "role: content" lines, handlers.rs:222-229).  `stop`, `n`,
 handlers.rs:143-182: a role chunk, content deltas, a finish chunk, then
 `data: [DONE]`.
 
+Tool calling (`tools`, `tool_choice`: declared in crates/rusteeze-core/src/request.rs:91-95,
+never read by the reference's handlers) renders the tools into the prompt; `required` or a
+named function constrains the reply to one JSON call by guided decoding; `auto` returns a
+call when the reply is one.
+
 The engine runs in its own thread behind `AsyncLLMEngine`; handlers only
 await per-request output queues.
 """
