@@ -93,6 +93,37 @@ class CompletionRequest(_SamplingFields):
     suffix: Optional[str] = None
 
 
+class EmbeddingRequest(BaseModel):
+    """crates/rusteeze-core/src/request.rs:627-672 (types the reference never routes), plus
+    `pooling` and `normalize`."""
+    model_config = ConfigDict(extra="ignore")
+    model: str = ""
+    input: Union[str, List[str], List[int], List[List[int]]]
+    encoding_format: Literal["float", "base64"] = "float"
+    dimensions: Optional[int] = None
+    user: Optional[str] = None
+    pooling: Literal["last", "mean"] = "last"
+    normalize: bool = True
+
+
+class EmbeddingData(BaseModel):
+    object: Literal["embedding"] = "embedding"
+    embedding: Union[List[float], str]
+    index: int
+
+
+class EmbeddingUsage(BaseModel):
+    prompt_tokens: int = 0
+    total_tokens: int = 0
+
+
+class EmbeddingResponse(BaseModel):
+    object: Literal["list"] = "list"
+    data: List[EmbeddingData]
+    model: str
+    usage: EmbeddingUsage
+
+
 class Usage(BaseModel):
     prompt_tokens: int = 0
     completion_tokens: int = 0

@@ -395,6 +395,46 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
             yield "data: " + json.dumps(e.to_openai()) + "\n\n"
         yield _sse("[DONE]")
 
+    # ------------------------------------------------------------------ embeddings
+    @app.post("/v1/embeddings")
+    async def embeddings(req: S.EmbeddingRequest, request: Request):
+        """The final hidden state of each input's last token (or the mean over its tokens),
+        L2-normalised; `dimensions` keeps the first d components (renormalised);
+        `encoding_format` base64 is the little-endian float32 bytes."""
+        _check_model(req.model)
+        inp = req.input
+        if isinstance(inp, str):
+            lists = [eng.tokenizer.encode(inp)]
+        elif inp and all(isinstance(x, str) for x in inp):
+            lists = [eng.tokenizer.encode(x) for x in inp]
+        elif inp and all(isinstance(x, int) for x in inp):
+            lists = [list(inp)]
+        else:
+            lists = [list(x) for x in inp]
+        if not lists or any(len(x) == 0 for x in lists):
+            raise InvalidRequestError("input must not be empty", param="input")
+        vecs = await async_engine.embed(lists, req.pooling, req.normalize)
+        import base64
+        import numpy as np
+        data = []
+        for i, v in enumerate(vecs):
+            v = np.asarray(v, dtype=np.float32)
+            if req.dimensions is not None:
+                if not 1 <= req.dimensions <= v.shape[0]:
+                    raise InvalidRequestError(f"dimensions must be in [1, {v.shape[0]}]", param="dimensions")
+                v = v[:req.dimensions]
+                if req.normalize:
+                    v = v / max(float(np.linalg.norm(v)), 1e-12)
+            emb = (base64.b64encode(v.astype("<f4").tobytes()).decode() if req.encoding_format == "base64"
+                   else v.tolist())
+            data.append(S.EmbeddingData(embedding=emb, index=i))
+        n = sum(len(x) for x in lists)
+        key = getattr(request.state, "rate_key", None)
+        if limiter is not None and key is not None:
+            limiter.charge(key, n)
+        return S.EmbeddingResponse(data=data, model=model_name,
+                                   usage=S.EmbeddingUsage(prompt_tokens=n, total_tokens=n))
+
     # ------------------------------------------------------------------ misc
     @app.get("/v1/models")
     async def models():

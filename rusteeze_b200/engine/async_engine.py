@@ -30,6 +30,15 @@ from rusteeze_b200.core.sampling_params import SamplingParams
 log = logging.getLogger("rusteeze.async_engine")
 
 
+def _settle(fut: "asyncio.Future", result, error) -> None:
+    if fut.done():                     # the caller gave up
+        return
+    if error is not None:
+        fut.set_exception(error)
+    else:
+        fut.set_result(result)
+
+
 @dataclass
 class _Submit:
     request_id: str
@@ -109,6 +118,16 @@ class AsyncLLMEngine:
         self._inbox.put(("abort", request_id))
         self._wake.set()
 
+    async def embed(self, inputs: List[List[int]], pooling: str = "last", normalize: bool = True) -> list:
+        """Embeddings (`LLMEngine.embed`), computed on the engine thread between steps."""
+        if not self.is_ready:
+            raise ServiceUnavailableError(self.last_error or "engine is not ready")
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        self._inbox.put(("embed", (inputs, pooling, normalize, loop, fut)))
+        self._wake.set()
+        return await fut
+
     def stats(self) -> dict:
         d = dict(self.engine.stats())
         d["uptime_s"] = time.time() - self.started_at
@@ -142,6 +161,18 @@ class AsyncLLMEngine:
                     self._deadlines[item.request_id] = time.monotonic() + self.request_timeout_s
                 except BaseException as e:  # noqa: BLE001 -- delivered to the caller
                     self._push(item, e)
+            elif kind == "embed":
+                inputs, pooling, normalize, loop, fut = item
+                try:
+                    if getattr(self.engine, "_inflight", None):
+                        self._deliver(self.engine._drain_inflight())
+                    res, err = self.engine.embed(inputs, pooling, normalize), None
+                except BaseException as e:  # noqa: BLE001 -- delivered to the caller
+                    res, err = None, e
+                try:
+                    loop.call_soon_threadsafe(_settle, fut, res, err)
+                except RuntimeError:        # the caller's event loop is gone
+                    pass
             elif kind == "abort":
                 sub = self._streams.pop(item, None)
                 if sub is not None:
@@ -236,18 +267,22 @@ class AsyncLLMEngine:
                 return
             finally:
                 self.last_step_start = None
-            for o in outs:
-                sub = self._streams.get(o.request_id)
-                if sub is None:
-                    continue
-                if not self._push(sub, o):
-                    # the client is gone: stop generating for it
-                    self._streams.pop(o.request_id, None)
-                    self._deadlines.pop(o.request_id, None)
-                    if not o.finished:
-                        self.engine.abort_request(o.request_id)
-                    continue
-                if o.finished:
-                    self._streams.pop(o.request_id, None)
-                    self._deadlines.pop(o.request_id, None)
-                    self.requests_processed += 1
+            self._deliver(outs)
+
+    def _deliver(self, outs) -> None:
+        """Hands each output to its request's stream."""
+        for o in outs:
+            sub = self._streams.get(o.request_id)
+            if sub is None:
+                continue
+            if not self._push(sub, o):
+                # the client is gone: stop generating for it
+                self._streams.pop(o.request_id, None)
+                self._deadlines.pop(o.request_id, None)
+                if not o.finished:
+                    self.engine.abort_request(o.request_id)
+                continue
+            if o.finished:
+                self._streams.pop(o.request_id, None)
+                self._deadlines.pop(o.request_id, None)
+                self.requests_processed += 1

@@ -207,6 +207,23 @@ class ReplicatedAsyncEngine:
             self._owner.pop(request_id, None)
             self.router.release(rep, time.monotonic() - t0, error=failed)
 
+    async def embed(self, inputs, pooling: str = "last", normalize: bool = True) -> list:
+        """Embeddings on the replica the router picks."""
+        self.router.probe()
+        try:
+            rep = self.router.select()
+        except RuntimeError as e:
+            raise ServiceUnavailableError(f"no ready replica: {e}") from None
+        t0 = time.monotonic()
+        failed = False
+        try:
+            return await rep.backend.embed(inputs, pooling, normalize)
+        except BaseException:
+            failed = True
+            raise
+        finally:
+            self.router.release(rep, time.monotonic() - t0, error=failed)
+
     def abort(self, request_id: str) -> None:
         rep = self._owner.get(request_id)
         for r in ([rep] if rep is not None else self.router.replicas):

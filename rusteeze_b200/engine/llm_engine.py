@@ -523,6 +523,69 @@ class LLMEngine:
                 touched.append(req)
         return touched
 
+    # ------------------------------------------------------------------ embeddings
+    @torch.no_grad()
+    def embed(self, inputs: List[List[int]], pooling: str = "last", normalize: bool = True) -> List[np.ndarray]:
+        """Embeddings of token sequences: the model's final normalised hidden state of the
+        last token (`last`, the pooling of decoder embedding models) or the mean over all
+        tokens (`mean`), L2-normalised unless `normalize` is False.
+
+        Each input is run between engine steps in blocks of its own: allocated under
+        placeholder token ids that no prefix-cache block matches and never published, so
+        an embedding neither reads nor rewrites the prefix cache.  Inputs longer than one
+        step's token budget run in chunks, attending to the chunks before them."""
+        if pooling not in ("last", "mean"):
+            raise InvalidRequestError(f"pooling must be last or mean, got {pooling!r}", param="pooling")
+        if self._inflight:
+            raise RuntimeError("embed() runs between steps: drain the pipelined steps first")
+        from rusteeze_b200.core.errors import ServiceUnavailableError
+        from rusteeze_b200.engine.sequence import _seq_ids
+        V = self.model_config.vocab_size
+        runner = self.runner
+        cap = getattr(runner, "max_tokens", None) or getattr(getattr(runner, "runner", None), "max_tokens", 512)
+        if pooling == "mean" and self.model_config_tp() > 1:
+            cap = min(cap, 512)           # every row's logits are computed (and dropped) at TP > 1
+        out = []
+        for toks in inputs:
+            L = len(toks)
+            if L == 0:
+                raise InvalidRequestError("an embedding input must not be empty")
+            if min(toks) < 0 or max(toks) >= V:
+                raise InvalidRequestError(f"token ids must be in [0, {V})")
+            if L > self.max_model_len:
+                raise ContextLengthExceededError(f"input has {L} tokens; the model context is {self.max_model_len}")
+            placeholder = np.full(L, -1, dtype=np.int64)
+            if self.bm.blocks_needed_for_prompt(placeholder, L) > self.bm.num_free_gpu_blocks():
+                raise ServiceUnavailableError("not enough free KV cache blocks for this input right now")
+            sid = next(_seq_ids)
+            arr = np.asarray(toks, dtype=np.int64)
+            self.bm.allocate_prompt(sid, placeholder)
+            try:
+                self.bm.ensure_capacity(sid, L, 0)
+                acc, vec, c0 = None, None, 0
+                while c0 < L:
+                    n = min(cap, L - c0)
+                    rows = n if pooling == "mean" else 1
+                    hs = runner.forward_arrays(self.bm, [sid], [c0], [n], arr[c0:c0 + n], rows, 0,
+                                               hidden=True).float()
+                    if pooling == "mean":
+                        part = hs.sum(0)
+                        acc = part if acc is None else acc + part
+                    elif c0 + n == L:
+                        vec = hs[-1]
+                    c0 += n
+            finally:
+                self.bm.free(sid)
+            if pooling == "mean":
+                vec = acc / L
+            if normalize:
+                vec = vec / vec.norm().clamp_min(1e-12)
+            out.append(vec.cpu().numpy())
+        return out
+
+    def model_config_tp(self) -> int:
+        return int(getattr(getattr(self.model, "tp", None), "size", 1) or 1)
+
     @torch.no_grad()
     def _score_prompt(self, s: Sequence, k: int) -> List[Optional[Dict[int, float]]]:
         """Prompt logprobs (`prompt_logprobs` = k): one extra forward over the prompt, whose

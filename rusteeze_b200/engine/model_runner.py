@@ -256,18 +256,26 @@ class ModelRunner:
 
     @torch.no_grad()
     def forward_arrays(self, bm, seq_ids, ctx, n_new, toks, logits_per_seq: int,
-                       num_decode: int = 0) -> torch.Tensor:
-        """Eager forward of an explicit token batch (speculative decoding):
-        sequence i gets n_new[i] tokens at positions ctx[i].., and the logits
-        of its last `logits_per_seq` tokens are returned in sequence order."""
+                       num_decode: int = 0, hidden: bool = False) -> torch.Tensor:
+        """Eager forward of an explicit token batch (speculative decoding, prompt scoring,
+        embeddings): sequence i gets n_new[i] tokens at positions ctx[i].., and the logits
+        (or, with `hidden`, the final normalised hidden states) of its last
+        `logits_per_seq` tokens are returned in sequence order."""
         meta, T, S = self.stage_arrays(bm, seq_ids, ctx, n_new, toks, logits_per_seq, num_decode)
-        return self.forward_staged(meta, T, S * logits_per_seq)
+        return self.forward_staged(meta, T, S * logits_per_seq, hidden=hidden)
 
-    def forward_staged(self, meta, T: int, n_rows: int) -> torch.Tensor:
-        """Forward of the staged batch; logits of the rows h_logits_idx[:n_rows]."""
+    def forward_staged(self, meta, T: int, n_rows: int, hidden: bool = False) -> torch.Tensor:
+        """Forward of the staged batch; logits (or hidden states) of the rows
+        h_logits_idx[:n_rows].  A tensor-parallel rank computes the logits even when it
+        returns hidden states: the LM head's all-gather is a collective that every rank
+        joins."""
         h = self.model(self.d_input_ids[:T], self.d_positions[:T], meta, self.kv_layers)
         idx = self.h_logits_idx[:n_rows].to(h.device, non_blocking=self.is_cuda)
-        return self.model.compute_logits(h.index_select(0, idx))
+        hs = h.index_select(0, idx)
+        if hidden and self.model.tp.size == 1:
+            return hs
+        logits = self.model.compute_logits(hs)
+        return hs if hidden else logits
 
     def stage_arrays(self, bm, seq_ids, ctx, n_new, toks, logits_per_seq: int, num_decode: int = 0):
         """Builds and uploads the batch of `forward_arrays` (block tables from `bm`);

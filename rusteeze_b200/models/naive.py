@@ -19,7 +19,8 @@ from rusteeze_b200.ops import reference as ref
 @torch.no_grad()
 def naive_logits(model: DecoderLM, ids, observer=None) -> torch.Tensor:
     """`observer(name, x)`, when given, sees the input of every attention / MLP linear under
-    its HF name (calibration for integer quantization)."""
+    its HF name (calibration for integer quantization), and the final normalised hidden
+    states as "lm_head" (the embedding oracle)."""
     cfg = model.cfg
     obs = observer or (lambda name, x: None)
     assert model.tp.size == 1
@@ -88,6 +89,7 @@ def naive_logits(model: DecoderLM, ids, observer=None) -> torch.Tensor:
             y = ref.rms_norm(y, f(L.post_ff_norm), eps, off)
         h = h + y
     h = ref.rms_norm(h, f(model.norm), eps, off)
+    obs("lm_head", h)
     logits = h @ f(model.lm_head_weight).t()
     logits = logits[:, :cfg.vocab_size]
     if cfg.final_logit_softcapping:

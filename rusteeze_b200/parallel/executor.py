@@ -156,7 +156,7 @@ class TPExecutor:
 
     @torch.no_grad()
     def forward_arrays(self, bm, seq_ids, ctx, n_new, toks, logits_per_seq: int,
-                       num_decode: int = 0) -> torch.Tensor:
+                       num_decode: int = 0, hidden: bool = False) -> torch.Tensor:
         """Speculative-decoding forwards (draft on the target, verify): rank 0 stages
         the explicit token batch, the plan carries its arrays and logits rows, and
         every rank runs the same forward on its shard."""
@@ -165,7 +165,7 @@ class TPExecutor:
         meta, T, S = r.stage_arrays(bm, seq_ids, ctx, n_new, toks, logits_per_seq, num_decode)
         n_rows = S * logits_per_seq
         self.ch.publish(MSG_STEP, {"arrays": n_rows, **_staged_plan(r, meta, T, S)})
-        return r.forward_staged(meta, T, n_rows)
+        return r.forward_staged(meta, T, n_rows, hidden=hidden)
 
     def timer(self, kind: str):
         """Device-timed window over every rank: "start" marks it on each rank's stream,

@@ -401,11 +401,11 @@ def test_tp2_alibi_slopes_follow_each_rank_s_heads():
 
 
 @pytest.mark.timeout(300)
-def test_tp2_prompt_logprobs_beam_search_and_guided_decoding_match_single_process():
+def test_tp2_prompt_logprobs_beam_search_guided_decoding_and_embeddings_match_single_process():
     """Host-side request features on a TP2 engine: prompt scoring (the executor's explicit
     forward), beam search (forked beams' block tables and copy-on-write copies reach the
-    workers through the plans) and guided decoding (rank 0's sampler masks the logits)
-    give what the single-process engine gives."""
+    workers through the plans), guided decoding (rank 0's sampler masks the logits) and
+    embeddings give what the single-process engine gives."""
     from rusteeze_b200.core.sampling_params import GuidedDecodingParams
     from rusteeze_b200.parallel.launcher import TPEngineLauncher
     rng = np.random.default_rng(3)
@@ -423,12 +423,18 @@ def test_tp2_prompt_logprobs_beam_search_and_guided_decoding_match_single_proces
                     done[o.request_id] = o
         return [done[i] for i in ids]
 
-    ref = run(LLMEngine(_cfg(1), model_config=MC))
+    single = LLMEngine(_cfg(1), model_config=MC)
+    ref = run(single)
+    ref_emb = single.embed(prompts, "last") + single.embed(prompts, "mean")
     launcher = TPEngineLauncher(_cfg(2), model_config=MC, device_type="cpu")
     try:
         got = run(launcher.engine())
+        # embeddings: rank 0 returns hidden rows and still joins the LM head's all-gather
+        emb = launcher.engine().embed(prompts, "last") + launcher.engine().embed(prompts, "mean")
     finally:
         launcher.shutdown()
+    for a, b in zip(emb, ref_emb):
+        assert np.abs(a - b).max() < 1e-4
     for a, b in zip(got, ref):
         assert [c.token_ids for c in a.outputs] == [c.token_ids for c in b.outputs]
         if b.prompt_logprobs is not None:
