@@ -13,7 +13,9 @@ engine advances the guide with every token the sequence takes.
 
 End of output: where the DFA accepts, the EOS ids are allowed too; where it accepts and
 cannot continue, only EOS is.  A request with `ignore_eos` ends ("stop") when its guide
-can no longer continue.
+can no longer continue.  Where no token of the vocabulary can continue a partial match
+(the pattern needs a character no whole-character token spells), EOS is allowed and the
+request ends ("stop") rather than leave the constraint.
 
 Tokens whose text is empty (special tokens) or not whole characters (a byte-level
 tokenizer's partial UTF-8 bytes) are never allowed, so guided outputs are spelled with
@@ -183,12 +185,20 @@ class Guide:
                 _masks[key] = m
                 while len(_masks) > MASK_CACHE_STATES:
                     _masks.popitem(last=False)
-        if allow_eos and self.fsm.accepting(self.state):
+        # EOS where the output is a match, and where no token can continue it (a dead end
+        # the vocabulary cannot spell: the request then ends instead of leaving the constraint)
+        if allow_eos and (self.fsm.accepting(self.state) or not m.any()):
             m = m.copy()
             for e in self.eos_ids:
                 if 0 <= e < m.shape[0]:
                     m[e] = True
         return m
+
+    def stuck(self) -> bool:
+        """No token can continue the output and it is not a complete match."""
+        if self.state < 0:
+            return True
+        return not self.fsm.accepting(self.state) and not self.mask(allow_eos=False).any()
 
     def advance(self, tok: int) -> None:
         if tok in self.eos_ids:

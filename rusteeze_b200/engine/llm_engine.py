@@ -646,9 +646,9 @@ class LLMEngine:
         if reason is None and ((p.max_tokens is not None and n >= p.max_tokens)
                                or len(s.token_ids) >= self.max_model_len):
             reason = "length"
-        if (reason is None and s.guide is not None and (p.ignore_eos or not self.eos_ids)
-                and (s.guide.complete or s.guide.state < 0)):
-            reason = "stop"               # the constrained output is complete and no EOS will come
+        if reason is None and s.guide is not None and (
+                ((p.ignore_eos or not self.eos_ids) and s.guide.complete) or s.guide.stuck()):
+            reason = "stop"               # complete with no EOS to come, or no token can continue it
         if reason is not None:
             s.finish_reason = reason
             s.status = RequestStatus.FINISHED_STOPPED if reason == "stop" else RequestStatus.FINISHED_LENGTH

@@ -182,6 +182,14 @@ def test_ignore_eos_stops_when_the_constraint_is_complete(eng):
     assert all(o.text in ("alpha", "beta") and o.finish_reason == "stop" for o in outs)
 
 
+def test_a_pattern_the_vocabulary_cannot_spell_ends_the_request(eng):
+    """The byte tokenizer has no whole-character token for "é" (two UTF-8 bytes): after
+    "ab" nothing can continue, so the request ends there instead of leaving the pattern."""
+    for ignore_eos in (False, True):
+        o = _gen(eng, GuidedDecodingParams(regex="abé+"), temp=0.0, ignore_eos=ignore_eos)[0]
+        assert o.text == "ab" and o.finish_reason == "stop"
+
+
 def test_invalid_constraints_are_refused(eng):
     for g in (GuidedDecodingParams(), GuidedDecodingParams(regex="a", choice=["a"]),
               GuidedDecodingParams(grammar="root ::= 'a'"), GuidedDecodingParams(regex="(a")):
