@@ -262,15 +262,22 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                 final = None
                 agen = async_engine.generate(text, sp, f"{rid}-{pi}", ids, priority=req.priority)
                 completed = False
+                sent, offs = {}, {}                # tokens and text characters already sent, per output
                 try:
                     async for out in agen:
                         final = out
                         for c, delta in zip(out.outputs, out.delta_text):
-                            if delta or c.finish_reason:
+                            lp = None
+                            if req.logprobs is not None and len(c.token_ids) > sent.get(c.index, 0):
+                                lp = _cmpl_logprobs(eng.tokenizer, _TokSlice(c, sent.get(c.index, 0)),
+                                                    offset=offs.get(c.index, 0))
+                                sent[c.index] = len(c.token_ids)
+                                offs[c.index] = lp.text_offset[-1] + len(lp.tokens[-1])
+                            if delta or c.finish_reason or lp is not None:
                                 chunk = S.CompletionResponse(
                                     id=rid, model=model_name, usage=S.Usage(),
                                     choices=[S.CompletionChoice(index=pi * sp.n + c.index, text=delta,
-                                                                finish_reason=c.finish_reason)])
+                                                                finish_reason=c.finish_reason, logprobs=lp)])
                                 yield "data: " + chunk.model_dump_json(exclude={"usage"}, exclude_none=True) + "\n\n"
                     completed = True
                 finally:
@@ -351,6 +358,7 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                 # whether it is a call (sent as one tool_calls delta) or text
                 held: dict = {}
                 passthrough: dict = {}
+                sent: dict = {}                   # tokens whose logprobs were sent, per output
                 async for out in agen:
                     final = out
                     for c, delta in zip(out.outputs, out.delta_text):
@@ -363,9 +371,13 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
                                 delta, held[i] = held[i], ""
                             else:
                                 delta = ""
-                        if delta:
+                        lp = None
+                        if req.logprobs and not held.get(i) and len(c.token_ids) > sent.get(i, 0):
+                            lp = _chat_logprobs(eng.tokenizer, _TokSlice(c, sent.get(i, 0)))
+                            sent[i] = len(c.token_ids)
+                        if delta or lp is not None:
                             yield _sse(S.ChatCompletionChunk(id=rid, model=model_name, choices=[
-                                S.ChatChunkChoice(index=i, delta=S.ChatDelta(content=delta))]))
+                                S.ChatChunkChoice(index=i, delta=S.ChatDelta(content=delta), logprobs=lp)]))
                         if c.finish_reason:
                             reason = c.finish_reason
                             if held.get(i):
@@ -481,11 +493,21 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
     return app
 
 
-def _cmpl_logprobs(tok, c, prompt=None) -> S.CompletionLogProbs:
+class _TokSlice:
+    """The tokens (and their logprob tables) of one output not yet sent on a stream."""
+    __slots__ = ("token_ids", "logprobs")
+
+    def __init__(self, c, start: int):
+        self.token_ids = c.token_ids[start:]
+        self.logprobs = (c.logprobs or [])[start:]
+
+
+def _cmpl_logprobs(tok, c, prompt=None, offset: int = 0) -> S.CompletionLogProbs:
     """OpenAI completion logprobs; with `echo`, the prompt's tokens come first (the first
-    one without a logprob, as it has no context)."""
+    one without a logprob, as it has no context).  `offset`: text offset of the first token
+    (streams send later tokens in later chunks)."""
     lp = S.CompletionLogProbs()
-    off = 0
+    off = offset
     if prompt is not None:
         ids, plp = prompt
         for tid, d in zip(ids, plp):
@@ -510,8 +532,9 @@ def _chat_logprobs(tok, c) -> S.ChatLogProbs:
     for tid, d in zip(c.token_ids, c.logprobs or []):
         s = tok.decode([tid])
         content.append(S.TokenLogProb(token=s, logprob=d.get(tid, 0.0), bytes=list(s.encode()),
-                                      top_logprobs=[S.TopLogProb(token=tok.decode([k]), logprob=v)
-                                                    for k, v in d.items() if k != tid]))
+                                      top_logprobs=[S.TopLogProb(token=t, logprob=v, bytes=list(t.encode()))
+                                                    for t, v in ((tok.decode([k]), v) for k, v in d.items()
+                                                                 if k != tid)]))
     return S.ChatLogProbs(content=content)
 
 

@@ -187,6 +187,36 @@ def test_tokens_per_minute_limit_through_the_api(engine):
         ae.shutdown()
 
 
+def test_streamed_logprobs_equal_the_non_streamed_ones(engine):
+    """Each stream chunk carries the logprobs of the tokens it adds; joined, they are the
+    non-streamed response's (completions with absolute text offsets, and chat)."""
+    c, ae = _client(engine)
+    try:
+        body = {"prompt": [7, 8, 9, 10], "max_tokens": 6, "temperature": 0, "ignore_eos": True, "logprobs": 2}
+        full = c.post("/v1/completions", json=body).json()["choices"][0]["logprobs"]
+        r = c.post("/v1/completions", json=dict(body, stream=True))
+        joined = {"tokens": [], "token_logprobs": [], "top_logprobs": [], "text_offset": []}
+        for ln in r.text.splitlines():
+            if ln.startswith("data: {"):
+                for ch in json.loads(ln[6:])["choices"]:
+                    for k in joined:
+                        joined[k] += (ch.get("logprobs") or {}).get(k, [])
+        assert joined == full
+        msgs = [{"role": "user", "content": "hi"}]
+        chat = {"messages": msgs, "max_tokens": 5, "temperature": 0, "ignore_eos": True, "logprobs": True,
+                "top_logprobs": 2}
+        full = c.post("/v1/chat/completions", json=chat).json()["choices"][0]["logprobs"]["content"]
+        r = c.post("/v1/chat/completions", json=dict(chat, stream=True))
+        got = []
+        for ln in r.text.splitlines():
+            if ln.startswith("data: {"):
+                for ch in json.loads(ln[6:])["choices"]:
+                    got += (ch.get("logprobs") or {}).get("content") or []
+        assert got == full and len(got) == 5
+    finally:
+        ae.shutdown()
+
+
 def test_ready_reports_unhealthy_after_engine_failure():
     cfg = _cfg()
     eng = LLMEngine(cfg)
