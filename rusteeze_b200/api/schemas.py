@@ -106,6 +106,23 @@ class EmbeddingRequest(BaseModel):
     normalize: bool = True
 
 
+class TokenizeRequest(BaseModel):
+    """`/tokenize`: a prompt, or chat messages rendered with the server's chat template."""
+    model_config = ConfigDict(extra="ignore")
+    model: str = ""
+    prompt: Optional[str] = None
+    messages: Optional[List[ChatMessage]] = None
+    add_special_tokens: bool = True
+    add_generation_prompt: bool = True
+
+
+class DetokenizeRequest(BaseModel):
+    model_config = ConfigDict(extra="ignore")
+    model: str = ""
+    tokens: List[int]
+    skip_special_tokens: bool = False
+
+
 class EmbeddingData(BaseModel):
     object: Literal["embedding"] = "embedding"
     embedding: Union[List[float], str]

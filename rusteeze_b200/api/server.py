@@ -447,6 +447,30 @@ def create_app(async_engine, config=None, metrics: Optional[EngineMetrics] = Non
         return S.EmbeddingResponse(data=data, model=model_name,
                                    usage=S.EmbeddingUsage(prompt_tokens=n, total_tokens=n))
 
+    # ------------------------------------------------------------------ tokenizer
+    @app.post("/tokenize")
+    async def tokenize(req: S.TokenizeRequest):
+        """Token ids of a prompt (or of chat messages as the chat endpoint renders them),
+        with the model's context length, so a client can count before it sends."""
+        _check_model(req.model)
+        if (req.prompt is None) == (req.messages is None):
+            raise InvalidRequestError("give exactly one of prompt or messages")
+        if req.messages is not None:
+            text = template.apply([m.model_dump() for m in req.messages],
+                                  add_generation_prompt=req.add_generation_prompt)
+            ids = eng.tokenizer.encode(text, add_special_tokens=False) or eng.tokenizer.encode(text)
+        else:
+            ids = eng.tokenizer.encode(req.prompt, add_special_tokens=req.add_special_tokens)
+        return {"tokens": ids, "count": len(ids), "max_model_len": getattr(eng, "max_model_len", None)}
+
+    @app.post("/detokenize")
+    async def detokenize(req: S.DetokenizeRequest):
+        _check_model(req.model)
+        V = eng.model_config.vocab_size
+        if any(not 0 <= t < V for t in req.tokens):
+            raise InvalidRequestError(f"token ids must be in [0, {V})", param="tokens")
+        return {"prompt": eng.tokenizer.decode(req.tokens, req.skip_special_tokens)}
+
     # ------------------------------------------------------------------ misc
     @app.get("/v1/models")
     async def models():

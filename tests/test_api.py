@@ -217,6 +217,27 @@ def test_streamed_logprobs_equal_the_non_streamed_ones(engine):
         ae.shutdown()
 
 
+def test_tokenize_and_detokenize(engine):
+    c, ae = _client(engine)
+    try:
+        r = c.post("/tokenize", json={"prompt": "hello"})
+        d = r.json()
+        assert d["tokens"] == engine.tokenizer.encode("hello") and d["count"] == len(d["tokens"])
+        assert d["max_model_len"] == engine.max_model_len
+        r = c.post("/tokenize", json={"prompt": "hello", "add_special_tokens": False})
+        assert r.json()["tokens"] == engine.tokenizer.encode("hello", add_special_tokens=False)
+        msgs = [{"role": "user", "content": "hi"}]
+        n_chat = c.post("/tokenize", json={"messages": msgs}).json()["count"]
+        done = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 1}).json()
+        assert n_chat == done["usage"]["prompt_tokens"]
+        r = c.post("/detokenize", json={"tokens": engine.tokenizer.encode("hello", add_special_tokens=False)})
+        assert r.json()["prompt"] == "hello"
+        assert c.post("/detokenize", json={"tokens": [10 ** 9]}).status_code == 400
+        assert c.post("/tokenize", json={}).status_code == 400
+    finally:
+        ae.shutdown()
+
+
 def test_ready_reports_unhealthy_after_engine_failure():
     cfg = _cfg()
     eng = LLMEngine(cfg)
