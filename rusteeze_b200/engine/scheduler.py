@@ -298,8 +298,12 @@ class Scheduler:
                 toks = seq.tokens_np()
                 cached = bm.cached_prefix_len(toks) if not bm.has_seq(seq.seq_id) else seq.num_computed
                 remaining = seq.total_len - cached
-                if not cfg.enable_chunked_prefill and remaining > token_budget:
-                    break
+                if (not cfg.enable_chunked_prefill and remaining > token_budget
+                        and remaining <= cfg.max_num_batched_tokens):
+                    break                   # waits for a step with room for all of it
+                # (longer than any step's budget: without chunks it could never run, so it
+                # is chunked even with chunked prefill off -- a long prompt, or a sequence
+                # that grew past the budget and was preempted by recompute)
                 n = min(remaining, token_budget)
                 need = bm.blocks_needed_for_prompt(toks, cached + n)
                 if need + self._watermark_blocks > bm.num_free_gpu_blocks():

@@ -66,6 +66,16 @@ def test_without_chunked_prefill(oracle):
     assert run(eng, prompts) == ref
 
 
+@pytest.mark.timeout(120)
+def test_without_chunked_prefill_a_prompt_longer_than_the_step_budget_still_runs(oracle):
+    """Chunked prefill off, a 64-token step budget: prompts (and recompute-preempted
+    sequences) longer than any step could hold are chunked anyway instead of waiting forever."""
+    prompts, ref = oracle
+    eng = make_engine(chunked=False, max_tokens=64, num_blocks=24)
+    assert run(eng, prompts) == ref
+    assert eng.scheduler.num_preemptions > 0
+
+
 def test_recompute_preemption_under_memory_pressure(oracle):
     prompts, ref = oracle
     eng = make_engine(num_blocks=24)
