@@ -37,7 +37,8 @@ def _model_args(p: argparse.ArgumentParser, required: bool = True) -> None:
     p.add_argument("--tensor-parallel-size", type=int, default=None)
     p.add_argument("--data-parallel-size", type=int, default=None,
                    help="serve: D engine replicas (one GPU each) behind a request router")
-    p.add_argument("--router-policy", default=None, choices=["least_loaded", "round_robin", "random"])
+    p.add_argument("--router-policy", default=None,
+                   choices=["least_loaded", "round_robin", "random", "prefix_affinity"])
     p.add_argument("--max-model-len", type=int, default=None)
     p.add_argument("--gpu-memory-utilization", type=float, default=None)
     p.add_argument("--quantization", default=None, choices=[None, "fp8_block", "fp8"])

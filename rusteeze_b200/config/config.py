@@ -95,7 +95,7 @@ class ServerSection:
     tls: Optional[TlsConfig] = None
     rate_limit: Optional[RateLimitConfig] = None
     metrics_port: Optional[int] = None
-    router_policy: str = "least_loaded"    # data-parallel replicas: least_loaded | round_robin | random
+    router_policy: str = "least_loaded"    # data-parallel replicas: least_loaded | round_robin | random | prefix_affinity
     # a chat request's own Jinja `chat_template` runs only when this is set: the sandbox
     # stops code execution, not templates built to loop or allocate without bound
     trust_request_chat_template: bool = False

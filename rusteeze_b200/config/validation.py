@@ -34,8 +34,9 @@ def collect_errors(cfg) -> List[str]:
         e.append("model.data_parallel_size > 1 serves tensor_parallel_size 1 replicas (one GPU each)")
     if m.data_parallel_size > 1 and m.device.startswith("cuda:"):
         e.append("model.device must be auto|cuda|cpu with data_parallel_size > 1 (replica i runs on cuda:i)")
-    if s.router_policy not in ("least_loaded", "round_robin", "random"):
-        e.append(f"server.router_policy must be least_loaded|round_robin|random, got {s.router_policy!r}")
+    if s.router_policy not in ("least_loaded", "round_robin", "random", "prefix_affinity"):
+        e.append("server.router_policy must be least_loaded|round_robin|random|prefix_affinity, "
+                 f"got {s.router_policy!r}")
     if m.pipeline_parallel_size != 1:
         e.append("model.pipeline_parallel_size > 1 is not supported: one NVSwitch domain serves these "
                  "models with tensor/expert parallelism")

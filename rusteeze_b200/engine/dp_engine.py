@@ -30,7 +30,7 @@ from typing import AsyncIterator, Callable, Dict, List, Optional
 from rusteeze_b200.core.errors import ServiceUnavailableError
 from rusteeze_b200.core.outputs import RequestOutput
 from rusteeze_b200.core.sampling_params import SamplingParams
-from rusteeze_b200.engine.router import Policy, Replica, ReplicaRouter
+from rusteeze_b200.engine.router import Policy, Replica, ReplicaRouter, affinity_key
 
 
 def replica_configs(config) -> List:
@@ -186,8 +186,9 @@ class ReplicatedAsyncEngine:
                        prompt_token_ids: Optional[List[int]] = None,
                        priority: int = 0) -> AsyncIterator[RequestOutput]:
         self.router.probe()
+        key = (affinity_key(prompt_token_ids, prompt) if self.router.policy == Policy.PREFIX_AFFINITY else None)
         try:
-            rep = self.router.select()
+            rep = self.router.select(key)
         except RuntimeError as e:
             raise ServiceUnavailableError(f"no ready replica: {e}") from None
         self._owner[request_id] = rep

@@ -7,10 +7,18 @@ reference calls.  Here a `ReplicaRouter` fronts several engine replicas
 (8 x TP1 on one box, one GPU each) for the data-parallel serving front end
 (`engine.dp_engine.ReplicatedAsyncEngine`); health is driven by a prober
 callback (the replica engine's readiness).
+
+`prefix_affinity` (not in the reference) sends requests whose prompts start alike to the
+same replica, so its prefix cache serves the shared part: the key is a hash of the
+prompt's first `AFFINITY_TOKENS` tokens, and the replica is chosen by rendezvous hashing
+(the live replica with the highest hash of (key, name)), so a replica that goes down or
+comes back moves only its own keys.  A load guard sends the request to the least-loaded
+replica instead when the chosen one has `AFFINITY_SLACK` more requests in flight.
 """
 from __future__ import annotations
 
 import enum
+import hashlib
 import math
 import random
 import threading
@@ -22,6 +30,25 @@ class Policy(str, enum.Enum):
     LEAST_LOADED = "least_loaded"
     ROUND_ROBIN = "round_robin"
     RANDOM = "random"
+    PREFIX_AFFINITY = "prefix_affinity"
+
+
+AFFINITY_TOKENS = 256
+AFFINITY_SLACK = 8
+
+
+def affinity_key(prompt_token_ids=None, prompt: str = None) -> int:
+    """A stable key of a prompt's opening: its first AFFINITY_TOKENS token ids, or (text
+    prompts, before tokenisation) its first 4 * AFFINITY_TOKENS characters."""
+    if prompt_token_ids is not None:
+        data = b",".join(str(int(t)).encode() for t in list(prompt_token_ids)[:AFFINITY_TOKENS])
+    else:
+        data = (prompt or "")[:4 * AFFINITY_TOKENS].encode("utf-8", "surrogatepass")
+    return int.from_bytes(hashlib.blake2b(data, digest_size=8).digest(), "little")
+
+
+def _rendezvous(key: int, name: str) -> int:
+    return int.from_bytes(hashlib.blake2b(f"{key}:{name}".encode(), digest_size=8).digest(), "little")
 
 
 class LatencyHistogram:
@@ -88,12 +115,18 @@ class ReplicaRouter:
                 return
         raise KeyError(f"no replica named {name!r}")
 
-    def select(self) -> Replica:
+    def select(self, key: Optional[int] = None) -> Replica:
+        """Picks a live replica; `key` (an `affinity_key`) is used by `prefix_affinity`."""
         with self._lock:
             live = [r for r in self.replicas if r.healthy]
             if not live:
                 raise RuntimeError("no healthy replica")
-            if self.policy == Policy.ROUND_ROBIN:
+            if self.policy == Policy.PREFIX_AFFINITY and key is not None:
+                r = max(live, key=lambda x: _rendezvous(key, x.name))
+                least = min(live, key=lambda x: (x.in_flight, x.served))
+                if r.in_flight - least.in_flight >= AFFINITY_SLACK:
+                    r = least
+            elif self.policy == Policy.ROUND_ROBIN:
                 r = live[self._rr % len(live)]
                 self._rr += 1
             elif self.policy == Policy.RANDOM:

@@ -76,6 +76,41 @@ def test_least_loaded_balances_a_steady_stream():
     assert max(served) - min(served) <= 1
 
 
+def test_prefix_affinity_is_sticky_balanced_and_moves_only_a_dead_replica_s_keys():
+    from rusteeze_b200.engine.router import AFFINITY_SLACK, affinity_key
+    reps = [Replica(f"dp{i}", None) for i in range(4)]
+    r = ReplicaRouter(reps, Policy.PREFIX_AFFINITY)
+    keys = [affinity_key(list(range(i, i + 300))) for i in range(400)]
+    first = {}
+    for k in keys:
+        x = r.select(k)
+        r.release(x)
+        first[k] = x.name
+        y = r.select(k)                           # the same prompt opening: the same replica
+        r.release(y)
+        assert y.name == x.name
+    spread = collections.Counter(first.values())
+    assert len(spread) == 4 and min(spread.values()) > 400 / 4 * 0.6, spread
+    # only tokens past AFFINITY_TOKENS differ: same key
+    assert affinity_key(list(range(300)) + [1]) == affinity_key(list(range(300)) + [2])
+    assert affinity_key(prompt="a system prompt") == affinity_key(prompt="a system prompt")
+    r.set_health("dp2", False)
+    for k in keys:
+        x = r.select(k)
+        r.release(x)
+        if first[k] != "dp2":
+            assert x.name == first[k]             # keys of live replicas stay put
+        else:
+            assert x.name != "dp2"
+    # load guard: a hot key spills to the least-loaded replica
+    r.set_health("dp2", True)
+    k = keys[0]
+    held = [r.select(k) for _ in range(AFFINITY_SLACK)]
+    assert all(h.name == first[k] for h in held)
+    spill = r.select(k)
+    assert spill.name != first[k]
+
+
 def test_unknown_replica_name_is_an_error():
     rt = ReplicaRouter([Replica("a", None)])
     with pytest.raises(KeyError):
@@ -201,3 +236,30 @@ def test_a_failed_replica_is_routed_around(dp_app):
     front.replicas[0].healthy = False
     assert c.post("/v1/completions", json={"prompt": "x", "max_tokens": 2}).status_code == 503
     assert c.get("/health/ready").status_code == 503
+
+
+def test_dp_prefix_affinity_keeps_a_shared_prefix_on_one_replica():
+    """Two CPU replicas with prefix caching: requests that share a long opening all reach
+    the same replica, whose prefix cache serves the shared blocks."""
+    from rusteeze_b200.core.sampling_params import SamplingParams
+    from rusteeze_b200.engine.dp_engine import ReplicatedAsyncEngine
+    cfg = _cfg()
+    cfg.engine.enable_prefix_caching = True
+    cfg.server.router_policy = "prefix_affinity"
+    front = ReplicatedAsyncEngine.from_config(cfg).start()
+    system = list(range(100, 400))                       # 300 shared tokens
+    sp = SamplingParams(temperature=0.0, max_tokens=2, ignore_eos=True)
+
+    async def run():
+        for i in range(6):
+            async for _ in front.generate(None, sp, f"r{i}", system + [7, i]):
+                pass
+
+    try:
+        asyncio.run(run())
+        served = sorted(r["served"] for r in front.stats()["replicas"])
+        assert served == [0, 6], served
+        hits = [ae.engine.bm.stats()["prefix_block_hits"] for ae in front.replicas]
+        assert max(hits) >= 5 * (300 // 16)
+    finally:
+        front.shutdown()
