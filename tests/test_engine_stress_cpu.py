@@ -1,5 +1,6 @@
 """Randomised engine stress on CPU (seeded): request mixes with varied prompt and output
-lengths, sampling modes, n / best_of, random aborts, tight KV caches, recompute and
+lengths, sampling modes, n / best_of, beam search, guided decoding, prompt scoring, random
+(early) aborts, tight KV caches, recompute and
 swap preemption, prefix caching and chunked prefill on and off, the synchronous and the
 pipelined schedule.  Every request must end
 (finished or aborted) within a step cap -- no livelock -- every finished request must be
@@ -39,8 +40,17 @@ def _engine(rng, mode, prefix, chunked, spec=None):
 
 
 def _params(rng):
-    kind = rng.integers(0, 4)
+    kind = rng.integers(0, 7)
     mx = int(rng.integers(1, 40))
+    if kind == 4:       # beam search (width 2: every engine here runs at least 2 sequences)
+        return SamplingParams(n=int(rng.integers(1, 3)), best_of=2, use_beam_search=True, temperature=0.0,
+                          max_tokens=mx, ignore_eos=bool(rng.random() < 0.5))
+    if kind == 5:       # guided decoding
+        from rusteeze_b200.core.sampling_params import GuidedDecodingParams
+        return SamplingParams(temperature=0.9, max_tokens=mx, seed=int(rng.integers(1 << 30)),
+                              guided_decoding=GuidedDecodingParams(regex=r"[a-f]{1,30}( [0-9]+)?"))
+    if kind == 6:       # prompt scoring
+        return SamplingParams(temperature=0.0, max_tokens=mx, ignore_eos=True, prompt_logprobs=1)
     if kind == 0:
         return SamplingParams(temperature=0.0, max_tokens=mx, ignore_eos=True)
     if kind == 1:
@@ -70,7 +80,7 @@ def test_random_request_mixes_always_drain(seed):
     live = set()
     n_req = 24
     submitted = 0
-    for _ in range(3000):
+    for step in range(3000):
         while submitted < n_req and rng.random() < 0.5:         # a few arrivals per step
             L = int(rng.integers(1, 200))
             toks = (shared[: int(rng.integers(0, 48))] if rng.random() < 0.5 else []) + \
@@ -79,7 +89,9 @@ def test_random_request_mixes_always_drain(seed):
             eng.add_request(rid, None, _params(rng), toks[:480])
             live.add(rid)
             submitted += 1
-        if live and rng.random() < 0.03:                        # random aborts
+        # random aborts, early only: an abort must not rescue a request that is stuck (a
+        # livelock then shows as a request that never drains)
+        if live and step < 300 and rng.random() < 0.03:
             rid = sorted(live)[int(rng.integers(0, len(live)))]
             eng.abort_request(rid)
             live.discard(rid)
