@@ -200,15 +200,17 @@ _SPEC_SEEDS = sorted(set(range(int(os.environ.get("RZ_STRESS_SEEDS", "4")))) | {
 @pytest.mark.parametrize("seed", _SPEC_SEEDS)
 def test_speculative_decoding_under_random_mixes(seed):
     """Speculative decoding (self-draft on even seeds, a separate 1-layer draft on odd
-    ones) under tight caches, both preemption modes, random aborts and mixed sampling:
-    every request ends and is reported, invariants hold, and greedy requests emit exactly
-    the tokens of a non-speculative engine."""
+    ones, prompt lookup on every third seed with self-repeating prompts) under tight caches,
+    both preemption modes, random aborts and mixed sampling: every request ends and is
+    reported, invariants hold, and greedy requests emit exactly the tokens of a
+    non-speculative engine."""
     import dataclasses
     from rusteeze_b200.config.config import SpeculativeSection
     rng = np.random.default_rng(3000 + seed)
     mode = ["recompute", "swap"][(seed >> 1) % 2]
     draft_dir = None
-    if seed % 2:
+    ngram = seed % 3 == 2
+    if seed % 2 and not ngram:
         import tempfile
         from rusteeze_b200.models.loader import build_model, save_hf_checkpoint
         draft_dir = tempfile.mkdtemp(prefix="rz_draft_")
@@ -220,13 +222,17 @@ def test_speculative_decoding_under_random_mixes(seed):
         p = (SamplingParams(temperature=0.0, max_tokens=int(rng.integers(1, 30)), ignore_eos=True) if greedy else
              SamplingParams(temperature=0.9, top_p=0.95, max_tokens=int(rng.integers(1, 30)),
                             seed=int(rng.integers(1 << 30))))
-        reqs.append((f"s{i}", rng.integers(0, 300, int(rng.integers(1, 90))).tolist(), p, greedy))
+        toks = rng.integers(0, 300, int(rng.integers(1, 90))).tolist()
+        if ngram:
+            toks = (toks[:int(rng.integers(2, 12))] * 12)[:len(toks) + 20]
+        reqs.append((f"s{i}", toks, p, greedy))
     aborts = {int(x) for x in rng.integers(0, 14, 2)}
 
     def run(spec):
         r2 = np.random.default_rng(4000 + seed)
         eng = _engine(r2, mode, prefix=bool(seed & 4), chunked=True,
-                      spec=SpeculativeSection(draft_model=draft_dir, num_speculative_tokens=3) if spec else None)
+                      spec=(SpeculativeSection(method="ngram", num_speculative_tokens=3) if ngram else
+                            SpeculativeSection(draft_model=draft_dir, num_speculative_tokens=3)) if spec else None)
         done = {}
         for i, (rid, toks, p, _) in enumerate(reqs):
             eng.add_request(rid, None, p, toks)
