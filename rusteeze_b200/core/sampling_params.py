@@ -132,8 +132,8 @@ class SamplingParams:
             bad(f"mirostat_tau must be >= 0, got {self.mirostat_tau}")
         if not 0.0 <= self.top_p <= 1.0:
             bad(f"top_p must be in [0, 1], got {self.top_p}")
-        if self.top_k == 0 or self.top_k < -1:
-            bad(f"top_k must be -1 (disabled) or >= 1, got {self.top_k}")
+        if self.top_k == 0 or self.top_k < -1 or self.top_k > 2 ** 31 - 1:
+            bad(f"top_k must be -1 (disabled) or in [1, 2**31 - 1], got {self.top_k}")
         if not 0.0 <= self.min_p <= 1.0:
             bad(f"min_p must be in [0, 1], got {self.min_p}")
         if not 0.0 <= self.typical_p <= 1.0:
@@ -142,6 +142,8 @@ class SamplingParams:
             bad(f"frequency_penalty must be in [-2, 2], got {self.frequency_penalty}")
         if not -2.0 <= self.presence_penalty <= 2.0:
             bad(f"presence_penalty must be in [-2, 2], got {self.presence_penalty}")
+        if not -100.0 <= self.length_penalty <= 100.0:
+            bad(f"length_penalty must be in [-100, 100], got {self.length_penalty}")
         if self.repetition_penalty <= 0.0:
             bad(f"repetition_penalty must be > 0, got {self.repetition_penalty}")
         if self.n < 1:

@@ -33,6 +33,7 @@ stalling it.
 from __future__ import annotations
 
 import copy
+import math
 from typing import Dict, List, Optional, Tuple
 
 from rusteeze_b200.core.sampling_params import EarlyStoppingMode, SamplingParams
@@ -43,7 +44,14 @@ _MASKED = -1e20
 
 
 def beam_score(cumulative_logprob: float, num_output_tokens: int, length_penalty: float) -> float:
-    return cumulative_logprob / (max(1, num_output_tokens) ** length_penalty)
+    """cumulative logprob / L ** length_penalty, with L ** length_penalty taken in log space
+    so that no penalty overflows (an infinite divisor gives 0, a vanishing one -inf)."""
+    e = length_penalty * math.log(max(1, num_output_tokens))
+    if e > 700.0:
+        return 0.0
+    if e < -700.0:
+        return -math.inf if cumulative_logprob < 0 else 0.0
+    return cumulative_logprob / math.exp(e)
 
 
 class BeamState:

@@ -105,9 +105,13 @@ class _Compiler:
         if "const" in s:
             return _lit(s["const"])
         if "enum" in s:
+            if not isinstance(s["enum"], list) or not s["enum"]:
+                raise SchemaError("enum must be a non-empty list")
             return _alt([_lit(v) for v in s["enum"]])
         for key in ("anyOf", "oneOf"):
             if key in s:
+                if not isinstance(s[key], list) or not s[key]:
+                    raise SchemaError(f"{key} must be a non-empty list")
                 return _alt([self.value(x) for x in s[key]])
         t = s.get("type")
         if isinstance(t, list):

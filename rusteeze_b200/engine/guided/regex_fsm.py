@@ -257,6 +257,9 @@ class _NFA:
             self.edges[s].append((self.set_id(node[1]), e))
             return s, e
         if kind == "cat":
+            if not node[1]:                    # the empty pattern: only the empty string
+                s = self.new()
+                return s, s
             s, e = self.build(node[1][0])
             for sub in node[1][1:]:
                 s2, e2 = self.build(sub)

@@ -65,7 +65,30 @@ def _body(rng, chat, V):
     if rng.random() < 0.1:
         b["model"] = rng.choice(["tiny-llama", "other", 7])
     if rng.random() < 0.1:
-        b["response_format"] = rng.choice([{"type": "json_object"}, {"type": "nope"}, "x"])
+        b["response_format"] = rng.choice([
+            {"type": "json_object"}, {"type": "nope"}, "x", {"type": "json_schema"},
+            {"type": "json_schema", "json_schema": {"schema": {"type": "integer"}}},
+            {"type": "json_schema", "json_schema": {"schema": 5}}, {"type": "json_schema", "json_schema": []}])
+    if rng.random() < 0.1:
+        b["guided_regex"] = rng.choice(["[a-z]{2}", "(", "a{99999}", "(?=x)", 5, None, ""])
+    if rng.random() < 0.1:
+        b["guided_choice"] = rng.choice([["a", "b"], [], "x", [1], [""]])
+    if rng.random() < 0.1:
+        b["guided_json"] = rng.choice([{"type": "object"}, {"type": "weird"}, "not json", '{"type": "boolean"}',
+                                       {"$ref": "#/nowhere"}, {"enum": []}, 3])
+    if rng.random() < 0.1:
+        b["use_beam_search"] = rng.choice([True, False, "x"])
+        b["length_penalty"] = rng.choice([1.0, -2.0, 0, "x", 1e308])
+        b["early_stopping"] = rng.choice([True, False, "never", "sometimes", 3])
+    if chat and rng.random() < 0.15:
+        b["tools"] = rng.choice([
+            [{"type": "function", "function": {"name": "f", "parameters": {"type": "object",
+                                                                          "properties": {"a": {"type": "integer"}}}}}],
+            [{"type": "function"}], "x", [5], [], [{"type": "function", "function": {"name": "f", "parameters": 7}}]])
+        b["tool_choice"] = rng.choice(["auto", "none", "required", {"type": "function", "function": {"name": "f"}},
+                                       {"type": "x"}, 7, None])
+    if not chat and rng.random() < 0.1:
+        b["echo"] = rng.choice([True, False])
     b.setdefault("max_tokens", rng.choice([1, 3, 5]))
     return b
 
@@ -109,6 +132,50 @@ def test_random_bodies_never_get_a_server_error(client, seed):
     assert codes.get(200, 0) > 0 and sum(v for k, v in codes.items() if k >= 400) > 0, codes
     code, text = _post(c, "/v1/completions", {"prompt": "fine", "max_tokens": 2, "ignore_eos": True})
     assert code == 200 and json.loads(text)["usage"]["completion_tokens"] == 2
+
+
+@pytest.mark.parametrize("body", [
+    {"prompt": [1, 2, 3], "top_k": 2 ** 63, "temperature": 0.5},                 # overflowed the sampler
+    {"prompt": [1, 2, 3], "use_beam_search": True, "best_of": 2, "length_penalty": 1e308},
+    {"prompt": [1, 2, 3], "guided_json": {"enum": []}},                          # crashed the NFA builder
+    {"prompt": [1, 2, 3], "guided_regex": ""},
+])
+def test_inputs_that_once_broke_the_engine_are_refused_or_served(client, body):
+    c, ae = client
+    code, text = _post(c, "/v1/completions", dict(body, max_tokens=3))
+    assert code < 500, text[:300]
+    assert ae.is_ready, ae.last_error
+    code, _ = _post(c, "/v1/completions", {"prompt": "fine", "max_tokens": 2})
+    assert code == 200
+
+
+@pytest.mark.parametrize("seed", range(2))
+def test_random_embedding_and_tokenizer_bodies_never_get_a_server_error(client, seed):
+    c, ae = client
+    V = ae.engine.model_config.vocab_size
+    rng = random.Random(100 + seed)
+    for _ in range(40):
+        url = rng.choice(["/v1/embeddings", "/tokenize", "/detokenize"])
+        body = {}
+        if url == "/v1/embeddings":
+            if rng.random() < 0.9:
+                body["input"] = rng.choice(["abc", "", ["a", "bb"], [1, 2, 3], [[1], [2, 3]], [[]], [V], [-1], 5,
+                                            None, "w " * 300, [[1] * 200]])
+            for k, vals in (("encoding_format", ["float", "base64", "hex", 1]), ("dimensions", [1, 8, 0, -1, 10 ** 6, "x"]),
+                            ("pooling", ["last", "mean", "max"]), ("normalize", [True, False, "x"])):
+                if rng.random() < 0.3:
+                    body[k] = rng.choice(vals)
+        elif url == "/tokenize":
+            for k, vals in (("prompt", ["hi", "", 5, None]), ("messages", [[{"role": "user", "content": "x"}], [], "x"]),
+                            ("add_special_tokens", [True, False, "x"])):
+                if rng.random() < 0.5:
+                    body[k] = rng.choice(vals)
+        else:
+            body["tokens"] = rng.choice([[5, 6], [], [V], [-1], "x", [1.5], None])
+        code, text = _post(c, url, body)
+        assert code < 500, (url, body, code, text[:400])
+        assert ae.is_ready
+    assert c.post("/v1/embeddings", json={"input": "fine"}).status_code == 200
 
 
 def test_request_chat_templates_need_the_operator_s_consent():

@@ -34,6 +34,15 @@ def test_fsm_matches_python_re_and_partial_matches(pat, s):
     assert alive == (regex_mod.fullmatch(pat, s, partial=True) is not None)
 
 
+def test_empty_patterns_match_only_the_empty_string():
+    for p in ("", "()", "(|a)b?"):
+        f = RegexFSM(p)
+        assert f.fullmatch("") and not f.fullmatch("c")
+    for bad in ({"enum": []}, {"anyOf": []}, {"oneOf": "x"}):
+        with pytest.raises(ValueError):
+            schema_to_regex(bad)
+
+
 def test_unsupported_patterns_are_refused():
     for p in (r"(a)\1", r"(?=a)b", r"a{5,2}", "[abc", "(ab", "*a"):
         with pytest.raises(RegexError):
