@@ -153,7 +153,7 @@ class LLMEngine:
         self.seq_to_request: Dict[int, Request] = {}
         self._rng = np.random.default_rng(mc.seed)
         self.stats_counters = {"steps": 0, "prompt_tokens": 0, "generation_tokens": 0,
-                               "requests_finished": 0, "requests_aborted": 0}
+                               "requests_finished": 0, "requests_aborted": 0, "requests_failed": 0}
         self.observers: List[Callable] = []
         self._prefix_caching = bool(ec.enable_prefix_caching)
         # device sampling slots (one per live sequence) of the rank that samples
@@ -393,7 +393,10 @@ class LLMEngine:
             req.metrics.last_token_time = now
             req.metrics.num_generated = max(req.metrics.num_generated, s.num_generated)
             self.stats_counters["generation_tokens"] += 1
-            self._check_stop(s, tok)
+            try:
+                self._check_stop(s, tok)
+            except Exception as e:  # noqa: BLE001 -- this request's host-side processing only
+                self._fail_request(req, e)
             if id(req) not in seen:
                 seen.add(id(req))
                 touched.append(req)
@@ -476,52 +479,84 @@ class LLMEngine:
                 self.stats_counters["prompt_tokens"] += ss.num_new
         i = 0
         beams = {}
+        failed = set()
         for ss, k in owners:
             s = ss.seq
             req = s.request
-            if req.params.prompt_logprobs is not None and req.prompt_lp is None and s.num_generated == 0:
-                req.prompt_lp = self._score_prompt(s, req.params.prompt_logprobs)
-            if req.beam is not None:
-                beams.setdefault(id(req), (req, []))[1].append((s, ss, res.top_logprobs[i]))
-                i += k
+            i0, i = i, i + k
+            if id(req) in failed:
                 continue
-            toks = res.tokens[i:i + k]
-            lps = res.logprobs[i:i + k]
-            tops = res.top_logprobs[i:i + k]
-            mus = res.mirostat_mu[i:i + k]
-            i += k
-            targets = [s]
-            if k > 1:   # fork best_of - 1 children sharing the prompt's blocks (copy-on-write)
-                for j in range(1, k):
-                    c = Sequence(req, req.prompt_token_ids, index=j)
-                    c.num_computed = s.num_computed
-                    c.num_cached = s.num_cached
-                    c.guide = s.guide.copy() if s.guide is not None else None
-                    self.bm.fork(s.seq_id, c.seq_id)
-                    req.seqs.append(c)
-                    self._register_seq(req, c)
-                    self.scheduler.add_running(c)
-                    targets.append(c)
-                req.forked = True
-            for t, tok, lp, top, mu in zip(targets, toks, lps, tops, mus):
-                t.append_token(tok, lp, top)
-                if mu is not None:
-                    t.mirostat_mu = mu
-                if req.metrics.first_token_time is None:
-                    req.metrics.first_token_time = now
-                req.metrics.last_token_time = now
-                req.metrics.num_generated = max(req.metrics.num_generated, t.num_generated)
-                self.stats_counters["generation_tokens"] += 1
-                self._check_stop(t, tok)
+            try:
+                if req.params.prompt_logprobs is not None and req.prompt_lp is None and s.num_generated == 0:
+                    req.prompt_lp = self._score_prompt(s, req.params.prompt_logprobs)
+                if req.beam is not None:
+                    beams.setdefault(id(req), (req, []))[1].append((s, ss, res.top_logprobs[i0]))
+                    continue
+                self._apply_samples(req, s, k, res, i0, now)
+            except Exception as e:  # noqa: BLE001 -- this request's host-side processing only
+                failed.add(id(req))
+                self._fail_request(req, e)
             if id(req) not in seen:
                 seen.add(id(req))
                 touched.append(req)
         for key, (req, entries) in beams.items():
-            self._beams.step(req, entries, now)
+            if key in failed:
+                continue
+            try:
+                self._beams.step(req, entries, now)
+            except Exception as e:  # noqa: BLE001
+                self._fail_request(req, e)
             if key not in seen:
                 seen.add(key)
                 touched.append(req)
         return touched
+
+    def _apply_samples(self, req: Request, s: Sequence, k: int, res, i: int, now: float) -> None:
+        """The k tokens sampled for sequence `s` (k > 1: the prompt row of a best_of
+        request, whose samples fork the sequence)."""
+        toks = res.tokens[i:i + k]
+        lps = res.logprobs[i:i + k]
+        tops = res.top_logprobs[i:i + k]
+        mus = res.mirostat_mu[i:i + k]
+        targets = [s]
+        if k > 1:   # fork best_of - 1 children sharing the prompt's blocks (copy-on-write)
+            for j in range(1, k):
+                c = Sequence(req, req.prompt_token_ids, index=j)
+                c.num_computed = s.num_computed
+                c.num_cached = s.num_cached
+                c.guide = s.guide.copy() if s.guide is not None else None
+                self.bm.fork(s.seq_id, c.seq_id)
+                req.seqs.append(c)
+                self._register_seq(req, c)
+                self.scheduler.add_running(c)
+                targets.append(c)
+            req.forked = True
+        for t, tok, lp, top, mu in zip(targets, toks, lps, tops, mus):
+            t.append_token(tok, lp, top)
+            if mu is not None:
+                t.mirostat_mu = mu
+            if req.metrics.first_token_time is None:
+                req.metrics.first_token_time = now
+            req.metrics.last_token_time = now
+            req.metrics.num_generated = max(req.metrics.num_generated, t.num_generated)
+            self.stats_counters["generation_tokens"] += 1
+            self._check_stop(t, tok)
+
+    def _fail_request(self, req: Request, exc: BaseException) -> None:
+        """A request's host-side processing (detokenisation, stop checks, guided decoding,
+        beam search, prompt scoring) raised: that request ends, aborted, with the error as
+        its stop reason, and the rest of the batch carries on.  Errors of the step itself
+        (the forward, the sampler, a device fault) still fail the engine."""
+        log.error("request %s failed in post-processing: %r", req.request_id, exc, exc_info=exc)
+        for s in req.seqs:
+            if not s.is_finished():
+                self.scheduler.remove(s)
+                self.bm.free(s.seq_id)
+                s.status = RequestStatus.FINISHED_ABORTED
+                s.finish_reason = "abort"
+                s.stop_reason = f"error: {exc!r}"[:300]
+        req.forked = True
+        self.stats_counters["requests_failed"] = self.stats_counters.get("requests_failed", 0) + 1
 
     # ------------------------------------------------------------------ embeddings
     @torch.no_grad()

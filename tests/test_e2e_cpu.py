@@ -66,7 +66,6 @@ def test_without_chunked_prefill(oracle):
     assert run(eng, prompts) == ref
 
 
-@pytest.mark.timeout(120)
 def test_without_chunked_prefill_a_prompt_longer_than_the_step_budget_still_runs(oracle):
     """Chunked prefill off, a 64-token step budget: prompts (and recompute-preempted
     sequences) longer than any step could hold are chunked anyway instead of waiting forever."""

@@ -239,3 +239,53 @@ def test_requests_larger_than_the_kv_cache_are_reported_not_stuck(mode):
     assert done["big"].finish_reason == "length" and done["big"].token_ids == []
     assert done["grows"].finish_reason == "length" and 0 < len(done["grows"].token_ids) < 200
     assert done["small"].finish_reason == "length" and len(done["small"].token_ids) == 3
+
+
+@pytest.mark.parametrize("pipelined", [False, True])
+def test_one_request_s_host_side_failure_ends_only_that_request(pipelined):
+    """An exception in one request's post-processing (here injected into its stop check)
+    aborts that request with the error as its stop reason; the batch's other requests
+    finish with the tokens they would have had, and the engine keeps serving."""
+    import numpy as np
+    from rusteeze_b200.config.config import Config
+    from rusteeze_b200.engine.llm_engine import LLMEngine
+
+    def make():
+        cfg = Config()
+        cfg.model.preset, cfg.model.device, cfg.model.dtype = "tiny-llama", "cpu", "float32"
+        cfg.engine.num_gpu_blocks = 64
+        eng = LLMEngine(cfg)
+        eng._async = pipelined
+        return eng
+
+    rng = np.random.default_rng(0)
+    prompts = {f"r{i}": rng.integers(3, 200, 20).tolist() for i in range(3)}
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+
+    def run(eng):
+        for rid, p in prompts.items():
+            eng.add_request(rid, None, sp, p)
+        done = {}
+        while eng.has_unfinished_requests():
+            for o in eng.step():
+                if o.finished:
+                    done[o.request_id] = o.outputs[0]
+        return done
+
+    ref = run(make())
+    eng = make()
+    real = eng._check_stop
+
+    def flaky(s, tok):
+        if s.request.request_id == "r1" and s.num_generated == 3:
+            raise RuntimeError("injected post-processing failure")
+        return real(s, tok)
+    eng._check_stop = flaky
+    got = run(eng)
+    assert got["r1"].finish_reason == "abort" and "injected" in got["r1"].stop_reason
+    for rid in ("r0", "r2"):
+        assert got[rid].token_ids == ref[rid].token_ids and got[rid].finish_reason == "length"
+    assert eng.stats_counters["requests_failed"] == 1
+    assert eng.bm.num_free_gpu_blocks() == eng.bm.num_gpu_blocks
+    eng._check_stop = real
+    assert run(eng)["r0"].token_ids == ref["r0"].token_ids     # still serving
