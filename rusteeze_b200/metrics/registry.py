@@ -121,6 +121,10 @@ class EngineMetrics:
             self._last_preempt = sch.num_preemptions
 
     def on_request_finished(self, out, endpoint: str = "completions", status: str = "success") -> None:
+        if out is not None and any(c.finish_reason == "abort" and str(c.stop_reason or "").startswith("error:")
+                                   for c in out.outputs):
+            status = "error"                   # ended by a failure of its own post-processing
+            self.errors.labels("request_failed").inc()
         self.requests_total.labels(status).inc()
         self.g_requests.labels(status, self.model, endpoint).inc()
         m = out.metrics if out is not None else None

@@ -289,3 +289,16 @@ def test_one_request_s_host_side_failure_ends_only_that_request(pipelined):
     assert eng.bm.num_free_gpu_blocks() == eng.bm.num_gpu_blocks
     eng._check_stop = real
     assert run(eng)["r0"].token_ids == ref["r0"].token_ids     # still serving
+
+
+def test_a_failed_request_is_counted_as_an_error_in_the_metrics():
+    from rusteeze_b200.core.outputs import CompletionOutput, RequestOutput
+    from rusteeze_b200.metrics.registry import EngineMetrics
+    m = EngineMetrics(model_name="m")
+    bad = RequestOutput("r", None, [1], [CompletionOutput(0, "", [], finish_reason="abort",
+                                                          stop_reason="error: RuntimeError('x')")], True)
+    m.on_request_finished(bad, "completions")
+    text = m.export().decode()
+    assert 'errors_total{type="request_failed"} 1.0' in text
+    assert any('status="error"' in ln and ln.rstrip().endswith(" 1.0") for ln in text.splitlines()
+               if "requests_total" in ln)
