@@ -34,6 +34,32 @@ def test_fsm_matches_python_re_and_partial_matches(pat, s):
     assert alive == (regex_mod.fullmatch(pat, s, partial=True) is not None)
 
 
+def _regex_strategy():
+    """Random patterns over a small alphabet: literals, escapes, classes (negated, ranges),
+    dots, groups, alternation and every quantifier form, nested."""
+    atoms = st.sampled_from(["a", "b", "c", "-", r"\.", r"\d", r"\w", r"\s", ".", "[ab]", "[^a]", "[a-c]",
+                             "[0-9x]", r"[\d.]", "1"])
+
+    def extend(inner):
+        quant = st.sampled_from(["*", "+", "?", "{2}", "{0,2}", "{1,}", "*?", "{1,3}"])
+        return st.one_of(
+            st.tuples(inner, quant).map(lambda t: f"(?:{t[0]}){t[1]}"),
+            st.lists(inner, min_size=2, max_size=3).map("".join),
+            st.lists(inner, min_size=2, max_size=3).map(lambda xs: "(" + "|".join(xs) + ")"),
+        )
+    return st.recursive(atoms, extend, max_leaves=8)
+
+
+@settings(max_examples=300, deadline=None)
+@given(_regex_strategy(), st.lists(st.text(alphabet="abc1x-. ", max_size=7), min_size=1, max_size=6))
+def test_random_patterns_match_python_re(pat, strings):
+    f = RegexFSM(pat)
+    for s in strings:
+        assert f.fullmatch(s) == bool(re.fullmatch(pat, s)), (pat, s)
+        alive = f.walk(f.start, s) >= 0
+        assert alive == (regex_mod.fullmatch(pat, s, partial=True) is not None), (pat, s)
+
+
 def test_empty_patterns_match_only_the_empty_string():
     for p in ("", "()", "(|a)b?"):
         f = RegexFSM(p)
