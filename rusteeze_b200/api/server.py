@@ -22,7 +22,6 @@ await per-request output queues.
 from __future__ import annotations
 
 import json
-import os
 import time
 import uuid
 from typing import AsyncIterator, List, Optional

@@ -14,7 +14,6 @@ num_gpu_blocks override, model presets for random-init benchmarks.
 from __future__ import annotations
 
 import dataclasses
-import json
 import os
 from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional

@@ -22,7 +22,6 @@ import pickle
 import time
 from typing import Optional, Tuple
 
-import numpy as np
 import torch
 
 from rusteeze_b200.engine.model_runner import ModelRunner

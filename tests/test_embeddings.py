@@ -7,7 +7,6 @@ import base64
 
 import numpy as np
 import pytest
-import torch
 
 from rusteeze_b200.config.config import Config
 from rusteeze_b200.core.errors import InvalidRequestError
