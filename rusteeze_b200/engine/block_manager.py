@@ -12,7 +12,6 @@ import importlib
 from collections import OrderedDict
 from typing import Dict, List, Tuple
 
-import numpy as np
 
 
 def host_ext():

@@ -15,7 +15,6 @@ Tested on gloo ranks against the dense oracle (tests/test_context_parallel.py).
 """
 from __future__ import annotations
 
-import math
 from typing import List, Optional, Tuple
 
 import torch

@@ -1,5 +1,4 @@
 """sm_100a kernel numerics vs the fp32 PyTorch oracles (ops.reference)."""
-import math
 
 import pytest
 import torch
