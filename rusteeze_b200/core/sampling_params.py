@@ -193,11 +193,11 @@ class SamplingParams:
                 or self.presence_penalty != 0.0)
 
     def needs_host_sampling(self) -> bool:
-        """Mirostat, typical-p, eta/epsilon cutoffs and guided decoding run on
-        the host sampler; everything else is handled by the GPU sampler."""
+        """Mirostat, typical-p and eta/epsilon cutoffs run on the host sampler; everything
+        else (guided decoding too: its constraint is a mask on the logits) is handled by
+        the batched sampler."""
         return (self.mirostat_mode > 0 or self.typical_p > 0.0 or self.eta_cutoff > 0.0
-                or self.epsilon_cutoff > 0.0 or self.guided_decoding is not None
-                or self.use_beam_search)
+                or self.epsilon_cutoff > 0.0 or self.use_beam_search)
 
     def strategy(self) -> SamplingStrategy:
         if self.use_beam_search:

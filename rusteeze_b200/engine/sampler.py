@@ -258,6 +258,7 @@ class Sampler:
         and min_tokens (up to 32 stop ids with EOS) live in the device slot tables; host
         samplers and top logprobs do not."""
         return (not params.needs_host_sampling() and params.logprobs is None and params.prompt_logprobs is None
+                and params.guided_decoding is None
                 and len(params.logit_bias) <= 320 and len(params.stop_token_ids) <= 48)
 
     def slots(self, device, max_slots: int) -> SlotTable:
@@ -364,6 +365,7 @@ class Sampler:
         # the host-side rules index the logits in place: fp32 (the GPU path hands bf16 views)
         logits = logits.float()
         logits = self._process_logits(logits, rows)
+        _apply_guides(logits, rows)
         host_rows = [i for i, r in enumerate(rows) if r.params.needs_host_sampling()]
         tokens: List[int] = [0] * R
         lps: List[Optional[float]] = [None] * R
@@ -418,6 +420,22 @@ class Sampler:
         both = torch.stack([toks.double(), lp.double()]).cpu()
         self.last_d2h_bytes += both.numel() * 8
         return [int(x) for x in both[0].tolist()], both[1].tolist()
+
+
+def _apply_guides(logits: torch.Tensor, rows: List[SampleRow]) -> None:
+    """Guided decoding: tokens outside each guided row's `allowed` mask get -inf, in place,
+    so the batched sampler (the GPU kernel, or its host restatement) draws only allowed
+    tokens with the row's own temperature / top-k / top-p / min-p."""
+    idx = [i for i, r in enumerate(rows) if r.allowed is not None and r.allowed.any()]
+    if not idx:
+        return
+    V = logits.shape[1]
+    m = torch.from_numpy(np.stack([rows[i].allowed[:V] for i in idx]))
+    dev = logits.device
+    sel = torch.tensor(idx, dtype=torch.long, device=dev)
+    sub = logits.index_select(0, sel)
+    sub.masked_fill_(~m.to(dev), float("-inf"))
+    logits.index_copy_(0, sel, sub)
 
 
 def _apply_penalties_device(sub: torch.Tensor, rows: List[SampleRow], rep, freq, pres) -> torch.Tensor:

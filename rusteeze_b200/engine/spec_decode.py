@@ -158,6 +158,7 @@ class SpecDecoder:
             s.seq.request.params.top_k <= 0 and s.seq.request.params.top_p >= 1.0 and
             s.seq.request.params.min_p == 0.0 and not s.seq.request.params.needs_host_sampling()
             and not s.seq.request.params.has_penalties() and s.seq.request.params.logprobs is None
+            and s.seq.request.params.guided_decoding is None
             and (not self.ngram or s.seq.request.params.is_greedy)
             for s in so.decodes)
         if not spec_ok:
