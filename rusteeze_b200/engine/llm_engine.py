@@ -758,7 +758,9 @@ class LLMEngine:
 
 
 class LLM:
-    """Offline batch API: `LLM(...).generate(prompts, SamplingParams(...))`."""
+    """Offline batch API: `LLM(...).generate(prompts, SamplingParams(...))`, `chat(messages)`
+    (rendered with the model's chat template, as the chat endpoint renders them) and
+    `embed(texts)`."""
 
     def __init__(self, model: Optional[str] = None, *, preset: Optional[str] = None,
                  config: Optional[Config] = None, **engine_kw):
@@ -804,3 +806,31 @@ class LLM:
                 if out.finished:
                     done[out.request_id] = out
         return [done[i] for i in ids]
+
+    @property
+    def tokenizer(self):
+        return self.engine.tokenizer
+
+    def chat(self, messages, sampling_params: Optional[SamplingParams] = None, tools: Optional[List[Dict]] = None,
+             chat_template: Optional[str] = None, add_generation_prompt: bool = True) -> List[RequestOutput]:
+        """One conversation (a list of {role, content} messages) or a list of them."""
+        from rusteeze_b200.tokenizer.chat_template import ChatTemplate
+        convs = [messages] if messages and isinstance(messages[0], dict) else list(messages)
+        eng = self.engine
+        cfg = eng.config.model
+        tmpl = (ChatTemplate(jinja=chat_template) if chat_template else
+                ChatTemplate.for_model(cfg.path or eng.model_name, eng.tokenizer, cfg.chat_template))
+        ids = []
+        for conv in convs:
+            text = tmpl.apply(conv, add_generation_prompt=add_generation_prompt, tools=tools)
+            ids.append(eng.tokenizer.encode(text, add_special_tokens=False) or eng.tokenizer.encode(text))
+        return self.generate(None, sampling_params, prompt_token_ids=ids)
+
+    def embed(self, inputs: Union[str, List[str], List[List[int]]], pooling: str = "last",
+              normalize: bool = True) -> List[np.ndarray]:
+        """Embeddings of texts (tokenised with the model's tokenizer) or token id lists."""
+        if isinstance(inputs, str):
+            inputs = [inputs]
+        lists = [self.engine.tokenizer.encode(x) if isinstance(x, str) else list(x) for x in inputs]
+        return self.engine.embed(lists, pooling, normalize)
+
