@@ -133,7 +133,18 @@ def cmd_generate(a) -> int:
             prompts += [ln.rstrip("\n") for ln in f if ln.strip()]
     if not prompts:
         prompts = [sys.stdin.read()]
-    sp = _sp_from(a)
+    kw = {}
+    guided = {k: v for k, v in (("regex", a.regex), ("choice", a.choice or None)) if v}
+    if a.json_schema:
+        with open(a.json_schema) as f:
+            guided["json_schema"] = json.load(f)
+    if guided:
+        from rusteeze_b200.core.sampling_params import GuidedDecodingParams
+        kw["guided_decoding"] = GuidedDecodingParams(**guided)
+    if a.beam_width:
+        kw.update(use_beam_search=True, best_of=a.beam_width, length_penalty=a.length_penalty)
+        a.temperature, a.top_p, a.top_k = 0.0, 1.0, None
+    sp = _sp_from(a, **kw)
     results = []
     for i, p in enumerate(prompts):
         rid = f"gen-{i}"
@@ -428,6 +439,11 @@ def build_parser() -> argparse.ArgumentParser:
     g.add_argument("--stop", action="append", default=[])
     g.add_argument("--sampling-seed", dest="seed_sampling", type=int, default=None)
     g.add_argument("-n", type=int, default=1)
+    g.add_argument("--beam-width", type=int, default=None, help="beam search with this many beams (n best returned)")
+    g.add_argument("--length-penalty", type=float, default=1.0)
+    g.add_argument("--regex", default=None, help="constrain the output to this regular expression")
+    g.add_argument("--choice", action="append", default=[], help="constrain the output to one of these (repeatable)")
+    g.add_argument("--json-schema", default=None, help="constrain the output to JSON valid for this schema file")
     g.add_argument("--stream", action="store_true")
     g.add_argument("-o", "--output")
     g.set_defaults(fn=cmd_generate)

@@ -1,5 +1,6 @@
 """Config precedence (defaults < file < env < CLI), validation, and CLI smoke tests."""
 import json
+import re
 import os
 import subprocess
 import sys
@@ -92,6 +93,23 @@ def test_cli_generate_and_benchmark_tiny():
              "--input-len", "16", "--output-len", "4", "--concurrency", "4", "--warmup", "1")
     assert r.returncode == 0, r.stderr
     assert json.loads(r.stdout)["output_tokens_per_s"] > 0
+
+
+def test_cli_generate_beam_search_and_structured_output(tmp_path):
+    base = ("--json", "generate", "-m", "tiny-llama", "--device", "cpu", "--dtype", "float32", "-p", "hello")
+    r = _cli(*base, "--max-tokens", "20", "--regex", "[0-9]{3}-[a-z]{2}")
+    assert r.returncode == 0, r.stderr
+    assert re.fullmatch("[0-9]{3}-[a-z]{2}", json.loads(r.stdout)[0]["outputs"][0]["text"])
+    r = _cli(*base, "--max-tokens", "10", "--choice", "red", "--choice", "blue", "-n", "2")
+    assert {c["text"] for c in json.loads(r.stdout)[0]["outputs"]} <= {"red", "blue"}
+    schema = tmp_path / "s.json"
+    schema.write_text(json.dumps({"type": "object", "properties": {"ok": {"type": "boolean"}}, "required": ["ok"]}))
+    r = _cli(*base, "--max-tokens", "40", "--json-schema", str(schema), "--temperature", "0")
+    assert r.returncode == 0, r.stderr
+    assert isinstance(json.loads(json.loads(r.stdout)[0]["outputs"][0]["text"])["ok"], bool)
+    r = _cli(*base, "--max-tokens", "4", "--beam-width", "3", "-n", "2")
+    assert r.returncode == 0, r.stderr
+    assert len(json.loads(r.stdout)[0]["outputs"]) == 2
 
 
 def test_cli_rejects_pipeline_parallel():
