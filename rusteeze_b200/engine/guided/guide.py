@@ -60,10 +60,18 @@ class TokenIndex:
 
     def __init__(self, tokenizer, vocab_size: int):
         self.vocab_size = vocab_size
+        # a token's text is what it adds after other text: decoded alone, a SentencePiece
+        # token drops its leading space ("▁hello" -> "hello"), so each token is decoded
+        # after a fixed plain prefix token and the prefix's own text is cut off
+        prefix, ptext = self._prefix(tokenizer)
         texts: List[str] = []
         for i in range(vocab_size):
             try:
-                t = tokenizer.decode([i], True)
+                if prefix is not None:
+                    full = tokenizer.decode([prefix, i], True)
+                    t = full[len(ptext):] if full.startswith(ptext) else tokenizer.decode([i], True)
+                else:
+                    t = tokenizer.decode([i], True)
             except Exception:  # noqa: BLE001 -- ids the tokenizer does not know
                 t = ""
             texts.append("" if "�" in t else t)
@@ -91,6 +99,18 @@ class TokenIndex:
         self.starts = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
         self.flat = np.fromiter((pos[ch] for i in self.tok_ids for ch in texts[i]), dtype=np.int64,
                                 count=int(lens.sum()))
+
+    @staticmethod
+    def _prefix(tokenizer):
+        """A token that decodes to plain text on its own ("a"), or (None, "")."""
+        try:
+            ids = tokenizer.encode("a", add_special_tokens=False)
+        except Exception:  # noqa: BLE001
+            return None, ""
+        if len(ids) != 1:
+            return None, ""
+        t = tokenizer.decode(ids, True)
+        return (ids[0], t) if t else (None, "")
 
     def allowed(self, fsm: RegexFSM, state: int) -> np.ndarray:
         """Bool mask [vocab]: tokens whose whole text keeps the DFA alive from `state`.

@@ -131,6 +131,27 @@ def test_token_masks_equal_a_brute_force_check():
         assert (m == want).all()
 
 
+class _PieceTokenizer:
+    """SentencePiece-style: "▁" marks a word start and is a space, except at the very start
+    of a decoded sequence, where it is dropped."""
+    PIECES = ["<s>", "</s>", "a", "▁a", "b", "▁b", "▁", "1", "▁1", "-"]
+
+    def encode(self, text, add_special_tokens=True):
+        return [self.PIECES.index(text)] if text in self.PIECES else []
+
+    def decode(self, ids, skip=True):
+        s = "".join(self.PIECES[i] for i in ids if not (skip and i < 2)).replace("▁", " ")
+        return s[1:] if s.startswith(" ") else s
+
+
+def test_token_texts_keep_sentencepiece_leading_spaces():
+    ix = TokenIndex(_PieceTokenizer(), len(_PieceTokenizer.PIECES))
+    assert ix.texts[:6] == ["", "", "a", " a", "b", " b"]
+    f = fsm_for("[ab]+")                            # words without spaces: "▁a" must be refused
+    m = ix.allowed(f, f.start)
+    assert m[2] and m[4] and not m[3] and not m[5]
+
+
 class _WordTokenizer:
     """A large synthetic vocabulary (multi-character tokens), to reach the self-loop path."""
 
