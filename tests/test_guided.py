@@ -25,7 +25,7 @@ PATTERNS = [r"[0-9]{3}-[a-c]+", r"(ab|ba)*c?", r"a{2,4}b{0,2}", r"(x|yz)+(\.[xy]
 ALPHA = "abcxyz0123-. \n"
 
 
-@settings(max_examples=400, deadline=None)
+@settings(max_examples=400, deadline=None, derandomize=True)
 @given(st.sampled_from(PATTERNS), st.text(alphabet=ALPHA, max_size=8))
 def test_fsm_matches_python_re_and_partial_matches(pat, s):
     f = fsm_for(pat)
@@ -50,14 +50,17 @@ def _regex_strategy():
     return st.recursive(atoms, extend, max_leaves=8)
 
 
-@settings(max_examples=300, deadline=None)
+@settings(max_examples=300, deadline=None, derandomize=True)
 @given(_regex_strategy(), st.lists(st.text(alphabet="abc1x-. ", max_size=7), min_size=1, max_size=6))
 def test_random_patterns_match_python_re(pat, strings):
     f = RegexFSM(pat)
+    # the regex module's partial matching mishandles lazy quantifiers ("(?:a)*?a" takes
+    # "a1" as a partial match); lazy and greedy forms define the same language
+    greedy = pat.replace("*?", "*")
     for s in strings:
         assert f.fullmatch(s) == bool(re.fullmatch(pat, s)), (pat, s)
         alive = f.walk(f.start, s) >= 0
-        assert alive == (regex_mod.fullmatch(pat, s, partial=True) is not None), (pat, s)
+        assert alive == (regex_mod.fullmatch(greedy, s, partial=True) is not None), (pat, s)
 
 
 def test_empty_patterns_match_only_the_empty_string():
