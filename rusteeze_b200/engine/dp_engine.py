@@ -101,6 +101,8 @@ class ReplicaView:
         engines = [r.backend.engine for r in front.router.replicas]
         first = engines[0]
         self.tokenizer = first.tokenizer
+        self.model_config = first.model_config
+        self.eos_ids = first.eos_ids
         self.model_name = first.model_name
         self.max_model_len = first.max_model_len
         self.config = first.config

@@ -263,3 +263,16 @@ def test_dp_prefix_affinity_keeps_a_shared_prefix_on_one_replica():
         assert max(hits) >= 5 * (300 // 16)
     finally:
         front.shutdown()
+
+
+def test_dp_front_end_serves_embeddings_and_the_tokenizer_endpoints(dp_app):
+    c, front = dp_app
+    r = c.post("/v1/embeddings", json={"input": [[5, 6, 7], [8, 9]]})
+    assert r.status_code == 200, r.text
+    import numpy as np
+    want = front.replicas[0].engine.embed([[5, 6, 7]])[0]
+    assert np.abs(np.array(r.json()["data"][0]["embedding"]) - want).max() < 1e-5
+    t = c.post("/tokenize", json={"prompt": "hello"})
+    assert t.status_code == 200 and t.json()["count"] > 0
+    d = c.post("/detokenize", json={"tokens": t.json()["tokens"]})
+    assert d.status_code == 200 and "hello" in d.json()["prompt"]
