@@ -261,7 +261,10 @@ class SpecDecoder:
                 req.metrics.num_generated = max(req.metrics.num_generated, s.num_generated)
                 eng.stats_counters["generation_tokens"] += 1
                 self.stats["emitted"] += 1
-                eng._check_stop(s, tok)
+                try:
+                    eng._check_stop(s, tok)
+                except Exception as e:  # noqa: BLE001 -- this request's host-side processing only
+                    eng._fail_request(req, e)
                 if s.is_finished():
                     break
             if not s.is_finished():
