@@ -75,6 +75,29 @@ _NARGS = {"PEEK": 2, "DECOMPOSE": 2, "SUBCALL_VAR": 2, "SUBCALL": 2, "BATCH_SUBC
           "TRANSFORM": 3}
 
 
+_NAME = r"[A-Za-z_][A-Za-z0-9_]{0,63}"
+# every character `str.splitlines` breaks a line at
+_EOL = r"\n\r\x0b\x0c\x1c\x1d\x1e\x85\u2028\u2029"
+_TEXT = rf"[^{_EOL}]{{1,1000}}"            # free text: may hold commas and parentheses
+_INT = r"[0-9]{1,9}"
+_SEP = r", ?"
+# one operation line, as `parse_model_output` reads it: the regex the orchestrator's
+# turns are constrained to (guided decoding), so every turn parses to an operation
+OP_PATTERN = "(" + "|".join([
+    rf"PEEK\({_INT}{_SEP}{_INT}\)",
+    rf"SEARCH\({_TEXT}\)",
+    rf"DECOMPOSE\({_INT}({_SEP}{_INT})?\)",
+    rf"SUBCALL\([^,{_EOL}]{{1,1000}},{_TEXT}\)",
+    rf"SUBCALL_VAR\({_NAME}{_SEP}{_TEXT}\)",
+    rf"BATCH_SUBCALL\({_NAME}{_SEP}{_TEXT}\)",
+    rf"SET_VAR\({_NAME}{_SEP}{_TEXT}\)",
+    rf"GET_VAR\({_NAME}\)",
+    rf"TRANSFORM\({_NAME}{_SEP}{_NAME}{_SEP}{_TEXT}\)",
+    rf"FINAL\({_TEXT}\)",
+    rf"FINAL_VAR\({_NAME}\)",
+]) + ")"
+
+
 def _strip(s: str) -> str:
     return s.strip().strip('"').strip("'")
 

@@ -23,7 +23,7 @@ import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Protocol, Tuple
 
-from rusteeze_b200.rlm.prompt_env import (EnvLimits, ExecResult, PromptEnvironment, adaptive_chunk,
+from rusteeze_b200.rlm.prompt_env import (OP_PATTERN, EnvLimits, ExecResult, PromptEnvironment, adaptive_chunk,
                                           parse_model_output)
 from rusteeze_b200.rlm.recursive_scheduler import RecursiveScheduler, SchedulerLimits
 
@@ -71,6 +71,9 @@ class RLMConfig:
     cost_per_1k_input: float = 0.001
     cost_per_1k_output: float = 0.003
     per_level_concurrency: int = 16
+    # constrain the orchestrator's turns to one operation line (`OP_PATTERN`, guided
+    # decoding) when the model supports it: a turn can then always be parsed
+    constrain_ops: bool = True
 
 
 @dataclass
@@ -129,7 +132,9 @@ class RecursiveEngine:
             env.iteration = it + 1
             stats.iterations += 1
             context = SYSTEM_PROMPT + task + "\n" + (last if it == 0 else env.iteration_metadata(last))
-            r = self.model.infer(context, cfg.root_max_tokens)
+            kw = ({"pattern": OP_PATTERN} if cfg.constrain_ops and getattr(self.model, "supports_pattern", False)
+                  else {})
+            r = self.model.infer(context, cfg.root_max_tokens, **kw)
             stats.prompt_tokens += r.prompt_tokens
             stats.completion_tokens += r.completion_tokens
             op = parse_model_output(r.text)
@@ -226,15 +231,19 @@ class EngineInferenceModel:
             ids = ids[:room // 2] + ids[-(room - room // 2):]
         return ids, min(max_tokens, self.max_ctx - len(ids))
 
-    def infer_batch(self, prompts: List[str], max_tokens: int) -> List[InferenceResult]:
-        from rusteeze_b200.core.sampling_params import SamplingParams
+    supports_pattern = True
+
+    def infer_batch(self, prompts: List[str], max_tokens: int,
+                    pattern: Optional[str] = None) -> List[InferenceResult]:
+        from rusteeze_b200.core.sampling_params import GuidedDecodingParams, SamplingParams
+        guided = GuidedDecodingParams(regex=pattern) if pattern else None
         rids = []
         for p in prompts:
             ids, mt = self._clip(self.engine.tokenizer.encode(p), max_tokens)
             self._n += 1
             rid = f"rlm-{self._n}"
-            self.engine.add_request(rid, None, SamplingParams(temperature=self.temperature, max_tokens=max(1, mt)),
-                                    ids)
+            self.engine.add_request(rid, None, SamplingParams(temperature=self.temperature, max_tokens=max(1, mt),
+                                                              guided_decoding=guided), ids)
             rids.append(rid)
         done: Dict[str, object] = {}
         while any(r not in done for r in rids):
@@ -247,8 +256,8 @@ class EngineInferenceModel:
             out.append(InferenceResult(o.outputs[0].text, len(o.prompt_token_ids), len(o.outputs[0].token_ids)))
         return out
 
-    def infer(self, prompt: str, max_tokens: int) -> InferenceResult:
-        return self.infer_batch([prompt], max_tokens)[0]
+    def infer(self, prompt: str, max_tokens: int, pattern: Optional[str] = None) -> InferenceResult:
+        return self.infer_batch([prompt], max_tokens, pattern)[0]
 
 
 class MockInferenceModel:

@@ -145,3 +145,36 @@ def test_rlm_over_tiny_cpu_engine():
     assert len(outs) == 3 and all(o.completion_tokens >= 1 for o in outs)
     res = RecursiveEngine(m, RLMConfig(max_iterations=2, root_max_tokens=8)).process("some long text " * 20)
     assert res.stats.iterations == 2
+
+
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+from rusteeze_b200.rlm.prompt_env import OP_PATTERN, parse_model_output  # noqa: E402
+
+
+@settings(max_examples=300, deadline=None, derandomize=True)
+@given(st.from_regex(OP_PATTERN, fullmatch=True))
+def test_every_string_of_the_operation_pattern_parses_to_an_operation(s):
+    assert parse_model_output(s).kind != "THINK", s
+
+
+def test_constrained_root_turns_are_operations():
+    """With random weights, the orchestrator's turns (guided by the operation pattern) are
+    operation lines or prefixes of one cut by max_tokens -- never free text."""
+    from rusteeze_b200.config.config import Config
+    from rusteeze_b200.engine.guided import fsm_for
+    from rusteeze_b200.engine.llm_engine import LLMEngine
+    from rusteeze_b200.rlm import EngineInferenceModel
+    cfg = Config()
+    cfg.model.preset, cfg.model.device, cfg.model.dtype = "tiny-llama", "cpu", "float32"
+    cfg.model.max_model_len = 2048
+    cfg.engine.num_gpu_blocks = 256
+    cfg.engine.max_num_batched_tokens = 2048
+    cfg.engine.enable_chunked_prefill = True
+    m = EngineInferenceModel(LLMEngine(cfg), temperature=0.8)
+    f = fsm_for(OP_PATTERN)
+    for prompt in ("task one", "task two", "task three"):
+        out = m.infer(prompt, 60, pattern=OP_PATTERN).text
+        assert f.walk(f.start, out) >= 0, out
+    res = RecursiveEngine(m, RLMConfig(max_iterations=3, root_max_tokens=60)).process("some long text " * 20)
+    assert res.stats.iterations >= 1
