@@ -116,6 +116,65 @@ def test_schema_regex_accepts_instances_and_rejects_others():
     assert RegexFSM(any_object()).fullmatch('{"a": [1, {"b": null}], "c": "x"}')
 
 
+def _conforms(v, sch, root):
+    """The schema subset the compiler supports, checked on a parsed value."""
+    if "$ref" in sch:
+        node = root
+        for part in sch["$ref"][2:].split("/"):
+            node = node[part]
+        return _conforms(v, node, root)
+    if "const" in sch:
+        return v == sch["const"]
+    if "enum" in sch:
+        return v in sch["enum"]
+    for k in ("anyOf", "oneOf"):
+        if k in sch:
+            return any(_conforms(v, x, root) for x in sch[k])
+    t = sch.get("type")
+    if isinstance(t, list):
+        return any(_conforms(v, dict(sch, type=x), root) for x in t)
+    if t == "string":
+        return isinstance(v, str) and len(v) <= sch.get("maxLength", 10 ** 9) and len(v) >= sch.get("minLength", 0)
+    if t == "integer":
+        return type(v) is int
+    if t == "number":
+        return type(v) in (int, float)
+    if t == "boolean":
+        return type(v) is bool
+    if t == "null":
+        return v is None
+    if t == "array":
+        return (isinstance(v, list) and sch.get("minItems", 0) <= len(v) <= sch.get("maxItems", 10 ** 9)
+                and all(_conforms(x, sch.get("items", {}), root) for x in v))
+    if t == "object":
+        props = sch.get("properties", {})
+        return (isinstance(v, dict) and set(v) <= set(props) and set(sch.get("required", [])) <= set(v)
+                and all(_conforms(v[k], props[k], root) for k in v))
+    return True
+
+
+_SCHEMAS = [
+    SCHEMA,
+    {"type": "object", "properties": {"s": {"type": "string"}, "n": {"type": "number"},
+                                      "o": {"type": "object", "properties": {"x": {"type": "null"}}}},
+     "required": ["s"]},
+    {"type": "array", "items": {"anyOf": [{"type": "integer"}, {"const": "k"}]}, "minItems": 1, "maxItems": 3},
+    {"type": "object", "properties": {"a": {"type": "boolean"}, "b": {"enum": [1, "two", None]}}},
+]
+
+
+@pytest.mark.parametrize("i", range(len(_SCHEMAS)))
+def test_every_string_of_a_schema_regex_is_conforming_json(i):
+    sch = _SCHEMAS[i]
+    pat = schema_to_regex(sch)
+
+    @settings(max_examples=150, deadline=None, derandomize=True)
+    @given(st.from_regex(pat, fullmatch=True))
+    def check(text):
+        assert _conforms(json.loads(text), sch, sch), text
+    check()
+
+
 def test_token_masks_equal_a_brute_force_check():
     tok = ByteTokenizer(300)
     ix = TokenIndex(tok, 300)
