@@ -2,7 +2,9 @@
 
 `GuidedDecodingParams` (choice, regex, JSON schema, JSON object) compiles to one regex
 and its lazily built DFA (`regex_fsm.RegexFSM`, cached per pattern).  A `TokenIndex`
-holds, per tokenizer, the text of every token and a character trie over those texts.
+holds, per tokenizer, the text of every token and a character trie over those texts
+(built on the first guided request: about 1 s and 115 MB of host memory for a
+128K-token vocabulary).
 The tokens allowed in a DFA state are found by walking the trie and the DFA together,
 cutting a branch as soon as the DFA dies, so shared token prefixes are stepped once (or,
 in states where most characters loop back, by a vectorised check of whole tokens); the
