@@ -240,6 +240,9 @@ def main():
     ap.add_argument("--e2e-requests", type=int, default=None,
                     help="requests of the end-to-end run (default: --requests, scaled like it)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-http", action="store_true",
+                    help="run the end-to-end stream through the HTTP server (streamed /v1/completions calls) "
+                         "instead of LLMEngine.add_request (one engine, one process)")
     ap.add_argument("--dtype", default="fp8", choices=["fp8", "bf16"],
                     help="fp8: block-scaled e4m3 weights (the Llama-3-8B serving configuration); bf16: unquantised")
     ap.add_argument("--fp8", action="store_true", help="same as --dtype fp8 (the default)")
@@ -365,6 +368,56 @@ def serve_tp(args, world, rank):
         runner.release_graphs()            # graphs holding NCCL calls go before the process group
         Device(str(info.device)).sync()
         dist.destroy_process_group()
+
+
+def e2e_over_http(eng, V, prompts, olens, arrivals, dev):
+    """The end-to-end run through the OpenAI-compatible HTTP server (one process, one
+    engine): the server runs in this process on a local port, and every request of the
+    stream is a streamed /v1/completions call sent at its Poisson arrival time; output
+    tok/s over the wall time from the first send to the last [DONE]."""
+    import asyncio
+    import socket
+    import threading
+    import uvicorn
+    from rusteeze_b200.api.server import create_app
+    from rusteeze_b200.config.config import Config
+    from rusteeze_b200.engine.async_engine import AsyncLLMEngine
+    from rusteeze_b200.utils.http_bench import run_http_benchmark
+    cfg = Config()
+    cfg.logging.request_logging = False
+    cfg.server.max_connections = max(cfg.server.max_connections, len(prompts) + 16)
+    h2d0, d2h0, steps0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes, eng.stats_counters["steps"]
+    ae = AsyncLLMEngine(eng).start()
+    sk = socket.socket()
+    sk.bind(("127.0.0.1", 0))
+    port = sk.getsockname()[1]
+    sk.close()
+    server = uvicorn.Server(uvicorn.Config(create_app(ae, cfg), host="127.0.0.1", port=port, log_level="error"))
+    th = threading.Thread(target=server.run, daemon=True)
+    th.start()
+    t_wait = time.monotonic()
+    while not server.started and time.monotonic() - t_wait < 60:
+        time.sleep(0.05)
+    try:
+        res = asyncio.run(run_http_benchmark(
+            f"http://127.0.0.1:{port}", "", V, len(prompts), 0, 0, concurrency=len(prompts),
+            prompts=[list(map(int, p)) for p in prompts], output_lens=[int(x) for x in olens],
+            arrivals=[float(a) for a in arrivals], extra_body={"temperature": 0.7, "top_p": 0.9}))
+    finally:
+        server.should_exit = True
+        th.join(30)
+        ae.shutdown()
+    dev.sync()
+    steps = max(1, eng.stats_counters["steps"] - steps0)
+    return {"value": res["output_tokens_per_s"], "unit": "output_tokens/s",
+            "h2d_bytes_per_step": int((eng.runner.h2d_bytes - h2d0) / steps),
+            "d2h_bytes_per_step": int((eng.runner.d2h_bytes - d2h0) / steps),
+            "requests": res["num_prompts"], "completed": res["completed"], "wall_s": round(res["duration_s"], 3),
+            "via": "http",
+            "workload": f"{len(prompts)} requests, Poisson {len(prompts) / max(arrivals[-1], 1e-9):.0f}/s arrivals, "
+                        "same length ranges and sampling as the timed run, each a streamed /v1/completions call "
+                        "to the in-process HTTP server; wall clock from the first send to the last [DONE]",
+            "ttft_p50_s": None if res["ttft_p50_ms"] is None else round(res["ttft_p50_ms"] / 1e3, 4)}
 
 
 def serve(args, eng, device, rank, local, world, tp_timer=None):
@@ -501,7 +554,13 @@ def serve(args, eng, device, rank, local, world, tp_timer=None):
 
     # ---------------------------------------------------------------- end-to-end through the public API
     e2e = None
-    if not args.no_e2e:
+    http_e2e = bool(getattr(args, "e2e_http", False)) and world == 1 and tp_timer is None
+    if not args.no_e2e and http_e2e:
+        for rid in list(eng.requests):
+            eng.abort_request(rid)
+        e_prompts, e_olens, e_arr = build_workload(args.e2e_requests, 5000, V, args.rate, plen, olen)
+        e2e = e2e_over_http(eng, V, e_prompts, e_olens, e_arr, dev)
+    if not args.no_e2e and not http_e2e:
         # drain the steady-state run so the e2e run starts from an empty engine
         for rid in list(eng.requests):
             eng.abort_request(rid)

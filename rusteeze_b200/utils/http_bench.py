@@ -17,9 +17,10 @@ import time
 from typing import Dict, List, Optional
 
 
-async def _one(client, url: str, model: str, prompt: List[int], max_tokens: int, sem, out: List[Dict]) -> None:
+async def _one(client, url: str, model: str, prompt: List[int], max_tokens: int, sem, out: List[Dict],
+               extra: Optional[Dict] = None) -> None:
     body = {"model": model, "prompt": [prompt], "max_tokens": max_tokens, "temperature": 0.0,
-            "ignore_eos": True, "stream": True, "stream_options": {"include_usage": True}}
+            "ignore_eos": True, "stream": True, "stream_options": {"include_usage": True}, **(extra or {})}
     async with sem:
         t0 = time.perf_counter()
         first = last = None
@@ -52,19 +53,30 @@ async def _one(client, url: str, model: str, prompt: List[int], max_tokens: int,
 
 async def run_http_benchmark(url: str, model: str, vocab: int, num_prompts: int, input_len: int, output_len: int,
                              concurrency: int, request_rate: Optional[float] = None, seed: int = 0,
-                             timeout_s: float = 600.0) -> Dict:
+                             timeout_s: float = 600.0, prompts: Optional[List[List[int]]] = None,
+                             output_lens: Optional[List[int]] = None,
+                             arrivals: Optional[List[float]] = None, extra_body: Optional[Dict] = None) -> Dict:
+    """Random prompts of `input_len` ids and `output_len` tokens each, or an explicit
+    workload: `prompts` with their `output_lens`, sent at the `arrivals` offsets (seconds
+    from the start) when given."""
     import httpx
     rng = random.Random(seed)
-    prompts = [[rng.randrange(vocab) for _ in range(input_len)] for _ in range(num_prompts)]
+    if prompts is None:
+        prompts = [[rng.randrange(vocab) for _ in range(input_len)] for _ in range(num_prompts)]
+    olens = output_lens or [output_len] * len(prompts)
+    num_prompts = len(prompts)
     sem = asyncio.Semaphore(max(1, concurrency))
     out: List[Dict] = []
     limits = httpx.Limits(max_connections=max(1, concurrency) + 4)
     async with httpx.AsyncClient(timeout=timeout_s, limits=limits) as client:
         t0 = time.perf_counter()
         tasks = []
-        for p in prompts:
-            tasks.append(asyncio.create_task(_one(client, url.rstrip("/"), model, p, output_len, sem, out)))
-            if request_rate:
+        for i, p in enumerate(prompts):
+            if arrivals is not None:
+                await asyncio.sleep(max(0.0, arrivals[i] - (time.perf_counter() - t0)))
+            tasks.append(asyncio.create_task(_one(client, url.rstrip("/"), model, p, int(olens[i]), sem, out,
+                                                  extra_body)))
+            if request_rate and arrivals is None:
                 await asyncio.sleep(rng.expovariate(request_rate))
         await asyncio.gather(*tasks)
         wall = time.perf_counter() - t0

@@ -130,3 +130,16 @@ def test_bench_moe_static_batches_one_process_and_tp2_on_gloo():
     assert r.returncode == 0, r.stderr[-3000:]
     lines = _json_lines(r.stdout)
     assert lines and lines[-1]["n_gpus"] == 2 and lines[-1]["value"] > 0
+
+
+@pytest.mark.timeout(900)
+def test_bench_e2e_over_http_serves_the_whole_stream():
+    """`--e2e-http`: the end-to-end stream goes through the OpenAI-compatible server as
+    streamed /v1/completions calls; every request completes and the line says so."""
+    r = subprocess.run([sys.executable, "bench.py"] + _POISSON + ["--e2e-http"], cwd=ROOT, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    d = _json_lines(r.stdout)[-1]
+    e = d["e2e"]
+    assert e["via"] == "http" and e["value"] > 0 and e["completed"] == e["requests"] == 4, e
+    assert e["h2d_bytes_per_step"] > 0 and e["d2h_bytes_per_step"] >= 0
