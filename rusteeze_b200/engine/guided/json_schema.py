@@ -27,6 +27,7 @@ NUMBER = INTEGER + r"(\.[0-9]{1,16})?([eE][+-]?[0-9]{1,3})?"
 BOOLEAN = "(true|false)"
 NULL = "null"
 ANY_DEPTH = 3
+_MAX_BOUND = 1000          # counted repetitions the automaton unrolls
 
 
 class SchemaError(ValueError):
@@ -128,6 +129,8 @@ class _Compiler:
                 p = s["pattern"]
                 return '"(' + (p[1:] if p.startswith("^") else p).rstrip("$") + ')"'
             lo, hi = int(s.get("minLength", 0)), s.get("maxLength")
+            if max(lo, int(hi or 0)) > _MAX_BOUND:
+                raise SchemaError(f"minLength / maxLength above {_MAX_BOUND} are not supported")
             if lo == 0 and hi is None:
                 return STRING
             return f'"{STRING_CHAR}' + ("{%d,}" % lo if hi is None else "{%d,%d}" % (lo, int(hi))) + '"'
@@ -143,6 +146,8 @@ class _Compiler:
             item = self.value(s.get("items", {}))
             lo = int(s.get("minItems", 0))
             hi = s.get("maxItems")
+            if max(lo, int(hi or 0)) > _MAX_BOUND:
+                raise SchemaError(f"minItems / maxItems above {_MAX_BOUND} are not supported")
             return _list(item, lo, None if hi is None else int(hi))
         if t == "object":
             return self.obj(s)
@@ -170,6 +175,13 @@ class _Compiler:
 
 
 def schema_to_regex(schema: Any) -> str:
+    """The regex of a schema; a schema this subset cannot express, or a malformed one,
+    raises SchemaError (a ValueError: the client's mistake, not the server's)."""
     if isinstance(schema, str):
         schema = json.loads(schema)
-    return _Compiler(schema if isinstance(schema, dict) else {}).value(schema)
+    try:
+        return _Compiler(schema if isinstance(schema, dict) else {}).value(schema)
+    except SchemaError:
+        raise
+    except (TypeError, AttributeError, KeyError, IndexError, ValueError) as e:
+        raise SchemaError(f"malformed JSON schema: {e}") from None

@@ -310,7 +310,11 @@ def test_a_pattern_the_vocabulary_cannot_spell_ends_the_request(eng):
 
 def test_invalid_constraints_are_refused(eng):
     for g in (GuidedDecodingParams(), GuidedDecodingParams(regex="a", choice=["a"]),
-              GuidedDecodingParams(grammar="root ::= 'a'"), GuidedDecodingParams(regex="(a")):
+              GuidedDecodingParams(grammar="root ::= 'a'"), GuidedDecodingParams(regex="(a"),
+              # malformed or unsupported schemas are the client's error, never a server one
+              GuidedDecodingParams(json_schema={"properties": 7}), GuidedDecodingParams(json_schema={"$ref": 5}),
+              GuidedDecodingParams(json_schema={"type": "string", "maxLength": 5000}),
+              GuidedDecodingParams(json_schema={"type": "array", "maxItems": {"a": 1}})):
         with pytest.raises(InvalidRequestError):
             eng.add_request(None, "x", SamplingParams(guided_decoding=g))
     with pytest.raises(InvalidRequestError):
