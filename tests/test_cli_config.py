@@ -147,3 +147,20 @@ def test_a_model_is_required_from_somewhere(tmp_path, monkeypatch):
         _load_config(build_parser().parse_args(["serve"]))
     monkeypatch.setenv("RUSTEEZE_MODEL", "tiny-llama")
     assert _load_config(build_parser().parse_args(["serve"])).model.preset == "tiny-llama"
+
+
+def test_validate_accepts_the_newer_knobs_and_refuses_bad_values(tmp_path):
+    good = tmp_path / "good.yaml"
+    good.write_text("engine:\n  speculative: {method: ngram, num_speculative_tokens: 4, ngram_max: 4, ngram_min: 1}\n"
+                    "metrics:\n  push_gateway: {url: 'http://gw:9091', job: rz}\n"
+                    "server:\n  router_policy: prefix_affinity\n"
+                    "  rate_limit: {enabled: true, tokens_per_minute: 1000, tokens_per_day: 100000}\n")
+    r = _cli("-c", str(good), "validate")
+    assert r.returncode == 0 and "valid" in r.stdout, r.stderr
+    bad = tmp_path / "bad.yaml"
+    bad.write_text("engine:\n  speculative: {method: medusa}\nmetrics:\n  push_gateway: {url: 'gw', job: ''}\n"
+                   "server:\n  router_policy: sticky\n  rate_limit: {enabled: true, tokens_per_minute: 0}\n")
+    r = _cli("-c", str(bad), "validate")
+    assert r.returncode != 0
+    for needle in ("medusa", "push_gateway.url", "push_gateway.job", "router_policy", "tokens_per_minute"):
+        assert needle in r.stdout + r.stderr, needle
