@@ -13,9 +13,10 @@ parallel_sampler.rs:86-89), and logprobs.
 On the GPU the whole batch is sampled by one kernel launch (sm_100a
 `topk_topp_sample`: per-row max/normaliser, histogram threshold selection
 for top-k/top-p/min-p, Gumbel-max draw from a counter-based Philox stream
-keyed by (seed, step)), or `argmax_sample` when every row is greedy.  Rows
-that need Mirostat, typical-p, eta/epsilon cutoffs or guided decoding are
-copied to the host and sampled there.
+keyed by (seed, step)), or `argmax_sample` when every row is greedy.  Guided
+rows have their excluded tokens set to -inf first and are sampled with the rest.
+Rows that need Mirostat, typical-p or eta/epsilon cutoffs are copied to the host
+and sampled there.
 """
 from __future__ import annotations
 
