@@ -229,9 +229,12 @@ def cmd_benchmark(a) -> int:
         # a running server over HTTP (streamed /v1/completions), no engine in this process
         import asyncio
         from rusteeze_b200.utils.http_bench import run_http_benchmark
+        extra = {"temperature": a.url_temperature} if a.url_temperature is not None else {}
+        if a.url_top_p is not None:
+            extra["top_p"] = a.url_top_p
         res = asyncio.run(run_http_benchmark(a.url, a.served_model or a.model or "default", a.vocab_size,
                                              a.num_prompts, a.input_len, a.output_len, a.concurrency,
-                                             a.request_rate, a.seed or 0))
+                                             a.request_rate, a.seed or 0, extra_body=extra or None))
         s = json.dumps(res, indent=None if a.json else 1)
         print(s)
         if a.output:
@@ -469,6 +472,8 @@ def build_parser() -> argparse.ArgumentParser:
     b.add_argument("--url", default=None,
                    help="benchmark a running OpenAI-compatible server at this base URL over HTTP instead")
     b.add_argument("--request-rate", type=float, default=None, help="--url: Poisson arrivals per second")
+    b.add_argument("--url-temperature", type=float, default=None, help="--url: sampling temperature (default greedy)")
+    b.add_argument("--url-top-p", type=float, default=None, help="--url: top-p of the requests")
     b.add_argument("--served-model", default=None, help="--url: the model name sent in requests")
     b.add_argument("--vocab-size", type=int, default=32000, help="--url: range of the random prompt token ids")
     b.set_defaults(fn=cmd_benchmark)

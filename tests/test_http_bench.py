@@ -69,7 +69,8 @@ def test_cli_benchmark_url(server_url, tmp_path):
     out = tmp_path / "r.json"
     r = subprocess.run([sys.executable, "-m", "rusteeze_b200", "--json", "benchmark", "--url", server_url,
                         "--served-model", "tiny-llama", "--vocab-size", "256", "-n", "4", "--input-len", "16",
-                        "--output-len", "5", "--concurrency", "2", "-o", str(out)],
+                        "--output-len", "5", "--concurrency", "2", "--url-temperature", "0.7", "--url-top-p", "0.9",
+                        "-o", str(out)],
                        capture_output=True, text=True, timeout=240, cwd=ROOT, env=dict(os.environ, PYTHONPATH=ROOT))
     assert r.returncode == 0, r.stderr
     d = json.loads(out.read_text())
